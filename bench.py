@@ -1,0 +1,365 @@
+"""Benchmark: Walsh-512 prefill tokens/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl walsh|reference]
+
+Workload (per rank, weak scaling): mHCWalsh Walsh-512 (L16, H32, C512, 16
+experts top-6, channel modulation, 4 mHC streams, vocab 50257), bf16
+activations, batch 64 x seq 1024 random token ids, seeded random weights with
+ternary latents and router logits scaled to ~N(0, 1).  One step = one full
+prefill forward (last-position logits).  The per-layer stream state
+(64*1024*4*512 bf16 = 268 MB) exceeds the 126 MB L2, so no flush is needed
+between steps.
+
+Prints one JSON line (rank 0).  `value` times graph replays of the forward
+with inputs resident in HBM; `e2e` times the public ``mHCWalsh.forward`` call
+with the token ids copied from pinned host memory and the logits copied back
+every step.  `--impl reference` times the CPU oracle (a numpy restatement of
+the reference's PyTorch forward) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = dict(block_size=1024, vocab_size=50257, n_layer=16, n_head=32, n_embd=512, dropout=0.0, bias=False,
+              head_mixing=True, algebra="hadamard", hash_embeddings=False, use_moe=True, moe_threshold=0.1,
+              moe_min_experts=1, moe_max_experts=6, use_channel_mod=True)
+N_STREAMS = 4
+BATCH, SEQ = 64, 1024
+ROUTER_SCALE = 18.3
+METRIC = "Walsh-512 prefill tokens/s"
+UNIT = "tokens/s"
+CPU_SAMPLE = (1, 1024)  # oracle sample per step: B1 x T1024
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def build_model_cpu(seed=0):
+    """The seeded recipe: package init, ternary latents i.i.d. uniform {-1,0,1},
+    router output layer scaled so router logits are ~N(0,1)."""
+    from walsh_research_b200.model import WalshConfig, mHCWalsh
+    torch.manual_seed(seed)
+    model = mHCWalsh(WalshConfig(**CONFIG), n_streams=N_STREAMS).eval()
+    g = torch.Generator().manual_seed(seed)
+    pat = re.compile(r"\.inner\.weight$|experts\.(gate|up|down)_weights$|channel_mod\.context_mlp\.\d\.weight$")
+    with torch.no_grad():
+        for name, p in sorted(model.named_parameters()):
+            if pat.search(name):
+                p.copy_(torch.randint(-1, 2, p.shape, generator=g).float())
+        for layer in model.layers:
+            layer.feed_forward.router.gate[2].weight.mul_(ROUTER_SCALE)
+    return model
+
+
+def token_ids(B, T, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, CONFIG["vocab_size"], (B, T), generator=g)
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={CLOCK_FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the numpy oracle on the host cores
+# ---------------------------------------------------------------------------
+
+def oracle_inputs():
+    model = build_model_cpu()
+    sd = {k: v.detach().float().numpy() for k, v in model.state_dict().items()
+          if k != "freqs_cis" and not k.endswith(".H")}
+    return sd
+
+
+def time_oracle(sd, steps, warmup):
+    from oracle import walsh_oracle as O
+    B, T = CPU_SAMPLE
+    idx = token_ids(B, T, seed=2).numpy()
+    for _ in range(warmup):
+        O.mhc_walsh_forward(CONFIG, sd, idx, N_STREAMS, dtype=np.float32)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        O.mhc_walsh_forward(CONFIG, sd, idx, N_STREAMS, dtype=np.float32)
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    return B * T / sec, sec
+
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        return max([i.get("num_threads", 1) for i in info] or [os.cpu_count()])
+    except Exception:
+        return os.cpu_count()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sd = oracle_inputs()
+    value, sec = time_oracle(sd, args.steps, args.warmup)
+    B, T = CPU_SAMPLE
+    cores = cpu_threads()
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"Walsh-512 mHC+MoE+chmod prefill (config 3 architecture), sample B{B}xT{T}",
+                       "global_batch": B, "seq_len": T},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"one B{B}xT{T} forward of the numpy oracle per step, float32"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------
+
+def kernel_launches_per_forward(L=16):
+    # embed gather 1; per layer: map 2, qkv 1, attn 1, head mixer 1, wo 1, post 1, moe 1, chmod 3;
+    # merge linear 1, rmsnorm 1, logits linear 1
+    return 1 + L * 12 + 3
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="walsh", choices=["walsh", "reference"])
+    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="run one warm-up and one eager forward only (for ncu launch lists)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.profile:
+        return run_profile(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model.mhc import MAP_EPS, site_params
+
+    B, T = args.batch, SEQ
+    cpu_model = build_model_cpu()
+    sd_np = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sd_np = {k: v.detach().float().numpy() for k, v in cpu_model.state_dict().items()
+                 if k != "freqs_cis" and not k.endswith(".H")}
+    model = cpu_model.to(dev).eval()
+    model.compute_dtype = torch.bfloat16
+    idx_host = token_ids(B, T, seed=1 + rank).pin_memory()
+    idx = idx_host.to(dev)
+
+    # graph-captured forward: inputs resident in HBM
+    with torch.no_grad():
+        for _ in range(2):
+            model(idx)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits_g, _ = model(idx)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            torch.cuda.synchronize()
+            start.record()
+            for _ in range(args.steps):
+                graph.replay()
+            end.record()
+            torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / args.steps
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        value = world * B * T / (ms / 1e3)
+
+        # end to end through the public API: H2D ids, forward, D2H logits
+        logits_host = torch.empty((B, 1, CONFIG["vocab_size"]), dtype=torch.float32).pin_memory()
+        for _ in range(2):
+            idx.copy_(idx_host, non_blocking=True)
+            lg, _ = model(idx)
+            logits_host.copy_(lg, non_blocking=True)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e_steps = max(3, args.steps // 2)
+        start.record()
+        for _ in range(e_steps):
+            idx_dev = idx_host.to(dev, non_blocking=True)
+            lg, _ = model(idx_dev)
+            logits_host.copy_(lg, non_blocking=True)
+        end.record()
+        torch.cuda.synchronize()
+        e_ms = start.elapsed_time(end) / e_steps
+        if dist:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": world * B * T / (e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": idx_host.numel() * idx_host.element_size(),
+               "d2h_bytes_per_step": logits_host.numel() * logits_host.element_size()}
+
+        # dominant kernel timed alone with CUDA events on the launching stream:
+        # prefill attention of one layer (q/k/v of layer 0 recomputed in place)
+        roof = dominant_kernel_roofline(model, idx, B, T, dev)
+
+    del graph
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None
+    if sd_np is not None:
+        v, sec = time_oracle(sd_np, steps=2, warmup=1)
+        Bc, Tc = CPU_SAMPLE
+        cpu = {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+               "sample": f"numpy oracle float32, one B{Bc}xT{Tc} forward per step (same architecture and weights)"}
+    hbm, tflops, src = peaks()
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 3: Walsh-512 mHC+MoE(16e top-6)+chmod prefill", "global_batch": world * B,
+                       "batch_per_gpu": B, "seq_len": T, "parallelism": f"replicas x{world} (batch-sharded)",
+                       "l2": "working set > L2 (stream state 268 MB per layer), no flush"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+            "gpu_launches": kernel_launches_per_forward(CONFIG["n_layer"]) * args.steps,
+            "peaks": src}
+    print(json.dumps(line), flush=True)
+
+
+def run_profile(args):
+    """One warm-up forward then one profiled forward, eager (no graph)."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    model = build_model_cpu().to(dev).eval()
+    model.compute_dtype = torch.bfloat16
+    idx = token_ids(args.batch, SEQ).to(dev)
+    with torch.no_grad():
+        model(idx)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("walsh_forward")
+        model(idx)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    print("profile forward done", flush=True)
+
+
+def dominant_kernel_roofline(model, idx, B, T, dev):
+    """Time the prefill attention kernel alone (CUDA events, current stream)."""
+    from walsh_research_b200 import ops
+    H, C = CONFIG["n_head"], CONFIG["n_embd"]
+    hd = C // H
+    q = torch.randn((B, H, T, hd), device=dev).to(torch.bfloat16)
+    k = torch.randn((B, H, T, hd), device=dev).to(torch.bfloat16)
+    v = torch.randn((B, H, T, hd), device=dev).to(torch.bfloat16)
+    o = torch.empty((B, T, H, hd), device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        ops.attention(q, k, v, 0, out=o)
+    n = 10
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(n):
+        ops.attention(q, k, v, 0, out=o)
+    e.record()
+    torch.cuda.synchronize()
+    sec = s.elapsed_time(e) / n / 1e3
+    flops = 4.0 * B * H * hd * (T * (T + 1) / 2)
+    hbm, tflops, src = peaks()
+    achieved = flops / sec / 1e12
+    return {"kernel": "walsh_attn_fwd (prefill, causal, hd16, bf16)", "bound": "tensor", "achieved": achieved,
+            "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops, "traffic": None,
+            "launch_ms": sec * 1e3, "peak_source": src}
+
+
+if __name__ == "__main__":
+    main()

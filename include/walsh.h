@@ -1,0 +1,262 @@
+/*
+ * libwalsh — C ABI of the B200 (sm_100a) kernels for Walsh's forward hot path.
+ *
+ * The reference (pulseofthemachine/Walsh-Research) has no FFI: its "plugin"
+ * boundary is Python module substitution inside src/model (the import-time
+ * choice at src/model/physics.py:84-91, the factories at
+ * src/model/chassis.py:54-94).  Each entry point below replaces the forward
+ * of one reference module or one fused group of them; the reference
+ * interface it stands in for is cited beside it.  The Python package
+ * walsh_research_b200.model re-exposes them behind the reference's class
+ * names and state-dict keys.
+ *
+ * Conventions
+ *  - All pointers are device pointers unless stated otherwise; every buffer
+ *    is allocated and owned by the caller.  Nothing here allocates device
+ *    memory on the forward path, frees caller memory or synchronises.
+ *  - Activations are either float32 (dtype WALSH_F32) or bfloat16
+ *    (WALSH_BF16); arithmetic is float32 in both cases.
+ *  - Every call launches on `stream` (a cudaStream_t passed as void*) and
+ *    returns a walsh_status: 0 on success, a negative code on a rejected
+ *    argument (checked on the host before any launch) or a launch failure.
+ *  - Ternary weights are 2 bits each in the reference's encoding
+ *    (-1 -> 00, 0 -> 01, +1 -> 10; four per byte, first value in the most
+ *    significant bits; src/model/fht_cuda.py:65-93), rows of length K padded
+ *    to ceil(K/4) bytes with the zero code.
+ */
+#ifndef WALSH_H_
+#define WALSH_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int walsh_status;
+
+enum {
+  WALSH_OK = 0,
+  WALSH_ERR_ARG = -1,      /* null pointer / bad scalar argument */
+  WALSH_ERR_SHAPE = -2,    /* unsupported or inconsistent sizes */
+  WALSH_ERR_DTYPE = -3,    /* unknown dtype code */
+  WALSH_ERR_ALIGN = -4,    /* pointer not aligned as required */
+  WALSH_ERR_LAUNCH = -5,   /* CUDA launch error */
+  WALSH_ERR_TIMEOUT = -6,  /* a bounded device-side wait gave up */
+  WALSH_ERR_INJECTED = -7, /* host-side fault injector fired (tests) */
+  WALSH_ERR_NOT_INIT = -8, /* library not initialised for this device */
+  WALSH_ERR_INDEX = -9     /* a device kernel saw an out-of-range token id */
+};
+
+enum { WALSH_F32 = 0, WALSH_BF16 = 1 };
+
+/* Human-readable text of a status code (static storage). */
+const char* walsh_status_str(walsh_status s);
+/* ABI version of this library (bumped on any signature change). */
+int walsh_abi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Ternary weights (load-time)
+ * ------------------------------------------------------------------------- */
+
+/* Absmean ternary quantisation + 2-bit packing of a latent weight tensor
+ * viewed as [rows, k]: gamma = mean|W| + 1e-8 over the whole tensor,
+ * q = clamp(round_half_even(W / gamma), -1, 1).  Writes packed
+ * [rows, ceil(k/4)] and gamma (one device float).
+ * Replaces physics.quantize_ternary (src/model/physics.py:13-51) and
+ * moe.quantize_ternary (src/model/moe.py:268-303; the scaled form is
+ * q * gamma, i.e. the same q with gamma applied by the consumer) followed by
+ * pack_ternary_weights (src/model/fht_cuda.py:65-93). */
+walsh_status walsh_ternary_quantize_pack(const float* w, int64_t rows, int k,
+                                         uint8_t* packed, float* gamma, void* stream);
+
+/* Unpack [rows, ceil(k/4)] -> float [rows, k].
+ * Replaces unpack_ternary_weights (src/model/fht_cuda.py:96-117). */
+walsh_status walsh_ternary_unpack(const uint8_t* packed, int64_t rows, int k, float* out,
+                                  void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Hadamard-32 algebra
+ * ------------------------------------------------------------------------- */
+
+/* y[t] = w_scale * beta . H . W_q . H . (alpha . x[t]) for ntok tokens, with x
+ * viewed as [32 groups, in_o] and y as [32, out_o]; H is the Sylvester
+ * Hadamard matrix / sqrt(32).  w2bit: [32, out_o, ceil(in_o/4)], alpha:
+ * [32, in_o], beta: [32, out_o] (float32).  Supported (in_o, out_o):
+ * 16x16, 64x64, 16x64, 64x16.
+ * Replaces HadamardLinear.forward (src/model/fht_cuda.py:489-519) and
+ * HadamardTernaryLinearTuple.forward (src/model/fht_cuda.py:550-569). */
+walsh_status walsh_hadamard_linear_fwd(const void* x, int x_dtype, int64_t ntok, int in_o,
+                                       int out_o, const uint8_t* w2bit, float w_scale,
+                                       const float* alpha, const float* beta, void* y,
+                                       int y_dtype, void* stream);
+
+/* Hadamard head mixing on token-major [ntok, n_head, hd]: each group of 32
+ * consecutive heads is mixed as y = beta . H (W_h x_h) H with one shared
+ * W [32, hd, hd] and beta [hd] (float32).  In-place is allowed.
+ * Replaces HadamardHeadMixerFused.forward (src/model/fht_cuda.py:652-670) as
+ * called per head group by CausalSelfAttention (src/model/chassis.py:468-477). */
+walsh_status walsh_head_mixer_fwd(const void* x, int dtype, int64_t ntok, int n_head, int hd,
+                                  const float* W, const float* beta, void* y, void* stream);
+
+/* Fused q/k/v projection + RoPE + KV-cache write for one attention layer.
+ * u: [B, T, C] (C = 32*in_o); w*_2bit/alpha/beta as walsh_hadamard_linear_fwd
+ * with in_o = out_o = C/32; rope_cos/sin: float [n_pos >= T, hd/2], row t
+ * rotating token t (the real and imaginary parts of the reference's
+ * freqs_cis buffer, offset by the caller to the first token's position).
+ * Writes q: [B, H, T, hd] and k, v into the caches [B, H, ctx, hd] at
+ * positions start_pos..start_pos+T-1.
+ * Replaces CausalSelfAttention.forward lines 426-440 (src/model/chassis.py):
+ * wq/wk/wv, apply_rotary_emb (src/model/chassis.py:339-345) and
+ * KVCache.update (src/model/chassis.py:297-322). */
+walsh_status walsh_attn_qkv_fwd(const void* u, int dtype, int B, int T, int C, int n_head,
+                                const uint8_t* wq_2bit, const float* wq_alpha, const float* wq_beta,
+                                const uint8_t* wk_2bit, const float* wk_alpha, const float* wk_beta,
+                                const uint8_t* wv_2bit, const float* wv_alpha, const float* wv_beta,
+                                const float* rope_cos, const float* rope_sin, int n_pos,
+                                int start_pos, void* q, void* k_cache, void* v_cache, int ctx,
+                                void* stream);
+
+/* Causal attention over the KV cache: query t (position start_pos+t) sees
+ * keys 0..start_pos+t, scale 1/sqrt(hd).  q: [B, H, T, hd]; caches
+ * [B, H, ctx, hd]; o: token-major [B, T, H, hd].  hd in {16, 32}.
+ * Replaces the scaled_dot_product_attention calls of
+ * CausalSelfAttention.forward (src/model/chassis.py:442-466). */
+walsh_status walsh_attn_fwd(const void* q, const void* k_cache, const void* v_cache, int dtype,
+                            int B, int H, int T, int hd, int ctx, int start_pos, void* o,
+                            void* stream);
+
+/* ---------------------------------------------------------------------------
+ * mHC residual streams (n_streams = 4)
+ * ------------------------------------------------------------------------- */
+
+/* Site prologue for x: [ntok, 4, C]:
+ *   r = rsqrt(mean(x^2) + map_eps) over all 4C values;
+ *   d = phi . (r x) with phi [24, 4C] = rows of H_pre | H_post | H_res;
+ *   H_pre = sigmoid(a0 d[0:4] + b[0:4]), H_post = 2 sigmoid(a1 d[4:8] + b[4:8]),
+ *   H_res = Sinkhorn_20(a2 d[8:24] + b[8:24]) (exp, then column and row
+ *   normalisation with eps 1e-8);
+ *   u = sum_j H_pre[j] x_j, then (if norm_w != NULL) the chassis RMSNorm
+ *   u / sqrt(mean(u^2) + norm_eps) * norm_w.
+ * mparams: float [28] = {a_pre, a_post, a_res, unused, b_pre[4], b_post[4],
+ * b_res[16]}.  Writes u [ntok, C] and hmix float [ntok, 24] =
+ * {H_pre[4], H_post[4], H_res[16] row-major}.
+ * Replaces ResidualStreamMapping.forward x3 and the pre-mix of
+ * mHCResidualStream.forward (src/model/mhc.py:283-318, 345-364) plus the
+ * attention_norm / ffn_norm RMSNorm of mHCLlamaBlock (src/model/mhc.py:514-523). */
+walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
+                           const float* mparams, float map_eps, const float* norm_w,
+                           float norm_eps, void* u, float* hmix, void* stream);
+
+/* Site epilogue: x_out[i] = sum_j H_res[i][j] x[j] + H_post[i] f for each
+ * token (x, x_out: [ntok, 4, C]; f: [ntok, C]; x_out may alias x).
+ * Replaces mHCResidualStream.forward lines 366-381 (src/model/mhc.py). */
+walsh_status walsh_mhc_post(const void* x, const void* f, const float* hmix, int dtype,
+                            int64_t ntok, int C, void* x_out, void* stream);
+
+/* Sinkhorn-Knopp projection of n 4x4 matrices (float32), exp then `iters`
+ * (column, row) normalisations with `eps`.
+ * Replaces SinkhornKnopp.forward (src/model/mhc.py:214-229). */
+walsh_status walsh_sinkhorn(const float* h, int64_t n, int iters, float eps, float* out,
+                            void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Hadamard MoE
+ * ------------------------------------------------------------------------- */
+
+/* Router + experts for u: [ntok, C], E = C/32 experts of hidden 128:
+ *   p = softmax(W2 silu(W1 u)) with w1t = W1 transposed, [C, C/4], and
+ *   w2 = W2 [E, C/4] (float32);
+ *   top_k largest p selected (ties to the lower index), weights w = p/sum;
+ *   y[e] = w_e * gd * Dq silu(gg Gq u_e) * (gu Uq u_e) for selected e, 0 else,
+ *   where u_e is the e-th 32-wide block and Gq/Uq [E,128,32], Dq [E,32,128]
+ *   are 2-bit ternary with gammas {gg, gu, gd} (device float[3]).
+ * Router-only call: gate/up/down/gammas all NULL (only the optional mask,
+ * probs and weights outputs are written).
+ * When weights_in (float [ntok, E]) is not NULL the router is skipped (w1t,
+ * w2 may be NULL) and
+ * every expert with a non-zero weight in it is evaluated with that weight
+ * (FastMoEExperts with caller-given routing weights; mask/probs/weights
+ * outputs are then not written).
+ * When fuse_post != 0, `y` is not written; instead the mHC site epilogue is
+ * applied: x_out = H_res x + H_post y (x, x_out [ntok, 4, C], hmix as
+ * walsh_mhc_map; x_out may alias x).  mask_out (uint8 [ntok, E]), probs_out
+ * and weights_out (float [ntok, E]) are optional (NULL to skip).
+ * Replaces HadamardRouter.forward (src/model/moe.py:418-447),
+ * FastMoEExperts.forward (src/model/moe.py:337-380) and HadamardMoE.forward
+ * (src/model/moe.py:512-542) followed by the ffn-site epilogue of
+ * mHCResidualStream.forward (src/model/mhc.py:366-381). */
+walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int top_k,
+                           const float* w1t, const float* w2, const uint8_t* gate_2bit,
+                           const uint8_t* up_2bit, const uint8_t* down_2bit, const float* gammas,
+                           void* y, int fuse_post, const void* x, const float* hmix, void* x_out,
+                           const float* weights_in, uint8_t* mask_out, float* probs_out,
+                           float* weights_out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Channel modulation (x viewed as [nseg, seg_len, C], segment = seg_len
+ * consecutive rows of the flat [rows, C] tensor, as the reference's
+ * x.view(B*n, T, C) at src/model/mhc.py:530)
+ * ------------------------------------------------------------------------- */
+
+/* Partial segment sums of the RMSNorm'd rows xn = x/sqrt(mean(x^2)+eps)*norm_w
+ * (xn = x when norm_w is NULL):
+ * partial[s, c, :] = sum of xn over rows [c*chunk, (c+1)*chunk) of segment s,
+ * chunk = walsh_chmod_chunk_rows(seg_len); partial: float [nseg, nchunk, C]. */
+int walsh_chmod_chunk_rows(int seg_len);
+walsh_status walsh_chmod_stats(const void* x, int dtype, int64_t nrows, int C, int seg_len,
+                               const float* norm_w, float norm_eps, float* partial, void* stream);
+
+/* bulk = (sum of partials)/seg_len; h = silu(g1 W1q bulk); m = g2 W2q h;
+ * scale = 1 + clamp(scale_temp, 0.1, 0.5) tanh(m[:E]); shift = m[E:].
+ * W1q [C/4, C], W2q [2E, C/4] 2-bit ternary, gammas device float[2].
+ * Replaces HadamardChannelModulation.forward lines 694-710 and
+ * _forward_ternary (src/model/moe.py:694-710, 753-762). */
+walsh_status walsh_chmod_mlp(const float* partial, int nseg, int seg_len, int C,
+                             const uint8_t* w1_2bit, const uint8_t* w2_2bit,
+                             const float* gammas, const float* scale_temp, float* scale,
+                             float* shift, void* stream);
+
+/* out = [x +] xn + r (xn * scale_b + 0.1 shift_b - xn) per 32-wide block b,
+ * r = residual_scale (0.5 in mHCLlamaBlock),
+ * with xn the RMSNorm'd row (xn = x when norm_w is NULL) and (scale, shift)
+ * [nseg, E] of the row's segment; the leading x is added when add_input != 0.
+ * out may alias x.
+ * Replaces the channel-modulation residual of mHCLlamaBlock.forward
+ * (src/model/mhc.py:528-532) with the modulation apply of
+ * src/model/moe.py:724-751. */
+walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrows, int C, int seg_len,
+                               const float* norm_w, float norm_eps, const float* scale,
+                               const float* shift, float residual_scale, int add_input, void* out,
+                               void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Dense helpers around the layer stack
+ * ------------------------------------------------------------------------- */
+
+/* Gather rows of a [V, D] table for token ids idx[ntok] (int64) into
+ * out [ntok, D].  Ids outside [0, V) write zeros and set *err to
+ * WALSH_ERR_INDEX (err may be NULL).
+ * Replaces tok_embeddings (nn.Embedding) followed by stream_proj, whose
+ * weights are folded into the table at load (src/model/mhc.py:634-640). */
+walsh_status walsh_embed_gather(const int64_t* idx, int64_t ntok, const void* table, int dtype,
+                                int64_t V, int D, void* out, int* err, void* stream);
+
+/* y[m, n] = sum_k x[m*ldx + k] w[n, k] + bias[n] (bias may be NULL).
+ * x, w, y each float32 or bfloat16.  Used for stream_merge, the tied output
+ * projection and the load-time embedding/stream_proj fold
+ * (src/model/mhc.py:654-676). */
+walsh_status walsh_linear_fwd(const void* x, int x_dtype, int64_t M, int K, int64_t ldx,
+                              const void* w, int w_dtype, int64_t N, const float* bias, void* y,
+                              int y_dtype, void* stream);
+
+/* Chassis RMSNorm: y = x / sqrt(mean(x^2) + eps) * w over rows of C.
+ * Replaces RMSNorm.forward (src/model/chassis.py:96-106). */
+walsh_status walsh_rmsnorm(const void* x, int dtype, int64_t rows, int C, const float* w,
+                           float eps, void* y, int y_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WALSH_H_ */

@@ -135,10 +135,10 @@ def hadamard_linear(x, w_latent, alpha, beta, dtype=np.float64):
     wq = quantize_ternary(w_latent).astype(dtype)
     out_o = wq.shape[1]
     H = hadamard_matrix(G, dtype=dtype)
-    xs = x.reshape(lead + (G, in_o)) * alpha.astype(dtype)
-    xm = np.einsum("...gi,gh->...hi", xs, H)
-    yp = np.einsum("...gi,goi->...go", xm, wq)
-    ym = np.einsum("...go,gh->...ho", yp, H)
+    xs = x.reshape(-1, G, in_o) * alpha.astype(dtype)
+    xm = np.matmul(H.T, xs)                                   # sum_g H[g,h] xs[g,i]
+    yp = np.matmul(xm.transpose(1, 0, 2), wq.transpose(0, 2, 1)).transpose(1, 0, 2)  # per-group W_g
+    ym = np.matmul(H.T, yp)
     return (ym * beta.astype(dtype)).reshape(lead + (G * out_o,))
 
 
@@ -147,9 +147,10 @@ def hadamard_head_mixer(x, W, beta, dtype=np.float64):
     (src/model/fht_cuda.py:652-670)."""
     x = np.asarray(x, dtype=dtype)
     H = hadamard_matrix(32, dtype=dtype)
-    xf = np.einsum("bhti,hg->bgti", x, H)
-    y = np.einsum("bhti,hio->bhto", xf, W.astype(dtype))
-    yf = np.einsum("bhti,hg->bgti", y, H)
+    B, _, Tn, D = x.shape
+    xf = np.matmul(H.T, x.reshape(B, 32, Tn * D)).reshape(B, 32, Tn, D)
+    y = np.matmul(xf, W.astype(dtype)[None])                  # per-head W_h
+    yf = np.matmul(H.T, y.reshape(B, 32, Tn * D)).reshape(B, 32, Tn, D)
     return yf * beta.astype(dtype)
 
 
@@ -202,11 +203,38 @@ def apply_rope(x, cos, sin):
     return out
 
 
-def sdpa(q, k, v, mask):
-    """scaled_dot_product_attention with a boolean keep-mask [Tq, Tk]; q,k,v [B, H, T, hd]."""
-    s = np.einsum("bhqd,bhkd->bhqk", q, k) / math.sqrt(q.shape[-1])
-    s = np.where(mask[None, None], s, -np.inf)
-    return np.einsum("bhqk,bhkd->bhqd", softmax(s, -1), v)
+_POOL = None
+
+
+def _pool():
+    global _POOL
+    if _POOL is None:
+        import concurrent.futures as cf
+        import os
+        _POOL = cf.ThreadPoolExecutor(max_workers=os.cpu_count() or 1)
+    return _POOL
+
+
+def sdpa(q, k, v, mask, block=256):
+    """scaled_dot_product_attention with a boolean keep-mask [Tq, Tk]; q,k,v [B, H, T, hd].
+    Evaluated per (batch, head) in query blocks over each block's visible key
+    prefix (numpy releases the GIL, so heads run on all host threads)."""
+    B, H, Tq, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    out = np.empty(q.shape[:-1] + (v.shape[-1],), dtype=np.result_type(q, v))
+    last = np.where(mask.any(1), mask.shape[1] - 1 - np.argmax(mask[:, ::-1], axis=1), -1)
+
+    def one(bh):
+        b, h = divmod(bh, H)
+        for q0 in range(0, Tq, block):
+            q1 = min(Tq, q0 + block)
+            kend = int(last[q0:q1].max()) + 1
+            s = (q[b, h, q0:q1] @ k[b, h, :kend].T) * scale
+            s = np.where(mask[q0:q1, :kend], s, -np.inf)
+            out[b, h, q0:q1] = softmax(s, -1) @ v[b, h, :kend]
+
+    list(_pool().map(one, range(B * H)))
+    return out
 
 
 def sinkhorn(Hm, n_iter=20, eps=1e-8):
@@ -252,9 +280,12 @@ def experts(xb, weights, gate_w, up_w, down_w):
     g = quantize_ternary_scaled(gate_w).astype(dt)
     u = quantize_ternary_scaled(up_w).astype(dt)
     dw = quantize_ternary_scaled(down_w).astype(dt)
-    gate = np.einsum("...ed,ehd->...eh", xb, g)
-    up = np.einsum("...ed,ehd->...eh", xb, u)
-    out = np.einsum("...eh,edh->...ed", silu(gate) * up, dw)
+    lead, E = xb.shape[:-2], xb.shape[-2]
+    xe = xb.reshape(-1, E, xb.shape[-1]).transpose(1, 0, 2)          # [E, N, 32]
+    gate = np.matmul(xe, g.transpose(0, 2, 1))                        # [E, N, 128]
+    up = np.matmul(xe, u.transpose(0, 2, 1))
+    out = np.matmul(silu(gate) * up, dw.transpose(0, 2, 1))           # [E, N, 32]
+    out = out.transpose(1, 0, 2).reshape(lead + (E, -1))
     return out * weights[..., None]
 
 

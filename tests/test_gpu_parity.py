@@ -1,0 +1,436 @@
+"""GPU parity: the sm_100a kernels (through libwalsh's C ABI) against the
+golden fixtures produced by the reference's own code and, at larger sizes,
+against the numpy oracle.
+
+Tolerances (max |ours - ref| / max |ref| unless stated):
+  * ternary packing / unpacking / top-k selection: bit-exact
+  * float32 activations: 1e-5 per op, 1e-4 for whole-model logits
+  * bfloat16 activations: 2e-2 max-abs on logits (fp32 reference), with the
+    routing sets matched; per-op 2e-2 relative.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import walsh_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+DEV = "cuda"
+
+
+def golden(name):
+    return np.load(os.path.join(GOLDEN, name + ".npz"))
+
+
+def T(a, dtype=torch.float32):
+    return torch.from_numpy(np.array(a)).to(DEV, dtype)
+
+
+def rel(a, b):
+    a = a.detach().float().cpu().numpy() if torch.is_tensor(a) else np.asarray(a)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def build_model(name, dtype=torch.float32):
+    from walsh_research_b200.model import WalshConfig, mHCWalsh
+    cfg, n, idx, sd = cases.model_inputs(name)
+    model = mHCWalsh(WalshConfig(**cfg), n_streams=n)
+    model.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in sd.items()}, strict=False)
+    model = model.to(DEV).eval()
+    model.compute_dtype = dtype
+    return cfg, n, idx, sd, model
+
+
+# ---------------------------------------------------------------------------
+# ternary weights
+# ---------------------------------------------------------------------------
+
+def test_pack_unpack_bit_exact():
+    from walsh_research_b200 import ops
+    d, g = cases.op_case("pack"), golden("pack")
+    for k in ("w_a", "w_b", "w_c"):
+        packed, _ = ops.quantize_pack(T(d[k]))
+        assert np.array_equal(packed.cpu().numpy(), g[k + "_packed"]), k
+        back = ops.unpack(T(g[k + "_packed"], torch.uint8), d[k].shape[-1])
+        assert np.array_equal(back.cpu().numpy(), d[k]), k
+
+
+def test_quantize_matches_reference():
+    from walsh_research_b200.model.moe import quantize_ternary as qs
+    from walsh_research_b200.model.physics import quantize_ternary as qu
+    d, g = cases.op_case("quant"), golden("quant")
+    np.testing.assert_allclose(qu(T(d["w_unscaled"])).cpu().numpy(), g["unscaled"], atol=2e-7, rtol=0)
+    ours = qs(T(d["w_scaled"])).cpu().numpy()
+    assert np.array_equal(np.sign(ours), np.sign(g["scaled"]))
+    np.testing.assert_allclose(ours, g["scaled"], rtol=3e-7, atol=0)
+
+
+def test_quantize_ragged_k_and_odd_rows():
+    from walsh_research_b200 import ops
+    rng = np.random.default_rng(5)
+    w = rng.normal(size=(7, 13, 171)).astype(np.float32)
+    packed, gamma = ops.quantize_pack(T(w))
+    assert packed.shape == (7, 13, 43)
+    np.testing.assert_array_equal(packed.cpu().numpy(), O.pack_ternary(O.quantize_ternary(w)))
+    np.testing.assert_allclose(gamma.item(), O.absmean_gamma(w), rtol=2e-7)
+
+
+# ---------------------------------------------------------------------------
+# Hadamard algebra
+# ---------------------------------------------------------------------------
+
+def _hlin(d):
+    from walsh_research_b200.model.fht_cuda import HadamardLinear
+    fin, fout = d["x"].shape[-1], d["weight"].shape[1] * 32
+    layer = HadamardLinear(fin, fout)
+    with torch.no_grad():
+        layer.weight.copy_(torch.from_numpy(d["weight"]))
+        layer.alpha.copy_(torch.from_numpy(d["alpha"]))
+        layer.beta.copy_(torch.from_numpy(d["beta"]))
+    return layer.to(DEV)
+
+
+@pytest.mark.parametrize("name", ["hlin_512", "hlin_512_latent", "hlin_2048", "hlin_512x2048", "hlin_2048x512"])
+def test_hadamard_linear_fp32(name):
+    d, g = cases.op_case(name), golden(name)
+    y = _hlin(d)(T(d["x"]))
+    assert y.dtype == torch.float32
+    assert rel(y, g["y"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", ["hlin_512", "hlin_2048"])
+def test_hadamard_linear_bf16(name):
+    d, g = cases.op_case(name), golden(name)
+    y = _hlin(d)(T(d["x"], torch.bfloat16))
+    assert y.dtype == torch.bfloat16
+    assert rel(y, g["y"]) < 2e-2
+
+
+@pytest.mark.parametrize("fin,fout,ntok", [(512, 512, 4096 + 3), (2048, 2048, 517), (512, 2048, 33),
+                                            (2048, 512, 1), (512, 512, 1)])
+def test_hadamard_linear_vs_oracle_sizes(fin, fout, ntok):
+    """Ragged token counts (tails of the token tiles) against the oracle."""
+    rng = np.random.default_rng(ntok)
+    d = dict(x=rng.normal(size=(1, ntok, fin)).astype(np.float32),
+             weight=rng.integers(-1, 2, size=(32, fout // 32, fin // 32)).astype(np.float32),
+             alpha=rng.uniform(0.5, 1.5, (32, fin // 32)).astype(np.float32),
+             beta=rng.uniform(0.1, 0.3, (32, fout // 32)).astype(np.float32))
+    y = _hlin(d)(T(d["x"]))
+    ref = O.hadamard_linear(d["x"], d["weight"], d["alpha"], d["beta"])
+    assert rel(y, ref) < 1e-5
+
+
+@pytest.mark.parametrize("name", ["headmix", "headmix32"])
+def test_head_mixer(name):
+    from walsh_research_b200.model.fht_cuda import HadamardHeadMixerFused
+    d, g = cases.op_case(name), golden(name)
+    m = HadamardHeadMixerFused(d["x"].shape[-1])
+    with torch.no_grad():
+        m.W.copy_(torch.from_numpy(d["W"]))
+        m.beta.copy_(torch.from_numpy(d["beta"]))
+    m = m.to(DEV)
+    assert rel(m(T(d["x"])), g["y"]) < 1e-5
+    assert rel(m(T(d["x"], torch.bfloat16)), g["y"]) < 2e-2
+
+
+# ---------------------------------------------------------------------------
+# mHC
+# ---------------------------------------------------------------------------
+
+def test_sinkhorn():
+    from walsh_research_b200.model import SinkhornKnopp
+    d, g = cases.op_case("sinkhorn"), golden("sinkhorn")
+    assert rel(SinkhornKnopp()(T(d["H"])), g["y"]) < 1e-5
+
+
+def test_stream_mapping():
+    from walsh_research_b200.model.mhc import ResidualStreamMapping
+    d, g = cases.op_case("mapping"), golden("mapping")
+    for kind in ("pre", "post", "res"):
+        m = ResidualStreamMapping(512, 4, kind)
+        with torch.no_grad():
+            m.phi.weight.copy_(torch.from_numpy(d[f"{kind}_phi"]))
+            m.alpha.copy_(torch.from_numpy(np.array(d[f"{kind}_alpha"])))
+            m.bias.copy_(torch.from_numpy(d[f"{kind}_bias"]))
+        h = m.to(DEV)(T(d["x"]))
+        assert h.shape == g[kind].shape
+        assert rel(h, g[kind]) < 1e-5, kind
+
+
+def test_residual_stream_site_matches_oracle():
+    """map (with norm) + an identity layer + post against the oracle."""
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model.mhc import MAP_EPS
+    rng = np.random.default_rng(3)
+    C, B, Tn = 512, 3, 37
+    x = (rng.normal(size=(B, Tn, 4, C)) * 0.5).astype(np.float32)
+    phi = rng.normal(0, 0.02, (24, 4 * C)).astype(np.float32)
+    al = rng.uniform(0.1, 0.5, 3).astype(np.float32)
+    bias = np.concatenate([rng.normal(0, .5, 8), (2 * np.eye(4) + rng.normal(0, .5, (4, 4))).ravel()]).astype(np.float32)
+    nw = (1 + rng.normal(0, .1, C)).astype(np.float32)
+    mp = np.concatenate([al, [0], bias]).astype(np.float32)
+    u, hmix = ops.mhc_map(T(x), T(phi), T(mp), MAP_EPS, T(nw), 1e-6)
+    xf = x.reshape(B, Tn, 4 * C).astype(np.float64)
+    hp = O.stream_mapping(xf, phi[:4], al[0], bias[:4], "pre")
+    ho = O.stream_mapping(xf, phi[4:8], al[1], bias[4:8], "post")
+    hr = O.stream_mapping(xf, phi[8:], al[2], bias[8:].reshape(4, 4), "res")
+    u_ref = O.rmsnorm((hp @ x.astype(np.float64))[:, :, 0], nw)
+    assert rel(hmix[..., :4], hp[..., 0, :]) < 1e-5
+    assert rel(hmix[..., 4:8], ho[..., 0, :]) < 1e-5
+    assert rel(hmix[..., 8:].reshape(B, Tn, 4, 4), hr) < 1e-5
+    assert rel(u, u_ref) < 1e-5
+    f = rng.normal(size=(B, Tn, C)).astype(np.float32)
+    xo = ops.mhc_post(T(x), T(f), hmix)
+    ref = hr @ x.astype(np.float64) + np.swapaxes(ho, -1, -2) @ f[:, :, None, :].astype(np.float64)
+    assert rel(xo, ref) < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# MoE and channel modulation
+# ---------------------------------------------------------------------------
+
+def _moe_module(d):
+    from walsh_research_b200.model import WalshConfig
+    from walsh_research_b200.model.moe import HadamardMoE
+    m = HadamardMoE(WalshConfig(n_embd=512), max_experts=int(d["top_k"]))
+    with torch.no_grad():
+        m.router.gate[0].weight.copy_(torch.from_numpy(d["gate0"]))
+        m.router.gate[2].weight.copy_(torch.from_numpy(d["gate2"]))
+        m.experts.gate_weights.copy_(torch.from_numpy(d["gate_w"]))
+        m.experts.up_weights.copy_(torch.from_numpy(d["up_w"]))
+        m.experts.down_weights.copy_(torch.from_numpy(d["down_w"]))
+    return m.to(DEV).eval()
+
+
+def test_moe_fp32():
+    d, g = cases.op_case("moe"), golden("moe")
+    m = _moe_module(d)
+    w, mask, probs = m.router(T(d["x"]))
+    assert np.array_equal(mask.cpu().numpy().astype(np.uint8), g["mask"])
+    assert rel(probs, g["probs"]) < 1e-5
+    assert rel(w, g["weights"]) < 1e-5
+    y = m(T(d["x"]))
+    assert rel(y, g["y"]) < 1e-5
+    assert np.array_equal(m._last_expert_mask.cpu().numpy().astype(np.uint8), g["mask"])
+    # experts with caller-given weights
+    ye = m.experts(T(d["x"]).view(2, 8, 16, 32), T(g["weights"]))
+    assert rel(ye.reshape(2, 8, 512), g["y"]) < 1e-5
+
+
+def test_moe_bf16_with_matched_routing():
+    d, g = cases.op_case("moe"), golden("moe")
+    m = _moe_module(d)
+    y = m(T(d["x"], torch.bfloat16))
+    mask = m._last_expert_mask.cpu().numpy().astype(np.uint8)
+    probs = g["probs"]
+    # tie rule: a differing selection is excused only where the k-th/(k+1)-th gap is < 1e-2 (bf16 input)
+    srt = -np.sort(-probs, axis=-1)
+    gap = srt[..., 5] - srt[..., 6]
+    bad = (mask != g["mask"]).any(-1) & (gap > 1e-2)
+    assert not bad.any()
+    same = (mask == g["mask"]).all(-1)
+    diff = np.abs(y.float().cpu().numpy() - g["y"])[same]
+    assert diff.max() / np.abs(g["y"]).max() < 2e-2
+
+
+def test_moe_large_vs_oracle_topk_sets():
+    """2000 tokens with router gaps from scaled logits: selection sets bit-exact."""
+    from walsh_research_b200 import ops
+    d = cases.op_case("moe")
+    rng = np.random.default_rng(9)
+    x = rng.normal(size=(1, 2000, 512)).astype(np.float32)
+    m = _moe_module(d)
+    w1t, w2, gp, up, dp, gam, k = m.kernel_args()
+    y, mask, probs, w = ops.moe(T(x), w1t, w2, gp, up, dp, gam, k, want_stats=True)
+    p = {"r.router.gate.0.weight": d["gate0"], "r.router.gate.2.weight": d["gate2"],
+         "r.experts.gate_weights": d["gate_w"], "r.experts.up_weights": d["up_w"], "r.experts.down_weights": d["down_w"]}
+    y_ref, mask_ref, probs_ref = O.moe(x.astype(np.float64), p, "r.", 6)
+    srt = -np.sort(-probs_ref, axis=-1)
+    tie = (srt[..., 5] - srt[..., 6]) < 1e-6
+    diff = (mask.cpu().numpy() != mask_ref).any(-1)
+    assert not (diff & ~tie).any()
+    ok = ~diff
+    assert np.abs(y.cpu().numpy() - y_ref)[ok].max() / np.abs(y_ref).max() < 1e-5
+
+
+def test_channel_modulation():
+    from walsh_research_b200.model.moe import HadamardChannelModulation
+    d, g = cases.op_case("chmod"), golden("chmod")
+    m = HadamardChannelModulation(512, use_ternary=True, residual_scale=0.5)
+    with torch.no_grad():
+        m.context_mlp[0].weight.copy_(torch.from_numpy(d["w0"]))
+        m.context_mlp[2].weight.copy_(torch.from_numpy(d["w2"]))
+        m.scale_temp.copy_(torch.from_numpy(d["scale_temp"]))
+    m = m.to(DEV)
+    assert rel(m(T(d["x"])), g["y"]) < 1e-5
+    assert rel(m(T(d["x"], torch.bfloat16)), g["y"]) < 2e-2
+
+
+def test_channel_modulation_long_segments_vs_oracle():
+    """Segments longer than one stats chunk (ragged last chunk)."""
+    from walsh_research_b200.model.moe import HadamardChannelModulation
+    rng = np.random.default_rng(4)
+    x = rng.normal(size=(3, 150, 512)).astype(np.float32)
+    w0 = rng.integers(-1, 2, (128, 512)).astype(np.float32)
+    w2 = rng.normal(size=(32, 128)).astype(np.float32)
+    m = HadamardChannelModulation(512)
+    with torch.no_grad():
+        m.context_mlp[0].weight.copy_(torch.from_numpy(w0))
+        m.context_mlp[2].weight.copy_(torch.from_numpy(w2))
+        m.scale_temp.fill_(0.25)
+    y = m.to(DEV)(T(x))
+    assert rel(y, O.channel_mod(x.astype(np.float64), w0, w2, np.array([0.25]))) < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# whole model
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name", ["model_h512", "model_h512_noscale", "model_h2048"])
+def test_model_fp32_matches_reference(name):
+    cfg, n, idx, sd, model = build_model(name)
+    g = golden(name)
+    with torch.no_grad():
+        logits, _, h = model(T(idx, torch.int64), return_hidden=True)
+        logits_last, _ = model(T(idx, torch.int64))
+    assert rel(h, g["hidden"]) < 1e-4
+    assert rel(logits, g["logits"]) < 1e-4
+    assert rel(logits_last, g["logits"]) < 1e-4
+    if "router_mask" in g.files:
+        for l, layer in enumerate(model.layers):
+            mask = layer.feed_forward._last_expert_mask.cpu().numpy().astype(np.uint8)
+            assert np.array_equal(mask, g["router_mask"][l]), l
+    model.check_token_ids()
+
+
+def test_model_bf16_matches_reference():
+    cfg, n, idx, sd, model = build_model("model_h512", torch.bfloat16)
+    g = golden("model_h512")
+    with torch.no_grad():
+        logits, _ = model(T(idx, torch.int64))
+    masks = [layer.feed_forward._last_expert_mask.cpu().numpy().astype(np.uint8) for layer in model.layers]
+    if all(np.array_equal(m, g["router_mask"][l]) for l, m in enumerate(masks)):
+        assert float(np.abs(logits.cpu().numpy() - g["logits"]).max()) < 2e-2
+    else:
+        pytest.skip("bf16 routing diverged from the fp32 reference on a near-tie")
+
+
+def test_model_autocast_selects_bf16():
+    cfg, n, idx, sd, model = build_model("model_h512")
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        logits, _ = model(T(idx, torch.int64))
+    g = golden("model_h512")
+    assert float(np.abs(logits.cpu().numpy() - g["logits"]).max()) < 2e-2
+
+
+def test_model_larger_batch_vs_oracle():
+    """B4 x T96 (several attention tiles, chmod chunks) against the oracle."""
+    cfg, n, _, sd, model = build_model("model_h512")
+    cfg = dict(cfg, block_size=128)
+    from walsh_research_b200.model import WalshConfig, mHCWalsh
+    model = mHCWalsh(WalshConfig(**cfg), n_streams=n)
+    model.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in sd.items()}, strict=False)
+    model = model.to(DEV).eval()
+    idx = np.random.default_rng(8).integers(0, cfg["vocab_size"], (4, 96))
+    with torch.no_grad():
+        logits, _, h = model(T(idx, torch.int64), return_hidden=True)
+    ref_logits, ref_h = O.mhc_walsh_forward(cfg, sd, idx, n)
+    assert rel(h, ref_h) < 1e-4
+    assert rel(logits, ref_logits) < 1e-4
+
+
+def test_cached_decode_matches_reference():
+    from walsh_research_b200.model import KVCache, WalshConfig, mHCWalsh
+    cfg, n, toks, T0, steps, sd = cases.decode_inputs("decode_h512")
+    model = mHCWalsh(WalshConfig(**cfg), n_streams=n)
+    model.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in sd.items()}, strict=False)
+    model = model.to(DEV).eval()
+    C, H = cfg["n_embd"], cfg["n_head"]
+    cache = KVCache(cfg["n_layer"], cfg["block_size"], H, C // H, torch.device(DEV), torch.float32)
+    outs = []
+    with torch.no_grad():
+        lg, _ = model(T(toks[:, :T0], torch.int64), kv_cache=cache, start_pos=0)
+        cache.increment(T0)
+        outs.append(lg.cpu().numpy())
+        for s in range(steps):
+            lg, _ = model(T(toks[:, T0 + s:T0 + s + 1], torch.int64), kv_cache=cache, start_pos=cache.cached_len)
+            cache.increment(1)
+            outs.append(lg.cpu().numpy())
+    assert rel(np.concatenate(outs, axis=1), golden("decode_h512")["logits"]) < 1e-4
+
+
+def test_batched_decode_equals_per_sequence():
+    """B=3 sequences decoded together equal each sequence decoded alone (B=1)."""
+    from walsh_research_b200.model import KVCache, WalshConfig, mHCWalsh
+    cfg, n, _, T0, steps, sd = cases.decode_inputs("decode_h512")
+    model = mHCWalsh(WalshConfig(**cfg), n_streams=n)
+    model.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in sd.items()}, strict=False)
+    model = model.to(DEV).eval()
+    C, H = cfg["n_embd"], cfg["n_head"]
+    toks = np.random.default_rng(2).integers(0, cfg["vocab_size"], (3, T0 + steps))
+
+    def run(tk):
+        cache = KVCache(cfg["n_layer"], cfg["block_size"], H, C // H, torch.device(DEV), torch.float32,
+                        batch_size=tk.shape[0])
+        outs = []
+        with torch.no_grad():
+            lg, _ = model(T(tk[:, :T0], torch.int64), kv_cache=cache, start_pos=0)
+            cache.increment(T0)
+            outs.append(lg)
+            for s in range(steps):
+                lg, _ = model(T(tk[:, T0 + s:T0 + s + 1], torch.int64), kv_cache=cache, start_pos=cache.cached_len)
+                cache.increment(1)
+                outs.append(lg)
+        return torch.cat(outs, 1).cpu().numpy()
+
+    together = run(toks)
+    for b in range(3):
+        alone = run(toks[b:b + 1])
+        assert rel(together[b:b + 1], alone) < 1e-5
+
+
+def test_out_of_range_token_id_is_reported():
+    cfg, n, idx, sd, model = build_model("model_h512")
+    bad = idx.copy()
+    bad[0, 3] = cfg["vocab_size"] + 5
+    with torch.no_grad():
+        model(T(bad, torch.int64))
+    with pytest.raises(IndexError):
+        model.check_token_ids()
+
+
+# ---------------------------------------------------------------------------
+# attention kernels directly (tensor-core bf16 path and fp32 path)
+# ---------------------------------------------------------------------------
+
+def _attn_ref(q, k, v, start_pos):
+    """numpy causal attention of queries at positions start_pos.. over keys 0..start_pos+T-1."""
+    B, H, Tq, D = q.shape
+    Tk = start_pos + Tq
+    mask = np.tril(np.ones((Tq, Tk), dtype=bool), k=start_pos)
+    out = O.sdpa(q.astype(np.float64), k[:, :, :Tk].astype(np.float64), v[:, :, :Tk].astype(np.float64), mask)
+    return out.transpose(0, 2, 1, 3)  # token-major [B, T, H, D]
+
+
+@pytest.mark.parametrize("hd,Tq,start,ctx", [(16, 1000, 0, 1000), (32, 300, 0, 300), (16, 77, 130, 256),
+                                             (32, 5, 60, 70), (16, 2, 40, 48), (16, 129, 0, 129)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_attention_kernel_vs_oracle(hd, Tq, start, ctx, dtype):
+    from walsh_research_b200 import ops
+    rng = np.random.default_rng(hd * 1000 + Tq)
+    B, H = 2, 3
+    q = rng.normal(size=(B, H, Tq, hd)).astype(np.float32) * 2
+    k = rng.normal(size=(B, H, ctx, hd)).astype(np.float32)
+    v = rng.normal(size=(B, H, ctx, hd)).astype(np.float32)
+    qt, kt, vt = T(q, dtype), T(k, dtype), T(v, dtype)
+    o = ops.attention(qt, kt, vt, start)
+    # reference on the same (rounded) inputs
+    ref = _attn_ref(qt.float().cpu().numpy(), kt.float().cpu().numpy(), vt.float().cpu().numpy(), start)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert rel(o, ref) < tol

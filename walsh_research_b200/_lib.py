@@ -1,0 +1,116 @@
+"""ctypes binding of libwalsh.so (the C ABI declared in include/walsh.h).
+
+The library is loaded from the package directory (built in-tree by
+``python -m walsh_research_b200.build``).  There is no fallback: if it is
+missing, every op raises.  Every wrapper checks the returned walsh_status and
+raises ``WalshError`` with the library's own message.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_float, c_int, c_int64, c_void_p
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libwalsh.so")
+
+F32, BF16 = 0, 1
+P = c_void_p
+
+# name -> argument types (restype is int/walsh_status unless listed in _RESTYPE)
+SIGNATURES = {
+    "walsh_status_str": [c_int],
+    "walsh_abi_version": [],
+    "walsh_ternary_quantize_pack": [P, c_int64, c_int, P, P, P],
+    "walsh_ternary_unpack": [P, c_int64, c_int, P, P],
+    "walsh_hadamard_linear_fwd": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, P, c_int, P],
+    "walsh_head_mixer_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P],
+    "walsh_attn_qkv_fwd": [P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_int, c_int,
+                           P, P, P, c_int, P],
+    "walsh_attn_fwd": [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P],
+    "walsh_mhc_map": [P, c_int, c_int64, c_int, P, P, c_float, P, c_float, P, P, P],
+    "walsh_mhc_post": [P, P, P, c_int, c_int64, c_int, P, P],
+    "walsh_sinkhorn": [P, c_int64, c_int, c_float, P, P],
+    "walsh_moe_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, P, c_int, P, P, P, P, P, P, P, P],
+    "walsh_chmod_chunk_rows": [c_int],
+    "walsh_chmod_stats": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P],
+    "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],
+    "walsh_chmod_apply": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, c_float, c_int, P, P],
+    "walsh_embed_gather": [P, c_int64, P, c_int, c_int64, c_int, P, P, P],
+    "walsh_linear_fwd": [P, c_int, c_int64, c_int, c_int64, P, c_int, c_int64, P, P, c_int, P],
+    "walsh_rmsnorm": [P, c_int, c_int64, c_int, P, c_float, P, c_int, P],
+}
+_RESTYPE = {"walsh_status_str": ctypes.c_char_p}
+# entry points that return a plain int rather than a status
+_PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows"}
+
+
+class WalshError(RuntimeError):
+    def __init__(self, name: str, code: int, msg: str):
+        super().__init__(f"{name} failed: {msg} (status {code})")
+        self.code = code
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libwalsh.so once.  Raises if the library was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libwalsh.so not found at {LIB_PATH}; build it with "
+                               f"`python -m walsh_research_b200.build` (no CPU fallback exists)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPE.get(name, c_int)
+        _lib = L
+    return _lib
+
+
+def status_str(code: int) -> str:
+    return lib().walsh_status_str(code).decode()
+
+
+def call(name: str, *args) -> int:
+    rc = getattr(lib(), name)(*args)
+    if name in _PLAIN_INT or name in _RESTYPE:
+        return rc
+    if rc != 0:
+        raise WalshError(name, rc, status_str(rc))
+    return rc
+
+
+# ---------------------------------------------------------------------------
+# tensor helpers
+# ---------------------------------------------------------------------------
+
+def ptr(t):
+    """Device pointer of a tensor (None -> NULL)."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def dcode(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return F32
+    if dtype == torch.bfloat16:
+        return BF16
+    raise TypeError(f"walsh kernels take float32 or bfloat16 activations, got {dtype}")
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def require_cuda(*tensors):
+    """The hot path runs only on CUDA tensors; there is no CPU fallback."""
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("walsh_research_b200 runs on CUDA devices only (no CPU fallback); "
+                               f"got a tensor on {t.device}")

@@ -1,0 +1,341 @@
+// Causal attention over the KV cache (CausalSelfAttention, src/model/chassis.py:442-466).
+//
+// Layouts: q [B, H, T, hd]; caches [B, H, ctx, hd]; o token-major [B, T, H, hd]
+// so that the head mixer / wo kernels read whole token rows.  Query t sits at
+// position start_pos + t and sees keys 0..start_pos+t (is_causal for the
+// prompt, the tril(total-T) mask for cached steps).  Scores use exp2 with the
+// 1/sqrt(hd) scale pre-multiplied by log2(e).
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "mma.cuh"
+
+namespace walsh {
+
+// Prefill: CTA = (64-query tile, head, batch); one thread per query, keys
+// staged through shared memory 64 at a time.
+template <int HD, typename T>
+__global__ void __launch_bounds__(64)
+attn_prefill_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, int H, int Tq,
+                    int ctx, int start_pos, float scale_log2, T* __restrict__ o) {
+  constexpr int QT = 64, KT = 64;
+  __shared__ float ks[KT][HD];
+  __shared__ float vs[KT][HD];
+  const int b = blockIdx.z, h = blockIdx.y, qt = blockIdx.x;
+  const int t = qt * QT + threadIdx.x;
+  const bool valid = t < Tq;
+  const int qpos = start_pos + t;
+  const size_t bh = (size_t)b * H + h;
+  float qv[HD], acc[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    qv[d] = valid ? to_f(q[(bh * Tq + t) * HD + d]) * scale_log2 : 0.f;
+    acc[d] = 0.f;
+  }
+  float m = -CUDART_INF_F, l = 0.f;
+  const int kend = start_pos + min((qt + 1) * QT, Tq);  // one past the last key any query here sees
+  const T* kb = kc + bh * ctx * HD;
+  const T* vb = vc + bh * ctx * HD;
+  for (int k0 = 0; k0 < kend; k0 += KT) {
+    const int kn = min(KT, kend - k0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < KT * HD; i += QT) {
+      const int j = i / HD, d = i - j * HD;
+      const bool in = j < kn;
+      ks[j][d] = in ? to_f(kb[(size_t)(k0 + j) * HD + d]) : 0.f;
+      vs[j][d] = in ? to_f(vb[(size_t)(k0 + j) * HD + d]) : 0.f;
+    }
+    __syncthreads();
+    float s[KT];
+    float mt = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < KT; ++j) {
+      float dot = 0.f;
+#pragma unroll
+      for (int d = 0; d < HD; ++d) dot = fmaf(qv[d], ks[j][d], dot);
+      s[j] = (j < kn && k0 + j <= qpos) ? dot : -CUDART_INF_F;
+      mt = fmaxf(mt, s[j]);
+    }
+    const float mnew = fmaxf(m, mt);
+    if (mnew == -CUDART_INF_F) continue;
+    const float corr = exp2f(m - mnew);
+    l *= corr;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) acc[d] *= corr;
+#pragma unroll
+    for (int j = 0; j < KT; ++j) {
+      const float p = exp2f(s[j] - mnew);
+      l += p;
+#pragma unroll
+      for (int d = 0; d < HD; ++d) acc[d] = fmaf(p, vs[j][d], acc[d]);
+    }
+    m = mnew;
+  }
+  if (valid) {
+    const float inv = 1.0f / l;
+    T* op = o + (((size_t)b * Tq + t) * H + h) * HD;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) op[d] = from_f<T>(acc[d] * inv);
+  }
+}
+
+// Few queries (decode): CTA = (query, head, batch); 128 threads stride over
+// the keys with private online-softmax state, merged through shared memory.
+template <int HD, typename T>
+__global__ void __launch_bounds__(128)
+attn_decode_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, int H, int Tq,
+                   int ctx, int start_pos, float scale_log2, T* __restrict__ o) {
+  constexpr int NT = 128;
+  __shared__ float sm[NT], sl[NT];
+  __shared__ float sacc[NT / 32][HD];
+  const int b = blockIdx.z, h = blockIdx.y, t = blockIdx.x;
+  const size_t bh = (size_t)b * H + h;
+  const int nk = start_pos + t + 1;
+  float qv[HD], acc[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    qv[d] = to_f(q[(bh * Tq + t) * HD + d]) * scale_log2;
+    acc[d] = 0.f;
+  }
+  float m = -CUDART_INF_F, l = 0.f;
+  const T* kb = kc + bh * ctx * HD;
+  const T* vb = vc + bh * ctx * HD;
+  for (int k = threadIdx.x; k < nk; k += NT) {
+    float dot = 0.f;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) dot = fmaf(qv[d], to_f(kb[(size_t)k * HD + d]), dot);
+    const float mnew = fmaxf(m, dot);
+    const float corr = exp2f(m - mnew);
+    const float p = exp2f(dot - mnew);
+    l = l * corr + p;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) acc[d] = fmaf(p, to_f(vb[(size_t)k * HD + d]), acc[d] * corr);
+    m = mnew;
+  }
+  sm[threadIdx.x] = m;
+  __syncthreads();
+  float M = -CUDART_INF_F;
+  for (int i = 0; i < NT; ++i) M = fmaxf(M, sm[i]);
+  const float f = (m == -CUDART_INF_F) ? 0.f : exp2f(m - M);
+  sl[threadIdx.x] = l * f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    const float v = warp_sum(acc[d] * f);
+    if (lane == 0) sacc[warp][d] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < HD) {
+    float L = 0.f;
+    for (int i = 0; i < NT; ++i) L += sl[i];
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) v += sacc[w][threadIdx.x];
+    o[(((size_t)b * Tq + t) * H + h) * HD + threadIdx.x] = from_f<T>(v / L);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// bf16 prefill on the tensor cores (flash-attention dataflow with mma.sync):
+// CTA = 128 queries of one (batch, head), 8 warps x 16 query rows; K/V tiles
+// of 64 keys double-buffered in shared memory by cp.async; S = Q K^T and
+// O += P V with m16n8k16 bf16 MMAs (fp32 accumulate), the S accumulators
+// re-packed in registers as the A operand of P V; online softmax in exp2.
+// ---------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(256)
+attn_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
+                const __nv_bfloat16* __restrict__ vc, int H, int Tq, int ctx, int start_pos, float scale_log2,
+                __nv_bfloat16* __restrict__ o) {
+  constexpr int QT = 128, KT = 64, LD = HD + 8;  // padded rows: conflict-free ldmatrix
+  constexpr int CH = HD / 8;                     // 16-byte chunks per row
+  __shared__ __align__(16) __nv_bfloat16 Qs[QT][LD];
+  __shared__ __align__(16) __nv_bfloat16 Ks[2][KT][LD];
+  __shared__ __align__(16) __nv_bfloat16 Vs[2][KT][LD];
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int q0 = (gridDim.x - 1 - blockIdx.x) * QT;  // longest (latest) query tiles first
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const size_t bh = (size_t)b * H + h;
+  const __nv_bfloat16* qb = q + bh * Tq * HD;
+  const __nv_bfloat16* kb = kc + bh * ctx * HD;
+  const __nv_bfloat16* vb = vc + bh * ctx * HD;
+  const int kend = start_pos + min(q0 + QT, Tq);  // keys [0, kend) are visible to some query here
+  const int nkt = (kend + KT - 1) / KT;
+
+  for (int i = tid; i < QT * CH; i += 256) {
+    const int r = i / CH, c = i - r * CH;
+    const bool in = q0 + r < Tq;
+    cp_async16(&Qs[r][c * 8], qb + (size_t)(in ? q0 + r : 0) * HD + c * 8, in ? 16 : 0);
+  }
+  auto load_kv = [&](int kt, int buf) {
+    for (int i = tid; i < 2 * KT * CH; i += 256) {
+      const int which = i / (KT * CH), j = i - which * KT * CH;
+      const int r = j / CH, c = j - r * CH;
+      const int key = kt * KT + r;
+      const bool in = key < kend;
+      const __nv_bfloat16* src = (which ? vb : kb) + (size_t)(in ? key : 0) * HD + c * 8;
+      cp_async16(which ? &Vs[buf][r][c * 8] : &Ks[buf][r][c * 8], src, in ? 16 : 0);
+    }
+  };
+  load_kv(0, 0);
+  cp_async_commit();
+
+  const int qrow0 = warp * 16;
+  const int qp_lo = start_pos + q0 + qrow0 + g;  // query positions of this thread's two rows
+  const int qp_hi = qp_lo + 8;
+  const int qp_warp_max = start_pos + q0 + qrow0 + 15;
+  float m_lo = -CUDART_INF_F, m_hi = -CUDART_INF_F, l_lo = 0.f, l_hi = 0.f;
+  float oacc[HD / 8][4];
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
+  uint32_t qf[HD / 16][4];
+
+  for (int kt = 0; kt < nkt; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < nkt) load_kv(kt + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (kt == 0) {
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks)
+        ldsm_x4(qf[ks], &Qs[qrow0 + (lane & 15)][ks * 16 + (lane >> 4) * 8]);
+    }
+    if (kt * KT <= qp_warp_max) {  // some key of this tile is visible to this warp's rows
+      float s[KT / 8][4];
+#pragma unroll
+      for (int n = 0; n < KT / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks)
+#pragma unroll
+        for (int np = 0; np < KT / 16; ++np) {
+          uint32_t kf[4];
+          ldsm_x4(kf, &Ks[buf][np * 16 + (lane & 7) + ((lane >> 4) << 3)][ks * 16 + ((lane >> 3) & 1) * 8]);
+          mma_bf16(s[2 * np], qf[ks], kf[0], kf[1]);
+          mma_bf16(s[2 * np + 1], qf[ks], kf[2], kf[3]);
+        }
+      const bool diag = (kt + 1) * KT - 1 > start_pos + q0 + qrow0;  // tile may hold masked keys
+      float mt_lo = -CUDART_INF_F, mt_hi = -CUDART_INF_F;
+#pragma unroll
+      for (int n = 0; n < KT / 8; ++n) {
+        const int key = kt * KT + n * 8 + 2 * t4;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float a = s[n][e] * scale_log2, c = s[n][2 + e] * scale_log2;
+          if (diag) {
+            if (key + e > qp_lo) a = -CUDART_INF_F;
+            if (key + e > qp_hi) c = -CUDART_INF_F;
+          }
+          s[n][e] = a;
+          s[n][2 + e] = c;
+          mt_lo = fmaxf(mt_lo, a);
+          mt_hi = fmaxf(mt_hi, c);
+        }
+      }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        mt_lo = fmaxf(mt_lo, __shfl_xor_sync(0xffffffffu, mt_lo, off));
+        mt_hi = fmaxf(mt_hi, __shfl_xor_sync(0xffffffffu, mt_hi, off));
+      }
+      const float mn_lo = fmaxf(m_lo, mt_lo), mn_hi = fmaxf(m_hi, mt_hi);
+      // rows with no visible key yet keep m = -inf; use 0 as the subtrahend so exp2 gives 0, not NaN
+      const float sub_lo = mn_lo == -CUDART_INF_F ? 0.f : mn_lo;
+      const float sub_hi = mn_hi == -CUDART_INF_F ? 0.f : mn_hi;
+      const float corr_lo = exp2f(m_lo - sub_lo), corr_hi = exp2f(m_hi - sub_hi);
+      m_lo = mn_lo;
+      m_hi = mn_hi;
+      float rs_lo = 0.f, rs_hi = 0.f;
+      uint32_t pf[KT / 16][4];
+#pragma unroll
+      for (int n = 0; n < KT / 8; ++n) {
+        const float p0 = exp2f(s[n][0] - sub_lo), p1 = exp2f(s[n][1] - sub_lo);
+        const float p2 = exp2f(s[n][2] - sub_hi), p3 = exp2f(s[n][3] - sub_hi);
+        rs_lo += p0 + p1;
+        rs_hi += p2 + p3;
+        pf[n >> 1][(n & 1) * 2 + 0] = pack_bf16(p0, p1);
+        pf[n >> 1][(n & 1) * 2 + 1] = pack_bf16(p2, p3);
+      }
+      l_lo = l_lo * corr_lo + rs_lo;
+      l_hi = l_hi * corr_hi + rs_hi;
+#pragma unroll
+      for (int i = 0; i < HD / 8; ++i) {
+        oacc[i][0] *= corr_lo; oacc[i][1] *= corr_lo;
+        oacc[i][2] *= corr_hi; oacc[i][3] *= corr_hi;
+      }
+#pragma unroll
+      for (int kk = 0; kk < KT / 16; ++kk) {
+        // A operand = P[16 rows][16 keys]: registers {tile 2kk (c0c1), tile 2kk (c2c3), tile 2kk+1 (c0c1), tile 2kk+1 (c2c3)}
+        const uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
+#pragma unroll
+        for (int dp = 0; dp < HD / 16; ++dp) {
+          uint32_t vf[4];
+          ldsm_x4_t(vf, &Vs[buf][kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8]);
+          mma_bf16(oacc[2 * dp], a, vf[0], vf[1]);
+          mma_bf16(oacc[2 * dp + 1], a, vf[2], vf[3]);
+        }
+      }
+    }
+    __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
+  }
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
+  }
+  const float inv_lo = 1.0f / l_lo, inv_hi = 1.0f / l_hi;
+  const int t_lo = q0 + qrow0 + g, t_hi = t_lo + 8;
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) {
+    const int d = i * 8 + 2 * t4;
+    if (t_lo < Tq)
+      *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + t_lo) * H + h) * HD + d) =
+          pack_bf16(oacc[i][0] * inv_lo, oacc[i][1] * inv_lo);
+    if (t_hi < Tq)
+      *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + t_hi) * H + h) * HD + d) =
+          pack_bf16(oacc[i][2] * inv_hi, oacc[i][3] * inv_hi);
+  }
+}
+
+template <int HD, typename T>
+static int launch_attn(const void* q, const void* kc, const void* vc, int B, int H, int Tq, int ctx,
+                       int start_pos, void* o, cudaStream_t s) {
+  const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
+  const bool aligned = ((((uintptr_t)q) | ((uintptr_t)kc) | ((uintptr_t)vc)) & 15u) == 0;
+  if (sizeof(T) == 2 && Tq > 4 && aligned) {
+    dim3 grid((Tq + 127) / 128, H, B);
+    attn_mma_kernel<HD><<<grid, 256, 0, s>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)kc,
+                                             (const __nv_bfloat16*)vc, H, Tq, ctx, start_pos, scale_log2,
+                                             (__nv_bfloat16*)o);
+    return launch_status();
+  }
+  if (Tq <= 4) {
+    dim3 grid(Tq, H, B);
+    attn_decode_kernel<HD, T><<<grid, 128, 0, s>>>((const T*)q, (const T*)kc, (const T*)vc, H, Tq, ctx,
+                                                  start_pos, scale_log2, (T*)o);
+  } else {
+    dim3 grid((Tq + 63) / 64, H, B);
+    attn_prefill_kernel<HD, T><<<grid, 64, 0, s>>>((const T*)q, (const T*)kc, (const T*)vc, H, Tq, ctx,
+                                                  start_pos, scale_log2, (T*)o);
+  }
+  return launch_status();
+}
+
+}  // namespace walsh
+
+using namespace walsh;
+
+extern "C" walsh_status walsh_attn_fwd(const void* q, const void* k_cache, const void* v_cache, int dtype,
+                                       int B, int H, int T, int hd, int ctx, int start_pos, void* o,
+                                       void* stream) {
+  if (int e = injected("attn_fwd")) return e;
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_ARG(q && k_cache && v_cache && o);
+  WALSH_CHECK_SHAPE(B > 0 && H > 0 && T > 0 && start_pos >= 0 && start_pos + T <= ctx);
+  WALSH_CHECK_SHAPE(B <= 65535 && H <= 65535);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (hd == 16) return dtype == WALSH_F32 ? launch_attn<16, float>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s)
+                                          : launch_attn<16, __nv_bfloat16>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s);
+  if (hd == 32) return dtype == WALSH_F32 ? launch_attn<32, float>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s)
+                                          : launch_attn<32, __nv_bfloat16>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s);
+  return WALSH_ERR_SHAPE;
+}

@@ -1,0 +1,181 @@
+// Channel modulation (HadamardChannelModulation, src/model/moe.py:681-762,
+// as used by mHCLlamaBlock.forward, src/model/mhc.py:528-532).
+//
+// The block views the stream state [B, T, n, C] as [B*n, T, C]: a "segment"
+// is seg_len consecutive rows of the flat [B*T*n, C] tensor.  Three steps:
+//   stats: partial sums over row chunks of RMSNorm(x) (chassis RMSNorm with
+//          the channel_mod_norm weight), written per (segment, chunk) so the
+//          reduction order is fixed;
+//   mlp:   bulk mean -> scaled-ternary MLP -> per-(segment, block) scale/shift;
+//   apply: out = x + xn + 0.5 * (xn * scale + 0.1 * shift - xn).
+#include "common.cuh"
+
+namespace walsh {
+
+constexpr int kChunkRows = 64;
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+chmod_stats_kernel(const T* __restrict__ x, int C, int seg_len, const float* __restrict__ w, float eps,
+                   float* __restrict__ partial) {
+  __shared__ float inv[kChunkRows];
+  const int seg = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int r0 = ch * kChunkRows;
+  const int nr = min(kChunkRows, seg_len - r0);
+  const int64_t row0 = (int64_t)seg * seg_len + r0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < nr; r += 8) {
+    const T* xr = x + (row0 + r) * C;
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float v = to_f(xr[c]);
+      s = fmaf(v, v, s);
+    }
+    s = warp_sum(s);
+    if (lane == 0) inv[r] = w ? rsqrtf(s / (float)C + eps) : 1.0f;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += 256) {
+    float acc = 0.f;
+    for (int r = 0; r < nr; ++r) acc = fmaf(to_f(x[(row0 + r) * C + c]), inv[r], acc);
+    partial[((size_t)seg * nch + ch) * C + c] = w ? acc * __ldg(w + c) : acc;
+  }
+}
+
+// One CTA per segment.
+__global__ void __launch_bounds__(256)
+chmod_mlp_kernel(const float* __restrict__ partial, int nch, int seg_len, int C, const uint8_t* __restrict__ w1,
+                 const uint8_t* __restrict__ w2, const float* __restrict__ gammas,
+                 const float* __restrict__ scale_temp, float* __restrict__ scale, float* __restrict__ shift) {
+  extern __shared__ float4 smem4[];
+  float* bulk = reinterpret_cast<float*>(smem4);  // [C]
+  float* hid = bulk + C;                           // [C/4]
+  const int seg = blockIdx.x;
+  const int HIDN = C / 4, E = C / 32;
+  for (int c = threadIdx.x; c < C; c += 256) {
+    float s = 0.f;
+    for (int k = 0; k < nch; ++k) s += partial[((size_t)seg * nch + k) * C + c];
+    bulk[c] = s / (float)seg_len;
+  }
+  __syncthreads();
+  const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
+  const int kb1 = C / 4;
+  for (int j = threadIdx.x; j < HIDN; j += 256) {
+    const uint8_t* row = w1 + (size_t)j * kb1;
+    float acc = 0.f;
+    for (int b = 0; b < kb1; ++b) {
+      const uint32_t byte = __ldg(row + b);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc = fmaf(tern_val(byte, q), bulk[4 * b + q], acc);
+    }
+    acc *= g1;
+    hid[j] = acc / (1.0f + expf(-acc));
+  }
+  __syncthreads();
+  const float st = fminf(fmaxf(__ldg(scale_temp), 0.1f), 0.5f);
+  const int kb2 = HIDN / 4;
+  for (int r = threadIdx.x; r < 2 * E; r += 256) {
+    const uint8_t* row = w2 + (size_t)r * kb2;
+    float acc = 0.f;
+    for (int b = 0; b < kb2; ++b) {
+      const uint32_t byte = __ldg(row + b);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc = fmaf(tern_val(byte, q), hid[4 * b + q], acc);
+    }
+    acc *= g2;
+    if (r < E) scale[(size_t)seg * E + r] = 1.0f + st * tanhf(acc);
+    else shift[(size_t)seg * E + (r - E)] = acc;
+  }
+}
+
+// Warp per row.
+template <typename T>
+__global__ void __launch_bounds__(256)
+chmod_apply_kernel(const T* x, int64_t nrows, int C, int seg_len, const float* __restrict__ w, float eps,
+                   const float* __restrict__ scale, const float* __restrict__ shift, float rscale, int add_input,
+                   T* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = C / 32;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < nrows; row += (int64_t)gridDim.x * 8) {
+    const T* xr = x + row * C;
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float v = to_f(xr[c]);
+      s = fmaf(v, v, s);
+    }
+    s = warp_sum(s);
+    const float r = w ? rsqrtf(s / (float)C + eps) : 1.0f;
+    const int64_t seg = row / seg_len;
+    const float* sc = scale + seg * E;
+    const float* sh = shift + seg * E;
+    T* orow = out + row * C;
+    for (int c = lane; c < C; c += 32) {
+      const float xv = to_f(xr[c]);
+      const float xn = w ? xv * r * __ldg(w + c) : xv;
+      const int b = c >> 5;
+      const float xm = xn * __ldg(sc + b) + __ldg(sh + b) * 0.1f;
+      const float xo = xn + rscale * (xm - xn);
+      orow[c] = from_f<T>(add_input ? xv + xo : xo);
+    }
+  }
+}
+
+}  // namespace walsh
+
+using namespace walsh;
+
+extern "C" int walsh_chmod_chunk_rows(int seg_len) {
+  (void)seg_len;
+  return kChunkRows;
+}
+
+extern "C" walsh_status walsh_chmod_stats(const void* x, int dtype, int64_t nrows, int C, int seg_len,
+                                          const float* norm_w, float norm_eps, float* partial, void* stream) {
+  if (int e = injected("chmod_stats")) return e;
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_ARG(x && partial);
+  WALSH_CHECK_SHAPE(nrows > 0 && C > 0 && C % 32 == 0 && seg_len > 0 && nrows % seg_len == 0);
+  const int64_t nseg = nrows / seg_len;
+  WALSH_CHECK_SHAPE(nseg <= 65535);
+  dim3 grid((seg_len + kChunkRows - 1) / kChunkRows, (unsigned)nseg);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == WALSH_F32)
+    chmod_stats_kernel<float><<<grid, 256, 0, s>>>((const float*)x, C, seg_len, norm_w, norm_eps, partial);
+  else
+    chmod_stats_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)x, C, seg_len, norm_w, norm_eps,
+                                                           partial);
+  return launch_status();
+}
+
+extern "C" walsh_status walsh_chmod_mlp(const float* partial, int nseg, int seg_len, int C, const uint8_t* w1_2bit,
+                                        const uint8_t* w2_2bit, const float* gammas, const float* scale_temp,
+                                        float* scale, float* shift, void* stream) {
+  if (int e = injected("chmod_mlp")) return e;
+  WALSH_CHECK_ARG(partial && w1_2bit && w2_2bit && gammas && scale_temp && scale && shift);
+  WALSH_CHECK_SHAPE(nseg > 0 && seg_len > 0 && C > 0 && C % 32 == 0);
+  const int nch = (seg_len + kChunkRows - 1) / kChunkRows;
+  const size_t smem = (size_t)(C + C / 4) * sizeof(float);
+  chmod_mlp_kernel<<<nseg, 256, smem, (cudaStream_t)stream>>>(partial, nch, seg_len, C, w1_2bit, w2_2bit, gammas,
+                                                             scale_temp, scale, shift);
+  return launch_status();
+}
+
+extern "C" walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrows, int C, int seg_len,
+                                          const float* norm_w, float norm_eps, const float* scale, const float* shift,
+                                          float residual_scale, int add_input, void* out, void* stream) {
+  if (int e = injected("chmod_apply")) return e;
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_ARG(x && scale && shift && out);
+  WALSH_CHECK_SHAPE(nrows > 0 && C > 0 && C % 32 == 0 && seg_len > 0 && nrows % seg_len == 0);
+  int64_t g = (nrows + 7) / 8;
+  if (g > 148 * 32) g = 148 * 32;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == WALSH_F32)
+    chmod_apply_kernel<float><<<(unsigned)g, 256, 0, s>>>((const float*)x, nrows, C, seg_len, norm_w, norm_eps, scale,
+                                                          shift, residual_scale, add_input, (float*)out);
+  else
+    chmod_apply_kernel<__nv_bfloat16><<<(unsigned)g, 256, 0, s>>>((const __nv_bfloat16*)x, nrows, C, seg_len, norm_w,
+                                                                  norm_eps, scale, shift, residual_scale, add_input,
+                                                                  (__nv_bfloat16*)out);
+  return launch_status();
+}

@@ -1,0 +1,80 @@
+// Shared device/host helpers for libwalsh (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "walsh.h"
+
+namespace walsh {
+
+constexpr int kGroups = 32;      // Hadamard algebra dimension
+constexpr int kStreams = 4;      // mHC residual streams supported by the fused kernels
+constexpr int kMapRows = 24;     // phi rows: pre(4) | post(4) | res(16)
+constexpr int kExpertHidden = 128;
+constexpr int kBlock = 32;       // Hadamard block width (experts, channel modulation)
+
+// ---- activation storage types -------------------------------------------------
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// ---- math --------------------------------------------------------------------
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float siluf_(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// In-register unnormalised 32-point Walsh-Hadamard transform (Sylvester order:
+// out[h] = sum_g (-1)^popc(g&h) in[g]).
+__device__ __forceinline__ void fht32(float* v) {
+#pragma unroll
+  for (int s = 1; s < 32; s <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if ((i & s) == 0) {
+        float a = v[i], b = v[i + s];
+        v[i] = a + b;
+        v[i + s] = a - b;
+      }
+    }
+  }
+}
+
+// 2-bit ternary code (reference encoding: -1 -> 0b00, 0 -> 0b01, +1 -> 0b10),
+// four values per byte, first value in the two most significant bits.
+__device__ __forceinline__ float tern_val(uint32_t byte, int j) {
+  return (float)((int)((byte >> (6 - 2 * j)) & 3u) - 1);
+}
+
+}  // namespace walsh
+
+// ---- host-side argument checking ------------------------------------------------
+#define WALSH_CHECK_ARG(cond) \
+  do { if (!(cond)) return WALSH_ERR_ARG; } while (0)
+#define WALSH_CHECK_SHAPE(cond) \
+  do { if (!(cond)) return WALSH_ERR_SHAPE; } while (0)
+#define WALSH_CHECK_DTYPE(d) \
+  do { if ((d) != WALSH_F32 && (d) != WALSH_BF16) return WALSH_ERR_DTYPE; } while (0)
+
+namespace walsh {
+// Returns WALSH_ERR_INJECTED when the host-side fault injector is armed for
+// `site` (environment variable WALSH_INJECT_FAULT=<site name> or "all").
+int injected(const char* site);
+// Converts the last launch error into a status code.
+int launch_status();
+}  // namespace walsh

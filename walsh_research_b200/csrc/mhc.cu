@@ -1,0 +1,243 @@
+// mHC residual-stream kernels (n_streams = 4).
+//
+// walsh_mhc_map fuses, per token, the three ResidualStreamMapping.forward
+// calls (src/model/mhc.py:283-318) -- which each recompute the same weightless
+// RMSNorm of x_flat -- into one pass over x: one sum of squares, one
+// [24 x 4C] projection, then sigmoid / 2*sigmoid / Sinkhorn-20 in registers,
+// followed by the pre-mix H_pre @ x (src/model/mhc.py:364) and the block's
+// attention_norm / ffn_norm RMSNorm (src/model/mhc.py:514-523).
+#include "common.cuh"
+
+namespace walsh {
+
+// Sinkhorn-Knopp on a 4x4 matrix held in registers (src/model/mhc.py:214-229).
+__device__ __forceinline__ void sinkhorn4(float* M, int iters, float eps) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) M[i] = expf(M[i]);
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float s = ((M[c] + M[4 + c]) + M[8 + c]) + M[12 + c];
+      const float den = s + eps;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) M[4 * r + c] = __fdiv_rn(M[4 * r + c], den);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float s = ((M[4 * r] + M[4 * r + 1]) + M[4 * r + 2]) + M[4 * r + 3];
+      const float den = s + eps;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) M[4 * r + c] = __fdiv_rn(M[4 * r + c], den);
+    }
+  }
+}
+
+// Turns the 24 raw projections d (already multiplied by the RMS factor) into
+// {H_pre[4], H_post[4], H_res[16]}.
+__device__ __forceinline__ void map_activations(const float* d, const float* __restrict__ mp, float* hm) {
+  const float a_pre = __ldg(mp + 0), a_post = __ldg(mp + 1), a_res = __ldg(mp + 2);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    hm[j] = 1.0f / (1.0f + expf(-(a_pre * d[j] + __ldg(mp + 4 + j))));
+    hm[4 + j] = 2.0f * (1.0f / (1.0f + expf(-(a_post * d[4 + j] + __ldg(mp + 8 + j)))));
+  }
+  float M[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) M[i] = a_res * d[8 + i] + __ldg(mp + 12 + i);
+  sinkhorn4(M, 20, 1e-8f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) hm[8 + i] = M[i];
+}
+
+// CTA = 8 warps x TPW tokens.  phi is staged through shared memory in chunks
+// of KC columns so that each phi value read serves TPW tokens.
+template <typename T, int TPW>
+__global__ void __launch_bounds__(256)
+mhc_map_kernel(const T* __restrict__ x, int64_t ntok, int C, const float* __restrict__ phi,
+               const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
+               T* __restrict__ u, float* __restrict__ hmix) {
+  constexpr int KC = 128;
+  extern __shared__ float4 smem4[];
+  float* phis = reinterpret_cast<float*>(smem4);      // [24][KC]
+  float* hs = phis + kMapRows * KC;                    // [8][TPW][24]
+  float* us = hs + 8 * TPW * kMapRows;                 // [8][C]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = 4 * C;
+  const int64_t tok0 = ((int64_t)blockIdx.x * 8 + warp) * TPW;
+  float acc[TPW][kMapRows];
+  float ss[TPW];
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+    ss[t] = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) acc[t][r] = 0.f;
+  }
+  for (int k0 = 0; k0 < D; k0 += KC) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kMapRows * KC; i += 256) {
+      const int r = i / KC, kk = i - r * KC;
+      phis[i] = __ldg(phi + (size_t)r * D + k0 + kk);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < KC / 32; ++j) {
+      const int kk = lane + 32 * j;
+      float xv[TPW];
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        xv[t] = (tok0 + t < ntok) ? to_f(x[(tok0 + t) * D + k0 + kk]) : 0.f;
+        ss[t] = fmaf(xv[t], xv[t], ss[t]);
+      }
+#pragma unroll
+      for (int r = 0; r < kMapRows; ++r) {
+        const float w = phis[r * KC + kk];
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) acc[t][r] = fmaf(w, xv[t], acc[t][r]);
+      }
+    }
+  }
+  // reduce across the warp; lane t < TPW keeps token t's values
+  float mine[kMapRows];
+  float myss = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMapRows; ++r) mine[r] = 0.f;
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+    const float s = warp_sum(ss[t]);
+    if (lane == t) myss = s;
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) {
+      const float v = warp_sum(acc[t][r]);
+      if (lane == t) mine[r] = v;
+    }
+  }
+  float* hw = hs + warp * TPW * kMapRows;
+  if (lane < TPW) {
+    const float rms = rsqrtf(myss / (float)D + map_eps);
+    float d[kMapRows], hm[kMapRows];
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) d[r] = mine[r] * rms;
+    map_activations(d, mp, hm);
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) hw[lane * kMapRows + r] = hm[r];
+  }
+  __syncwarp();
+  float* uw = us + warp * C;
+#pragma unroll 1
+  for (int t = 0; t < TPW; ++t) {
+    const int64_t tok = tok0 + t;
+    if (tok >= ntok) break;
+    if (lane < kMapRows) hmix[tok * kMapRows + lane] = hw[t * kMapRows + lane];
+    const float h0 = hw[t * kMapRows + 0], h1 = hw[t * kMapRows + 1];
+    const float h2 = hw[t * kMapRows + 2], h3 = hw[t * kMapRows + 3];
+    const T* xt = x + tok * D;
+    float s2 = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float v = ((h0 * to_f(xt[c]) + h1 * to_f(xt[C + c])) + h2 * to_f(xt[2 * C + c])) + h3 * to_f(xt[3 * C + c]);
+      uw[c] = v;
+      s2 = fmaf(v, v, s2);
+    }
+    s2 = warp_sum(s2);
+    const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
+    T* ut = u + tok * C;
+    for (int c = lane; c < C; c += 32) {
+      const float v = uw[c] * rn;
+      ut[c] = from_f<T>(norm_w ? v * __ldg(norm_w + c) : v);
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T>
+__global__ void mhc_post_kernel(const T* x, const T* __restrict__ f, const float* __restrict__ hmix, int64_t ntok,
+                                int C, T* xo) {
+  const int64_t total = ntok * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tok = i / C;
+    const int c = (int)(i - tok * C);
+    const float* hm = hmix + tok * kMapRows;
+    const size_t base = (size_t)tok * 4 * C + c;
+    const float x0 = to_f(x[base]), x1 = to_f(x[base + C]), x2 = to_f(x[base + 2 * C]), x3 = to_f(x[base + 3 * C]);
+    const float fv = to_f(f[i]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float* hr = hm + 8 + 4 * r;
+      const float v = (((hr[0] * x0 + hr[1] * x1) + hr[2] * x2) + hr[3] * x3) + hm[4 + r] * fv;
+      xo[base + (size_t)r * C] = from_f<T>(v);
+    }
+  }
+}
+
+__global__ void sinkhorn_kernel(const float* __restrict__ h, int64_t n, int iters, float eps, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float M[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) M[k] = h[i * 16 + k];
+    sinkhorn4(M, iters, eps);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) out[i * 16 + k] = M[k];
+  }
+}
+
+template <typename T, int TPW>
+static int launch_map(const void* x, int64_t ntok, int C, const float* phi, const float* mp, float map_eps,
+                      const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s) {
+  const size_t smem = (kMapRows * 128 + 8 * TPW * kMapRows + 8 * C) * sizeof(float);
+  auto kern = mhc_map_kernel<T, TPW>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int64_t grid = (ntok + 8 * TPW - 1) / (8 * TPW);
+  kern<<<(unsigned)grid, 256, smem, s>>>((const T*)x, ntok, C, phi, mp, map_eps, norm_w, norm_eps, (T*)u, hmix);
+  return launch_status();
+}
+
+static inline int grid_for(int64_t total, int threads) {
+  int64_t g = (total + threads - 1) / threads;
+  return (int)(g < 148 * 16 ? (g < 1 ? 1 : g) : 148 * 16);
+}
+
+}  // namespace walsh
+
+using namespace walsh;
+
+extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
+                                      const float* mparams, float map_eps, const float* norm_w, float norm_eps,
+                                      void* u, float* hmix, void* stream) {
+  if (int e = injected("mhc_map")) return e;
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_ARG(x && phi && mparams && u && hmix);
+  WALSH_CHECK_SHAPE(ntok >= 0 && C > 0 && C % 32 == 0 && C <= 8192);
+  if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool big = ntok >= 148 * 64;
+  if (dtype == WALSH_F32)
+    return big ? launch_map<float, 4>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s)
+               : launch_map<float, 1>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s);
+  return big ? launch_map<__nv_bfloat16, 4>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s)
+             : launch_map<__nv_bfloat16, 1>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s);
+}
+
+extern "C" walsh_status walsh_mhc_post(const void* x, const void* f, const float* hmix, int dtype, int64_t ntok,
+                                       int C, void* x_out, void* stream) {
+  if (int e = injected("mhc_post")) return e;
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_ARG(x && f && hmix && x_out);
+  WALSH_CHECK_SHAPE(ntok >= 0 && C > 0);
+  if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int g = grid_for(ntok * C, 256);
+  if (dtype == WALSH_F32)
+    mhc_post_kernel<float><<<g, 256, 0, s>>>((const float*)x, (const float*)f, hmix, ntok, C, (float*)x_out);
+  else
+    mhc_post_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)f, hmix, ntok, C,
+                                                     (__nv_bfloat16*)x_out);
+  return launch_status();
+}
+
+extern "C" walsh_status walsh_sinkhorn(const float* h, int64_t n, int iters, float eps, float* out, void* stream) {
+  if (int e = injected("sinkhorn")) return e;
+  WALSH_CHECK_ARG(h && out && iters >= 0);
+  WALSH_CHECK_SHAPE(n >= 0);
+  if (n == 0) return WALSH_OK;
+  sinkhorn_kernel<<<grid_for(n, 128), 128, 0, (cudaStream_t)stream>>>(h, n, iters, eps, out);
+  return launch_status();
+}

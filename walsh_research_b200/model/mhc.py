@@ -1,0 +1,350 @@
+"""Manifold hyper-connections and the mHCWalsh model (reference: src/model/mhc.py).
+
+The forward of ``mHCLlamaBlock`` / ``mHCWalsh`` is the fused B200 path:
+
+  per layer  walsh_mhc_map (RMSNorm + phi + sigmoid/Sinkhorn + pre-mix + norm)
+             walsh_attn_qkv_fwd (q/k/v + RoPE + KV write) -> walsh_attn_fwd
+             -> walsh_head_mixer_fwd -> walsh_hadamard_linear_fwd (wo)
+             -> walsh_mhc_post
+             walsh_mhc_map -> walsh_moe_fwd (router + experts + site epilogue)
+             walsh_chmod_stats -> walsh_chmod_mlp -> walsh_chmod_apply
+  around it  walsh_embed_gather (embedding with stream_proj folded in),
+             walsh_linear_fwd (stream_merge, tied logits), walsh_rmsnorm.
+
+The RMS of the weightless mapping norm uses eps = finfo(float32).eps, the
+reference's value for float32 activations, in both activation precisions.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import ops
+from . import _prep
+from .chassis import CausalSelfAttention, KVCache, RMSNorm, WalshConfig, precompute_freqs_cis, rope_tables
+
+MAP_EPS = float(torch.finfo(torch.float32).eps)
+
+
+class SinkhornKnopp(nn.Module):
+    """exp then n_iter x (column, row) normalisation (src/model/mhc.py:198-229)."""
+
+    def __init__(self, n_iter=20, eps=1e-8):
+        super().__init__()
+        self.n_iter = n_iter
+        self.eps = eps
+
+    def forward(self, H):
+        return ops.sinkhorn(H, self.n_iter, self.eps)
+
+
+class ResidualStreamMapping(nn.Module):
+    """H = manifold(alpha * phi(RMSNorm(x)) + bias) (src/model/mhc.py:232-318)."""
+
+    def __init__(self, n_embd, n_streams, mapping_type="res"):
+        super().__init__()
+        self.n_embd = n_embd
+        self.n_streams = n_streams
+        self.mapping_type = mapping_type
+        self.alpha = nn.Parameter(torch.tensor(0.01))
+        if mapping_type == "res":
+            self.phi = nn.Linear(n_streams * n_embd, n_streams * n_streams, bias=False)
+            self.bias = nn.Parameter(torch.eye(n_streams) * 2.0)
+            self.sinkhorn = SinkhornKnopp(n_iter=20)
+        else:
+            self.phi = nn.Linear(n_streams * n_embd, n_streams, bias=False)
+            self.bias = nn.Parameter(torch.zeros(1, n_streams))
+        nn.init.normal_(self.phi.weight, std=0.01)
+
+    def forward(self, x):
+        """x [B, T, n*C] -> [B, T, 1, n] ('pre'/'post') or [B, T, n, n] ('res')."""
+        B, T, _ = x.shape
+        n, C = self.n_streams, self.n_embd
+        if n != 4:
+            raise NotImplementedError("the fused mapping kernel implements n_streams = 4")
+        rows = {"pre": (0, 4), "post": (4, 8), "res": (8, 24)}[self.mapping_type]
+        phi = torch.zeros(24, n * C, device=x.device, dtype=torch.float32)
+        phi[rows[0]:rows[1]] = self.phi.weight.detach().float()
+        mp = torch.zeros(28, device=x.device, dtype=torch.float32)
+        slot = {"pre": 0, "post": 1, "res": 2}[self.mapping_type]
+        mp[slot] = self.alpha.detach().float()
+        mp[4 + rows[0]:4 + rows[1]] = self.bias.detach().float().reshape(-1)
+        _, hmix = ops.mhc_map(x.reshape(B, T, n, C), phi, mp, MAP_EPS)
+        h = hmix[..., rows[0]:rows[1]]
+        return h.reshape(B, T, n, n) if self.mapping_type == "res" else h.reshape(B, T, 1, n)
+
+
+def site_params(stream: "mHCResidualStream"):
+    """phi [24, n*C] and mparams [28] of one mHC site, on the device."""
+    pre, post, res = stream.H_pre, stream.H_post, stream.H_res
+
+    def build():
+        phi = torch.cat([pre.phi.weight, post.phi.weight, res.phi.weight]).detach().float().contiguous()
+        dev = phi.device
+        mp = torch.cat([torch.stack([pre.alpha, post.alpha, res.alpha]).detach().float().reshape(3),
+                        torch.zeros(1, device=dev),
+                        pre.bias.detach().float().reshape(-1), post.bias.detach().float().reshape(-1),
+                        res.bias.detach().float().reshape(-1)]).contiguous()
+        return phi, mp
+    srcs = [pre.phi.weight, post.phi.weight, res.phi.weight, pre.alpha, post.alpha, res.alpha,
+            pre.bias, post.bias, res.bias]
+    return _prep.cached(stream, "site", srcs, build)
+
+
+class mHCResidualStream(nn.Module):
+    """x' = H_res x + H_post^T F(H_pre x) (src/model/mhc.py:321-381)."""
+
+    def __init__(self, n_embd, n_streams=4):
+        super().__init__()
+        self.n_embd = n_embd
+        self.n_streams = n_streams
+        self.H_pre = ResidualStreamMapping(n_embd, n_streams, "pre")
+        self.H_post = ResidualStreamMapping(n_embd, n_streams, "post")
+        self.H_res = ResidualStreamMapping(n_embd, n_streams, "res")
+
+    def forward(self, x, layer_fn):
+        phi, mp = site_params(self)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS)
+        return ops.mhc_post(x, layer_fn(u), hmix)
+
+
+class mHCLlamaBlock(nn.Module):
+    """Block with mHC streams, MoE/SwiGLU FFN and channel modulation
+    (src/model/mhc.py:451-534)."""
+
+    def __init__(self, config, n_streams=4):
+        super().__init__()
+        self.n_streams = n_streams
+        self.n_embd = config.n_embd
+        self.attention_norm = RMSNorm(config.n_embd)
+        self.ffn_norm = RMSNorm(config.n_embd)
+        self.attention = CausalSelfAttention(config)
+        if getattr(config, "use_moe", False):
+            from .moe import HadamardMoE
+            self.feed_forward = HadamardMoE(config, threshold=getattr(config, "moe_threshold", 0.1),
+                                            min_experts=getattr(config, "moe_min_experts", 1),
+                                            max_experts=getattr(config, "moe_max_experts", 4))
+        else:
+            from .cayley_dickson_cuda import SwiGLUMLP
+            self.feed_forward = SwiGLUMLP(config)
+        self.use_channel_mod = getattr(config, "use_channel_mod", False)
+        if self.use_channel_mod:
+            from .moe import HadamardChannelModulation
+            self.channel_mod = HadamardChannelModulation(n_embd=config.n_embd, n_blocks=None, use_ternary=True,
+                                                         residual_scale=0.5)
+            self.channel_mod_norm = RMSNorm(config.n_embd)
+        self.attn_stream = mHCResidualStream(config.n_embd, n_streams)
+        self.ffn_stream = mHCResidualStream(config.n_embd, n_streams)
+
+    def _w(self, p):
+        return p.detach().float().contiguous()
+
+    def forward_fused(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, record_stats=True):
+        """x [B, T, n, C] (updated in place and returned)."""
+        B, T, n, C = x.shape
+        # attention site
+        phi, mp = site_params(self.attn_stream)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.attention_norm.weight), self.attention_norm.eps)
+        f = self.attention.forward_cached(u, rope_cos, rope_sin, k_cache, v_cache, start_pos)
+        ops.mhc_post(x, f, hmix, out=x)
+        # ffn site
+        phi, mp = site_params(self.ffn_stream)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.ffn_norm.weight), self.ffn_norm.eps)
+        ff = self.feed_forward
+        if hasattr(ff, "kernel_args"):
+            w1t, w2, g, up, d, gam, k = ff.kernel_args()
+            if record_stats:
+                _, mask, probs, _ = ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True)
+                ff._record(mask.float(), probs, B * T)
+            else:
+                ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x))
+        else:
+            ops.mhc_post(x, ff(u), hmix, out=x)
+        # channel modulation over the [B*n, T, C] reinterpretation of x
+        if self.use_channel_mod:
+            w1, w2c, gam, temp = self.channel_mod.kernel_args()
+            _, scale, shift = ops.chmod(x.view(B * T * n, C), T, w1, w2c, gam, temp,
+                                        norm_w=self._w(self.channel_mod_norm.weight),
+                                        norm_eps=self.channel_mod_norm.eps, add_input=True, out=x.view(B * T * n, C),
+                                        residual_scale=self.channel_mod.residual_scale)
+            self.channel_mod._last_scale, self.channel_mod._last_shift = scale, shift
+        return x
+
+    def forward(self, x, freqs_cis, kv_cache=None, layer_idx=0):
+        B, T, n, C = x.shape
+        x = x.contiguous().clone()
+        cos = freqs_cis[:T].real.float().contiguous()
+        sin = freqs_cis[:T].imag.float().contiguous()
+        H, hd = self.attention.n_head, self.attention.head_dim
+        if kv_cache is None:
+            kc = torch.empty((B, H, T, hd), dtype=x.dtype, device=x.device)
+            vc = torch.empty_like(kc)
+            start = 0
+        else:
+            kc, vc, start = kv_cache.k_cache[layer_idx], kv_cache.v_cache[layer_idx], kv_cache.cached_len
+        return self.forward_fused(x, cos, sin, kc, vc, start)
+
+
+class mHCWalsh(nn.Module):
+    """Walsh with mHC residual streams (src/model/mhc.py:537-789).
+
+    ``compute_dtype`` (float32 or bfloat16) selects the activation precision;
+    a forward run under ``torch.autocast('cuda', dtype=torch.bfloat16)`` uses
+    bfloat16 as well.  Parameters stay float32, as in the reference."""
+
+    def __init__(self, config, n_streams=4, gradient_checkpointing=False):
+        super().__init__()
+        self.config = config
+        self.n_streams = n_streams
+        self.gradient_checkpointing = gradient_checkpointing
+        self.compute_dtype = torch.float32
+        if getattr(config, "hash_embeddings", False):
+            raise NotImplementedError("hash embeddings are outside the B200 hot path")
+        self.tok_embeddings = nn.Embedding(config.vocab_size, config.n_embd)
+        self.output = nn.Linear(config.n_embd, config.vocab_size, bias=False)
+        self.tok_embeddings.weight = self.output.weight
+        self.stream_proj = nn.Linear(config.n_embd, n_streams * config.n_embd)
+        self.layers = nn.ModuleList([mHCLlamaBlock(config, n_streams) for _ in range(config.n_layer)])
+        self.stream_merge = nn.Linear(n_streams * config.n_embd, config.n_embd)
+        self.norm = RMSNorm(config.n_embd)
+        self.register_buffer("freqs_cis", precompute_freqs_cis(config.n_embd // config.n_head, config.block_size * 2))
+        self.apply(self._init_weights)
+        with torch.no_grad():
+            C = config.n_embd
+            self.stream_proj.weight.copy_(torch.eye(C).repeat(n_streams, 1) / math.sqrt(n_streams))
+            self.stream_proj.bias.zero_()
+            self.stream_merge.weight.copy_(torch.eye(C).repeat(1, n_streams) / n_streams)
+            self.stream_merge.bias.zero_()
+
+    def _init_weights(self, module):
+        if isinstance(module, nn.Linear):
+            torch.nn.init.normal_(module.weight, mean=0.0, std=0.02)
+            if module.bias is not None:
+                torch.nn.init.zeros_(module.bias)
+        elif isinstance(module, nn.Embedding):
+            torch.nn.init.normal_(module.weight, mean=0.0, std=0.02)
+
+    # -- device-side derived weights ------------------------------------------------
+    def _act_dtype(self):
+        if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+            return torch.bfloat16
+        return self.compute_dtype
+
+    def stream_table(self, dtype):
+        """tok_embeddings folded with stream_proj: row v = stream_proj(emb[v]), [V, n*C]."""
+        emb, W, b = self.tok_embeddings.weight, self.stream_proj.weight, self.stream_proj.bias
+        return _prep.cached(self, f"table_{dtype}", [emb, W, b],
+                            lambda: ops.linear(emb.detach().float().contiguous(), W.detach().float(), b.detach(),
+                                               out_dtype=dtype))
+
+    def head_weights(self, dtype):
+        emb = self.tok_embeddings.weight
+        return _prep.cached(self, f"emb_{dtype}", [emb], lambda: emb.detach().to(dtype).contiguous())
+
+    def _merge_norm(self, x, rows_last_only: bool):
+        B, T, n, C = x.shape
+        Wm = self.stream_merge.weight.detach().float().contiguous()
+        bm = self.stream_merge.bias.detach().float().contiguous()
+        if rows_last_only:
+            xl = x[:, T - 1]                                   # [B, n, C] strided view
+            hm = ops.linear(xl, Wm, bm, ldx=T * n * C, M=B)    # [B, C] float32
+            h = ops.rmsnorm(hm, self.norm.weight.detach().float().contiguous(), self.norm.eps, torch.float32)
+            return h.view(B, 1, C)
+        hm = ops.linear(x.view(B, T, n * C), Wm, bm)
+        return ops.rmsnorm(hm, self.norm.weight.detach().float().contiguous(), self.norm.eps, torch.float32)
+
+    def forward(self, idx, targets=None, kv_cache=None, start_pos=0, return_hidden=False):
+        if not idx.is_cuda:
+            raise RuntimeError("walsh_research_b200 runs on CUDA devices only (no CPU fallback)")
+        B, T = idx.shape
+        C, n = self.config.n_embd, self.n_streams
+        dt = self._act_dtype()
+        err = torch.zeros(1, dtype=torch.int32, device=idx.device)
+        x = ops.embed_gather(idx, self.stream_table(dt), err).view(B, T, n, C)
+        cos_all, sin_all = rope_tables(self, self.freqs_cis)
+        cos, sin = cos_all[start_pos:start_pos + T], sin_all[start_pos:start_pos + T]
+        if kv_cache is None:
+            H, hd = self.config.n_head, C // self.config.n_head
+            kc = torch.empty((B, H, T, hd), dtype=dt, device=idx.device)
+            vc = torch.empty_like(kc)
+        elif kv_cache.dtype != dt or kv_cache.batch_size != B:
+            raise ValueError(f"KV cache holds {kv_cache.batch_size} x {kv_cache.dtype}; forward has {B} x {dt}")
+        elif kv_cache.cached_len + T > kv_cache.max_seq_len:
+            raise ValueError("KV cache is full")
+        for l, layer in enumerate(self.layers):
+            if kv_cache is not None:
+                kc, vc = kv_cache.k_cache[l], kv_cache.v_cache[l]
+                cpos = kv_cache.cached_len
+            else:
+                cpos = 0
+            layer.forward_fused(x, cos, sin, kc, vc, cpos)
+        self._last_index_error = err
+        need_all = return_hidden or targets is not None
+        h_out = self._merge_norm(x, rows_last_only=not need_all)
+        emb = self.head_weights(dt)
+        if targets is not None:
+            logits = ops.linear(h_out, emb, None, out_dtype=torch.float32)
+            loss = F.cross_entropy(logits.view(-1, logits.size(-1)), targets.view(-1), ignore_index=-1)
+        else:
+            last = h_out[:, -1, :] if need_all else h_out[:, 0, :]
+            logits = ops.linear(last.contiguous(), emb, None, out_dtype=torch.float32).view(B, 1, -1)
+            loss = None
+        if return_hidden:
+            return logits, loss, h_out
+        return logits, loss
+
+    def check_token_ids(self):
+        """Raise if the last forward saw a token id outside the vocabulary."""
+        err = getattr(self, "_last_index_error", None)
+        if err is not None and int(err.item()) != 0:
+            raise IndexError("token id out of range in the last forward")
+
+    @property
+    def num_parameters(self):
+        total = sum(p.numel() for p in self.parameters())
+        return total, sum(p.numel() for p in self.parameters() if p.requires_grad)
+
+    def get_aux_loss(self):
+        aux = 0.0
+        for layer in self.layers:
+            if hasattr(layer.feed_forward, "get_aux_loss"):
+                aux = aux + layer.feed_forward.get_aux_loss()
+        return aux
+
+    def get_moe_stats(self) -> dict:
+        stats = [l.feed_forward.get_expert_stats() for l in self.layers if hasattr(l.feed_forward, "get_expert_stats")]
+        if not stats:
+            return {}
+        E = len(stats[0]["expert_load"])
+        avg = [sum(s["expert_load"][i] for s in stats) / len(stats) for i in range(E)]
+        return {"expert_load": avg, "avg_experts": sum(s["avg_experts"] for s in stats) / len(stats),
+                "load_balance": sum(s["load_balance"] for s in stats) / len(stats)}
+
+    def reset_moe_stats(self):
+        for layer in self.layers:
+            if hasattr(layer.feed_forward, "reset_stats"):
+                layer.feed_forward.reset_stats()
+
+    def get_channel_mod_stats(self) -> dict:
+        stats = [l.channel_mod.get_modulation_stats() for l in self.layers if hasattr(l, "channel_mod")]
+        if not stats:
+            return {}
+        return {k: sum(s[k] for s in stats) / len(stats) for k in ("scale_mean", "scale_std", "shift_mean")}
+
+    @torch.no_grad()
+    def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None):
+        """Sampling loop with the reference's semantics (src/model/mhc.py:753-789):
+        full re-forward of the (block-size-cropped) context per new token."""
+        for _ in range(max_new_tokens):
+            idx_cond = idx if idx.size(1) <= self.config.block_size else idx[:, -self.config.block_size:]
+            logits, _ = self(idx_cond)
+            logits = logits[:, -1, :] / temperature
+            if top_k is not None and top_k > 0:
+                v, _ = torch.topk(logits, min(top_k, logits.size(-1)))
+                logits[logits < v[:, [-1]]] = -float("Inf")
+            probs = F.softmax(logits, dim=-1)
+            idx = torch.cat((idx, torch.multinomial(probs, num_samples=1)), dim=1)
+        return idx

@@ -1,0 +1,243 @@
+"""Functional wrappers over the C ABI: tensors in, tensors out.
+
+Each function validates devices, allocates outputs with torch (the caching
+allocator is the only allocator on the forward path), and launches one
+libwalsh entry point on the current stream.  No function here computes
+anything on the host.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import call, dcode, ptr, require_cuda, stream
+
+
+def _c(t):
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# ternary weights
+# ---------------------------------------------------------------------------
+
+def quantize_pack(w: torch.Tensor):
+    """Absmean ternary quantisation + 2-bit packing along the last dim.
+    Returns (packed uint8 [..., ceil(k/4)], gamma float32 [1])."""
+    require_cuda(w)
+    w = _c(w.detach().float())
+    k = w.shape[-1]
+    rows = w.numel() // k
+    packed = torch.empty(w.shape[:-1] + ((k + 3) // 4,), dtype=torch.uint8, device=w.device)
+    gamma = torch.empty(1, dtype=torch.float32, device=w.device)
+    call("walsh_ternary_quantize_pack", ptr(w), rows, k, ptr(packed), ptr(gamma), stream())
+    return packed, gamma
+
+
+def unpack(packed: torch.Tensor, k: int) -> torch.Tensor:
+    require_cuda(packed)
+    packed = _c(packed)
+    rows = packed.numel() // packed.shape[-1]
+    out = torch.empty(packed.shape[:-1] + (k,), dtype=torch.float32, device=packed.device)
+    call("walsh_ternary_unpack", ptr(packed), rows, k, ptr(out), stream())
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Hadamard algebra
+# ---------------------------------------------------------------------------
+
+def hadamard_linear(x, packed, alpha, beta, w_scale: float = 1.0, out_dtype=None):
+    require_cuda(x)
+    x = _c(x)
+    in_o = alpha.shape[1]
+    out_o = beta.shape[1]
+    if x.shape[-1] != 32 * in_o:
+        raise ValueError(f"HadamardLinear expects last dim {32 * in_o}, got {x.shape[-1]}")
+    out_dtype = out_dtype or x.dtype
+    y = torch.empty(x.shape[:-1] + (32 * out_o,), dtype=out_dtype, device=x.device)
+    ntok = x.numel() // x.shape[-1]
+    call("walsh_hadamard_linear_fwd", ptr(x), dcode(x.dtype), ntok, in_o, out_o, ptr(packed), float(w_scale),
+         ptr(alpha), ptr(beta), ptr(y), dcode(out_dtype), stream())
+    return y
+
+
+def head_mixer_tokens(x, W, beta, out=None):
+    """Hadamard head mixing on token-major [..., n_head, hd]."""
+    require_cuda(x)
+    x = _c(x)
+    n_head, hd = x.shape[-2], x.shape[-1]
+    y = out if out is not None else torch.empty_like(x)
+    ntok = x.numel() // (n_head * hd)
+    call("walsh_head_mixer_fwd", ptr(x), dcode(x.dtype), ntok, n_head, hd, ptr(W), ptr(beta), ptr(y), stream())
+    return y
+
+
+# ---------------------------------------------------------------------------
+# mHC
+# ---------------------------------------------------------------------------
+
+def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6):
+    """x [..., 4, C] -> (u [..., C], hmix float [..., 24])."""
+    require_cuda(x)
+    x = _c(x)
+    C = x.shape[-1]
+    lead = x.shape[:-2]
+    ntok = x.numel() // (4 * C)
+    u = torch.empty(lead + (C,), dtype=x.dtype, device=x.device)
+    hmix = torch.empty(lead + (24,), dtype=torch.float32, device=x.device)
+    call("walsh_mhc_map", ptr(x), dcode(x.dtype), ntok, C, ptr(phi), ptr(mparams), float(map_eps), ptr(norm_w),
+         float(norm_eps), ptr(u), ptr(hmix), stream())
+    return u, hmix
+
+
+def mhc_post(x, f, hmix, out=None):
+    require_cuda(x, f)
+    x, f = _c(x), _c(f.to(x.dtype))
+    C = x.shape[-1]
+    ntok = x.numel() // (4 * C)
+    out = out if out is not None else torch.empty_like(x)
+    call("walsh_mhc_post", ptr(x), ptr(f), ptr(hmix), dcode(x.dtype), ntok, C, ptr(out), stream())
+    return out
+
+
+def sinkhorn(h, iters=20, eps=1e-8):
+    require_cuda(h)
+    if h.shape[-2:] != (4, 4):
+        raise ValueError("walsh_sinkhorn supports 4x4 matrices (n_streams = 4)")
+    hf = _c(h.float())
+    out = torch.empty_like(hf)
+    call("walsh_sinkhorn", ptr(hf), hf.numel() // 16, int(iters), float(eps), ptr(out), stream())
+    return out.to(h.dtype)
+
+
+# ---------------------------------------------------------------------------
+# MoE and channel modulation
+# ---------------------------------------------------------------------------
+
+def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=None, want_stats=False):
+    """Router + experts.  With ``fuse=(x, hmix, x_out)`` the mHC epilogue is
+    applied and ``x_out`` returned; otherwise the expert output y.
+    With ``want_stats`` also returns (mask uint8, probs, weights)."""
+    require_cuda(u)
+    u = _c(u)
+    C = u.shape[-1]
+    E = C // 32
+    ntok = u.numel() // C
+    lead = u.shape[:-1]
+    mask = probs = weights = None
+    if want_stats:
+        mask = torch.empty(lead + (E,), dtype=torch.uint8, device=u.device)
+        probs = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
+        weights = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
+    if weights_in is not None:
+        weights_in = _c(weights_in.float())
+    if fuse is None:
+        y = torch.empty_like(u)
+        call("walsh_moe_fwd", ptr(u), dcode(u.dtype), ntok, C, int(top_k), ptr(w1t), ptr(w2), ptr(gate_p),
+             ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0, None, None, None, ptr(weights_in), ptr(mask),
+             ptr(probs), ptr(weights), stream())
+        out = y
+    else:
+        x, hmix, x_out = fuse
+        call("walsh_moe_fwd", ptr(u), dcode(u.dtype), ntok, C, int(top_k), ptr(w1t), ptr(w2), ptr(gate_p),
+             ptr(up_p), ptr(down_p), ptr(gammas), None, 1, ptr(x), ptr(hmix), ptr(x_out), ptr(weights_in),
+             ptr(mask), ptr(probs), ptr(weights), stream())
+        out = x_out
+    return (out, mask, probs, weights) if want_stats else out
+
+
+def chmod(x, seg_len, w1_p, w2_p, gammas, scale_temp, norm_w=None, norm_eps=1e-6, add_input=True, out=None,
+          residual_scale=0.5):
+    """Channel modulation over rows of x viewed as [nseg, seg_len, C]."""
+    require_cuda(x)
+    x = _c(x)
+    C = x.shape[-1]
+    nrows = x.numel() // C
+    if nrows % seg_len:
+        raise ValueError("rows must be a multiple of the segment length")
+    nseg = nrows // seg_len
+    chunk = call("walsh_chmod_chunk_rows", int(seg_len))
+    nch = (seg_len + chunk - 1) // chunk
+    partial = torch.empty((nseg, nch, C), dtype=torch.float32, device=x.device)
+    call("walsh_chmod_stats", ptr(x), dcode(x.dtype), nrows, C, int(seg_len), ptr(norm_w), float(norm_eps),
+         ptr(partial), stream())
+    E = C // 32
+    scale = torch.empty((nseg, E), dtype=torch.float32, device=x.device)
+    shift = torch.empty((nseg, E), dtype=torch.float32, device=x.device)
+    call("walsh_chmod_mlp", ptr(partial), nseg, int(seg_len), C, ptr(w1_p), ptr(w2_p), ptr(gammas),
+         ptr(scale_temp), ptr(scale), ptr(shift), stream())
+    out = out if out is not None else torch.empty_like(x)
+    call("walsh_chmod_apply", ptr(x), dcode(x.dtype), nrows, C, int(seg_len), ptr(norm_w), float(norm_eps),
+         ptr(scale), ptr(shift), float(residual_scale), 1 if add_input else 0, ptr(out), stream())
+    return out, scale, shift
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+
+def attn_qkv(u, n_head, wq, wk, wv, rope_cos, rope_sin, start_pos, q, k_cache, v_cache):
+    """wq/wk/wv: (packed, alpha, beta) triples; rope_cos/sin [>=T, hd/2] hold the
+    rows of the tokens' own positions; k/v land at cache rows start_pos.."""
+    require_cuda(u)
+    u = _c(u)
+    B, T, C = u.shape
+    call("walsh_attn_qkv_fwd", ptr(u), dcode(u.dtype), B, T, C, n_head,
+         ptr(wq[0]), ptr(wq[1]), ptr(wq[2]), ptr(wk[0]), ptr(wk[1]), ptr(wk[2]),
+         ptr(wv[0]), ptr(wv[1]), ptr(wv[2]), ptr(rope_cos), ptr(rope_sin), rope_cos.shape[0], int(start_pos),
+         ptr(q), ptr(k_cache), ptr(v_cache), k_cache.shape[-2], stream())
+
+
+def attention(q, k_cache, v_cache, start_pos, out=None):
+    """q [B, H, T, hd], caches [B, H, ctx, hd] -> o [B, T, H, hd]."""
+    require_cuda(q)
+    B, H, T, hd = q.shape
+    ctx = k_cache.shape[-2]
+    o = out if out is not None else torch.empty((B, T, H, hd), dtype=q.dtype, device=q.device)
+    call("walsh_attn_fwd", ptr(q), ptr(k_cache), ptr(v_cache), dcode(q.dtype), B, H, T, hd, ctx, int(start_pos),
+         ptr(o), stream())
+    return o
+
+
+# ---------------------------------------------------------------------------
+# dense helpers
+# ---------------------------------------------------------------------------
+
+def embed_gather(idx, table, err=None, out=None):
+    require_cuda(idx, table)
+    idx = _c(idx.to(torch.int64))
+    V, D = table.shape
+    out = out if out is not None else torch.empty(idx.shape + (D,), dtype=table.dtype, device=table.device)
+    call("walsh_embed_gather", ptr(idx), idx.numel(), ptr(table), dcode(table.dtype), V, D, ptr(out), ptr(err),
+         stream())
+    return out
+
+
+def linear(x, w, bias=None, out_dtype=torch.float32, ldx=None, M=None, out=None):
+    """y = x W^T + b with x rows of stride ldx (defaults to contiguous rows)."""
+    require_cuda(x, w)
+    w = _c(w)
+    N, K = w.shape
+    if ldx is None:
+        x = _c(x)
+        ldx = K
+        M = x.numel() // K
+        lead = x.shape[:-1]
+    else:
+        lead = (M,)
+    y = out if out is not None else torch.empty(lead + (N,), dtype=out_dtype, device=x.device)
+    call("walsh_linear_fwd", ptr(x), dcode(x.dtype), M, K, ldx, ptr(w), dcode(w.dtype), N,
+         ptr(None if bias is None else _c(bias.float())), ptr(y), dcode(y.dtype), stream())
+    return y
+
+
+def rmsnorm(x, w, eps=1e-6, out_dtype=None):
+    require_cuda(x)
+    x = _c(x)
+    C = x.shape[-1]
+    out_dtype = out_dtype or x.dtype
+    y = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    call("walsh_rmsnorm", ptr(x), dcode(x.dtype), x.numel() // C, C, ptr(w), float(eps), ptr(y), dcode(out_dtype),
+         stream())
+    return y
