@@ -14,8 +14,11 @@
  *  - All pointers are device pointers unless stated otherwise; every buffer
  *    is allocated and owned by the caller.  Nothing here allocates device
  *    memory on the forward path, frees caller memory or synchronises.
- *  - Activations are either float32 (dtype WALSH_F32) or bfloat16
- *    (WALSH_BF16); arithmetic is float32 in both cases.
+ *  - Activations are float32 (dtype WALSH_F32), bfloat16 (WALSH_BF16) or
+ *    float16 (WALSH_F16); arithmetic is float32 (tensor-core kernels: fp16 or
+ *    bf16 operands, fp32 accumulation).  The model's bfloat16 mode keeps the
+ *    residual stream in bf16 and the normalised activations it feeds the
+ *    layers (u, q/k/v, attention output) in fp16.
  *  - Every call launches on `stream` (a cudaStream_t passed as void*) and
  *    returns a walsh_status: 0 on success, a negative code on a rejected
  *    argument (checked on the host before any launch) or a launch failure.
@@ -48,7 +51,7 @@ enum {
   WALSH_ERR_INDEX = -9     /* a device kernel saw an out-of-range token id */
 };
 
-enum { WALSH_F32 = 0, WALSH_BF16 = 1 };
+enum { WALSH_F32 = 0, WALSH_BF16 = 1, WALSH_F16 = 2 };
 
 /* Human-readable text of a status code (static storage). */
 const char* walsh_status_str(walsh_status s);
@@ -105,7 +108,7 @@ walsh_status walsh_head_mixer_fwd(const void* x, int dtype, int64_t ntok, int n_
  * rotating token t (the real and imaginary parts of the reference's
  * freqs_cis buffer, offset by the caller to the first token's position).
  * Writes q: [B, H, T, hd] and k, v into the caches [B, H, ctx, hd] at
- * positions start_pos..start_pos+T-1.
+ * positions start_pos..start_pos+T-1, all in out_dtype (u is in dtype).
  * Replaces CausalSelfAttention.forward lines 426-440 (src/model/chassis.py):
  * wq/wk/wv, apply_rotary_emb (src/model/chassis.py:339-345) and
  * KVCache.update (src/model/chassis.py:297-322). */
@@ -115,7 +118,7 @@ walsh_status walsh_attn_qkv_fwd(const void* u, int dtype, int B, int T, int C, i
                                 const uint8_t* wv_2bit, const float* wv_alpha, const float* wv_beta,
                                 const float* rope_cos, const float* rope_sin, int n_pos,
                                 int start_pos, void* q, void* k_cache, void* v_cache, int ctx,
-                                void* stream);
+                                int out_dtype, void* stream);
 
 /* Causal attention over the KV cache: query t (position start_pos+t) sees
  * keys 0..start_pos+t, scale 1/sqrt(hd).  q: [B, H, T, hd]; caches
@@ -125,6 +128,43 @@ walsh_status walsh_attn_qkv_fwd(const void* u, int dtype, int B, int T, int C, i
 walsh_status walsh_attn_fwd(const void* q, const void* k_cache, const void* v_cache, int dtype,
                             int B, int H, int T, int hd, int ctx, int start_pos, void* o,
                             void* stream);
+
+/* Tensor-core forms for bfloat16 activations with C = 512 (32 groups x 16):
+ * each 32-point transform is a +-1 32x32 MMA contraction, the per-group
+ * ternary mat-vecs are grouped MMAs (fp16 operands, fp32 accumulation).
+ * Weights are fp16 copies laid out [32 groups][out 16][in 16] (ternary values
+ * for HadamardLinear; for the head mixer the transpose of W[h][i][o]).  All
+ * pointers 16-byte aligned.
+ *
+ * walsh_hadamard_linear_tc_fwd: y = w_scale * beta . H W H (alpha . x), x and
+ * y bfloat16 [ntok, 512].  Replaces HadamardLinear.forward
+ * (src/model/fht_cuda.py:489-519). */
+walsh_status walsh_hadamard_linear_tc_fwd(const void* x, int64_t ntok, const void* w_f16,
+                                          float w_scale, const float* alpha, const float* beta,
+                                          void* y, void* stream);
+
+/* walsh_attn_qkv_tc_fwd: walsh_attn_qkv_fwd for C = 512 on the tensor cores
+ * (same layouts and RoPE/cache semantics; weights as above); u, q and the
+ * caches are fp16. */
+walsh_status walsh_attn_qkv_tc_fwd(const void* u, int B, int T, int n_head, const void* wq_f16,
+                                   const float* wq_alpha, const float* wq_beta, const void* wk_f16,
+                                   const float* wk_alpha, const float* wk_beta, const void* wv_f16,
+                                   const float* wv_alpha, const float* wv_beta,
+                                   const float* rope_cos, const float* rope_sin, int n_pos,
+                                   int start_pos, void* q, void* k_cache, void* v_cache, int ctx,
+                                   void* stream);
+
+/* walsh_attn_out_tc_fwd: for the fp16 attention output o [ntok, 512]
+ * (token-major, 32 heads x 16) and a bf16 residual stream x: optional Hadamard head mixing (wmix_f16 = W^T per head,
+ * beta_mix [16]; NULL skips it), the wo HadamardLinear, and the mHC site
+ * epilogue x_out = H_res x + H_post f (x, x_out [ntok, 4, 512], may alias;
+ * hmix as walsh_mhc_map).  Replaces CausalSelfAttention.forward lines
+ * 468-483 (src/model/chassis.py) and mHCResidualStream.forward lines 366-381
+ * (src/model/mhc.py). */
+walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const void* wmix_f16,
+                                   const float* beta_mix, const void* wo_f16,
+                                   const float* wo_alpha, const float* wo_beta, const void* x,
+                                   const float* hmix, void* x_out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * mHC residual streams (n_streams = 4)
@@ -139,14 +179,17 @@ walsh_status walsh_attn_fwd(const void* q, const void* k_cache, const void* v_ca
  *   u = sum_j H_pre[j] x_j, then (if norm_w != NULL) the chassis RMSNorm
  *   u / sqrt(mean(u^2) + norm_eps) * norm_w.
  * mparams: float [28] = {a_pre, a_post, a_res, unused, b_pre[4], b_post[4],
- * b_res[16]}.  Writes u [ntok, C] and hmix float [ntok, 24] =
+ * b_res[16]}.  phi_bf16 (optional, may be NULL): a bfloat16 copy of phi; with
+ * bf16 x it selects the tensor-core kernel (C = 512 or 2048).  u is written
+ * in u_dtype (the model's bf16 mode writes fp16).  Writes u [ntok, C] and hmix float [ntok, 24] =
  * {H_pre[4], H_post[4], H_res[16] row-major}.
  * Replaces ResidualStreamMapping.forward x3 and the pre-mix of
  * mHCResidualStream.forward (src/model/mhc.py:283-318, 345-364) plus the
  * attention_norm / ffn_norm RMSNorm of mHCLlamaBlock (src/model/mhc.py:514-523). */
 walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
-                           const float* mparams, float map_eps, const float* norm_w,
-                           float norm_eps, void* u, float* hmix, void* stream);
+                           const void* phi_bf16, const float* mparams, float map_eps,
+                           const float* norm_w, float norm_eps, void* u, int u_dtype, float* hmix,
+                           void* stream);
 
 /* Site epilogue: x_out[i] = sum_j H_res[i][j] x[j] + H_post[i] f for each
  * token (x, x_out: [ntok, 4, C]; f: [ntok, C]; x_out may alias x).
@@ -179,19 +222,32 @@ walsh_status walsh_sinkhorn(const float* h, int64_t n, int iters, float eps, flo
  * (FastMoEExperts with caller-given routing weights; mask/probs/weights
  * outputs are then not written).
  * When fuse_post != 0, `y` is not written; instead the mHC site epilogue is
- * applied: x_out = H_res x + H_post y (x, x_out [ntok, 4, C], hmix as
- * walsh_mhc_map; x_out may alias x).  mask_out (uint8 [ntok, E]), probs_out
+ * applied: x_out = H_res x + H_post y (x, x_out [ntok, 4, C] in x_dtype, hmix
+ * as walsh_mhc_map; x_out may alias x).  mask_out (uint8 [ntok, E]), probs_out
  * and weights_out (float [ntok, E]) are optional (NULL to skip).
+ * tc (host pointer, may be NULL): bf16/fp16 copies of the weights; with bf16
+ * or fp16 u, C = 512 and a bf16 stream they select the tensor-core kernel (router and
+ * experts on m16n8k16 MMAs; all experts evaluated densely and weighted by
+ * the routing weight, zero outside the top-k, as the reference does).
  * Replaces HadamardRouter.forward (src/model/moe.py:418-447),
  * FastMoEExperts.forward (src/model/moe.py:337-380) and HadamardMoE.forward
  * (src/model/moe.py:512-542) followed by the ffn-site epilogue of
  * mHCResidualStream.forward (src/model/mhc.py:366-381). */
+typedef struct {   /* all in the dtype of u (bf16 or fp16) */
+  const void* w1;   /* [C/4, C]   router layer 1 (nn.Linear layout) */
+  const void* w2;   /* [E, C/4]   router layer 2 */
+  const void* gate; /* [E, 128, 32] ternary values, gamma not applied */
+  const void* up;   /* [E, 128, 32] */
+  const void* down; /* [E, 32, 128] */
+} walsh_moe_tc_weights;
+
 walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int top_k,
                            const float* w1t, const float* w2, const uint8_t* gate_2bit,
                            const uint8_t* up_2bit, const uint8_t* down_2bit, const float* gammas,
-                           void* y, int fuse_post, const void* x, const float* hmix, void* x_out,
-                           const float* weights_in, uint8_t* mask_out, float* probs_out,
-                           float* weights_out, void* stream);
+                           void* y, int fuse_post, const void* x, int x_dtype, const float* hmix,
+                           void* x_out, const float* weights_in, uint8_t* mask_out,
+                           float* probs_out, float* weights_out, const walsh_moe_tc_weights* tc,
+                           void* stream);
 
 /* ---------------------------------------------------------------------------
  * Channel modulation (x viewed as [nseg, seg_len, C], segment = seg_len

@@ -57,7 +57,7 @@ def test_fault_injection(monkeypatch):
     L = _lib.lib()
     monkeypatch.setenv("WALSH_INJECT_FAULT", "moe_fwd")
     p = ctypes.c_void_p(16)
-    rc = L.walsh_moe_fwd(p, 0, 4, 512, 6, p, p, p, p, p, p, p, 0, None, None, None, None, None, None, None, None)
+    rc = L.walsh_moe_fwd(p, 0, 4, 512, 6, p, p, p, p, p, p, p, 0, None, 0, None, None, None, None, None, None, None, None)
     assert rc == -7
     monkeypatch.setenv("WALSH_INJECT_FAULT", "sinkhorn")
     with pytest.raises(_lib.WalshError, match="injected"):

@@ -16,7 +16,7 @@ import torch
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libwalsh.so")
 
-F32, BF16 = 0, 1
+F32, BF16, F16 = 0, 1, 2
 P = c_void_p
 
 # name -> argument types (restype is int/walsh_status unless listed in _RESTYPE)
@@ -28,12 +28,17 @@ SIGNATURES = {
     "walsh_hadamard_linear_fwd": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, P, c_int, P],
     "walsh_head_mixer_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P],
     "walsh_attn_qkv_fwd": [P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_int, c_int,
-                           P, P, P, c_int, P],
+                           P, P, P, c_int, c_int, P],
     "walsh_attn_fwd": [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P],
-    "walsh_mhc_map": [P, c_int, c_int64, c_int, P, P, c_float, P, c_float, P, P, P],
+    "walsh_hadamard_linear_tc_fwd": [P, c_int64, P, c_float, P, P, P, P],
+    "walsh_attn_qkv_tc_fwd": [P, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_int, c_int, P, P, P,
+                              c_int, P],
+    "walsh_attn_out_tc_fwd": [P, c_int64, P, P, P, P, P, P, P, P, P],
+    "walsh_mhc_map": [P, c_int, c_int64, c_int, P, P, P, c_float, P, c_float, P, c_int, P, P],
     "walsh_mhc_post": [P, P, P, c_int, c_int64, c_int, P, P],
     "walsh_sinkhorn": [P, c_int64, c_int, c_float, P, P],
-    "walsh_moe_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, P, c_int, P, P, P, P, P, P, P, P],
+    "walsh_moe_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, P, c_int, P, c_int, P, P, P, P, P, P, P,
+                      P],
     "walsh_chmod_chunk_rows": [c_int],
     "walsh_chmod_stats": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P],
     "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],
@@ -45,6 +50,11 @@ SIGNATURES = {
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p}
 # entry points that return a plain int rather than a status
 _PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows"}
+
+
+class MoeTcWeights(ctypes.Structure):
+    """walsh_moe_tc_weights: bfloat16 copies of the router / expert weights."""
+    _fields_ = [("w1", P), ("w2", P), ("gate", P), ("up", P), ("down", P)]
 
 
 class WalshError(RuntimeError):
@@ -101,7 +111,17 @@ def dcode(dtype: torch.dtype) -> int:
         return F32
     if dtype == torch.bfloat16:
         return BF16
-    raise TypeError(f"walsh kernels take float32 or bfloat16 activations, got {dtype}")
+    if dtype == torch.float16:
+        return F16
+    raise TypeError(f"walsh kernels take float32, bfloat16 or float16 activations, got {dtype}")
+
+
+def inner_dtype(stream_dtype: torch.dtype) -> torch.dtype:
+    """Storage type of the normalised activations (u, q/k/v, attention output)
+    for a residual stream of ``stream_dtype``: float16 next to a bfloat16
+    stream (values are bounded by the normalisations, fp16 keeps 3 more
+    mantissa bits), float32 next to a float32 stream."""
+    return torch.float16 if stream_dtype == torch.bfloat16 else stream_dtype
 
 
 def stream() -> int:

@@ -142,23 +142,22 @@ attn_decode_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* _
 // O += P V with m16n8k16 bf16 MMAs (fp32 accumulate), the S accumulators
 // re-packed in registers as the A operand of P V; online softmax in exp2.
 // ---------------------------------------------------------------------------
-template <int HD>
+template <int HD, typename TE>
 __global__ void __launch_bounds__(256)
-attn_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
-                const __nv_bfloat16* __restrict__ vc, int H, int Tq, int ctx, int start_pos, float scale_log2,
-                __nv_bfloat16* __restrict__ o) {
+attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* __restrict__ vc, int H, int Tq,
+                int ctx, int start_pos, float scale_log2, TE* __restrict__ o) {
   constexpr int QT = 128, KT = 64, LD = HD + 8;  // padded rows: conflict-free ldmatrix
   constexpr int CH = HD / 8;                     // 16-byte chunks per row
-  __shared__ __align__(16) __nv_bfloat16 Qs[QT][LD];
-  __shared__ __align__(16) __nv_bfloat16 Ks[2][KT][LD];
-  __shared__ __align__(16) __nv_bfloat16 Vs[2][KT][LD];
+  __shared__ __align__(16) TE Qs[QT][LD];
+  __shared__ __align__(16) TE Ks[2][KT][LD];
+  __shared__ __align__(16) TE Vs[2][KT][LD];
   const int b = blockIdx.z, h = blockIdx.y;
   const int q0 = (gridDim.x - 1 - blockIdx.x) * QT;  // longest (latest) query tiles first
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const size_t bh = (size_t)b * H + h;
-  const __nv_bfloat16* qb = q + bh * Tq * HD;
-  const __nv_bfloat16* kb = kc + bh * ctx * HD;
-  const __nv_bfloat16* vb = vc + bh * ctx * HD;
+  const TE* qb = q + bh * Tq * HD;
+  const TE* kb = kc + bh * ctx * HD;
+  const TE* vb = vc + bh * ctx * HD;
   const int kend = start_pos + min(q0 + QT, Tq);  // keys [0, kend) are visible to some query here
   const int nkt = (kend + KT - 1) / KT;
 
@@ -173,7 +172,7 @@ attn_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __rest
       const int r = j / CH, c = j - r * CH;
       const int key = kt * KT + r;
       const bool in = key < kend;
-      const __nv_bfloat16* src = (which ? vb : kb) + (size_t)(in ? key : 0) * HD + c * 8;
+      const TE* src = (which ? vb : kb) + (size_t)(in ? key : 0) * HD + c * 8;
       cp_async16(which ? &Vs[buf][r][c * 8] : &Ks[buf][r][c * 8], src, in ? 16 : 0);
     }
   };
@@ -211,8 +210,8 @@ attn_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __rest
         for (int np = 0; np < KT / 16; ++np) {
           uint32_t kf[4];
           ldsm_x4(kf, &Ks[buf][np * 16 + (lane & 7) + ((lane >> 4) << 3)][ks * 16 + ((lane >> 3) & 1) * 8]);
-          mma_bf16(s[2 * np], qf[ks], kf[0], kf[1]);
-          mma_bf16(s[2 * np + 1], qf[ks], kf[2], kf[3]);
+          mma16<TE>(s[2 * np], qf[ks], kf[0], kf[1]);
+          mma16<TE>(s[2 * np + 1], qf[ks], kf[2], kf[3]);
         }
       const bool diag = (kt + 1) * KT - 1 > start_pos + q0 + qrow0;  // tile may hold masked keys
       float mt_lo = -CUDART_INF_F, mt_hi = -CUDART_INF_F;
@@ -252,8 +251,8 @@ attn_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __rest
         const float p2 = exp2f(s[n][2] - sub_hi), p3 = exp2f(s[n][3] - sub_hi);
         rs_lo += p0 + p1;
         rs_hi += p2 + p3;
-        pf[n >> 1][(n & 1) * 2 + 0] = pack_bf16(p0, p1);
-        pf[n >> 1][(n & 1) * 2 + 1] = pack_bf16(p2, p3);
+        pf[n >> 1][(n & 1) * 2 + 0] = pack2<TE>(p0, p1);
+        pf[n >> 1][(n & 1) * 2 + 1] = pack2<TE>(p2, p3);
       }
       l_lo = l_lo * corr_lo + rs_lo;
       l_hi = l_hi * corr_hi + rs_hi;
@@ -270,8 +269,8 @@ attn_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __rest
         for (int dp = 0; dp < HD / 16; ++dp) {
           uint32_t vf[4];
           ldsm_x4_t(vf, &Vs[buf][kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8]);
-          mma_bf16(oacc[2 * dp], a, vf[0], vf[1]);
-          mma_bf16(oacc[2 * dp + 1], a, vf[2], vf[3]);
+          mma16<TE>(oacc[2 * dp], a, vf[0], vf[1]);
+          mma16<TE>(oacc[2 * dp + 1], a, vf[2], vf[3]);
         }
       }
     }
@@ -289,10 +288,10 @@ attn_mma_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __rest
     const int d = i * 8 + 2 * t4;
     if (t_lo < Tq)
       *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + t_lo) * H + h) * HD + d) =
-          pack_bf16(oacc[i][0] * inv_lo, oacc[i][1] * inv_lo);
+          pack2<TE>(oacc[i][0] * inv_lo, oacc[i][1] * inv_lo);
     if (t_hi < Tq)
       *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + t_hi) * H + h) * HD + d) =
-          pack_bf16(oacc[i][2] * inv_hi, oacc[i][3] * inv_hi);
+          pack2<TE>(oacc[i][2] * inv_hi, oacc[i][3] * inv_hi);
   }
 }
 
@@ -301,12 +300,13 @@ static int launch_attn(const void* q, const void* kc, const void* vc, int B, int
                        int start_pos, void* o, cudaStream_t s) {
   const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
   const bool aligned = ((((uintptr_t)q) | ((uintptr_t)kc) | ((uintptr_t)vc)) & 15u) == 0;
-  if (sizeof(T) == 2 && Tq > 4 && aligned) {
-    dim3 grid((Tq + 127) / 128, H, B);
-    attn_mma_kernel<HD><<<grid, 256, 0, s>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)kc,
-                                             (const __nv_bfloat16*)vc, H, Tq, ctx, start_pos, scale_log2,
-                                             (__nv_bfloat16*)o);
-    return launch_status();
+  if constexpr (sizeof(T) == 2) {
+    if (Tq > 4 && aligned) {
+      dim3 grid((Tq + 127) / 128, H, B);
+      attn_mma_kernel<HD, T><<<grid, 256, 0, s>>>((const T*)q, (const T*)kc, (const T*)vc, H, Tq, ctx, start_pos,
+                                                 scale_log2, (T*)o);
+      return launch_status();
+    }
   }
   if (Tq <= 4) {
     dim3 grid(Tq, H, B);
@@ -333,9 +333,7 @@ extern "C" walsh_status walsh_attn_fwd(const void* q, const void* k_cache, const
   WALSH_CHECK_SHAPE(B > 0 && H > 0 && T > 0 && start_pos >= 0 && start_pos + T <= ctx);
   WALSH_CHECK_SHAPE(B <= 65535 && H <= 65535);
   cudaStream_t s = (cudaStream_t)stream;
-  if (hd == 16) return dtype == WALSH_F32 ? launch_attn<16, float>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s)
-                                          : launch_attn<16, __nv_bfloat16>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s);
-  if (hd == 32) return dtype == WALSH_F32 ? launch_attn<32, float>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s)
-                                          : launch_attn<32, __nv_bfloat16>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s);
-  return WALSH_ERR_SHAPE;
+  if (hd != 16 && hd != 32) return WALSH_ERR_SHAPE;
+  return WALSH_DISPATCH_DTYPE(dtype, ET, hd == 16 ? launch_attn<16, ET>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s)
+                                                  : launch_attn<32, ET>(q, k_cache, v_cache, B, H, T, ctx, start_pos, o, s));
 }

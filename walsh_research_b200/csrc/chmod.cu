@@ -139,12 +139,9 @@ extern "C" walsh_status walsh_chmod_stats(const void* x, int dtype, int64_t nrow
   WALSH_CHECK_SHAPE(nseg <= 65535);
   dim3 grid((seg_len + kChunkRows - 1) / kChunkRows, (unsigned)nseg);
   cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == WALSH_F32)
-    chmod_stats_kernel<float><<<grid, 256, 0, s>>>((const float*)x, C, seg_len, norm_w, norm_eps, partial);
-  else
-    chmod_stats_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)x, C, seg_len, norm_w, norm_eps,
-                                                           partial);
-  return launch_status();
+  return WALSH_DISPATCH_DTYPE(dtype, T, (chmod_stats_kernel<T><<<grid, 256, 0, s>>>((const T*)x, C, seg_len, norm_w,
+                                                                                  norm_eps, partial),
+                                         launch_status()));
 }
 
 extern "C" walsh_status walsh_chmod_mlp(const float* partial, int nseg, int seg_len, int C, const uint8_t* w1_2bit,
@@ -170,12 +167,8 @@ extern "C" walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrow
   int64_t g = (nrows + 7) / 8;
   if (g > 148 * 32) g = 148 * 32;
   cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == WALSH_F32)
-    chmod_apply_kernel<float><<<(unsigned)g, 256, 0, s>>>((const float*)x, nrows, C, seg_len, norm_w, norm_eps, scale,
-                                                          shift, residual_scale, add_input, (float*)out);
-  else
-    chmod_apply_kernel<__nv_bfloat16><<<(unsigned)g, 256, 0, s>>>((const __nv_bfloat16*)x, nrows, C, seg_len, norm_w,
-                                                                  norm_eps, scale, shift, residual_scale, add_input,
-                                                                  (__nv_bfloat16*)out);
-  return launch_status();
+  return WALSH_DISPATCH_DTYPE(dtype, T, (chmod_apply_kernel<T><<<(unsigned)g, 256, 0, s>>>(
+                                             (const T*)x, nrows, C, seg_len, norm_w, norm_eps, scale, shift,
+                                             residual_scale, add_input, (T*)out),
+                                         launch_status()));
 }

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "walsh.h"
@@ -18,9 +19,14 @@ constexpr int kBlock = 32;       // Hadamard block width (experts, channel modul
 // ---- activation storage types -------------------------------------------------
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 template <typename T> __device__ __forceinline__ T from_f(float v);
 template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+// fp16 stores saturate at +-65504 rather than overflowing to inf
+template <> __device__ __forceinline__ __half from_f<__half>(float v) {
+  return __float2half_rn(fminf(fmaxf(v, -65504.f), 65504.f));
+}
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
@@ -69,7 +75,15 @@ __device__ __forceinline__ float tern_val(uint32_t byte, int j) {
 #define WALSH_CHECK_SHAPE(cond) \
   do { if (!(cond)) return WALSH_ERR_SHAPE; } while (0)
 #define WALSH_CHECK_DTYPE(d) \
-  do { if ((d) != WALSH_F32 && (d) != WALSH_BF16) return WALSH_ERR_DTYPE; } while (0)
+  do { if ((d) != WALSH_F32 && (d) != WALSH_BF16 && (d) != WALSH_F16) return WALSH_ERR_DTYPE; } while (0)
+
+// Calls F<T>(args...) with T the storage type of dtype code d.
+#define WALSH_DISPATCH_DTYPE(d, T, ...)                        \
+  [&]() -> int {                                               \
+    if ((d) == WALSH_F32) { using T = float; return __VA_ARGS__; }         \
+    if ((d) == WALSH_BF16) { using T = __nv_bfloat16; return __VA_ARGS__; } \
+    { using T = __half; return __VA_ARGS__; }                  \
+  }()
 
 namespace walsh {
 // Returns WALSH_ERR_INJECTED when the host-side fault injector is armed for

@@ -94,20 +94,6 @@ static int launch_linear(const void* x, int64_t M, int K, int64_t ldx, const voi
   return launch_status();
 }
 
-template <typename Tx, typename Tw>
-static int linear_y(const void* x, int64_t M, int K, int64_t ldx, const void* w, int64_t N, const float* bias,
-                    void* y, int yd, cudaStream_t s) {
-  if (yd == WALSH_F32) return launch_linear<Tx, Tw, float>(x, M, K, ldx, w, N, bias, y, s);
-  return launch_linear<Tx, Tw, __nv_bfloat16>(x, M, K, ldx, w, N, bias, y, s);
-}
-
-template <typename Tx>
-static int linear_w(const void* x, int64_t M, int K, int64_t ldx, const void* w, int wd, int64_t N,
-                    const float* bias, void* y, int yd, cudaStream_t s) {
-  if (wd == WALSH_F32) return linear_y<Tx, float>(x, M, K, ldx, w, N, bias, y, yd, s);
-  return linear_y<Tx, __nv_bfloat16>(x, M, K, ldx, w, N, bias, y, yd, s);
-}
-
 }  // namespace walsh
 
 using namespace walsh;
@@ -122,12 +108,9 @@ extern "C" walsh_status walsh_embed_gather(const int64_t* idx, int64_t ntok, con
   int64_t g = (ntok * D + 255) / 256;
   if (g > 148 * 16) g = 148 * 16;
   cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == WALSH_F32)
-    gather_kernel<float><<<(unsigned)g, 256, 0, s>>>(idx, ntok, (const float*)table, V, D, (float*)out, err);
-  else
-    gather_kernel<__nv_bfloat16><<<(unsigned)g, 256, 0, s>>>(idx, ntok, (const __nv_bfloat16*)table, V, D,
-                                                             (__nv_bfloat16*)out, err);
-  return launch_status();
+  return WALSH_DISPATCH_DTYPE(dtype, T, (gather_kernel<T><<<(unsigned)g, 256, 0, s>>>(idx, ntok, (const T*)table, V, D,
+                                                                                    (T*)out, err),
+                                         launch_status()));
 }
 
 extern "C" walsh_status walsh_linear_fwd(const void* x, int x_dtype, int64_t M, int K, int64_t ldx, const void* w,
@@ -142,8 +125,8 @@ extern "C" walsh_status walsh_linear_fwd(const void* x, int x_dtype, int64_t M, 
   WALSH_CHECK_SHAPE((M + 63) / 64 <= 65535);
   if (M == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  if (x_dtype == WALSH_F32) return linear_w<float>(x, M, K, ldx, w, w_dtype, N, bias, y, y_dtype, s);
-  return linear_w<__nv_bfloat16>(x, M, K, ldx, w, w_dtype, N, bias, y, y_dtype, s);
+  return WALSH_DISPATCH_DTYPE(x_dtype, TX, WALSH_DISPATCH_DTYPE(w_dtype, TW, WALSH_DISPATCH_DTYPE(y_dtype, TY,
+      (launch_linear<TX, TW, TY>(x, M, K, ldx, w, N, bias, y, s)))));
 }
 
 extern "C" walsh_status walsh_rmsnorm(const void* x, int dtype, int64_t rows, int C, const float* w, float eps,
@@ -157,14 +140,6 @@ extern "C" walsh_status walsh_rmsnorm(const void* x, int dtype, int64_t rows, in
   int64_t g = (rows + 7) / 8;
   if (g > 148 * 32) g = 148 * 32;
   cudaStream_t s = (cudaStream_t)stream;
-  using bf = __nv_bfloat16;
-  if (dtype == WALSH_F32 && y_dtype == WALSH_F32)
-    rmsnorm_kernel<float, float><<<(unsigned)g, 256, 0, s>>>((const float*)x, rows, C, w, eps, (float*)y);
-  else if (dtype == WALSH_F32)
-    rmsnorm_kernel<float, bf><<<(unsigned)g, 256, 0, s>>>((const float*)x, rows, C, w, eps, (bf*)y);
-  else if (y_dtype == WALSH_F32)
-    rmsnorm_kernel<bf, float><<<(unsigned)g, 256, 0, s>>>((const bf*)x, rows, C, w, eps, (float*)y);
-  else
-    rmsnorm_kernel<bf, bf><<<(unsigned)g, 256, 0, s>>>((const bf*)x, rows, C, w, eps, (bf*)y);
-  return launch_status();
+  return WALSH_DISPATCH_DTYPE(dtype, T, WALSH_DISPATCH_DTYPE(y_dtype, TY,
+      (rmsnorm_kernel<T, TY><<<(unsigned)g, 256, 0, s>>>((const T*)x, rows, C, w, eps, (TY*)y), launch_status())));
 }

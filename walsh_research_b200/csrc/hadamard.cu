@@ -157,9 +157,9 @@ hlin_kernel(const Tin* __restrict__ x, int64_t ntok, const uint8_t* __restrict__
 // KV caches [B,H,ctx,hd].  The raw token tile is loaded once and re-scaled by
 // each projection's alpha.
 // ---------------------------------------------------------------------------
-template <int IO, typename T>
+template <int IO, typename TI, typename T>
 __global__ void __launch_bounds__(256)
-qkv_kernel(const T* __restrict__ u, int64_t ntok, const uint8_t* __restrict__ wq,
+qkv_kernel(const TI* __restrict__ u, int64_t ntok, const uint8_t* __restrict__ wq,
            const uint8_t* __restrict__ wk, const uint8_t* __restrict__ wv, const float* __restrict__ aq,
            const float* __restrict__ ak, const float* __restrict__ av, const float* __restrict__ bq,
            const float* __restrict__ bk, const float* __restrict__ bv, T* __restrict__ q,
@@ -277,22 +277,19 @@ static int launch_hlin(const void* x, int64_t ntok, const uint8_t* wp, float out
 template <int IN_O, int OUT_O>
 static int dispatch_hlin(const void* x, int xd, int64_t ntok, const uint8_t* wp, float out_scale,
                          const float* alpha, const float* beta, void* y, int yd, cudaStream_t s) {
-  using bf = __nv_bfloat16;
-  if (xd == WALSH_F32 && yd == WALSH_F32) return launch_hlin<IN_O, OUT_O, float, float>(x, ntok, wp, out_scale, alpha, beta, y, s);
-  if (xd == WALSH_F32 && yd == WALSH_BF16) return launch_hlin<IN_O, OUT_O, float, bf>(x, ntok, wp, out_scale, alpha, beta, y, s);
-  if (xd == WALSH_BF16 && yd == WALSH_F32) return launch_hlin<IN_O, OUT_O, bf, float>(x, ntok, wp, out_scale, alpha, beta, y, s);
-  return launch_hlin<IN_O, OUT_O, bf, bf>(x, ntok, wp, out_scale, alpha, beta, y, s);
+  return WALSH_DISPATCH_DTYPE(xd, TX, WALSH_DISPATCH_DTYPE(yd, TY,
+      (launch_hlin<IN_O, OUT_O, TX, TY>(x, ntok, wp, out_scale, alpha, beta, y, s))));
 }
 
-template <int IO, typename T>
+template <int IO, typename TI, typename T>
 static int launch_qkv(const void* u, int64_t ntok, const uint8_t* const* w, const float* const* a,
                       const float* const* b, void* q, void* kc, void* vc, QkvEpilogue ep, cudaStream_t s) {
   using C = HCfg<IO, IO>;
   const size_t smem = (2 * C::XS + C::YS) * sizeof(float);
-  auto kern = qkv_kernel<IO, T>;
+  auto kern = qkv_kernel<IO, TI, T>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t grid = (ntok + C::TM - 1) / C::TM;
-  kern<<<(unsigned)grid, 256, smem, s>>>((const T*)u, ntok, w[0], w[1], w[2], a[0], a[1], a[2], b[0], b[1],
+  kern<<<(unsigned)grid, 256, smem, s>>>((const TI*)u, ntok, w[0], w[1], w[2], a[0], a[1], a[2], b[0], b[1],
                                          b[2], (T*)q, (T*)kc, (T*)vc, ep);
   return launch_status();
 }
@@ -338,9 +335,10 @@ extern "C" walsh_status walsh_attn_qkv_fwd(const void* u, int dtype, int B, int 
                                            const uint8_t* wv_2bit, const float* wv_alpha, const float* wv_beta,
                                            const float* rope_cos, const float* rope_sin, int n_pos,
                                            int start_pos, void* q, void* k_cache, void* v_cache, int ctx,
-                                           void* stream) {
+                                           int out_dtype, void* stream) {
   if (int e = injected("attn_qkv_fwd")) return e;
   WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_DTYPE(out_dtype);
   WALSH_CHECK_ARG(u && wq_2bit && wq_alpha && wq_beta && wk_2bit && wk_alpha && wk_beta && wv_2bit &&
                   wv_alpha && wv_beta && rope_cos && rope_sin && q && k_cache && v_cache);
   WALSH_CHECK_SHAPE(B > 0 && T > 0 && n_head > 0 && C % n_head == 0 && C % 32 == 0);
@@ -353,11 +351,10 @@ extern "C" walsh_status walsh_attn_qkv_fwd(const void* u, int dtype, int B, int 
   const int64_t ntok = (int64_t)B * T;
   cudaStream_t s = (cudaStream_t)stream;
   const int io = C / 32;
-  if (io == 16) return dtype == WALSH_F32 ? launch_qkv<16, float>(u, ntok, w, a, b, q, k_cache, v_cache, ep, s)
-                                          : launch_qkv<16, __nv_bfloat16>(u, ntok, w, a, b, q, k_cache, v_cache, ep, s);
-  if (io == 64) return dtype == WALSH_F32 ? launch_qkv<64, float>(u, ntok, w, a, b, q, k_cache, v_cache, ep, s)
-                                          : launch_qkv<64, __nv_bfloat16>(u, ntok, w, a, b, q, k_cache, v_cache, ep, s);
-  return WALSH_ERR_SHAPE;
+  if (io != 16 && io != 64) return WALSH_ERR_SHAPE;
+  return WALSH_DISPATCH_DTYPE(dtype, TI, WALSH_DISPATCH_DTYPE(out_dtype, TO,
+      io == 16 ? launch_qkv<16, TI, TO>(u, ntok, w, a, b, q, k_cache, v_cache, ep, s)
+               : launch_qkv<64, TI, TO>(u, ntok, w, a, b, q, k_cache, v_cache, ep, s)));
 }
 
 extern "C" walsh_status walsh_head_mixer_fwd(const void* x, int dtype, int64_t ntok, int n_head, int hd,
@@ -369,9 +366,7 @@ extern "C" walsh_status walsh_head_mixer_fwd(const void* x, int dtype, int64_t n
   if (ntok == 0) return WALSH_OK;
   const int64_t units = ntok * (n_head / 32);
   cudaStream_t s = (cudaStream_t)stream;
-  if (hd == 16) return dtype == WALSH_F32 ? launch_headmix<16, float>(x, units, W, beta, y, s)
-                                          : launch_headmix<16, __nv_bfloat16>(x, units, W, beta, y, s);
-  if (hd == 32) return dtype == WALSH_F32 ? launch_headmix<32, float>(x, units, W, beta, y, s)
-                                          : launch_headmix<32, __nv_bfloat16>(x, units, W, beta, y, s);
-  return WALSH_ERR_SHAPE;
+  if (hd != 16 && hd != 32) return WALSH_ERR_SHAPE;
+  return WALSH_DISPATCH_DTYPE(dtype, T, hd == 16 ? launch_headmix<16, T>(x, units, W, beta, y, s)
+                                                 : launch_headmix<32, T>(x, units, W, beta, y, s));
 }

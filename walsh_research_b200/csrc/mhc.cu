@@ -6,7 +6,10 @@
 // [24 x 4C] projection, then sigmoid / 2*sigmoid / Sinkhorn-20 in registers,
 // followed by the pre-mix H_pre @ x (src/model/mhc.py:364) and the block's
 // attention_norm / ffn_norm RMSNorm (src/model/mhc.py:514-523).
+#include <type_traits>
+
 #include "common.cuh"
+#include "mma.cuh"
 
 namespace walsh {
 
@@ -51,11 +54,11 @@ __device__ __forceinline__ void map_activations(const float* d, const float* __r
 
 // CTA = 8 warps x TPW tokens.  phi is staged through shared memory in chunks
 // of KC columns so that each phi value read serves TPW tokens.
-template <typename T, int TPW>
+template <typename T, typename TU, int TPW>
 __global__ void __launch_bounds__(256)
 mhc_map_kernel(const T* __restrict__ x, int64_t ntok, int C, const float* __restrict__ phi,
                const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
-               T* __restrict__ u, float* __restrict__ hmix) {
+               TU* __restrict__ u, float* __restrict__ hmix) {
   constexpr int KC = 128;
   extern __shared__ float4 smem4[];
   float* phis = reinterpret_cast<float*>(smem4);      // [24][KC]
@@ -139,12 +142,154 @@ mhc_map_kernel(const T* __restrict__ x, int64_t ntok, int C, const float* __rest
     }
     s2 = warp_sum(s2);
     const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
-    T* ut = u + tok * C;
+    TU* ut = u + tok * C;
     for (int c = lane; c < C; c += 32) {
       const float v = uw[c] * rn;
-      ut[c] = from_f<T>(norm_w ? v * __ldg(norm_w + c) : v);
+      ut[c] = from_f<TU>(norm_w ? v * __ldg(norm_w + c) : v);
     }
     __syncwarp();
+  }
+}
+
+// bf16 variant on the tensor cores: CTA = 4 warps x 16 tokens.  Each warp
+// streams its tokens' 4C values through shared memory in 128-column chunks
+// (cp.async, double-buffered), feeds them to m16n8k16 MMAs against phi
+// (bf16 copy, [24, 4C], read through L1) and takes the sum of squares from
+// the same A fragments.  Then lanes 0..15 finish one token each (RMS factor,
+// sigmoid / Sinkhorn) and the warp does the pre-mix + RMSNorm per token.
+template <int C, typename TU>
+__global__ void __launch_bounds__(128)
+mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv_bfloat16* __restrict__ phib,
+                   const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
+                   TU* __restrict__ u, float* __restrict__ hmix) {
+  constexpr int D = 4 * C, KC = 128, LDX = KC + 8, NCH = D / KC;
+  __shared__ __align__(16) __nv_bfloat16 xs[4][2][16][LDX];
+  __shared__ float ds[4][16][kMapRows + 1];
+  __shared__ float sss[4][16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * 16;
+
+  auto load_chunk = [&](int ch, int buf) {
+#pragma unroll
+    for (int i = 0; i < (16 * KC / 8) / 32; ++i) {
+      const int idx = lane + 32 * i;
+      const int r = idx / (KC / 8), c = idx - r * (KC / 8);
+      const bool in = tok0 + r < ntok;
+      const __nv_bfloat16* src = x + (in ? (tok0 + r) * D : 0) + ch * KC + c * 8;
+      cp_async16(&xs[warp][buf][r][c * 8], src, in ? 16 : 0);
+    }
+  };
+  float acc[3][4];
+#pragma unroll
+  for (int n = 0; n < 3; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  float ss_lo = 0.f, ss_hi = 0.f;
+  load_chunk(0, 0);
+  cp_async_commit();
+  for (int ch = 0; ch < NCH; ++ch) {
+    const int buf = ch & 1;
+    if (ch + 1 < NCH) load_chunk(ch + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+#pragma unroll
+    for (int ks = 0; ks < KC / 16; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(a, &xs[warp][buf][lane & 15][ks * 16 + (lane >> 4) * 8]);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&a[r]);
+        const float v0 = __low2float(v), v1 = __high2float(v);
+        if (r & 1) ss_hi = fmaf(v0, v0, fmaf(v1, v1, ss_hi));
+        else ss_lo = fmaf(v0, v0, fmaf(v1, v1, ss_lo));
+      }
+      const int k0 = ch * KC + ks * 16 + 2 * t4;
+#pragma unroll
+      for (int n = 0; n < 3; ++n) {
+        const __nv_bfloat16* prow = phib + (size_t)(8 * n + g) * D + k0;
+        const uint32_t b0 = __ldg(reinterpret_cast<const unsigned int*>(prow));
+        const uint32_t b1 = __ldg(reinterpret_cast<const unsigned int*>(prow + 8));
+        mma_bf16(acc[n], a, b0, b1);
+      }
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    ss_lo += __shfl_xor_sync(0xffffffffu, ss_lo, off);
+    ss_hi += __shfl_xor_sync(0xffffffffu, ss_hi, off);
+  }
+#pragma unroll
+  for (int n = 0; n < 3; ++n) {
+    ds[warp][g][8 * n + 2 * t4] = acc[n][0];
+    ds[warp][g][8 * n + 2 * t4 + 1] = acc[n][1];
+    ds[warp][g + 8][8 * n + 2 * t4] = acc[n][2];
+    ds[warp][g + 8][8 * n + 2 * t4 + 1] = acc[n][3];
+  }
+  if (t4 == 0) {
+    sss[warp][g] = ss_lo;
+    sss[warp][g + 8] = ss_hi;
+  }
+  __syncwarp();
+  if (lane < 16) {
+    const float rms = rsqrtf(sss[warp][lane] / (float)D + map_eps);
+    float d[kMapRows], hm[kMapRows];
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) d[r] = ds[warp][lane][r] * rms;
+    map_activations(d, mp, hm);
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) ds[warp][lane][r] = hm[r];
+    if (tok0 + lane < ntok) {
+#pragma unroll
+      for (int r = 0; r < kMapRows; ++r) hmix[(tok0 + lane) * kMapRows + r] = hm[r];
+    }
+  }
+  __syncwarp();
+  // pre-mix u = sum_j H_pre[j] x_j and the block RMSNorm, 8 columns per lane per step
+  constexpr int VPL = C / 256;  // uint4 chunks per lane
+  for (int t = 0; t < 16; ++t) {
+    const int64_t tok = tok0 + t;
+    if (tok >= ntok) break;
+    const float h0 = ds[warp][t][0], h1 = ds[warp][t][1], h2 = ds[warp][t][2], h3 = ds[warp][t][3];
+    const __nv_bfloat16* xt = x + tok * D;
+    float uv[VPL][8];
+    float s2 = 0.f;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int c = (lane + 32 * v) * 8;
+      const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xt + c));
+      const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xt + C + c));
+      const uint4 q2 = __ldg(reinterpret_cast<const uint4*>(xt + 2 * C + c));
+      const uint4 q3 = __ldg(reinterpret_cast<const uint4*>(xt + 3 * C + c));
+      const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&q0);
+      const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&q1);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&q2);
+      const __nv_bfloat162* p3 = reinterpret_cast<const __nv_bfloat162*>(&q3);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f0 = __bfloat1622float2(p0[e]), f1 = __bfloat1622float2(p1[e]);
+        const float2 f2 = __bfloat1622float2(p2[e]), f3 = __bfloat1622float2(p3[e]);
+        uv[v][2 * e] = ((h0 * f0.x + h1 * f1.x) + h2 * f2.x) + h3 * f3.x;
+        uv[v][2 * e + 1] = ((h0 * f0.y + h1 * f1.y) + h2 * f2.y) + h3 * f3.y;
+        s2 = fmaf(uv[v][2 * e], uv[v][2 * e], fmaf(uv[v][2 * e + 1], uv[v][2 * e + 1], s2));
+      }
+    }
+    s2 = warp_sum(s2);
+    const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int c = (lane + 32 * v) * 8;
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float a = uv[v][2 * e] * rn, b = uv[v][2 * e + 1] * rn;
+        if (norm_w) {
+          a *= __ldg(norm_w + c + 2 * e);
+          b *= __ldg(norm_w + c + 2 * e + 1);
+        }
+        w[e] = sizeof(TU) == 2 && !std::is_same<TU, __nv_bfloat16>::value ? pack_f16_sat(a, b) : pack_bf16(a, b);
+      }
+      *reinterpret_cast<uint4*>(u + tok * C + c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   }
 }
 
@@ -179,14 +324,14 @@ __global__ void sinkhorn_kernel(const float* __restrict__ h, int64_t n, int iter
   }
 }
 
-template <typename T, int TPW>
+template <typename T, typename TU, int TPW>
 static int launch_map(const void* x, int64_t ntok, int C, const float* phi, const float* mp, float map_eps,
                       const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s) {
   const size_t smem = (kMapRows * 128 + 8 * TPW * kMapRows + 8 * C) * sizeof(float);
-  auto kern = mhc_map_kernel<T, TPW>;
+  auto kern = mhc_map_kernel<T, TU, TPW>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t grid = (ntok + 8 * TPW - 1) / (8 * TPW);
-  kern<<<(unsigned)grid, 256, smem, s>>>((const T*)x, ntok, C, phi, mp, map_eps, norm_w, norm_eps, (T*)u, hmix);
+  kern<<<(unsigned)grid, 256, smem, s>>>((const T*)x, ntok, C, phi, mp, map_eps, norm_w, norm_eps, (TU*)u, hmix);
   return launch_status();
 }
 
@@ -200,20 +345,37 @@ static inline int grid_for(int64_t total, int threads) {
 using namespace walsh;
 
 extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
-                                      const float* mparams, float map_eps, const float* norm_w, float norm_eps,
-                                      void* u, float* hmix, void* stream) {
+                                      const void* phi_bf16, const float* mparams, float map_eps,
+                                      const float* norm_w, float norm_eps, void* u, int u_dtype, float* hmix,
+                                      void* stream) {
   if (int e = injected("mhc_map")) return e;
   WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_DTYPE(u_dtype);
   WALSH_CHECK_ARG(x && phi && mparams && u && hmix);
   WALSH_CHECK_SHAPE(ntok >= 0 && C > 0 && C % 32 == 0 && C <= 8192);
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
+  const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_bf16)) & 15u) == 0;
+  if (dtype == WALSH_BF16 && u_dtype != WALSH_F32 && phi_bf16 && vec_ok && (C == 512 || C == 2048)) {
+    const unsigned grid = (unsigned)((ntok + 63) / 64);
+    const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
+    const __nv_bfloat16* pb = (const __nv_bfloat16*)phi_bf16;
+    if (C == 512 && u_dtype == WALSH_F16)
+      mhc_map_mma_kernel<512, __half><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps, (__half*)u, hmix);
+    else if (C == 512)
+      mhc_map_mma_kernel<512, __nv_bfloat16><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps,
+                                                                  (__nv_bfloat16*)u, hmix);
+    else if (u_dtype == WALSH_F16)
+      mhc_map_mma_kernel<2048, __half><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps, (__half*)u, hmix);
+    else
+      mhc_map_mma_kernel<2048, __nv_bfloat16><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps,
+                                                                   (__nv_bfloat16*)u, hmix);
+    return launch_status();
+  }
   const bool big = ntok >= 148 * 64;
-  if (dtype == WALSH_F32)
-    return big ? launch_map<float, 4>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s)
-               : launch_map<float, 1>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s);
-  return big ? launch_map<__nv_bfloat16, 4>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s)
-             : launch_map<__nv_bfloat16, 1>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s);
+  return WALSH_DISPATCH_DTYPE(dtype, TX, WALSH_DISPATCH_DTYPE(u_dtype, TU,
+      big ? launch_map<TX, TU, 4>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s)
+          : launch_map<TX, TU, 1>(x, ntok, C, phi, mparams, map_eps, norm_w, norm_eps, u, hmix, s)));
 }
 
 extern "C" walsh_status walsh_mhc_post(const void* x, const void* f, const float* hmix, int dtype, int64_t ntok,
@@ -225,12 +387,8 @@ extern "C" walsh_status walsh_mhc_post(const void* x, const void* f, const float
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
   const int g = grid_for(ntok * C, 256);
-  if (dtype == WALSH_F32)
-    mhc_post_kernel<float><<<g, 256, 0, s>>>((const float*)x, (const float*)f, hmix, ntok, C, (float*)x_out);
-  else
-    mhc_post_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)f, hmix, ntok, C,
-                                                     (__nv_bfloat16*)x_out);
-  return launch_status();
+  return WALSH_DISPATCH_DTYPE(dtype, T, (mhc_post_kernel<T><<<g, 256, 0, s>>>((const T*)x, (const T*)f, hmix, ntok, C,
+                                                                            (T*)x_out), launch_status()));
 }
 
 extern "C" walsh_status walsh_sinkhorn(const float* h, int64_t n, int iters, float eps, float* out, void* stream) {

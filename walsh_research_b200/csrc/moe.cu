@@ -10,6 +10,7 @@
 #include <math_constants.h>
 
 #include "common.cuh"
+#include "mma.cuh"
 
 namespace walsh {
 
@@ -24,12 +25,12 @@ struct MoeCfg {
   static constexpr int MAXK = 8;   // largest top_k the router accepts
 };
 
-template <typename T, int C>
+template <typename T, typename TX, int C>
 __global__ void __launch_bounds__(256)
 moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __restrict__ w1t,
            const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
            const uint8_t* __restrict__ dp, const float* __restrict__ gammas, T* __restrict__ y, int fuse_post,
-           const T* x, const float* __restrict__ hmix, T* xo, const float* __restrict__ weights_in,
+           const TX* x, const float* __restrict__ hmix, TX* xo, const float* __restrict__ weights_in,
            uint8_t* __restrict__ mask_out, float* __restrict__ probs_out, float* __restrict__ weights_out) {
   using M = MoeCfg<C>;
   constexpr int E = M::E, HID = M::HID, TM = M::TM;
@@ -221,12 +222,225 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
     for (int r = 0; r < 4; ++r) {
       const float* hr = hm + 8 + 4 * r;
       const float v = (((hr[0] * x0 + hr[1] * x1) + hr[2] * x2) + hr[3] * x3) + hm[4 + r] * fv;
-      xo[base + (size_t)r * C] = from_f<T>(v);
+      xo[base + (size_t)r * C] = from_f<TX>(v);
     }
   }
 }
 
-template <typename T, int C>
+// ---------------------------------------------------------------------------
+// bf16 tensor-core variant for C = 512 (E = 16, router hidden 128).
+// CTA = 4 warps x 16 tokens; each warp keeps its 16 token rows of u in shared
+// memory and runs, with m16n8k16 MMAs:
+//   router   h = silu(u W1^T) [16x128] -> logits = h W2^T [16x16] (h re-packed
+//            from accumulators to A fragments in registers);
+//   top-k    lanes 0..15 one token each (softmax, top_k, renormalise);
+//   experts  all 16 experts densely: per expert and per half of the hidden
+//            units, g = u_e G_e^T, v = u_e U_e^T, a = silu(gg g) (gu v),
+//            y_e += a D_e^T; the routing weight (0 when not selected) and gd
+//            scale y_e, then the mHC site epilogue (or a plain store) writes
+//            the expert's 32 columns.
+// Ternary weights are exact in bf16 ({-1, 0, +1}); the gammas are applied in
+// float32.  bf16 weight copies: w1 [128][512], w2 [16][128], gate/up
+// [16][128][32], down [16][32][128].
+// ---------------------------------------------------------------------------
+template <typename TU>
+__global__ void __launch_bounds__(128)
+moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* __restrict__ w1b,
+                  const TU* __restrict__ w2b, const TU* __restrict__ gb, const TU* __restrict__ ub,
+                  const TU* __restrict__ db, const float* __restrict__ gammas, TU* __restrict__ y, int fuse_post,
+                  const __nv_bfloat16* x, const float* __restrict__ hmix, __nv_bfloat16* xo,
+                  uint8_t* __restrict__ mask_out, float* __restrict__ probs_out, float* __restrict__ weights_out) {
+  constexpr int C = 512, E = 16, HID = 128, LDU = C + 8;
+  extern __shared__ float4 smem4[];  // us: [4 warps][16 rows][LDU] (66.5 KB, opt-in size)
+  TU (*us)[16][LDU] = reinterpret_cast<TU (*)[16][LDU]>(smem4);
+  __shared__ float lg[4][16][E + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * 16;
+#pragma unroll
+  for (int i = 0; i < (16 * C / 8) / 32; ++i) {
+    const int idx = lane + 32 * i;
+    const int r = idx / (C / 8), c = idx - r * (C / 8);
+    const bool in = tok0 + r < ntok;
+    cp_async16(&us[warp][r][c * 8], u + (in ? (tok0 + r) * C : 0) + c * 8, in ? 16 : 0);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncwarp();
+
+  // ---- router layer 1: [16 x 512] x [512 x 128]
+  float hacc[HID / 8][4];
+#pragma unroll
+  for (int n = 0; n < HID / 8; ++n) hacc[n][0] = hacc[n][1] = hacc[n][2] = hacc[n][3] = 0.f;
+#pragma unroll 2
+  for (int ks = 0; ks < C / 16; ++ks) {
+    uint32_t a[4];
+    ldsm_x4(a, &us[warp][lane & 15][ks * 16 + (lane >> 4) * 8]);
+#pragma unroll
+    for (int n = 0; n < HID / 8; ++n) {
+      const TU* wr = w1b + (size_t)(8 * n + g) * C + ks * 16 + 2 * t4;
+      mma16<TU>(hacc[n], a, __ldg(reinterpret_cast<const unsigned int*>(wr)),
+                __ldg(reinterpret_cast<const unsigned int*>(wr + 8)));
+    }
+  }
+  // ---- silu, repack as A fragments, router layer 2: [16 x 128] x [128 x 16]
+  float lacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+  for (int kk = 0; kk < HID / 16; ++kk) {
+    uint32_t a[4];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float* c = hacc[2 * kk + half];
+      a[half * 2 + 0] = pack2<TU>(siluf_(c[0]), siluf_(c[1]));
+      a[half * 2 + 1] = pack2<TU>(siluf_(c[2]), siluf_(c[3]));
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const TU* wr = w2b + (size_t)(8 * n + g) * HID + kk * 16 + 2 * t4;
+      mma16<TU>(lacc[n], a, __ldg(reinterpret_cast<const unsigned int*>(wr)),
+                __ldg(reinterpret_cast<const unsigned int*>(wr + 8)));
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+    lg[warp][g][8 * n + 2 * t4] = lacc[n][0];
+    lg[warp][g][8 * n + 2 * t4 + 1] = lacc[n][1];
+    lg[warp][g + 8][8 * n + 2 * t4] = lacc[n][2];
+    lg[warp][g + 8][8 * n + 2 * t4 + 1] = lacc[n][3];
+  }
+  __syncwarp();
+  // ---- softmax + top-k: lane t < 16 owns token t; lg row becomes the routing weight
+  if (lane < 16) {
+    float* l = lg[warp][lane];
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int e = 0; e < E; ++e) mx = fmaxf(mx, l[e]);
+    float p[E], sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) { p[e] = expf(l[e] - mx); sum += p[e]; }
+#pragma unroll
+    for (int e = 0; e < E; ++e) p[e] = __fdiv_rn(p[e], sum);
+    uint32_t chosen = 0;
+    for (int k = 0; k < top_k; ++k) {
+      int best = -1;
+      float bv = -1.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (!((chosen >> e) & 1u) && p[e] > bv) { bv = p[e]; best = e; }
+      if (best < 0)
+        for (int e = E - 1; e >= 0; --e)
+          if (!((chosen >> e) & 1u)) best = e;
+      chosen |= 1u << best;
+    }
+    float wsum = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      if ((chosen >> e) & 1u) wsum += p[e];
+    wsum = fmaxf(wsum, 1e-8f);
+    const int64_t tok = tok0 + lane;
+    const bool in = tok < ntok;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const bool on = (chosen >> e) & 1u;
+      const float w = on ? __fdiv_rn(p[e], wsum) : 0.f;
+      l[e] = w;
+      if (in) {
+        if (mask_out) mask_out[tok * E + e] = on ? 1 : 0;
+        if (probs_out) probs_out[tok * E + e] = p[e];
+        if (weights_out) weights_out[tok * E + e] = w;
+      }
+    }
+  }
+  __syncwarp();
+  if (!gb) return;  // router-only call
+
+  // ---- experts
+  const float gg = __ldg(gammas + 0), gu = __ldg(gammas + 1), gd = __ldg(gammas + 2);
+  const int64_t tlo = tok0 + g, thi = tlo + 8;
+  float hm_lo[20], hm_hi[20];  // {H_post[4], H_res[16]} of rows g and g+8
+  if (fuse_post) {
+#pragma unroll
+    for (int i = 0; i < 20; ++i) {
+      hm_lo[i] = tlo < ntok ? __ldg(hmix + tlo * kMapRows + 4 + i) : 0.f;
+      hm_hi[i] = thi < ntok ? __ldg(hmix + thi * kMapRows + 4 + i) : 0.f;
+    }
+  }
+#pragma unroll 1
+  for (int e = 0; e < E; ++e) {
+    uint32_t ae[2][4];
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) ldsm_x4(ae[ks], &us[warp][lane & 15][e * 32 + ks * 16 + (lane >> 4) * 8]);
+    float yacc[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) yacc[n][0] = yacc[n][1] = yacc[n][2] = yacc[n][3] = 0.f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float ga[8][4], va[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; ++n) ga[n][0] = ga[n][1] = ga[n][2] = ga[n][3] = va[n][0] = va[n][1] = va[n][2] = va[n][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const size_t row = (size_t)e * HID + half * 64 + 8 * n + g;
+          const TU* gr = gb + row * 32 + ks * 16 + 2 * t4;
+          const TU* ur = ub + row * 32 + ks * 16 + 2 * t4;
+          mma16<TU>(ga[n], ae[ks], __ldg(reinterpret_cast<const unsigned int*>(gr)),
+                    __ldg(reinterpret_cast<const unsigned int*>(gr + 8)));
+          mma16<TU>(va[n], ae[ks], __ldg(reinterpret_cast<const unsigned int*>(ur)),
+                    __ldg(reinterpret_cast<const unsigned int*>(ur + 8)));
+        }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {  // hidden units half*64 + 16 kk .. +15
+        uint32_t a[4];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float* G = ga[2 * kk + hh];
+          const float* V = va[2 * kk + hh];
+          a[hh * 2 + 0] = pack2<TU>(siluf_(gg * G[0]) * (gu * V[0]), siluf_(gg * G[1]) * (gu * V[1]));
+          a[hh * 2 + 1] = pack2<TU>(siluf_(gg * G[2]) * (gu * V[2]), siluf_(gg * G[3]) * (gu * V[3]));
+        }
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const TU* dr = db + ((size_t)e * 32 + 8 * n + g) * HID + half * 64 + kk * 16 + 2 * t4;
+          mma16<TU>(yacc[n], a, __ldg(reinterpret_cast<const unsigned int*>(dr)),
+                    __ldg(reinterpret_cast<const unsigned int*>(dr + 8)));
+        }
+      }
+    }
+    const float w_lo = lg[warp][g][e] * gd, w_hi = lg[warp][g + 8][e] * gd;
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int c = e * 32 + 8 * n + 2 * t4;
+      const float y0 = yacc[n][0] * w_lo, y1 = yacc[n][1] * w_lo;
+      const float y2 = yacc[n][2] * w_hi, y3 = yacc[n][3] * w_hi;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int64_t tok = rr ? thi : tlo;
+        if (tok >= ntok) continue;
+        const float ya = rr ? y2 : y0, yb = rr ? y3 : y1;
+        if (!fuse_post) {
+          *reinterpret_cast<uint32_t*>(y + tok * C + c) = pack2<TU>(ya, yb);
+          continue;
+        }
+        const float* hm = rr ? hm_hi : hm_lo;
+        const size_t base = (size_t)tok * 4 * C + c;
+        float2 xv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          xv[j] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + base + (size_t)j * C));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float* hr = hm + 4 + 4 * i;
+          const float va0 = (((hr[0] * xv[0].x + hr[1] * xv[1].x) + hr[2] * xv[2].x) + hr[3] * xv[3].x) + hm[i] * ya;
+          const float va1 = (((hr[0] * xv[0].y + hr[1] * xv[1].y) + hr[2] * xv[2].y) + hr[3] * xv[3].y) + hm[i] * yb;
+          *reinterpret_cast<uint32_t*>(xo + base + (size_t)i * C) = pack_bf16(va0, va1);
+        }
+      }
+    }
+  }
+}
+
+template <typename T, typename TX, int C>
 static int launch_moe(const void* u, int64_t ntok, int top_k, const float* w1t, const float* w2, const uint8_t* gp,
                       const uint8_t* upp, const uint8_t* dp, const float* gammas, void* y, int fuse_post,
                       const void* x, const float* hmix, void* xo, const float* weights_in, uint8_t* mask_out,
@@ -234,11 +448,25 @@ static int launch_moe(const void* u, int64_t ntok, int top_k, const float* w1t, 
   using M = MoeCfg<C>;
   const size_t smem = (2 * M::TM * C + M::TM * M::HID + M::TM * M::E + 8 * kExpertHidden) * sizeof(float) +
                       M::TM * M::E * (sizeof(int) + sizeof(float)) + M::TM * sizeof(int);
-  auto kern = moe_kernel<T, C>;
+  auto kern = moe_kernel<T, TX, C>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t grid = (ntok + M::TM - 1) / M::TM;
   kern<<<(unsigned)grid, 256, smem, s>>>((const T*)u, ntok, top_k, w1t, w2, gp, upp, dp, gammas, (T*)y, fuse_post,
-                                         (const T*)x, hmix, (T*)xo, weights_in, mask_out, probs_out, weights_out);
+                                         (const TX*)x, hmix, (TX*)xo, weights_in, mask_out, probs_out, weights_out);
+  return launch_status();
+}
+
+template <typename TU>
+static int launch_moe_mma(const void* u, int64_t ntok, int top_k, const walsh_moe_tc_weights* tc, bool experts,
+                          const float* gammas, void* y, int fuse_post, const void* x, const float* hmix, void* xo,
+                          uint8_t* mask_out, float* probs_out, float* weights_out, cudaStream_t s) {
+  const unsigned grid = (unsigned)((ntok + 63) / 64);
+  const int smem = 4 * 16 * (512 + 8) * (int)sizeof(TU);
+  cudaFuncSetAttribute(moe_mma512_kernel<TU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  moe_mma512_kernel<TU><<<grid, 128, smem, s>>>(
+      (const TU*)u, ntok, top_k, (const TU*)tc->w1, (const TU*)tc->w2, experts ? (const TU*)tc->gate : nullptr,
+      (const TU*)tc->up, (const TU*)tc->down, gammas, (TU*)y, fuse_post, (const __nv_bfloat16*)x, hmix,
+      (__nv_bfloat16*)xo, mask_out, probs_out, weights_out);
   return launch_status();
 }
 
@@ -249,10 +477,12 @@ using namespace walsh;
 extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int top_k, const float* w1,
                                       const float* w2, const uint8_t* gate_2bit, const uint8_t* up_2bit,
                                       const uint8_t* down_2bit, const float* gammas, void* y, int fuse_post,
-                                      const void* x, const float* hmix, void* x_out, const float* weights_in,
-                                      uint8_t* mask_out, float* probs_out, float* weights_out, void* stream) {
+                                      const void* x, int x_dtype, const float* hmix, void* x_out,
+                                      const float* weights_in, uint8_t* mask_out, float* probs_out,
+                                      float* weights_out, const walsh_moe_tc_weights* tc, void* stream) {
   if (int e = injected("moe_fwd")) return e;
   WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_DTYPE(x_dtype);
   const bool experts = gate_2bit || up_2bit || down_2bit;
   WALSH_CHECK_ARG(u);
   WALSH_CHECK_ARG(weights_in || (w1 && w2));                               // router needs its weights
@@ -265,17 +495,21 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
                   ((((uintptr_t)gate_2bit | (uintptr_t)up_2bit) & 7u) == 0 && ((uintptr_t)down_2bit & 15u) == 0));
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
-#define WALSH_MOE_CASE(CC)                                                                                    \
-  if (C == CC)                                                                                               \
-    return dtype == WALSH_F32                                                                                \
-               ? launch_moe<float, CC>(u, ntok, top_k, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y,    \
-                                       fuse_post, x, hmix, x_out, weights_in, mask_out, probs_out,          \
-                                       weights_out, s)                                                      \
-               : launch_moe<__nv_bfloat16, CC>(u, ntok, top_k, w1, w2, gate_2bit, up_2bit, down_2bit,      \
-                                               gammas, y, fuse_post, x, hmix, x_out, weights_in, mask_out,  \
-                                               probs_out, weights_out, s);
-  WALSH_MOE_CASE(512)
-  WALSH_MOE_CASE(2048)
-#undef WALSH_MOE_CASE
-  return WALSH_ERR_SHAPE;
+  if (dtype != WALSH_F32 && C == 512 && tc && tc->w1 && tc->w2 && !weights_in &&
+      (!experts || (tc->gate && tc->up && tc->down)) && (!fuse_post || x_dtype == WALSH_BF16) &&
+      ((((uintptr_t)u) | ((uintptr_t)tc->w1) | ((uintptr_t)tc->w2) | ((uintptr_t)tc->gate) |
+        ((uintptr_t)tc->up) | ((uintptr_t)tc->down)) & 15u) == 0) {
+    return dtype == WALSH_F16
+               ? launch_moe_mma<__half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out, mask_out,
+                                        probs_out, weights_out, s)
+               : launch_moe_mma<__nv_bfloat16>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out,
+                                               mask_out, probs_out, weights_out, s);
+  }
+  if (C != 512 && C != 2048) return WALSH_ERR_SHAPE;
+  return WALSH_DISPATCH_DTYPE(dtype, TU, WALSH_DISPATCH_DTYPE(x_dtype, TX,
+      C == 512 ? launch_moe<TU, TX, 512>(u, ntok, top_k, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y, fuse_post,
+                                         x, hmix, x_out, weights_in, mask_out, probs_out, weights_out, s)
+               : launch_moe<TU, TX, 2048>(u, ntok, top_k, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y,
+                                          fuse_post, x, hmix, x_out, weights_in, mask_out, probs_out, weights_out,
+                                          s)));
 }

@@ -137,14 +137,42 @@ class CausalSelfAttention(nn.Module):
 
     def _triple(self, lin):
         inner = lin.inner
-        return (inner.packed(), inner.alpha.detach().float().contiguous(), inner.beta.detach().float().contiguous())
+        return (inner.packed(),) + inner.scales()
 
-    def forward_cached(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int):
-        """x [B, T, C] (already normed); rope rows for the T tokens; k/v written
-        at cache rows start_pos..; returns the wo output [B, T, C]."""
+    def _triple_tc(self, lin):
+        inner = lin.inner
+        return (inner.ternary_f16(),) + inner.scales()
+
+    def _tc(self, x) -> bool:
+        return self.algebra == "hadamard" and ops.tc_eligible(x, torch.float16) and self.n_embd == 512
+
+    def forward_site(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, xs, hmix):
+        """Attention plus the mHC site epilogue: xs [B, T, n, C] <- H_res xs + H_post attn(x)."""
+        if not self._tc(x) or xs.dtype != torch.bfloat16:
+            f = self.forward_cached(x, rope_cos, rope_sin, k_cache, v_cache, start_pos, out_dtype=xs.dtype)
+            return ops.mhc_post(xs, f, hmix, out=xs)
         B, T, C = x.shape
         H, hd = self.n_head, self.head_dim
         q = torch.empty((B, H, T, hd), dtype=x.dtype, device=x.device)
+        ops.attn_qkv_tc(x, H, self._triple_tc(self.wq), self._triple_tc(self.wk), self._triple_tc(self.wv),
+                        rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
+        o = ops.attention(q, k_cache, v_cache, start_pos)
+        wmix = bmix = None
+        if self.head_mixer is not None:
+            if hd != 16:
+                o = self.head_mixer.forward_tokens(o, out=o)
+            else:
+                wmix, bmix = self.head_mixer.weights_tc()
+        wo = self.wo.inner
+        return ops.attn_out_tc(o.view(B, T, C), wmix, bmix, wo.ternary_f16(), *wo.scales(), xs, hmix, out=xs)
+
+    def forward_cached(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, out_dtype=None):
+        """x [B, T, C] (already normed); rope rows for the T tokens; k/v written
+        at cache rows start_pos.. (q/k/v in the caches' dtype); returns the wo
+        output [B, T, C] in out_dtype (default x's)."""
+        B, T, C = x.shape
+        H, hd = self.n_head, self.head_dim
+        q = torch.empty((B, H, T, hd), dtype=k_cache.dtype, device=x.device)
         if self.algebra == "hadamard":
             ops.attn_qkv(x, H, self._triple(self.wq), self._triple(self.wk), self._triple(self.wv),
                          rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
@@ -155,8 +183,10 @@ class CausalSelfAttention(nn.Module):
             o = self.head_mixer.forward_tokens(o, out=o)
         y = o.view(B, T, C)
         if self.algebra == "hadamard":
-            return self.wo.inner(y)
-        return self.wo.forward_flat(y)
+            inner = self.wo.inner
+            alpha, beta = inner.scales()
+            return ops.hadamard_linear(y, inner.packed(), alpha, beta, 1.0, out_dtype=out_dtype or x.dtype)
+        return self.wo.forward_flat(y, out_dtype=out_dtype or x.dtype)
 
     def _octonion_qkv(self, x, rope_cos, rope_sin, start_pos, q, k_cache, v_cache):
         from .cayley_dickson_cuda import octonion_qkv

@@ -71,9 +71,20 @@ class HadamardLinear(nn.Module):
         return _prep.cached(self, "packed", [self.weight],
                             lambda: ops.quantize_pack(self.weight)[0])
 
+    def ternary_f16(self):
+        """Ternary values as float16 [32, out_o, in_o] (operands of the tensor-core kernels)."""
+        return _prep.cached(self, "tern_f16", [self.weight],
+                            lambda: ops.unpack(self.packed(), self.in_o).to(torch.float16).contiguous())
+
+    def scales(self):
+        return _prep.cached(self, "scales", [self.alpha, self.beta],
+                            lambda: (self.alpha.detach().float().contiguous(), self.beta.detach().float().contiguous()))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return ops.hadamard_linear(x, self.packed(), self.alpha.detach().float().contiguous(),
-                                   self.beta.detach().float().contiguous(), 1.0, out_dtype=x.dtype)
+        alpha, beta = self.scales()
+        if ops.tc_eligible(x) and self.in_features == 512 and self.out_features == 512:
+            return ops.hadamard_linear_tc(x, self.ternary_f16(), alpha, beta)
+        return ops.hadamard_linear(x, self.packed(), alpha, beta, 1.0, out_dtype=x.dtype)
 
     def extra_repr(self) -> str:
         return f"in={self.in_features}, out={self.out_features}, algebra=hadamard32"
@@ -118,7 +129,14 @@ class HadamardHeadMixerFused(nn.Module):
         self.register_buffer("H", hadamard_matrix(ALGEBRA_DIM, normalize=True))
 
     def weights(self):
-        return (self.W.detach().float().contiguous(), self.beta.detach().float().contiguous())
+        return _prep.cached(self, "w", [self.W, self.beta],
+                            lambda: (self.W.detach().float().contiguous(), self.beta.detach().float().contiguous()))
+
+    def weights_tc(self):
+        """(W^T per head as float16 [32, hd_out, hd_in], beta float32)."""
+        return _prep.cached(self, "wtc", [self.W, self.beta],
+                            lambda: (self.W.detach().transpose(1, 2).to(torch.float16).contiguous(),
+                                     self.beta.detach().float().contiguous()))
 
     def forward_tokens(self, y: torch.Tensor, out=None) -> torch.Tensor:
         """Token-major entry: y [..., n_head, hd], groups of 32 heads share W."""

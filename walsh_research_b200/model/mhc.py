@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .. import ops
+from .. import _lib, ops
 from . import _prep
 from .chassis import CausalSelfAttention, KVCache, RMSNorm, WalshConfig, precompute_freqs_cis, rope_tables
 
@@ -83,12 +83,13 @@ def site_params(stream: "mHCResidualStream"):
 
     def build():
         phi = torch.cat([pre.phi.weight, post.phi.weight, res.phi.weight]).detach().float().contiguous()
+        phi_bf16 = phi.to(torch.bfloat16).contiguous()
         dev = phi.device
         mp = torch.cat([torch.stack([pre.alpha, post.alpha, res.alpha]).detach().float().reshape(3),
                         torch.zeros(1, device=dev),
                         pre.bias.detach().float().reshape(-1), post.bias.detach().float().reshape(-1),
                         res.bias.detach().float().reshape(-1)]).contiguous()
-        return phi, mp
+        return phi, mp, phi_bf16
     srcs = [pre.phi.weight, post.phi.weight, res.phi.weight, pre.alpha, post.alpha, res.alpha,
             pre.bias, post.bias, res.bias]
     return _prep.cached(stream, "site", srcs, build)
@@ -106,8 +107,8 @@ class mHCResidualStream(nn.Module):
         self.H_res = ResidualStreamMapping(n_embd, n_streams, "res")
 
     def forward(self, x, layer_fn):
-        phi, mp = site_params(self)
-        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS)
+        phi, mp, phib = site_params(self)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, phi_bf16=phib)
         return ops.mhc_post(x, layer_fn(u), hmix)
 
 
@@ -145,22 +146,24 @@ class mHCLlamaBlock(nn.Module):
     def forward_fused(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, record_stats=True):
         """x [B, T, n, C] (updated in place and returned)."""
         B, T, n, C = x.shape
+        idt = k_cache.dtype  # storage type of u, q/k/v and the attention output
         # attention site
-        phi, mp = site_params(self.attn_stream)
-        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.attention_norm.weight), self.attention_norm.eps)
-        f = self.attention.forward_cached(u, rope_cos, rope_sin, k_cache, v_cache, start_pos)
-        ops.mhc_post(x, f, hmix, out=x)
+        phi, mp, phib = site_params(self.attn_stream)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.attention_norm.weight), self.attention_norm.eps,
+                              phi_bf16=phib, u_dtype=idt)
+        self.attention.forward_site(u, rope_cos, rope_sin, k_cache, v_cache, start_pos, x, hmix)
         # ffn site
-        phi, mp = site_params(self.ffn_stream)
-        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.ffn_norm.weight), self.ffn_norm.eps)
+        phi, mp, phib = site_params(self.ffn_stream)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.ffn_norm.weight), self.ffn_norm.eps, phi_bf16=phib,
+                              u_dtype=idt)
         ff = self.feed_forward
         if hasattr(ff, "kernel_args"):
-            w1t, w2, g, up, d, gam, k = ff.kernel_args()
+            w1t, w2, g, up, d, gam, k, tc = ff.kernel_args(idt)
             if record_stats:
-                _, mask, probs, _ = ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True)
+                _, mask, probs, _ = ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True, tc=tc)
                 ff._record(mask.float(), probs, B * T)
             else:
-                ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x))
+                ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), tc=tc)
         else:
             ops.mhc_post(x, ff(u), hmix, out=x)
         # channel modulation over the [B*n, T, C] reinterpretation of x
@@ -180,7 +183,7 @@ class mHCLlamaBlock(nn.Module):
         sin = freqs_cis[:T].imag.float().contiguous()
         H, hd = self.attention.n_head, self.attention.head_dim
         if kv_cache is None:
-            kc = torch.empty((B, H, T, hd), dtype=x.dtype, device=x.device)
+            kc = torch.empty((B, H, T, hd), dtype=_lib.inner_dtype(x.dtype), device=x.device)
             vc = torch.empty_like(kc)
             start = 0
         else:
@@ -240,9 +243,10 @@ class mHCWalsh(nn.Module):
                             lambda: ops.linear(emb.detach().float().contiguous(), W.detach().float(), b.detach(),
                                                out_dtype=dtype))
 
-    def head_weights(self, dtype):
+    def head_weights(self):
+        """The tied output projection, float32 (logits are always computed against fp32 weights)."""
         emb = self.tok_embeddings.weight
-        return _prep.cached(self, f"emb_{dtype}", [emb], lambda: emb.detach().to(dtype).contiguous())
+        return _prep.cached(self, "emb_f32", [emb], lambda: emb.detach().float().contiguous())
 
     def _merge_norm(self, x, rows_last_only: bool):
         B, T, n, C = x.shape
@@ -266,12 +270,14 @@ class mHCWalsh(nn.Module):
         x = ops.embed_gather(idx, self.stream_table(dt), err).view(B, T, n, C)
         cos_all, sin_all = rope_tables(self, self.freqs_cis)
         cos, sin = cos_all[start_pos:start_pos + T], sin_all[start_pos:start_pos + T]
+        idt = _lib.inner_dtype(dt)
         if kv_cache is None:
             H, hd = self.config.n_head, C // self.config.n_head
-            kc = torch.empty((B, H, T, hd), dtype=dt, device=idx.device)
+            kc = torch.empty((B, H, T, hd), dtype=idt, device=idx.device)
             vc = torch.empty_like(kc)
-        elif kv_cache.dtype != dt or kv_cache.batch_size != B:
-            raise ValueError(f"KV cache holds {kv_cache.batch_size} x {kv_cache.dtype}; forward has {B} x {dt}")
+        elif kv_cache.dtype != idt or kv_cache.batch_size != B:
+            raise ValueError(f"KV cache holds {kv_cache.batch_size} x {kv_cache.dtype}; this forward needs "
+                             f"{B} x {idt} (a {dt} residual stream keeps attention in {idt})")
         elif kv_cache.cached_len + T > kv_cache.max_seq_len:
             raise ValueError("KV cache is full")
         for l, layer in enumerate(self.layers):
@@ -284,7 +290,7 @@ class mHCWalsh(nn.Module):
         self._last_index_error = err
         need_all = return_hidden or targets is not None
         h_out = self._merge_norm(x, rows_last_only=not need_all)
-        emb = self.head_weights(dt)
+        emb = self.head_weights()
         if targets is not None:
             logits = ops.linear(h_out, emb, None, out_dtype=torch.float32)
             loss = F.cross_entropy(logits.view(-1, logits.size(-1)), targets.view(-1), ignore_index=-1)

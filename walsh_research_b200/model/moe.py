@@ -48,6 +48,16 @@ class FastMoEExperts(nn.Module):
             return g, u, d, torch.cat([gg, gu, gd])
         return _prep.cached(self, "packed", [self.gate_weights, self.up_weights, self.down_weights], build)
 
+    def ternary_tc(self, dtype):
+        """(gate, up, down) ternary values {-1, 0, +1} in ``dtype`` (bf16 or fp16; gamma
+        not applied), the operands of the tensor-core expert kernel."""
+        def build():
+            g, u, d, _ = self.packed()
+            return (ops.unpack(g, self.dim).to(dtype).contiguous(),
+                    ops.unpack(u, self.dim).to(dtype).contiguous(),
+                    ops.unpack(d, self.hidden).to(dtype).contiguous())
+        return _prep.cached(self, f"tern_{dtype}", [self.gate_weights, self.up_weights, self.down_weights], build)
+
     def forward(self, x: torch.Tensor, expert_weights: torch.Tensor) -> torch.Tensor:
         B, T, E, D = x.shape
         g, u, d, gam = self.packed()
@@ -84,9 +94,16 @@ class HadamardRouter(nn.Module):
                             lambda: (self.gate[0].weight.detach().float().t().contiguous(),
                                      self.gate[2].weight.detach().float().contiguous()))
 
+    def weights_tc(self, dtype):
+        """(W1 [C/4, C], W2 [E, C/4]) copies in ``dtype`` (bf16 or fp16) for the tensor-core kernel."""
+        return _prep.cached(self, f"w_{dtype}", [self.gate[0].weight, self.gate[2].weight],
+                            lambda: (self.gate[0].weight.detach().to(dtype).contiguous(),
+                                     self.gate[2].weight.detach().to(dtype).contiguous()))
+
     def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         w1t, w2 = self.weights_dev()
-        _, mask, probs, weights = ops.moe(x, w1t, w2, None, None, None, None, self.top_k, want_stats=True)
+        tc = self.weights_tc(x.dtype) + (None, None, None) if x.dtype != torch.float32 else None
+        _, mask, probs, weights = ops.moe(x, w1t, w2, None, None, None, None, self.top_k, want_stats=True, tc=tc)
         return weights, mask.float(), probs
 
 
@@ -112,10 +129,15 @@ class HadamardMoE(nn.Module):
         self.register_buffer("_total_tokens", torch.zeros(1), persistent=False)
         self._last_expert_mask = None
 
-    def kernel_args(self):
+    def kernel_args(self, dtype=torch.float16):
+        """Arguments of ops.moe for activations u of ``dtype``:
+        (w1t, w2, gate, up, down, gammas, top_k, tc)."""
         w1t, w2 = self.router.weights_dev()
         g, u, d, gam = self.experts.packed()
-        return w1t, w2, g, u, d, gam, self.router.top_k
+        tc = None
+        if dtype != torch.float32:
+            tc = self.router.weights_tc(dtype) + self.experts.ternary_tc(dtype)
+        return w1t, w2, g, u, d, gam, self.router.top_k, tc
 
     def _record(self, mask, probs, ntok):
         self._last_expert_mask = mask
@@ -128,8 +150,8 @@ class HadamardMoE(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, C = x.shape
-        w1t, w2, g, u, d, gam, k = self.kernel_args()
-        y, mask, probs, _ = ops.moe(x, w1t, w2, g, u, d, gam, k, want_stats=True)
+        w1t, w2, g, u, d, gam, k, tc = self.kernel_args(x.dtype)
+        y, mask, probs, _ = ops.moe(x, w1t, w2, g, u, d, gam, k, want_stats=True, tc=tc)
         self._record(mask.float(), probs, B * T)
         return y
 

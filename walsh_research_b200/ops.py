@@ -7,6 +7,8 @@ anything on the host.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -62,6 +64,30 @@ def hadamard_linear(x, packed, alpha, beta, w_scale: float = 1.0, out_dtype=None
     return y
 
 
+def tc_eligible(x, dtype=torch.bfloat16) -> bool:
+    """True when the tensor-core Hadamard kernels apply: rows of 512 in ``dtype``."""
+    return x.dtype == dtype and x.shape[-1] == 512
+
+
+def hadamard_linear_tc(x, w_f16, alpha, beta, w_scale: float = 1.0):
+    require_cuda(x)
+    x = _c(x)
+    y = torch.empty_like(x)
+    call("walsh_hadamard_linear_tc_fwd", ptr(x), x.numel() // 512, ptr(w_f16), float(w_scale), ptr(alpha),
+         ptr(beta), ptr(y), stream())
+    return y
+
+
+def attn_out_tc(o, wmix, beta_mix, wo, alpha_o, beta_o, x, hmix, out=None):
+    """Head mixer (wmix may be None) + wo + mHC site epilogue; returns x_out."""
+    require_cuda(o, x)
+    o = _c(o)
+    out = out if out is not None else torch.empty_like(x)
+    call("walsh_attn_out_tc_fwd", ptr(o), o.numel() // 512, ptr(wmix), ptr(beta_mix), ptr(wo), ptr(alpha_o),
+         ptr(beta_o), ptr(x), ptr(hmix), ptr(out), stream())
+    return out
+
+
 def head_mixer_tokens(x, W, beta, out=None):
     """Hadamard head mixing on token-major [..., n_head, hd]."""
     require_cuda(x)
@@ -77,17 +103,19 @@ def head_mixer_tokens(x, W, beta, out=None):
 # mHC
 # ---------------------------------------------------------------------------
 
-def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6):
-    """x [..., 4, C] -> (u [..., C], hmix float [..., 24])."""
+def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6, phi_bf16=None, u_dtype=None):
+    """x [..., 4, C] -> (u [..., C] in u_dtype (default x's), hmix float [..., 24]).
+    ``phi_bf16`` (a bfloat16 copy of phi) enables the tensor-core kernel for bf16 x."""
     require_cuda(x)
     x = _c(x)
     C = x.shape[-1]
     lead = x.shape[:-2]
     ntok = x.numel() // (4 * C)
-    u = torch.empty(lead + (C,), dtype=x.dtype, device=x.device)
+    u_dtype = u_dtype or x.dtype
+    u = torch.empty(lead + (C,), dtype=u_dtype, device=x.device)
     hmix = torch.empty(lead + (24,), dtype=torch.float32, device=x.device)
-    call("walsh_mhc_map", ptr(x), dcode(x.dtype), ntok, C, ptr(phi), ptr(mparams), float(map_eps), ptr(norm_w),
-         float(norm_eps), ptr(u), ptr(hmix), stream())
+    call("walsh_mhc_map", ptr(x), dcode(x.dtype), ntok, C, ptr(phi), ptr(phi_bf16), ptr(mparams), float(map_eps),
+         ptr(norm_w), float(norm_eps), ptr(u), dcode(u_dtype), ptr(hmix), stream())
     return u, hmix
 
 
@@ -115,11 +143,16 @@ def sinkhorn(h, iters=20, eps=1e-8):
 # MoE and channel modulation
 # ---------------------------------------------------------------------------
 
-def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=None, want_stats=False):
+def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=None, want_stats=False, tc=None):
     """Router + experts.  With ``fuse=(x, hmix, x_out)`` the mHC epilogue is
     applied and ``x_out`` returned; otherwise the expert output y.
-    With ``want_stats`` also returns (mask uint8, probs, weights)."""
+    With ``want_stats`` also returns (mask uint8, probs, weights).
+    ``tc``: (w1, w2, gate, up, down) bfloat16 copies enabling the tensor-core kernel."""
     require_cuda(u)
+    tcs = None
+    if tc is not None:
+        tcs = _lib.MoeTcWeights(*[ptr(t) for t in tc])
+    tcp = ctypes.byref(tcs) if tcs is not None else None
     u = _c(u)
     C = u.shape[-1]
     E = C // 32
@@ -135,14 +168,14 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
     if fuse is None:
         y = torch.empty_like(u)
         call("walsh_moe_fwd", ptr(u), dcode(u.dtype), ntok, C, int(top_k), ptr(w1t), ptr(w2), ptr(gate_p),
-             ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0, None, None, None, ptr(weights_in), ptr(mask),
-             ptr(probs), ptr(weights), stream())
+             ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0, None, dcode(u.dtype), None, None, ptr(weights_in),
+             ptr(mask), ptr(probs), ptr(weights), tcp, stream())
         out = y
     else:
         x, hmix, x_out = fuse
         call("walsh_moe_fwd", ptr(u), dcode(u.dtype), ntok, C, int(top_k), ptr(w1t), ptr(w2), ptr(gate_p),
-             ptr(up_p), ptr(down_p), ptr(gammas), None, 1, ptr(x), ptr(hmix), ptr(x_out), ptr(weights_in),
-             ptr(mask), ptr(probs), ptr(weights), stream())
+             ptr(up_p), ptr(down_p), ptr(gammas), None, 1, ptr(x), dcode(x.dtype), ptr(hmix), ptr(x_out),
+             ptr(weights_in), ptr(mask), ptr(probs), ptr(weights), tcp, stream())
         out = x_out
     return (out, mask, probs, weights) if want_stats else out
 
@@ -184,6 +217,17 @@ def attn_qkv(u, n_head, wq, wk, wv, rope_cos, rope_sin, start_pos, q, k_cache, v
     u = _c(u)
     B, T, C = u.shape
     call("walsh_attn_qkv_fwd", ptr(u), dcode(u.dtype), B, T, C, n_head,
+         ptr(wq[0]), ptr(wq[1]), ptr(wq[2]), ptr(wk[0]), ptr(wk[1]), ptr(wk[2]),
+         ptr(wv[0]), ptr(wv[1]), ptr(wv[2]), ptr(rope_cos), ptr(rope_sin), rope_cos.shape[0], int(start_pos),
+         ptr(q), ptr(k_cache), ptr(v_cache), k_cache.shape[-2], dcode(q.dtype), stream())
+
+
+def attn_qkv_tc(u, n_head, wq, wk, wv, rope_cos, rope_sin, start_pos, q, k_cache, v_cache):
+    """attn_qkv on the tensor cores (C = 512; u, q and caches float16); wq/wk/wv: (w_f16, alpha, beta)."""
+    require_cuda(u)
+    u = _c(u)
+    B, T, C = u.shape
+    call("walsh_attn_qkv_tc_fwd", ptr(u), B, T, n_head,
          ptr(wq[0]), ptr(wq[1]), ptr(wq[2]), ptr(wk[0]), ptr(wk[1]), ptr(wk[2]),
          ptr(wv[0]), ptr(wv[1]), ptr(wv[2]), ptr(rope_cos), ptr(rope_sin), rope_cos.shape[0], int(start_pos),
          ptr(q), ptr(k_cache), ptr(v_cache), k_cache.shape[-2], stream())
