@@ -7,6 +7,8 @@
 // 1/sqrt(hd) scale pre-multiplied by log2(e).
 #include <math_constants.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "mma.cuh"
 
@@ -184,9 +186,9 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
   const int qp_hi = qp_lo + 8;
   const int qp_warp_max = start_pos + q0 + qrow0 + 15;
   float m_lo = -CUDART_INF_F, m_hi = -CUDART_INF_F, l_lo = 0.f, l_hi = 0.f;
-  float oacc[HD / 8][4];
+  float oacc[HD / 8 + 1][4];  // last n-tile: P row sums (fp16 path)
 #pragma unroll
-  for (int i = 0; i < HD / 8; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
+  for (int i = 0; i < HD / 8 + 1; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
   uint32_t qf[HD / 16][4];
 
   for (int kt = 0; kt < nkt; ++kt) {
@@ -214,21 +216,19 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
           mma16<TE>(s[2 * np + 1], qf[ks], kf[2], kf[3]);
         }
       const bool diag = (kt + 1) * KT - 1 > start_pos + q0 + qrow0;  // tile may hold masked keys
+      // row maxima of the raw scores (masked entries -inf)
       float mt_lo = -CUDART_INF_F, mt_hi = -CUDART_INF_F;
 #pragma unroll
       for (int n = 0; n < KT / 8; ++n) {
         const int key = kt * KT + n * 8 + 2 * t4;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          float a = s[n][e] * scale_log2, c = s[n][2 + e] * scale_log2;
           if (diag) {
-            if (key + e > qp_lo) a = -CUDART_INF_F;
-            if (key + e > qp_hi) c = -CUDART_INF_F;
+            if (key + e > qp_lo) s[n][e] = -CUDART_INF_F;
+            if (key + e > qp_hi) s[n][2 + e] = -CUDART_INF_F;
           }
-          s[n][e] = a;
-          s[n][2 + e] = c;
-          mt_lo = fmaxf(mt_lo, a);
-          mt_hi = fmaxf(mt_hi, c);
+          mt_lo = fmaxf(mt_lo, s[n][e]);
+          mt_hi = fmaxf(mt_hi, s[n][2 + e]);
         }
       }
 #pragma unroll
@@ -237,27 +237,38 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
         mt_hi = fmaxf(mt_hi, __shfl_xor_sync(0xffffffffu, mt_hi, off));
       }
       const float mn_lo = fmaxf(m_lo, mt_lo), mn_hi = fmaxf(m_hi, mt_hi);
-      // rows with no visible key yet keep m = -inf; use 0 as the subtrahend so exp2 gives 0, not NaN
-      const float sub_lo = mn_lo == -CUDART_INF_F ? 0.f : mn_lo;
-      const float sub_hi = mn_hi == -CUDART_INF_F ? 0.f : mn_hi;
-      const float corr_lo = exp2f(m_lo - sub_lo), corr_hi = exp2f(m_hi - sub_hi);
+      // rows with no visible key yet keep m = -inf; subtract 0 so exp2 gives 0, not NaN
+      const float sub_lo = mn_lo == -CUDART_INF_F ? 0.f : mn_lo * scale_log2;
+      const float sub_hi = mn_hi == -CUDART_INF_F ? 0.f : mn_hi * scale_log2;
+      const float corr_lo = exp2f(m_lo * scale_log2 - sub_lo), corr_hi = exp2f(m_hi * scale_log2 - sub_hi);
       m_lo = mn_lo;
       m_hi = mn_hi;
-      float rs_lo = 0.f, rs_hi = 0.f;
       uint32_t pf[KT / 16][4];
+      if constexpr (std::is_same<TE, __half>::value) {
+        // p = 2^(s * scale - m * scale) two at a time in fp16 (the P V operand precision)
 #pragma unroll
-      for (int n = 0; n < KT / 8; ++n) {
-        const float p0 = exp2f(s[n][0] - sub_lo), p1 = exp2f(s[n][1] - sub_lo);
-        const float p2 = exp2f(s[n][2] - sub_hi), p3 = exp2f(s[n][3] - sub_hi);
-        rs_lo += p0 + p1;
-        rs_hi += p2 + p3;
-        pf[n >> 1][(n & 1) * 2 + 0] = pack2<TE>(p0, p1);
-        pf[n >> 1][(n & 1) * 2 + 1] = pack2<TE>(p2, p3);
+        for (int n = 0; n < KT / 8; ++n) {
+          const __half2 p01 = h2exp2(__floats2half2_rn(fmaf(s[n][0], scale_log2, -sub_lo), fmaf(s[n][1], scale_log2, -sub_lo)));
+          const __half2 p23 = h2exp2(__floats2half2_rn(fmaf(s[n][2], scale_log2, -sub_hi), fmaf(s[n][3], scale_log2, -sub_hi)));
+          pf[n >> 1][(n & 1) * 2 + 0] = *reinterpret_cast<const uint32_t*>(&p01);
+          pf[n >> 1][(n & 1) * 2 + 1] = *reinterpret_cast<const uint32_t*>(&p23);
+        }
+      } else {
+        float rs_lo = 0.f, rs_hi = 0.f;
+#pragma unroll
+        for (int n = 0; n < KT / 8; ++n) {
+          const float p0 = exp2f(fmaf(s[n][0], scale_log2, -sub_lo)), p1 = exp2f(fmaf(s[n][1], scale_log2, -sub_lo));
+          const float p2 = exp2f(fmaf(s[n][2], scale_log2, -sub_hi)), p3 = exp2f(fmaf(s[n][3], scale_log2, -sub_hi));
+          rs_lo += p0 + p1;
+          rs_hi += p2 + p3;
+          pf[n >> 1][(n & 1) * 2 + 0] = pack2<TE>(p0, p1);
+          pf[n >> 1][(n & 1) * 2 + 1] = pack2<TE>(p2, p3);
+        }
+        l_lo = l_lo * corr_lo + rs_lo;
+        l_hi = l_hi * corr_hi + rs_hi;
       }
-      l_lo = l_lo * corr_lo + rs_lo;
-      l_hi = l_hi * corr_hi + rs_hi;
 #pragma unroll
-      for (int i = 0; i < HD / 8; ++i) {
+      for (int i = 0; i < HD / 8 + 1; ++i) {
         oacc[i][0] *= corr_lo; oacc[i][1] *= corr_lo;
         oacc[i][2] *= corr_hi; oacc[i][3] *= corr_hi;
       }
@@ -272,14 +283,21 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
           mma16<TE>(oacc[2 * dp], a, vf[0], vf[1]);
           mma16<TE>(oacc[2 * dp + 1], a, vf[2], vf[3]);
         }
+        if constexpr (std::is_same<TE, __half>::value)  // row sums of P on the tensor cores (V column of ones)
+          mma16<TE>(oacc[HD / 8], a, 0x3C003C00u, 0x3C003C00u);
       }
     }
     __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
   }
+  if constexpr (std::is_same<TE, __half>::value) {
+    l_lo = oacc[HD / 8][0];
+    l_hi = oacc[HD / 8][2];
+  } else {
 #pragma unroll
-  for (int off = 1; off <= 2; off <<= 1) {
-    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
-    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
+    for (int off = 1; off <= 2; off <<= 1) {
+      l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
+      l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
+    }
   }
   const float inv_lo = 1.0f / l_lo, inv_hi = 1.0f / l_hi;
   const int t_lo = q0 + qrow0 + g, t_hi = t_lo + 8;

@@ -42,6 +42,100 @@ chmod_stats_kernel(const T* __restrict__ x, int C, int seg_len, const float* __r
   }
 }
 
+// Vectorised single-pass variant (C a multiple of 256, 16-byte aligned rows):
+// each warp takes rows warp, warp + 8, ... of the chunk, keeps a row in
+// registers (8 consecutive channels per lane per 256-column pass), forms its
+// RMS factor with one warp reduction and accumulates the normalised row; the
+// 8 warps' partial sums are combined through shared memory.
+template <typename T, int C>
+__global__ void __launch_bounds__(256)
+chmod_stats_vec_kernel(const T* __restrict__ x, int seg_len, const float* __restrict__ w, float eps,
+                       float* __restrict__ partial) {
+  constexpr int NP = C / 256;
+  __shared__ float red[8][C];
+  const int seg = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int r0 = ch * kChunkRows;
+  const int nr = min(kChunkRows, seg_len - r0);
+  const int64_t row0 = (int64_t)seg * seg_len + r0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc[NP][8];
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[p][e] = 0.f;
+  for (int r = warp; r < nr; r += 8) {
+    const T* xr = x + (row0 + r) * C;
+    float v[NP][8];
+    float s = 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      load8(xr + p * 256 + lane * 8, v[p]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(v[p][e], v[p][e], s);
+    }
+    s = warp_sum(s);
+    const float inv = w ? rsqrtf(s / (float)C + eps) : 1.0f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[p][e] = fmaf(v[p][e], inv, acc[p][e]);
+  }
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) red[warp][p * 256 + lane * 8 + e] = acc[p][e];
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += 256) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][c];
+    partial[((size_t)seg * nch + ch) * C + c] = w ? t * __ldg(w + c) : t;
+  }
+}
+
+// Vectorised apply (C a multiple of 256): warp per row, 8 channels per lane per pass.
+template <typename T, int C>
+__global__ void __launch_bounds__(256)
+chmod_apply_vec_kernel(const T* x, int64_t nrows, int seg_len, const float* __restrict__ w, float eps,
+                       const float* __restrict__ scale, const float* __restrict__ shift, float rscale, int add_input,
+                       T* out) {
+  constexpr int NP = C / 256, E = C / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float wv[NP][8];
+#pragma unroll
+  for (int p = 0; p < NP; ++p)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) wv[p][e] = w ? __ldg(w + p * 256 + lane * 8 + e) : 1.f;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < nrows; row += (int64_t)gridDim.x * 8) {
+    const T* xr = x + row * C;
+    float v[NP][8];
+    float s = 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      load8(xr + p * 256 + lane * 8, v[p]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(v[p][e], v[p][e], s);
+    }
+    s = warp_sum(s);
+    const float r = w ? rsqrtf(s / (float)C + eps) : 1.0f;
+    const int64_t seg = row / seg_len;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      const int b = (p * 256 + lane * 8) >> 5;  // the lane's 8 channels lie in one 32-wide block
+      const float sc = __ldg(scale + seg * E + b), sh = __ldg(shift + seg * E + b) * 0.1f;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xn = w ? v[p][e] * r * wv[p][e] : v[p][e];
+        const float xm = xn * sc + sh;
+        const float xo = xn + rscale * (xm - xn);
+        o[e] = add_input ? v[p][e] + xo : xo;
+      }
+      store8(out + row * C + p * 256 + lane * 8, o);
+    }
+  }
+}
+
 // One CTA per segment.
 __global__ void __launch_bounds__(256)
 chmod_mlp_kernel(const float* __restrict__ partial, int nch, int seg_len, int C, const uint8_t* __restrict__ w1,
@@ -139,6 +233,10 @@ extern "C" walsh_status walsh_chmod_stats(const void* x, int dtype, int64_t nrow
   WALSH_CHECK_SHAPE(nseg <= 65535);
   dim3 grid((seg_len + kChunkRows - 1) / kChunkRows, (unsigned)nseg);
   cudaStream_t s = (cudaStream_t)stream;
+  if (C == 512 && (((uintptr_t)x) & 15u) == 0)
+    return WALSH_DISPATCH_DTYPE(dtype, T, (chmod_stats_vec_kernel<T, 512><<<grid, 256, 0, s>>>(
+                                               (const T*)x, seg_len, norm_w, norm_eps, partial),
+                                           launch_status()));
   return WALSH_DISPATCH_DTYPE(dtype, T, (chmod_stats_kernel<T><<<grid, 256, 0, s>>>((const T*)x, C, seg_len, norm_w,
                                                                                   norm_eps, partial),
                                          launch_status()));
@@ -167,6 +265,18 @@ extern "C" walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrow
   int64_t g = (nrows + 7) / 8;
   if (g > 148 * 32) g = 148 * 32;
   cudaStream_t s = (cudaStream_t)stream;
+  if (C % 256 == 0 && C <= 2048 && ((((uintptr_t)x) | ((uintptr_t)out)) & 15u) == 0) {
+    if (C == 512)
+      return WALSH_DISPATCH_DTYPE(dtype, T, (chmod_apply_vec_kernel<T, 512><<<(unsigned)g, 256, 0, s>>>(
+                                                 (const T*)x, nrows, seg_len, norm_w, norm_eps, scale, shift,
+                                                 residual_scale, add_input, (T*)out),
+                                             launch_status()));
+    if (C == 2048)
+      return WALSH_DISPATCH_DTYPE(dtype, T, (chmod_apply_vec_kernel<T, 2048><<<(unsigned)g, 256, 0, s>>>(
+                                                 (const T*)x, nrows, seg_len, norm_w, norm_eps, scale, shift,
+                                                 residual_scale, add_input, (T*)out),
+                                             launch_status()));
+  }
   return WALSH_DISPATCH_DTYPE(dtype, T, (chmod_apply_kernel<T><<<(unsigned)g, 256, 0, s>>>(
                                              (const T*)x, nrows, C, seg_len, norm_w, norm_eps, scale, shift,
                                              residual_scale, add_input, (T*)out),

@@ -30,9 +30,52 @@ template <> __device__ __forceinline__ __half from_f<__half>(float v) {
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
+// 8 consecutive elements <-> float[8] (16-byte accesses for 16-bit types, 2 x 16 for float).
+__device__ __forceinline__ void load8(const float* p, float* v) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <typename T16>
+__device__ __forceinline__ void load8_16(const T16* p, float* v) {
+  const uint4 q = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    T16 lo, hi;
+    const uint16_t l = (uint16_t)(w[i] & 0xffffu), h = (uint16_t)(w[i] >> 16);
+    memcpy(&lo, &l, 2);
+    memcpy(&hi, &h, 2);
+    v[2 * i] = to_f(lo);
+    v[2 * i + 1] = to_f(hi);
+  }
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) { load8_16(p, v); }
+__device__ __forceinline__ void load8(const __half* p, float* v) { load8_16(p, v); }
+
+__device__ __forceinline__ void store8(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+template <typename T16>
+__device__ __forceinline__ void store8_16(T16* p, const float* v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const T16 lo = from_f<T16>(v[2 * i]), hi = from_f<T16>(v[2 * i + 1]);
+    uint16_t l, h;
+    memcpy(&l, &lo, 2);
+    memcpy(&h, &hi, 2);
+    w[i] = (uint32_t)l | ((uint32_t)h << 16);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) { store8_16(p, v); }
+__device__ __forceinline__ void store8(__half* p, const float* v) { store8_16(p, v); }
+
 // ---- math --------------------------------------------------------------------
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
-__device__ __forceinline__ float siluf_(float x) { return x / (1.0f + __expf(-x)); }
+// fast SiLU for the bf16/fp16 tensor-core paths (2-ulp exp and division)
+__device__ __forceinline__ float siluf_(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -176,14 +176,11 @@ qkv_tc_kernel(const __half* __restrict__ u, int64_t ntok, const __half* __restri
               const float* __restrict__ bk, const float* __restrict__ bv, __half* __restrict__ q,
               __half* __restrict__ kc, __half* __restrict__ vc, TcQkvEpilogue ep) {
   constexpr int HALF = HD / 2;
-  constexpr int NP = kTcC / 64;  // channel pairs per lane: c = 2 * lane + 64 * i
-  static_assert(64 % HD == 0, "a lane's pairs must share d");
+  static_assert(HD % 8 == 0 && 256 % HD == 0, "a lane's 8 channels lie in one head");
   extern __shared__ float4 smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __half* tile = reinterpret_cast<__half*>(smem4) + warp * kTcTok * kTcRow;
   const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * kTcTok;
-  const int d = (2 * lane) % HD;           // the same head dimension for all of this lane's pairs
-  const int head0 = (2 * lane) / HD;       // head of pair i is head0 + i * (64 / HD)
   uint32_t hb[2][4][2];
   hadamard_bfrags(hb);
 #pragma unroll 1
@@ -195,30 +192,44 @@ qkv_tc_kernel(const __half* __restrict__ u, int64_t ntok, const __half* __restri
     stage_rows(tile, u, tok0, ntok);  // re-read per projection (L2-resident); keeps one tile per warp
     scale_rows_to_f16<__half>(tile, al);
     hadamard_chain(tile, wt, hb);
-    float b0[NP], b1[NP];
+    // epilogue: lane owns channels c = 256 * pass + 8 * lane .. +7 (one head, dims d0..d0+7)
+    float bl[2][8];
 #pragma unroll
-    for (int i = 0; i < NP; ++i) {
-      b0[i] = __ldg(be + 2 * lane + 64 * i);
-      b1[i] = __ldg(be + 2 * lane + 64 * i + 1);
+    for (int pass = 0; pass < 2; ++pass) {
+      const float4 lo = __ldg(reinterpret_cast<const float4*>(be + pass * 256 + lane * 8));
+      const float4 hi = __ldg(reinterpret_cast<const float4*>(be + pass * 256 + lane * 8 + 4));
+      bl[pass][0] = lo.x; bl[pass][1] = lo.y; bl[pass][2] = lo.z; bl[pass][3] = lo.w;
+      bl[pass][4] = hi.x; bl[pass][5] = hi.y; bl[pass][6] = hi.z; bl[pass][7] = hi.w;
     }
+    const int d0 = (lane * 8) % HD;
     for (int t = 0; t < kTcTok; ++t) {
       const int64_t tok = tok0 + t;
       if (tok >= ntok) break;
       const int b = (int)(tok / ep.T), tt = (int)(tok - (int64_t)b * ep.T);
-      float cs = 1.f, sn = 0.f;
+      float cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
       if (set < 2) {
-        cs = __ldg(ep.cos + (size_t)tt * HALF + (d >> 1));
-        sn = __ldg(ep.sin + (size_t)tt * HALF + (d >> 1));
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(ep.cos + (size_t)tt * HALF + (d0 >> 1)));
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(ep.sin + (size_t)tt * HALF + (d0 >> 1)));
+        cs[0] = c4.x; cs[1] = c4.y; cs[2] = c4.z; cs[3] = c4.w;
+        sn[0] = s4.x; sn[1] = s4.y; sn[2] = s4.z; sn[3] = s4.w;
       }
       const size_t plane = set == 0 ? (size_t)ep.T : (size_t)ep.ctx;  // rows per head plane
       const size_t row = set == 0 ? (size_t)tt : (size_t)(ep.start_pos + tt);
-      __half* base = dst + ((size_t)b * ep.n_head * plane + row) * HD + d;
 #pragma unroll
-      for (int i = 0; i < NP; ++i) {
-        const float2 v = unpack_f16(*reinterpret_cast<const uint32_t*>(tile + t * kTcRow + 2 * lane + 64 * i));
-        const float v0 = v.x * b0[i], v1 = v.y * b1[i];
-        const float r0 = v0 * cs - v1 * sn, r1 = v0 * sn + v1 * cs;
-        *reinterpret_cast<uint32_t*>(base + (size_t)(head0 + i * (64 / HD)) * plane * HD) = pack_f16_sat(r0, r1);
+      for (int pass = 0; pass < 2; ++pass) {
+        const int c = pass * 256 + lane * 8;
+        const int head = c / HD;
+        const uint4 v = *reinterpret_cast<const uint4*>(tile + t * kTcRow + c);
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) {
+          const float2 f = unpack_f16(vw[q2]);
+          const float v0 = f.x * bl[pass][2 * q2], v1 = f.y * bl[pass][2 * q2 + 1];
+          ow[q2] = pack_f16_sat(v0 * cs[q2] - v1 * sn[q2], v0 * sn[q2] + v1 * cs[q2]);
+        }
+        *reinterpret_cast<uint4*>(dst + (((size_t)b * ep.n_head + head) * plane + row) * HD + d0) =
+            make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
     }
     __syncwarp();
@@ -258,6 +269,15 @@ attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __r
     scale_rows_to_f16<__half>(tile, alpha_o);
   }
   hadamard_chain(tile, wo, hb);
+  // epilogue: lane owns channels c = 256 * pass + 8 * lane .. +7; 16-byte loads and stores
+  float bo[2][8];
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const float4 lo = __ldg(reinterpret_cast<const float4*>(beta_o + pass * 256 + lane * 8));
+    const float4 hi = __ldg(reinterpret_cast<const float4*>(beta_o + pass * 256 + lane * 8 + 4));
+    bo[pass][0] = lo.x; bo[pass][1] = lo.y; bo[pass][2] = lo.z; bo[pass][3] = lo.w;
+    bo[pass][4] = hi.x; bo[pass][5] = hi.y; bo[pass][6] = hi.z; bo[pass][7] = hi.w;
+  }
   for (int t = 0; t < kTcTok; ++t) {
     const int64_t tok = tok0 + t;
     if (tok >= ntok) break;
@@ -267,22 +287,34 @@ attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __r
     for (int i = 0; i < 4; ++i) hp[i] = __ldg(hm + 4 + i);
 #pragma unroll
     for (int i = 0; i < 16; ++i) hr[i] = __ldg(hm + 8 + i);
-    for (int cp = lane; cp < kTcC / 2; cp += 32) {
-      const int c = 2 * cp;
-      const float2 v = unpack_f16(*reinterpret_cast<const uint32_t*>(tile + t * kTcRow + c));
-      const float f0 = v.x * __ldg(beta_o + c), f1 = v.y * __ldg(beta_o + c + 1);
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      const int c = pass * 256 + lane * 8;
       const size_t base = (size_t)tok * 4 * kTcC + c;
-      float2 xv[4];
+      uint4 xq[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        xv[j] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + base + (size_t)j * kTcC));
+      for (int j = 0; j < 4; ++j) xq[j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * kTcC);
+      const uint4 v = *reinterpret_cast<const uint4*>(tile + t * kTcRow + c);
+      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+      uint32_t ow[4][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float* r = hr + 4 * i;
-        const float a0 = (((r[0] * xv[0].x + r[1] * xv[1].x) + r[2] * xv[2].x) + r[3] * xv[3].x) + hp[i] * f0;
-        const float a1 = (((r[0] * xv[0].y + r[1] * xv[1].y) + r[2] * xv[2].y) + r[3] * xv[3].y) + hp[i] * f1;
-        *reinterpret_cast<uint32_t*>(xo + base + (size_t)i * kTcC) = pack_bf16(a0, a1);
+      for (int q2 = 0; q2 < 4; ++q2) {
+        const float2 f = unpack_f16(vw[q2]);
+        const float f0 = f.x * bo[pass][2 * q2], f1 = f.y * bo[pass][2 * q2 + 1];
+        float2 xf[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xf[j] = unpack2<__nv_bfloat16>((&xq[j].x)[q2]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float* r = hr + 4 * i;
+          const float a0 = (((r[0] * xf[0].x + r[1] * xf[1].x) + r[2] * xf[2].x) + r[3] * xf[3].x) + hp[i] * f0;
+          const float a1 = (((r[0] * xf[0].y + r[1] * xf[1].y) + r[2] * xf[2].y) + r[3] * xf[3].y) + hp[i] * f1;
+          ow[i][q2] = pack_bf16(a0, a1);
+        }
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(xo + base + (size_t)i * kTcC) = make_uint4(ow[i][0], ow[i][1], ow[i][2], ow[i][3]);
     }
   }
 }
@@ -326,7 +358,8 @@ extern "C" walsh_status walsh_attn_qkv_tc_fwd(const void* u, int B, int T, int n
   const int hd = kTcC / n_head;
   WALSH_CHECK_SHAPE((hd == 16 || hd == 32) && start_pos >= 0 && start_pos + T <= ctx && T <= n_pos);
   WALSH_CHECK_ARG(al16(u) && al16(wq_f16) && al16(wk_f16) && al16(wv_f16));
-  WALSH_CHECK_ARG((((uintptr_t)q | (uintptr_t)k_cache | (uintptr_t)v_cache) & 3u) == 0);
+  WALSH_CHECK_ARG(al16(q) && al16(k_cache) && al16(v_cache) && al16(wq_beta) && al16(wk_beta) && al16(wv_beta) &&
+                  al16(rope_cos) && al16(rope_sin));
   const int64_t ntok = (int64_t)B * T;
   const int smem = 4 * kTcTok * kTcRow * (int)sizeof(__half);
   TcQkvEpilogue ep{T, n_head, hd, ctx, start_pos, rope_cos, rope_sin};
@@ -347,8 +380,8 @@ extern "C" walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const
   WALSH_CHECK_ARG(o && wo_f16 && wo_alpha && wo_beta && x && hmix && x_out);
   WALSH_CHECK_ARG(!wmix_f16 || beta_mix);
   WALSH_CHECK_SHAPE(ntok >= 0);
-  WALSH_CHECK_ARG(al16(o) && al16(wo_f16) && (!wmix_f16 || al16(wmix_f16)) &&
-                  (((uintptr_t)x | (uintptr_t)x_out) & 3u) == 0);
+  WALSH_CHECK_ARG(al16(o) && al16(wo_f16) && (!wmix_f16 || al16(wmix_f16)) && al16(x) && al16(x_out) &&
+                  al16(wo_beta));
   if (ntok == 0) return WALSH_OK;
   const int smem = 4 * kTcTok * kTcRow * (int)sizeof(__half);
   if (smem_set((const void*)attn_out_tc_kernel, smem)) return WALSH_ERR_LAUNCH;

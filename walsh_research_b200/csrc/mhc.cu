@@ -6,6 +6,7 @@
 // [24 x 4C] projection, then sigmoid / 2*sigmoid / Sinkhorn-20 in registers,
 // followed by the pre-mix H_pre @ x (src/model/mhc.py:364) and the block's
 // attention_norm / ffn_norm RMSNorm (src/model/mhc.py:514-523).
+#include <stdlib.h>
 #include <type_traits>
 
 #include "common.cuh"
@@ -151,32 +152,49 @@ mhc_map_kernel(const T* __restrict__ x, int64_t ntok, int C, const float* __rest
   }
 }
 
-// bf16 variant on the tensor cores: CTA = 4 warps x 16 tokens.  Each warp
-// streams its tokens' 4C values through shared memory in 128-column chunks
-// (cp.async, double-buffered), feeds them to m16n8k16 MMAs against phi
-// (bf16 copy, [24, 4C], read through L1) and takes the sum of squares from
-// the same A fragments.  Then lanes 0..15 finish one token each (RMS factor,
-// sigmoid / Sinkhorn) and the warp does the pre-mix + RMSNorm per token.
+// bf16 variant on the tensor cores: CTA = 8 warps x 16 tokens.  The CTA
+// streams its 128 tokens' 4C values and the matching 128-column chunk of phi
+// (bf16 copy, [24, 4C]) through double-buffered shared memory with cp.async;
+// each warp runs m16n8k16 MMAs for its 16 tokens with both operands from
+// shared memory (ldmatrix) and takes the sum of squares from the same A
+// fragments.  Then lanes 0..15 finish one token each (RMS factor, sigmoid /
+// Sinkhorn) and the warp does the pre-mix + RMSNorm per token.
+namespace map_tc {
+constexpr int NW = 8, TOK = NW * 16, KC = 128, LDX = KC + 8;
+template <int C>
+constexpr size_t smem_bytes() {
+  return (size_t)2 * (TOK + kMapRows) * LDX * sizeof(__nv_bfloat16) + (size_t)NW * 16 * (kMapRows + 1) * sizeof(float) +
+         (size_t)NW * 16 * sizeof(float);
+}
+}  // namespace map_tc
+
 template <int C, typename TU>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv_bfloat16* __restrict__ phib,
                    const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
                    TU* __restrict__ u, float* __restrict__ hmix) {
-  constexpr int D = 4 * C, KC = 128, LDX = KC + 8, NCH = D / KC;
-  __shared__ __align__(16) __nv_bfloat16 xs[4][2][16][LDX];
-  __shared__ float ds[4][16][kMapRows + 1];
-  __shared__ float sss[4][16];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
-  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * 16;
+  using namespace map_tc;
+  constexpr int D = 4 * C, NCH = D / KC;
+  extern __shared__ float4 smem4[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);   // [2][TOK][LDX]
+  __nv_bfloat16* ps = xs + 2 * TOK * LDX;                          // [2][24][LDX]
+  float (*ds)[16][kMapRows + 1] = reinterpret_cast<float (*)[16][kMapRows + 1]>(ps + 2 * kMapRows * LDX);
+  float (*sss)[16] = reinterpret_cast<float (*)[16]>(reinterpret_cast<float*>(ds) + NW * 16 * (kMapRows + 1));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int64_t cta0 = (int64_t)blockIdx.x * TOK;
+  const int64_t tok0 = cta0 + warp * 16;
 
   auto load_chunk = [&](int ch, int buf) {
-#pragma unroll
-    for (int i = 0; i < (16 * KC / 8) / 32; ++i) {
-      const int idx = lane + 32 * i;
-      const int r = idx / (KC / 8), c = idx - r * (KC / 8);
-      const bool in = tok0 + r < ntok;
-      const __nv_bfloat16* src = x + (in ? (tok0 + r) * D : 0) + ch * KC + c * 8;
-      cp_async16(&xs[warp][buf][r][c * 8], src, in ? 16 : 0);
+    __nv_bfloat16* xd = xs + buf * TOK * LDX;
+    for (int i = tid; i < TOK * (KC / 8); i += 256) {
+      const int r = i / (KC / 8), c = i - r * (KC / 8);
+      const bool in = cta0 + r < ntok;
+      cp_async16(xd + r * LDX + c * 8, x + (in ? (cta0 + r) * D : 0) + ch * KC + c * 8, in ? 16 : 0);
+    }
+    __nv_bfloat16* pd = ps + buf * kMapRows * LDX;
+    for (int i = tid; i < kMapRows * (KC / 8); i += 256) {
+      const int r = i / (KC / 8), c = i - r * (KC / 8);
+      cp_async16(pd + r * LDX + c * 8, phib + (size_t)r * D + ch * KC + c * 8, 16);
     }
   };
   float acc[3][4];
@@ -190,28 +208,26 @@ mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv
     if (ch + 1 < NCH) load_chunk(ch + 1, buf ^ 1);
     cp_async_commit();
     cp_async_wait<1>();
-    __syncwarp();
+    __syncthreads();
+    const __nv_bfloat16* xw = xs + buf * TOK * LDX + warp * 16 * LDX;
+    const __nv_bfloat16* pw = ps + buf * kMapRows * LDX;
 #pragma unroll
     for (int ks = 0; ks < KC / 16; ++ks) {
-      uint32_t a[4];
-      ldsm_x4(a, &xs[warp][buf][lane & 15][ks * 16 + (lane >> 4) * 8]);
+      uint32_t a[4], b01[4], b2[2];
+      ldsm_x4(a, xw + (lane & 15) * LDX + ks * 16 + (lane >> 4) * 8);
+      ldsm_x4(b01, pw + ((lane & 7) + ((lane >> 4) << 3)) * LDX + ks * 16 + ((lane >> 3) & 1) * 8);
+      ldsm_x2(b2[0], b2[1], pw + (16 + (lane & 7)) * LDX + ks * 16 + ((lane >> 3) & 1) * 8);
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&a[r]);
-        const float v0 = __low2float(v), v1 = __high2float(v);
-        if (r & 1) ss_hi = fmaf(v0, v0, fmaf(v1, v1, ss_hi));
-        else ss_lo = fmaf(v0, v0, fmaf(v1, v1, ss_lo));
+        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a[r]));
+        if (r & 1) ss_hi = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_hi));
+        else ss_lo = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_lo));
       }
-      const int k0 = ch * KC + ks * 16 + 2 * t4;
-#pragma unroll
-      for (int n = 0; n < 3; ++n) {
-        const __nv_bfloat16* prow = phib + (size_t)(8 * n + g) * D + k0;
-        const uint32_t b0 = __ldg(reinterpret_cast<const unsigned int*>(prow));
-        const uint32_t b1 = __ldg(reinterpret_cast<const unsigned int*>(prow + 8));
-        mma_bf16(acc[n], a, b0, b1);
-      }
+      mma_bf16(acc[0], a, b01[0], b01[1]);
+      mma_bf16(acc[1], a, b01[2], b01[3]);
+      mma_bf16(acc[2], a, b2[0], b2[1]);
     }
-    __syncwarp();
+    __syncthreads();
   }
 #pragma unroll
   for (int off = 1; off <= 2; off <<= 1) {
@@ -256,21 +272,15 @@ mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
       const int c = (lane + 32 * v) * 8;
-      const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xt + c));
-      const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xt + C + c));
-      const uint4 q2 = __ldg(reinterpret_cast<const uint4*>(xt + 2 * C + c));
-      const uint4 q3 = __ldg(reinterpret_cast<const uint4*>(xt + 3 * C + c));
-      const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&q0);
-      const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&q1);
-      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&q2);
-      const __nv_bfloat162* p3 = reinterpret_cast<const __nv_bfloat162*>(&q3);
+      float f0[8], f1[8], f2[8], f3[8];
+      load8(xt + c, f0);
+      load8(xt + C + c, f1);
+      load8(xt + 2 * C + c, f2);
+      load8(xt + 3 * C + c, f3);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f0 = __bfloat1622float2(p0[e]), f1 = __bfloat1622float2(p1[e]);
-        const float2 f2 = __bfloat1622float2(p2[e]), f3 = __bfloat1622float2(p3[e]);
-        uv[v][2 * e] = ((h0 * f0.x + h1 * f1.x) + h2 * f2.x) + h3 * f3.x;
-        uv[v][2 * e + 1] = ((h0 * f0.y + h1 * f1.y) + h2 * f2.y) + h3 * f3.y;
-        s2 = fmaf(uv[v][2 * e], uv[v][2 * e], fmaf(uv[v][2 * e + 1], uv[v][2 * e + 1], s2));
+      for (int e = 0; e < 8; ++e) {
+        uv[v][e] = ((h0 * f0[e] + h1 * f1[e]) + h2 * f2[e]) + h3 * f3[e];
+        s2 = fmaf(uv[v][e], uv[v][e], s2);
       }
     }
     s2 = warp_sum(s2);
@@ -278,17 +288,10 @@ mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
       const int c = (lane + 32 * v) * 8;
-      uint32_t w[4];
+      float o[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float a = uv[v][2 * e] * rn, b = uv[v][2 * e + 1] * rn;
-        if (norm_w) {
-          a *= __ldg(norm_w + c + 2 * e);
-          b *= __ldg(norm_w + c + 2 * e + 1);
-        }
-        w[e] = sizeof(TU) == 2 && !std::is_same<TU, __nv_bfloat16>::value ? pack_f16_sat(a, b) : pack_bf16(a, b);
-      }
-      *reinterpret_cast<uint4*>(u + tok * C + c) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int e = 0; e < 8; ++e) o[e] = uv[v][e] * rn * (norm_w ? __ldg(norm_w + c + e) : 1.f);
+      store8(u + tok * C + c, o);
     }
   }
 }
@@ -357,19 +360,21 @@ extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, in
   cudaStream_t s = (cudaStream_t)stream;
   const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_bf16)) & 15u) == 0;
   if (dtype == WALSH_BF16 && u_dtype != WALSH_F32 && phi_bf16 && vec_ok && (C == 512 || C == 2048)) {
-    const unsigned grid = (unsigned)((ntok + 63) / 64);
+    const unsigned grid = (unsigned)((ntok + map_tc::TOK - 1) / map_tc::TOK);
     const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
     const __nv_bfloat16* pb = (const __nv_bfloat16*)phi_bf16;
-    if (C == 512 && u_dtype == WALSH_F16)
-      mhc_map_mma_kernel<512, __half><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps, (__half*)u, hmix);
-    else if (C == 512)
-      mhc_map_mma_kernel<512, __nv_bfloat16><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps,
-                                                                  (__nv_bfloat16*)u, hmix);
-    else if (u_dtype == WALSH_F16)
-      mhc_map_mma_kernel<2048, __half><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps, (__half*)u, hmix);
-    else
-      mhc_map_mma_kernel<2048, __nv_bfloat16><<<grid, 128, 0, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps,
-                                                                   (__nv_bfloat16*)u, hmix);
+#define WALSH_MAP_TC(CC, TU)                                                                                  \
+  {                                                                                                          \
+    const int smem = (int)map_tc::smem_bytes<CC>();                                                          \
+    cudaFuncSetAttribute(mhc_map_mma_kernel<CC, TU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);     \
+    mhc_map_mma_kernel<CC, TU><<<grid, 256, smem, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps,    \
+                                                      (TU*)u, hmix);                                         \
+  }
+    if (C == 512 && u_dtype == WALSH_F16) WALSH_MAP_TC(512, __half)
+    else if (C == 512) WALSH_MAP_TC(512, __nv_bfloat16)
+    else if (u_dtype == WALSH_F16) WALSH_MAP_TC(2048, __half)
+    else WALSH_MAP_TC(2048, __nv_bfloat16)
+#undef WALSH_MAP_TC
     return launch_status();
   }
   const bool big = ntok >= 148 * 64;

@@ -118,3 +118,9 @@ template <>
 __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) { return unpack_f16(v); }
 
 }  // namespace walsh
+
+namespace walsh {
+__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r0), "=r"(r1) : "r"(smem_addr(p)));
+}
+}  // namespace walsh

@@ -228,9 +228,12 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
 }
 
 // ---------------------------------------------------------------------------
-// bf16 tensor-core variant for C = 512 (E = 16, router hidden 128).
-// CTA = 4 warps x 16 tokens; each warp keeps its 16 token rows of u in shared
-// memory and runs, with m16n8k16 MMAs:
+// Tensor-core variant for C = 512 (E = 16, router hidden 128), u in TU = bf16
+// or fp16 with weights copied to TU.
+// CTA = 8 warps x 16 tokens (128 tokens).  Shared memory holds the CTA's u
+// rows and, streamed with cp.async through a double buffer, the router's W1
+// in 64-column chunks and then each expert's gate/up/down weights, so every
+// MMA B operand comes from shared memory via ldmatrix:
 //   router   h = silu(u W1^T) [16x128] -> logits = h W2^T [16x16] (h re-packed
 //            from accumulators to A fragments in registers);
 //   top-k    lanes 0..15 one token each (softmax, top_k, renormalise);
@@ -239,49 +242,105 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
 //            y_e += a D_e^T; the routing weight (0 when not selected) and gd
 //            scale y_e, then the mHC site epilogue (or a plain store) writes
 //            the expert's 32 columns.
-// Ternary weights are exact in bf16 ({-1, 0, +1}); the gammas are applied in
-// float32.  bf16 weight copies: w1 [128][512], w2 [16][128], gate/up
-// [16][128][32], down [16][32][128].
+// Ternary weights are exact in bf16/fp16; the gammas are applied in fp32.
 // ---------------------------------------------------------------------------
+namespace moe_tc {
+constexpr int C = 512, E = 16, HID = 128, NW = 8, TOK = NW * 16;
+constexpr int LDU = C + 8;               // u rows
+constexpr int KC = 64, LDW1 = KC + 8;    // router W1 chunk [128][KC]
+constexpr int LDG = 32 + 8;              // gate/up rows [128][32]
+constexpr int LDD = HID + 8;             // down rows [32][128]
+constexpr int LDW2 = HID + 8;            // W2 [16][128]
+constexpr int EXPERT_ELEMS = 2 * HID * LDG + 32 * LDD;  // one expert buffer (gate, up, down)
+constexpr int BUF_ELEMS = EXPERT_ELEMS > 2 * 0 + HID * LDW1 ? EXPERT_ELEMS : HID * LDW1;
 template <typename TU>
-__global__ void __launch_bounds__(128)
+constexpr size_t smem_bytes() {
+  return (size_t)(TOK * LDU + 2 * BUF_ELEMS + E * LDW2) * sizeof(TU) + (size_t)NW * 16 * (E + 1) * sizeof(float);
+}
+}  // namespace moe_tc
+
+template <typename TU>
+__global__ void __launch_bounds__(256, 1)
 moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* __restrict__ w1b,
                   const TU* __restrict__ w2b, const TU* __restrict__ gb, const TU* __restrict__ ub,
                   const TU* __restrict__ db, const float* __restrict__ gammas, TU* __restrict__ y, int fuse_post,
                   const __nv_bfloat16* x, const float* __restrict__ hmix, __nv_bfloat16* xo,
                   uint8_t* __restrict__ mask_out, float* __restrict__ probs_out, float* __restrict__ weights_out) {
-  constexpr int C = 512, E = 16, HID = 128, LDU = C + 8;
-  extern __shared__ float4 smem4[];  // us: [4 warps][16 rows][LDU] (66.5 KB, opt-in size)
-  TU (*us)[16][LDU] = reinterpret_cast<TU (*)[16][LDU]>(smem4);
-  __shared__ float lg[4][16][E + 1];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
-  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * 16;
-#pragma unroll
-  for (int i = 0; i < (16 * C / 8) / 32; ++i) {
-    const int idx = lane + 32 * i;
-    const int r = idx / (C / 8), c = idx - r * (C / 8);
-    const bool in = tok0 + r < ntok;
-    cp_async16(&us[warp][r][c * 8], u + (in ? (tok0 + r) * C : 0) + c * 8, in ? 16 : 0);
-  }
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncwarp();
+  using namespace moe_tc;
+  extern __shared__ float4 smem4[];
+  TU* us = reinterpret_cast<TU*>(smem4);                   // [TOK][LDU]
+  TU* buf0 = us + TOK * LDU;                               // 2 x BUF_ELEMS
+  TU* w2s = buf0 + 2 * BUF_ELEMS;                          // [E][LDW2]
+  float* lgs = reinterpret_cast<float*>(w2s + E * LDW2);   // [NW][16][E+1]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int64_t cta0 = (int64_t)blockIdx.x * TOK;
+  const int64_t tok0 = cta0 + warp * 16;
+  TU* uw = us + warp * 16 * LDU;
+  float (*lg)[E + 1] = reinterpret_cast<float (*)[E + 1]>(lgs + warp * 16 * (E + 1));
 
-  // ---- router layer 1: [16 x 512] x [512 x 128]
+  // ---- stage u rows (zero past ntok), W2, W1 chunk 0
+  for (int i = tid; i < TOK * (C / 8); i += 256) {
+    const int r = i / (C / 8), c = i - r * (C / 8);
+    const bool in = cta0 + r < ntok;
+    cp_async16(us + r * LDU + c * 8, u + (in ? (cta0 + r) * C : 0) + c * 8, in ? 16 : 0);
+  }
+  for (int i = tid; i < E * (HID / 8); i += 256) {
+    const int r = i / (HID / 8), c = i - r * (HID / 8);
+    cp_async16(w2s + r * LDW2 + c * 8, w2b + r * HID + c * 8, 16);
+  }
+  auto load_w1 = [&](int kc, TU* dst) {
+    for (int i = tid; i < HID * (KC / 8); i += 256) {
+      const int r = i / (KC / 8), c = i - r * (KC / 8);
+      cp_async16(dst + r * LDW1 + c * 8, w1b + (size_t)r * C + kc * KC + c * 8, 16);
+    }
+  };
+  load_w1(0, buf0);
+  cp_async_commit();
+
+  // ---- router layer 1: [16 x 512] x [512 x 128], W1 streamed in KC-column chunks
   float hacc[HID / 8][4];
 #pragma unroll
   for (int n = 0; n < HID / 8; ++n) hacc[n][0] = hacc[n][1] = hacc[n][2] = hacc[n][3] = 0.f;
-#pragma unroll 2
-  for (int ks = 0; ks < C / 16; ++ks) {
-    uint32_t a[4];
-    ldsm_x4(a, &us[warp][lane & 15][ks * 16 + (lane >> 4) * 8]);
+  for (int kc = 0; kc < C / KC; ++kc) {
+    TU* cur = buf0 + (kc & 1) * BUF_ELEMS;
+    if (kc + 1 < C / KC) load_w1(kc + 1, buf0 + ((kc + 1) & 1) * BUF_ELEMS);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
 #pragma unroll
-    for (int n = 0; n < HID / 8; ++n) {
-      const TU* wr = w1b + (size_t)(8 * n + g) * C + ks * 16 + 2 * t4;
-      mma16<TU>(hacc[n], a, __ldg(reinterpret_cast<const unsigned int*>(wr)),
-                __ldg(reinterpret_cast<const unsigned int*>(wr + 8)));
+    for (int ks = 0; ks < KC / 16; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(a, uw + (lane & 15) * LDU + kc * KC + ks * 16 + (lane >> 4) * 8);
+#pragma unroll
+      for (int np = 0; np < HID / 16; ++np) {
+        uint32_t bf[4];
+        ldsm_x4(bf, cur + (np * 16 + (lane & 7) + ((lane >> 4) << 3)) * LDW1 + ks * 16 + ((lane >> 3) & 1) * 8);
+        mma16<TU>(hacc[2 * np], a, bf[0], bf[1]);
+        mma16<TU>(hacc[2 * np + 1], a, bf[2], bf[3]);
+      }
     }
+    __syncthreads();
   }
+  // prefetch expert 0 while the router finishes
+  auto load_expert = [&](int e, TU* dst) {
+    TU* gd = dst;
+    TU* ud = dst + HID * LDG;
+    TU* dd = dst + 2 * HID * LDG;
+    for (int i = tid; i < 3 * 512; i += 256) {
+      const int part = i >> 9, j = i & 511;
+      if (part < 2) {  // gate / up: 128 rows x 4 chunks
+        const int r = j >> 2, c = j & 3;
+        const TU* src = (part == 0 ? gb : ub) + ((size_t)e * HID + r) * 32 + c * 8;
+        cp_async16((part == 0 ? gd : ud) + r * LDG + c * 8, src, 16);
+      } else {         // down: 32 rows x 16 chunks
+        const int r = j >> 4, c = j & 15;
+        cp_async16(dd + r * LDD + c * 8, db + ((size_t)e * 32 + r) * HID + c * 8, 16);
+      }
+    }
+  };
+  if (gb) load_expert(0, buf0);
+  cp_async_commit();
+
   // ---- silu, repack as A fragments, router layer 2: [16 x 128] x [128 x 16]
   float lacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -293,24 +352,22 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
       a[half * 2 + 0] = pack2<TU>(siluf_(c[0]), siluf_(c[1]));
       a[half * 2 + 1] = pack2<TU>(siluf_(c[2]), siluf_(c[3]));
     }
-#pragma unroll
-    for (int n = 0; n < 2; ++n) {
-      const TU* wr = w2b + (size_t)(8 * n + g) * HID + kk * 16 + 2 * t4;
-      mma16<TU>(lacc[n], a, __ldg(reinterpret_cast<const unsigned int*>(wr)),
-                __ldg(reinterpret_cast<const unsigned int*>(wr + 8)));
-    }
+    uint32_t bf[4];
+    ldsm_x4(bf, w2s + ((lane & 7) + ((lane >> 4) << 3)) * LDW2 + kk * 16 + ((lane >> 3) & 1) * 8);
+    mma16<TU>(lacc[0], a, bf[0], bf[1]);
+    mma16<TU>(lacc[1], a, bf[2], bf[3]);
   }
 #pragma unroll
   for (int n = 0; n < 2; ++n) {
-    lg[warp][g][8 * n + 2 * t4] = lacc[n][0];
-    lg[warp][g][8 * n + 2 * t4 + 1] = lacc[n][1];
-    lg[warp][g + 8][8 * n + 2 * t4] = lacc[n][2];
-    lg[warp][g + 8][8 * n + 2 * t4 + 1] = lacc[n][3];
+    lg[g][8 * n + 2 * t4] = lacc[n][0];
+    lg[g][8 * n + 2 * t4 + 1] = lacc[n][1];
+    lg[g + 8][8 * n + 2 * t4] = lacc[n][2];
+    lg[g + 8][8 * n + 2 * t4 + 1] = lacc[n][3];
   }
   __syncwarp();
-  // ---- softmax + top-k: lane t < 16 owns token t; lg row becomes the routing weight
+  // ---- softmax + top-k: lane t < 16 owns token t; its lg row becomes the routing weight
   if (lane < 16) {
-    float* l = lg[warp][lane];
+    float* l = lg[lane];
     float mx = -CUDART_INF_F;
 #pragma unroll
     for (int e = 0; e < E; ++e) mx = fmaxf(mx, l[e]);
@@ -351,24 +408,28 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
     }
   }
   __syncwarp();
-  if (!gb) return;  // router-only call
-
-  // ---- experts
-  const float gg = __ldg(gammas + 0), gu = __ldg(gammas + 1), gd = __ldg(gammas + 2);
-  const int64_t tlo = tok0 + g, thi = tlo + 8;
-  float hm_lo[20], hm_hi[20];  // {H_post[4], H_res[16]} of rows g and g+8
-  if (fuse_post) {
-#pragma unroll
-    for (int i = 0; i < 20; ++i) {
-      hm_lo[i] = tlo < ntok ? __ldg(hmix + tlo * kMapRows + 4 + i) : 0.f;
-      hm_hi[i] = thi < ntok ? __ldg(hmix + thi * kMapRows + 4 + i) : 0.f;
-    }
+  if (!gb) {  // router-only call
+    cp_async_wait<0>();
+    return;
   }
+
+  // ---- experts (weights double-buffered in shared memory).  Expert e's
+  // weighted output replaces the warp's (already consumed) u block e in
+  // shared memory; the site epilogue streams the rows out afterwards.
+  const float gg = __ldg(gammas + 0), gu = __ldg(gammas + 1), gd = __ldg(gammas + 2);
 #pragma unroll 1
   for (int e = 0; e < E; ++e) {
+    const TU* cur = buf0 + (e & 1) * BUF_ELEMS;
+    if (e + 1 < E) load_expert(e + 1, buf0 + ((e + 1) & 1) * BUF_ELEMS);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const TU* gs = cur;
+    const TU* uss = cur + HID * LDG;
+    const TU* ds = cur + 2 * HID * LDG;
     uint32_t ae[2][4];
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) ldsm_x4(ae[ks], &us[warp][lane & 15][e * 32 + ks * 16 + (lane >> 4) * 8]);
+    for (int ks = 0; ks < 2; ++ks) ldsm_x4(ae[ks], uw + (lane & 15) * LDU + e * 32 + ks * 16 + (lane >> 4) * 8);
     float yacc[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) yacc[n][0] = yacc[n][1] = yacc[n][2] = yacc[n][3] = 0.f;
@@ -380,14 +441,16 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const size_t row = (size_t)e * HID + half * 64 + 8 * n + g;
-          const TU* gr = gb + row * 32 + ks * 16 + 2 * t4;
-          const TU* ur = ub + row * 32 + ks * 16 + 2 * t4;
-          mma16<TU>(ga[n], ae[ks], __ldg(reinterpret_cast<const unsigned int*>(gr)),
-                    __ldg(reinterpret_cast<const unsigned int*>(gr + 8)));
-          mma16<TU>(va[n], ae[ks], __ldg(reinterpret_cast<const unsigned int*>(ur)),
-                    __ldg(reinterpret_cast<const unsigned int*>(ur + 8)));
+        for (int np = 0; np < 4; ++np) {
+          const int row = half * 64 + np * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int col = ks * 16 + ((lane >> 3) & 1) * 8;
+          uint32_t bg[4], bu[4];
+          ldsm_x4(bg, gs + row * LDG + col);
+          ldsm_x4(bu, uss + row * LDG + col);
+          mma16<TU>(ga[2 * np], ae[ks], bg[0], bg[1]);
+          mma16<TU>(ga[2 * np + 1], ae[ks], bg[2], bg[3]);
+          mma16<TU>(va[2 * np], ae[ks], bu[0], bu[1]);
+          mma16<TU>(va[2 * np + 1], ae[ks], bu[2], bu[3]);
         }
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {  // hidden units half*64 + 16 kk .. +15
@@ -400,42 +463,67 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
           a[hh * 2 + 1] = pack2<TU>(siluf_(gg * G[2]) * (gu * V[2]), siluf_(gg * G[3]) * (gu * V[3]));
         }
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const TU* dr = db + ((size_t)e * 32 + 8 * n + g) * HID + half * 64 + kk * 16 + 2 * t4;
-          mma16<TU>(yacc[n], a, __ldg(reinterpret_cast<const unsigned int*>(dr)),
-                    __ldg(reinterpret_cast<const unsigned int*>(dr + 8)));
+        for (int np = 0; np < 2; ++np) {
+          uint32_t bd[4];
+          ldsm_x4(bd, ds + (np * 16 + (lane & 7) + ((lane >> 4) << 3)) * LDD + half * 64 + kk * 16 +
+                          ((lane >> 3) & 1) * 8);
+          mma16<TU>(yacc[2 * np], a, bd[0], bd[1]);
+          mma16<TU>(yacc[2 * np + 1], a, bd[2], bd[3]);
         }
       }
     }
-    const float w_lo = lg[warp][g][e] * gd, w_hi = lg[warp][g + 8][e] * gd;
+    const float w_lo = lg[g][e] * gd, w_hi = lg[g + 8][e] * gd;
+    __syncwarp();  // every lane's ldmatrix of u block e is done before it is overwritten
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
       const int c = e * 32 + 8 * n + 2 * t4;
-      const float y0 = yacc[n][0] * w_lo, y1 = yacc[n][1] * w_lo;
-      const float y2 = yacc[n][2] * w_hi, y3 = yacc[n][3] * w_hi;
+      *reinterpret_cast<uint32_t*>(uw + g * LDU + c) = pack2<TU>(yacc[n][0] * w_lo, yacc[n][1] * w_lo);
+      *reinterpret_cast<uint32_t*>(uw + (g + 8) * LDU + c) = pack2<TU>(yacc[n][2] * w_hi, yacc[n][3] * w_hi);
+    }
+    __syncthreads();  // buffer (e & 1) is refilled by the next iteration's prefetch
+  }
+  // ---- epilogue: 8 consecutive columns per lane, 16-byte loads and stores
+  for (int t = 0; t < 16; ++t) {
+    const int64_t tok = tok0 + t;
+    if (tok >= ntok) break;
+    float hp[4], hr[16];
+    if (fuse_post) {
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int64_t tok = rr ? thi : tlo;
-        if (tok >= ntok) continue;
-        const float ya = rr ? y2 : y0, yb = rr ? y3 : y1;
-        if (!fuse_post) {
-          *reinterpret_cast<uint32_t*>(y + tok * C + c) = pack2<TU>(ya, yb);
-          continue;
-        }
-        const float* hm = rr ? hm_hi : hm_lo;
-        const size_t base = (size_t)tok * 4 * C + c;
-        float2 xv[4];
+      for (int i = 0; i < 4; ++i) hp[i] = __ldg(hmix + tok * kMapRows + 4 + i);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          xv[j] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + base + (size_t)j * C));
+      for (int i = 0; i < 16; ++i) hr[i] = __ldg(hmix + tok * kMapRows + 8 + i);
+    }
+#pragma unroll
+    for (int pass = 0; pass < C / 256; ++pass) {
+      const int c = pass * 256 + lane * 8;
+      const uint4 yv = *reinterpret_cast<const uint4*>(uw + t * LDU + c);
+      if (!fuse_post) {
+        *reinterpret_cast<uint4*>(y + tok * C + c) = yv;
+        continue;
+      }
+      const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+      const size_t base = (size_t)tok * 4 * C + c;
+      uint4 xq[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xq[j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * C);
+      uint32_t ow[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 yf = unpack2<TU>(yw[q]);
+        float2 xf[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xf[j] = unpack2<__nv_bfloat16>((&xq[j].x)[q]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float* hr = hm + 4 + 4 * i;
-          const float va0 = (((hr[0] * xv[0].x + hr[1] * xv[1].x) + hr[2] * xv[2].x) + hr[3] * xv[3].x) + hm[i] * ya;
-          const float va1 = (((hr[0] * xv[0].y + hr[1] * xv[1].y) + hr[2] * xv[2].y) + hr[3] * xv[3].y) + hm[i] * yb;
-          *reinterpret_cast<uint32_t*>(xo + base + (size_t)i * C) = pack_bf16(va0, va1);
+          const float* r = hr + 4 * i;
+          const float a0 = (((r[0] * xf[0].x + r[1] * xf[1].x) + r[2] * xf[2].x) + r[3] * xf[3].x) + hp[i] * yf.x;
+          const float a1 = (((r[0] * xf[0].y + r[1] * xf[1].y) + r[2] * xf[2].y) + r[3] * xf[3].y) + hp[i] * yf.y;
+          ow[i][q] = pack_bf16(a0, a1);
         }
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(xo + base + (size_t)i * C) = make_uint4(ow[i][0], ow[i][1], ow[i][2], ow[i][3]);
     }
   }
 }
@@ -460,10 +548,11 @@ template <typename TU>
 static int launch_moe_mma(const void* u, int64_t ntok, int top_k, const walsh_moe_tc_weights* tc, bool experts,
                           const float* gammas, void* y, int fuse_post, const void* x, const float* hmix, void* xo,
                           uint8_t* mask_out, float* probs_out, float* weights_out, cudaStream_t s) {
-  const unsigned grid = (unsigned)((ntok + 63) / 64);
-  const int smem = 4 * 16 * (512 + 8) * (int)sizeof(TU);
-  cudaFuncSetAttribute(moe_mma512_kernel<TU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  moe_mma512_kernel<TU><<<grid, 128, smem, s>>>(
+  const unsigned grid = (unsigned)((ntok + moe_tc::TOK - 1) / moe_tc::TOK);
+  const int smem = (int)moe_tc::smem_bytes<TU>();
+  if (cudaFuncSetAttribute(moe_mma512_kernel<TU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return WALSH_ERR_LAUNCH;
+  moe_mma512_kernel<TU><<<grid, 256, smem, s>>>(
       (const TU*)u, ntok, top_k, (const TU*)tc->w1, (const TU*)tc->w2, experts ? (const TU*)tc->gate : nullptr,
       (const TU*)tc->up, (const TU*)tc->down, gammas, (TU*)y, fuse_post, (const __nv_bfloat16*)x, hmix,
       (__nv_bfloat16*)xo, mask_out, probs_out, weights_out);
@@ -498,7 +587,7 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
   if (dtype != WALSH_F32 && C == 512 && tc && tc->w1 && tc->w2 && !weights_in &&
       (!experts || (tc->gate && tc->up && tc->down)) && (!fuse_post || x_dtype == WALSH_BF16) &&
       ((((uintptr_t)u) | ((uintptr_t)tc->w1) | ((uintptr_t)tc->w2) | ((uintptr_t)tc->gate) |
-        ((uintptr_t)tc->up) | ((uintptr_t)tc->down)) & 15u) == 0) {
+        ((uintptr_t)tc->up) | ((uintptr_t)tc->down) | ((uintptr_t)y) | ((uintptr_t)x) | ((uintptr_t)x_out)) & 15u) == 0) {
     return dtype == WALSH_F16
                ? launch_moe_mma<__half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out, mask_out,
                                         probs_out, weights_out, s)
