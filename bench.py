@@ -186,12 +186,6 @@ def run_reference(args):
 # the B200 arm
 # ---------------------------------------------------------------------------
 
-def kernel_launches_per_forward(L=16):
-    # embed gather 1; per layer: map 2, qkv 1, attn 1, head mixer 1, wo 1, post 1, moe 1, chmod 3;
-    # merge linear 1, rmsnorm 1, logits linear 1
-    return 1 + L * 12 + 3
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -239,8 +233,11 @@ def main():
             model(idx)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
+        from walsh_research_b200 import _lib
+        n0 = _lib.launch_count
         with torch.cuda.graph(graph):
             logits_g, _ = model(idx)
+        launches_per_forward = _lib.launch_count - n0
         for _ in range(args.warmup):
             graph.replay()
         torch.cuda.synchronize()
@@ -311,7 +308,7 @@ def main():
                        "batch_per_gpu": B, "seq_len": T, "parallelism": f"replicas x{world} (batch-sharded)",
                        "l2": "working set > L2 (stream state 268 MB per layer), no flush"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-            "gpu_launches": kernel_launches_per_forward(CONFIG["n_layer"]) * args.steps,
+            "gpu_launches": launches_per_forward * args.steps,
             "peaks": src}
     print(json.dumps(line), flush=True)
 

@@ -48,6 +48,10 @@ SIGNATURES = {
     "walsh_rmsnorm": [P, c_int, c_int64, c_int, P, c_float, P, c_int, P],
 }
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p}
+# kernels each entry point launches (for the launch accounting reported by bench.py)
+KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
+                    "walsh_abi_version": 0}
+launch_count = 0
 # entry points that return a plain int rather than a status
 _PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows"}
 
@@ -87,7 +91,9 @@ def status_str(code: int) -> str:
 
 
 def call(name: str, *args) -> int:
+    global launch_count
     rc = getattr(lib(), name)(*args)
+    launch_count += KERNELS_PER_CALL.get(name, 1)
     if name in _PLAIN_INT or name in _RESTYPE:
         return rc
     if rc != 0:

@@ -161,7 +161,7 @@ class mHCLlamaBlock(nn.Module):
             w1t, w2, g, up, d, gam, k, tc = ff.kernel_args(idt)
             if record_stats:
                 _, mask, probs, _ = ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True, tc=tc)
-                ff._record(mask.float(), probs, B * T)
+                ff._record(mask, probs, B * T)
             else:
                 ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), tc=tc)
         else:

@@ -127,7 +127,7 @@ class HadamardMoE(nn.Module):
         self._last_router_probs = None
         self.register_buffer("_expert_counts", torch.zeros(n_experts), persistent=False)
         self.register_buffer("_total_tokens", torch.zeros(1), persistent=False)
-        self._last_expert_mask = None
+        self.__dict__["_last_mask_u8"] = None
 
     def kernel_args(self, dtype=torch.float16):
         """Arguments of ops.moe for activations u of ``dtype``:
@@ -139,8 +139,18 @@ class HadamardMoE(nn.Module):
             tc = self.router.weights_tc(dtype) + self.experts.ternary_tc(dtype)
         return w1t, w2, g, u, d, gam, self.router.top_k, tc
 
+    @property
+    def _last_expert_mask(self):
+        """0/1 float mask [B, T, E] of the last forward's selections (src/model/moe.py:529)."""
+        m = self.__dict__.get("_last_mask_u8")
+        return None if m is None else m.float()
+
+    @_last_expert_mask.setter
+    def _last_expert_mask(self, value):
+        self.__dict__["_last_mask_u8"] = value
+
     def _record(self, mask, probs, ntok):
-        self._last_expert_mask = mask
+        self.__dict__["_last_mask_u8"] = mask  # kept as the kernel's uint8; converted on access
         self._last_router_probs = probs
         self._aux_loss = None  # reduced lazily by get_aux_loss
         if self.training:
@@ -152,7 +162,7 @@ class HadamardMoE(nn.Module):
         B, T, C = x.shape
         w1t, w2, g, u, d, gam, k, tc = self.kernel_args(x.dtype)
         y, mask, probs, _ = ops.moe(x, w1t, w2, g, u, d, gam, k, want_stats=True, tc=tc)
-        self._record(mask.float(), probs, B * T)
+        self._record(mask, probs, B * T)
         return y
 
     def _compute_aux_loss(self, router_probs, expert_mask):
