@@ -7,6 +7,7 @@
 // 1/sqrt(hd) scale pre-multiplied by log2(e).
 #include <math_constants.h>
 
+#include <stdlib.h>
 #include <type_traits>
 
 #include "common.cuh"
@@ -144,11 +145,11 @@ attn_decode_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* _
 // O += P V with m16n8k16 bf16 MMAs (fp32 accumulate), the S accumulators
 // re-packed in registers as the A operand of P V; online softmax in exp2.
 // ---------------------------------------------------------------------------
-template <int HD, typename TE>
+template <int HD, typename TE, int KT>
 __global__ void __launch_bounds__(256)
 attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* __restrict__ vc, int H, int Tq,
                 int ctx, int start_pos, float scale_log2, TE* __restrict__ o) {
-  constexpr int QT = 128, KT = 64, LD = HD + 8;  // padded rows: conflict-free ldmatrix
+  constexpr int QT = 128, LD = HD + 8;  // padded rows: conflict-free ldmatrix
   constexpr int CH = HD / 8;                     // 16-byte chunks per row
   __shared__ __align__(16) TE Qs[QT][LD];
   __shared__ __align__(16) TE Ks[2][KT][LD];
@@ -240,7 +241,10 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
       // rows with no visible key yet keep m = -inf; subtract 0 so exp2 gives 0, not NaN
       const float sub_lo = mn_lo == -CUDART_INF_F ? 0.f : mn_lo * scale_log2;
       const float sub_hi = mn_hi == -CUDART_INF_F ? 0.f : mn_hi * scale_log2;
-      const float corr_lo = exp2f(m_lo * scale_log2 - sub_lo), corr_hi = exp2f(m_hi * scale_log2 - sub_hi);
+      // the O / row-sum rescale is skipped when no row maximum of this warp moved
+      const bool moved = __any_sync(0xffffffffu, mn_lo != m_lo || mn_hi != m_hi);
+      const float corr_lo = moved ? ex2_f32(m_lo * scale_log2 - sub_lo) : 1.f;
+      const float corr_hi = moved ? ex2_f32(m_hi * scale_log2 - sub_hi) : 1.f;
       m_lo = mn_lo;
       m_hi = mn_hi;
       uint32_t pf[KT / 16][4];
@@ -248,10 +252,10 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
         // p = 2^(s * scale - m * scale) two at a time in fp16 (the P V operand precision)
 #pragma unroll
         for (int n = 0; n < KT / 8; ++n) {
-          const __half2 p01 = h2exp2(__floats2half2_rn(fmaf(s[n][0], scale_log2, -sub_lo), fmaf(s[n][1], scale_log2, -sub_lo)));
-          const __half2 p23 = h2exp2(__floats2half2_rn(fmaf(s[n][2], scale_log2, -sub_hi), fmaf(s[n][3], scale_log2, -sub_hi)));
-          pf[n >> 1][(n & 1) * 2 + 0] = *reinterpret_cast<const uint32_t*>(&p01);
-          pf[n >> 1][(n & 1) * 2 + 1] = *reinterpret_cast<const uint32_t*>(&p23);
+          pf[n >> 1][(n & 1) * 2 + 0] =
+              ex2_f16x2(pack_f16(fmaf(s[n][0], scale_log2, -sub_lo), fmaf(s[n][1], scale_log2, -sub_lo)));
+          pf[n >> 1][(n & 1) * 2 + 1] =
+              ex2_f16x2(pack_f16(fmaf(s[n][2], scale_log2, -sub_hi), fmaf(s[n][3], scale_log2, -sub_hi)));
         }
       } else {
         float rs_lo = 0.f, rs_hi = 0.f;
@@ -267,10 +271,12 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
         l_lo = l_lo * corr_lo + rs_lo;
         l_hi = l_hi * corr_hi + rs_hi;
       }
+      if (moved) {
 #pragma unroll
-      for (int i = 0; i < HD / 8 + 1; ++i) {
-        oacc[i][0] *= corr_lo; oacc[i][1] *= corr_lo;
-        oacc[i][2] *= corr_hi; oacc[i][3] *= corr_hi;
+        for (int i = 0; i < HD / 8 + 1; ++i) {
+          oacc[i][0] *= corr_lo; oacc[i][1] *= corr_lo;
+          oacc[i][2] *= corr_hi; oacc[i][3] *= corr_hi;
+        }
       }
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk) {
@@ -321,8 +327,8 @@ static int launch_attn(const void* q, const void* kc, const void* vc, int B, int
   if constexpr (sizeof(T) == 2) {
     if (Tq > 4 && aligned) {
       dim3 grid((Tq + 127) / 128, H, B);
-      attn_mma_kernel<HD, T><<<grid, 256, 0, s>>>((const T*)q, (const T*)kc, (const T*)vc, H, Tq, ctx, start_pos,
-                                                 scale_log2, (T*)o);
+      attn_mma_kernel<HD, T, 64><<<grid, 256, 0, s>>>((const T*)q, (const T*)kc, (const T*)vc, H, Tq, ctx,
+                                                       start_pos, scale_log2, (T*)o);
       return launch_status();
     }
   }

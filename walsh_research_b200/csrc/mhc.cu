@@ -14,24 +14,25 @@
 
 namespace walsh {
 
-// Sinkhorn-Knopp on a 4x4 matrix held in registers (src/model/mhc.py:214-229).
+// Sinkhorn-Knopp on a 4x4 matrix held in registers (src/model/mhc.py:214-229):
+// exp, then `iters` x (column, row) normalisation.  Each normalisation takes one
+// correctly rounded reciprocal of (sum + eps) and four multiplies (within one
+// ulp of the reference's four divisions per line).
 __device__ __forceinline__ void sinkhorn4(float* M, int iters, float eps) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) M[i] = expf(M[i]);
   for (int it = 0; it < iters; ++it) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float s = ((M[c] + M[4 + c]) + M[8 + c]) + M[12 + c];
-      const float den = s + eps;
+      const float inv = __frcp_rn((((M[c] + M[4 + c]) + M[8 + c]) + M[12 + c]) + eps);
 #pragma unroll
-      for (int r = 0; r < 4; ++r) M[4 * r + c] = __fdiv_rn(M[4 * r + c], den);
+      for (int r = 0; r < 4; ++r) M[4 * r + c] *= inv;
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const float s = ((M[4 * r] + M[4 * r + 1]) + M[4 * r + 2]) + M[4 * r + 3];
-      const float den = s + eps;
+      const float inv = __frcp_rn((((M[4 * r] + M[4 * r + 1]) + M[4 * r + 2]) + M[4 * r + 3]) + eps);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) M[4 * r + c] = __fdiv_rn(M[4 * r + c], den);
+      for (int c = 0; c < 4; ++c) M[4 * r + c] *= inv;
     }
   }
 }

@@ -56,10 +56,30 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // Two floats -> packed fp16x2, saturating at +-65504 instead of overflowing to inf.
 __device__ __forceinline__ uint32_t pack_f16_sat(float lo, float hi) {
-  lo = fminf(fmaxf(lo, -65504.f), 65504.f);
-  hi = fminf(fmaxf(hi, -65504.f), 65504.f);
-  __half2 v = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+  uint32_t r;  // one conversion instruction; the first source lands in the upper half
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Two floats -> packed fp16x2 (round to nearest, no saturation; first source in the upper half).
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2^x on both fp16 halves (PTX ex2.approx.f16x2); -inf -> +0.
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;\n" : "=r"(r) : "r"(x));
+  return r;
+}
+
+// 2^x (PTX ex2.approx.ftz.f32); -inf -> +0.
+__device__ __forceinline__ float ex2_f32(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(x));
+  return r;
 }
 
 __device__ __forceinline__ float2 unpack_f16(uint32_t v) {
