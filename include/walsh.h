@@ -48,7 +48,8 @@ enum {
   WALSH_ERR_TIMEOUT = -6,  /* a bounded device-side wait gave up */
   WALSH_ERR_INJECTED = -7, /* host-side fault injector fired (tests) */
   WALSH_ERR_NOT_INIT = -8, /* library not initialised for this device */
-  WALSH_ERR_INDEX = -9     /* a device kernel saw an out-of-range token id */
+  WALSH_ERR_INDEX = -9,    /* a device kernel saw an out-of-range token id */
+  WALSH_ERR_SCRATCH = -10  /* problem larger than an allocation-free entry point's fixed scratch */
 };
 
 enum { WALSH_F32 = 0, WALSH_BF16 = 1, WALSH_F16 = 2 };
@@ -285,6 +286,25 @@ walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrows, int C, i
                                const float* norm_w, float norm_eps, const float* scale,
                                const float* shift, float residual_scale, int add_input, void* out,
                                void* stream);
+
+/* Allocation-free channel modulation: stats, mlp and apply above in one call,
+ * with the scratch (partial sums, scale, shift) in a fixed device array inside
+ * the library instead of caller buffers.  No counterpart in the reference (its
+ * PyTorch forward allocates freely); it exists for hosts that cannot allocate
+ * device memory at call time.  Arguments mean what they mean for
+ * walsh_chmod_stats/_mlp/_apply; out may alias x.
+ * Limit: round64(nseg*nchunk*C) + 2*round64(nseg*C/32) <= 1,048,576 floats
+ * (4 MiB; nchunk = ceil(seg_len / walsh_chmod_chunk_rows), round64 = round up
+ * to a multiple of 64), else WALSH_ERR_SCRATCH before any launch.
+ * The first call on a device, with that device current, looks up the array's
+ * address (set-up); make it before any stream capture.  The array is shared:
+ * calls that overlap on the device race and must be ordered by the caller.
+ * Nothing in it needs to start at zero. */
+walsh_status walsh_chmod_fwd_noalloc(const void* x, int dtype, int64_t nrows, int C, int seg_len,
+                                     const float* norm_w, float norm_eps, const uint8_t* w1_2bit,
+                                     const uint8_t* w2_2bit, const float* gammas,
+                                     const float* scale_temp, float residual_scale, int add_input,
+                                     void* out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Dense helpers around the layer stack

@@ -43,13 +43,14 @@ SIGNATURES = {
     "walsh_chmod_stats": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P],
     "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],
     "walsh_chmod_apply": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, c_float, c_int, P, P],
+    "walsh_chmod_fwd_noalloc": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, P, P, c_float, c_int, P, P],
     "walsh_embed_gather": [P, c_int64, P, c_int, c_int64, c_int, P, P, P],
     "walsh_linear_fwd": [P, c_int, c_int64, c_int, c_int64, P, c_int, c_int64, P, P, c_int, P],
     "walsh_rmsnorm": [P, c_int, c_int64, c_int, P, c_float, P, c_int, P],
 }
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p}
 # kernels each entry point launches (for the launch accounting reported by bench.py)
-KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
+KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
                     "walsh_abi_version": 0}
 launch_count = 0
 # entry points that return a plain int rather than a status

@@ -35,6 +35,7 @@ extern "C" const char* walsh_status_str(walsh_status s) {
     case WALSH_ERR_INJECTED: return "fault injected by WALSH_INJECT_FAULT";
     case WALSH_ERR_NOT_INIT: return "library not initialised for this device";
     case WALSH_ERR_INDEX: return "token id out of range";
+    case WALSH_ERR_SCRATCH: return "problem needs more scratch than the fixed array of an allocation-free entry point";
     default: return "unknown walsh status";
   }
 }

@@ -8,6 +8,9 @@
 //          reduction order is fixed;
 //   mlp:   bulk mean -> scaled-ternary MLP -> per-(segment, block) scale/shift;
 //   apply: out = x + xn + 0.5 * (xn * scale + 0.1 * shift - xn).
+#include <atomic>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace walsh {
@@ -281,4 +284,99 @@ extern "C" walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrow
                                              (const T*)x, nrows, C, seg_len, norm_w, norm_eps, scale, shift,
                                              residual_scale, add_input, (T*)out),
                                          launch_status()));
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free channel modulation.
+//
+// walsh_chmod_stats / _mlp / _apply leave the scratch (per-chunk partial
+// sums, per-segment scale and shift) to the caller.  Some callers cannot
+// obtain device memory at the moment they run the layer: a host whose device
+// memory is planned once at start-up and which has no allocator at call time
+// (a plain C runtime, a memory-budgeted serving process), or code running
+// where an allocation would have to synchronise the device.  For them the
+// entry point below keeps the scratch in a fixed array in the library's own
+// device memory; the call itself allocates nothing.
+//
+// Every scratch word a step reads was written earlier in the same call
+// (stats writes every partial, mlp every scale and shift), so nothing has to
+// start at zero.  The array is one per device and shared by all callers:
+// two calls whose executions overlap on the device (other streams, other
+// host threads) race on it and must be ordered by the caller.
+// ---------------------------------------------------------------------------
+
+namespace walsh {
+
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;  // 4 MiB of float32
+constexpr int64_t kNoAllocAlignFloats = 64;                  // 256-byte sub-buffers
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) float g_chmod_scratch[kNoAllocScratchFloats];
+
+std::atomic<float*> g_chmod_scratch_ptr[kNoAllocMaxDevices];
+std::mutex g_chmod_scratch_mu;
+
+static int64_t round_up_floats(int64_t n) { return (n + kNoAllocAlignFloats - 1) / kNoAllocAlignFloats * kNoAllocAlignFloats; }
+
+// Device address of this device's scratch array, looked up once per device
+// (with that device current) and cached.
+static walsh_status chmod_scratch_for_current_device(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    cudaGetLastError();
+    return WALSH_ERR_NOT_INIT;
+  }
+  float* p = g_chmod_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    std::lock_guard<std::mutex> lock(g_chmod_scratch_mu);
+    p = g_chmod_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (!p) {
+      void* addr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&addr, g_chmod_scratch);
+      if (e != cudaSuccess || addr == nullptr) {
+        cudaGetLastError();
+        return WALSH_ERR_NOT_INIT;
+      }
+      p = static_cast<float*>(addr);
+      g_chmod_scratch_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return WALSH_OK;
+}
+
+}  // namespace walsh
+
+// Floats of scratch a call needs: partial [nseg, nchunk, C], scale and shift
+// [nseg, C/32], each sub-buffer rounded up to 256 bytes.
+static int64_t chmod_noalloc_scratch_floats(int64_t nseg, int C, int seg_len) {
+  const int64_t nch = (seg_len + kChunkRows - 1) / kChunkRows;
+  const int64_t E = C / 32;
+  return round_up_floats(nseg * nch * C) + 2 * round_up_floats(nseg * E);
+}
+
+extern "C" walsh_status walsh_chmod_fwd_noalloc(const void* x, int dtype, int64_t nrows, int C, int seg_len,
+                                                const float* norm_w, float norm_eps, const uint8_t* w1_2bit,
+                                                const uint8_t* w2_2bit, const float* gammas,
+                                                const float* scale_temp, float residual_scale, int add_input,
+                                                void* out, void* stream) {
+  if (int e = injected("chmod_fwd_noalloc")) return e;
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_ARG(x && w1_2bit && w2_2bit && gammas && scale_temp && out);
+  WALSH_CHECK_SHAPE(nrows > 0 && C > 0 && C % 32 == 0 && seg_len > 0 && nrows % seg_len == 0);
+  const int64_t nseg = nrows / seg_len;
+  WALSH_CHECK_SHAPE(nseg <= 65535);
+  if (chmod_noalloc_scratch_floats(nseg, C, seg_len) > kNoAllocScratchFloats) return WALSH_ERR_SCRATCH;
+  float* scratch = nullptr;
+  if (walsh_status st = chmod_scratch_for_current_device(&scratch)) return st;
+  const int64_t nch = (seg_len + kChunkRows - 1) / kChunkRows;
+  float* partial = scratch;
+  float* scale = partial + round_up_floats(nseg * nch * C);
+  float* shift = scale + round_up_floats(nseg * (C / 32));
+  if (walsh_status st = walsh_chmod_stats(x, dtype, nrows, C, seg_len, norm_w, norm_eps, partial, stream)) return st;
+  if (walsh_status st = walsh_chmod_mlp(partial, (int)nseg, seg_len, C, w1_2bit, w2_2bit, gammas, scale_temp, scale,
+                                        shift, stream))
+    return st;
+  return walsh_chmod_apply(x, dtype, nrows, C, seg_len, norm_w, norm_eps, scale, shift, residual_scale, add_input,
+                           out, stream);
 }
