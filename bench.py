@@ -42,6 +42,7 @@ ROUTER_SCALE = 18.3
 METRIC = "Walsh-512 prefill tokens/s"
 UNIT = "tokens/s"
 CPU_SAMPLE = (1, 1024)  # oracle sample per step: B1 x T1024
+DECODE_BATCH, DECODE_CTX = 256, 1024
 
 
 def peaks():
@@ -194,7 +195,8 @@ def main():
     ap.add_argument("--impl", default="walsh", choices=["walsh", "reference"])
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", action="store_true",
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode measurement")
+    ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode"],
                     help="run one warm-up and one eager forward only (for ncu launch lists)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -287,8 +289,10 @@ def main():
         # dominant kernel timed alone with CUDA events on the launching stream:
         # prefill attention of one layer (q/k/v of layer 0 recomputed in place)
         roof = dominant_kernel_roofline(model, idx, B, T, dev)
+    del graph, logits_g
+    torch.cuda.empty_cache()
+    decode = None if args.no_decode else measure_decode(model, dev, args.steps, max(3, args.warmup), rank, world, dist)
 
-    del graph
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -307,7 +311,7 @@ def main():
             "config": {"workload": "config 3: Walsh-512 mHC+MoE(16e top-6)+chmod prefill", "global_batch": world * B,
                        "batch_per_gpu": B, "seq_len": T, "parallelism": f"replicas x{world} (batch-sharded)",
                        "l2": "working set > L2 (stream state 268 MB per layer), no flush"},
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(), "decode": decode,
             "gpu_launches": launches_per_forward * args.steps,
             "peaks": src}
     print(json.dumps(line), flush=True)
@@ -319,6 +323,25 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     model = build_model_cpu().to(dev).eval()
     model.compute_dtype = torch.bfloat16
+    if args.profile == "decode":
+        from walsh_research_b200.model import KVCache
+        B, ctx = DECODE_BATCH, DECODE_CTX
+        H, C = CONFIG["n_head"], CONFIG["n_embd"]
+        kv = KVCache(CONFIG["n_layer"], ctx, H, C // H, dev, dtype=torch.float16, batch_size=B)
+        P = ctx - 2
+        with torch.no_grad():
+            model(token_ids(B, P, seed=3).to(dev), kv_cache=kv, start_pos=0)
+            kv.increment(P)
+            ids = token_ids(B, 2, seed=5).to(dev)
+            model(ids[:, :1], kv_cache=kv, start_pos=P)
+            kv.increment(1)
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("walsh_forward")
+            model(ids[:, 1:], kv_cache=kv, start_pos=P + 1)
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.synchronize()
+        print("profile decode step done", flush=True)
+        return
     idx = token_ids(args.batch, SEQ).to(dev)
     with torch.no_grad():
         model(idx)
@@ -328,6 +351,100 @@ def run_profile(args):
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     print("profile forward done", flush=True)
+
+
+def measure_decode(model, dev, steps, warmup, rank=0, world=1, dist=None, B=None, ctx=None):
+    """Steady-state batched decode (Walsh-512, B sequences, KV cache of ctx
+    positions): the cache is prefilled to ctx - (warmup + steps) tokens, then
+    each step appends one token per sequence.  Every position gets its own
+    captured CUDA graph (the cache row and RoPE row are launch arguments), so
+    the timed region replays the graphs of the last `steps` positions back to
+    back.  The KV cache (16 layers x 2 x B x 32 x ctx x 16 fp16 = 8.6 GB at
+    B256 x ctx1024) is far larger than L2.  `e2e` runs the same steps eagerly
+    through the public forward with the token ids copied from pinned host
+    memory and the logits copied back every step."""
+    from walsh_research_b200 import _lib
+    from walsh_research_b200.model import KVCache
+    B = B or DECODE_BATCH
+    ctx = ctx or DECODE_CTX
+    H, C, L = CONFIG["n_head"], CONFIG["n_embd"], CONFIG["n_layer"]
+    n = warmup + steps
+    P = ctx - n
+    kv = KVCache(L, ctx, H, C // H, dev, dtype=torch.float16, batch_size=B)
+    prompt = token_ids(B, P, seed=3 + rank).to(dev)
+    ids_host = token_ids(B, n, seed=5 + rank).pin_memory()
+    ids = ids_host.to(dev)
+    with torch.no_grad():
+        model(prompt, kv_cache=kv, start_pos=0)
+        kv.increment(P)
+        model(ids[:, :1], kv_cache=kv, start_pos=P)      # eager warm-up of the decode path
+        torch.cuda.synchronize()
+        graphs, outs = [], []
+        pool = None
+        n0 = _lib.launch_count
+        for i in range(n):
+            kv.cached_len = P + i
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                lg, _ = model(ids[:, i:i + 1], kv_cache=kv, start_pos=P + i)
+            pool = g.pool()
+            graphs.append(g)
+            outs.append(lg)
+        launches_per_step = (_lib.launch_count - n0) // n
+        kv.cached_len = P
+        for i in range(warmup):
+            graphs[i].replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(warmup, n):
+            graphs[i].replay()
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / steps
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        del graphs, outs
+
+        # eager end to end through the public API
+        logits_host = torch.empty((B, 1, CONFIG["vocab_size"]), dtype=torch.float32).pin_memory()
+        kv.cached_len = P
+        for i in range(warmup):
+            lg, _ = model(ids_host[:, i:i + 1].to(dev, non_blocking=True), kv_cache=kv, start_pos=P + i)
+            logits_host.copy_(lg, non_blocking=True)
+            kv.increment(1)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        start.record()
+        for i in range(warmup, n):
+            lg, _ = model(ids_host[:, i:i + 1].to(dev, non_blocking=True), kv_cache=kv, start_pos=P + i)
+            logits_host.copy_(lg, non_blocking=True)
+            kv.increment(1)
+        end.record()
+        torch.cuda.synchronize()
+        e_ms = start.elapsed_time(end) / steps
+        if dist:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+    del kv
+    torch.cuda.empty_cache()
+    kv_bytes = L * 2 * B * H * ctx * (C // H) * 2
+    return {"metric": "Walsh-512 decode tokens/s", "value": world * B / (ms / 1e3), "unit": UNIT,
+            "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "config": {"workload": f"Walsh-512 batched decode, B{B} per GPU, KV cache ctx {ctx} (positions "
+                                   f"{P + warmup}..{ctx - 1} timed), fp16 KV cache, bf16 stream",
+                       "batch_per_gpu": B, "ctx": ctx, "kv_cache_bytes": kv_bytes,
+                       "l2": "KV cache 8.6 GB > L2, no flush"},
+            "e2e": {"value": world * B / (e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * CONFIG["vocab_size"] * 4},
+            "gpu_launches": launches_per_step * steps}
 
 
 def dominant_kernel_roofline(model, idx, B, T, dev):

@@ -326,6 +326,17 @@ walsh_status walsh_linear_fwd(const void* x, int x_dtype, int64_t M, int K, int6
                               const void* w, int w_dtype, int64_t N, const float* bias, void* y,
                               int y_dtype, void* stream);
 
+/* y[m, n] = sum_k x[m*ldx + k] w[n, k] + bias[n] in float32 on the tensor
+ * cores, with w given as two bfloat16 matrices w_hi + w_lo (w_hi = bf16(w),
+ * w_lo = bf16(w - w_hi)); a float32 x is split the same way, a bfloat16 x is
+ * used as is.  x float32 or bfloat16 (16-byte aligned, ldx*size a multiple of
+ * 16), K a multiple of 32, y float32 [M, N].  Accuracy about 2^-16 relative
+ * per product.  Same role as walsh_linear_fwd for stream_merge and the tied
+ * output projection (src/model/mhc.py:654-676). */
+walsh_status walsh_linear_split_fwd(const void* x, int x_dtype, int64_t M, int K, int64_t ldx,
+                                    const void* w_hi, const void* w_lo, int64_t N, const float* bias,
+                                    float* y, void* stream);
+
 /* Chassis RMSNorm: y = x / sqrt(mean(x^2) + eps) * w over rows of C.
  * Replaces RMSNorm.forward (src/model/chassis.py:96-106). */
 walsh_status walsh_rmsnorm(const void* x, int dtype, int64_t rows, int C, const float* w,

@@ -350,6 +350,14 @@ def test_model_bf16_larger_batch():
     _bf16_model_check("model_h512", idx=idx, cfg_override={"block_size": 256})
 
 
+def test_model_bf16_prefill_sized_batch():
+    """B10 x T1000: enough tokens for the prefill-shaped (tensor-core, 128
+    tokens per CTA) map and MoE kernels and the four-warp q/k/v and output
+    kernels, which smaller batches do not reach."""
+    idx = np.random.default_rng(37).integers(0, 50257, (10, 1000))
+    _bf16_model_check("model_h512", idx=idx, cfg_override={"block_size": 1024})
+
+
 def test_model_autocast_selects_bf16():
     cfg, n, idx, sd, model = build_model("model_h512")
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
@@ -465,6 +473,27 @@ def test_attention_kernel_vs_oracle(hd, Tq, start, ctx, dtype):
     assert rel(o, ref) < tol
 
 
+@pytest.mark.parametrize("hd,Tq,start,ctx", [(16, 1, 1023, 1024), (32, 1, 2047, 2048), (16, 4, 3, 8),
+                                             (16, 3, 500, 600), (32, 1, 0, 1), (32, 2, 130, 200),
+                                             (16, 1, 4000, 4001)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_decode_attention_vs_oracle(hd, Tq, start, ctx, dtype):
+    """The bandwidth decode kernel (Tq <= 4, 16-bit caches): long and short
+    caches, fewer visible keys than key slots, several queries per step."""
+    from walsh_research_b200 import ops
+    rng = np.random.default_rng(hd * 7 + Tq * 131 + start)
+    B, H = 3, 5
+    q = rng.normal(size=(B, H, Tq, hd)).astype(np.float32) * 2
+    k = rng.normal(size=(B, H, ctx, hd)).astype(np.float32)
+    v = rng.normal(size=(B, H, ctx, hd)).astype(np.float32)
+    qt, kt, vt = T(q, dtype), T(k, dtype), T(v, dtype)
+    o = ops.attention(qt, kt, vt, start)
+    ref = _attn_ref(qt.float().cpu().numpy(), kt.float().cpu().numpy(), vt.float().cpu().numpy(), start)
+    # fp32 arithmetic on the rounded inputs; only the output rounding differs
+    tol = 2e-3 if dtype == torch.float16 else 1e-2
+    assert rel(o, ref) < tol
+
+
 @pytest.mark.parametrize("udt", [torch.bfloat16, torch.float16])
 def test_moe_tensor_core_vs_oracle(udt):
     """Tensor-core MoE (router + dense experts) on 3000 tokens with the fused
@@ -524,15 +553,18 @@ def test_hadamard_linear_tc_vs_oracle(ntok):
     assert rel(y, ref) < 2e-2
 
 
-def test_qkv_tc_matches_fp32_path():
-    """Tensor-core q/k/v + RoPE + cache write vs the fp32 kernel on the same inputs."""
+@pytest.mark.parametrize("B,Tn,ctx,start", [(2, 45, 80, 20), (10, 1000, 1100, 20)])
+def test_qkv_tc_matches_fp32_path(B, Tn, ctx, start):
+    """Tensor-core q/k/v + RoPE + cache write vs the fp32 kernel on the same
+    inputs, at a decode-sized token count (one warp and one projection per CTA)
+    and a prefill-sized one (four warps, all projections per CTA)."""
     from walsh_research_b200 import ops
     from walsh_research_b200.model.chassis import precompute_freqs_cis
     rng = np.random.default_rng(7)
     layers = [_rand_hlin(rng) for _ in range(3)]
-    B, Tn, H, hd, ctx, start = 2, 45, 32, 16, 80, 20
+    H, hd = 32, 16
     u = rng.normal(size=(B, Tn, 512)).astype(np.float32)
-    f = precompute_freqs_cis(hd, 160)
+    f = precompute_freqs_cis(hd, ctx + 80)
     cos = f.real[start:start + Tn].float().contiguous().to(DEV)
     sin = f.imag[start:start + Tn].float().contiguous().to(DEV)
     outs = {}
@@ -556,12 +588,12 @@ def test_qkv_tc_matches_fp32_path():
 
 
 @pytest.mark.parametrize("mix", [True, False])
-def test_attn_out_tc_matches_composition(mix):
+@pytest.mark.parametrize("ntok", [300, 10000])
+def test_attn_out_tc_matches_composition(mix, ntok):
     """head mixer + wo + site epilogue (one kernel) vs the three fp32 ops."""
     from walsh_research_b200 import ops
     from walsh_research_b200.model.fht_cuda import HadamardHeadMixerFused
     rng = np.random.default_rng(11)
-    ntok = 300
     wo = _rand_hlin(rng)
     hm = HadamardHeadMixerFused(16)
     with torch.no_grad():
@@ -580,3 +612,25 @@ def test_attn_out_tc_matches_composition(mix):
     f = wo(of)
     ref = ops.mhc_post(xs.float(), f, hmix)
     assert rel(out, ref.cpu().numpy()) < 2e-2
+
+
+@pytest.mark.parametrize("M,K,N,strided", [(1, 512, 1031, False), (70, 2048, 512, True), (256, 512, 4099, False),
+                                           (129, 64, 200, True)])
+@pytest.mark.parametrize("xdt", [torch.float32, torch.bfloat16])
+def test_linear_split_vs_float64(M, K, N, strided, xdt):
+    """Split-bf16 tensor-core linear (stream_merge / logits) at float32 accuracy."""
+    from walsh_research_b200 import ops
+    rng = np.random.default_rng(M * 7 + K + N)
+    ld = K * 3 if strided else K
+    xs = rng.normal(size=(M, ld)).astype(np.float32) * 3
+    w = (rng.normal(size=(N, K)) * 0.02).astype(np.float32)
+    b = rng.normal(size=(N,)).astype(np.float32)
+    xt = T(xs, xdt)
+    hi, lo = ops.split_bf16(T(w))
+    if strided:
+        y = ops.linear_split(xt, hi, lo, T(b), ldx=ld, M=M)
+    else:
+        y = ops.linear_split(xt, hi, lo, T(b))
+    xr = xt.float().cpu().numpy().astype(np.float64)[:, :K]
+    ref = xr @ w.astype(np.float64).T + b
+    assert rel(y, ref) < 3e-5

@@ -46,6 +46,7 @@ SIGNATURES = {
     "walsh_chmod_fwd_noalloc": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, P, P, c_float, c_int, P, P],
     "walsh_embed_gather": [P, c_int64, P, c_int, c_int64, c_int, P, P, P],
     "walsh_linear_fwd": [P, c_int, c_int64, c_int, c_int64, P, c_int, c_int64, P, P, c_int, P],
+    "walsh_linear_split_fwd": [P, c_int, c_int64, c_int, c_int64, P, P, c_int64, P, P, P],
     "walsh_rmsnorm": [P, c_int, c_int64, c_int, P, c_float, P, c_int, P],
 }
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p}

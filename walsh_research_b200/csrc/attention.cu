@@ -139,6 +139,119 @@ attn_decode_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* _
 }
 
 // ---------------------------------------------------------------------------
+// Decode attention for 16-bit caches (the batched decode step: one or a few
+// new queries against a long cache).  Pure KV streaming, so the kernel is
+// built for HBM bandwidth: CTA = one query of one (batch, head); LPK = HD/8
+// lanes share one key row, each lane loading one 16-byte vector of K and of
+// V, so a warp-wide load covers 32/LPK whole rows (512 contiguous bytes);
+// every thread issues the loads of KPT keys before using any of them; an
+// online softmax (exp2 domain) runs per chunk of KPT keys; the per-thread
+// (max, sum, acc) triples are merged across lanes with shuffles and across
+// warps through shared memory.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void merge_parts(float& m, float& l, float* acc, float m2, float l2, const float* acc2) {
+  const float mn = fmaxf(m, m2);
+  const float f1 = mn == -CUDART_INF_F ? 0.f : ex2_f32(m - mn);
+  const float f2 = mn == -CUDART_INF_F ? 0.f : ex2_f32(m2 - mn);
+  l = l * f1 + l2 * f2;
+#pragma unroll
+  for (int d = 0; d < 8; ++d) acc[d] = acc[d] * f1 + acc2[d] * f2;
+  m = mn;
+}
+
+template <int HD, typename T>
+__global__ void __launch_bounds__(128)
+attn_decode_vec_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, int H, int Tq,
+                       int ctx, int start_pos, float scale_log2, T* __restrict__ o) {
+  constexpr int NT = 128, NW = NT / 32, LPK = HD / 8, KPT = 8;
+  constexpr int SLOTS = NT / LPK;  // keys in flight per load step of the CTA
+  __shared__ float red[NW][LPK][10];
+  const int b = blockIdx.z, h = blockIdx.y, t = blockIdx.x;
+  const size_t bh = (size_t)b * H + h;
+  const int nk = start_pos + t + 1;  // keys visible to this query
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int sub = lane % LPK, slot = tid / LPK;
+  float qv[8];
+  load8(q + (bh * Tq + t) * HD + sub * 8, qv);
+#pragma unroll
+  for (int d = 0; d < 8; ++d) qv[d] *= scale_log2;
+  const uint4* kb = reinterpret_cast<const uint4*>(kc + bh * (size_t)ctx * HD) + sub;
+  const uint4* vb = reinterpret_cast<const uint4*>(vc + bh * (size_t)ctx * HD) + sub;
+  float m = -CUDART_INF_F, l = 0.f, acc[8];
+#pragma unroll
+  for (int d = 0; d < 8; ++d) acc[d] = 0.f;
+  // the trip count is the same for every thread (the dot shuffles need the whole warp)
+  for (int c0 = 0; c0 < nk; c0 += SLOTS * KPT) {
+    const int k0 = c0 + slot;
+    uint4 kr[KPT], vr[KPT];
+#pragma unroll
+    for (int i = 0; i < KPT; ++i) {
+      const int k = k0 + i * SLOTS;
+      if (k < nk) {
+        kr[i] = __ldg(kb + (size_t)k * LPK);
+        vr[i] = __ldg(vb + (size_t)k * LPK);
+      } else {
+        kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    float s[KPT];
+    float cm = -CUDART_INF_F;
+#pragma unroll
+    for (int i = 0; i < KPT; ++i) {
+      float kv[8];
+      unpack8(kr[i], kv, (const T*)nullptr);
+      float dot = 0.f;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) dot = fmaf(qv[d], kv[d], dot);
+#pragma unroll
+      for (int off = 1; off < LPK; off <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      s[i] = (k0 + i * SLOTS < nk) ? dot : -CUDART_INF_F;
+      cm = fmaxf(cm, s[i]);
+    }
+    const float mn = fmaxf(m, cm);  // -inf only while this thread has seen no visible key
+    const float corr = mn == -CUDART_INF_F ? 1.f : ex2_f32(m - mn);
+    const float sub_m = mn == -CUDART_INF_F ? 0.f : mn;
+    l *= corr;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) acc[d] *= corr;
+#pragma unroll
+    for (int i = 0; i < KPT; ++i) {
+      const float p = ex2_f32(s[i] - sub_m);  // masked keys: 2^-inf = 0
+      float vv[8];
+      unpack8(vr[i], vv, (const T*)nullptr);
+      l += p;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) acc[d] = fmaf(p, vv[d], acc[d]);
+    }
+    m = mn;
+  }
+  // lanes of the same channel group hold disjoint key sets: merge them
+#pragma unroll
+  for (int off = LPK; off < 32; off <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, off), l2 = __shfl_xor_sync(0xffffffffu, l, off);
+    float a2[8];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) a2[d] = __shfl_xor_sync(0xffffffffu, acc[d], off);
+    merge_parts(m, l, acc, m2, l2, a2);
+  }
+  if (lane < LPK) {
+    red[warp][sub][0] = m;
+    red[warp][sub][1] = l;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) red[warp][sub][2 + d] = acc[d];
+  }
+  __syncthreads();
+  if (tid < LPK) {
+#pragma unroll
+    for (int w = 1; w < NW; ++w) merge_parts(m, l, acc, red[w][sub][0], red[w][sub][1], &red[w][sub][2]);
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) acc[d] *= inv;
+    store8(o + (((size_t)b * Tq + t) * H + h) * HD + sub * 8, acc);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // bf16 prefill on the tensor cores (flash-attention dataflow with mma.sync):
 // CTA = 128 queries of one (batch, head), 8 warps x 16 query rows; K/V tiles
 // of 64 keys double-buffered in shared memory by cp.async; S = Q K^T and
@@ -329,6 +442,14 @@ static int launch_attn(const void* q, const void* kc, const void* vc, int B, int
       dim3 grid((Tq + 127) / 128, H, B);
       attn_mma_kernel<HD, T, 64><<<grid, 256, 0, s>>>((const T*)q, (const T*)kc, (const T*)vc, H, Tq, ctx,
                                                        start_pos, scale_log2, (T*)o);
+      return launch_status();
+    }
+  }
+  if constexpr (sizeof(T) == 2) {
+    if (Tq <= 4 && aligned && (((uintptr_t)o) & 15u) == 0) {
+      dim3 grid(Tq, H, B);
+      attn_decode_vec_kernel<HD, T><<<grid, 128, 0, s>>>((const T*)q, (const T*)kc, (const T*)vc, H, Tq, ctx,
+                                                        start_pos, scale_log2, (T*)o);
       return launch_status();
     }
   }

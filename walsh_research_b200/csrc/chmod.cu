@@ -139,49 +139,76 @@ chmod_apply_vec_kernel(const T* x, int64_t nrows, int seg_len, const float* __re
   }
 }
 
-// One CTA per segment.
+// SPB segments per CTA: the packed weights are read once per CTA and every
+// weight is applied to SPB segments' activations (register-blocked); each
+// segment's sums keep the single-segment order, so results do not depend
+// on SPB.
+template <int SPB>
 __global__ void __launch_bounds__(256)
-chmod_mlp_kernel(const float* __restrict__ partial, int nch, int seg_len, int C, const uint8_t* __restrict__ w1,
-                 const uint8_t* __restrict__ w2, const float* __restrict__ gammas,
+chmod_mlp_kernel(const float* __restrict__ partial, int nseg, int nch, int seg_len, int C,
+                 const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2, const float* __restrict__ gammas,
                  const float* __restrict__ scale_temp, float* __restrict__ scale, float* __restrict__ shift) {
   extern __shared__ float4 smem4[];
-  float* bulk = reinterpret_cast<float*>(smem4);  // [C]
-  float* hid = bulk + C;                           // [C/4]
-  const int seg = blockIdx.x;
+  float* bulk = reinterpret_cast<float*>(smem4);  // [SPB][C]
+  float* hid = bulk + SPB * C;                     // [SPB][C/4]
+  const int seg0 = blockIdx.x * SPB;
+  const int ns = min(SPB, nseg - seg0);
   const int HIDN = C / 4, E = C / 32;
-  for (int c = threadIdx.x; c < C; c += 256) {
-    float s = 0.f;
-    for (int k = 0; k < nch; ++k) s += partial[((size_t)seg * nch + k) * C + c];
-    bulk[c] = s / (float)seg_len;
+  for (int i = threadIdx.x; i < SPB * C; i += 256) {
+    const int j = i / C, c = i - j * C;
+    float sum = 0.f;
+    if (j < ns)
+      for (int k = 0; k < nch; ++k) sum += partial[((size_t)(seg0 + j) * nch + k) * C + c];
+    bulk[i] = sum / (float)seg_len;
   }
   __syncthreads();
   const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
   const int kb1 = C / 4;
   for (int j = threadIdx.x; j < HIDN; j += 256) {
     const uint8_t* row = w1 + (size_t)j * kb1;
-    float acc = 0.f;
+    float acc[SPB];
+#pragma unroll
+    for (int z = 0; z < SPB; ++z) acc[z] = 0.f;
     for (int b = 0; b < kb1; ++b) {
       const uint32_t byte = __ldg(row + b);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc = fmaf(tern_val(byte, q), bulk[4 * b + q], acc);
+      for (int q = 0; q < 4; ++q) {
+        const float w = tern_val(byte, q);
+#pragma unroll
+        for (int z = 0; z < SPB; ++z) acc[z] = fmaf(w, bulk[z * C + 4 * b + q], acc[z]);
+      }
     }
-    acc *= g1;
-    hid[j] = acc / (1.0f + expf(-acc));
+#pragma unroll
+    for (int z = 0; z < SPB; ++z) {
+      const float a = acc[z] * g1;
+      hid[z * HIDN + j] = a / (1.0f + expf(-a));
+    }
   }
   __syncthreads();
   const float st = fminf(fmaxf(__ldg(scale_temp), 0.1f), 0.5f);
   const int kb2 = HIDN / 4;
   for (int r = threadIdx.x; r < 2 * E; r += 256) {
     const uint8_t* row = w2 + (size_t)r * kb2;
-    float acc = 0.f;
+    float acc[SPB];
+#pragma unroll
+    for (int z = 0; z < SPB; ++z) acc[z] = 0.f;
     for (int b = 0; b < kb2; ++b) {
       const uint32_t byte = __ldg(row + b);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc = fmaf(tern_val(byte, q), hid[4 * b + q], acc);
+      for (int q = 0; q < 4; ++q) {
+        const float w = tern_val(byte, q);
+#pragma unroll
+        for (int z = 0; z < SPB; ++z) acc[z] = fmaf(w, hid[z * HIDN + 4 * b + q], acc[z]);
+      }
     }
-    acc *= g2;
-    if (r < E) scale[(size_t)seg * E + r] = 1.0f + st * tanhf(acc);
-    else shift[(size_t)seg * E + (r - E)] = acc;
+#pragma unroll
+    for (int z = 0; z < SPB; ++z) {
+      if (z >= ns) break;
+      const float a = acc[z] * g2;
+      const size_t seg = (size_t)(seg0 + z);
+      if (r < E) scale[seg * E + r] = 1.0f + st * tanhf(a);
+      else shift[seg * E + (r - E)] = a;
+    }
   }
 }
 
@@ -252,10 +279,26 @@ extern "C" walsh_status walsh_chmod_mlp(const float* partial, int nseg, int seg_
   WALSH_CHECK_ARG(partial && w1_2bit && w2_2bit && gammas && scale_temp && scale && shift);
   WALSH_CHECK_SHAPE(nseg > 0 && seg_len > 0 && C > 0 && C % 32 == 0);
   const int nch = (seg_len + kChunkRows - 1) / kChunkRows;
-  const size_t smem = (size_t)(C + C / 4) * sizeof(float);
-  chmod_mlp_kernel<<<nseg, 256, smem, (cudaStream_t)stream>>>(partial, nch, seg_len, C, w1_2bit, w2_2bit, gammas,
-                                                             scale_temp, scale, shift);
-  return launch_status();
+  cudaStream_t s = (cudaStream_t)stream;
+  // segments per CTA: enough CTAs to fill the SMs, weights shared beyond that
+  const int spb = nseg >= 148 * 8 ? 8 : nseg >= 148 * 4 ? 4 : nseg >= 148 * 2 ? 2 : 1;
+  const size_t smem = (size_t)spb * (C + C / 4) * sizeof(float);
+  const unsigned grid = (unsigned)((nseg + spb - 1) / spb);
+  auto go = [&](auto kernel) -> int {
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return launch_status();
+    kernel<<<grid, 256, smem, s>>>(partial, nseg, nch, seg_len, C, w1_2bit, w2_2bit, gammas, scale_temp, scale,
+                                   shift);
+    return launch_status();
+  };
+  if (smem > 200 * 1024) return WALSH_ERR_SHAPE;
+  switch (spb) {
+    case 8: return go(chmod_mlp_kernel<8>);
+    case 4: return go(chmod_mlp_kernel<4>);
+    case 2: return go(chmod_mlp_kernel<2>);
+    default: return go(chmod_mlp_kernel<1>);
+  }
 }
 
 extern "C" walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrows, int C, int seg_len,

@@ -49,6 +49,21 @@ __device__ __forceinline__ void load8_16(const T16* p, float* v) {
     v[2 * i + 1] = to_f(hi);
   }
 }
+// 8 16-bit values already in registers (a 16-byte vector) to float; the
+// pointer argument only selects the element type.
+template <typename T16>
+__device__ __forceinline__ void unpack8(const uint4 q, float* v, const T16*) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    T16 lo, hi;
+    const uint16_t l = (uint16_t)(w[i] & 0xffffu), h = (uint16_t)(w[i] >> 16);
+    memcpy(&lo, &l, 2);
+    memcpy(&hi, &h, 2);
+    v[2 * i] = to_f(lo);
+    v[2 * i + 1] = to_f(hi);
+  }
+}
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) { load8_16(p, v); }
 __device__ __forceinline__ void load8(const __half* p, float* v) { load8_16(p, v); }
 

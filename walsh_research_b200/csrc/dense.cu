@@ -2,6 +2,7 @@
 // y = x W^T + b kernel (stream_merge, tied logits, load-time folding of
 // stream_proj into the embedding table) and the chassis RMSNorm.
 #include "common.cuh"
+#include "mma.cuh"
 
 namespace walsh {
 
@@ -86,6 +87,140 @@ rmsnorm_kernel(const T* x, int64_t rows, int C, const float* __restrict__ w, flo
   }
 }
 
+// ---------------------------------------------------------------------------
+// y = x W^T + b at float32 accuracy on the bf16 tensor cores (stream_merge and
+// the tied logits).  W is held as two bf16 matrices, W = W_hi + W_lo
+// (W_lo = bf16(W - W_hi)), which together carry 16 significant bits with
+// float32's exponent range; a float32 x is split the same way in registers.
+// Each product accumulates x_hi W_hi + x_hi W_lo + x_lo W_hi in float32
+// (x_lo W_lo, below 2^-16 relative, is dropped); a bf16 x is exact in one
+// term.  CTA tile 64 x 128, 8 warps of 32 x 32, K staged 32 wide in a
+// 3-stage cp.async pipeline; zero-filled rows past M and N.
+// ---------------------------------------------------------------------------
+namespace lin_split {
+constexpr int BM = 64, BN = 128, BK = 32, STAGES = 3, LD = BK + 8;
+template <typename Tx>
+constexpr int stage_bytes() { return 2 * BN * LD * 2 + BM * LD * (int)sizeof(Tx); }
+
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16(a, b);
+  const float2 h = unpack2<__nv_bfloat16>(hi);
+  lo = pack_bf16(a - h.x, b - h.y);
+}
+}  // namespace lin_split
+
+template <typename Tx>
+__global__ void __launch_bounds__(256)
+linear_split_kernel(const Tx* __restrict__ x, int64_t M, int K, int64_t ldx, const __nv_bfloat16* __restrict__ whi,
+                    const __nv_bfloat16* __restrict__ wlo, int64_t N, const float* __restrict__ bias,
+                    float* __restrict__ y) {
+  using namespace lin_split;
+  constexpr bool XF = sizeof(Tx) == 4;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int wm = warp & 1, wn = warp >> 1;
+  const int nk = K / BK;
+  auto Wh = [&](int st) { return reinterpret_cast<__nv_bfloat16*>(smem_raw + st * stage_bytes<Tx>()); };
+  auto Wl = [&](int st) { return Wh(st) + BN * LD; };
+  auto Xs = [&](int st) { return reinterpret_cast<Tx*>(smem_raw + st * stage_bytes<Tx>() + 2 * BN * LD * 2); };
+  auto load_stage = [&](int kt, int st) {
+    const int k0 = kt * BK;
+    __nv_bfloat16* wh = Wh(st);
+    __nv_bfloat16* wl = Wl(st);
+    for (int i = tid; i < BN * (BK / 8); i += 256) {
+      const int r = i / (BK / 8), c = (i % (BK / 8)) * 8;
+      const int64_t n = n0 + r;
+      const bool in = n < N;
+      const size_t off = (size_t)(in ? n : 0) * K + k0 + c;
+      cp_async16(wh + r * LD + c, whi + off, in ? 16 : 0);
+      cp_async16(wl + r * LD + c, wlo + off, in ? 16 : 0);
+    }
+    constexpr int XV = 16 / (int)sizeof(Tx);  // elements per 16-byte chunk
+    Tx* xs = Xs(st);
+    for (int i = tid; i < BM * (BK / XV); i += 256) {
+      const int r = i / (BK / XV), c = (i % (BK / XV)) * XV;
+      const int64_t m = m0 + r;
+      const bool in = m < M;
+      cp_async16(xs + r * LD + c, x + (size_t)(in ? m : 0) * ldx + k0 + c, in ? 16 : 0);
+    }
+  };
+#pragma unroll
+  for (int st = 0; st < STAGES - 1; ++st) {
+    if (st < nk) load_stage(st, st);
+    cp_async_commit();
+  }
+  float acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
+  for (int kt = 0; kt < nk; ++kt) {
+    cp_async_wait<STAGES - 2>();
+    __syncthreads();
+    if (kt + STAGES - 1 < nk) load_stage(kt + STAGES - 1, (kt + STAGES - 1) % STAGES);
+    cp_async_commit();
+    const int st = kt % STAGES;
+    const __nv_bfloat16* wh = Wh(st);
+    const __nv_bfloat16* wl = Wl(st);
+    const Tx* xs = Xs(st);
+#pragma unroll
+    for (int kk = 0; kk < BK; kk += 16) {
+      uint32_t ah[2][4], al[2][4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const int r = wm * 32 + mi * 16;
+        if constexpr (XF) {
+          const float* xf = reinterpret_cast<const float*>(xs);
+          const float2 v0 = *reinterpret_cast<const float2*>(xf + (r + g) * LD + kk + 2 * t4);
+          const float2 v1 = *reinterpret_cast<const float2*>(xf + (r + g + 8) * LD + kk + 2 * t4);
+          const float2 v2 = *reinterpret_cast<const float2*>(xf + (r + g) * LD + kk + 8 + 2 * t4);
+          const float2 v3 = *reinterpret_cast<const float2*>(xf + (r + g + 8) * LD + kk + 8 + 2 * t4);
+          split2(v0.x, v0.y, ah[mi][0], al[mi][0]);
+          split2(v1.x, v1.y, ah[mi][1], al[mi][1]);
+          split2(v2.x, v2.y, ah[mi][2], al[mi][2]);
+          split2(v3.x, v3.y, ah[mi][3], al[mi][3]);
+        } else {
+          ldsm_x4(ah[mi], xs + (r + (lane & 15)) * LD + kk + (lane >> 4) * 8);
+        }
+      }
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        const int rn = wn * 32 + np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int cn = kk + ((lane >> 3) & 1) * 8;
+        uint32_t bh[4], bl[4];
+        ldsm_x4(bh, wh + rn * LD + cn);
+        ldsm_x4(bl, wl + rn * LD + cn);
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float* c = acc[mi][2 * np + h];
+            if constexpr (XF) mma_bf16(c, al[mi], bh[2 * h], bh[2 * h + 1]);
+            mma_bf16(c, ah[mi], bl[2 * h], bl[2 * h + 1]);
+            mma_bf16(c, ah[mi], bh[2 * h], bh[2 * h + 1]);
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+      const int64_t n = n0 + wn * 32 + ni * 8 + 2 * t4;
+#pragma unroll
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        const int64_t m = m0 + wm * 32 + mi * 16 + g + hrow * 8;
+        if (m >= M) continue;
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          if (n + e < N) y[m * N + n + e] = acc[mi][ni][hrow * 2 + e] + (bias ? __ldg(bias + n + e) : 0.f);
+      }
+    }
+}
+
 template <typename Tx, typename Tw, typename Ty>
 static int launch_linear(const void* x, int64_t M, int K, int64_t ldx, const void* w, int64_t N, const float* bias,
                          void* y, cudaStream_t s) {
@@ -142,4 +277,32 @@ extern "C" walsh_status walsh_rmsnorm(const void* x, int dtype, int64_t rows, in
   cudaStream_t s = (cudaStream_t)stream;
   return WALSH_DISPATCH_DTYPE(dtype, T, WALSH_DISPATCH_DTYPE(y_dtype, TY,
       (rmsnorm_kernel<T, TY><<<(unsigned)g, 256, 0, s>>>((const T*)x, rows, C, w, eps, (TY*)y), launch_status())));
+}
+
+extern "C" walsh_status walsh_linear_split_fwd(const void* x, int x_dtype, int64_t M, int K, int64_t ldx,
+                                               const void* w_hi, const void* w_lo, int64_t N, const float* bias,
+                                               float* y, void* stream) {
+  using namespace lin_split;
+  if (int e = injected("linear_split_fwd")) return e;
+  WALSH_CHECK_DTYPE(x_dtype);
+  WALSH_CHECK_ARG(x && w_hi && w_lo && y);
+  WALSH_CHECK_SHAPE(M >= 0 && K > 0 && N > 0 && ldx >= K && K % BK == 0);
+  WALSH_CHECK_SHAPE(x_dtype == WALSH_F32 || x_dtype == WALSH_BF16);
+  WALSH_CHECK_SHAPE((N + BN - 1) / BN <= 65535);
+  const int esz = x_dtype == WALSH_F32 ? 4 : 2;
+  if ((((uintptr_t)x) | ((uintptr_t)w_hi) | ((uintptr_t)w_lo)) & 15u) return WALSH_ERR_ALIGN;
+  if ((ldx * esz) % 16) return WALSH_ERR_ALIGN;
+  if (M == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
+  auto go = [&](auto kernel, int smem, auto xp) -> int {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return launch_status();
+    kernel<<<grid, 256, smem, s>>>(xp, M, K, ldx, (const __nv_bfloat16*)w_hi, (const __nv_bfloat16*)w_lo, N, bias,
+                                   y);
+    return launch_status();
+  };
+  if (x_dtype == WALSH_F32)
+    return go(linear_split_kernel<float>, STAGES * stage_bytes<float>(), (const float*)x);
+  return go(linear_split_kernel<__nv_bfloat16>, STAGES * stage_bytes<__nv_bfloat16>(), (const __nv_bfloat16*)x);
 }

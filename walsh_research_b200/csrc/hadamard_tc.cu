@@ -147,7 +147,7 @@ hlin_tc_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __half* 
   extern __shared__ float4 smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __half* tile = reinterpret_cast<__half*>(smem4) + warp * kTcTok * kTcRow;
-  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * kTcTok;
+  const int64_t tok0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * kTcTok;
   uint32_t hb[2][4][2];
   hadamard_bfrags(hb);
   stage_rows(tile, x, tok0, ntok);
@@ -180,11 +180,13 @@ qkv_tc_kernel(const __half* __restrict__ u, int64_t ntok, const __half* __restri
   extern __shared__ float4 smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __half* tile = reinterpret_cast<__half*>(smem4) + warp * kTcTok * kTcRow;
-  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * kTcTok;
+  const int64_t tok0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * kTcTok;
   uint32_t hb[2][4][2];
   hadamard_bfrags(hb);
+  // gridDim.y == 3: one projection per CTA (small token counts); else all three
+  const int set_lo = gridDim.y == 3 ? (int)blockIdx.y : 0, set_hi = gridDim.y == 3 ? set_lo + 1 : 3;
 #pragma unroll 1
-  for (int set = 0; set < 3; ++set) {
+  for (int set = set_lo; set < set_hi; ++set) {
     const float* al = set == 0 ? aq : (set == 1 ? ak : av);
     const float* be = set == 0 ? bq : (set == 1 ? bk : bv);
     const __half* wt = set == 0 ? wq : (set == 1 ? wk : wv);
@@ -250,7 +252,7 @@ attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __r
   extern __shared__ float4 smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __half* tile = reinterpret_cast<__half*>(smem4) + warp * kTcTok * kTcRow;
-  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + warp) * kTcTok;
+  const int64_t tok0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * kTcTok;
   uint32_t hb[2][4][2];
   hadamard_bfrags(hb);
   stage_rows(tile, o, tok0, ntok);
@@ -329,6 +331,10 @@ static inline bool al16(const void* p) { return (((uintptr_t)p) & 15u) == 0; }
 
 using namespace walsh;
 
+// Warps (16 tokens each) per CTA: 4 normally; 1 when the token count would
+// leave most SMs idle (decode steps).
+static int tc_warps_per_cta(int64_t ntok) { return ntok >= 148 * 4 * kTcTok ? 4 : 1; }
+
 extern "C" walsh_status walsh_hadamard_linear_tc_fwd(const void* x, int64_t ntok, const void* w_f16,
                                                      float w_scale, const float* alpha, const float* beta, void* y,
                                                      void* stream) {
@@ -361,12 +367,13 @@ extern "C" walsh_status walsh_attn_qkv_tc_fwd(const void* u, int B, int T, int n
   WALSH_CHECK_ARG(al16(q) && al16(k_cache) && al16(v_cache) && al16(wq_beta) && al16(wk_beta) && al16(wv_beta) &&
                   al16(rope_cos) && al16(rope_sin));
   const int64_t ntok = (int64_t)B * T;
+  const int wpc = tc_warps_per_cta(ntok);
   const int smem = 4 * kTcTok * kTcRow * (int)sizeof(__half);
   TcQkvEpilogue ep{T, n_head, hd, ctx, start_pos, rope_cos, rope_sin};
-  const unsigned grid = (unsigned)((ntok + 63) / 64);
+  const dim3 grid((unsigned)((ntok + wpc * kTcTok - 1) / (wpc * kTcTok)), wpc == 4 ? 1 : 3);
   auto kern = hd == 16 ? qkv_tc_kernel<16> : qkv_tc_kernel<32>;
   if (smem_set((const void*)kern, smem)) return WALSH_ERR_LAUNCH;
-  kern<<<grid, 128, smem, (cudaStream_t)stream>>>(
+  kern<<<grid, 32 * wpc, wpc * kTcTok * kTcRow * sizeof(__half), (cudaStream_t)stream>>>(
       (const __half*)u, ntok, (const __half*)wq_f16, (const __half*)wk_f16, (const __half*)wv_f16, wq_alpha,
       wk_alpha, wv_alpha, wq_beta, wk_beta, wv_beta, (__half*)q, (__half*)k_cache, (__half*)v_cache, ep);
   return launch_status();
@@ -383,10 +390,11 @@ extern "C" walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const
   WALSH_CHECK_ARG(al16(o) && al16(wo_f16) && (!wmix_f16 || al16(wmix_f16)) && al16(x) && al16(x_out) &&
                   al16(wo_beta));
   if (ntok == 0) return WALSH_OK;
+  const int wpc = tc_warps_per_cta(ntok);
   const int smem = 4 * kTcTok * kTcRow * (int)sizeof(__half);
   if (smem_set((const void*)attn_out_tc_kernel, smem)) return WALSH_ERR_LAUNCH;
-  const unsigned grid = (unsigned)((ntok + 63) / 64);
-  attn_out_tc_kernel<<<grid, 128, smem, (cudaStream_t)stream>>>(
+  const unsigned grid = (unsigned)((ntok + wpc * kTcTok - 1) / (wpc * kTcTok));
+  attn_out_tc_kernel<<<grid, 32 * wpc, wpc * kTcTok * kTcRow * sizeof(__half), (cudaStream_t)stream>>>(
       (const __half*)o, ntok, (const __half*)wmix_f16, beta_mix, (const __half*)wo_f16,
       wo_alpha, wo_beta, (const __nv_bfloat16*)x, hmix, (__nv_bfloat16*)x_out);
   return launch_status();

@@ -360,7 +360,10 @@ extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, in
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
   const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_bf16)) & 15u) == 0;
-  if (dtype == WALSH_BF16 && u_dtype != WALSH_F32 && phi_bf16 && vec_ok && (C == 512 || C == 2048)) {
+  // the tensor-core kernel takes 128 tokens per CTA: below about a wave of
+  // those (decode steps), the warp-per-token kernel spreads over more SMs
+  const bool many = ntok >= 148 * 64;
+  if (many && dtype == WALSH_BF16 && u_dtype != WALSH_F32 && phi_bf16 && vec_ok && (C == 512 || C == 2048)) {
     const unsigned grid = (unsigned)((ntok + map_tc::TOK - 1) / map_tc::TOK);
     const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
     const __nv_bfloat16* pb = (const __nv_bfloat16*)phi_bf16;

@@ -248,17 +248,40 @@ class mHCWalsh(nn.Module):
         emb = self.tok_embeddings.weight
         return _prep.cached(self, "emb_f32", [emb], lambda: emb.detach().float().contiguous())
 
+    def head_weights_split(self):
+        """The tied output projection as its bf16 split (w_hi, w_lo)."""
+        emb = self.tok_embeddings.weight
+        return _prep.cached(self, "emb_split", [emb], lambda: ops.split_bf16(emb))
+
+    def merge_weights_split(self):
+        W = self.stream_merge.weight
+        return _prep.cached(self, "merge_split", [W], lambda: ops.split_bf16(W))
+
     def _merge_norm(self, x, rows_last_only: bool):
         B, T, n, C = x.shape
         Wm = self.stream_merge.weight.detach().float().contiguous()
         bm = self.stream_merge.bias.detach().float().contiguous()
+        nw = self.norm.weight.detach().float().contiguous()
         if rows_last_only:
             xl = x[:, T - 1]                                   # [B, n, C] strided view
-            hm = ops.linear(xl, Wm, bm, ldx=T * n * C, M=B)    # [B, C] float32
-            h = ops.rmsnorm(hm, self.norm.weight.detach().float().contiguous(), self.norm.eps, torch.float32)
+            if ops.split_eligible(xl, n * C, ldx=T * n * C):
+                hm = ops.linear_split(xl, *self.merge_weights_split(), bm, ldx=T * n * C, M=B)
+            else:
+                hm = ops.linear(xl, Wm, bm, ldx=T * n * C, M=B)    # [B, C] float32
+            h = ops.rmsnorm(hm, nw, self.norm.eps, torch.float32)
             return h.view(B, 1, C)
-        hm = ops.linear(x.view(B, T, n * C), Wm, bm)
-        return ops.rmsnorm(hm, self.norm.weight.detach().float().contiguous(), self.norm.eps, torch.float32)
+        xf = x.view(B, T, n * C)
+        if ops.split_eligible(xf, n * C):
+            hm = ops.linear_split(xf, *self.merge_weights_split(), bm)
+        else:
+            hm = ops.linear(xf, Wm, bm)
+        return ops.rmsnorm(hm, nw, self.norm.eps, torch.float32)
+
+    def _logits(self, h):
+        """h [M, C] float32 -> logits [M, V] float32 against the tied embedding."""
+        if ops.split_eligible(h, h.shape[-1]):
+            return ops.linear_split(h, *self.head_weights_split())
+        return ops.linear(h, self.head_weights(), None, out_dtype=torch.float32)
 
     def forward(self, idx, targets=None, kv_cache=None, start_pos=0, return_hidden=False):
         if not idx.is_cuda:
@@ -290,13 +313,12 @@ class mHCWalsh(nn.Module):
         self._last_index_error = err
         need_all = return_hidden or targets is not None
         h_out = self._merge_norm(x, rows_last_only=not need_all)
-        emb = self.head_weights()
         if targets is not None:
-            logits = ops.linear(h_out, emb, None, out_dtype=torch.float32)
+            logits = self._logits(h_out.reshape(B * T, C)).view(B, T, -1)
             loss = F.cross_entropy(logits.view(-1, logits.size(-1)), targets.view(-1), ignore_index=-1)
         else:
             last = h_out[:, -1, :] if need_all else h_out[:, 0, :]
-            logits = ops.linear(last.contiguous(), emb, None, out_dtype=torch.float32).view(B, 1, -1)
+            logits = self._logits(last.contiguous()).view(B, 1, -1)
             loss = None
         if return_hidden:
             return logits, loss, h_out

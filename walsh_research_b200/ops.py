@@ -276,6 +276,38 @@ def linear(x, w, bias=None, out_dtype=torch.float32, ldx=None, M=None, out=None)
     return y
 
 
+def split_bf16(w):
+    """(w_hi, w_lo) bfloat16 with w_hi + w_lo = w to about 2^-16 relative."""
+    wf = w.detach().float()
+    hi = wf.to(torch.bfloat16)
+    lo = (wf - hi.float()).to(torch.bfloat16)
+    return hi.contiguous(), lo.contiguous()
+
+
+def split_eligible(x, K, ldx=None) -> bool:
+    esz = x.element_size()
+    ld = K if ldx is None else ldx
+    return (x.dtype in (torch.float32, torch.bfloat16) and K % 32 == 0 and x.data_ptr() % 16 == 0
+            and (ld * esz) % 16 == 0)
+
+
+def linear_split(x, w_hi, w_lo, bias=None, ldx=None, M=None, out=None):
+    """y = x W^T + b (float32) with W given as its bf16 split (see split_bf16)."""
+    require_cuda(x, w_hi, w_lo)
+    N, K = w_hi.shape
+    if ldx is None:
+        x = _c(x)
+        ldx = K
+        M = x.numel() // K
+        lead = x.shape[:-1]
+    else:
+        lead = (M,)
+    y = out if out is not None else torch.empty(lead + (N,), dtype=torch.float32, device=x.device)
+    call("walsh_linear_split_fwd", ptr(x), dcode(x.dtype), M, K, ldx, ptr(w_hi), ptr(w_lo), N,
+         ptr(None if bias is None else _c(bias.float())), ptr(y), stream())
+    return y
+
+
 def rmsnorm(x, w, eps=1e-6, out_dtype=None):
     require_cuda(x)
     x = _c(x)
