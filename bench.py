@@ -307,7 +307,7 @@ def main():
     hbm, tflops, src = peaks()
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f16 operands, f32 accumulate (16-bit mode)", "data": "synthetic",
             "config": {"workload": "config 3: Walsh-512 mHC+MoE(16e top-6)+chmod prefill", "global_batch": world * B,
                        "batch_per_gpu": B, "seq_len": T, "parallelism": f"replicas x{world} (batch-sharded)",
                        "l2": "working set > L2 (stream state 268 MB per layer), no flush"},

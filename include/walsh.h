@@ -156,7 +156,8 @@ walsh_status walsh_attn_qkv_tc_fwd(const void* u, int B, int T, int n_head, cons
                                    void* stream);
 
 /* walsh_attn_out_tc_fwd: for the fp16 attention output o [ntok, 512]
- * (token-major, 32 heads x 16) and a bf16 residual stream x: optional Hadamard head mixing (wmix_f16 = W^T per head,
+ * (token-major, 32 heads x 16) and a 16-bit residual stream x (x_dtype
+ * WALSH_BF16 or WALSH_F16): optional Hadamard head mixing (wmix_f16 = W^T per head,
  * beta_mix [16]; NULL skips it), the wo HadamardLinear, and the mHC site
  * epilogue x_out = H_res x + H_post f (x, x_out [ntok, 4, 512], may alias;
  * hmix as walsh_mhc_map).  Replaces CausalSelfAttention.forward lines
@@ -165,7 +166,7 @@ walsh_status walsh_attn_qkv_tc_fwd(const void* u, int B, int T, int n_head, cons
 walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const void* wmix_f16,
                                    const float* beta_mix, const void* wo_f16,
                                    const float* wo_alpha, const float* wo_beta, const void* x,
-                                   const float* hmix, void* x_out, void* stream);
+                                   int x_dtype, const float* hmix, void* x_out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * mHC residual streams (n_streams = 4)
@@ -180,15 +181,16 @@ walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const void* wmix
  *   u = sum_j H_pre[j] x_j, then (if norm_w != NULL) the chassis RMSNorm
  *   u / sqrt(mean(u^2) + norm_eps) * norm_w.
  * mparams: float [28] = {a_pre, a_post, a_res, unused, b_pre[4], b_post[4],
- * b_res[16]}.  phi_bf16 (optional, may be NULL): a bfloat16 copy of phi; with
- * bf16 x it selects the tensor-core kernel (C = 512 or 2048).  u is written
- * in u_dtype (the model's bf16 mode writes fp16).  Writes u [ntok, C] and hmix float [ntok, 24] =
+ * b_res[16]}.  phi_lp (optional, may be NULL): a copy of phi in x's 16-bit
+ * type (bfloat16 for bf16 x, float16 for fp16 x); with it, a 16-bit x selects
+ * the tensor-core kernel (C = 512 or 2048).  u is written in u_dtype (the
+ * model's 16-bit mode writes fp16).  Writes u [ntok, C] and hmix float [ntok, 24] =
  * {H_pre[4], H_post[4], H_res[16] row-major}.
  * Replaces ResidualStreamMapping.forward x3 and the pre-mix of
  * mHCResidualStream.forward (src/model/mhc.py:283-318, 345-364) plus the
  * attention_norm / ffn_norm RMSNorm of mHCLlamaBlock (src/model/mhc.py:514-523). */
 walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
-                           const void* phi_bf16, const float* mparams, float map_eps,
+                           const void* phi_lp, const float* mparams, float map_eps,
                            const float* norm_w, float norm_eps, void* u, int u_dtype, float* hmix,
                            void* stream);
 
@@ -249,6 +251,56 @@ walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int to
                            void* x_out, const float* weights_in, uint8_t* mask_out,
                            float* probs_out, float* weights_out, const walsh_moe_tc_weights* tc,
                            void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Octonion (Cayley-Dickson) layers as tensor-core GEMMs
+ *
+ * w_hi [N, K] is the dense signed expansion of an OctonionTernaryLinear's
+ * eight ternary blocks: w[(i, o), (j, k)] = SIGN[i][j] Wq[WIDX[i][j]][o][k]
+ * (src/model/constants.py:15-52), exact in fp16/bf16.  w_dtype must be
+ * WALSH_F16 for fp16 x and WALSH_BF16 for bf16 or float32 x; w_lo (optional,
+ * float32 x only) is a bf16 correction w - w_hi for non-ternary matrices
+ * (the folded head mixer).  float32 x is split into bf16 hi + lo in the
+ * kernel (float32 accuracy).  scale[n] multiplies output column n (beta of
+ * the output part).  K a multiple of 8, N even, x/w 16-byte aligned.
+ * ------------------------------------------------------------------------- */
+
+/* y = scale . (x w^T), y in x's dtype [M, N].
+ * Replaces OctonionTernaryLinearRef.forward / OctonionFusedLinear.forward
+ * (src/model/physics.py:66-82, src/model/cayley_dickson_cuda.py:654-668). */
+walsh_status walsh_octo_linear_fwd(const void* x, int dtype, int64_t M, int K, const void* w_hi,
+                                   const void* w_lo, int w_dtype, int64_t N, const float* scale,
+                                   void* y, void* stream);
+
+/* q/k/v in one GEMM: w [3C, C] = wq | wk | wv rows, scale [3C]; RoPE
+ * (interleaved pairs, rope_cos/sin [>= T, hd/2] rows of the tokens' own
+ * positions) on q and k; q -> [B, H, T, hd], k/v -> caches [B, H, ctx, hd] at
+ * rows start_pos..; outputs in u's dtype.
+ * Replaces CausalSelfAttention.forward lines 424-447 for the octonion algebra
+ * (src/model/chassis.py:424-447, apply_rotary_emb :339-345). */
+walsh_status walsh_octo_qkv_fwd(const void* u, int dtype, int B, int T, int C, int n_head,
+                                const void* w_hi, const void* w_lo, int w_dtype, const float* scale,
+                                const float* rope_cos, const float* rope_sin, int n_pos, int start_pos,
+                                void* q, void* k_cache, void* v_cache, int ctx, void* stream);
+
+/* h = silu(g) * v with g, v the gate/up outputs: w [2 hidden, K] holds the
+ * gate and up rows interleaved (row 2j = gate unit j, row 2j+1 = up unit j),
+ * scale interleaved the same way; h [M, hidden] in u's dtype.
+ * Replaces SwiGLUMLP.forward up to down_proj (src/model/chassis.py:497-505). */
+walsh_status walsh_octo_swiglu_fwd(const void* u, int dtype, int64_t M, int K, const void* w_hi,
+                                   const void* w_lo, int w_dtype, const float* scale, int64_t hidden,
+                                   void* h, void* stream);
+
+/* f = scale . (a w^T) [M, C] followed by the mHC site epilogue
+ * x_out[m, i] = sum_j H_res[i][j] x[m, j] + H_post[i] f[m] (x, x_out
+ * [M, 4, C] float32 or bfloat16, may alias; hmix as for walsh_mhc_post).
+ * Used for wo (with the octonion head mixer folded into w) and down_proj.
+ * Replaces SwiGLUMLP down_proj / wo followed by mHCResidualStream's output
+ * mixing (src/model/chassis.py:476-483, 505-507; src/model/mhc.py:376-381). */
+walsh_status walsh_octo_post_fwd(const void* a, int dtype, int64_t M, int K, const void* w_hi,
+                                 const void* w_lo, int w_dtype, const float* scale, int C,
+                                 const void* x, int x_dtype, const float* hmix, void* x_out,
+                                 void* stream);
 
 /* ---------------------------------------------------------------------------
  * Channel modulation (x viewed as [nseg, seg_len, C], segment = seg_len
@@ -328,9 +380,9 @@ walsh_status walsh_linear_fwd(const void* x, int x_dtype, int64_t M, int K, int6
 
 /* y[m, n] = sum_k x[m*ldx + k] w[n, k] + bias[n] in float32 on the tensor
  * cores, with w given as two bfloat16 matrices w_hi + w_lo (w_hi = bf16(w),
- * w_lo = bf16(w - w_hi)); a float32 x is split the same way, a bfloat16 x is
- * used as is.  x float32 or bfloat16 (16-byte aligned, ldx*size a multiple of
- * 16), K a multiple of 32, y float32 [M, N].  Accuracy about 2^-16 relative
+ * w_lo = bf16(w - w_hi)); a float32 or float16 x is split the same way, a
+ * bfloat16 x is used as is.  x 16-byte aligned with ldx*size a multiple of
+ * 16, K a multiple of 32, y float32 [M, N].  Accuracy about 2^-16 relative
  * per product.  Same role as walsh_linear_fwd for stream_merge and the tied
  * output projection (src/model/mhc.py:654-676). */
 walsh_status walsh_linear_split_fwd(const void* x, int x_dtype, int64_t M, int K, int64_t ldx,

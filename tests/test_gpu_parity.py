@@ -163,6 +163,40 @@ def test_stream_mapping():
         assert rel(h, g[kind]) < 1e-5, kind
 
 
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
+def test_tensor_core_mapping_vs_oracle(xdt):
+    """The tensor-core site prologue (chosen from 9472 tokens up) for either
+    16-bit stream type: H_pre/H_post/H_res vs the oracle on the same rounded
+    stream values, and the pre-mixed, normed u."""
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model.mhc import MAP_EPS, ResidualStreamMapping, mHCResidualStream, site_params
+    rng = np.random.default_rng(41)
+    st = mHCResidualStream(512, 4)
+    with torch.no_grad():
+        for m in (st.H_pre, st.H_post, st.H_res):
+            m.phi.weight.copy_(torch.from_numpy(rng.normal(0, 0.02, tuple(m.phi.weight.shape)).astype(np.float32)))
+            m.alpha.fill_(0.7)
+            m.bias.copy_(torch.from_numpy(rng.normal(0, 0.5, tuple(m.bias.shape)).astype(np.float32)))
+    st = st.to(DEV)
+    ntok = 10000
+    x = T(rng.normal(size=(ntok, 4, 512)).astype(np.float32) * 3, xdt)
+    nw = T((1 + 0.1 * rng.normal(size=512)).astype(np.float32))
+    phi, mp, phil = site_params(st, xdt)
+    u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, nw, 1e-6, phi_lp=phil, u_dtype=torch.float16)
+    xf = x.float().cpu().numpy().astype(np.float64).reshape(1, ntok, 4 * 512)
+    p = {k: v.detach().cpu().numpy() for k, v in st.state_dict().items()}
+    hp = O.stream_mapping(xf, p["H_pre.phi.weight"], p["H_pre.alpha"], p["H_pre.bias"], "pre")
+    ho = O.stream_mapping(xf, p["H_post.phi.weight"], p["H_post.alpha"], p["H_post.bias"], "post")
+    hr = O.stream_mapping(xf, p["H_res.phi.weight"], p["H_res.alpha"], p["H_res.bias"], "res")
+    h = hmix.cpu().numpy()
+    assert np.abs(h[:, :4] - hp.reshape(ntok, 4)).max() < 5e-3
+    assert np.abs(h[:, 4:8] - ho.reshape(ntok, 4)).max() < 1e-2
+    assert np.abs(h[:, 8:] - hr.reshape(ntok, 16)).max() < 5e-3
+    pre = (h[:, None, :4] @ x.float().cpu().numpy().astype(np.float64))[:, 0]
+    ref_u = O.rmsnorm(pre, nw.cpu().numpy().astype(np.float64))
+    assert rel(u, ref_u) < 5e-3
+
+
 def test_residual_stream_site_matches_oracle():
     """map (with norm) + an identity layer + post against the oracle."""
     from walsh_research_b200 import ops

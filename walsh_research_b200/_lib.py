@@ -33,12 +33,17 @@ SIGNATURES = {
     "walsh_hadamard_linear_tc_fwd": [P, c_int64, P, c_float, P, P, P, P],
     "walsh_attn_qkv_tc_fwd": [P, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_int, c_int, P, P, P,
                               c_int, P],
-    "walsh_attn_out_tc_fwd": [P, c_int64, P, P, P, P, P, P, P, P, P],
+    "walsh_attn_out_tc_fwd": [P, c_int64, P, P, P, P, P, P, c_int, P, P, P],
     "walsh_mhc_map": [P, c_int, c_int64, c_int, P, P, P, c_float, P, c_float, P, c_int, P, P],
     "walsh_mhc_post": [P, P, P, c_int, c_int64, c_int, P, P],
     "walsh_sinkhorn": [P, c_int64, c_int, c_float, P, P],
     "walsh_moe_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, P, c_int, P, c_int, P, P, P, P, P, P, P,
                       P],
+    "walsh_octo_linear_fwd": [P, c_int, c_int64, c_int, P, P, c_int, c_int64, P, P, P],
+    "walsh_octo_qkv_fwd": [P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int, P, P, P, c_int,
+                           P],
+    "walsh_octo_swiglu_fwd": [P, c_int, c_int64, c_int, P, P, c_int, P, c_int64, P, P],
+    "walsh_octo_post_fwd": [P, c_int, c_int64, c_int, P, P, c_int, P, c_int, P, c_int, P, P, P],
     "walsh_chmod_chunk_rows": [c_int],
     "walsh_chmod_stats": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P],
     "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],
@@ -126,10 +131,10 @@ def dcode(dtype: torch.dtype) -> int:
 
 def inner_dtype(stream_dtype: torch.dtype) -> torch.dtype:
     """Storage type of the normalised activations (u, q/k/v, attention output)
-    for a residual stream of ``stream_dtype``: float16 next to a bfloat16
+    for a residual stream of ``stream_dtype``: float16 next to a 16-bit
     stream (values are bounded by the normalisations, fp16 keeps 3 more
-    mantissa bits), float32 next to a float32 stream."""
-    return torch.float16 if stream_dtype == torch.bfloat16 else stream_dtype
+    mantissa bits than bf16), float32 next to a float32 stream."""
+    return torch.float16 if stream_dtype in (torch.bfloat16, torch.float16) else stream_dtype
 
 
 def stream() -> int:

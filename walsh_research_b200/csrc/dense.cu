@@ -1,6 +1,8 @@
 // Dense helpers around the layer stack: embedding gather, a tiled
 // y = x W^T + b kernel (stream_merge, tied logits, load-time folding of
 // stream_proj into the embedding table) and the chassis RMSNorm.
+#include <type_traits>
+
 #include "common.cuh"
 #include "mma.cuh"
 
@@ -115,7 +117,7 @@ linear_split_kernel(const Tx* __restrict__ x, int64_t M, int K, int64_t ldx, con
                     const __nv_bfloat16* __restrict__ wlo, int64_t N, const float* __restrict__ bias,
                     float* __restrict__ y) {
   using namespace lin_split;
-  constexpr bool XF = sizeof(Tx) == 4;
+  constexpr bool XF = !std::is_same<Tx, __nv_bfloat16>::value;  // float or fp16 x: split into bf16 hi + lo
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
@@ -171,11 +173,16 @@ linear_split_kernel(const Tx* __restrict__ x, int64_t M, int K, int64_t ldx, con
       for (int mi = 0; mi < 2; ++mi) {
         const int r = wm * 32 + mi * 16;
         if constexpr (XF) {
-          const float* xf = reinterpret_cast<const float*>(xs);
-          const float2 v0 = *reinterpret_cast<const float2*>(xf + (r + g) * LD + kk + 2 * t4);
-          const float2 v1 = *reinterpret_cast<const float2*>(xf + (r + g + 8) * LD + kk + 2 * t4);
-          const float2 v2 = *reinterpret_cast<const float2*>(xf + (r + g) * LD + kk + 8 + 2 * t4);
-          const float2 v3 = *reinterpret_cast<const float2*>(xf + (r + g + 8) * LD + kk + 8 + 2 * t4);
+          auto pair = [&](int idx) -> float2 {
+            if constexpr (std::is_same<Tx, float>::value)
+              return *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(xs) + idx);
+            else
+              return unpack2<__half>(*reinterpret_cast<const uint32_t*>(xs + idx));
+          };
+          const float2 v0 = pair((r + g) * LD + kk + 2 * t4);
+          const float2 v1 = pair((r + g + 8) * LD + kk + 2 * t4);
+          const float2 v2 = pair((r + g) * LD + kk + 8 + 2 * t4);
+          const float2 v3 = pair((r + g + 8) * LD + kk + 8 + 2 * t4);
           split2(v0.x, v0.y, ah[mi][0], al[mi][0]);
           split2(v1.x, v1.y, ah[mi][1], al[mi][1]);
           split2(v2.x, v2.y, ah[mi][2], al[mi][2]);
@@ -287,7 +294,6 @@ extern "C" walsh_status walsh_linear_split_fwd(const void* x, int x_dtype, int64
   WALSH_CHECK_DTYPE(x_dtype);
   WALSH_CHECK_ARG(x && w_hi && w_lo && y);
   WALSH_CHECK_SHAPE(M >= 0 && K > 0 && N > 0 && ldx >= K && K % BK == 0);
-  WALSH_CHECK_SHAPE(x_dtype == WALSH_F32 || x_dtype == WALSH_BF16);
   WALSH_CHECK_SHAPE((N + BN - 1) / BN <= 65535);
   const int esz = x_dtype == WALSH_F32 ? 4 : 2;
   if ((((uintptr_t)x) | ((uintptr_t)w_hi) | ((uintptr_t)w_lo)) & 15u) return WALSH_ERR_ALIGN;
@@ -304,5 +310,7 @@ extern "C" walsh_status walsh_linear_split_fwd(const void* x, int x_dtype, int64
   };
   if (x_dtype == WALSH_F32)
     return go(linear_split_kernel<float>, STAGES * stage_bytes<float>(), (const float*)x);
+  if (x_dtype == WALSH_F16)
+    return go(linear_split_kernel<__half>, STAGES * stage_bytes<__half>(), (const __half*)x);
   return go(linear_split_kernel<__nv_bfloat16>, STAGES * stage_bytes<__nv_bfloat16>(), (const __nv_bfloat16*)x);
 }

@@ -244,11 +244,12 @@ qkv_tc_kernel(const __half* __restrict__ u, int64_t ntok, const __half* __restri
 //   mixer: Y = beta_m[d] . H (W_h) H o / 32; then wo: f = beta_o . H W_o H (alpha_o . Y) / 32
 //   x_out[i] = sum_j H_res[i][j] x[j] + H_post[i] f   (x, x_out [ntok][4][512]; may alias)
 // ---------------------------------------------------------------------------
+template <typename TX>
 __global__ void __launch_bounds__(128)
 attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __restrict__ wmix,
                    const float* __restrict__ beta_mix, const __half* __restrict__ wo,
-                   const float* __restrict__ alpha_o, const float* __restrict__ beta_o, const __nv_bfloat16* x,
-                   const float* __restrict__ hmix, __nv_bfloat16* xo) {
+                   const float* __restrict__ alpha_o, const float* __restrict__ beta_o, const TX* x,
+                   const float* __restrict__ hmix, TX* xo) {
   extern __shared__ float4 smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __half* tile = reinterpret_cast<__half*>(smem4) + warp * kTcTok * kTcRow;
@@ -305,13 +306,13 @@ attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __r
         const float f0 = f.x * bo[pass][2 * q2], f1 = f.y * bo[pass][2 * q2 + 1];
         float2 xf[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xf[j] = unpack2<__nv_bfloat16>((&xq[j].x)[q2]);
+        for (int j = 0; j < 4; ++j) xf[j] = unpack2<TX>((&xq[j].x)[q2]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float* r = hr + 4 * i;
           const float a0 = (((r[0] * xf[0].x + r[1] * xf[1].x) + r[2] * xf[2].x) + r[3] * xf[3].x) + hp[i] * f0;
           const float a1 = (((r[0] * xf[0].y + r[1] * xf[1].y) + r[2] * xf[2].y) + r[3] * xf[3].y) + hp[i] * f1;
-          ow[i][q2] = pack_bf16(a0, a1);
+          ow[i][q2] = pack2<TX>(a0, a1);
         }
       }
 #pragma unroll
@@ -381,21 +382,32 @@ extern "C" walsh_status walsh_attn_qkv_tc_fwd(const void* u, int B, int T, int n
 
 extern "C" walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const void* wmix_f16,
                                               const float* beta_mix, const void* wo_f16, const float* wo_alpha,
-                                              const float* wo_beta, const void* x, const float* hmix, void* x_out,
-                                              void* stream) {
+                                              const float* wo_beta, const void* x, int x_dtype, const float* hmix,
+                                              void* x_out, void* stream) {
   if (int e = injected("attn_out_tc_fwd")) return e;
   WALSH_CHECK_ARG(o && wo_f16 && wo_alpha && wo_beta && x && hmix && x_out);
   WALSH_CHECK_ARG(!wmix_f16 || beta_mix);
   WALSH_CHECK_SHAPE(ntok >= 0);
+  WALSH_CHECK_DTYPE(x_dtype);
+  WALSH_CHECK_SHAPE(x_dtype == WALSH_BF16 || x_dtype == WALSH_F16);
   WALSH_CHECK_ARG(al16(o) && al16(wo_f16) && (!wmix_f16 || al16(wmix_f16)) && al16(x) && al16(x_out) &&
                   al16(wo_beta));
   if (ntok == 0) return WALSH_OK;
   const int wpc = tc_warps_per_cta(ntok);
   const int smem = 4 * kTcTok * kTcRow * (int)sizeof(__half);
-  if (smem_set((const void*)attn_out_tc_kernel, smem)) return WALSH_ERR_LAUNCH;
   const unsigned grid = (unsigned)((ntok + wpc * kTcTok - 1) / (wpc * kTcTok));
-  attn_out_tc_kernel<<<grid, 32 * wpc, wpc * kTcTok * kTcRow * sizeof(__half), (cudaStream_t)stream>>>(
-      (const __half*)o, ntok, (const __half*)wmix_f16, beta_mix, (const __half*)wo_f16,
-      wo_alpha, wo_beta, (const __nv_bfloat16*)x, hmix, (__nv_bfloat16*)x_out);
+  const size_t dsmem = wpc * kTcTok * kTcRow * sizeof(__half);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (x_dtype == WALSH_F16) {
+    if (smem_set((const void*)attn_out_tc_kernel<__half>, smem)) return WALSH_ERR_LAUNCH;
+    attn_out_tc_kernel<__half><<<grid, 32 * wpc, dsmem, s>>>((const __half*)o, ntok, (const __half*)wmix_f16,
+                                                            beta_mix, (const __half*)wo_f16, wo_alpha, wo_beta,
+                                                            (const __half*)x, hmix, (__half*)x_out);
+  } else {
+    if (smem_set((const void*)attn_out_tc_kernel<__nv_bfloat16>, smem)) return WALSH_ERR_LAUNCH;
+    attn_out_tc_kernel<__nv_bfloat16><<<grid, 32 * wpc, dsmem, s>>>(
+        (const __half*)o, ntok, (const __half*)wmix_f16, beta_mix, (const __half*)wo_f16, wo_alpha, wo_beta,
+        (const __nv_bfloat16*)x, hmix, (__nv_bfloat16*)x_out);
+  }
   return launch_status();
 }

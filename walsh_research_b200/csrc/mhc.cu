@@ -169,16 +169,16 @@ constexpr size_t smem_bytes() {
 }
 }  // namespace map_tc
 
-template <int C, typename TU>
+template <int C, typename TU, typename TX>
 __global__ void __launch_bounds__(256)
-mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv_bfloat16* __restrict__ phib,
+mhc_map_mma_kernel(const TX* __restrict__ x, int64_t ntok, const TX* __restrict__ phib,
                    const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
                    TU* __restrict__ u, float* __restrict__ hmix) {
   using namespace map_tc;
   constexpr int D = 4 * C, NCH = D / KC;
   extern __shared__ float4 smem4[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem4);   // [2][TOK][LDX]
-  __nv_bfloat16* ps = xs + 2 * TOK * LDX;                          // [2][24][LDX]
+  TX* xs = reinterpret_cast<TX*>(smem4);   // [2][TOK][LDX]
+  TX* ps = xs + 2 * TOK * LDX;                          // [2][24][LDX]
   float (*ds)[16][kMapRows + 1] = reinterpret_cast<float (*)[16][kMapRows + 1]>(ps + 2 * kMapRows * LDX);
   float (*sss)[16] = reinterpret_cast<float (*)[16]>(reinterpret_cast<float*>(ds) + NW * 16 * (kMapRows + 1));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
@@ -186,13 +186,13 @@ mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv
   const int64_t tok0 = cta0 + warp * 16;
 
   auto load_chunk = [&](int ch, int buf) {
-    __nv_bfloat16* xd = xs + buf * TOK * LDX;
+    TX* xd = xs + buf * TOK * LDX;
     for (int i = tid; i < TOK * (KC / 8); i += 256) {
       const int r = i / (KC / 8), c = i - r * (KC / 8);
       const bool in = cta0 + r < ntok;
       cp_async16(xd + r * LDX + c * 8, x + (in ? (cta0 + r) * D : 0) + ch * KC + c * 8, in ? 16 : 0);
     }
-    __nv_bfloat16* pd = ps + buf * kMapRows * LDX;
+    TX* pd = ps + buf * kMapRows * LDX;
     for (int i = tid; i < kMapRows * (KC / 8); i += 256) {
       const int r = i / (KC / 8), c = i - r * (KC / 8);
       cp_async16(pd + r * LDX + c * 8, phib + (size_t)r * D + ch * KC + c * 8, 16);
@@ -210,8 +210,8 @@ mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const __nv_bfloat16* xw = xs + buf * TOK * LDX + warp * 16 * LDX;
-    const __nv_bfloat16* pw = ps + buf * kMapRows * LDX;
+    const TX* xw = xs + buf * TOK * LDX + warp * 16 * LDX;
+    const TX* pw = ps + buf * kMapRows * LDX;
 #pragma unroll
     for (int ks = 0; ks < KC / 16; ++ks) {
       uint32_t a[4], b01[4], b2[2];
@@ -220,13 +220,13 @@ mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv
       ldsm_x2(b2[0], b2[1], pw + (16 + (lane & 7)) * LDX + ks * 16 + ((lane >> 3) & 1) * 8);
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a[r]));
+        const float2 v = unpack2<TX>(a[r]);
         if (r & 1) ss_hi = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_hi));
         else ss_lo = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_lo));
       }
-      mma_bf16(acc[0], a, b01[0], b01[1]);
-      mma_bf16(acc[1], a, b01[2], b01[3]);
-      mma_bf16(acc[2], a, b2[0], b2[1]);
+      mma16<TX>(acc[0], a, b01[0], b01[1]);
+      mma16<TX>(acc[1], a, b01[2], b01[3]);
+      mma16<TX>(acc[2], a, b2[0], b2[1]);
     }
     __syncthreads();
   }
@@ -267,7 +267,7 @@ mhc_map_mma_kernel(const __nv_bfloat16* __restrict__ x, int64_t ntok, const __nv
     const int64_t tok = tok0 + t;
     if (tok >= ntok) break;
     const float h0 = ds[warp][t][0], h1 = ds[warp][t][1], h2 = ds[warp][t][2], h3 = ds[warp][t][3];
-    const __nv_bfloat16* xt = x + tok * D;
+    const TX* xt = x + tok * D;
     float uv[VPL][8];
     float s2 = 0.f;
 #pragma unroll
@@ -349,7 +349,7 @@ static inline int grid_for(int64_t total, int threads) {
 using namespace walsh;
 
 extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
-                                      const void* phi_bf16, const float* mparams, float map_eps,
+                                      const void* phi_lp, const float* mparams, float map_eps,
                                       const float* norm_w, float norm_eps, void* u, int u_dtype, float* hmix,
                                       void* stream) {
   if (int e = injected("mhc_map")) return e;
@@ -359,25 +359,32 @@ extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, in
   WALSH_CHECK_SHAPE(ntok >= 0 && C > 0 && C % 32 == 0 && C <= 8192);
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_bf16)) & 15u) == 0;
+  const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_lp)) & 15u) == 0;
   // the tensor-core kernel takes 128 tokens per CTA: below about a wave of
   // those (decode steps), the warp-per-token kernel spreads over more SMs
   const bool many = ntok >= 148 * 64;
-  if (many && dtype == WALSH_BF16 && u_dtype != WALSH_F32 && phi_bf16 && vec_ok && (C == 512 || C == 2048)) {
+  if (many && (dtype == WALSH_BF16 || dtype == WALSH_F16) && u_dtype != WALSH_F32 && phi_lp && vec_ok &&
+      (C == 512 || C == 2048)) {
     const unsigned grid = (unsigned)((ntok + map_tc::TOK - 1) / map_tc::TOK);
-    const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
-    const __nv_bfloat16* pb = (const __nv_bfloat16*)phi_bf16;
-#define WALSH_MAP_TC(CC, TU)                                                                                  \
+#define WALSH_MAP_TC(CC, TU, TX)                                                                              \
   {                                                                                                          \
     const int smem = (int)map_tc::smem_bytes<CC>();                                                          \
-    cudaFuncSetAttribute(mhc_map_mma_kernel<CC, TU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);     \
-    mhc_map_mma_kernel<CC, TU><<<grid, 256, smem, s>>>(xb, ntok, pb, mparams, map_eps, norm_w, norm_eps,    \
-                                                      (TU*)u, hmix);                                         \
+    cudaFuncSetAttribute(mhc_map_mma_kernel<CC, TU, TX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    mhc_map_mma_kernel<CC, TU, TX><<<grid, 256, smem, s>>>((const TX*)x, ntok, (const TX*)phi_lp, mparams,   \
+                                                          map_eps, norm_w, norm_eps, (TU*)u, hmix);          \
   }
-    if (C == 512 && u_dtype == WALSH_F16) WALSH_MAP_TC(512, __half)
-    else if (C == 512) WALSH_MAP_TC(512, __nv_bfloat16)
-    else if (u_dtype == WALSH_F16) WALSH_MAP_TC(2048, __half)
-    else WALSH_MAP_TC(2048, __nv_bfloat16)
+    const bool uh = u_dtype == WALSH_F16;
+    if (dtype == WALSH_BF16) {
+      if (C == 512 && uh) WALSH_MAP_TC(512, __half, __nv_bfloat16)
+      else if (C == 512) WALSH_MAP_TC(512, __nv_bfloat16, __nv_bfloat16)
+      else if (uh) WALSH_MAP_TC(2048, __half, __nv_bfloat16)
+      else WALSH_MAP_TC(2048, __nv_bfloat16, __nv_bfloat16)
+    } else {
+      if (C == 512 && uh) WALSH_MAP_TC(512, __half, __half)
+      else if (C == 512) WALSH_MAP_TC(512, __nv_bfloat16, __half)
+      else if (uh) WALSH_MAP_TC(2048, __half, __half)
+      else WALSH_MAP_TC(2048, __nv_bfloat16, __half)
+    }
 #undef WALSH_MAP_TC
     return launch_status();
   }

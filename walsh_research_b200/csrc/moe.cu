@@ -259,12 +259,12 @@ constexpr size_t smem_bytes() {
 }
 }  // namespace moe_tc
 
-template <typename TU>
+template <typename TU, typename TX>
 __global__ void __launch_bounds__(256, 1)
 moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* __restrict__ w1b,
                   const TU* __restrict__ w2b, const TU* __restrict__ gb, const TU* __restrict__ ub,
                   const TU* __restrict__ db, const float* __restrict__ gammas, TU* __restrict__ y, int fuse_post,
-                  const __nv_bfloat16* x, const float* __restrict__ hmix, __nv_bfloat16* xo,
+                  const TX* x, const float* __restrict__ hmix, TX* xo,
                   uint8_t* __restrict__ mask_out, float* __restrict__ probs_out, float* __restrict__ weights_out) {
   using namespace moe_tc;
   extern __shared__ float4 smem4[];
@@ -512,13 +512,13 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
         const float2 yf = unpack2<TU>(yw[q]);
         float2 xf[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xf[j] = unpack2<__nv_bfloat16>((&xq[j].x)[q]);
+        for (int j = 0; j < 4; ++j) xf[j] = unpack2<TX>((&xq[j].x)[q]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float* r = hr + 4 * i;
           const float a0 = (((r[0] * xf[0].x + r[1] * xf[1].x) + r[2] * xf[2].x) + r[3] * xf[3].x) + hp[i] * yf.x;
           const float a1 = (((r[0] * xf[0].y + r[1] * xf[1].y) + r[2] * xf[2].y) + r[3] * xf[3].y) + hp[i] * yf.y;
-          ow[i][q] = pack_bf16(a0, a1);
+          ow[i][q] = pack2<TX>(a0, a1);
         }
       }
 #pragma unroll
@@ -544,18 +544,19 @@ static int launch_moe(const void* u, int64_t ntok, int top_k, const float* w1t, 
   return launch_status();
 }
 
-template <typename TU>
+template <typename TU, typename TX>
 static int launch_moe_mma(const void* u, int64_t ntok, int top_k, const walsh_moe_tc_weights* tc, bool experts,
                           const float* gammas, void* y, int fuse_post, const void* x, const float* hmix, void* xo,
                           uint8_t* mask_out, float* probs_out, float* weights_out, cudaStream_t s) {
   const unsigned grid = (unsigned)((ntok + moe_tc::TOK - 1) / moe_tc::TOK);
   const int smem = (int)moe_tc::smem_bytes<TU>();
-  if (cudaFuncSetAttribute(moe_mma512_kernel<TU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  if (cudaFuncSetAttribute(moe_mma512_kernel<TU, TX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
     return WALSH_ERR_LAUNCH;
-  moe_mma512_kernel<TU><<<grid, 256, smem, s>>>(
+  moe_mma512_kernel<TU, TX><<<grid, 256, smem, s>>>(
       (const TU*)u, ntok, top_k, (const TU*)tc->w1, (const TU*)tc->w2, experts ? (const TU*)tc->gate : nullptr,
-      (const TU*)tc->up, (const TU*)tc->down, gammas, (TU*)y, fuse_post, (const __nv_bfloat16*)x, hmix,
-      (__nv_bfloat16*)xo, mask_out, probs_out, weights_out);
+      (const TU*)tc->up, (const TU*)tc->down, gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo, mask_out,
+      probs_out, weights_out);
   return launch_status();
 }
 
@@ -585,14 +586,20 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype != WALSH_F32 && C == 512 && tc && tc->w1 && tc->w2 && !weights_in &&
-      (!experts || (tc->gate && tc->up && tc->down)) && (!fuse_post || x_dtype == WALSH_BF16) &&
+      (!experts || (tc->gate && tc->up && tc->down)) &&
+      (!fuse_post || x_dtype == WALSH_BF16 || x_dtype == WALSH_F16) &&
       ((((uintptr_t)u) | ((uintptr_t)tc->w1) | ((uintptr_t)tc->w2) | ((uintptr_t)tc->gate) |
         ((uintptr_t)tc->up) | ((uintptr_t)tc->down) | ((uintptr_t)y) | ((uintptr_t)x) | ((uintptr_t)x_out)) & 15u) == 0) {
-    return dtype == WALSH_F16
-               ? launch_moe_mma<__half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out, mask_out,
-                                        probs_out, weights_out, s)
-               : launch_moe_mma<__nv_bfloat16>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out,
-                                               mask_out, probs_out, weights_out, s);
+    const bool xh = fuse_post && x_dtype == WALSH_F16;  // stream type of the fused epilogue
+    if (dtype == WALSH_F16)
+      return xh ? launch_moe_mma<__half, __half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out,
+                                                 mask_out, probs_out, weights_out, s)
+                : launch_moe_mma<__half, __nv_bfloat16>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix,
+                                                        x_out, mask_out, probs_out, weights_out, s);
+    return xh ? launch_moe_mma<__nv_bfloat16, __half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix,
+                                                      x_out, mask_out, probs_out, weights_out, s)
+              : launch_moe_mma<__nv_bfloat16, __nv_bfloat16>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x,
+                                                             hmix, x_out, mask_out, probs_out, weights_out, s);
   }
   if (C != 512 && C != 2048) return WALSH_ERR_SHAPE;
   return WALSH_DISPATCH_DTYPE(dtype, TU, WALSH_DISPATCH_DTYPE(x_dtype, TX,

@@ -1,0 +1,385 @@
+// Octonion (Cayley-Dickson) layers as tensor-core GEMMs with fused epilogues.
+//
+// Reference: OctonionTernaryLinearRef / OctonionFusedLinear
+// (src/model/physics.py:53-82, src/model/cayley_dickson_cuda.py:622-668):
+//   y_i = beta * sum_j SIGN[i][j] x_j @ Wq[WIDX[i][j]]^T   (i, j = 0..7 parts)
+// with Wq the unscaled absmean ternary of the [8, out_o, in_o] latent.  The
+// host expands the eight blocks once per parameter version into the dense
+// signed matrix W[(i, o), (j, k)] = SIGN[i][j] Wq[WIDX[i][j]][o][k] (ternary,
+// exact in fp16/bf16), so every octonion layer is one GEMM y = x W^T whose
+// epilogue applies beta per output column and the op that follows:
+//   plain   y = beta . (x W^T)                                (module forward)
+//   qkv     q/k/v of CausalSelfAttention in one GEMM (N = 3C): beta, RoPE
+//           on the interleaved pairs, q written [B, H, T, hd], k/v written
+//           into the caches at rows start_pos..           (chassis.py:424-447)
+//   swiglu  gate and up rows interleaved (N = 2 hidden): h = silu(g) * u
+//                                                            (chassis.py:497-507)
+//   post    the mHC site epilogue x'_i = sum_j H_res[i][j] x_j + H_post[i] f
+//           (wo with the octonion head mixer folded in, and down_proj)
+//                                                            (mhc.py:345-381)
+//
+// Mainloop: CTA tile 128 x 128, 8 warps of 64 x 32, K staged 32 wide through a
+// 3-stage cp.async pipeline; mma.sync m16n8k16 with fp32 accumulation.
+// Operand types: fp16 x with fp16 W; bf16 x with bf16 W; fp32 x split in
+// registers into bf16 hi + lo (x_hi W + x_lo W, and + x_hi W_lo when a W_lo
+// correction matrix is given), which keeps float32 accuracy.
+#include <type_traits>
+
+#include "common.cuh"
+#include "mma.cuh"
+
+namespace walsh {
+namespace octo {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, LD = BK + 8, NT = 256;
+
+template <typename TA>
+using TE = typename std::conditional<std::is_same<TA, __half>::value, __half, __nv_bfloat16>::type;
+
+template <typename TA>
+constexpr int stage_bytes() {
+  return BM * LD * (int)sizeof(TA) + 2 * BN * LD * 2;  // A, W_hi, W_lo
+}
+template <typename TA>
+constexpr int smem_bytes() {
+  return STAGES * stage_bytes<TA>();
+}
+
+__device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16(a, b);
+  const float2 h = unpack2<__nv_bfloat16>(hi);
+  lo = pack_bf16(a - h.x, b - h.y);
+}
+
+template <typename T>
+__device__ __forceinline__ void store2(T* p, float a, float b);
+template <>
+__device__ __forceinline__ void store2<float>(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+template <>
+__device__ __forceinline__ void store2<__half>(__half* p, float a, float b) {
+  *reinterpret_cast<uint32_t*>(p) = pack_f16_sat(a, b);
+}
+template <>
+__device__ __forceinline__ void store2<__nv_bfloat16>(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<uint32_t*>(p) = pack_bf16(a, b);
+}
+
+template <typename T>
+__device__ __forceinline__ float2 load2(const T* p);
+template <>
+__device__ __forceinline__ float2 load2<float>(const float* p) {
+  return *reinterpret_cast<const float2*>(p);
+}
+template <>
+__device__ __forceinline__ float2 load2<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return unpack2<__nv_bfloat16>(*reinterpret_cast<const uint32_t*>(p));
+}
+template <>
+__device__ __forceinline__ float2 load2<__half>(const __half* p) {
+  return unpack2<__half>(*reinterpret_cast<const uint32_t*>(p));
+}
+
+// ---- epilogues: called once per (row m, column pair n, n+1), n even ----------
+template <typename TY>
+struct EpiPlain {
+  const float* scale;
+  TY* y;
+  int64_t N;
+  __device__ __forceinline__ void operator()(int64_t m, int64_t n, float v0, float v1) const {
+    store2(y + m * N + n, v0 * __ldg(scale + n), v1 * __ldg(scale + n + 1));
+  }
+};
+
+template <typename TY>
+struct EpiQkv {
+  const float* scale;  // [3C]
+  TY* q;               // [B, H, T, hd]
+  TY* kc;              // [B, H, ctx, hd]
+  TY* vc;
+  const float* cos;  // [T, hd/2]: rows of the tokens' own positions
+  const float* sin;
+  int T, n_head, hd, C, ctx, start_pos;
+  __device__ __forceinline__ void operator()(int64_t m, int64_t n, float v0, float v1) const {
+    const int which = (int)(n / C);
+    const int c = (int)(n - (int64_t)which * C);
+    const int head = c / hd, d = c - head * hd;
+    const int b = (int)(m / T), t = (int)(m - (int64_t)b * T);
+    v0 *= __ldg(scale + n);
+    v1 *= __ldg(scale + n + 1);
+    if (which < 2) {
+      const float cs = __ldg(cos + (size_t)t * (hd / 2) + (d >> 1)), sn = __ldg(sin + (size_t)t * (hd / 2) + (d >> 1));
+      const float r0 = v0 * cs - v1 * sn, r1 = v0 * sn + v1 * cs;
+      v0 = r0;
+      v1 = r1;
+    }
+    TY* dst = which == 0 ? q + (((size_t)b * n_head + head) * T + t) * hd + d
+                         : (which == 1 ? kc : vc) + (((size_t)b * n_head + head) * ctx + start_pos + t) * hd + d;
+    store2(dst, v0, v1);
+  }
+};
+
+template <typename TY>
+struct EpiSwiglu {
+  const float* scale;  // [2 hidden], interleaved like the weight rows
+  TY* h;               // [M, hidden]
+  int64_t hid;
+  __device__ __forceinline__ void operator()(int64_t m, int64_t n, float g, float u) const {
+    g *= __ldg(scale + n);
+    u *= __ldg(scale + n + 1);
+    h[m * hid + (n >> 1)] = from_f<TY>(g / (1.0f + expf(-g)) * u);
+  }
+};
+
+template <typename TX>
+struct EpiPost {
+  const float* scale;  // [C]
+  const TX* x;         // [M, 4, C]  (may alias xo)
+  const float* hmix;   // [M, 24]: H_pre | H_post | H_res (row-major 4 x 4)
+  TX* xo;
+  int C;
+  __device__ __forceinline__ void operator()(int64_t m, int64_t n, float f0, float f1) const {
+    f0 *= __ldg(scale + n);
+    f1 *= __ldg(scale + n + 1);
+    const float* hm = hmix + m * kMapRows;
+    const size_t base = (size_t)m * 4 * C + n;
+    const float2 x0 = load2(x + base), x1 = load2(x + base + C), x2 = load2(x + base + 2 * C),
+                 x3 = load2(x + base + 3 * C);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float* hr = hm + 8 + 4 * r;
+      const float a = (((hr[0] * x0.x + hr[1] * x1.x) + hr[2] * x2.x) + hr[3] * x3.x) + hm[4 + r] * f0;
+      const float b = (((hr[0] * x0.y + hr[1] * x1.y) + hr[2] * x2.y) + hr[3] * x3.y) + hm[4 + r] * f1;
+      store2(xo + base + (size_t)r * C, a, b);
+    }
+  }
+};
+
+}  // namespace octo
+
+template <typename TA, class Epi>
+__global__ void __launch_bounds__(octo::NT)
+octo_gemm_kernel(const TA* __restrict__ a, int64_t M, int K, const octo::TE<TA>* __restrict__ whi,
+                 const octo::TE<TA>* __restrict__ wlo, int64_t N, Epi epi) {
+  using namespace octo;
+  using W = TE<TA>;
+  constexpr bool SPLIT = std::is_same<TA, float>::value;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int wm = warp & 1, wn = warp >> 1;  // 2 x 4 warps: 64 rows x 32 columns each
+  const int nk = (K + BK - 1) / BK;
+  const bool lo = wlo != nullptr;
+  auto As = [&](int st) { return reinterpret_cast<TA*>(smem_raw + st * stage_bytes<TA>()); };
+  auto Wh = [&](int st) {
+    return reinterpret_cast<W*>(smem_raw + st * stage_bytes<TA>() + BM * LD * (int)sizeof(TA));
+  };
+  auto Wl = [&](int st) { return Wh(st) + BN * LD; };
+  auto load_stage = [&](int kt, int st) {
+    const int k0 = kt * BK;
+    constexpr int AV = 16 / (int)sizeof(TA);  // A elements per 16-byte chunk
+    TA* as = As(st);
+    for (int i = tid; i < BM * (BK / AV); i += NT) {
+      const int r = i / (BK / AV), c = (i % (BK / AV)) * AV;
+      const int64_t m = m0 + r;
+      const bool in = m < M && k0 + c < K;  // K is a multiple of 8: chunks are all in or all out
+      cp_async16(as + r * LD + c, a + (in ? (size_t)m * K + k0 + c : 0), in ? 16 : 0);
+    }
+    W* wh = Wh(st);
+    W* wl = Wl(st);
+    for (int i = tid; i < BN * (BK / 8); i += NT) {
+      const int r = i / (BK / 8), c = (i % (BK / 8)) * 8;
+      const int64_t n = n0 + r;
+      const bool in = n < N && k0 + c < K;
+      const size_t off = in ? (size_t)n * K + k0 + c : 0;
+      cp_async16(wh + r * LD + c, whi + off, in ? 16 : 0);
+      if (lo) cp_async16(wl + r * LD + c, wlo + off, in ? 16 : 0);
+    }
+  };
+#pragma unroll
+  for (int st = 0; st < STAGES - 1; ++st) {
+    if (st < nk) load_stage(st, st);
+    cp_async_commit();
+  }
+  float acc[4][4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
+
+  for (int kt = 0; kt < nk; ++kt) {
+    cp_async_wait<STAGES - 2>();
+    __syncthreads();
+    if (kt + STAGES - 1 < nk) load_stage(kt + STAGES - 1, (kt + STAGES - 1) % STAGES);
+    cp_async_commit();
+    const int st = kt % STAGES;
+    const TA* as = As(st);
+    const W* wh = Wh(st);
+    const W* wl = Wl(st);
+#pragma unroll
+    for (int kk = 0; kk < BK; kk += 16) {
+      uint32_t ah[4][4], al[4][4];
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi) {
+        const int r = wm * 64 + mi * 16;
+        if constexpr (SPLIT) {
+          const float* af = reinterpret_cast<const float*>(as);
+          const float2 v0 = *reinterpret_cast<const float2*>(af + (r + g) * LD + kk + 2 * t4);
+          const float2 v1 = *reinterpret_cast<const float2*>(af + (r + g + 8) * LD + kk + 2 * t4);
+          const float2 v2 = *reinterpret_cast<const float2*>(af + (r + g) * LD + kk + 8 + 2 * t4);
+          const float2 v3 = *reinterpret_cast<const float2*>(af + (r + g + 8) * LD + kk + 8 + 2 * t4);
+          split_bf16(v0.x, v0.y, ah[mi][0], al[mi][0]);
+          split_bf16(v1.x, v1.y, ah[mi][1], al[mi][1]);
+          split_bf16(v2.x, v2.y, ah[mi][2], al[mi][2]);
+          split_bf16(v3.x, v3.y, ah[mi][3], al[mi][3]);
+        } else {
+          ldsm_x4(ah[mi], as + (r + (lane & 15)) * LD + kk + (lane >> 4) * 8);
+        }
+      }
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        const int rn = wn * 32 + np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int cn = kk + ((lane >> 3) & 1) * 8;
+        uint32_t bh[4], bl[4];
+        ldsm_x4(bh, wh + rn * LD + cn);
+        if (lo) ldsm_x4(bl, wl + rn * LD + cn);
+#pragma unroll
+        for (int mi = 0; mi < 4; ++mi) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float* c = acc[mi][2 * np + h];
+            if constexpr (SPLIT) mma16<W>(c, al[mi], bh[2 * h], bh[2 * h + 1]);
+            if (lo) mma16<W>(c, ah[mi], bl[2 * h], bl[2 * h + 1]);
+            mma16<W>(c, ah[mi], bh[2 * h], bh[2 * h + 1]);
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+      const int64_t n = n0 + wn * 32 + ni * 8 + 2 * t4;
+      if (n >= N) continue;  // N is even: the pair (n, n + 1) is all in or all out
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int64_t m = m0 + wm * 64 + mi * 16 + g + hr * 8;
+        if (m < M) epi(m, n, acc[mi][ni][2 * hr], acc[mi][ni][2 * hr + 1]);
+      }
+    }
+}
+
+template <typename TA, class Epi>
+static int launch_octo(const void* a, int64_t M, int K, const void* whi, const void* wlo, int64_t N, const Epi& epi,
+                       cudaStream_t s) {
+  using namespace octo;
+  auto kern = octo_gemm_kernel<TA, Epi>;
+  const int smem = smem_bytes<TA>();
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return launch_status();
+  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
+  kern<<<grid, NT, smem, s>>>((const TA*)a, M, K, (const TE<TA>*)whi, (const TE<TA>*)wlo, N, epi);
+  return launch_status();
+}
+
+// Shared argument checks: x dtype selects the weight dtype (fp16 W for fp16
+// x, bf16 W otherwise); a W_lo correction matrix is only used with fp32 x.
+static walsh_status octo_check(const void* x, int dtype, int64_t M, int K, const void* whi, const void* wlo,
+                               int w_dtype, int64_t N) {
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_ARG(x && whi);
+  WALSH_CHECK_SHAPE(M >= 0 && K > 0 && N > 0 && K % 8 == 0 && N % 2 == 0);
+  WALSH_CHECK_SHAPE((M + octo::BM - 1) / octo::BM <= 2147483647LL && (N + octo::BN - 1) / octo::BN <= 65535);
+  const int want = dtype == WALSH_F16 ? WALSH_F16 : WALSH_BF16;
+  if (w_dtype != want) return WALSH_ERR_DTYPE;
+  if (wlo && dtype != WALSH_F32) return WALSH_ERR_ARG;
+  if ((((uintptr_t)x) | ((uintptr_t)whi) | ((uintptr_t)wlo)) & 15u) return WALSH_ERR_ALIGN;
+  return WALSH_OK;
+}
+
+#define WALSH_OCTO_DISPATCH(dtype, TA, ...)                         \
+  ((dtype) == WALSH_F32    ? ([&] { using TA = float; return __VA_ARGS__; }())   \
+   : (dtype) == WALSH_BF16 ? ([&] { using TA = __nv_bfloat16; return __VA_ARGS__; }()) \
+                           : ([&] { using TA = __half; return __VA_ARGS__; }()))
+
+}  // namespace walsh
+
+using namespace walsh;
+
+extern "C" walsh_status walsh_octo_linear_fwd(const void* x, int dtype, int64_t M, int K, const void* w_hi,
+                                              const void* w_lo, int w_dtype, int64_t N, const float* scale, void* y,
+                                              void* stream) {
+  if (int e = injected("octo_linear_fwd")) return e;
+  if (walsh_status st = octo_check(x, dtype, M, K, w_hi, w_lo, w_dtype, N)) return st;
+  WALSH_CHECK_ARG(scale && y);
+  if (((uintptr_t)y) & 7u) return WALSH_ERR_ALIGN;
+  if (M == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  return WALSH_OCTO_DISPATCH(dtype, TA,
+                             launch_octo<TA>(x, M, K, w_hi, w_lo, N, octo::EpiPlain<TA>{scale, (TA*)y, N}, s));
+}
+
+extern "C" walsh_status walsh_octo_qkv_fwd(const void* u, int dtype, int B, int T, int C, int n_head,
+                                           const void* w_hi, const void* w_lo, int w_dtype, const float* scale,
+                                           const float* rope_cos, const float* rope_sin, int n_pos, int start_pos,
+                                           void* q, void* k_cache, void* v_cache, int ctx, void* stream) {
+  if (int e = injected("octo_qkv_fwd")) return e;
+  WALSH_CHECK_SHAPE(B > 0 && T > 0 && C > 0 && n_head > 0 && C % n_head == 0);
+  const int hd = C / n_head;
+  WALSH_CHECK_SHAPE(hd % 2 == 0 && start_pos >= 0 && start_pos + T <= ctx && T <= n_pos);
+  const int64_t M = (int64_t)B * T;
+  if (walsh_status st = octo_check(u, dtype, M, C, w_hi, w_lo, w_dtype, 3 * (int64_t)C)) return st;
+  WALSH_CHECK_ARG(scale && rope_cos && rope_sin && q && k_cache && v_cache);
+  if ((((uintptr_t)q) | ((uintptr_t)k_cache) | ((uintptr_t)v_cache)) & 7u) return WALSH_ERR_ALIGN;
+  cudaStream_t s = (cudaStream_t)stream;
+  return WALSH_OCTO_DISPATCH(dtype, TA,
+                             launch_octo<TA>(u, M, C, w_hi, w_lo, 3 * (int64_t)C,
+                                             octo::EpiQkv<TA>{scale, (TA*)q, (TA*)k_cache, (TA*)v_cache, rope_cos,
+                                                              rope_sin, T, n_head, hd, C, ctx, start_pos},
+                                             s));
+}
+
+extern "C" walsh_status walsh_octo_swiglu_fwd(const void* u, int dtype, int64_t M, int K, const void* w_hi,
+                                              const void* w_lo, int w_dtype, const float* scale, int64_t hidden,
+                                              void* h, void* stream) {
+  if (int e = injected("octo_swiglu_fwd")) return e;
+  WALSH_CHECK_SHAPE(hidden > 0);
+  if (walsh_status st = octo_check(u, dtype, M, K, w_hi, w_lo, w_dtype, 2 * hidden)) return st;
+  WALSH_CHECK_ARG(scale && h);
+  if (M == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  return WALSH_OCTO_DISPATCH(dtype, TA,
+                             launch_octo<TA>(u, M, K, w_hi, w_lo, 2 * hidden,
+                                             octo::EpiSwiglu<TA>{scale, (TA*)h, hidden}, s));
+}
+
+extern "C" walsh_status walsh_octo_post_fwd(const void* a, int dtype, int64_t M, int K, const void* w_hi,
+                                            const void* w_lo, int w_dtype, const float* scale, int C, const void* x,
+                                            int x_dtype, const float* hmix, void* x_out, void* stream) {
+  if (int e = injected("octo_post_fwd")) return e;
+  WALSH_CHECK_SHAPE(C > 0);
+  if (walsh_status st = octo_check(a, dtype, M, K, w_hi, w_lo, w_dtype, C)) return st;
+  WALSH_CHECK_ARG(scale && x && hmix && x_out);
+  WALSH_CHECK_DTYPE(x_dtype);
+  if ((((uintptr_t)x) | ((uintptr_t)x_out)) & 7u) return WALSH_ERR_ALIGN;
+  if (M == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (x_dtype == WALSH_F16)
+    return WALSH_OCTO_DISPATCH(dtype, TA,
+                               launch_octo<TA>(a, M, K, w_hi, w_lo, C,
+                                               octo::EpiPost<__half>{scale, (const __half*)x, hmix, (__half*)x_out, C},
+                                               s));
+  if (x_dtype == WALSH_F32)
+    return WALSH_OCTO_DISPATCH(dtype, TA,
+                               launch_octo<TA>(a, M, K, w_hi, w_lo, C,
+                                               octo::EpiPost<float>{scale, (const float*)x, hmix, (float*)x_out, C},
+                                               s));
+  return WALSH_OCTO_DISPATCH(
+      dtype, TA,
+      launch_octo<TA>(a, M, K, w_hi, w_lo, C,
+                      octo::EpiPost<__nv_bfloat16>{scale, (const __nv_bfloat16*)x, hmix, (__nv_bfloat16*)x_out, C},
+                      s));
+}

@@ -148,7 +148,9 @@ class CausalSelfAttention(nn.Module):
 
     def forward_site(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, xs, hmix):
         """Attention plus the mHC site epilogue: xs [B, T, n, C] <- H_res xs + H_post attn(x)."""
-        if not self._tc(x) or xs.dtype != torch.bfloat16:
+        if self.algebra != "hadamard":
+            return self._octonion_site(x, rope_cos, rope_sin, k_cache, v_cache, start_pos, xs, hmix)
+        if not self._tc(x) or xs.dtype not in (torch.bfloat16, torch.float16):
             f = self.forward_cached(x, rope_cos, rope_sin, k_cache, v_cache, start_pos, out_dtype=xs.dtype)
             return ops.mhc_post(xs, f, hmix, out=xs)
         B, T, C = x.shape
@@ -179,18 +181,32 @@ class CausalSelfAttention(nn.Module):
         else:
             self._octonion_qkv(x, rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
         o = ops.attention(q, k_cache, v_cache, start_pos)           # [B, T, H, hd]
-        if self.head_mixer is not None:
-            o = self.head_mixer.forward_tokens(o, out=o)
         y = o.view(B, T, C)
         if self.algebra == "hadamard":
+            if self.head_mixer is not None:
+                o = self.head_mixer.forward_tokens(o, out=o)
             inner = self.wo.inner
             alpha, beta = inner.scales()
             return ops.hadamard_linear(y, inner.packed(), alpha, beta, 1.0, out_dtype=out_dtype or x.dtype)
-        return self.wo.forward_flat(y, out_dtype=out_dtype or x.dtype)
+        from .cayley_dickson_cuda import folded_output
+        w, s = folded_output(self, y.dtype)
+        f = ops.octo_linear(y, w, s)
+        return f if out_dtype in (None, f.dtype) else f.to(out_dtype)
 
     def _octonion_qkv(self, x, rope_cos, rope_sin, start_pos, q, k_cache, v_cache):
         from .cayley_dickson_cuda import octonion_qkv
         octonion_qkv(self, x, rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
+
+    def _octonion_site(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos, xs, hmix):
+        """q/k/v GEMM (RoPE, cache write) -> attention -> one GEMM for the head
+        mixer and wo with the mHC site epilogue."""
+        from .cayley_dickson_cuda import folded_output
+        B, T, C = x.shape
+        q = torch.empty((B, self.n_head, T, self.head_dim), dtype=k_cache.dtype, device=x.device)
+        self._octonion_qkv(x, rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
+        o = ops.attention(q, k_cache, v_cache, start_pos)
+        w, s = folded_output(self, o.dtype)
+        return ops.octo_post(o.view(B, T, C), w, s, xs, hmix, out=xs)
 
     def forward(self, x, freqs_cis, kv_cache: Optional[KVCache] = None, layer_idx: int = 0):
         B, T, C = x.shape

@@ -80,6 +80,17 @@ class HadamardLinear(nn.Module):
         return _prep.cached(self, "scales", [self.alpha, self.beta],
                             lambda: (self.alpha.detach().float().contiguous(), self.beta.detach().float().contiguous()))
 
+    def dense(self) -> torch.Tensor:
+        """The layer as one matrix, float32 [out, in]:
+        W[(h, o), (p, i)] = beta[h, o] sum_g H[g, h] w[g, o, i] H[p, g] alpha[p, i]."""
+        def build():
+            Hm = hadamard_matrix(ALGEBRA_DIM, normalize=True).double().to(self.weight.device)
+            w = ops.unpack(self.packed(), self.in_o).double()
+            W = torch.einsum("gh,goi,pg->hopi", Hm, w, Hm)
+            W = W * self.beta.detach().double()[:, :, None, None] * self.alpha.detach().double()[None, None]
+            return W.reshape(self.out_features, self.in_features).float().contiguous()
+        return _prep.cached(self, "dense", [self.weight, self.alpha, self.beta], build)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         alpha, beta = self.scales()
         if ops.tc_eligible(x) and self.in_features == 512 and self.out_features == 512:

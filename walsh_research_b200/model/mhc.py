@@ -77,22 +77,23 @@ class ResidualStreamMapping(nn.Module):
         return h.reshape(B, T, n, n) if self.mapping_type == "res" else h.reshape(B, T, 1, n)
 
 
-def site_params(stream: "mHCResidualStream"):
-    """phi [24, n*C] and mparams [28] of one mHC site, on the device."""
+def site_params(stream: "mHCResidualStream", dtype=torch.bfloat16):
+    """phi [24, n*C], mparams [28] and phi in the 16-bit stream dtype (the
+    tensor-core operand copy) of one mHC site, on the device."""
     pre, post, res = stream.H_pre, stream.H_post, stream.H_res
 
     def build():
         phi = torch.cat([pre.phi.weight, post.phi.weight, res.phi.weight]).detach().float().contiguous()
-        phi_bf16 = phi.to(torch.bfloat16).contiguous()
+        phi_lp = phi.to(dtype if dtype != torch.float32 else torch.bfloat16).contiguous()
         dev = phi.device
         mp = torch.cat([torch.stack([pre.alpha, post.alpha, res.alpha]).detach().float().reshape(3),
                         torch.zeros(1, device=dev),
                         pre.bias.detach().float().reshape(-1), post.bias.detach().float().reshape(-1),
                         res.bias.detach().float().reshape(-1)]).contiguous()
-        return phi, mp, phi_bf16
+        return phi, mp, phi_lp
     srcs = [pre.phi.weight, post.phi.weight, res.phi.weight, pre.alpha, post.alpha, res.alpha,
             pre.bias, post.bias, res.bias]
-    return _prep.cached(stream, "site", srcs, build)
+    return _prep.cached(stream, f"site_{dtype}", srcs, build)
 
 
 class mHCResidualStream(nn.Module):
@@ -107,8 +108,8 @@ class mHCResidualStream(nn.Module):
         self.H_res = ResidualStreamMapping(n_embd, n_streams, "res")
 
     def forward(self, x, layer_fn):
-        phi, mp, phib = site_params(self)
-        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, phi_bf16=phib)
+        phi, mp, phib = site_params(self, x.dtype)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, phi_lp=phib)
         return ops.mhc_post(x, layer_fn(u), hmix)
 
 
@@ -148,13 +149,13 @@ class mHCLlamaBlock(nn.Module):
         B, T, n, C = x.shape
         idt = k_cache.dtype  # storage type of u, q/k/v and the attention output
         # attention site
-        phi, mp, phib = site_params(self.attn_stream)
+        phi, mp, phib = site_params(self.attn_stream, x.dtype)
         u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.attention_norm.weight), self.attention_norm.eps,
-                              phi_bf16=phib, u_dtype=idt)
+                              phi_lp=phib, u_dtype=idt)
         self.attention.forward_site(u, rope_cos, rope_sin, k_cache, v_cache, start_pos, x, hmix)
         # ffn site
-        phi, mp, phib = site_params(self.ffn_stream)
-        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.ffn_norm.weight), self.ffn_norm.eps, phi_bf16=phib,
+        phi, mp, phib = site_params(self.ffn_stream, x.dtype)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.ffn_norm.weight), self.ffn_norm.eps, phi_lp=phib,
                               u_dtype=idt)
         ff = self.feed_forward
         if hasattr(ff, "kernel_args"):
@@ -164,6 +165,8 @@ class mHCLlamaBlock(nn.Module):
                 ff._record(mask, probs, B * T)
             else:
                 ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), tc=tc)
+        elif hasattr(ff, "forward_site"):
+            ff.forward_site(u, x, hmix)
         else:
             ops.mhc_post(x, ff(u), hmix, out=x)
         # channel modulation over the [B*n, T, C] reinterpretation of x
@@ -196,7 +199,15 @@ class mHCWalsh(nn.Module):
 
     ``compute_dtype`` (float32 or bfloat16) selects the activation precision;
     a forward run under ``torch.autocast('cuda', dtype=torch.bfloat16)`` uses
-    bfloat16 as well.  Parameters stay float32, as in the reference."""
+    bfloat16 as well.  Parameters stay float32, as in the reference.
+
+    In 16-bit mode every tensor-core operand is 16-bit with float32
+    accumulation, and the residual stream is stored in ``stream_dtype``:
+    float16 by default (8x finer rounding than bfloat16; the stream is
+    bounded by the convex H_res mixing, H_post < 2 and the normalised
+    channel-modulation terms), or ``torch.bfloat16`` for bfloat16's range.
+    The normalised activations (u, q/k/v, attention output, SwiGLU hidden)
+    are float16 in both cases."""
 
     def __init__(self, config, n_streams=4, gradient_checkpointing=False):
         super().__init__()
@@ -204,6 +215,7 @@ class mHCWalsh(nn.Module):
         self.n_streams = n_streams
         self.gradient_checkpointing = gradient_checkpointing
         self.compute_dtype = torch.float32
+        self.stream_dtype = None  # 16-bit mode stream storage: None -> float16
         if getattr(config, "hash_embeddings", False):
             raise NotImplementedError("hash embeddings are outside the B200 hot path")
         self.tok_embeddings = nn.Embedding(config.vocab_size, config.n_embd)
@@ -232,9 +244,13 @@ class mHCWalsh(nn.Module):
 
     # -- device-side derived weights ------------------------------------------------
     def _act_dtype(self):
+        """Residual-stream storage type of this forward."""
+        dt = self.compute_dtype
         if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
-            return torch.bfloat16
-        return self.compute_dtype
+            dt = torch.bfloat16
+        if dt == torch.float32:
+            return dt
+        return self.stream_dtype or torch.float16
 
     def stream_table(self, dtype):
         """tok_embeddings folded with stream_proj: row v = stream_proj(emb[v]), [V, n*C]."""

@@ -84,7 +84,7 @@ def attn_out_tc(o, wmix, beta_mix, wo, alpha_o, beta_o, x, hmix, out=None):
     o = _c(o)
     out = out if out is not None else torch.empty_like(x)
     call("walsh_attn_out_tc_fwd", ptr(o), o.numel() // 512, ptr(wmix), ptr(beta_mix), ptr(wo), ptr(alpha_o),
-         ptr(beta_o), ptr(x), ptr(hmix), ptr(out), stream())
+         ptr(beta_o), ptr(x), dcode(x.dtype), ptr(hmix), ptr(out), stream())
     return out
 
 
@@ -103,9 +103,9 @@ def head_mixer_tokens(x, W, beta, out=None):
 # mHC
 # ---------------------------------------------------------------------------
 
-def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6, phi_bf16=None, u_dtype=None):
+def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6, phi_lp=None, u_dtype=None):
     """x [..., 4, C] -> (u [..., C] in u_dtype (default x's), hmix float [..., 24]).
-    ``phi_bf16`` (a bfloat16 copy of phi) enables the tensor-core kernel for bf16 x."""
+    ``phi_lp`` (phi in x's 16-bit dtype) enables the tensor-core kernel for 16-bit x."""
     require_cuda(x)
     x = _c(x)
     C = x.shape[-1]
@@ -114,7 +114,9 @@ def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6, phi_bf16=None,
     u_dtype = u_dtype or x.dtype
     u = torch.empty(lead + (C,), dtype=u_dtype, device=x.device)
     hmix = torch.empty(lead + (24,), dtype=torch.float32, device=x.device)
-    call("walsh_mhc_map", ptr(x), dcode(x.dtype), ntok, C, ptr(phi), ptr(phi_bf16), ptr(mparams), float(map_eps),
+    if phi_lp is not None and phi_lp.dtype != x.dtype:
+        phi_lp = None
+    call("walsh_mhc_map", ptr(x), dcode(x.dtype), ntok, C, ptr(phi), ptr(phi_lp), ptr(mparams), float(map_eps),
          ptr(norm_w), float(norm_eps), ptr(u), dcode(u_dtype), ptr(hmix), stream())
     return u, hmix
 
@@ -245,6 +247,73 @@ def attention(q, k_cache, v_cache, start_pos, out=None):
 
 
 # ---------------------------------------------------------------------------
+# octonion (Cayley-Dickson) GEMMs; w = (w_hi, w_lo or None) in the operand
+# dtype the x dtype selects (float16 for float16 x, bfloat16 otherwise)
+# ---------------------------------------------------------------------------
+
+def octo_operand_dtype(x_dtype):
+    return torch.float16 if x_dtype == torch.float16 else torch.bfloat16
+
+
+def _octo_w(x, w):
+    hi, lo = w
+    if hi.dtype != octo_operand_dtype(x.dtype):
+        raise ValueError(f"octonion weights are {hi.dtype}; {x.dtype} activations need {octo_operand_dtype(x.dtype)}")
+    if x.dtype != torch.float32:
+        lo = None
+    return hi, lo
+
+
+def octo_linear(x, w, scale, out=None):
+    """y = scale . (x w^T); x [..., K] -> y [..., N] in x's dtype."""
+    require_cuda(x)
+    x = _c(x)
+    hi, lo = _octo_w(x, w)
+    N, K = hi.shape
+    M = x.numel() // K
+    y = out if out is not None else torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    call("walsh_octo_linear_fwd", ptr(x), dcode(x.dtype), M, K, ptr(hi), ptr(lo), dcode(hi.dtype), N, ptr(scale),
+         ptr(y), stream())
+    return y
+
+
+def octo_qkv(u, n_head, w, scale, rope_cos, rope_sin, start_pos, q, k_cache, v_cache):
+    require_cuda(u)
+    u = _c(u)
+    B, T, C = u.shape
+    hi, lo = _octo_w(u, w)
+    call("walsh_octo_qkv_fwd", ptr(u), dcode(u.dtype), B, T, C, n_head, ptr(hi), ptr(lo), dcode(hi.dtype),
+         ptr(scale), ptr(rope_cos), ptr(rope_sin), rope_cos.shape[0], int(start_pos), ptr(q), ptr(k_cache),
+         ptr(v_cache), k_cache.shape[-2], stream())
+
+
+def octo_swiglu(u, w, scale, hidden, out=None):
+    """h = silu(gate(u)) * up(u) with gate/up rows interleaved in w [2 hidden, K]."""
+    require_cuda(u)
+    u = _c(u)
+    hi, lo = _octo_w(u, w)
+    K = hi.shape[1]
+    M = u.numel() // K
+    h = out if out is not None else torch.empty(u.shape[:-1] + (hidden,), dtype=u.dtype, device=u.device)
+    call("walsh_octo_swiglu_fwd", ptr(u), dcode(u.dtype), M, K, ptr(hi), ptr(lo), dcode(hi.dtype), ptr(scale),
+         int(hidden), ptr(h), stream())
+    return h
+
+
+def octo_post(a, w, scale, x, hmix, out=None):
+    """f = scale . (a w^T), then x_out = H_res x + H_post f (x [..., 4, C])."""
+    require_cuda(a, x)
+    a = _c(a)
+    hi, lo = _octo_w(a, w)
+    C, K = hi.shape
+    M = a.numel() // K
+    out = out if out is not None else torch.empty_like(x)
+    call("walsh_octo_post_fwd", ptr(a), dcode(a.dtype), M, K, ptr(hi), ptr(lo), dcode(hi.dtype), ptr(scale), C,
+         ptr(x), dcode(x.dtype), ptr(hmix), ptr(out), stream())
+    return out
+
+
+# ---------------------------------------------------------------------------
 # dense helpers
 # ---------------------------------------------------------------------------
 
@@ -287,7 +356,7 @@ def split_bf16(w):
 def split_eligible(x, K, ldx=None) -> bool:
     esz = x.element_size()
     ld = K if ldx is None else ldx
-    return (x.dtype in (torch.float32, torch.bfloat16) and K % 32 == 0 and x.data_ptr() % 16 == 0
+    return (x.dtype in (torch.float32, torch.bfloat16, torch.float16) and K % 32 == 0 and x.data_ptr() % 16 == 0
             and (ld * esz) % 16 == 0)
 
 
