@@ -70,6 +70,25 @@ def build_model_cpu(seed=0):
     return model
 
 
+OCTO_CONFIG = dict(CONFIG, algebra="octonion", use_moe=False)
+OCTO_BATCH = 32
+
+
+def build_octonion_cpu(seed=0):
+    """Config 2: the same recipe on the octonion variant (SwiGLU FFN, no MoE)."""
+    from walsh_research_b200.model import WalshConfig, mHCWalsh
+    torch.manual_seed(seed)
+    model = mHCWalsh(WalshConfig(**OCTO_CONFIG), n_streams=N_STREAMS).eval()
+    g = torch.Generator().manual_seed(seed)
+    pat = re.compile(r"attention\.w[qkvo]\.weight$|feed_forward\.(gate|up|down)_proj\.weight$|"
+                     r"channel_mod\.context_mlp\.\d\.weight$")
+    with torch.no_grad():
+        for name, p in sorted(model.named_parameters()):
+            if pat.search(name):
+                p.copy_(torch.randint(-1, 2, p.shape, generator=g).float())
+    return model
+
+
 def token_ids(B, T, seed=1):
     g = torch.Generator().manual_seed(seed)
     return torch.randint(0, CONFIG["vocab_size"], (B, T), generator=g)
@@ -196,7 +215,8 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode measurement")
-    ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode"],
+    ap.add_argument("--no-octonion", action="store_true", help="skip the config-2 octonion measurement")
+    ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode", "octonion"],
                     help="run one warm-up and one eager forward only (for ncu launch lists)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -292,6 +312,7 @@ def main():
     del graph, logits_g
     torch.cuda.empty_cache()
     decode = None if args.no_decode else measure_decode(model, dev, args.steps, max(3, args.warmup), rank, world, dist)
+    octo = None if args.no_octonion else measure_octonion(dev, args.steps, max(3, args.warmup), rank, world, dist)
 
     if dist:
         dist.barrier()
@@ -312,6 +333,7 @@ def main():
                        "batch_per_gpu": B, "seq_len": T, "parallelism": f"replicas x{world} (batch-sharded)",
                        "l2": "working set > L2 (stream state 268 MB per layer), no flush"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(), "decode": decode,
+            "octonion": octo,
             "gpu_launches": launches_per_forward * args.steps,
             "peaks": src}
     print(json.dumps(line), flush=True)
@@ -342,7 +364,12 @@ def run_profile(args):
             torch.cuda.synchronize()
         print("profile decode step done", flush=True)
         return
-    idx = token_ids(args.batch, SEQ).to(dev)
+    B = args.batch
+    if args.profile == "octonion":
+        model = build_octonion_cpu().to(dev).eval()
+        model.compute_dtype = torch.bfloat16
+        B = OCTO_BATCH
+    idx = token_ids(B, SEQ).to(dev)
     with torch.no_grad():
         model(idx)
         torch.cuda.synchronize()
@@ -445,6 +472,48 @@ def measure_decode(model, dev, steps, warmup, rank=0, world=1, dist=None, B=None
             "e2e": {"value": world * B / (e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * CONFIG["vocab_size"] * 4},
             "gpu_launches": launches_per_step * steps}
+
+
+def measure_octonion(dev, steps, warmup, rank=0, world=1, dist=None):
+    """Config 2 prefill (octonion Walsh-512, B32 x T1024 per GPU): graph
+    replays of the forward with the ids resident in HBM, as for config 3."""
+    from walsh_research_b200 import _lib
+    model = build_octonion_cpu().to(dev).eval()
+    model.compute_dtype = torch.bfloat16
+    B, T = OCTO_BATCH, SEQ
+    idx = token_ids(B, T, seed=7 + rank).to(dev)
+    with torch.no_grad():
+        for _ in range(2):
+            model(idx)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        n0 = _lib.launch_count
+        with torch.cuda.graph(g):
+            model(idx)
+        launches = _lib.launch_count - n0
+        for _ in range(warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            g.replay()
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / steps
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+    del g, model
+    torch.cuda.empty_cache()
+    return {"metric": "Walsh-512 octonion prefill tokens/s", "value": world * B * T / (ms / 1e3), "unit": UNIT,
+            "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "config": {"workload": "config 2: octonion Walsh-512 (SwiGLU 1368, head mixing, chmod) prefill",
+                       "batch_per_gpu": B, "seq_len": T, "l2": "stream state 134 MB per layer > L2, no flush"},
+            "gpu_launches": launches * steps}
 
 
 def dominant_kernel_roofline(model, idx, B, T, dev):

@@ -265,6 +265,20 @@ walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int to
  * the output part).  K a multiple of 8, N even, x/w 16-byte aligned.
  * ------------------------------------------------------------------------- */
 
+/* 16-bit x runs on the 5th-generation tensor cores (TMA-staged operands,
+ * tcgen05.mma into Tensor Memory) unless switched off here; float32 x, and
+ * any call with w_lo, use the mma.sync mainloop.  Returns the previous
+ * setting.  Process-wide; not thread-safe against concurrent launches.
+ * No counterpart in the reference (selects between this library's own two
+ * mainloops, e.g. to compare them in tests). */
+int walsh_octo_set_mainloop(int tcgen05);
+
+/* Status word of the tcgen05 kernels on the current device: 0, or
+ * WALSH_ERR_TIMEOUT once a bounded wait inside one of them gave up (the
+ * affected tile is not written).  Synchronous read; reset != 0 clears it.
+ * No counterpart in the reference. */
+int walsh_tc05_error(int reset);
+
 /* y = scale . (x w^T), y in x's dtype [M, N].
  * Replaces OctonionTernaryLinearRef.forward / OctonionFusedLinear.forward
  * (src/model/physics.py:66-82, src/model/cayley_dickson_cuda.py:654-668). */

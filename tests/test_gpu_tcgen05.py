@@ -1,0 +1,94 @@
+"""The tcgen05 GEMM mainloop (TMA + tensor memory) against the mma.sync
+mainloop and the oracle, for every fused epilogue: ragged M/N/K tiles, both
+16-bit operand types, and the device status word of the bounded waits."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import walsh_oracle as O
+from test_gpu_parity import DEV, T, rel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def mainloop():
+    from walsh_research_b200 import _lib
+    _lib.call("walsh_tc05_error", 1)
+    prev = _lib.call("walsh_octo_set_mainloop", 1)
+
+    def run(fn, tcgen05):
+        _lib.call("walsh_octo_set_mainloop", 1 if tcgen05 else 0)
+        out = fn()
+        torch.cuda.synchronize()
+        return out
+    yield run
+    _lib.call("walsh_octo_set_mainloop", prev)
+    assert _lib.call("walsh_tc05_error", 1) == 0
+
+
+def _layer(fin, fout, rng):
+    from walsh_research_b200.model.cayley_dickson_cuda import OctonionFusedLinear
+    m = OctonionFusedLinear(fin, fout)
+    with torch.no_grad():
+        m.weight.copy_(torch.from_numpy(rng.uniform(-1, 1, (8, fout // 8, fin // 8)).astype(np.float32)))
+        m.beta.copy_(torch.from_numpy(rng.uniform(0.05, 0.2, (fout // 8,)).astype(np.float32)))
+    return m.to(DEV)
+
+
+@pytest.mark.parametrize("M,fin,fout", [(1, 512, 512), (128, 512, 512), (1000, 1368, 512), (333, 512, 1368),
+                                        (4099, 512, 1536), (77, 64, 48)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_plain_gemm_matches_mma_sync_and_oracle(mainloop, M, fin, fout, dtype):
+    rng = np.random.default_rng(M + 3 * fin + fout)
+    m = _layer(fin, fout, rng)
+    x = T(rng.normal(size=(M, fin)).astype(np.float32), dtype)
+    a = mainloop(lambda: m.forward_flat(x), True)
+    b = mainloop(lambda: m.forward_flat(x), False)
+    w, be = m.weight.detach().cpu().numpy(), m.beta.detach().cpu().numpy()
+    ref = O.octonion_linear(x.float().cpu().numpy(), w, be)
+    tol = 3e-3 if dtype == torch.float16 else 1e-2
+    assert rel(a, ref) < tol
+    # same products, fp32 accumulation in a different order: outputs agree to the output rounding
+    assert rel(a, b.float().cpu().numpy()) < (2e-3 if dtype == torch.float16 else 8e-3)
+
+
+@pytest.mark.parametrize("tokens", [37, 5000])
+def test_qkv_swiglu_post_epilogues_match_mma_sync(mainloop, tokens):
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model import WalshConfig
+    from walsh_research_b200.model.cayley_dickson_cuda import SwiGLUMLP, qkv_operands
+    from walsh_research_b200.model.chassis import CausalSelfAttention, precompute_freqs_cis
+    rng = np.random.default_rng(tokens)
+    cfg = WalshConfig(n_embd=512, n_head=32, algebra="octonion", head_mixing=True)
+    attn = CausalSelfAttention(cfg)
+    mlp = SwiGLUMLP(cfg)
+    with torch.no_grad():
+        for lin in (attn.wq, attn.wk, attn.wv, attn.wo, mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+            lin.weight.copy_(torch.from_numpy(rng.uniform(-1, 1, tuple(lin.weight.shape)).astype(np.float32)))
+    attn, mlp = attn.to(DEV), mlp.to(DEV)
+    B = 1
+    Tn, ctx, start = tokens, tokens + 9, 9
+    u = T(rng.normal(size=(B, Tn, 512)).astype(np.float32), torch.float16)
+    f = precompute_freqs_cis(16, ctx + 16)
+    cos, sin = f.real[start:start + Tn].float().contiguous().to(DEV), f.imag[start:start + Tn].float().contiguous().to(DEV)
+
+    def qkv():
+        q = torch.zeros((B, 32, Tn, 16), dtype=torch.float16, device=DEV)
+        kc = torch.zeros((B, 32, ctx, 16), dtype=torch.float16, device=DEV)
+        vc = torch.zeros_like(kc)
+        attn._octonion_qkv(u, cos, sin, start, q, kc, vc)
+        return torch.cat([q.flatten(), kc.flatten(), vc.flatten()])
+    assert rel(mainloop(qkv, True), mainloop(qkv, False).float().cpu().numpy()) < 2e-3
+
+    h = mainloop(lambda: mlp.hidden_act(u), True)
+    h2 = mainloop(lambda: mlp.hidden_act(u), False)
+    assert rel(h, h2.float().cpu().numpy()) < 2e-3
+
+    xs = T(rng.normal(size=(B * Tn, 4, 512)).astype(np.float32), torch.float16)
+    hmix = torch.rand((B * Tn, 24), device=DEV)
+
+    def post():
+        w, s = mlp.down_operands(h.dtype)
+        return ops.octo_post(h, w, s, xs, hmix)
+    assert rel(mainloop(post, True), mainloop(post, False).float().cpu().numpy()) < 2e-3

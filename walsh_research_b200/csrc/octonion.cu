@@ -23,12 +23,22 @@
 // Operand types: fp16 x with fp16 W; bf16 x with bf16 W; fp32 x split in
 // registers into bf16 hi + lo (x_hi W + x_lo W, and + x_hi W_lo when a W_lo
 // correction matrix is given), which keeps float32 accuracy.
+#include <cudaTypedefs.h>
+
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
 #include "mma.cuh"
+#include "tc05.cuh"
 
 namespace walsh {
+
+// The tcgen05 mainloop is used for 16-bit operands unless switched off with
+// walsh_octo_set_mainloop (tests run both mainloops on the same inputs).
+static int g_octo_tc05 = 1;
+static inline bool octo_tc05_enabled() { return g_octo_tc05 != 0; }
+
 namespace octo {
 
 constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, LD = BK + 8, NT = 256;
@@ -81,7 +91,20 @@ __device__ __forceinline__ float2 load2<__half>(const __half* p) {
   return unpack2<__half>(*reinterpret_cast<const uint32_t*>(p));
 }
 
-// ---- epilogues: called once per (row m, column pair n, n+1), n even ----------
+template <typename T>
+__device__ __forceinline__ void store16(T* p, const float* v) {
+  store8(p, v);
+  store8(p + 8, v + 8);
+}
+template <typename T>
+__device__ __forceinline__ void load16(const T* p, float* v) {
+  load8(p, v);
+  load8(p + 8, v + 8);
+}
+
+// ---- epilogues: operator() once per (row m, column pair n, n+1), n even;
+// chunk16 once per row and 16 consecutive columns n..n+15 (n a multiple of
+// 16, destination rows aligned for 16-byte vectors; the launcher checks) ----
 template <typename TY>
 struct EpiPlain {
   const float* scale;
@@ -90,6 +113,17 @@ struct EpiPlain {
   __device__ __forceinline__ void operator()(int64_t m, int64_t n, float v0, float v1) const {
     store2(y + m * N + n, v0 * __ldg(scale + n), v1 * __ldg(scale + n + 1));
   }
+  __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = v[j] * __ldg(scale + n + j);
+    store16(y + m * N + n, o);
+  }
+  __device__ __forceinline__ void chunk32(int64_t m, int64_t n, const float* v) const {
+    chunk16(m, n, v);
+    chunk16(m, n + 16, v + 16);
+  }
+  __host__ bool vec_ok() const { return N % 16 == 0; }
 };
 
 template <typename TY>
@@ -118,6 +152,35 @@ struct EpiQkv {
                          : (which == 1 ? kc : vc) + (((size_t)b * n_head + head) * ctx + start_pos + t) * hd + d;
     store2(dst, v0, v1);
   }
+  // 16 columns = 16 dims of one head (hd a multiple of 16)
+  __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
+    const int which = (int)(n / C);
+    const int c = (int)(n - (int64_t)which * C);
+    const int head = c / hd, d = c - head * hd;
+    const int b = (int)(m / T), t = (int)(m - (int64_t)b * T);
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = v[j] * __ldg(scale + n + j);
+    if (which < 2) {
+      const float* cr = cos + (size_t)t * (hd / 2) + (d >> 1);
+      const float* sr = sin + (size_t)t * (hd / 2) + (d >> 1);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float cs = __ldg(cr + j), sn = __ldg(sr + j);
+        const float a = o[2 * j], bb = o[2 * j + 1];
+        o[2 * j] = a * cs - bb * sn;
+        o[2 * j + 1] = a * sn + bb * cs;
+      }
+    }
+    TY* dst = which == 0 ? q + (((size_t)b * n_head + head) * T + t) * hd + d
+                         : (which == 1 ? kc : vc) + (((size_t)b * n_head + head) * ctx + start_pos + t) * hd + d;
+    store16(dst, o);
+  }
+  __device__ __forceinline__ void chunk32(int64_t m, int64_t n, const float* v) const {
+    chunk16(m, n, v);
+    chunk16(m, n + 16, v + 16);
+  }
+  __host__ bool vec_ok() const { return hd % 16 == 0 && C % 16 == 0; }
 };
 
 template <typename TY>
@@ -130,6 +193,26 @@ struct EpiSwiglu {
     u *= __ldg(scale + n + 1);
     h[m * hid + (n >> 1)] = from_f<TY>(g / (1.0f + expf(-g)) * u);
   }
+  __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float g = v[2 * j] * __ldg(scale + n + 2 * j), u = v[2 * j + 1] * __ldg(scale + n + 2 * j + 1);
+      o[j] = g / (1.0f + expf(-g)) * u;
+    }
+    store8(h + m * hid + (n >> 1), o);
+  }
+  // 16 outputs h[m, n/2 .. n/2 + 15]; fast exp and division (16-bit output)
+  __device__ __forceinline__ void chunk32(int64_t m, int64_t n, const float* v) const {
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float g = v[2 * j] * __ldg(scale + n + 2 * j), u = v[2 * j + 1] * __ldg(scale + n + 2 * j + 1);
+      o[j] = siluf_(g) * u;
+    }
+    store16(h + m * hid + (n >> 1), o);
+  }
+  __host__ bool vec_ok() const { return hid % 8 == 0; }
 };
 
 template <typename TX>
@@ -154,6 +237,64 @@ struct EpiPost {
       store2(xo + base + (size_t)r * C, a, b);
     }
   }
+  __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
+    const float* hm = hmix + m * kMapRows;
+    const size_t base = (size_t)m * 4 * C + n;
+    float xs[4][16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) load16(x + base + (size_t)j * C, xs[j]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float* hr = hm + 8 + 4 * r;
+      const float hp = hm[4 + r];
+      float o[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float f = v[e] * __ldg(scale + n + e);
+        o[e] = (((hr[0] * xs[0][e] + hr[1] * xs[1][e]) + hr[2] * xs[2][e]) + hr[3] * xs[3][e]) + hp * f;
+      }
+      store16(xo + base + (size_t)r * C, o);
+    }
+  }
+  // all 4 x 32 stream values are loaded before any store (x and xo may alias)
+  __device__ __forceinline__ void chunk32(int64_t m, int64_t n, const float* v) const {
+    static_assert(sizeof(TX) == 2 || sizeof(TX) == 4, "stream type");
+    const float* hm = hmix + m * kMapRows;
+    float hr[16], hp[4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) hr[i] = __ldg(hm + 8 + i);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hp[i] = __ldg(hm + 4 + i);
+    const size_t base = (size_t)m * 4 * C + n;
+    if constexpr (sizeof(TX) == 2) {
+      uint4 xr[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xr[j][k] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * C + 8 * k);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float xf[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) unpack8(xr[j][k], xf[j], (const TX*)nullptr);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float f = v[8 * k + e] * __ldg(scale + n + 8 * k + e);
+            o[e] = (((hr[4 * r] * xf[0][e] + hr[4 * r + 1] * xf[1][e]) + hr[4 * r + 2] * xf[2][e]) +
+                    hr[4 * r + 3] * xf[3][e]) + hp[r] * f;
+          }
+          store8(xo + base + (size_t)r * C + 8 * k, o);
+        }
+      }
+    } else {
+      chunk16(m, n, v);
+      chunk16(m, n + 16, v + 16);
+    }
+  }
+  __host__ bool vec_ok() const { return C % 16 == 0; }
 };
 
 }  // namespace octo
@@ -272,10 +413,233 @@ octo_gemm_kernel(const TA* __restrict__ a, int64_t M, int K, const octo::TE<TA>*
     }
 }
 
+// ---------------------------------------------------------------------------
+// The same GEMMs on the 5th-generation tensor cores (16-bit x, no W_lo).
+// Persistent, warp-specialised kernel, one CTA per SM:
+//   warp 0     TMA producer: A [128 x 64] and B [256 x 64] tiles (128-byte
+//              swizzle) into a 4-stage shared-memory ring (48 KB a stage);
+//   warp 1     allocates all 512 TMEM columns and issues tcgen05.mma
+//              (M128 N256 K16, fp32 accumulators), freeing each ring stage
+//              with tcgen05.commit; two 256-column accumulators alternate
+//              between tiles;
+//   warps 2-9  epilogue, two warps per TMEM lane quarter (one per half of
+//              the 256 columns): tcgen05.ld of their 32 accumulator rows, 32
+//              columns at a time, into the fused epilogue, then release the
+//              accumulator so the MMAs of the tile after next can start.
+// So the epilogue of one tile overlaps the MMAs of the next.  Tiles are
+// walked N-fastest so CTAs running at the same time share A rows in L2.
+// ---------------------------------------------------------------------------
+namespace octo_tc {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, ACC_COLS = 256, TMEM_COLS = 512;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+}  // namespace octo_tc
+
+// Set when a bounded wait of a tcgen05 kernel in this file gave up.
+__device__ int g_tc05_error;
+
+template <typename TA, class Epi>
+__global__ void __launch_bounds__(octo_tc::NTHREADS, 1)
+octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                      int64_t M, int K, int64_t N, Epi epi, int vec) {
+  using namespace octo_tc;
+  using namespace tc05;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (K + BK - 1) / BK;
+  const int64_t mt = (M + BM - 1) / BM, ntl = (N + BN - 1) / BN, tiles = mt * ntl;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t IDESC = idesc_f16(std::is_same<TA, __nv_bfloat16>::value, BM, BN);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int64_t g = 0;  // k-iterations issued by this CTA
+      for (int64_t t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (int)((t / ntl) * BM), n0 = (int)((t % ntl) * BN);
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int st = (int)(g % STAGES);
+          if (g >= STAGES && !mbar_wait(&empty[st], (uint32_t)(((g / STAGES) - 1) & 1))) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], STAGE_BYTES);
+          tma_load_2d(smem + st * STAGE_BYTES, &tma_a, &full[st], kt * BK, m0);
+          tma_load_2d(smem + st * STAGE_BYTES + A_BYTES, &tma_b, &full[st], kt * BK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int64_t g = 0;
+      int i = 0;  // tiles of this CTA
+      for (int64_t t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait(&acc_empty[b], (uint32_t)(((i >> 1) - 1) & 1))) {
+          *abort_flag = 1;
+          break;
+        }
+        fence_after_sync();
+        const uint32_t d = tmem + (uint32_t)(b * ACC_COLS);
+        bool ok = true;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int st = (int)(g % STAGES);
+          if (!mbar_wait(&full[st], (uint32_t)((g / STAGES) & 1))) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint32_t a0 = smem_u32(smem + st * STAGE_BYTES);
+          const uint64_t ad = sw128_desc(a0), bd = sw128_desc(a0 + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) umma_f16(d, ad + 2 * k, bd + 2 * k, IDESC, (kt | k) != 0);
+          umma_commit(&empty[st]);
+        }
+        umma_commit(&acc_full[b]);
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+  } else {
+    // epilogue warps 2..9: TMEM lane quarter (warp % 4) holds accumulator rows
+    // 32 (warp % 4) ..; warps 2-5 take columns 0..127, warps 6-9 128..255
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    int i = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      if (!mbar_wait(&acc_full[b], (uint32_t)((i >> 1) & 1)) || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      const int64_t m = (t / ntl) * BM + q * 32 + lane, n0 = (t % ntl) * BN + half * (BN / 2);
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * ACC_COLS + half * (BN / 2));
+#pragma unroll 1
+      for (int c = 0; c < BN / 2; c += 32) {
+        float v[32];
+        tmem_ld32(base + (uint32_t)c, v);
+        const int64_t n = n0 + c;
+        if (m < M && n < N) {
+          if (vec && n + 32 <= N) {
+            epi.chunk32(m, n, v);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2)
+              if (n + j < N) epi(m, n + j, v[j], v[j + 1]);
+          }
+        }
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  __syncwarp();
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_tc05_error, (int)WALSH_ERR_TIMEOUT);
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda needed).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// Row-major [rows, K] 16-bit matrix, boxes of 64 (K) x box_rows, 128B swizzle.
+static bool make_operand_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows, int K, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)octo_tc::BK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 1 when the tcgen05 path ran, 0 when it does not apply (caller falls back),
+// negative on a launch error.
+template <typename TA, class Epi>
+static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int64_t N, const Epi& epi,
+                            cudaStream_t s) {
+  using namespace octo_tc;
+  if (M < 1 || M > 2147483647LL || N > 2147483647LL) return 0;
+  constexpr bool BF = std::is_same<TA, __nv_bfloat16>::value;
+  CUtensorMap ma, mb;
+  if (!make_operand_map(&ma, a, BF, M, K, BM) || !make_operand_map(&mb, w, BF, N, K, BN)) return 0;
+  auto kern = octo_gemm_tc05_kernel<TA, Epi>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    return launch_status();
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                   cudaSuccess)
+      sms = 148;
+  }
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+  kern<<<grid, NTHREADS, SMEM, s>>>(ma, mb, M, K, N, epi, epi.vec_ok() ? 1 : 0);
+  const int st = launch_status();
+  return st == WALSH_OK ? 1 : st;
+}
+
 template <typename TA, class Epi>
 static int launch_octo(const void* a, int64_t M, int K, const void* whi, const void* wlo, int64_t N, const Epi& epi,
                        cudaStream_t s) {
   using namespace octo;
+  if constexpr (!std::is_same<TA, float>::value) {
+    if (!wlo && octo_tc05_enabled()) {
+      const int r = launch_octo_tc05<TA>(a, M, K, whi, N, epi, s);
+      if (r != 0) return r > 0 ? WALSH_OK : r;
+    }
+  }
   auto kern = octo_gemm_kernel<TA, Epi>;
   const int smem = smem_bytes<TA>();
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -382,4 +746,23 @@ extern "C" walsh_status walsh_octo_post_fwd(const void* a, int dtype, int64_t M,
       launch_octo<TA>(a, M, K, w_hi, w_lo, C,
                       octo::EpiPost<__nv_bfloat16>{scale, (const __nv_bfloat16*)x, hmix, (__nv_bfloat16*)x_out, C},
                       s));
+}
+
+extern "C" int walsh_octo_set_mainloop(int tcgen05) {
+  const int prev = g_octo_tc05;
+  g_octo_tc05 = tcgen05 ? 1 : 0;
+  return prev;
+}
+
+extern "C" int walsh_tc05_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tc05_error, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return WALSH_ERR_LAUNCH;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_tc05_error, &zero, sizeof(int));
+  }
+  return v;
 }
