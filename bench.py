@@ -43,6 +43,7 @@ METRIC = "Walsh-512 prefill tokens/s"
 UNIT = "tokens/s"
 CPU_SAMPLE = (1, 1024)  # oracle sample per step: B1 x T1024
 DECODE_BATCH, DECODE_CTX = 256, 1024
+ATTN_TRAFFIC_B64 = 252.96e6  # ncu DRAM bytes of one prefill attention launch at B64 x T1024
 
 
 def peaks():
@@ -521,10 +522,11 @@ def dominant_kernel_roofline(model, idx, B, T, dev):
     from walsh_research_b200 import ops
     H, C = CONFIG["n_head"], CONFIG["n_embd"]
     hd = C // H
-    q = torch.randn((B, H, T, hd), device=dev).to(torch.bfloat16)
-    k = torch.randn((B, H, T, hd), device=dev).to(torch.bfloat16)
-    v = torch.randn((B, H, T, hd), device=dev).to(torch.bfloat16)
-    o = torch.empty((B, T, H, hd), device=dev, dtype=torch.bfloat16)
+    # the model's attention operands in 16-bit mode are fp16
+    q = torch.randn((B, H, T, hd), device=dev).to(torch.float16)
+    k = torch.randn((B, H, T, hd), device=dev).to(torch.float16)
+    v = torch.randn((B, H, T, hd), device=dev).to(torch.float16)
+    o = torch.empty((B, T, H, hd), device=dev, dtype=torch.float16)
     for _ in range(3):
         ops.attention(q, k, v, 0, out=o)
     n = 10
@@ -539,9 +541,13 @@ def dominant_kernel_roofline(model, idx, B, T, dev):
     flops = 4.0 * B * H * hd * (T * (T + 1) / 2)
     hbm, tflops, src = peaks()
     achieved = flops / sec / 1e12
-    return {"kernel": "walsh_attn_fwd (prefill, causal, hd16, bf16)", "bound": "tensor", "achieved": achieved,
-            "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops, "traffic": None,
-            "launch_ms": sec * 1e3, "peak_source": src}
+    # DRAM bytes read + written by one launch of this kernel at B64 x T1024, from one ncu
+    # capture (dram__bytes_read.sum 201.34 MB + dram__bytes_write.sum 51.61 MB)
+    traffic = ATTN_TRAFFIC_B64 * B / 64 if T == SEQ else None
+    return {"kernel": "walsh_attn_fwd (prefill, causal, hd16, fp16)", "bound": "tensor", "achieved": achieved,
+            "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops, "traffic": traffic,
+            "traffic_unit": "bytes per launch", "algorithmic_bytes": 4 * B * H * T * hd * 2,
+            "flops_per_launch": flops, "launch_ms": sec * 1e3, "peak_source": src}
 
 
 if __name__ == "__main__":
