@@ -183,16 +183,25 @@ walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const void* wmix
  * mparams: float [28] = {a_pre, a_post, a_res, unused, b_pre[4], b_post[4],
  * b_res[16]}.  phi_lp (optional, may be NULL): a copy of phi in x's 16-bit
  * type (bfloat16 for bf16 x, float16 for fp16 x); with it, a 16-bit x selects
- * the tensor-core kernel (C = 512 or 2048).  u is written in u_dtype (the
+ * the tensor-core kernel (C = 512 or 2048).  phi_frag (optional): phi_lp
+ * rearranged into mma.sync B-fragment order, [4C/16 k-steps][32 lanes][3
+ * n-tiles][2 regs] of packed 16-bit pairs (element (n, k) with n = 8 nt + lane/4,
+ * k = 16 ks + 8 reg + 2 (lane%4) + {0,1}); with it, C = 512 and 16-bit x/u select
+ * the single-pass kernel that reads x once (TMA).  u is written in u_dtype (the
  * model's 16-bit mode writes fp16).  Writes u [ntok, C] and hmix float [ntok, 24] =
  * {H_pre[4], H_post[4], H_res[16] row-major}.
  * Replaces ResidualStreamMapping.forward x3 and the pre-mix of
  * mHCResidualStream.forward (src/model/mhc.py:283-318, 345-364) plus the
  * attention_norm / ffn_norm RMSNorm of mHCLlamaBlock (src/model/mhc.py:514-523). */
 walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
-                           const void* phi_lp, const float* mparams, float map_eps,
-                           const float* norm_w, float norm_eps, void* u, int u_dtype, float* hmix,
-                           void* stream);
+                           const void* phi_lp, const void* phi_frag, const float* mparams,
+                           float map_eps, const float* norm_w, float norm_eps, void* u, int u_dtype,
+                           float* hmix, void* stream);
+
+/* Status word of the single-pass map kernel's bounded TMA wait (0 or
+ * WALSH_ERR_TIMEOUT); synchronous read, reset != 0 clears it.  No counterpart
+ * in the reference. */
+int walsh_map_error(int reset);
 
 /* Site epilogue: x_out[i] = sum_j H_res[i][j] x[j] + H_post[i] f for each
  * token (x, x_out: [ntok, 4, C]; f: [ntok, C]; x_out may alias x).

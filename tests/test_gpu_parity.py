@@ -164,10 +164,14 @@ def test_stream_mapping():
 
 
 @pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
-def test_tensor_core_mapping_vs_oracle(xdt):
-    """The tensor-core site prologue (chosen from 9472 tokens up) for either
-    16-bit stream type: H_pre/H_post/H_res vs the oracle on the same rounded
-    stream values, and the pre-mixed, normed u."""
+@pytest.mark.parametrize("kernel,ntok", [("two_pass", 10000), ("single_pass", 9000), ("single_pass", 37)])
+def test_tensor_core_mapping_vs_oracle(xdt, kernel, ntok):
+    """The tensor-core site prologues for either 16-bit stream type: the
+    two-pass kernel (chosen from 9472 tokens up) and the single-pass TMA
+    kernel (phi in fragment order; below 9472 tokens, ragged last tile):
+    H_pre/H_post/H_res vs the oracle on the same rounded stream values, and
+    the pre-mixed, normed u."""
+    from walsh_research_b200 import _lib
     from walsh_research_b200 import ops
     from walsh_research_b200.model.mhc import MAP_EPS, ResidualStreamMapping, mHCResidualStream, site_params
     rng = np.random.default_rng(41)
@@ -178,11 +182,14 @@ def test_tensor_core_mapping_vs_oracle(xdt):
             m.alpha.fill_(0.7)
             m.bias.copy_(torch.from_numpy(rng.normal(0, 0.5, tuple(m.bias.shape)).astype(np.float32)))
     st = st.to(DEV)
-    ntok = 10000
     x = T(rng.normal(size=(ntok, 4, 512)).astype(np.float32) * 3, xdt)
     nw = T((1 + 0.1 * rng.normal(size=512)).astype(np.float32))
-    phi, mp, phil = site_params(st, xdt)
-    u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, nw, 1e-6, phi_lp=phil, u_dtype=torch.float16)
+    phi, mp, phil, phif = site_params(st, xdt)
+    _lib.call("walsh_map_error", 1)
+    u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, nw, 1e-6, phi_lp=phil, u_dtype=torch.float16,
+                          phi_frag=phif if kernel == "single_pass" else None)
+    torch.cuda.synchronize()
+    assert _lib.call("walsh_map_error", 1) == 0
     xf = x.float().cpu().numpy().astype(np.float64).reshape(1, ntok, 4 * 512)
     p = {k: v.detach().cpu().numpy() for k, v in st.state_dict().items()}
     hp = O.stream_mapping(xf, p["H_pre.phi.weight"], p["H_pre.alpha"], p["H_pre.bias"], "pre")

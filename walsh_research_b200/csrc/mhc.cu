@@ -11,6 +11,8 @@
 
 #include "common.cuh"
 #include "mma.cuh"
+#include "tc05.cuh"
+#include "tma_host.cuh"
 
 namespace walsh {
 
@@ -297,6 +299,167 @@ mhc_map_mma_kernel(const TX* __restrict__ x, int64_t ntok, const TX* __restrict_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Single-pass site prologue for C = 512 (16-bit x): 16 tokens per CTA, their
+// whole stream rows (16 x 2048 x 2 B = 64 KB) loaded once by TMA into shared
+// memory (32 boxes of 64 columns x 16 rows, 128-byte swizzle), then
+//   1. the 8 warps split the 2048 columns (256 each): sum of squares and the
+//      24 projections on the tensor cores, A = x from shared memory through
+//      ldmatrix, B = phi pre-arranged in MMA-fragment order and read from L2;
+//   2. one thread per token adds the 8 partials, applies the RMS scale,
+//      sigmoid / 2 sigmoid / Sinkhorn and writes hmix;
+//   3. the pre-mix u = sum_j H_pre[j] x_j and the block RMSNorm from shared
+//      memory, two tokens per warp.
+// x is read from HBM once (the two-pass kernel reads it twice).
+// ---------------------------------------------------------------------------
+namespace map_tma {
+constexpr int TOK = 16, NW = 8, D = 2048, BOXC = 64, NBOX = D / BOXC;
+constexpr int BOX_BYTES = TOK * BOXC * 2;  // 2 KB
+constexpr int X_BYTES = NBOX * BOX_BYTES;  // 64 KB
+constexpr int RED_FLOATS = NW * TOK * (kMapRows + 1);
+constexpr int SMEM = X_BYTES + RED_FLOATS * 4 + TOK * kMapRows * 4 + 1024 + 64;
+}  // namespace map_tma
+
+// Shared-memory address of x[row][col] in the swizzled box layout.
+__device__ __forceinline__ uint32_t map_tma_off(int row, int col) {
+  const int b = col >> 6, ch = (col & 63) >> 3;
+  return (uint32_t)(b * map_tma::BOX_BYTES + row * 128 + ((ch ^ (row & 7)) << 4) + ((col & 7) << 1));
+}
+
+__device__ int g_map_tma_error;
+
+template <typename TX, typename TU>
+__global__ void __launch_bounds__(256, 2)
+mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const uint2* __restrict__ phif,
+                   const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
+                   TU* __restrict__ u, float* __restrict__ hmix) {
+  using namespace map_tma;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* xs = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  float* red = reinterpret_cast<float*>(xs + X_BYTES);  // [NW][TOK][25]
+  float* hc = red + RED_FLOATS;                         // [TOK][24]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(hc + TOK * kMapRows);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int64_t tok0 = (int64_t)blockIdx.x * TOK;
+  if (tid == 0) {
+    tc05::mbar_init(bar, 1);
+    tc05::fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    tc05::prefetch_tensormap(&tmx);
+    tc05::mbar_arrive_expect_tx(bar, X_BYTES);
+    for (int b = 0; b < NBOX; ++b) tc05::tma_load_2d(xs + b * BOX_BYTES, &tmx, bar, b * BOXC, (int)tok0);
+  }
+  if (!tc05::mbar_wait(bar, 0)) {
+    if (tid == 0) atomicExch(&g_map_tma_error, (int)WALSH_ERR_TIMEOUT);
+    return;
+  }
+  // 1. partial projections over this warp's 256 columns
+  float acc[3][4];
+#pragma unroll
+  for (int n = 0; n < 3; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  float ss_lo = 0.f, ss_hi = 0.f;
+  const uint32_t xbase = tc05::smem_u32(xs);
+#pragma unroll 4
+  for (int ks = warp * 16; ks < warp * 16 + 16; ++ks) {
+    const int r = lane & 15, col = ks * 16 + (lane >> 4) * 8;
+    uint32_t a[4];
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                 : "r"(xbase + map_tma_off(r, col)));
+    const uint2* fp = phif + ((size_t)ks * 32 + lane) * 3;
+    const uint2 f0 = __ldg(fp), f1 = __ldg(fp + 1), f2 = __ldg(fp + 2);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 v = unpack2<TX>(a[q]);
+      if (q & 1) ss_hi = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_hi));
+      else ss_lo = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_lo));
+    }
+    mma16<TX>(acc[0], a, f0.x, f0.y);
+    mma16<TX>(acc[1], a, f1.x, f1.y);
+    mma16<TX>(acc[2], a, f2.x, f2.y);
+  }
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    ss_lo += __shfl_xor_sync(0xffffffffu, ss_lo, off);
+    ss_hi += __shfl_xor_sync(0xffffffffu, ss_hi, off);
+  }
+  float* rw = red + warp * TOK * (kMapRows + 1);
+#pragma unroll
+  for (int n = 0; n < 3; ++n) {
+    rw[g * (kMapRows + 1) + 8 * n + 2 * t4] = acc[n][0];
+    rw[g * (kMapRows + 1) + 8 * n + 2 * t4 + 1] = acc[n][1];
+    rw[(g + 8) * (kMapRows + 1) + 8 * n + 2 * t4] = acc[n][2];
+    rw[(g + 8) * (kMapRows + 1) + 8 * n + 2 * t4 + 1] = acc[n][3];
+  }
+  if (t4 == 0) {
+    rw[g * (kMapRows + 1) + kMapRows] = ss_lo;
+    rw[(g + 8) * (kMapRows + 1) + kMapRows] = ss_hi;
+  }
+  __syncthreads();
+  // 2. one thread per token
+  if (tid < TOK) {
+    float d[kMapRows], hm[kMapRows], ssum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) d[r] = 0.f;
+    for (int w = 0; w < NW; ++w) {
+      const float* src = red + (w * TOK + tid) * (kMapRows + 1);
+#pragma unroll
+      for (int r = 0; r < kMapRows; ++r) d[r] += src[r];
+      ssum += src[kMapRows];
+    }
+    const float rms = rsqrtf(ssum / (float)D + map_eps);
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) d[r] *= rms;
+    map_activations(d, mp, hm);
+#pragma unroll
+    for (int r = 0; r < kMapRows; ++r) hc[tid * kMapRows + r] = hm[r];
+    if (tok0 + tid < ntok) {
+#pragma unroll
+      for (int r = 0; r < kMapRows; ++r) hmix[(tok0 + tid) * kMapRows + r] = hm[r];
+    }
+  }
+  __syncthreads();
+  // 3. pre-mix and RMSNorm: warp w takes tokens 2w, 2w + 1; lane covers 16 columns
+  constexpr int C = D / 4;
+#pragma unroll 1
+  for (int tt = 0; tt < 2; ++tt) {
+    const int t = warp * 2 + tt;
+    const int64_t tok = tok0 + t;
+    if (tok >= ntok) break;
+    const float h0 = hc[t * kMapRows], h1 = hc[t * kMapRows + 1], h2 = hc[t * kMapRows + 2],
+                h3 = hc[t * kMapRows + 3];
+    float uv[2][8];
+    float s2 = 0.f;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const int c = (lane + 32 * v) * 8;
+      float f[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 q = *reinterpret_cast<const uint4*>(xs + map_tma_off(t, j * C + c));
+        unpack8(q, f[j], (const TX*)nullptr);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        uv[v][e] = ((h0 * f[0][e] + h1 * f[1][e]) + h2 * f[2][e]) + h3 * f[3][e];
+        s2 = fmaf(uv[v][e], uv[v][e], s2);
+      }
+    }
+    s2 = warp_sum(s2);
+    const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const int c = (lane + 32 * v) * 8;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = uv[v][e] * rn * (norm_w ? __ldg(norm_w + c + e) : 1.f);
+      store8(u + tok * C + c, o);
+    }
+  }
+}
+
 template <typename T>
 __global__ void mhc_post_kernel(const T* x, const T* __restrict__ f, const float* __restrict__ hmix, int64_t ntok,
                                 int C, T* xo) {
@@ -348,10 +511,27 @@ static inline int grid_for(int64_t total, int threads) {
 
 using namespace walsh;
 
+// Single-pass TMA kernel launch; 1 = ran, 0 = not applicable, < 0 = error.
+template <typename TX, typename TU>
+static int launch_map_tma(const void* x, int64_t ntok, const void* phi_frag, const float* mp, float map_eps,
+                          const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s) {
+  using namespace map_tma;
+  if (ntok > 2147483647LL) return 0;
+  CUtensorMap m;
+  if (!make_tile_map(&m, x, std::is_same<TX, __nv_bfloat16>::value, ntok, D, BOXC, TOK)) return 0;
+  auto kern = mhc_map_tma_kernel<TX, TU>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    return launch_status();
+  kern<<<(unsigned)((ntok + TOK - 1) / TOK), 256, SMEM, s>>>(m, ntok, (const uint2*)phi_frag, mp, map_eps, norm_w,
+                                                             norm_eps, (TU*)u, hmix);
+  const int st = launch_status();
+  return st == WALSH_OK ? 1 : st;
+}
+
 extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
-                                      const void* phi_lp, const float* mparams, float map_eps,
-                                      const float* norm_w, float norm_eps, void* u, int u_dtype, float* hmix,
-                                      void* stream) {
+                                      const void* phi_lp, const void* phi_frag, const float* mparams,
+                                      float map_eps, const float* norm_w, float norm_eps, void* u, int u_dtype,
+                                      float* hmix, void* stream) {
   if (int e = injected("mhc_map")) return e;
   WALSH_CHECK_DTYPE(dtype);
   WALSH_CHECK_DTYPE(u_dtype);
@@ -359,10 +539,28 @@ extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, in
   WALSH_CHECK_SHAPE(ntok >= 0 && C > 0 && C % 32 == 0 && C <= 8192);
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_lp)) & 15u) == 0;
-  // the tensor-core kernel takes 128 tokens per CTA: below about a wave of
-  // those (decode steps), the warp-per-token kernel spreads over more SMs
+  // single-pass kernel: 16 tokens per CTA, latency-bound on its Sinkhorn and
+  // load chains, so it wins at decode token counts; prefill-sized calls take
+  // the 128-token two-pass kernel below
   const bool many = ntok >= 148 * 64;
+  if (!many && phi_frag && C == 512 && (dtype == WALSH_BF16 || dtype == WALSH_F16) && u_dtype != WALSH_F32 &&
+      ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_frag)) & 15u) == 0) {
+    int r;
+    if (dtype == WALSH_BF16)
+      r = u_dtype == WALSH_F16 ? launch_map_tma<__nv_bfloat16, __half>(x, ntok, phi_frag, mparams, map_eps, norm_w,
+                                                                       norm_eps, u, hmix, s)
+                               : launch_map_tma<__nv_bfloat16, __nv_bfloat16>(x, ntok, phi_frag, mparams, map_eps,
+                                                                              norm_w, norm_eps, u, hmix, s);
+    else
+      r = u_dtype == WALSH_F16 ? launch_map_tma<__half, __half>(x, ntok, phi_frag, mparams, map_eps, norm_w,
+                                                                norm_eps, u, hmix, s)
+                               : launch_map_tma<__half, __nv_bfloat16>(x, ntok, phi_frag, mparams, map_eps, norm_w,
+                                                                       norm_eps, u, hmix, s);
+    if (r != 0) return r > 0 ? WALSH_OK : r;
+  }
+  const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_lp)) & 15u) == 0;
+  // the two-pass tensor-core kernel takes 128 tokens per CTA: below about a
+  // wave of those (decode steps), the warp-per-token kernel spreads wider
   if (many && (dtype == WALSH_BF16 || dtype == WALSH_F16) && u_dtype != WALSH_F32 && phi_lp && vec_ok &&
       (C == 512 || C == 2048)) {
     const unsigned grid = (unsigned)((ntok + map_tc::TOK - 1) / map_tc::TOK);
@@ -414,4 +612,17 @@ extern "C" walsh_status walsh_sinkhorn(const float* h, int64_t n, int iters, flo
   if (n == 0) return WALSH_OK;
   sinkhorn_kernel<<<grid_for(n, 128), 128, 0, (cudaStream_t)stream>>>(h, n, iters, eps, out);
   return launch_status();
+}
+
+extern "C" int walsh_map_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_map_tma_error, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return WALSH_ERR_LAUNCH;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_map_tma_error, &zero, sizeof(int));
+  }
+  return v;
 }

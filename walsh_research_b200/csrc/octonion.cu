@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "mma.cuh"
 #include "tc05.cuh"
+#include "tma_host.cuh"
 
 namespace walsh {
 
@@ -572,37 +573,6 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
-// against libcuda needed).
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    else
-      cudaGetLastError();
-  });
-  return fn;
-}
-
-// Row-major [rows, K] 16-bit matrix, boxes of 64 (K) x box_rows, 128B swizzle.
-static bool make_operand_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows, int K, int box_rows) {
-  auto enc = tensor_map_encoder();
-  if (!enc) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)octo_tc::BK, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // 1 when the tcgen05 path ran, 0 when it does not apply (caller falls back),
 // negative on a launch error.
 template <typename TA, class Epi>
@@ -612,7 +582,7 @@ static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int6
   if (M < 1 || M > 2147483647LL || N > 2147483647LL) return 0;
   constexpr bool BF = std::is_same<TA, __nv_bfloat16>::value;
   CUtensorMap ma, mb;
-  if (!make_operand_map(&ma, a, BF, M, K, BM) || !make_operand_map(&mb, w, BF, N, K, BN)) return 0;
+  if (!make_tile_map(&ma, a, BF, M, K, octo_tc::BK, BM) || !make_tile_map(&mb, w, BF, N, K, octo_tc::BK, BN)) return 0;
   auto kern = octo_gemm_tc05_kernel<TA, Epi>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
     return launch_status();

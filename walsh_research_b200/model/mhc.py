@@ -85,12 +85,13 @@ def site_params(stream: "mHCResidualStream", dtype=torch.bfloat16):
     def build():
         phi = torch.cat([pre.phi.weight, post.phi.weight, res.phi.weight]).detach().float().contiguous()
         phi_lp = phi.to(dtype if dtype != torch.float32 else torch.bfloat16).contiguous()
+        phi_frag = ops.phi_fragments(phi_lp) if phi_lp.shape[1] % 16 == 0 else None
         dev = phi.device
         mp = torch.cat([torch.stack([pre.alpha, post.alpha, res.alpha]).detach().float().reshape(3),
                         torch.zeros(1, device=dev),
                         pre.bias.detach().float().reshape(-1), post.bias.detach().float().reshape(-1),
                         res.bias.detach().float().reshape(-1)]).contiguous()
-        return phi, mp, phi_lp
+        return phi, mp, phi_lp, phi_frag
     srcs = [pre.phi.weight, post.phi.weight, res.phi.weight, pre.alpha, post.alpha, res.alpha,
             pre.bias, post.bias, res.bias]
     return _prep.cached(stream, f"site_{dtype}", srcs, build)
@@ -108,8 +109,8 @@ class mHCResidualStream(nn.Module):
         self.H_res = ResidualStreamMapping(n_embd, n_streams, "res")
 
     def forward(self, x, layer_fn):
-        phi, mp, phib = site_params(self, x.dtype)
-        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, phi_lp=phib)
+        phi, mp, phib, phif = site_params(self, x.dtype)
+        u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, phi_lp=phib, phi_frag=phif)
         return ops.mhc_post(x, layer_fn(u), hmix)
 
 
@@ -149,13 +150,14 @@ class mHCLlamaBlock(nn.Module):
         B, T, n, C = x.shape
         idt = k_cache.dtype  # storage type of u, q/k/v and the attention output
         # attention site
-        phi, mp, phib = site_params(self.attn_stream, x.dtype)
+        phi, mp, phib, phif = site_params(self.attn_stream, x.dtype)
         u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.attention_norm.weight), self.attention_norm.eps,
-                              phi_lp=phib, u_dtype=idt)
+                              phi_lp=phib, u_dtype=idt, phi_frag=phif)
         self.attention.forward_site(u, rope_cos, rope_sin, k_cache, v_cache, start_pos, x, hmix)
         # ffn site
-        phi, mp, phib = site_params(self.ffn_stream, x.dtype)
+        phi, mp, phib, phif = site_params(self.ffn_stream, x.dtype)
         u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, self._w(self.ffn_norm.weight), self.ffn_norm.eps, phi_lp=phib,
+                              phi_frag=phif,
                               u_dtype=idt)
         ff = self.feed_forward
         if hasattr(ff, "kernel_args"):

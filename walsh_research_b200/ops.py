@@ -103,9 +103,17 @@ def head_mixer_tokens(x, W, beta, out=None):
 # mHC
 # ---------------------------------------------------------------------------
 
-def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6, phi_lp=None, u_dtype=None):
+def phi_fragments(phi_lp):
+    """phi [24, D] (16-bit) in mma.sync B-fragment order: [D/16, 32 lanes, 6 regs, 2]."""
+    D = phi_lp.shape[1]
+    return (phi_lp.reshape(3, 8, D // 16, 2, 4, 2).permute(2, 1, 4, 0, 3, 5)
+            .reshape(D // 16, 32, 6, 2).contiguous())
+
+
+def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6, phi_lp=None, u_dtype=None, phi_frag=None):
     """x [..., 4, C] -> (u [..., C] in u_dtype (default x's), hmix float [..., 24]).
-    ``phi_lp`` (phi in x's 16-bit dtype) enables the tensor-core kernel for 16-bit x."""
+    ``phi_lp`` (phi in x's 16-bit dtype) enables the tensor-core kernels for 16-bit
+    x; ``phi_frag`` (``phi_fragments(phi_lp)``) the single-pass one for C = 512."""
     require_cuda(x)
     x = _c(x)
     C = x.shape[-1]
@@ -115,8 +123,9 @@ def mhc_map(x, phi, mparams, map_eps, norm_w=None, norm_eps=1e-6, phi_lp=None, u
     u = torch.empty(lead + (C,), dtype=u_dtype, device=x.device)
     hmix = torch.empty(lead + (24,), dtype=torch.float32, device=x.device)
     if phi_lp is not None and phi_lp.dtype != x.dtype:
-        phi_lp = None
-    call("walsh_mhc_map", ptr(x), dcode(x.dtype), ntok, C, ptr(phi), ptr(phi_lp), ptr(mparams), float(map_eps),
+        phi_lp = phi_frag = None
+    call("walsh_mhc_map", ptr(x), dcode(x.dtype), ntok, C, ptr(phi), ptr(phi_lp), ptr(phi_frag), ptr(mparams),
+         float(map_eps),
          ptr(norm_w), float(norm_eps), ptr(u), dcode(u_dtype), ptr(hmix), stream())
     return u, hmix
 
