@@ -217,7 +217,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode measurement")
     ap.add_argument("--no-octonion", action="store_true", help="skip the config-2 octonion measurement")
-    ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode", "octonion"],
+    ap.add_argument("--no-micro", action="store_true", help="skip the config-1 HadamardLinear microbenchmark")
+    ap.add_argument("--no-2048", action="store_true", help="skip the config-4 Walsh-2048 decode measurement")
+    ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode", "octonion", "decode2048"],
                     help="run one warm-up and one eager forward only (for ncu launch lists)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -290,7 +292,7 @@ def main():
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
-        e_steps = max(3, args.steps // 2)
+        e_steps = max(3, args.steps)
         start.record()
         for _ in range(e_steps):
             idx_dev = idx_host.to(dev, non_blocking=True)
@@ -314,6 +316,8 @@ def main():
     torch.cuda.empty_cache()
     decode = None if args.no_decode else measure_decode(model, dev, args.steps, max(3, args.warmup), rank, world, dist)
     octo = None if args.no_octonion else measure_octonion(dev, args.steps, max(3, args.warmup), rank, world, dist)
+    micro = None if args.no_micro else measure_hlin_microbench(dev)
+    d2048 = None if args.no_2048 else measure_decode_2048(dev, args.steps, max(3, args.warmup), rank, world, dist)
 
     if dist:
         dist.barrier()
@@ -334,7 +338,7 @@ def main():
                        "batch_per_gpu": B, "seq_len": T, "parallelism": f"replicas x{world} (batch-sharded)",
                        "l2": "working set > L2 (stream state 268 MB per layer), no flush"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(), "decode": decode,
-            "octonion": octo,
+            "octonion": octo, "hlin_microbench": micro, "decode_2048": d2048,
             "gpu_launches": launches_per_forward * args.steps,
             "peaks": src}
     print(json.dumps(line), flush=True)
@@ -346,6 +350,27 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     model = build_model_cpu().to(dev).eval()
     model.compute_dtype = torch.bfloat16
+    if args.profile == "decode2048":
+        from walsh_research_b200.model import KVCache
+        model = build_walsh2048_cpu().to(dev).eval()
+        model.compute_dtype = torch.bfloat16
+        B, ctx = W2048_BATCH, W2048_CTX
+        H, C, L = W2048_CONFIG["n_head"], W2048_CONFIG["n_embd"], W2048_CONFIG["n_layer"]
+        kv = KVCache(L, ctx, H, C // H, dev, dtype=torch.float16, batch_size=B)
+        for t in kv.k_cache + kv.v_cache:
+            t.normal_()
+        ids = token_ids(B, 2, seed=13).to(dev)
+        with torch.no_grad():
+            kv.cached_len = ctx - 2
+            model(ids[:, :1], kv_cache=kv, start_pos=ctx - 2)
+            kv.cached_len = ctx - 1
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("walsh_forward")
+            model(ids[:, 1:], kv_cache=kv, start_pos=ctx - 1)
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.synchronize()
+        print("profile decode2048 step done", flush=True)
+        return
     if args.profile == "decode":
         from walsh_research_b200.model import KVCache
         B, ctx = DECODE_BATCH, DECODE_CTX
@@ -475,6 +500,87 @@ def measure_decode(model, dev, steps, warmup, rank=0, world=1, dist=None, B=None
             "gpu_launches": launches_per_step * steps}
 
 
+W2048_CONFIG = dict(CONFIG, block_size=2048, n_layer=24, n_head=64, n_embd=2048)
+W2048_BATCH, W2048_CTX = 256, 2048
+
+
+def build_walsh2048_cpu(seed=0):
+    """Config 4: Walsh-2048 (L24, H64, C2048, 64 experts top-6) with the seeded
+    recipe (ternary latents i.i.d. uniform {-1, 0, 1})."""
+    from walsh_research_b200.model import WalshConfig, mHCWalsh
+    torch.manual_seed(seed)
+    model = mHCWalsh(WalshConfig(**W2048_CONFIG), n_streams=N_STREAMS).eval()
+    g = torch.Generator().manual_seed(seed)
+    pat = re.compile(r"\.inner\.weight$|experts\.(gate|up|down)_weights$|channel_mod\.context_mlp\.\d\.weight$")
+    with torch.no_grad():
+        for name, p in sorted(model.named_parameters()):
+            if pat.search(name):
+                p.copy_(torch.randint(-1, 2, p.shape, generator=g).float())
+    return model
+
+
+def measure_decode_2048(dev, steps, warmup, rank=0, world=1, dist=None):
+    """Config 4: Walsh-2048 batched decode, B256 sequences at KV-cache positions
+    2048 - (warmup + steps) .. 2047.  The KV cache (24 layers x 2 x 256 x 64 x
+    2048 x 32 fp16 = 103 GB) is filled with seeded N(0, 1) values rather than
+    by a prefill: a decode step does the same work whatever the cached values.
+    One captured graph per position, as for the Walsh-512 decode line."""
+    from walsh_research_b200 import _lib
+    from walsh_research_b200.model import KVCache
+    B, ctx = W2048_BATCH, W2048_CTX
+    H, C, L = W2048_CONFIG["n_head"], W2048_CONFIG["n_embd"], W2048_CONFIG["n_layer"]
+    model = build_walsh2048_cpu().to(dev).eval()
+    model.compute_dtype = torch.bfloat16
+    n = warmup + steps
+    P = ctx - n
+    kv = KVCache(L, ctx, H, C // H, dev, dtype=torch.float16, batch_size=B)
+    gen = torch.Generator(device=dev).manual_seed(11 + rank)
+    for t in kv.k_cache + kv.v_cache:
+        t.normal_(generator=gen)
+    ids = token_ids(B, n, seed=13 + rank).to(dev)
+    kv.cached_len = P
+    with torch.no_grad():
+        model(ids[:, :1], kv_cache=kv, start_pos=P)   # eager warm-up (weight preparation)
+        torch.cuda.synchronize()
+        graphs, pool = [], None
+        n0 = _lib.launch_count
+        for i in range(n):
+            kv.cached_len = P + i
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                model(ids[:, i:i + 1], kv_cache=kv, start_pos=P + i)
+            pool = g.pool()
+            graphs.append(g)
+        launches = (_lib.launch_count - n0) // n
+        for i in range(warmup):
+            graphs[i].replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(warmup, n):
+            graphs[i].replay()
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / steps
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+    del graphs, kv, model
+    torch.cuda.empty_cache()
+    hbm, _, _ = peaks()
+    kv_read = L * 2 * B * H * ctx * (C // H) * 2
+    return {"metric": "Walsh-2048 decode tokens/s (config 4)", "value": world * B / (ms / 1e3), "unit": UNIT,
+            "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "config": {"workload": f"Walsh-2048 (L24 H64 C2048, 64 experts top-6) batched decode, B{B} per GPU, "
+                                   f"KV cache ctx {ctx} filled with seeded values", "batch_per_gpu": B,
+                       "ctx": ctx, "kv_cache_bytes": kv_read, "l2": "KV cache 103 GB > L2, no flush"},
+            "kv_read_floor_ms": kv_read / (hbm * 1e9) * 1e3,
+            "gpu_launches": launches * steps}
+
+
 def measure_octonion(dev, steps, warmup, rank=0, world=1, dist=None):
     """Config 2 prefill (octonion Walsh-512, B32 x T1024 per GPU): graph
     replays of the forward with the ids resident in HBM, as for config 3."""
@@ -515,6 +621,49 @@ def measure_octonion(dev, steps, warmup, rank=0, world=1, dist=None):
             "config": {"workload": "config 2: octonion Walsh-512 (SwiGLU 1368, head mixing, chmod) prefill",
                        "batch_per_gpu": B, "seq_len": T, "l2": "stream state 134 MB per layer > L2, no flush"},
             "gpu_launches": launches * steps}
+
+
+def measure_hlin_microbench(dev, iters=20):
+    """Config 1: HadamardLinear(n, n) on bf16 activations [T, n] (N(0, 1)), ternary
+    weights i.i.d. uniform {-1, 0, 1}, alpha ~ U(0.5, 1.5), beta at the reference
+    init.  Each entry times `iters` calls through the module's forward with CUDA
+    events, cycling over enough input/output buffers that one pass over them
+    exceeds L2 (no flush needed).  Algorithmic bytes per call:
+    T (32 in_o + 32 out_o) 2 + 32 out_o ceil(in_o / 4) + 4 * 32 (in_o + out_o)."""
+    from walsh_research_b200.model.fht_cuda import HadamardLinear
+    hbm, _, _ = peaks()
+    g = torch.Generator().manual_seed(0)
+    out = []
+    for n in (512, 2048):
+        lin = HadamardLinear(n, n)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randint(-1, 2, lin.weight.shape, generator=g).float())
+            lin.alpha.copy_(torch.rand(lin.alpha.shape, generator=g) + 0.5)
+        lin = lin.to(dev)
+        in_o = out_o = n // 32
+        for T in (1, 64, 4096, 65536):
+            nbuf = max(1, min(8, int(256e6 // (T * n * 2 * 2)) + 1))
+            xs = [torch.randn((T, n), generator=g).to(dev, torch.bfloat16) for _ in range(nbuf)]
+            with torch.no_grad():
+                for i in range(3):
+                    lin(xs[i % nbuf])
+                torch.cuda.synchronize()
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                for i in range(iters):
+                    lin(xs[i % nbuf])
+                s1.record()
+                torch.cuda.synchronize()
+            sec = s0.elapsed_time(s1) / iters / 1e3
+            nbytes = T * (32 * in_o + 32 * out_o) * 2 + 32 * out_o * ((in_o + 3) // 4) + 4 * 32 * (in_o + out_o)
+            e = {"n": n, "T": T, "us": sec * 1e6, "GB/s": nbytes / sec / 1e9}
+            if T >= 4096:
+                e["roofline_frac"] = nbytes / sec / 1e9 / hbm
+            out.append(e)
+            del xs
+    torch.cuda.empty_cache()
+    return {"metric": "HadamardLinear latency / HBM roofline (config 1)", "dtype": "bf16 in/out, fp32 accumulate",
+            "peak_GBs": hbm, "entries": out}
 
 
 def dominant_kernel_roofline(model, idx, B, T, dev):

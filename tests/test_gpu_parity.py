@@ -164,8 +164,9 @@ def test_stream_mapping():
 
 
 @pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("kernel,ntok", [("two_pass", 10000), ("single_pass", 9000), ("single_pass", 37)])
-def test_tensor_core_mapping_vs_oracle(xdt, kernel, ntok):
+@pytest.mark.parametrize("kernel,ntok,C", [("two_pass", 10000, 512), ("single_pass", 9000, 512),
+                                           ("single_pass", 37, 512), ("single_pass", 37, 2048)])
+def test_tensor_core_mapping_vs_oracle(xdt, kernel, ntok, C):
     """The tensor-core site prologues for either 16-bit stream type: the
     two-pass kernel (chosen from 9472 tokens up) and the single-pass TMA
     kernel (phi in fragment order; below 9472 tokens, ragged last tile):
@@ -175,22 +176,22 @@ def test_tensor_core_mapping_vs_oracle(xdt, kernel, ntok):
     from walsh_research_b200 import ops
     from walsh_research_b200.model.mhc import MAP_EPS, ResidualStreamMapping, mHCResidualStream, site_params
     rng = np.random.default_rng(41)
-    st = mHCResidualStream(512, 4)
+    st = mHCResidualStream(C, 4)
     with torch.no_grad():
         for m in (st.H_pre, st.H_post, st.H_res):
             m.phi.weight.copy_(torch.from_numpy(rng.normal(0, 0.02, tuple(m.phi.weight.shape)).astype(np.float32)))
             m.alpha.fill_(0.7)
             m.bias.copy_(torch.from_numpy(rng.normal(0, 0.5, tuple(m.bias.shape)).astype(np.float32)))
     st = st.to(DEV)
-    x = T(rng.normal(size=(ntok, 4, 512)).astype(np.float32) * 3, xdt)
-    nw = T((1 + 0.1 * rng.normal(size=512)).astype(np.float32))
+    x = T(rng.normal(size=(ntok, 4, C)).astype(np.float32) * 3, xdt)
+    nw = T((1 + 0.1 * rng.normal(size=C)).astype(np.float32))
     phi, mp, phil, phif = site_params(st, xdt)
     _lib.call("walsh_map_error", 1)
     u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, nw, 1e-6, phi_lp=phil, u_dtype=torch.float16,
                           phi_frag=phif if kernel == "single_pass" else None)
     torch.cuda.synchronize()
     assert _lib.call("walsh_map_error", 1) == 0
-    xf = x.float().cpu().numpy().astype(np.float64).reshape(1, ntok, 4 * 512)
+    xf = x.float().cpu().numpy().astype(np.float64).reshape(1, ntok, 4 * C)
     p = {k: v.detach().cpu().numpy() for k, v in st.state_dict().items()}
     hp = O.stream_mapping(xf, p["H_pre.phi.weight"], p["H_pre.alpha"], p["H_pre.bias"], "pre")
     ho = O.stream_mapping(xf, p["H_post.phi.weight"], p["H_post.alpha"], p["H_post.bias"], "post")
@@ -384,6 +385,12 @@ def _bf16_model_check(name, idx=None, cfg_override=None):
 
 def test_model_bf16_matches_reference():
     _bf16_model_check("model_h512")
+
+
+def test_model_bf16_walsh2048():
+    """C = 2048 (64 heads of 32, 64 experts) in 16-bit mode: the CUDA-core
+    q/k/v, MoE and mapping kernels and the hd-32 attention."""
+    _bf16_model_check("model_h2048")
 
 
 def test_model_bf16_larger_batch():

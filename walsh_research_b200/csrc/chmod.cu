@@ -164,18 +164,42 @@ chmod_mlp_kernel(const float* __restrict__ partial, int nseg, int nch, int seg_l
   __syncthreads();
   const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
   const int kb1 = C / 4;
+  // rows of kb1 = C/4 bytes are read 16 bytes at a time (C % 64 == 0), several
+  // loads in flight; the per-segment accumulation order is byte by byte as before
+  const bool vec1 = (kb1 & 15) == 0 && (((uintptr_t)w1) & 15u) == 0;
   for (int j = threadIdx.x; j < HIDN; j += 256) {
     const uint8_t* row = w1 + (size_t)j * kb1;
     float acc[SPB];
 #pragma unroll
     for (int z = 0; z < SPB; ++z) acc[z] = 0.f;
-    for (int b = 0; b < kb1; ++b) {
-      const uint32_t byte = __ldg(row + b);
+    if (vec1) {
+#pragma unroll 4
+      for (int b16 = 0; b16 < kb1; b16 += 16) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(row + b16));
+        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float w = tern_val(byte, q);
+        for (int wi = 0; wi < 4; ++wi)
 #pragma unroll
-        for (int z = 0; z < SPB; ++z) acc[z] = fmaf(w, bulk[z * C + 4 * b + q], acc[z]);
+          for (int bb = 0; bb < 4; ++bb) {
+            const uint32_t byte = (words[wi] >> (8 * bb)) & 0xffu;
+            const int b = b16 + 4 * wi + bb;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float w = tern_val(byte, q);
+#pragma unroll
+              for (int z = 0; z < SPB; ++z) acc[z] = fmaf(w, bulk[z * C + 4 * b + q], acc[z]);
+            }
+          }
+      }
+    } else {
+      for (int b = 0; b < kb1; ++b) {
+        const uint32_t byte = __ldg(row + b);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float w = tern_val(byte, q);
+#pragma unroll
+          for (int z = 0; z < SPB; ++z) acc[z] = fmaf(w, bulk[z * C + 4 * b + q], acc[z]);
+        }
       }
     }
 #pragma unroll
@@ -192,6 +216,7 @@ chmod_mlp_kernel(const float* __restrict__ partial, int nseg, int nch, int seg_l
     float acc[SPB];
 #pragma unroll
     for (int z = 0; z < SPB; ++z) acc[z] = 0.f;
+#pragma unroll 8
     for (int b = 0; b < kb2; ++b) {
       const uint32_t byte = __ldg(row + b);
 #pragma unroll

@@ -312,31 +312,36 @@ mhc_map_mma_kernel(const TX* __restrict__ x, int64_t ntok, const TX* __restrict_
 //      memory, two tokens per warp.
 // x is read from HBM once (the two-pass kernel reads it twice).
 // ---------------------------------------------------------------------------
-namespace map_tma {
-constexpr int TOK = 16, NW = 8, D = 2048, BOXC = 64, NBOX = D / BOXC;
-constexpr int BOX_BYTES = TOK * BOXC * 2;  // 2 KB
-constexpr int X_BYTES = NBOX * BOX_BYTES;  // 64 KB
-constexpr int RED_FLOATS = NW * TOK * (kMapRows + 1);
-constexpr int SMEM = X_BYTES + RED_FLOATS * 4 + TOK * kMapRows * 4 + 1024 + 64;
-}  // namespace map_tma
-
-// Shared-memory address of x[row][col] in the swizzled box layout.
-__device__ __forceinline__ uint32_t map_tma_off(int row, int col) {
-  const int b = col >> 6, ch = (col & 63) >> 3;
-  return (uint32_t)(b * map_tma::BOX_BYTES + row * 128 + ((ch ^ (row & 7)) << 4) + ((col & 7) << 1));
-}
+// C = 512: 16 tokens per CTA (64 KB of x); C = 2048: 8 tokens (128 KB; the
+// MMA's rows 8..15 then read the next box and are discarded).
+template <int C>
+struct MapTma {
+  static constexpr int TOK = C == 512 ? 16 : 8, NW = 8, D = 4 * C, BOXC = 64, NBOX = D / BOXC;
+  static constexpr int BOX_BYTES = TOK * BOXC * 2;
+  static constexpr int X_BYTES = NBOX * BOX_BYTES;
+  static constexpr int RED_FLOATS = NW * 16 * (kMapRows + 1);
+  static constexpr int SMEM = X_BYTES + RED_FLOATS * 4 + TOK * kMapRows * 4 + 1024 + 64;
+  // shared-memory byte offset of x[row][col] in the swizzled box layout
+  __device__ static __forceinline__ uint32_t off(int row, int col) {
+    const int b = col >> 6, ch = (col & 63) >> 3;
+    return (uint32_t)(b * BOX_BYTES + row * 128 + ((ch ^ (row & 7)) << 4) + ((col & 7) << 1));
+  }
+};
 
 __device__ int g_map_tma_error;
 
-template <typename TX, typename TU>
-__global__ void __launch_bounds__(256, 2)
+template <int C, typename TX, typename TU>
+__global__ void __launch_bounds__(256)
 mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const uint2* __restrict__ phif,
                    const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
                    TU* __restrict__ u, float* __restrict__ hmix) {
-  using namespace map_tma;
+  using G = MapTma<C>;
+  constexpr int TOK = G::TOK, NW = G::NW, D = G::D, BOXC = G::BOXC, NBOX = G::NBOX, BOX_BYTES = G::BOX_BYTES,
+                X_BYTES = G::X_BYTES, RED_FLOATS = G::RED_FLOATS;
+  constexpr int KS = D / 16 / NW;  // k-steps per warp
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* xs = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  float* red = reinterpret_cast<float*>(xs + X_BYTES);  // [NW][TOK][25]
+  float* red = reinterpret_cast<float*>(xs + X_BYTES);  // [NW][16][25]
   float* hc = red + RED_FLOATS;                         // [TOK][24]
   uint64_t* bar = reinterpret_cast<uint64_t*>(hc + TOK * kMapRows);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
@@ -362,12 +367,12 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
   float ss_lo = 0.f, ss_hi = 0.f;
   const uint32_t xbase = tc05::smem_u32(xs);
 #pragma unroll 4
-  for (int ks = warp * 16; ks < warp * 16 + 16; ++ks) {
+  for (int ks = warp * KS; ks < warp * KS + KS; ++ks) {
     const int r = lane & 15, col = ks * 16 + (lane >> 4) * 8;
     uint32_t a[4];
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                  : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
-                 : "r"(xbase + map_tma_off(r, col)));
+                 : "r"(xbase + G::off(r, col)));
     const uint2* fp = phif + ((size_t)ks * 32 + lane) * 3;
     const uint2 f0 = __ldg(fp), f1 = __ldg(fp + 1), f2 = __ldg(fp + 2);
 #pragma unroll
@@ -385,7 +390,7 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
     ss_lo += __shfl_xor_sync(0xffffffffu, ss_lo, off);
     ss_hi += __shfl_xor_sync(0xffffffffu, ss_hi, off);
   }
-  float* rw = red + warp * TOK * (kMapRows + 1);
+  float* rw = red + warp * 16 * (kMapRows + 1);
 #pragma unroll
   for (int n = 0; n < 3; ++n) {
     rw[g * (kMapRows + 1) + 8 * n + 2 * t4] = acc[n][0];
@@ -404,7 +409,7 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
 #pragma unroll
     for (int r = 0; r < kMapRows; ++r) d[r] = 0.f;
     for (int w = 0; w < NW; ++w) {
-      const float* src = red + (w * TOK + tid) * (kMapRows + 1);
+      const float* src = red + (w * 16 + tid) * (kMapRows + 1);
 #pragma unroll
       for (int r = 0; r < kMapRows; ++r) d[r] += src[r];
       ssum += src[kMapRows];
@@ -421,24 +426,24 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
     }
   }
   __syncthreads();
-  // 3. pre-mix and RMSNorm: warp w takes tokens 2w, 2w + 1; lane covers 16 columns
-  constexpr int C = D / 4;
+  // 3. pre-mix and RMSNorm: TOK / NW tokens per warp; lane covers C / 32 columns
+  constexpr int VPL = C / 256;
 #pragma unroll 1
-  for (int tt = 0; tt < 2; ++tt) {
-    const int t = warp * 2 + tt;
+  for (int tt = 0; tt < TOK / NW; ++tt) {
+    const int t = warp * (TOK / NW) + tt;
     const int64_t tok = tok0 + t;
     if (tok >= ntok) break;
     const float h0 = hc[t * kMapRows], h1 = hc[t * kMapRows + 1], h2 = hc[t * kMapRows + 2],
                 h3 = hc[t * kMapRows + 3];
-    float uv[2][8];
+    float uv[VPL][8];
     float s2 = 0.f;
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
+    for (int v = 0; v < VPL; ++v) {
       const int c = (lane + 32 * v) * 8;
       float f[4][8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint4 q = *reinterpret_cast<const uint4*>(xs + map_tma_off(t, j * C + c));
+        const uint4 q = *reinterpret_cast<const uint4*>(xs + G::off(t, j * C + c));
         unpack8(q, f[j], (const TX*)nullptr);
       }
 #pragma unroll
@@ -450,7 +455,7 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
     s2 = warp_sum(s2);
     const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
+    for (int v = 0; v < VPL; ++v) {
       const int c = (lane + 32 * v) * 8;
       float o[8];
 #pragma unroll
@@ -512,18 +517,18 @@ static inline int grid_for(int64_t total, int threads) {
 using namespace walsh;
 
 // Single-pass TMA kernel launch; 1 = ran, 0 = not applicable, < 0 = error.
-template <typename TX, typename TU>
+template <int C, typename TX, typename TU>
 static int launch_map_tma(const void* x, int64_t ntok, const void* phi_frag, const float* mp, float map_eps,
                           const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s) {
-  using namespace map_tma;
+  using G = MapTma<C>;
   if (ntok > 2147483647LL) return 0;
   CUtensorMap m;
-  if (!make_tile_map(&m, x, std::is_same<TX, __nv_bfloat16>::value, ntok, D, BOXC, TOK)) return 0;
-  auto kern = mhc_map_tma_kernel<TX, TU>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+  if (!make_tile_map(&m, x, std::is_same<TX, __nv_bfloat16>::value, ntok, G::D, G::BOXC, G::TOK)) return 0;
+  auto kern = mhc_map_tma_kernel<C, TX, TU>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM) != cudaSuccess)
     return launch_status();
-  kern<<<(unsigned)((ntok + TOK - 1) / TOK), 256, SMEM, s>>>(m, ntok, (const uint2*)phi_frag, mp, map_eps, norm_w,
-                                                             norm_eps, (TU*)u, hmix);
+  kern<<<(unsigned)((ntok + G::TOK - 1) / G::TOK), 256, G::SMEM, s>>>(m, ntok, (const uint2*)phi_frag, mp, map_eps,
+                                                                      norm_w, norm_eps, (TU*)u, hmix);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
 }
@@ -543,19 +548,27 @@ extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, in
   // load chains, so it wins at decode token counts; prefill-sized calls take
   // the 128-token two-pass kernel below
   const bool many = ntok >= 148 * 64;
-  if (!many && phi_frag && C == 512 && (dtype == WALSH_BF16 || dtype == WALSH_F16) && u_dtype != WALSH_F32 &&
-      ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_frag)) & 15u) == 0) {
+  if (!many && phi_frag && (C == 512 || C == 2048) && (dtype == WALSH_BF16 || dtype == WALSH_F16) &&
+      u_dtype != WALSH_F32 && ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_frag)) & 15u) == 0) {
     int r;
-    if (dtype == WALSH_BF16)
-      r = u_dtype == WALSH_F16 ? launch_map_tma<__nv_bfloat16, __half>(x, ntok, phi_frag, mparams, map_eps, norm_w,
-                                                                       norm_eps, u, hmix, s)
-                               : launch_map_tma<__nv_bfloat16, __nv_bfloat16>(x, ntok, phi_frag, mparams, map_eps,
-                                                                              norm_w, norm_eps, u, hmix, s);
-    else
-      r = u_dtype == WALSH_F16 ? launch_map_tma<__half, __half>(x, ntok, phi_frag, mparams, map_eps, norm_w,
-                                                                norm_eps, u, hmix, s)
-                               : launch_map_tma<__half, __nv_bfloat16>(x, ntok, phi_frag, mparams, map_eps, norm_w,
-                                                                       norm_eps, u, hmix, s);
+#define WALSH_MAP_TMA(CC)                                                                                        \
+  if (dtype == WALSH_BF16)                                                                                      \
+    r = u_dtype == WALSH_F16 ? launch_map_tma<CC, __nv_bfloat16, __half>(x, ntok, phi_frag, mparams, map_eps,   \
+                                                                         norm_w, norm_eps, u, hmix, s)          \
+                             : launch_map_tma<CC, __nv_bfloat16, __nv_bfloat16>(x, ntok, phi_frag, mparams,      \
+                                                                                map_eps, norm_w, norm_eps, u,    \
+                                                                                hmix, s);                        \
+  else                                                                                                          \
+    r = u_dtype == WALSH_F16 ? launch_map_tma<CC, __half, __half>(x, ntok, phi_frag, mparams, map_eps, norm_w,   \
+                                                                  norm_eps, u, hmix, s)                         \
+                             : launch_map_tma<CC, __half, __nv_bfloat16>(x, ntok, phi_frag, mparams, map_eps,    \
+                                                                         norm_w, norm_eps, u, hmix, s);
+    if (C == 512) {
+      WALSH_MAP_TMA(512)
+    } else {
+      WALSH_MAP_TMA(2048)
+    }
+#undef WALSH_MAP_TMA
     if (r != 0) return r > 0 ? WALSH_OK : r;
   }
   const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_lp)) & 15u) == 0;

@@ -74,7 +74,7 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
     for (int a = 0; a < M::JPT; ++a)
 #pragma unroll
       for (int t = 0; t < M::TPT; ++t) acc[a][t] = 0.f;
-#pragma unroll 4
+#pragma unroll 16
     for (int k = 0; k < C; ++k) {
       float w[M::JPT];
 #pragma unroll
@@ -102,7 +102,7 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
     const float* hp = hs + t * HID;
     const float* wp = w2 + (size_t)e * HID;
     float acc = 0.f;
-#pragma unroll 8
+#pragma unroll 16
     for (int j = 0; j < HID; ++j) acc = fmaf(hp[j], __ldg(wp + j), acc);
     lg[item] = acc;
   }

@@ -257,9 +257,14 @@ class mHCWalsh(nn.Module):
     def stream_table(self, dtype):
         """tok_embeddings folded with stream_proj: row v = stream_proj(emb[v]), [V, n*C]."""
         emb, W, b = self.tok_embeddings.weight, self.stream_proj.weight, self.stream_proj.bias
-        return _prep.cached(self, f"table_{dtype}", [emb, W, b],
-                            lambda: ops.linear(emb.detach().float().contiguous(), W.detach().float(), b.detach(),
-                                               out_dtype=dtype))
+
+        def build():
+            e = emb.detach().float().contiguous()
+            if ops.split_eligible(e, e.shape[1]):
+                t = ops.linear_split(e, *ops.split_bf16(W), b.detach())
+                return t if dtype == torch.float32 else t.to(dtype)
+            return ops.linear(e, W.detach().float(), b.detach(), out_dtype=dtype)
+        return _prep.cached(self, f"table_{dtype}", [emb, W, b], build)
 
     def head_weights(self):
         """The tied output projection, float32 (logits are always computed against fp32 weights)."""
