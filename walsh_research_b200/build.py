@@ -26,6 +26,9 @@ LIB = os.path.join(PKG, "libwalsh.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + INCLUDE, "-I" + CSRC]
+# developer hook: extra nvcc arguments (e.g. -D tuning constants); objects are
+# not rebuilt when only these change, so delete the affected _build/*.o first
+FLAGS += os.environ.get("WALSH_NVCC_FLAGS", "").split()
 
 
 def nvcc() -> str:

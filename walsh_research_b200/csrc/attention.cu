@@ -432,11 +432,186 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
   }
 }
 
+// ---------------------------------------------------------------------------
+// fp16 prefill, hd 16, whole-head variant: one CTA per (batch, head) holds
+// that head's visible K and V (up to 2048 keys, rows padded to 48 bytes for
+// conflict-free ldmatrix) in shared memory, loaded once with cp.async; the 8
+// warps then run 16-row query tiles independently (no barriers), tiles
+// dealt out snake-wise (w, 15 - w, 16 + w, ...) so every warp gets the same
+// causal work.  Per 64-key step: S = Q K^T (8 MMAs), row maxima, P = 2^(S
+// scale - m) as paired fp16 ex2, O += P V and the row sums of P (all-ones
+// V column) on the tensor cores.  The reference maximum m of a row only
+// moves when the row maximum exceeds it by more than 8 (P <= 256 in fp16),
+// so the O rescale is rare.
+// ---------------------------------------------------------------------------
+constexpr int kAttnHeadMaxKeys = 2048;
+// Bit n set: exponent pairs of n-tile n (of the 8 per 64-key step) are
+// evaluated by the FMA-pipe polynomial instead of MUFU ex2.  Measured on
+// B200 at B64 x H32 x T1024: 421 us with none, 458 us with 2 of 8, 481 us
+// with 3 of 8, 495 us with 4 of 8 -- with Q pre-scaled and three-input
+// maxima the MUFU pipe no longer bounds this kernel, so the default is none.
+#ifndef WALSH_ATTN_POLY_PAIRS
+#define WALSH_ATTN_POLY_PAIRS 0x00
+#endif
+
+__global__ void __launch_bounds__(256)
+attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc, int H,
+                 int Tq, int ctx, int start_pos, float scale_log2, __half* __restrict__ o) {
+  constexpr int HD = 16, LD = HD + 8, KT = 64;
+  extern __shared__ __align__(16) __half smh[];
+  __half* Ks = smh;  // [kpad][LD]
+  const int b = blockIdx.y, h = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const size_t bh = (size_t)b * H + h;
+  const int kend = start_pos + Tq;
+  const int kpad = (kend + KT - 1) / KT * KT;  // the last 64-key step reads up to here
+  __half* Vs = smh + (size_t)kpad * LD;        // [kpad][LD]
+  const __half* kb = kc + bh * ctx * HD;
+  const __half* vb = vc + bh * ctx * HD;
+  for (int i = tid; i < kpad * 2; i += 256) {
+    const int r = i >> 1, c = (i & 1) * 8;
+    const bool in = r < kend;  // rows kend..kpad-1 are zero-filled
+    cp_async16(Ks + r * LD + c, kb + (size_t)(in ? r : 0) * HD + c, in ? 16 : 0);
+    cp_async16(Vs + r * LD + c, vb + (size_t)(in ? r : 0) * HD + c, in ? 16 : 0);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+
+  const __half* qb = q + bh * Tq * HD;
+  const int nqt = (Tq + 15) / 16;
+  for (int i = 0;; ++i) {
+    const int qt = i * 8 + ((i & 1) ? 7 - warp : warp);
+    if (qt >= nqt) break;
+    const int q0 = qt * 16;
+    const int r_lo = q0 + g, r_hi = r_lo + 8;
+    // Q fragment straight from global memory (rows past Tq are zero)
+    uint32_t qf[4];
+    {
+      const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qb);
+      qf[0] = r_lo < Tq ? __ldg(q32 + (r_lo * HD + 2 * t4) / 2) : 0u;
+      qf[1] = r_hi < Tq ? __ldg(q32 + (r_hi * HD + 2 * t4) / 2) : 0u;
+      qf[2] = r_lo < Tq ? __ldg(q32 + (r_lo * HD + 2 * t4 + 8) / 2) : 0u;
+      qf[3] = r_hi < Tq ? __ldg(q32 + (r_hi * HD + 2 * t4 + 8) / 2) : 0u;
+      // fold the softmax scale (and log2 e) into Q: S comes out in the exp2 domain
+      const __half2 sc = __float2half2_rn(scale_log2);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __half2 v;
+        memcpy(&v, &qf[j], 4);
+        v = __hmul2(v, sc);
+        memcpy(&qf[j], &v, 4);
+      }
+    }
+    const int qp_lo = start_pos + r_lo, qp_hi = start_pos + r_hi;  // query positions
+    const int nkey = min(kend, start_pos + q0 + 16);                // keys visible to some row
+    float m_lo = -CUDART_INF_F, m_hi = -CUDART_INF_F;               // reference maxima (exp2 domain)
+    float oacc[HD / 8 + 1][4];
+#pragma unroll
+    for (int j = 0; j < HD / 8 + 1; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
+    for (int k0 = 0; k0 < nkey; k0 += KT) {
+      float s[KT / 8][4];
+#pragma unroll
+      for (int n = 0; n < KT / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+      for (int np = 0; np < KT / 16; ++np) {
+        uint32_t kf[4];
+        ldsm_x4(kf, Ks + (k0 + np * 16 + (lane & 7) + ((lane >> 4) << 3)) * LD + ((lane >> 3) & 1) * 8);
+        mma_f16(s[2 * np], qf, kf[0], kf[1]);
+        mma_f16(s[2 * np + 1], qf, kf[2], kf[3]);
+      }
+      // keys past a row's position (or past kend) are masked
+      const bool edge = k0 + KT > start_pos + q0 || k0 + KT > kend;
+      if (edge) {
+#pragma unroll
+        for (int n = 0; n < KT / 8; ++n)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = k0 + n * 8 + 2 * t4 + e;
+            if (key > qp_lo || key >= kend) s[n][e] = -CUDART_INF_F;
+            if (key > qp_hi || key >= kend) s[n][2 + e] = -CUDART_INF_F;
+          }
+      }
+      float mt_lo = -CUDART_INF_F, mt_hi = -CUDART_INF_F;
+#pragma unroll
+      for (int n = 0; n < KT / 8; ++n) {
+        mt_lo = fmax3(mt_lo, s[n][0], s[n][1]);
+        mt_hi = fmax3(mt_hi, s[n][2], s[n][3]);
+      }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        mt_lo = fmaxf(mt_lo, __shfl_xor_sync(0xffffffffu, mt_lo, off));
+        mt_hi = fmaxf(mt_hi, __shfl_xor_sync(0xffffffffu, mt_hi, off));
+      }
+      // move a reference maximum only when the row maximum passes it by more than 8
+      const bool mv_lo = mt_lo > m_lo + 8.f, mv_hi = mt_hi > m_hi + 8.f;
+      if (__any_sync(0xffffffffu, mv_lo || mv_hi)) {
+        const float nm_lo = mv_lo ? mt_lo : m_lo, nm_hi = mv_hi ? mt_hi : m_hi;
+        const float c_lo = m_lo == -CUDART_INF_F ? 0.f : ex2_f32(m_lo - nm_lo);
+        const float c_hi = m_hi == -CUDART_INF_F ? 0.f : ex2_f32(m_hi - nm_hi);
+#pragma unroll
+        for (int j = 0; j < HD / 8 + 1; ++j) {
+          oacc[j][0] *= c_lo; oacc[j][1] *= c_lo;
+          oacc[j][2] *= c_hi; oacc[j][3] *= c_hi;
+        }
+        m_lo = nm_lo;
+        m_hi = nm_hi;
+      }
+      // rows with no visible key yet keep m = -inf and P = 2^-inf = 0
+      const float sub_lo = m_lo == -CUDART_INF_F ? 0.f : m_lo, sub_hi = m_hi == -CUDART_INF_F ? 0.f : m_hi;
+      // P = 2^(S - m): the pairs selected by WALSH_ATTN_POLY_PAIRS on the FMA pipe, the
+      // rest as paired fp16 ex2 on the MUFU pipe (which would otherwise bound the kernel)
+      uint32_t pf[KT / 16][4];
+#pragma unroll
+      for (int n = 0; n < KT / 8; ++n) {
+        if ((WALSH_ATTN_POLY_PAIRS >> n) & 1) {
+          pf[n >> 1][(n & 1) * 2 + 0] = pack_f16(exp2_poly(s[n][0] - sub_lo), exp2_poly(s[n][1] - sub_lo));
+          pf[n >> 1][(n & 1) * 2 + 1] = pack_f16(exp2_poly(s[n][2] - sub_hi), exp2_poly(s[n][3] - sub_hi));
+        } else {
+          pf[n >> 1][(n & 1) * 2 + 0] = ex2_f16x2(pack_f16(s[n][0] - sub_lo, s[n][1] - sub_lo));
+          pf[n >> 1][(n & 1) * 2 + 1] = ex2_f16x2(pack_f16(s[n][2] - sub_hi, s[n][3] - sub_hi));
+        }
+      }
+#pragma unroll
+      for (int kk = 0; kk < KT / 16; ++kk) {
+        uint32_t vf[4];
+        ldsm_x4_t(vf, Vs + (k0 + kk * 16 + (lane & 15)) * LD + (lane >> 4) * 8);
+        mma_f16(oacc[0], pf[kk], vf[0], vf[1]);
+        mma_f16(oacc[1], pf[kk], vf[2], vf[3]);
+        mma_f16(oacc[HD / 8], pf[kk], 0x3C003C00u, 0x3C003C00u);  // row sums of P
+      }
+    }
+    const float inv_lo = 1.0f / oacc[HD / 8][0], inv_hi = 1.0f / oacc[HD / 8][2];
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      const int d = j * 8 + 2 * t4;
+      if (r_lo < Tq)
+        *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + r_lo) * H + h) * HD + d) =
+            pack_f16_sat(oacc[j][0] * inv_lo, oacc[j][1] * inv_lo);
+      if (r_hi < Tq)
+        *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + r_hi) * H + h) * HD + d) =
+            pack_f16_sat(oacc[j][2] * inv_hi, oacc[j][3] * inv_hi);
+    }
+  }
+}
+
 template <int HD, typename T>
 static int launch_attn(const void* q, const void* kc, const void* vc, int B, int H, int Tq, int ctx,
                        int start_pos, void* o, cudaStream_t s) {
   const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
   const bool aligned = ((((uintptr_t)q) | ((uintptr_t)kc) | ((uintptr_t)vc)) & 15u) == 0;
+  if constexpr (std::is_same<T, __half>::value && HD == 16) {
+    const int kend = start_pos + Tq;
+    if (Tq > 4 && aligned && kend <= kAttnHeadMaxKeys && H <= 65535 && B <= 65535) {
+      const int smem = 2 * ((kend + 63) / 64 * 64) * (HD + 8) * (int)sizeof(__half);
+      if (smem > 48 * 1024 &&
+          cudaFuncSetAttribute(attn_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return launch_status();
+      attn_head_kernel<<<dim3(H, B), 256, smem, s>>>((const __half*)q, (const __half*)kc, (const __half*)vc, H, Tq,
+                                                     ctx, start_pos, scale_log2, (__half*)o);
+      return launch_status();
+    }
+  }
   if constexpr (sizeof(T) == 2) {
     if (Tq > 4 && aligned) {
       dim3 grid((Tq + 127) / 128, H, B);
