@@ -46,6 +46,21 @@ DECODE_BATCH, DECODE_CTX = 256, 1024
 ATTN_TRAFFIC_B64 = 252.96e6  # ncu DRAM bytes of one prefill attention launch at B64 x T1024
 
 
+def max_over_ranks(value: float, dist, device) -> float:
+    """The largest per-rank value (step times are reported as the slowest
+    rank's); `dist` is torch.distributed or None for a single process."""
+    if not dist:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def rank_token_seed(base: int, rank: int) -> int:
+    """Each rank draws its own batch (weak scaling: batch-sharded replicas)."""
+    return base + rank
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -249,7 +264,7 @@ def main():
                  if k != "freqs_cis" and not k.endswith(".H")}
     model = cpu_model.to(dev).eval()
     model.compute_dtype = torch.bfloat16
-    idx_host = token_ids(B, T, seed=1 + rank).pin_memory()
+    idx_host = token_ids(B, T, seed=rank_token_seed(1, rank)).pin_memory()
     idx = idx_host.to(dev)
 
     # graph-captured forward: inputs resident in HBM
@@ -277,10 +292,7 @@ def main():
             end.record()
             torch.cuda.synchronize()
         ms = start.elapsed_time(end) / args.steps
-        if dist:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = max_over_ranks(ms, dist, dev)
         value = world * B * T / (ms / 1e3)
 
         # end to end through the public API: H2D ids, forward, D2H logits
@@ -301,10 +313,7 @@ def main():
         end.record()
         torch.cuda.synchronize()
         e_ms = start.elapsed_time(end) / e_steps
-        if dist:
-            t = torch.tensor([e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
+        e_ms = max_over_ranks(e_ms, dist, dev)
         e2e = {"value": world * B * T / (e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": idx_host.numel() * idx_host.element_size(),
                "d2h_bytes_per_step": logits_host.numel() * logits_host.element_size()}
@@ -424,8 +433,8 @@ def measure_decode(model, dev, steps, warmup, rank=0, world=1, dist=None, B=None
     n = warmup + steps
     P = ctx - n
     kv = KVCache(L, ctx, H, C // H, dev, dtype=torch.float16, batch_size=B)
-    prompt = token_ids(B, P, seed=3 + rank).to(dev)
-    ids_host = token_ids(B, n, seed=5 + rank).pin_memory()
+    prompt = token_ids(B, P, seed=rank_token_seed(3, rank)).to(dev)
+    ids_host = token_ids(B, n, seed=rank_token_seed(5, rank)).pin_memory()
     ids = ids_host.to(dev)
     with torch.no_grad():
         model(prompt, kv_cache=kv, start_pos=0)
@@ -458,10 +467,7 @@ def measure_decode(model, dev, steps, warmup, rank=0, world=1, dist=None, B=None
         end.record()
         torch.cuda.synchronize()
         ms = start.elapsed_time(end) / steps
-        if dist:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = max_over_ranks(ms, dist, dev)
         del graphs, outs
 
         # eager end to end through the public API
@@ -482,10 +488,7 @@ def measure_decode(model, dev, steps, warmup, rank=0, world=1, dist=None, B=None
         end.record()
         torch.cuda.synchronize()
         e_ms = start.elapsed_time(end) / steps
-        if dist:
-            t = torch.tensor([e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
+        e_ms = max_over_ranks(e_ms, dist, dev)
     del kv
     torch.cuda.empty_cache()
     kv_bytes = L * 2 * B * H * ctx * (C // H) * 2
@@ -537,7 +540,7 @@ def measure_decode_2048(dev, steps, warmup, rank=0, world=1, dist=None):
     gen = torch.Generator(device=dev).manual_seed(11 + rank)
     for t in kv.k_cache + kv.v_cache:
         t.normal_(generator=gen)
-    ids = token_ids(B, n, seed=13 + rank).to(dev)
+    ids = token_ids(B, n, seed=rank_token_seed(13, rank)).to(dev)
     kv.cached_len = P
     with torch.no_grad():
         model(ids[:, :1], kv_cache=kv, start_pos=P)   # eager warm-up (weight preparation)
@@ -564,10 +567,7 @@ def measure_decode_2048(dev, steps, warmup, rank=0, world=1, dist=None):
         end.record()
         torch.cuda.synchronize()
         ms = start.elapsed_time(end) / steps
-        if dist:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = max_over_ranks(ms, dist, dev)
     del graphs, kv, model
     torch.cuda.empty_cache()
     hbm, _, _ = peaks()
@@ -588,7 +588,7 @@ def measure_octonion(dev, steps, warmup, rank=0, world=1, dist=None):
     model = build_octonion_cpu().to(dev).eval()
     model.compute_dtype = torch.bfloat16
     B, T = OCTO_BATCH, SEQ
-    idx = token_ids(B, T, seed=7 + rank).to(dev)
+    idx = token_ids(B, T, seed=rank_token_seed(7, rank)).to(dev)
     with torch.no_grad():
         for _ in range(2):
             model(idx)
@@ -610,10 +610,7 @@ def measure_octonion(dev, steps, warmup, rank=0, world=1, dist=None):
         end.record()
         torch.cuda.synchronize()
         ms = start.elapsed_time(end) / steps
-        if dist:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = max_over_ranks(ms, dist, dev)
     del g, model
     torch.cuda.empty_cache()
     return {"metric": "Walsh-512 octonion prefill tokens/s", "value": world * B * T / (ms / 1e3), "unit": UNIT,

@@ -288,6 +288,12 @@ int walsh_octo_set_mainloop(int tcgen05);
  * No counterpart in the reference. */
 int walsh_tc05_error(int reset);
 
+/* Test hook for the bounded waits: one thread waits on an mbarrier that is
+ * never arrived at, gives up after budget_cycles SM clocks (at most 4e9) and
+ * sets the walsh_tc05_error status word to WALSH_ERR_TIMEOUT.  The context
+ * stays usable.  No counterpart in the reference. */
+walsh_status walsh_tc05_wait_selftest(long long budget_cycles, void* stream);
+
 /* y = scale . (x w^T), y in x's dtype [M, N].
  * Replaces OctonionTernaryLinearRef.forward / OctonionFusedLinear.forward
  * (src/model/physics.py:66-82, src/model/cayley_dickson_cuda.py:654-668). */

@@ -92,3 +92,22 @@ def test_qkv_swiglu_post_epilogues_match_mma_sync(mainloop, tokens):
         w, s = mlp.down_operands(h.dtype)
         return ops.octo_post(h, w, s, xs, hmix)
     assert rel(mainloop(post, True), mainloop(post, False).float().cpu().numpy()) < 2e-3
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    """A wait that can never complete gives up after its clock budget, the status
+    word reports WALSH_ERR_TIMEOUT, and the next GEMM runs normally."""
+    from walsh_research_b200 import _lib
+    _lib.call("walsh_tc05_error", 1)
+    _lib.call("walsh_tc05_wait_selftest", 2_000_000, _lib.stream())   # about 1 ms of SM clocks
+    torch.cuda.synchronize()
+    assert _lib.call("walsh_tc05_error", 1) == -6
+    assert _lib.call("walsh_tc05_error", 0) == 0
+    rng = np.random.default_rng(1)
+    m = _layer(512, 512, rng)
+    x = T(rng.normal(size=(300, 512)).astype(np.float32), torch.float16)
+    y = m.forward_flat(x)
+    torch.cuda.synchronize()
+    w, be = m.weight.detach().cpu().numpy(), m.beta.detach().cpu().numpy()
+    assert rel(y, O.octonion_linear(x.float().cpu().numpy(), w, be)) < 3e-3
+    assert _lib.call("walsh_tc05_error", 1) == 0

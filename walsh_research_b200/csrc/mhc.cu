@@ -360,30 +360,40 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
     if (tid == 0) atomicExch(&g_map_tma_error, (int)WALSH_ERR_TIMEOUT);
     return;
   }
-  // 1. partial projections over this warp's 256 columns
+  // 1. partial projections over this warp's columns (phi fragments loaded 8 k-steps at a time)
   float acc[3][4];
 #pragma unroll
   for (int n = 0; n < 3; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
   float ss_lo = 0.f, ss_hi = 0.f;
   const uint32_t xbase = tc05::smem_u32(xs);
-#pragma unroll 4
-  for (int ks = warp * KS; ks < warp * KS + KS; ++ks) {
-    const int r = lane & 15, col = ks * 16 + (lane >> 4) * 8;
-    uint32_t a[4];
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
-                 : "r"(xbase + G::off(r, col)));
-    const uint2* fp = phif + ((size_t)ks * 32 + lane) * 3;
-    const uint2 f0 = __ldg(fp), f1 = __ldg(fp + 1), f2 = __ldg(fp + 2);
+#pragma unroll 1
+  for (int kb8 = warp * KS; kb8 < warp * KS + KS; kb8 += 8) {
+    uint2 fr[8][3];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 v = unpack2<TX>(a[q]);
-      if (q & 1) ss_hi = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_hi));
-      else ss_lo = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_lo));
+    for (int j = 0; j < 8; ++j) {
+      const uint2* fp = phif + ((size_t)(kb8 + j) * 32 + lane) * 3;
+      fr[j][0] = __ldg(fp);
+      fr[j][1] = __ldg(fp + 1);
+      fr[j][2] = __ldg(fp + 2);
     }
-    mma16<TX>(acc[0], a, f0.x, f0.y);
-    mma16<TX>(acc[1], a, f1.x, f1.y);
-    mma16<TX>(acc[2], a, f2.x, f2.y);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int ks = kb8 + j;
+      const int r = lane & 15, col = ks * 16 + (lane >> 4) * 8;
+      uint32_t a[4];
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                   : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                   : "r"(xbase + G::off(r, col)));
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 v = unpack2<TX>(a[q]);
+        if (q & 1) ss_hi = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_hi));
+        else ss_lo = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_lo));
+      }
+      mma16<TX>(acc[0], a, fr[j][0].x, fr[j][0].y);
+      mma16<TX>(acc[1], a, fr[j][1].x, fr[j][1].y);
+      mma16<TX>(acc[2], a, fr[j][2].x, fr[j][2].y);
+    }
   }
 #pragma unroll
   for (int off = 1; off <= 2; off <<= 1) {
@@ -403,27 +413,57 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
     rw[(g + 8) * (kMapRows + 1) + kMapRows] = ss_hi;
   }
   __syncthreads();
-  // 2. one thread per token
-  if (tid < TOK) {
-    float d[kMapRows], hm[kMapRows], ssum = 0.f;
+  // 2a. per-token sums of the 8 warps' partials (warp order fixed): ds[t][v], v < 25
+  float* ds = red;  // reused in place: column v of warp 0's rows
+  {
+    float tmp[2] = {0.f, 0.f};
+    const int t = tid >> 4, e = tid & 15;
+    if (t < TOK) {
 #pragma unroll
-    for (int r = 0; r < kMapRows; ++r) d[r] = 0.f;
-    for (int w = 0; w < NW; ++w) {
-      const float* src = red + (w * 16 + tid) * (kMapRows + 1);
-#pragma unroll
-      for (int r = 0; r < kMapRows; ++r) d[r] += src[r];
-      ssum += src[kMapRows];
+      for (int k = 0; k < 2; ++k) {
+        const int v = e + 16 * k;
+        if (v <= kMapRows)
+          for (int w = 0; w < NW; ++w) tmp[k] += red[(w * 16 + t) * (kMapRows + 1) + v];
+      }
     }
-    const float rms = rsqrtf(ssum / (float)D + map_eps);
+    __syncthreads();
+    if (t < TOK) {
 #pragma unroll
-    for (int r = 0; r < kMapRows; ++r) d[r] *= rms;
-    map_activations(d, mp, hm);
-#pragma unroll
-    for (int r = 0; r < kMapRows; ++r) hc[tid * kMapRows + r] = hm[r];
-    if (tok0 + tid < ntok) {
-#pragma unroll
-      for (int r = 0; r < kMapRows; ++r) hmix[(tok0 + tid) * kMapRows + r] = hm[r];
+      for (int k = 0; k < 2; ++k) {
+        const int v = e + 16 * k;
+        if (v <= kMapRows) ds[t * (kMapRows + 1) + v] = tmp[k];
+      }
     }
+  }
+  __syncthreads();
+  // 2b. activations, 16 threads per token (one per H_res entry): thread e of token t
+  //     holds M[e] (row e / 4, column e % 4) and gathers columns and rows by shuffles,
+  //     adding in the same order as the single-thread sinkhorn4
+  if (tid < TOK * 16) {
+    const int t = tid >> 4, e = tid & 15, base = lane & 16, r = e >> 2, c = e & 3;
+    const float* dt = ds + t * (kMapRows + 1);
+    const float rms = rsqrtf(dt[kMapRows] / (float)D + map_eps);
+    const float a_pre = __ldg(mp + 0), a_post = __ldg(mp + 1), a_res = __ldg(mp + 2);
+    const int64_t tok = tok0 + t;
+    if (e < 4) {
+      const float hp = 1.0f / (1.0f + expf(-(a_pre * (dt[e] * rms) + __ldg(mp + 4 + e))));
+      hc[t * kMapRows + e] = hp;
+      if (tok < ntok) hmix[tok * kMapRows + e] = hp;
+    } else if (e < 8) {
+      const float ho = 2.0f * (1.0f / (1.0f + expf(-(a_post * (dt[e] * rms) + __ldg(mp + 8 + (e - 4))))));
+      if (tok < ntok) hmix[tok * kMapRows + e] = ho;
+    }
+    float M = expf(a_res * (dt[8 + e] * rms) + __ldg(mp + 12 + e));
+    for (int it = 0; it < 20; ++it) {
+      const float c0 = __shfl_sync(0xffffffffu, M, base + c), c1 = __shfl_sync(0xffffffffu, M, base + 4 + c),
+                  c2 = __shfl_sync(0xffffffffu, M, base + 8 + c), c3 = __shfl_sync(0xffffffffu, M, base + 12 + c);
+      M *= __frcp_rn((((c0 + c1) + c2) + c3) + 1e-8f);
+      const float r0 = __shfl_sync(0xffffffffu, M, base + 4 * r), r1 = __shfl_sync(0xffffffffu, M, base + 4 * r + 1),
+                  r2 = __shfl_sync(0xffffffffu, M, base + 4 * r + 2),
+                  r3 = __shfl_sync(0xffffffffu, M, base + 4 * r + 3);
+      M *= __frcp_rn((((r0 + r1) + r2) + r3) + 1e-8f);
+    }
+    if (tok < ntok) hmix[tok * kMapRows + 8 + e] = M;
   }
   __syncthreads();
   // 3. pre-mix and RMSNorm: TOK / NW tokens per warp; lane covers C / 32 columns
@@ -544,9 +584,10 @@ extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, in
   WALSH_CHECK_SHAPE(ntok >= 0 && C > 0 && C % 32 == 0 && C <= 8192);
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  // single-pass kernel: 16 tokens per CTA, latency-bound on its Sinkhorn and
-  // load chains, so it wins at decode token counts; prefill-sized calls take
-  // the 128-token two-pass kernel below
+  // single-pass kernel: 16 tokens per CTA (8 for C = 2048) with its load
+  // exposed per CTA; it wins at decode token counts (measured 190 us vs 145 us
+  // for the two-pass kernel at 65 536 tokens), so prefill-sized calls take the
+  // 128-token two-pass kernel below
   const bool many = ntok >= 148 * 64;
   if (!many && phi_frag && (C == 512 || C == 2048) && (dtype == WALSH_BF16 || dtype == WALSH_F16) &&
       u_dtype != WALSH_F32 && ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_frag)) & 15u) == 0) {

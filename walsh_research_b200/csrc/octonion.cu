@@ -718,6 +718,24 @@ extern "C" walsh_status walsh_octo_post_fwd(const void* a, int dtype, int64_t M,
                       s));
 }
 
+// Exercises the bounded-wait path of the tcgen05 kernels: one thread waits on
+// an mbarrier that nothing arrives at, gives up after `budget` clock cycles
+// and records WALSH_ERR_TIMEOUT like a stalled pipeline would.
+__global__ void tc05_wait_selftest_kernel(long long budget) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc05::mbar_init(&bar, 1);
+    tc05::fence_barrier_init();
+    if (!tc05::mbar_wait(&bar, 0, budget)) atomicExch(&g_tc05_error, (int)WALSH_ERR_TIMEOUT);
+  }
+}
+
+extern "C" walsh_status walsh_tc05_wait_selftest(long long budget_cycles, void* stream) {
+  WALSH_CHECK_ARG(budget_cycles > 0 && budget_cycles <= 4000000000LL);
+  tc05_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(budget_cycles);
+  return launch_status();
+}
+
 extern "C" int walsh_octo_set_mainloop(int tcgen05) {
   const int prev = g_octo_tc05;
   g_octo_tc05 = tcgen05 ? 1 : 0;

@@ -143,6 +143,18 @@ class CausalSelfAttention(nn.Module):
         inner = lin.inner
         return (inner.ternary_f16(),) + inner.scales()
 
+    def _qkv_dense(self, dtype):
+        """q | k | v HadamardLinear layers as one dense [3C, C] matrix (alpha, beta,
+        the two transforms and the ternary blocks folded together, float32 then
+        rounded to the operand dtype) with unit column scales: the operands of the
+        tcgen05 q/k/v GEMM."""
+        def build():
+            W = torch.cat([self.wq.inner.dense(), self.wk.inner.dense(), self.wv.inner.dense()], dim=0)
+            return (W.to(ops.octo_operand_dtype(dtype)).contiguous(), None), torch.ones(
+                W.shape[0], device=W.device, dtype=torch.float32)
+        ws = [p for lin in (self.wq, self.wk, self.wv) for p in (lin.weight, lin.inner.alpha, lin.inner.beta)]
+        return _prep.cached(self, f"qkv_dense_{dtype}", ws, build)
+
     def _tc(self, x) -> bool:
         return self.algebra == "hadamard" and ops.tc_eligible(x, torch.float16) and self.n_embd == 512
 
@@ -156,8 +168,9 @@ class CausalSelfAttention(nn.Module):
         B, T, C = x.shape
         H, hd = self.n_head, self.head_dim
         q = torch.empty((B, H, T, hd), dtype=x.dtype, device=x.device)
-        ops.attn_qkv_tc(x, H, self._triple_tc(self.wq), self._triple_tc(self.wk), self._triple_tc(self.wv),
-                        rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
+        # one tcgen05 GEMM over the dense q | k | v matrix, RoPE and the cache write in its epilogue
+        w, sc = self._qkv_dense(x.dtype)
+        ops.octo_qkv(x, H, w, sc, rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
         o = ops.attention(q, k_cache, v_cache, start_pos)
         wmix = bmix = None
         if self.head_mixer is not None:
