@@ -281,22 +281,36 @@ attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __r
     bo[pass][0] = lo.x; bo[pass][1] = lo.y; bo[pass][2] = lo.z; bo[pass][3] = lo.w;
     bo[pass][4] = hi.x; bo[pass][5] = hi.y; bo[pass][6] = hi.z; bo[pass][7] = hi.w;
   }
+  // software-pipelined over the warp's 16 tokens: token t + 1's stream rows and
+  // mixing coefficients are loaded before token t is computed and stored (the
+  // tokens' rows are disjoint, so this is safe when xo aliases x)
+  uint4 xq[2][4];
+  float4 hq[5];  // H_post[4] | H_res[16]
+  auto load_tok = [&](int64_t tok, uint4 (&xr)[2][4], float4 (&hr4)[5]) {
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      const size_t base = (size_t)tok * 4 * kTcC + pass * 256 + lane * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xr[pass][j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * kTcC);
+    }
+    const float4* h4 = reinterpret_cast<const float4*>(hmix + tok * kMapRows + 4);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) hr4[i] = __ldg(h4 + i);
+  };
+  if (tok0 < ntok) load_tok(tok0, xq, hq);
   for (int t = 0; t < kTcTok; ++t) {
     const int64_t tok = tok0 + t;
     if (tok >= ntok) break;
-    const float* hm = hmix + tok * kMapRows;
-    float hp[4], hr[16];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) hp[i] = __ldg(hm + 4 + i);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) hr[i] = __ldg(hm + 8 + i);
+    uint4 xn[2][4];
+    float4 hn[5];
+    if (t + 1 < kTcTok && tok + 1 < ntok) load_tok(tok + 1, xn, hn);
+    const float hp[4] = {hq[0].x, hq[0].y, hq[0].z, hq[0].w};
+    const float hr[16] = {hq[1].x, hq[1].y, hq[1].z, hq[1].w, hq[2].x, hq[2].y, hq[2].z, hq[2].w,
+                          hq[3].x, hq[3].y, hq[3].z, hq[3].w, hq[4].x, hq[4].y, hq[4].z, hq[4].w};
 #pragma unroll
     for (int pass = 0; pass < 2; ++pass) {
       const int c = pass * 256 + lane * 8;
       const size_t base = (size_t)tok * 4 * kTcC + c;
-      uint4 xq[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) xq[j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * kTcC);
       const uint4 v = *reinterpret_cast<const uint4*>(tile + t * kTcRow + c);
       const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
       uint32_t ow[4][4];
@@ -306,7 +320,7 @@ attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __r
         const float f0 = f.x * bo[pass][2 * q2], f1 = f.y * bo[pass][2 * q2 + 1];
         float2 xf[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xf[j] = unpack2<TX>((&xq[j].x)[q2]);
+        for (int j = 0; j < 4; ++j) xf[j] = unpack2<TX>((&xq[pass][j].x)[q2]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float* r = hr + 4 * i;
@@ -319,6 +333,12 @@ attn_out_tc_kernel(const __half* __restrict__ o, int64_t ntok, const __half* __r
       for (int i = 0; i < 4; ++i)
         *reinterpret_cast<uint4*>(xo + base + (size_t)i * kTcC) = make_uint4(ow[i][0], ow[i][1], ow[i][2], ow[i][3]);
     }
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xq[pass][j] = xn[pass][j];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) hq[i] = hn[i];
   }
 }
 
@@ -391,7 +411,7 @@ extern "C" walsh_status walsh_attn_out_tc_fwd(const void* o, int64_t ntok, const
   WALSH_CHECK_DTYPE(x_dtype);
   WALSH_CHECK_SHAPE(x_dtype == WALSH_BF16 || x_dtype == WALSH_F16);
   WALSH_CHECK_ARG(al16(o) && al16(wo_f16) && (!wmix_f16 || al16(wmix_f16)) && al16(x) && al16(x_out) &&
-                  al16(wo_beta));
+                  al16(wo_beta) && al16(hmix));
   if (ntok == 0) return WALSH_OK;
   const int wpc = tc_warps_per_cta(ntok);
   const int smem = 4 * kTcTok * kTcRow * (int)sizeof(__half);

@@ -482,37 +482,59 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
     }
     __syncthreads();  // buffer (e & 1) is refilled by the next iteration's prefetch
   }
-  // ---- epilogue: 8 consecutive columns per lane, 16-byte loads and stores
+  // ---- epilogue: 8 consecutive columns per lane, 16-byte loads and stores,
+  // software-pipelined over the warp's 16 tokens (token t + 1's stream rows and
+  // coefficients are loaded before token t is computed; rows are disjoint, so
+  // this is safe when xo aliases x)
+  if (!fuse_post) {
+    for (int t = 0; t < 16; ++t) {
+      const int64_t tok = tok0 + t;
+      if (tok >= ntok) break;
+#pragma unroll
+      for (int pass = 0; pass < C / 256; ++pass) {
+        const int c = pass * 256 + lane * 8;
+        *reinterpret_cast<uint4*>(y + tok * C + c) = *reinterpret_cast<const uint4*>(uw + t * LDU + c);
+      }
+    }
+    return;
+  }
+  constexpr int NP = C / 256;
+  uint4 xq[NP][4];
+  float4 hq[5];  // H_post[4] | H_res[16]
+  auto load_tok = [&](int64_t tok, uint4 (&xr)[NP][4], float4 (&hr4)[5]) {
+#pragma unroll
+    for (int pass = 0; pass < NP; ++pass) {
+      const size_t base = (size_t)tok * 4 * C + pass * 256 + lane * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xr[pass][j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * C);
+    }
+    const float4* h4 = reinterpret_cast<const float4*>(hmix + tok * kMapRows + 4);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) hr4[i] = __ldg(h4 + i);
+  };
+  if (tok0 < ntok) load_tok(tok0, xq, hq);
   for (int t = 0; t < 16; ++t) {
     const int64_t tok = tok0 + t;
     if (tok >= ntok) break;
-    float hp[4], hr[16];
-    if (fuse_post) {
+    uint4 xn[NP][4];
+    float4 hn[5];
+    if (t + 1 < 16 && tok + 1 < ntok) load_tok(tok + 1, xn, hn);
+    const float hp[4] = {hq[0].x, hq[0].y, hq[0].z, hq[0].w};
+    const float hr[16] = {hq[1].x, hq[1].y, hq[1].z, hq[1].w, hq[2].x, hq[2].y, hq[2].z, hq[2].w,
+                          hq[3].x, hq[3].y, hq[3].z, hq[3].w, hq[4].x, hq[4].y, hq[4].z, hq[4].w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) hp[i] = __ldg(hmix + tok * kMapRows + 4 + i);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) hr[i] = __ldg(hmix + tok * kMapRows + 8 + i);
-    }
-#pragma unroll
-    for (int pass = 0; pass < C / 256; ++pass) {
+    for (int pass = 0; pass < NP; ++pass) {
       const int c = pass * 256 + lane * 8;
       const uint4 yv = *reinterpret_cast<const uint4*>(uw + t * LDU + c);
-      if (!fuse_post) {
-        *reinterpret_cast<uint4*>(y + tok * C + c) = yv;
-        continue;
-      }
       const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
       const size_t base = (size_t)tok * 4 * C + c;
-      uint4 xq[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) xq[j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * C);
       uint32_t ow[4][4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float2 yf = unpack2<TU>(yw[q]);
         float2 xf[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xf[j] = unpack2<TX>((&xq[j].x)[q]);
+        for (int j = 0; j < 4; ++j) xf[j] = unpack2<TX>((&xq[pass][j].x)[q]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float* r = hr + 4 * i;
@@ -525,6 +547,12 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
       for (int i = 0; i < 4; ++i)
         *reinterpret_cast<uint4*>(xo + base + (size_t)i * C) = make_uint4(ow[i][0], ow[i][1], ow[i][2], ow[i][3]);
     }
+#pragma unroll
+    for (int pass = 0; pass < NP; ++pass)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xq[pass][j] = xn[pass][j];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) hq[i] = hn[i];
   }
 }
 
@@ -589,7 +617,8 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
       (!experts || (tc->gate && tc->up && tc->down)) &&
       (!fuse_post || x_dtype == WALSH_BF16 || x_dtype == WALSH_F16) &&
       ((((uintptr_t)u) | ((uintptr_t)tc->w1) | ((uintptr_t)tc->w2) | ((uintptr_t)tc->gate) |
-        ((uintptr_t)tc->up) | ((uintptr_t)tc->down) | ((uintptr_t)y) | ((uintptr_t)x) | ((uintptr_t)x_out)) & 15u) == 0) {
+        ((uintptr_t)tc->up) | ((uintptr_t)tc->down) | ((uintptr_t)y) | ((uintptr_t)x) | ((uintptr_t)x_out) |
+        ((uintptr_t)hmix)) & 15u) == 0) {
     const bool xh = fuse_post && x_dtype == WALSH_F16;  // stream type of the fused epilogue
     if (dtype == WALSH_F16)
       return xh ? launch_moe_mma<__half, __half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out,
