@@ -66,16 +66,26 @@ chmod_stats_vec_kernel(const T* __restrict__ x, int seg_len, const float* __rest
   for (int p = 0; p < NP; ++p)
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[p][e] = 0.f;
-  for (int r = warp; r < nr; r += 8) {
+  // the warp's next row is loaded before the current one is used
+  Vec8<T> cur[NP], nxt[NP];
+  auto load_row = [&](int r, Vec8<T> (&dst)[NP]) {
     const T* xr = x + (row0 + r) * C;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) dst[p] = ld_vec8(xr + p * 256 + lane * 8);
+  };
+  if (warp < nr) load_row(warp, cur);
+  for (int r = warp; r < nr; r += 8) {
+    if (r + 8 < nr) load_row(r + 8, nxt);
     float v[NP][8];
     float s = 0.f;
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
-      load8(xr + p * 256 + lane * 8, v[p]);
+      unpack_vec8(cur[p], v[p]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) s = fmaf(v[p][e], v[p][e], s);
     }
+#pragma unroll
+    for (int p = 0; p < NP; ++p) cur[p] = nxt[p];
     s = warp_sum(s);
     const float inv = w ? rsqrtf(s / (float)C + eps) : 1.0f;
 #pragma unroll
@@ -109,15 +119,31 @@ chmod_apply_vec_kernel(const T* x, int64_t nrows, int seg_len, const float* __re
   for (int p = 0; p < NP; ++p)
 #pragma unroll
     for (int e = 0; e < 8; ++e) wv[p][e] = w ? __ldg(w + p * 256 + lane * 8 + e) : 1.f;
-  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < nrows; row += (int64_t)gridDim.x * 8) {
+  // the warp's next row is loaded before the current one is stored (rows are
+  // disjoint, so this is safe when out aliases x)
+  const int64_t stride = (int64_t)gridDim.x * 8, first = (int64_t)blockIdx.x * 8 + warp;
+  Vec8<T> cur[NP], nxt[NP];
+  auto load_row = [&](int64_t row, Vec8<T> (&dst)[NP]) {
     const T* xr = x + row * C;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) dst[p] = ld_vec8(xr + p * 256 + lane * 8);
+  };
+  constexpr bool PF = NP <= 2;  // two rows in registers only for C = 512
+  if (PF && first < nrows) load_row(first, cur);
+  for (int64_t row = first; row < nrows; row += stride) {
+    if (!PF) load_row(row, cur);
+    else if (row + stride < nrows) load_row(row + stride, nxt);
     float v[NP][8];
     float s = 0.f;
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
-      load8(xr + p * 256 + lane * 8, v[p]);
+      unpack_vec8(cur[p], v[p]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) s = fmaf(v[p][e], v[p][e], s);
+    }
+    if (PF) {
+#pragma unroll
+      for (int p = 0; p < NP; ++p) cur[p] = nxt[p];
     }
     s = warp_sum(s);
     const float r = w ? rsqrtf(s / (float)C + eps) : 1.0f;

@@ -64,6 +64,38 @@ __device__ __forceinline__ void unpack8(const uint4 q, float* v, const T16*) {
     v[2 * i + 1] = to_f(hi);
   }
 }
+// 8 consecutive elements held raw in registers (loaded ahead of use), then
+// converted to float: one 16-byte vector for 16-bit types, two for float.
+template <typename T>
+struct Vec8 {
+  uint4 a;
+};
+template <>
+struct Vec8<float> {
+  float4 a, b;
+};
+template <typename T>
+__device__ __forceinline__ Vec8<T> ld_vec8(const T* p) {
+  Vec8<T> r;
+  r.a = *reinterpret_cast<const uint4*>(p);
+  return r;
+}
+template <>
+__device__ __forceinline__ Vec8<float> ld_vec8<float>(const float* p) {
+  Vec8<float> r;
+  r.a = *reinterpret_cast<const float4*>(p);
+  r.b = *reinterpret_cast<const float4*>(p + 4);
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ void unpack_vec8(const Vec8<T>& r, float* v) {
+  unpack8(r.a, v, (const T*)nullptr);
+}
+template <>
+__device__ __forceinline__ void unpack_vec8<float>(const Vec8<float>& r, float* v) {
+  v[0] = r.a.x; v[1] = r.a.y; v[2] = r.a.z; v[3] = r.a.w;
+  v[4] = r.b.x; v[5] = r.b.y; v[6] = r.b.z; v[7] = r.b.w;
+}
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) { load8_16(p, v); }
 __device__ __forceinline__ void load8(const __half* p, float* v) { load8_16(p, v); }
 

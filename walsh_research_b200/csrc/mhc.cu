@@ -263,28 +263,49 @@ mhc_map_mma_kernel(const TX* __restrict__ x, int64_t ntok, const TX* __restrict_
     }
   }
   __syncwarp();
-  // pre-mix u = sum_j H_pre[j] x_j and the block RMSNorm, 8 columns per lane per step
+  // pre-mix u = sum_j H_pre[j] x_j and the block RMSNorm, 8 columns per lane per step;
+  // for C = 512 token t + 1's stream rows are loaded before token t is computed
   constexpr int VPL = C / 256;  // uint4 chunks per lane
+  constexpr bool PREFETCH = VPL <= 2;  // two tokens' rows fit in registers
+  uint4 xr[VPL][4];
+  auto load_tok = [&](int64_t tok, uint4 (&dst)[VPL][4]) {
+    const TX* xt = x + tok * D;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[v][j] = __ldg(reinterpret_cast<const uint4*>(xt + j * C + (lane + 32 * v) * 8));
+  };
+  if (PREFETCH && tok0 < ntok) load_tok(tok0, xr);
   for (int t = 0; t < 16; ++t) {
     const int64_t tok = tok0 + t;
     if (tok >= ntok) break;
+    uint4 xn[VPL][4];
+    if (PREFETCH) {
+      if (t + 1 < 16 && tok + 1 < ntok) load_tok(tok + 1, xn);
+    } else {
+      load_tok(tok, xr);
+    }
     const float h0 = ds[warp][t][0], h1 = ds[warp][t][1], h2 = ds[warp][t][2], h3 = ds[warp][t][3];
-    const TX* xt = x + tok * D;
     float uv[VPL][8];
     float s2 = 0.f;
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
-      const int c = (lane + 32 * v) * 8;
       float f0[8], f1[8], f2[8], f3[8];
-      load8(xt + c, f0);
-      load8(xt + C + c, f1);
-      load8(xt + 2 * C + c, f2);
-      load8(xt + 3 * C + c, f3);
+      unpack8(xr[v][0], f0, (const TX*)nullptr);
+      unpack8(xr[v][1], f1, (const TX*)nullptr);
+      unpack8(xr[v][2], f2, (const TX*)nullptr);
+      unpack8(xr[v][3], f3, (const TX*)nullptr);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         uv[v][e] = ((h0 * f0[e] + h1 * f1[e]) + h2 * f2[e]) + h3 * f3[e];
         s2 = fmaf(uv[v][e], uv[v][e], s2);
       }
+    }
+    if (PREFETCH) {
+#pragma unroll
+      for (int v = 0; v < VPL; ++v)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xr[v][j] = xn[v][j];
     }
     s2 = warp_sum(s2);
     const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
