@@ -261,6 +261,23 @@ walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int to
                            float* probs_out, float* weights_out, const walsh_moe_tc_weights* tc,
                            void* stream);
 
+/* MoE after router layer 1 (for decode-sized token counts): hpre = u W1^T
+ * [ntok, C/4] (u's dtype, computed by the caller, e.g. walsh_octo_linear_fwd
+ * with the router's W1 and unit scales); then per token silu, logits =
+ * W2 silu(hpre), softmax, top_k experts (ties to the lower index), weights
+ * renormalised over the selected experts, only the selected ternary experts,
+ * and either y (fuse_post = 0) or the mHC site epilogue into x_out (as for
+ * walsh_moe_fwd).  C = 512 or 2048; w2 float32 [E, C/4] 16-byte aligned;
+ * expert weights as for walsh_moe_fwd.  mask/probs/weights optional.
+ * Replaces HadamardRouter.forward layer 2 onward and HadamardMoE.forward
+ * (src/model/moe.py:418-447, 337-380, 512-542). */
+walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, int dtype, int64_t ntok, int C,
+                                  int top_k, const float* w2, const uint8_t* gate_2bit,
+                                  const uint8_t* up_2bit, const uint8_t* down_2bit,
+                                  const float* gammas, void* y, int fuse_post, const void* x,
+                                  int x_dtype, const float* hmix, void* x_out, uint8_t* mask_out,
+                                  float* probs_out, float* weights_out, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Octonion (Cayley-Dickson) layers as tensor-core GEMMs
  *

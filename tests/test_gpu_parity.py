@@ -544,15 +544,16 @@ def test_decode_attention_vs_oracle(hd, Tq, start, ctx, dtype):
 
 
 @pytest.mark.parametrize("udt", [torch.bfloat16, torch.float16])
-def test_moe_tensor_core_vs_oracle(udt):
-    """Tensor-core MoE (router + dense experts) on 3000 tokens with the fused
-    mHC epilogue (bf16 stream): selection sets equal the oracle's wherever the
-    k-th/(k+1)-th probability gap exceeds the router's rounding error; outputs
-    within 2e-2."""
+@pytest.mark.parametrize("n", [3000, 10000])
+def test_moe_tensor_core_vs_oracle(udt, n):
+    """16-bit MoE with the fused mHC epilogue (bf16 stream) at a decode-sized
+    token count (router GEMM + warp-per-token kernel) and a prefill-sized one
+    (128-token tensor-core kernel): selection sets equal the oracle's wherever
+    the k-th/(k+1)-th probability gap exceeds the router's rounding error;
+    outputs within 2e-2."""
     from walsh_research_b200 import ops
     d = cases.op_case("moe")
     rng = np.random.default_rng(19)
-    n = 3000
     x = rng.normal(size=(n, 512)).astype(np.float32)
     m = _moe_module(d)
     w1t, w2, gp, up, dp, gam, k, tc = m.kernel_args(udt)
@@ -575,6 +576,44 @@ def test_moe_tensor_core_vs_oracle(udt):
     fused = ops.moe(xb, w1t, w2, gp, up, dp, gam, k, fuse=(xs, hm, torch.empty_like(xs)), tc=tc)
     ref = ops.mhc_post(xs, y.to(xs.dtype), hm)
     assert rel(fused, ref.float().cpu().numpy()) < 1e-2
+
+
+@pytest.mark.parametrize("udt", [torch.bfloat16, torch.float16])
+def test_moe_decode_path_c2048_vs_oracle(udt):
+    """C = 2048 (64 experts, top 6) through the router GEMM + warp-per-token
+    kernel: the oracle run with the GPU's own selections gives the same output;
+    selections differ from the oracle's own only on near-ties."""
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model import WalshConfig
+    from walsh_research_b200.model.moe import HadamardMoE
+    rng = np.random.default_rng(23)
+    m = HadamardMoE(WalshConfig(n_embd=2048), max_experts=6)
+    with torch.no_grad():
+        m.router.gate[0].weight.copy_(torch.from_numpy(rng.normal(0, 0.03, (512, 2048)).astype(np.float32)))
+        m.router.gate[2].weight.copy_(torch.from_numpy(rng.normal(0, 0.1, (64, 512)).astype(np.float32)))
+        for w in (m.experts.gate_weights, m.experts.up_weights, m.experts.down_weights):
+            w.copy_(torch.from_numpy(rng.integers(-1, 2, tuple(w.shape)).astype(np.float32)))
+    m = m.to(DEV).eval()
+    n = 77
+    xb = T(rng.normal(size=(n, 2048)).astype(np.float32), udt)
+    w1t, w2, gp, up, dp, gam, k, tc = m.kernel_args(udt)
+    y, mask, probs, w = ops.moe(xb, w1t, w2, gp, up, dp, gam, k, want_stats=True, tc=tc)
+    p = {"r.router.gate.0.weight": m.router.gate[0].weight.detach().cpu().numpy(),
+         "r.router.gate.2.weight": m.router.gate[2].weight.detach().cpu().numpy(),
+         "r.experts.gate_weights": m.experts.gate_weights.detach().cpu().numpy(),
+         "r.experts.up_weights": m.experts.up_weights.detach().cpu().numpy(),
+         "r.experts.down_weights": m.experts.down_weights.detach().cpu().numpy()}
+    xr = xb.float().cpu().numpy().astype(np.float64)
+    mk = mask.cpu().numpy().astype(np.float64)
+    assert (mk.sum(-1) == 6).all()
+    y_ref, _, probs_ref = O.moe(xr, p, "r.", 6, forced_mask=mk)
+    # router hidden layer stored in the operand dtype: bf16 keeps 8 bits, fp16 11
+    assert np.abs(probs.cpu().numpy() - probs_ref).max() < (5e-3 if udt == torch.float16 else 2e-2)
+    assert rel(y, y_ref) < 2e-2
+    _, own, _ = O.moe(xr, p, "r.", 6)
+    srt = -np.sort(-probs_ref, axis=-1)
+    near = (srt[..., 5] - srt[..., 6]) < (5e-3 if udt == torch.float16 else 2e-2)
+    assert not ((own != mk).any(-1) & ~near).any()
 
 
 # ---------------------------------------------------------------------------

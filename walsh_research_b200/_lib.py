@@ -48,6 +48,8 @@ SIGNATURES = {
                            P],
     "walsh_octo_swiglu_fwd": [P, c_int, c_int64, c_int, P, P, c_int, P, c_int64, P, P],
     "walsh_octo_post_fwd": [P, c_int, c_int64, c_int, P, P, c_int, P, c_int, P, c_int, P, P, P],
+    "walsh_moe_hidden_fwd": [P, P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, c_int, P, c_int, P, P, P, P, P,
+                             P],
     "walsh_chmod_chunk_rows": [c_int],
     "walsh_chmod_stats": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P],
     "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],

@@ -556,6 +556,216 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode-sized MoE (a few hundred tokens): router layer 1 is a tcgen05 GEMM
+// done by the caller (hpre = u W1^T, one row per token); this kernel runs one
+// warp per token for the rest: silu, router layer 2 (lane e holds expert e),
+// softmax, top-k (ties to the lower index), renormalisation over the selected
+// experts in ascending order, only the k selected ternary experts (gate/up
+// hidden units 4 per lane, down outputs 1 per lane), and the mHC site
+// epilogue.  Weights stay in L2; per-warp scratch (silu(hpre), the expert
+// hidden activations and the output row) is in shared memory.
+// ---------------------------------------------------------------------------
+template <typename TU, typename TX, int C>
+__global__ void __launch_bounds__(256)
+moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, int top_k,
+                 const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
+                 const uint8_t* __restrict__ dp, const float* __restrict__ gammas, TU* __restrict__ y,
+                 int fuse_post, const TX* x, const float* __restrict__ hmix, TX* xo, uint8_t* __restrict__ mask_out,
+                 float* __restrict__ probs_out, float* __restrict__ weights_out) {
+  constexpr int E = C / 32, HID = C / 4, EH = kExpertHidden, PER = HID + C + EH;
+  constexpr int EL = (E + 31) / 32;  // experts per lane (1 for E = 16, 2 for E = 64)
+  extern __shared__ float4 smem4[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* hs = reinterpret_cast<float*>(smem4) + warp * PER;  // [HID]
+  float* ys = hs + HID;                                        // [C]
+  float* as = ys + C;                                          // [EH]
+  const int64_t tok = (int64_t)blockIdx.x * 8 + warp;
+  if (tok >= ntok) return;  // whole warp
+  // silu of router layer 1
+  for (int j = lane; j < HID; j += 32) {
+    const float v = to_f(hpre[tok * HID + j]);
+    hs[j] = v / (1.0f + expf(-v));
+  }
+  for (int c = lane; c < C; c += 32) ys[c] = 0.f;
+  __syncwarp();
+  // router layer 2 and softmax
+  float l[EL], p[EL];
+#pragma unroll
+  for (int q = 0; q < EL; ++q) {
+    const int e = lane + 32 * q;
+    float acc = 0.f;
+    if (e < E) {
+      const float4* wr = reinterpret_cast<const float4*>(w2 + (size_t)e * HID);
+#pragma unroll 4
+      for (int j4 = 0; j4 < HID / 4; ++j4) {
+        const float4 w = __ldg(wr + j4);
+        acc = fmaf(hs[4 * j4], w.x, acc);
+        acc = fmaf(hs[4 * j4 + 1], w.y, acc);
+        acc = fmaf(hs[4 * j4 + 2], w.z, acc);
+        acc = fmaf(hs[4 * j4 + 3], w.w, acc);
+      }
+    }
+    l[q] = e < E ? acc : -CUDART_INF_F;
+  }
+  float mx = l[0];
+#pragma unroll
+  for (int q = 1; q < EL; ++q) mx = fmaxf(mx, l[q]);
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int q = 0; q < EL; ++q) {
+    p[q] = (lane + 32 * q < E) ? expf(l[q] - mx) : 0.f;
+    sum += p[q];
+  }
+  sum = warp_sum(sum);
+#pragma unroll
+  for (int q = 0; q < EL; ++q) p[q] = __fdiv_rn(p[q], sum);
+  // top-k by warp arg-max; ties go to the lower expert index
+  uint32_t chosen = 0;  // bit q: this lane's expert lane + 32 q
+  int sel[8];
+  for (int k = 0; k < top_k; ++k) {
+    float bv = -2.f;
+    int bi = E;
+#pragma unroll
+    for (int q = 0; q < EL; ++q) {
+      const int e = lane + 32 * q;
+      const float v = (e < E && !((chosen >> q) & 1u)) ? p[q] : -1.f;
+      if (v > bv) { bv = v; bi = e; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (bi >= E || bv < 0.f) {  // non-finite scores: the lowest expert not yet chosen
+      bi = E;
+      for (int e = E - 1; e >= 0; --e) {
+        const uint32_t cb = __shfl_sync(0xffffffffu, chosen, e & 31);
+        if (!((cb >> (e >> 5)) & 1u)) bi = e;
+      }
+    }
+    sel[k] = bi;
+    if ((bi & 31) == lane) chosen |= 1u << (bi >> 5);
+  }
+  // renormalise over the selected probabilities, summed in ascending expert order
+  float wsum = 0.f;
+  for (int e = 0; e < E; ++e) {
+    const float pe = __shfl_sync(0xffffffffu, p[e >> 5 < EL ? e >> 5 : 0], e & 31);
+    const uint32_t cb = __shfl_sync(0xffffffffu, chosen, e & 31);
+    if ((cb >> (e >> 5)) & 1u) wsum += pe;
+  }
+  wsum = fmaxf(wsum, 1e-8f);
+#pragma unroll
+  for (int q = 0; q < EL; ++q) {
+    const int e = lane + 32 * q;
+    if (e < E) {
+      const bool on = (chosen >> q) & 1u;
+      if (mask_out) mask_out[tok * E + e] = on ? 1 : 0;
+      if (probs_out) probs_out[tok * E + e] = p[q];
+      if (weights_out) weights_out[tok * E + e] = on ? __fdiv_rn(p[q], wsum) : 0.f;
+    }
+  }
+  // the selected experts
+  const float gg = __ldg(gammas + 0), gu = __ldg(gammas + 1), gd = __ldg(gammas + 2);
+  for (int k = 0; k < top_k; ++k) {
+    const int e = sel[k];
+    const float pe = __shfl_sync(0xffffffffu, p[e >> 5 < EL ? e >> 5 : 0], e & 31);
+    const float wgt = __fdiv_rn(pe, wsum);
+    const float ub = to_f(u[tok * C + e * 32 + lane]);  // lane k holds input k of the block
+    float ga[4] = {0.f, 0.f, 0.f, 0.f}, ua[4] = {0.f, 0.f, 0.f, 0.f};
+    uint2 gw[4], uw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int h = lane + 32 * i;
+      gw[i] = __ldg(reinterpret_cast<const uint2*>(gp + ((size_t)e * EH + h) * 8));
+      uw[i] = __ldg(reinterpret_cast<const uint2*>(upp + ((size_t)e * EH + h) * 8));
+    }
+#pragma unroll
+    for (int bb = 0; bb < 8; ++bb) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float xv = __shfl_sync(0xffffffffu, ub, bb * 4 + j);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t gbyte = ((bb < 4 ? gw[i].x : gw[i].y) >> (8 * (bb & 3))) & 0xffu;
+          const uint32_t ubyte = ((bb < 4 ? uw[i].x : uw[i].y) >> (8 * (bb & 3))) & 0xffu;
+          ga[i] = fmaf(tern_val(gbyte, j), xv, ga[i]);
+          ua[i] = fmaf(tern_val(ubyte, j), xv, ua[i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float g = ga[i] * gg, v = ua[i] * gu;
+      as[lane + 32 * i] = (g / (1.0f + expf(-g))) * v;
+    }
+    __syncwarp();
+    const uint4* drow = reinterpret_cast<const uint4*>(dp + ((size_t)e * 32 + lane) * 32);
+    float acc = 0.f;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const uint4 dw = __ldg(drow + v);
+      const uint32_t words[4] = {dw.x, dw.y, dw.z, dw.w};
+#pragma unroll
+      for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+          const uint32_t byte = (words[wi] >> (8 * bb)) & 0xffu;
+          const int h0 = v * 64 + wi * 16 + bb * 4;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc = fmaf(tern_val(byte, j), as[h0 + j], acc);
+        }
+    }
+    ys[e * 32 + lane] = acc * gd * wgt;
+    __syncwarp();
+  }
+  // output row, or the mHC site epilogue
+  if (!fuse_post) {
+    for (int c = lane; c < C; c += 32) y[tok * C + c] = from_f<TU>(ys[c]);
+    return;
+  }
+  const float* hm = hmix + tok * kMapRows;
+  float hp[4], hr[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hp[i] = __ldg(hm + 4 + i);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) hr[i] = __ldg(hm + 8 + i);
+  for (int c = lane * 8; c < C; c += 256) {
+    const size_t base = (size_t)tok * 4 * C + c;
+    float xs[4][8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) load8(x + base + (size_t)j * C, xs[j]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float o[8];
+#pragma unroll
+      for (int e8 = 0; e8 < 8; ++e8)
+        o[e8] = (((hr[4 * r] * xs[0][e8] + hr[4 * r + 1] * xs[1][e8]) + hr[4 * r + 2] * xs[2][e8]) +
+                 hr[4 * r + 3] * xs[3][e8]) + hp[r] * ys[c + e8];
+      store8(xo + base + (size_t)r * C, o);
+    }
+  }
+}
+
+template <typename TU, typename TX, int C>
+static int launch_moe_token(const void* u, const void* hpre, int64_t ntok, int top_k, const float* w2,
+                            const uint8_t* gp, const uint8_t* upp, const uint8_t* dp, const float* gammas, void* y,
+                            int fuse_post, const void* x, const float* hmix, void* xo, uint8_t* mask_out,
+                            float* probs_out, float* weights_out, cudaStream_t s) {
+  constexpr int PER = C / 4 + C + kExpertHidden;
+  const int smem = 8 * PER * (int)sizeof(float);
+  auto kern = moe_token_kernel<TU, TX, C>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return launch_status();
+  kern<<<(unsigned)((ntok + 7) / 8), 256, smem, s>>>((const TU*)u, (const TU*)hpre, ntok, top_k, w2, gp, upp, dp,
+                                                     gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo,
+                                                     mask_out, probs_out, weights_out);
+  return launch_status();
+}
+
 template <typename T, typename TX, int C>
 static int launch_moe(const void* u, int64_t ntok, int top_k, const float* w1t, const float* w2, const uint8_t* gp,
                       const uint8_t* upp, const uint8_t* dp, const float* gammas, void* y, int fuse_post,
@@ -637,4 +847,28 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
                : launch_moe<TU, TX, 2048>(u, ntok, top_k, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y,
                                           fuse_post, x, hmix, x_out, weights_in, mask_out, probs_out, weights_out,
                                           s)));
+}
+
+extern "C" walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, int dtype, int64_t ntok, int C,
+                                             int top_k, const float* w2, const uint8_t* gate_2bit,
+                                             const uint8_t* up_2bit, const uint8_t* down_2bit, const float* gammas,
+                                             void* y, int fuse_post, const void* x, int x_dtype, const float* hmix,
+                                             void* x_out, uint8_t* mask_out, float* probs_out, float* weights_out,
+                                             void* stream) {
+  if (int e = injected("moe_hidden_fwd")) return e;
+  WALSH_CHECK_DTYPE(dtype);
+  WALSH_CHECK_DTYPE(x_dtype);
+  WALSH_CHECK_ARG(u && hpre && w2 && gate_2bit && up_2bit && down_2bit && gammas);
+  WALSH_CHECK_ARG(fuse_post ? (x && hmix && x_out) : (y != nullptr));
+  WALSH_CHECK_SHAPE(ntok >= 0 && (C == 512 || C == 2048));
+  WALSH_CHECK_SHAPE(top_k >= 1 && top_k <= 8 && top_k <= C / 32);
+  WALSH_CHECK_ARG(((((uintptr_t)gate_2bit | (uintptr_t)up_2bit) & 7u) == 0) && (((uintptr_t)down_2bit & 15u) == 0) &&
+                  (((uintptr_t)w2 & 15u) == 0) && (!fuse_post || ((((uintptr_t)x) | ((uintptr_t)x_out)) & 15u) == 0));
+  if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  return WALSH_DISPATCH_DTYPE(dtype, TU, WALSH_DISPATCH_DTYPE(x_dtype, TX,
+      C == 512 ? launch_moe_token<TU, TX, 512>(u, hpre, ntok, top_k, w2, gate_2bit, up_2bit, down_2bit, gammas, y,
+                                               fuse_post, x, hmix, x_out, mask_out, probs_out, weights_out, s)
+               : launch_moe_token<TU, TX, 2048>(u, hpre, ntok, top_k, w2, gate_2bit, up_2bit, down_2bit, gammas,
+                                                y, fuse_post, x, hmix, x_out, mask_out, probs_out, weights_out, s)));
 }

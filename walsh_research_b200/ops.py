@@ -154,6 +154,19 @@ def sinkhorn(h, iters=20, eps=1e-8):
 # MoE and channel modulation
 # ---------------------------------------------------------------------------
 
+# below this many tokens (about a wave of 64-token tiles) the MoE runs as a
+# router GEMM plus the warp-per-token kernel instead of the 128-token kernels
+MOE_GEMM_ROUTER_BELOW = 148 * 64
+_ONES = {}
+
+
+def _ones(n, device):
+    key = (n, str(device))
+    if key not in _ONES:
+        _ONES[key] = torch.ones(n, dtype=torch.float32, device=device)
+    return _ONES[key]
+
+
 def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=None, want_stats=False, tc=None):
     """Router + experts.  With ``fuse=(x, hmix, x_out)`` the mHC epilogue is
     applied and ``x_out`` returned; otherwise the expert output y.
@@ -176,6 +189,19 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
         weights = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
     if weights_in is not None:
         weights_in = _c(weights_in.float())
+    if (tc is not None and gate_p is not None and weights_in is None and u.dtype != torch.float32
+            and C in (512, 2048) and ntok < MOE_GEMM_ROUTER_BELOW and tc[0].dtype == u.dtype):
+        # decode-sized: router layer 1 as a tcgen05 GEMM, the rest one warp per token
+        hid = C // 4
+        hpre = octo_linear(u.view(ntok, C), (tc[0], None), _ones(hid, u.device))
+        x, hmix, x_out = fuse if fuse is not None else (None, None, None)
+        y = torch.empty_like(u) if fuse is None else None
+        call("walsh_moe_hidden_fwd", ptr(u), ptr(hpre), dcode(u.dtype), ntok, C, int(top_k), ptr(w2), ptr(gate_p),
+             ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0 if fuse is None else 1, ptr(x),
+             dcode(x.dtype) if x is not None else dcode(u.dtype), ptr(hmix), ptr(x_out), ptr(mask), ptr(probs),
+             ptr(weights), stream())
+        out = y if fuse is None else x_out
+        return (out, mask, probs, weights) if want_stats else out
     if fuse is None:
         y = torch.empty_like(u)
         call("walsh_moe_fwd", ptr(u), dcode(u.dtype), ntok, C, int(top_k), ptr(w1t), ptr(w2), ptr(gate_p),
