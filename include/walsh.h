@@ -299,11 +299,19 @@ walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, int dtype, in
  * mainloops, e.g. to compare them in tests). */
 int walsh_octo_set_mainloop(int tcgen05);
 
-/* Status word of the tcgen05 kernels on the current device: 0, or
- * WALSH_ERR_TIMEOUT once a bounded wait inside one of them gave up (the
- * affected tile is not written).  Synchronous read; reset != 0 clears it.
- * No counterpart in the reference. */
+/* Status word of the tcgen05 kernels (GEMMs and prefill attention) on the
+ * current device: 0, or WALSH_ERR_TIMEOUT once a bounded wait inside one of
+ * them gave up (the affected tile is not written).  Synchronous read;
+ * reset != 0 clears it.  No counterpart in the reference. */
 int walsh_tc05_error(int reset);
+
+/* tcgen05 != 0: fp16 prefill attention with head dim 16 and at most 1024
+ * keys runs on the 5th-generation tensor cores (S and P V as tcgen05 MMAs
+ * into Tensor Memory); 0 (the default, faster at head dim 16): the mma.sync
+ * kernels of walsh_attn_fwd.  Returns the previous setting.  Process-wide.
+ * No counterpart in the reference (selects between this library's own
+ * kernels, e.g. to compare them in tests). */
+int walsh_attn_set_path(int tcgen05);
 
 /* Test hook for the bounded waits: one thread waits on an mbarrier that is
  * never arrived at, gives up after budget_cycles SM clocks (at most 4e9) and

@@ -42,6 +42,7 @@ SIGNATURES = {
                       P],
     "walsh_octo_set_mainloop": [c_int],
     "walsh_tc05_error": [c_int],
+    "walsh_attn_set_path": [c_int],
     "walsh_tc05_wait_selftest": [ctypes.c_longlong, P],
     "walsh_octo_linear_fwd": [P, c_int, c_int64, c_int, P, P, c_int, c_int64, P, P, P],
     "walsh_octo_qkv_fwd": [P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int, P, P, P, c_int,
@@ -63,12 +64,12 @@ SIGNATURES = {
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p}
 # kernels each entry point launches (for the launch accounting reported by bench.py)
 KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_octo_set_mainloop": 0,
-                    "walsh_tc05_error": 0, "walsh_map_error": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
+                    "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
                     "walsh_abi_version": 0}
 launch_count = 0
 # entry points that return a plain int rather than a status
 _PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows", "walsh_octo_set_mainloop", "walsh_tc05_error",
-              "walsh_map_error"}
+              "walsh_map_error", "walsh_attn_set_path"}
 
 
 class MoeTcWeights(ctypes.Structure):

@@ -438,11 +438,12 @@ attn_mma_kernel(const TE* __restrict__ q, const TE* __restrict__ kc, const TE* _
 // conflict-free ldmatrix) in shared memory, loaded once with cp.async; the 8
 // warps then run 16-row query tiles independently (no barriers), tiles
 // dealt out snake-wise (w, 15 - w, 16 + w, ...) so every warp gets the same
-// causal work.  Per 64-key step: S = Q K^T (8 MMAs), row maxima, P = 2^(S
-// scale - m) as paired fp16 ex2, O += P V and the row sums of P (all-ones
-// V column) on the tensor cores.  The reference maximum m of a row only
-// moves when the row maximum exceeds it by more than 8 (P <= 256 in fp16),
-// so the O rescale is rare.
+// causal work.  Per 64-key step: S - m = Q K^T - m (8 MMAs whose addend is
+// the row's reference maximum), row maxima, P = 2^(S - m) as paired fp16
+// ex2, O += P V and the row sums of P (all-ones V column) on the tensor
+// cores.  The reference maximum m of a row only moves when the row maximum
+// exceeds it by more than 8 (P <= 256 in fp16), so the O rescale (and the
+// explicit subtraction of the shift) is rare.
 // ---------------------------------------------------------------------------
 constexpr int kAttnHeadMaxKeys = 2048;
 // Bit n set: exponent pairs of n-tile n (of the 8 per 64-key step) are
@@ -505,20 +506,23 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
     }
     const int qp_lo = start_pos + r_lo, qp_hi = start_pos + r_hi;  // query positions
     const int nkey = min(kend, start_pos + q0 + 16);                // keys visible to some row
-    float m_lo = -CUDART_INF_F, m_hi = -CUDART_INF_F;               // reference maxima (exp2 domain)
+    // reference maxima (exp2 domain): 0 until a row sees its first key; the MMA
+    // starts from -m, so S - m comes out of the tensor core
+    float m_lo = 0.f, m_hi = 0.f;
+    // a row's reference maximum moves once its row maximum passes m + thr:
+    // thr = -inf until the row's first visible key, 8 after (P <= 256 in fp16)
+    float thr_lo = -CUDART_INF_F, thr_hi = -CUDART_INF_F;
     float oacc[HD / 8 + 1][4];
 #pragma unroll
     for (int j = 0; j < HD / 8 + 1; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
     for (int k0 = 0; k0 < nkey; k0 += KT) {
       float s[KT / 8][4];
 #pragma unroll
-      for (int n = 0; n < KT / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
       for (int np = 0; np < KT / 16; ++np) {
         uint32_t kf[4];
         ldsm_x4(kf, Ks + (k0 + np * 16 + (lane & 7) + ((lane >> 4) << 3)) * LD + ((lane >> 3) & 1) * 8);
-        mma_f16(s[2 * np], qf, kf[0], kf[1]);
-        mma_f16(s[2 * np + 1], qf, kf[2], kf[3]);
+        mma_f16_rowc(s[2 * np], qf, kf[0], kf[1], -m_lo, -m_hi);
+        mma_f16_rowc(s[2 * np + 1], qf, kf[2], kf[3], -m_lo, -m_hi);
       }
       // keys past a row's position (or past kend) are masked
       const bool edge = k0 + KT > start_pos + q0 || k0 + KT > kend;
@@ -532,6 +536,7 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
             if (key > qp_hi || key >= kend) s[n][2 + e] = -CUDART_INF_F;
           }
       }
+      // row maxima of S - m
       float mt_lo = -CUDART_INF_F, mt_hi = -CUDART_INF_F;
 #pragma unroll
       for (int n = 0; n < KT / 8; ++n) {
@@ -543,33 +548,40 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
         mt_lo = fmaxf(mt_lo, __shfl_xor_sync(0xffffffffu, mt_lo, off));
         mt_hi = fmaxf(mt_hi, __shfl_xor_sync(0xffffffffu, mt_hi, off));
       }
-      // move a reference maximum only when the row maximum passes it by more than 8
-      const bool mv_lo = mt_lo > m_lo + 8.f, mv_hi = mt_hi > m_hi + 8.f;
+      const bool mv_lo = mt_lo > thr_lo, mv_hi = mt_hi > thr_hi;
       if (__any_sync(0xffffffffu, mv_lo || mv_hi)) {
-        const float nm_lo = mv_lo ? mt_lo : m_lo, nm_hi = mv_hi ? mt_hi : m_hi;
-        const float c_lo = m_lo == -CUDART_INF_F ? 0.f : ex2_f32(m_lo - nm_lo);
-        const float c_hi = m_hi == -CUDART_INF_F ? 0.f : ex2_f32(m_hi - nm_hi);
+        // move m by d = the step's row maximum: O *= 2^-d, this step's S - m -= d
+        // (before a row's first key O is zero and stays so: factor 0, as 2^-d may overflow)
+        const float d_lo = mv_lo ? mt_lo : 0.f, d_hi = mv_hi ? mt_hi : 0.f;
+        const float c_lo = thr_lo == -CUDART_INF_F ? 0.f : ex2_f32(-d_lo);
+        const float c_hi = thr_hi == -CUDART_INF_F ? 0.f : ex2_f32(-d_hi);
 #pragma unroll
         for (int j = 0; j < HD / 8 + 1; ++j) {
           oacc[j][0] *= c_lo; oacc[j][1] *= c_lo;
           oacc[j][2] *= c_hi; oacc[j][3] *= c_hi;
         }
-        m_lo = nm_lo;
-        m_hi = nm_hi;
+#pragma unroll
+        for (int n = 0; n < KT / 8; ++n) {
+          s[n][0] -= d_lo; s[n][1] -= d_lo;
+          s[n][2] -= d_hi; s[n][3] -= d_hi;
+        }
+        m_lo += d_lo;
+        m_hi += d_hi;
+        if (mv_lo) thr_lo = 8.f;
+        if (mv_hi) thr_hi = 8.f;
       }
-      // rows with no visible key yet keep m = -inf and P = 2^-inf = 0
-      const float sub_lo = m_lo == -CUDART_INF_F ? 0.f : m_lo, sub_hi = m_hi == -CUDART_INF_F ? 0.f : m_hi;
-      // P = 2^(S - m): the pairs selected by WALSH_ATTN_POLY_PAIRS on the FMA pipe, the
-      // rest as paired fp16 ex2 on the MUFU pipe (which would otherwise bound the kernel)
+      // P = 2^(S - m) (rows with no visible key yet: 2^-inf = 0): the pairs selected
+      // by WALSH_ATTN_POLY_PAIRS on the FMA pipe, the rest as paired fp16 ex2 on
+      // the MUFU pipe
       uint32_t pf[KT / 16][4];
 #pragma unroll
       for (int n = 0; n < KT / 8; ++n) {
         if ((WALSH_ATTN_POLY_PAIRS >> n) & 1) {
-          pf[n >> 1][(n & 1) * 2 + 0] = pack_f16(exp2_poly(s[n][0] - sub_lo), exp2_poly(s[n][1] - sub_lo));
-          pf[n >> 1][(n & 1) * 2 + 1] = pack_f16(exp2_poly(s[n][2] - sub_hi), exp2_poly(s[n][3] - sub_hi));
+          pf[n >> 1][(n & 1) * 2 + 0] = pack_f16(exp2_poly(s[n][0]), exp2_poly(s[n][1]));
+          pf[n >> 1][(n & 1) * 2 + 1] = pack_f16(exp2_poly(s[n][2]), exp2_poly(s[n][3]));
         } else {
-          pf[n >> 1][(n & 1) * 2 + 0] = ex2_f16x2(pack_f16(s[n][0] - sub_lo, s[n][1] - sub_lo));
-          pf[n >> 1][(n & 1) * 2 + 1] = ex2_f16x2(pack_f16(s[n][2] - sub_hi, s[n][3] - sub_hi));
+          pf[n >> 1][(n & 1) * 2 + 0] = ex2_f16x2(pack_f16(s[n][0], s[n][1]));
+          pf[n >> 1][(n & 1) * 2 + 1] = ex2_f16x2(pack_f16(s[n][2], s[n][3]));
         }
       }
 #pragma unroll
@@ -595,12 +607,17 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
   }
 }
 
+// tcgen05 prefill kernel (attention_tc.cu): 1 when it ran, 0 when it does not apply
+int launch_attn_tc05(const void* q, const void* kc, const void* vc, int B, int H, int Tq, int ctx, int start_pos,
+                     float scale_log2, void* o, cudaStream_t s);
+
 template <int HD, typename T>
 static int launch_attn(const void* q, const void* kc, const void* vc, int B, int H, int Tq, int ctx,
                        int start_pos, void* o, cudaStream_t s) {
   const float scale_log2 = (1.0f / sqrtf((float)HD)) * 1.4426950408889634f;
   const bool aligned = ((((uintptr_t)q) | ((uintptr_t)kc) | ((uintptr_t)vc)) & 15u) == 0;
   if constexpr (std::is_same<T, __half>::value && HD == 16) {
+    if (const int r = launch_attn_tc05(q, kc, vc, B, H, Tq, ctx, start_pos, scale_log2, o, s)) return r < 0 ? r : WALSH_OK;
     const int kend = start_pos + Tq;
     if (Tq > 4 && aligned && kend <= kAttnHeadMaxKeys && H <= 65535 && B <= 65535) {
       const int smem = 2 * ((kend + 63) / 64 * 64) * (HD + 8) * (int)sizeof(__half);

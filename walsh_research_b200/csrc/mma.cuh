@@ -29,6 +29,17 @@ __device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, uint32_t b0
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// d = a . b + (c_lo, c_lo, c_hi, c_hi): fp16 operands, fp32 accumulate, the
+// addend one value per row half (rows g and g + 8 of the 16-row tile).
+__device__ __forceinline__ void mma_f16_rowc(float* d, const uint32_t* a, uint32_t b0, uint32_t b1, float c_lo,
+                                             float c_hi) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%11,%11};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c_lo), "f"(c_hi));
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }

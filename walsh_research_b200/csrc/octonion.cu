@@ -742,7 +742,12 @@ extern "C" int walsh_octo_set_mainloop(int tcgen05) {
   return prev;
 }
 
+namespace walsh {
+int attn_tc05_error(int reset);  // attention_tc.cu
+}
+
 extern "C" int walsh_tc05_error(int reset) {
+  const int va = walsh::attn_tc05_error(reset);
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_tc05_error, sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
@@ -752,5 +757,5 @@ extern "C" int walsh_tc05_error(int reset) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_tc05_error, &zero, sizeof(int));
   }
-  return v;
+  return v ? v : va;
 }
