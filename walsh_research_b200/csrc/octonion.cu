@@ -125,6 +125,7 @@ struct EpiPlain {
     chunk16(m, n + 16, v + 16);
   }
   __host__ bool vec_ok() const { return N % 16 == 0; }
+  static constexpr int kWarpScratch = 0;  // bytes of shared scratch per epilogue warp
 };
 
 template <typename TY>
@@ -182,6 +183,7 @@ struct EpiQkv {
     chunk16(m, n + 16, v + 16);
   }
   __host__ bool vec_ok() const { return hd % 16 == 0 && C % 16 == 0; }
+  static constexpr int kWarpScratch = 0;
 };
 
 template <typename TY>
@@ -214,6 +216,7 @@ struct EpiSwiglu {
     store16(h + m * hid + (n >> 1), o);
   }
   __host__ bool vec_ok() const { return hid % 8 == 0; }
+  static constexpr int kWarpScratch = 0;
 };
 
 template <typename TX>
@@ -295,7 +298,66 @@ struct EpiPost {
       chunk16(m, n + 16, v + 16);
     }
   }
-  __host__ bool vec_ok() const { return C % 16 == 0; }
+  __host__ bool vec_ok() const {
+    return C % 16 == 0 && ((((uintptr_t)hmix) | ((uintptr_t)scale)) & 15u) == 0;
+  }
+  // 16-bit streams: whole 32 x 32 blocks per warp, staged through shared
+  // memory so that four lanes cover one token row (coalesced 16-byte stream
+  // accesses) instead of each lane owning a row 4 C elements from the next
+  static constexpr int kPitch = 36;  // floats per staged row (16-byte aligned, conflict-free stores)
+  static constexpr int kWarpScratch = sizeof(TX) == 2 ? 32 * kPitch * 4 : 0;
+  // all 32 lanes: rows m0 .. m0 + 31 (lane i holds row m0 + i in v), columns n .. n + 31
+  __device__ __forceinline__ void warp_chunk32(int64_t m0, int64_t n, const float* v, int lane, float* scr,
+                                               int64_t M) const {
+    float* mine = scr + lane * kPitch;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      *reinterpret_cast<float4*>(mine + 4 * k) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    __syncwarp();
+    const int rq = lane >> 2, cs = (lane & 3) * 8;
+    float sc[8];
+    {
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + n + cs));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + n + cs + 4));
+      sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w;
+      sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+    }
+#pragma unroll 1
+    for (int p = 0; p < 4; ++p) {
+      const int r = p * 8 + rq;
+      const int64_t m = m0 + r;
+      if (m < M) {
+        const float* hm = hmix + m * kMapRows + 4;  // H_post[4] | H_res[16], 16-byte aligned
+        float h[20];
+#pragma unroll
+        for (int k = 0; k < 5; ++k) {
+          const float4 t = __ldg(reinterpret_cast<const float4*>(hm) + k);
+          h[4 * k] = t.x; h[4 * k + 1] = t.y; h[4 * k + 2] = t.z; h[4 * k + 3] = t.w;
+        }
+        const float4 y0 = *reinterpret_cast<const float4*>(scr + r * kPitch + cs);
+        const float4 y1 = *reinterpret_cast<const float4*>(scr + r * kPitch + cs + 4);
+        const float f[8] = {y0.x * sc[0], y0.y * sc[1], y0.z * sc[2], y0.w * sc[3],
+                            y1.x * sc[4], y1.y * sc[5], y1.z * sc[6], y1.w * sc[7]};
+        const size_t base = (size_t)m * 4 * C + n + cs;
+        uint4 xr[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xr[j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * C);
+        float xf[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) unpack8(xr[j], xf[j], (const TX*)nullptr);
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+          const float* hr = h + 4 + 4 * o;
+          float out[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            out[e] = (((hr[0] * xf[0][e] + hr[1] * xf[1][e]) + hr[2] * xf[2][e]) + hr[3] * xf[3][e]) + h[o] * f[e];
+          store8(xo + base + (size_t)o * C, out);
+        }
+      }
+    }
+    __syncwarp();
+  }
 };
 
 }  // namespace octo
@@ -437,6 +499,14 @@ constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
 }  // namespace octo_tc
 
+// mainloop stages: 4, or 3 when the epilogue needs per-warp shared scratch
+template <class Epi>
+struct OctoTcCfg {
+  static constexpr int STAGES = Epi::kWarpScratch ? 3 : octo_tc::STAGES;
+  static constexpr int SCRATCH_OFF = STAGES * octo_tc::STAGE_BYTES + 256;  // after the barriers
+  static constexpr int SMEM = SCRATCH_OFF + 8 * Epi::kWarpScratch + 1024;
+};
+
 // Set when a bounded wait of a tcgen05 kernel in this file gave up.
 __device__ int g_tc05_error;
 
@@ -446,6 +516,7 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
                       int64_t M, int K, int64_t N, Epi epi, int vec) {
   using namespace octo_tc;
   using namespace tc05;
+  constexpr int STAGES = OctoTcCfg<Epi>::STAGES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -551,6 +622,13 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
         float v[32];
         tmem_ld32(base + (uint32_t)c, v);
         const int64_t n = n0 + c;
+        if constexpr (Epi::kWarpScratch > 0) {
+          if (vec && n + 32 <= N) {  // uniform over the warp
+            float* scr = reinterpret_cast<float*>(smem + OctoTcCfg<Epi>::SCRATCH_OFF + (warp - 2) * Epi::kWarpScratch);
+            epi.warp_chunk32(m - lane, n, v, lane, scr, M);
+            continue;
+          }
+        }
         if (m < M && n < N) {
           if (vec && n + 32 <= N) {
             epi.chunk32(m, n, v);
@@ -584,7 +662,8 @@ static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int6
   CUtensorMap ma, mb;
   if (!make_tile_map(&ma, a, BF, M, K, octo_tc::BK, BM) || !make_tile_map(&mb, w, BF, N, K, octo_tc::BK, BN)) return 0;
   auto kern = octo_gemm_tc05_kernel<TA, Epi>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+  constexpr int SMEM_B = OctoTcCfg<Epi>::SMEM;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_B) != cudaSuccess)
     return launch_status();
   static int sms = 0;
   if (!sms) {
@@ -595,7 +674,7 @@ static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int6
   }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  kern<<<grid, NTHREADS, SMEM, s>>>(ma, mb, M, K, N, epi, epi.vec_ok() ? 1 : 0);
+  kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, M, K, N, epi, epi.vec_ok() ? 1 : 0);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
 }
