@@ -103,6 +103,22 @@ __device__ __forceinline__ void load16(const T* p, float* v) {
   load8(p + 8, v + 8);
 }
 
+// packed fp32 pairs (low = first element) for fma.rn.f32x2 / mul.rn.f32x2
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f2_dup(float v) { return f2_pack(v, v); }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
 // ---- epilogues: operator() once per (row m, column pair n, n+1), n even;
 // chunk16 once per row and 16 consecutive columns n..n+15 (n a multiple of
 // 16, destination rows aligned for 16-byte vectors; the launcher checks) ----
@@ -301,62 +317,112 @@ struct EpiPost {
   __host__ bool vec_ok() const {
     return C % 16 == 0 && ((((uintptr_t)hmix) | ((uintptr_t)scale)) & 15u) == 0;
   }
-  // 16-bit streams: whole 32 x 32 blocks per warp, staged through shared
-  // memory so that four lanes cover one token row (coalesced 16-byte stream
-  // accesses) instead of each lane owning a row 4 C elements from the next
-  static constexpr int kPitch = 36;  // floats per staged row (16-byte aligned, conflict-free stores)
-  static constexpr int kWarpScratch = sizeof(TX) == 2 ? 32 * kPitch * 4 : 0;
-  // all 32 lanes: rows m0 .. m0 + 31 (lane i holds row m0 + i in v), columns n .. n + 31
-  __device__ __forceinline__ void warp_chunk32(int64_t m0, int64_t n, const float* v, int lane, float* scr,
-                                               int64_t M) const {
-    float* mine = scr + lane * kPitch;
+  // 16-bit streams: a warp's whole 32-row x 128-column block.  Per 32-column
+  // chunk the accumulator rows (lane i = row i) are staged through shared
+  // memory so that four lanes cover one token row (8 columns each: 16-byte
+  // stream accesses, 8 rows per pass); the stream rows and mixing
+  // coefficients of the next two passes are already in flight (cp.async into
+  // a two-slot ring) while the current pass is mixed.
+  static constexpr int kPitch = 36;                      // floats per staged row
+  static constexpr int kYBytes = 32 * kPitch * 4;        // staged 32 x 32 chunk
+  static constexpr int kXSlot = 8 * 4 * 64;              // 8 rows x 4 streams x 32 columns (16-bit)
+  static constexpr int kHSlot = 8 * 80;                  // 8 rows x (H_post | H_res) floats
+  static constexpr int kSlot = kXSlot + kHSlot;
+  static constexpr int kWarpScratch = sizeof(TX) == 2 ? 1 : 0;  // has the warp path
+  static constexpr int warp_bytes(int depth) { return kYBytes + depth * kSlot; }
+  // one pass (chunk step / 4, rows 8 (step % 4) ..) into ring slot `slot`
+  __device__ __forceinline__ void prefetch(int64_t m0, int64_t n0, int step, int slot, int lane,
+                                           unsigned char* ring, int64_t M) const {
+    const int ch = step >> 2, p = step & 3;
+    unsigned char* sl = ring + slot * kSlot;
+    const int rq = lane >> 2, cq = lane & 3;
+    const int64_t m = m0 + p * 8 + rq;
+    const bool in = m < M;
+    const int64_t mm = in ? m : 0;
+    const TX* src = x + (size_t)mm * 4 * C + n0 + ch * 32 + cq * 8;
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      *reinterpret_cast<float4*>(mine + 4 * k) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-    __syncwarp();
-    const int rq = lane >> 2, cs = (lane & 3) * 8;
-    float sc[8];
-    {
-      const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + n + cs));
-      const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + n + cs + 4));
-      sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w;
-      sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+    for (int j = 0; j < 4; ++j) cp_async16(sl + (rq * 4 + j) * 64 + cq * 16, src + (size_t)j * C, in ? 16 : 0);
+    const float* hm = hmix + mm * kMapRows + 4;
+    cp_async16(sl + kXSlot + rq * 80 + cq * 16, hm + 4 * cq, in ? 16 : 0);
+    if (cq == 0) cp_async16(sl + kXSlot + rq * 80 + 64, hm + 16, in ? 16 : 0);
+  }
+  // all 32 lanes: rows m0 .. m0 + 31 (TMEM lane quarter of the warp), columns
+  // n0 .. n0 + 127 of the accumulator at tensor-memory address `tacc`; DEPTH
+  // ring slots, DEPTH - 1 passes in flight ahead of the one being mixed
+  template <int DEPTH>
+  __device__ __forceinline__ void warp_block(int64_t m0, int64_t n0, uint32_t tacc, int lane, unsigned char* scr,
+                                             int64_t M) const {
+    float* ys = reinterpret_cast<float*>(scr);
+    unsigned char* ring = scr + kYBytes;
+    const int rq = lane >> 2, cq = lane & 3;
+#pragma unroll
+    for (int k = 0; k < DEPTH - 1; ++k) {
+      prefetch(m0, n0, k, k, lane, ring, M);
+      cp_async_commit();
     }
+    float sc[8];
 #pragma unroll 1
-    for (int p = 0; p < 4; ++p) {
+    for (int step = 0; step < 16; ++step) {
+      const int ch = step >> 2, p = step & 3;
+      if (p == 0) {
+        float v[32];
+        tc05::tmem_ld32(tacc + (uint32_t)(ch * 32), v);
+        __syncwarp();  // previous chunk's staged rows fully read
+        float* mine = ys + lane * kPitch;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4*>(mine + 4 * k) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + n0 + ch * 32 + cq * 8));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + n0 + ch * 32 + cq * 8 + 4));
+        sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w;
+        sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+      }
+      cp_async_wait<DEPTH - 2>();
+      __syncwarp();
       const int r = p * 8 + rq;
       const int64_t m = m0 + r;
+      const unsigned char* sl = ring + (step % DEPTH) * kSlot;
       if (m < M) {
-        const float* hm = hmix + m * kMapRows + 4;  // H_post[4] | H_res[16], 16-byte aligned
         float h[20];
 #pragma unroll
         for (int k = 0; k < 5; ++k) {
-          const float4 t = __ldg(reinterpret_cast<const float4*>(hm) + k);
+          const float4 t = *reinterpret_cast<const float4*>(sl + kXSlot + rq * 80 + 16 * k);
           h[4 * k] = t.x; h[4 * k + 1] = t.y; h[4 * k + 2] = t.z; h[4 * k + 3] = t.w;
         }
-        const float4 y0 = *reinterpret_cast<const float4*>(scr + r * kPitch + cs);
-        const float4 y1 = *reinterpret_cast<const float4*>(scr + r * kPitch + cs + 4);
+        const float4 y0 = *reinterpret_cast<const float4*>(ys + r * kPitch + cq * 8);
+        const float4 y1 = *reinterpret_cast<const float4*>(ys + r * kPitch + cq * 8 + 4);
         const float f[8] = {y0.x * sc[0], y0.y * sc[1], y0.z * sc[2], y0.w * sc[3],
                             y1.x * sc[4], y1.y * sc[5], y1.z * sc[6], y1.w * sc[7]};
-        const size_t base = (size_t)m * 4 * C + n + cs;
-        uint4 xr[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) xr[j] = *reinterpret_cast<const uint4*>(x + base + (size_t)j * C);
         float xf[4][8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) unpack8(xr[j], xf[j], (const TX*)nullptr);
+        for (int j = 0; j < 4; ++j)
+          unpack8(*reinterpret_cast<const uint4*>(sl + (rq * 4 + j) * 64 + cq * 16), xf[j], (const TX*)nullptr);
+        const size_t base = (size_t)m * 4 * C + n0 + ch * 32 + cq * 8;
 #pragma unroll
         for (int o = 0; o < 4; ++o) {
           const float* hr = h + 4 + 4 * o;
+          const uint64_t h0 = f2_dup(hr[0]), h1 = f2_dup(hr[1]), h2 = f2_dup(hr[2]), h3 = f2_dup(hr[3]),
+                         hp = f2_dup(h[o]);
           float out[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            out[e] = (((hr[0] * xf[0][e] + hr[1] * xf[1][e]) + hr[2] * xf[2][e]) + hr[3] * xf[3][e]) + h[o] * f[e];
+          for (int e = 0; e < 8; e += 2) {
+            // (((H0 x0 + H1 x1) + H2 x2) + H3 x3) + H_post f, two columns per instruction
+            uint64_t a = f2_mul(h0, f2_pack(xf[0][e], xf[0][e + 1]));
+            a = f2_fma(h1, f2_pack(xf[1][e], xf[1][e + 1]), a);
+            a = f2_fma(h2, f2_pack(xf[2][e], xf[2][e + 1]), a);
+            a = f2_fma(h3, f2_pack(xf[3][e], xf[3][e + 1]), a);
+            a = f2_fma(hp, f2_pack(f[e], f[e + 1]), a);
+            out[e] = __uint_as_float((uint32_t)a);
+            out[e + 1] = __uint_as_float((uint32_t)(a >> 32));
+          }
           store8(xo + base + (size_t)o * C, out);
         }
       }
+      __syncwarp();  // the slot of step - 1 is free: refill it with step + DEPTH - 1
+      if (step + DEPTH - 1 < 16) prefetch(m0, n0, step + DEPTH - 1, (step + DEPTH - 1) % DEPTH, lane, ring, M);
+      cp_async_commit();
     }
-    __syncwarp();
+    cp_async_wait<0>();
   }
 };
 
@@ -499,12 +565,24 @@ constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
 }  // namespace octo_tc
 
-// mainloop stages: 4, or 3 when the epilogue needs per-warp shared scratch
+// Launch shape: mainloop stages, epilogue ring depth and shared memory.  An
+// epilogue with a warp path trades mainloop stages for in-flight stream
+// rows: 2 stages and a 4-slot ring for K <= 512 (short mainloops), else 3 and 2.
 template <class Epi>
-struct OctoTcCfg {
-  static constexpr int STAGES = Epi::kWarpScratch ? 3 : octo_tc::STAGES;
-  static constexpr int SCRATCH_OFF = STAGES * octo_tc::STAGE_BYTES + 256;  // after the barriers
-  static constexpr int SMEM = SCRATCH_OFF + 8 * Epi::kWarpScratch + 1024;
+struct OctoTcShape {
+  int stages, depth, smem;
+  explicit OctoTcShape(int K) {
+    if constexpr (Epi::kWarpScratch > 0) {
+      stages = K <= 512 ? 2 : 3;
+      depth = K <= 512 ? 4 : 2;
+      smem = scratch_off(stages) + 8 * Epi::warp_bytes(depth) + 1024;
+    } else {
+      stages = octo_tc::STAGES;
+      depth = 0;
+      smem = scratch_off(stages) + 1024;
+    }
+  }
+  __host__ __device__ static int scratch_off(int stages) { return stages * octo_tc::STAGE_BYTES + 256; }
 };
 
 // Set when a bounded wait of a tcgen05 kernel in this file gave up.
@@ -513,10 +591,10 @@ __device__ int g_tc05_error;
 template <typename TA, class Epi>
 __global__ void __launch_bounds__(octo_tc::NTHREADS, 1)
 octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                      int64_t M, int K, int64_t N, Epi epi, int vec) {
+                      int64_t M, int K, int64_t N, Epi epi, int vec, int nstage, int depth) {
   using namespace octo_tc;
   using namespace tc05;
-  constexpr int STAGES = OctoTcCfg<Epi>::STAGES;
+  const int STAGES = nstage;  // mainloop stages of this launch (2..4)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -617,18 +695,23 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       fence_after_sync();
       const int64_t m = (t / ntl) * BM + q * 32 + lane, n0 = (t % ntl) * BN + half * (BN / 2);
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * ACC_COLS + half * (BN / 2));
+      bool done = false;
+      if constexpr (Epi::kWarpScratch > 0) {
+        if (vec && n0 + BN / 2 <= N) {  // uniform over the warp
+          unsigned char* scr =
+              smem + OctoTcShape<Epi>::scratch_off(STAGES) + (warp - 2) * Epi::warp_bytes(depth);
+          if (depth == 4)
+            epi.template warp_block<4>(m - lane, n0, base, lane, scr, M);
+          else
+            epi.template warp_block<2>(m - lane, n0, base, lane, scr, M);
+          done = true;
+        }
+      }
 #pragma unroll 1
-      for (int c = 0; c < BN / 2; c += 32) {
+      for (int c = 0; c < BN / 2 && !done; c += 32) {
         float v[32];
         tmem_ld32(base + (uint32_t)c, v);
         const int64_t n = n0 + c;
-        if constexpr (Epi::kWarpScratch > 0) {
-          if (vec && n + 32 <= N) {  // uniform over the warp
-            float* scr = reinterpret_cast<float*>(smem + OctoTcCfg<Epi>::SCRATCH_OFF + (warp - 2) * Epi::kWarpScratch);
-            epi.warp_chunk32(m - lane, n, v, lane, scr, M);
-            continue;
-          }
-        }
         if (m < M && n < N) {
           if (vec && n + 32 <= N) {
             epi.chunk32(m, n, v);
@@ -662,7 +745,8 @@ static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int6
   CUtensorMap ma, mb;
   if (!make_tile_map(&ma, a, BF, M, K, octo_tc::BK, BM) || !make_tile_map(&mb, w, BF, N, K, octo_tc::BK, BN)) return 0;
   auto kern = octo_gemm_tc05_kernel<TA, Epi>;
-  constexpr int SMEM_B = OctoTcCfg<Epi>::SMEM;
+  const OctoTcShape<Epi> shp(K);
+  const int SMEM_B = shp.smem;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_B) != cudaSuccess)
     return launch_status();
   static int sms = 0;
@@ -674,7 +758,7 @@ static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int6
   }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, M, K, N, epi, epi.vec_ok() ? 1 : 0);
+  kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, M, K, N, epi, epi.vec_ok() ? 1 : 0, shp.stages, shp.depth);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
 }
