@@ -278,6 +278,35 @@ walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, int dtype, in
                                   int x_dtype, const float* hmix, void* x_out, uint8_t* mask_out,
                                   float* probs_out, float* weights_out, void* stream);
 
+/* Prefill-sized MoE for C = 512 (E = 16, router hidden 128) on the
+ * 5th-generation tensor cores, in two calls.
+ *
+ * walsh_moe_router_tc_fwd: h = u W1^T as a tcgen05 GEMM whose epilogue does
+ * the rest of the router per token: silu(h) rounded to u's dtype, logits =
+ * silu(h) W2^T, softmax, top_k (ties to the lower index), routing weights
+ * renormalised over the selected experts.  u [ntok, 512] bf16/fp16; w1
+ * [128, 512] and w2 [16, 128] in u's dtype; mask uint8, probs and weights
+ * float32 [ntok, 16].  All pointers 16-byte aligned.  Replaces
+ * HadamardRouter.forward (src/model/moe.py:418-447). */
+walsh_status walsh_moe_router_tc_fwd(const void* u, int dtype, int64_t ntok, const void* w1,
+                                     const void* w2, int top_k, uint8_t* mask, float* probs,
+                                     float* weights, void* stream);
+
+/* walsh_moe_experts_tc_fwd: the 16 ternary SwiGLU experts (all evaluated,
+ * weighted by `weights`, 0 outside the top-k) and either y [ntok, 512]
+ * (fuse_post = 0, u's dtype) or the mHC site epilogue into x_out (as for
+ * walsh_moe_fwd; x bf16/fp16).  w_gu [8, 256, 64]: for expert pair p, rows
+ * 0..127 are gate hidden units and 128..255 up hidden units, columns 0..31
+ * expert 2p's inputs and 32..63 expert 2p + 1's (ternary values in u's
+ * dtype); w_down [16, 32, 128]; gammas float[3] (gate, up, down).  All
+ * pointers 16-byte aligned.  Replaces FastMoEExperts.forward and the
+ * weighted combination of HadamardMoE.forward (src/model/moe.py:337-380,
+ * 512-542). */
+walsh_status walsh_moe_experts_tc_fwd(const void* u, int dtype, int64_t ntok, const float* weights,
+                                      const void* w_gu, const void* w_down, const float* gammas,
+                                      void* y, int fuse_post, const void* x, int x_dtype,
+                                      const float* hmix, void* x_out, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Octonion (Cayley-Dickson) layers as tensor-core GEMMs
  *

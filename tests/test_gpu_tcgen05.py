@@ -140,3 +140,50 @@ def test_attention_tcgen05_matches_mma_sync_and_oracle(B, H, Tq, start):
     ref = _attn_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), start)
     assert rel(a, ref) < 3e-3
     assert rel(a, b.float().cpu().numpy()) < 3e-3
+
+
+@pytest.mark.parametrize("n", [9472, 10000, 33000])
+@pytest.mark.parametrize("udt,xdt", [(torch.float16, torch.float16), (torch.bfloat16, torch.bfloat16),
+                                     (torch.float16, torch.bfloat16)])
+def test_moe_tcgen05_matches_mma_sync_kernel(n, udt, xdt):
+    """Prefill MoE on tcgen05 (router GEMM with the routing in its epilogue +
+    expert-pair kernel with the site epilogue) against the single mma.sync
+    kernel on the same inputs: equal selections except where the k-th and
+    (k+1)-th probabilities are within the router's rounding; equal routing
+    weights, expert outputs and fused site updates elsewhere; ragged last tile."""
+    from walsh_research_b200 import _lib, ops
+    from test_gpu_parity import _moe_module, cases
+    d = cases.op_case("moe")
+    rng = np.random.default_rng(n)
+    m = _moe_module(d)
+    args = m.kernel_args(udt)
+    u = T(rng.normal(size=(n, 512)).astype(np.float32), udt)
+    xs = T(rng.normal(size=(n, 4, 512)).astype(np.float32), xdt)
+    hm = torch.rand((n, 24), device=DEV)
+
+    def run(tc05):
+        prev = ops.MOE_TC05
+        ops.MOE_TC05 = tc05
+        try:
+            y, mask, probs, w = ops.moe(u, *args[:7], want_stats=True, tc=args[7])
+            f = ops.moe(u, *args[:7], fuse=(xs, hm, torch.empty_like(xs)), tc=args[7])
+            torch.cuda.synchronize()
+            return y.float().cpu().numpy(), mask.cpu().numpy(), probs.cpu().numpy(), w.cpu().numpy(), \
+                f.float().cpu().numpy()
+        finally:
+            ops.MOE_TC05 = prev
+    _lib.call("walsh_tc05_error", 1)
+    y1, m1, p1, w1, f1 = run(True)
+    assert _lib.call("walsh_tc05_error", 1) == 0
+    y0, m0, p0, w0, f0 = run(False)
+    srt = -np.sort(-p0, axis=-1)
+    near = (srt[:, 5] - srt[:, 6]) < 2e-3
+    diff = (m1 != m0).any(-1)
+    assert not (diff & ~near).any()
+    ok = ~diff
+    assert np.abs(p1 - p0).max() < 2e-3
+    assert np.abs(w1 - w0)[ok].max() < 2e-3
+    scale = np.abs(y0).max()
+    assert np.abs(y1 - y0)[ok].max() / scale < 1e-2
+    fs = np.abs(f0).max()
+    assert np.abs(f1 - f0)[ok].max() / fs < 1e-2

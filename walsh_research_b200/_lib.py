@@ -43,6 +43,8 @@ SIGNATURES = {
     "walsh_octo_set_mainloop": [c_int],
     "walsh_tc05_error": [c_int],
     "walsh_attn_set_path": [c_int],
+    "walsh_moe_router_tc_fwd": [P, c_int, c_int64, P, P, c_int, P, P, P, P],
+    "walsh_moe_experts_tc_fwd": [P, c_int, c_int64, P, P, P, P, P, c_int, P, c_int, P, P, P],
     "walsh_tc05_wait_selftest": [ctypes.c_longlong, P],
     "walsh_octo_linear_fwd": [P, c_int, c_int64, c_int, P, P, c_int, c_int64, P, P, P],
     "walsh_octo_qkv_fwd": [P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int, P, P, P, c_int,

@@ -11,6 +11,8 @@
 
 #include "common.cuh"
 #include "mma.cuh"
+#include "tc05.cuh"
+#include "tma_host.cuh"
 
 namespace walsh {
 
@@ -798,9 +800,465 @@ static int launch_moe_mma(const void* u, int64_t ntok, int top_k, const walsh_mo
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Prefill MoE experts on the 5th-generation tensor cores (C = 512, E = 16
+// experts on 32-wide Hadamard blocks, hidden 128; routing weights come from
+// the router GEMM).  A CTA runs 128-token tiles (persistent).  Per expert
+// pair p one TMA stage brings u[:, 64p .. 64p + 63] (both experts' input
+// blocks), the pair's gate/up rows packed side by side ([gate 128 | up 128
+// rows] x [32 inputs of expert 2p | 32 of 2p + 1]) and the two experts' down
+// rows; an expert's k-slice is selected by advancing the operand descriptors
+// 64 bytes.  Per expert:
+//   MMA1   D1[128 x 256] = u_e [gate_e | up_e]^T           (tensor memory 0..255)
+//   SwiGLU warps 2-5, thread per token row, all 128 hidden units:
+//          h = silu(gg g) (gu v) rounded to TU into a 128B-swizzled h tile
+//   MMA2   Yq[:, 32 (e % 4) ..] = h down_e^T   (tensor memory 256.., two quarters of 4 experts)
+// Warps 6-9 meanwhile take the previous quarter: each expert's 32 columns
+// scaled by routing weight x gd, rounded to TU (as the expert output is),
+// and the mHC site update of those columns (or y stored), 32 x 32 blocks
+// staged through shared memory so that four lanes cover one token row, the
+// next rows in flight (site_block).  So the MUFU-bound SwiGLU of quarter
+// j + 1 overlaps the HBM-bound site update of quarter j.  Warp 0 issues TMA,
+// warp 1 owns tensor memory and issues the MMAs.  Every wait is bounded; a
+// wait that runs out sets g_moe_tc05_error.
+// Replaces FastMoEExperts.forward + the site mix (src/model/moe.py:306-380,
+// src/model/mhc.py site update).
+// ---------------------------------------------------------------------------
+// probe hook (slot, index): no code unless a profiling build defines it
+#ifndef MOE_TC_TRACE
+#define MOE_TC_TRACE(slot, idx)
+#endif
+
+namespace moe_tc5 {
+constexpr int C = 512, E = 16, HID = 128, TOK = 128, NPAIR = 8;
+constexpr int U_BYTES = TOK * 128;          // 128 rows x 64 columns
+constexpr int G_BYTES = 256 * 128;          // 256 rows x 64 columns
+constexpr int D_ATOM = 32 * 128;            // 32 rows x 64 columns
+constexpr int D_EXP = 2 * D_ATOM;           // one expert's down rows (hidden 0..63 | 64..127)
+constexpr int STAGE = U_BYTES + G_BYTES + 2 * D_EXP;
+constexpr int NSTAGE = 2;
+constexpr int H_ATOM = TOK * 128;
+// site ring of one worker warp: per slot 8 rows x (4 streams x 32 columns of x,
+// H_post | H_res, the 16 routing weights)
+constexpr int XS = 8 * 4 * 64, HS = 8 * 80, WS = 8 * 64, SLOT = XS + HS + WS, DEPTH = 3, RING = DEPTH * SLOT;
+constexpr int OFF_H = NSTAGE * STAGE;
+constexpr int OFF_YS = OFF_H + 2 * H_ATOM;     // 4 site warps x 32 x 32 floats
+constexpr int OFF_RING = OFF_YS + 4 * 4096;
+constexpr int OFF_BAR = OFF_RING + 4 * RING;
+constexpr int SMEM = OFF_BAR + 256 + 1024;
+constexpr int NTHREADS = 320;
+constexpr uint32_t TMEM_COLS = 512, COL_D1 = 0, COL_Y = 256;  // Y: two 128-column quarters (4 experts each)
+__device__ __forceinline__ uint32_t sw_off(int r, int chunk) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4));
+}
+}  // namespace moe_tc5
+
+__device__ int g_moe_tc05_error;
+
+// One pass of the site update (8 rows x 32 columns = expert ex0 + step / 4)
+// into ring slot `slot`: the rows' 4 stream segments, mixing coefficients
+// and routing weights, by cp.async (rows past ntok are zero-filled).
+template <typename TX>
+__device__ __forceinline__ void site_prefetch(int64_t mw, int ex0, int step, int slot, int lane, unsigned char* ring,
+                                              int64_t ntok, const float* rw, const TX* x, const float* hmix) {
+  using namespace moe_tc5;
+  const int k = step >> 2, p = step & 3, rq = lane >> 2, cq = lane & 3;
+  unsigned char* sl = ring + slot * SLOT;
+  const int64_t m = mw + p * 8 + rq;
+  const bool in = m < ntok;
+  const int64_t mm = in ? m : 0;
+  if (x) {
+    const TX* src = x + (size_t)mm * 4 * C + (ex0 + k) * 32 + cq * 8;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cp_async16(sl + (rq * 4 + j) * 64 + cq * 16, src + (size_t)j * C, in ? 16 : 0);
+    const float* hm = hmix + mm * kMapRows + 4;
+    cp_async16(sl + XS + rq * 80 + cq * 16, hm + 4 * cq, in ? 16 : 0);
+    if (cq == 0) cp_async16(sl + XS + rq * 80 + 64, hm + 16, in ? 16 : 0);
+  }
+  cp_async16(sl + XS + HS + rq * 64 + cq * 16, rw + mm * E + 4 * cq, in ? 16 : 0);
+}
+
+// Site update (or y store) of one worker warp after 8 experts: rows mw ..
+// mw + 31 (its tensor-memory lane quarter), the 4 experts ex0 .. ex0 + 3 whose
+// outputs sit in tensor memory at tacc (32 columns each).  Per expert the 32
+// x 32 fp32 block is staged through the warp's 4 KB of the (idle) h tile
+// (16-byte chunks XOR-swizzled by row), then 4 passes of 8 rows with four
+// lanes per row (8 columns each); the next pass's rows are in flight while a
+// pass is mixed.  y = D2 w gd rounded to TU, then
+// x_o = H_res x + H_post y (or y stored).
+template <typename TU, typename TX>
+__device__ __forceinline__ void site_block(int64_t mw, int ex0, uint32_t tacc, int lane, float* ys,
+                                           unsigned char* ring, int64_t ntok, const float* rw, float gd, TU* y,
+                                           int fuse_post, const TX* x, const float* hmix, TX* xo) {
+  using namespace moe_tc5;
+  const int rq = lane >> 2, cq = lane & 3;
+  const TX* xs = fuse_post ? x : nullptr;
+#pragma unroll
+  for (int k = 0; k < DEPTH - 1; ++k) {
+    site_prefetch<TX>(mw, ex0, k, k, lane, ring, ntok, rw, xs, hmix);
+    cp_async_commit();
+  }
+#pragma unroll 1
+  for (int step = 0; step < 16; ++step) {
+    const int k = step >> 2, p = step & 3, ex = ex0 + k;
+    if (p == 0) {
+      float v[32];
+      tc05::tmem_ld32(tacc + (uint32_t)(32 * k), v);
+      __syncwarp();  // the previous expert's staged rows are fully read
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float4*>(ys + lane * 32 + 4 * (i ^ (lane & 7))) =
+            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+    cp_async_wait<DEPTH - 2>();
+    __syncwarp();
+    const int rr = p * 8 + rq;
+    const int64_t m = mw + rr;
+    const unsigned char* sl = ring + (step % DEPTH) * SLOT;
+    if (m < ntok) {
+      const float wgt = reinterpret_cast<const float*>(sl + XS + HS + rq * 64)[ex] * gd;
+      const float4 y0 = *reinterpret_cast<const float4*>(ys + rr * 32 + 4 * ((2 * cq) ^ (rr & 7)));
+      const float4 y1 = *reinterpret_cast<const float4*>(ys + rr * 32 + 4 * ((2 * cq + 1) ^ (rr & 7)));
+      float yf[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+      uint32_t yt[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        yt[i] = pack2<TU>(yf[2 * i] * wgt, yf[2 * i + 1] * wgt);
+        const float2 back = unpack2<TU>(yt[i]);
+        yf[2 * i] = back.x;
+        yf[2 * i + 1] = back.y;
+      }
+      const int col = ex * 32 + cq * 8;
+      if (!fuse_post) {
+        *reinterpret_cast<uint4*>(y + m * C + col) = make_uint4(yt[0], yt[1], yt[2], yt[3]);
+      } else {
+        float h[20];
+#pragma unroll
+        for (int i = 0; i < 5; ++i) {
+          const float4 hv = *reinterpret_cast<const float4*>(sl + XS + rq * 80 + 16 * i);
+          h[4 * i] = hv.x;
+          h[4 * i + 1] = hv.y;
+          h[4 * i + 2] = hv.z;
+          h[4 * i + 3] = hv.w;
+        }
+        float xf[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          unpack8(*reinterpret_cast<const uint4*>(sl + (rq * 4 + j) * 64 + cq * 16), xf[j], (const TX*)nullptr);
+        const size_t base = (size_t)m * 4 * C + col;
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+          const float* hr = h + 4 + 4 * o;
+          const uint64_t h0 = f2_dup(hr[0]), h1 = f2_dup(hr[1]), h2 = f2_dup(hr[2]), h3 = f2_dup(hr[3]),
+                         hpo = f2_dup(h[o]);
+          uint32_t ow[4];
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            // (((H0 x0 + H1 x1) + H2 x2) + H3 x3) + H_post y, two columns per instruction
+            uint64_t a = f2_mul(h0, f2_pack(xf[0][i], xf[0][i + 1]));
+            a = f2_fma(h1, f2_pack(xf[1][i], xf[1][i + 1]), a);
+            a = f2_fma(h2, f2_pack(xf[2][i], xf[2][i + 1]), a);
+            a = f2_fma(h3, f2_pack(xf[3][i], xf[3][i + 1]), a);
+            a = f2_fma(hpo, f2_pack(yf[i], yf[i + 1]), a);
+            ow[i >> 1] = pack2<TX>(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)(a >> 32)));
+          }
+          *reinterpret_cast<uint4*>(xo + base + (size_t)o * C) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+      }
+    }
+    __syncwarp();  // the slot of this step is free: refill it with step + DEPTH - 1
+    if (step + DEPTH - 1 < 16)
+      site_prefetch<TX>(mw, ex0, step + DEPTH - 1, (step + DEPTH - 1) % DEPTH, lane, ring, ntok, rw, xs, hmix);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+}
+
+template <typename TU, typename TX>
+__global__ void __launch_bounds__(moe_tc5::NTHREADS, 1)
+moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_g,
+                        const __grid_constant__ CUtensorMap tm_d, int64_t ntok, const float* __restrict__ rw,
+                        const float* __restrict__ gammas, TU* __restrict__ y, int fuse_post, const TX* x,
+                        const float* __restrict__ hmix, TX* xo) {
+  using namespace moe_tc5;
+  using namespace tc05;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = bars;          // [2] stage loaded (TMA)
+  uint64_t* empty = bars + 2;     // [2] stage consumed (MMA commit)
+  uint64_t* d1_full = bars + 4;   // MMA1 done (commit)
+  uint64_t* d1_empty = bars + 5;  // D1 read by the 4 SwiGLU warps
+  uint64_t* h_full = bars + 6;    // h tile written by the 4 SwiGLU warps
+  uint64_t* h_empty = bars + 7;   // MMA2 done with h (commit)
+  uint64_t* y_full = bars + 8;    // [2] a quarter's 4 MMA2s done (commit)
+  uint64_t* y_empty = bars + 10;  // [2] a quarter read by the 4 site warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tiles = (ntok + TOK - 1) / TOK;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      mbar_init(&y_full[i], 1);
+      mbar_init(&y_empty[i], 4);
+    }
+    mbar_init(d1_full, 1);
+    mbar_init(d1_empty, 4);
+    mbar_init(h_full, 4);
+    mbar_init(h_empty, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tm_u);
+    prefetch_tensormap(&tm_g);
+    prefetch_tensormap(&tm_d);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int64_t g = 0;  // expert pairs loaded by this CTA
+      for (int64_t t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+        for (int p = 0; p < NPAIR; ++p, ++g) {
+          const int st = (int)(g & 1);
+          if (g >= 2 && !mbar_wait_sleep(&empty[st], (uint32_t)(((g >> 1) - 1) & 1))) {
+            *abort_flag = 1;
+            break;
+          }
+          unsigned char* sb = smem + st * STAGE;
+          mbar_arrive_expect_tx(&full[st], STAGE);
+          tma_load_2d(sb, &tm_u, &full[st], 64 * p, (int)(t * TOK));
+          tma_load_2d(sb + U_BYTES, &tm_g, &full[st], 0, 256 * p);
+#pragma unroll
+          for (int ee = 0; ee < 2; ++ee)
+#pragma unroll
+            for (int a = 0; a < 2; ++a)
+              tma_load_2d(sb + U_BYTES + G_BYTES + ee * D_EXP + a * D_ATOM, &tm_d, &full[st], 64 * a,
+                          32 * (2 * p + ee));
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC1 = idesc_f16(std::is_same<TU, __nv_bfloat16>::value, 128, 256);
+      constexpr uint32_t IDESC2 = idesc_f16(std::is_same<TU, __nv_bfloat16>::value, 128, 32);
+      // iteration ge: MMA1 of expert ge (as soon as D1 is free), then MMA2 of
+      // expert ge - 1 (once its h tile is written); expert ge of this CTA is
+      // expert ge % 16 of its tile ge / 16, pair ge / 2 in stage (ge / 2) % 2
+      const int64_t total = ((tiles - blockIdx.x + gridDim.x - 1) / gridDim.x) * E;
+      bool ok = true;
+      const uint64_t dH = sw128_desc(smem_u32(smem + OFF_H));
+      for (int64_t ge = 0; ge <= total && ok; ++ge) {
+        if (ge < total) {
+          const int64_t pr = ge >> 1;
+          const int odd = (int)(ge & 1), st = (int)(pr & 1);
+          if (!odd) ok = mbar_wait_sleep(&full[st], (uint32_t)((pr >> 1) & 1));
+          if (ok && ge > 0) ok = mbar_wait_sleep(d1_empty, (uint32_t)((ge - 1) & 1));
+          if (!ok) break;
+          fence_after_sync();
+          const uint32_t sb = smem_u32(smem + st * STAGE);
+          const uint64_t dU = sw128_desc(sb), dG = sw128_desc(sb + U_BYTES);
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            umma_f16(tmem + COL_D1, dU + 4 * odd + 2 * k, dG + 4 * odd + 2 * k, IDESC1, k != 0);
+          umma_commit(d1_full);
+          MOE_TC_TRACE(0, (int)(ge & 15));
+        }
+        if (ge > 0) {
+          const int64_t g2 = ge - 1, pr = g2 >> 1, gq = g2 >> 2;
+          const int odd = (int)(g2 & 1), st = (int)(pr & 1), yb = (int)(gq & 1), e4 = (int)(g2 & 3);
+          ok = mbar_wait_sleep(h_full, (uint32_t)(g2 & 1));
+          if (ok && e4 == 0 && gq >= 2) ok = mbar_wait_sleep(&y_empty[yb], (uint32_t)(((gq >> 1) - 1) & 1));
+          if (!ok) break;
+          fence_after_sync();
+          const uint64_t dD = sw128_desc(smem_u32(smem + st * STAGE) + U_BYTES + G_BYTES + odd * D_EXP);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tmem + COL_Y + 128 * yb + 32 * e4, dH + (kk >> 2) * (H_ATOM >> 4) + 2 * (kk & 3),
+                     dD + (kk >> 2) * (D_ATOM >> 4) + 2 * (kk & 3), IDESC2, kk != 0);
+          umma_commit(h_empty);
+          MOE_TC_TRACE(1, (int)(g2 & 15));
+          if (e4 == 3) umma_commit(&y_full[yb]);
+          if (odd) umma_commit(&empty[st]);
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp < 6) {
+    // ---- SwiGLU warps 2-5: tensor-memory lanes 32 (warp % 4) .., thread = token row ----
+    const int q = warp & 3;
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+    const float gg = __ldg(gammas), gu = __ldg(gammas + 1);
+    const uint32_t sH = smem_u32(smem + OFF_H);
+    const int r = q * 32 + lane;
+    int64_t ge = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int e = 0; e < E && ok; ++e, ++ge) {
+        if (!__all_sync(0xffffffffu, mbar_wait(d1_full, (uint32_t)(ge & 1)))) {
+          ok = false;
+          break;
+        }
+        fence_after_sync();
+        MOE_TC_TRACE(2, e);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // hidden units 32 c .. 32 c + 31
+          float gv[32], uv[32];
+          tmem_ld32_nowait(tl + COL_D1 + 32 * c, gv);
+          tmem_ld32_nowait(tl + COL_D1 + 128 + 32 * c, uv);
+          tmem_wait_ld();
+          if (c == 3) {  // D1 fully read: the next expert's MMA1 may start
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d1_empty);
+          }
+          uint32_t a[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            a[i] = pack2<TU>(siluf_(gg * gv[2 * i]) * (gu * uv[2 * i]), siluf_(gg * gv[2 * i + 1]) * (gu * uv[2 * i + 1]));
+          if (c == 0 && ge > 0 && !__all_sync(0xffffffffu, mbar_wait(h_empty, (uint32_t)((ge - 1) & 1)))) {
+            ok = false;
+            break;
+          }
+          const uint32_t at = sH + (c >> 1) * H_ATOM;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(at + sw_off(r, 4 * (c & 1) + k)),
+                         "r"(a[4 * k]), "r"(a[4 * k + 1]), "r"(a[4 * k + 2]), "r"(a[4 * k + 3])
+                         : "memory");
+        }
+        if (!ok) break;
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(h_full);
+        MOE_TC_TRACE(3, e);
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  } else {
+    // ---- site warps 6-9: rows 32 (warp % 4) .., one quarter (4 experts) at a time ----
+    const int q = warp & 3;
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+    const float gd = __ldg(gammas + 2);
+    float* ys = reinterpret_cast<float*>(smem + OFF_YS + (warp - 6) * 4096);
+    unsigned char* ring = smem + OFF_RING + (warp - 6) * RING;
+    int64_t gq = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int qt = 0; qt < 4 && ok; ++qt, ++gq) {
+        const int yb = (int)(gq & 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&y_full[yb], (uint32_t)((gq >> 1) & 1)))) {
+          ok = false;
+          break;
+        }
+        fence_after_sync();
+        MOE_TC_TRACE(4, 4 * qt);
+        site_block<TU, TX>(t * TOK + q * 32, 4 * qt, tl + COL_Y + 128 * yb, lane, ys, ring, ntok, rw, gd, y,
+                           fuse_post, x, hmix, xo);
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&y_empty[yb]);
+        MOE_TC_TRACE(5, 4 * qt);
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  __syncwarp();
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_moe_tc05_error, (int)WALSH_ERR_TIMEOUT);
+  if (warp == 1) {
+    fence_after_sync();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// 1 = ran, 0 = not applicable, < 0 = launch error
+template <typename TU, typename TX>
+static int launch_moe_experts_tc05(const void* u, int64_t ntok, const float* rw, const void* wgu, const void* wdown,
+                                   const float* gammas, void* y, int fuse_post, const void* x, const float* hmix,
+                                   void* xo, cudaStream_t s) {
+  using namespace moe_tc5;
+  constexpr bool BF = std::is_same<TU, __nv_bfloat16>::value;
+  CUtensorMap mu, mg, md;
+  if (!make_tile_map(&mu, u, BF, ntok, C, 64, TOK) || !make_tile_map(&mg, wgu, BF, NPAIR * 256, 64, 64, 256) ||
+      !make_tile_map(&md, wdown, BF, E * 32, HID, 64, 32))
+    return 0;
+  auto kern = moe_experts_tc05_kernel<TU, TX>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    return launch_status();
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  const int64_t tiles = (ntok + TOK - 1) / TOK;
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+  kern<<<grid, NTHREADS, SMEM, s>>>(mu, mg, md, ntok, rw, gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo);
+  const int st = launch_status();
+  return st == WALSH_OK ? 1 : st;
+}
+
+int moe_tc05_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_moe_tc05_error, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return WALSH_ERR_LAUNCH;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_moe_tc05_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
 }  // namespace walsh
 
 using namespace walsh;
+
+extern "C" walsh_status walsh_moe_experts_tc_fwd(const void* u, int dtype, int64_t ntok, const float* weights,
+                                                 const void* w_gu, const void* w_down, const float* gammas, void* y,
+                                                 int fuse_post, const void* x, int x_dtype, const float* hmix,
+                                                 void* x_out, void* stream) {
+  if (int e = injected("moe_experts_tc_fwd")) return e;
+  WALSH_CHECK_ARG(u && weights && w_gu && w_down && gammas);
+  WALSH_CHECK_SHAPE(ntok >= 0 && ntok <= 2147483647LL);
+  if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  if (fuse_post) {
+    WALSH_CHECK_ARG(x && hmix && x_out);
+    if (x_dtype != WALSH_BF16 && x_dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  } else {
+    WALSH_CHECK_ARG(y);
+  }
+  if ((((uintptr_t)u) | ((uintptr_t)w_gu) | ((uintptr_t)w_down) | ((uintptr_t)x) | ((uintptr_t)x_out) |
+       ((uintptr_t)y) | ((uintptr_t)hmix)) & 15u)
+    return WALSH_ERR_ALIGN;
+  if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  int r;
+  const bool ubf = dtype == WALSH_BF16, xbf = !fuse_post || x_dtype == WALSH_BF16;
+  if (ubf)
+    r = xbf ? launch_moe_experts_tc05<__nv_bfloat16, __nv_bfloat16>(u, ntok, weights, w_gu, w_down, gammas, y,
+                                                                     fuse_post, x, hmix, x_out, s)
+            : launch_moe_experts_tc05<__nv_bfloat16, __half>(u, ntok, weights, w_gu, w_down, gammas, y, fuse_post,
+                                                             x, hmix, x_out, s);
+  else
+    r = xbf ? launch_moe_experts_tc05<__half, __nv_bfloat16>(u, ntok, weights, w_gu, w_down, gammas, y, fuse_post,
+                                                             x, hmix, x_out, s)
+            : launch_moe_experts_tc05<__half, __half>(u, ntok, weights, w_gu, w_down, gammas, y, fuse_post, x, hmix,
+                                                      x_out, s);
+  return r == 1 ? WALSH_OK : (r == 0 ? WALSH_ERR_SHAPE : r);
+}
 
 extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int top_k, const float* w1,
                                       const float* w2, const uint8_t* gate_2bit, const uint8_t* up_2bit,

@@ -24,6 +24,7 @@
 // registers into bf16 hi + lo (x_hi W + x_lo W, and + x_hi W_lo when a W_lo
 // correction matrix is given), which keeps float32 accuracy.
 #include <cudaTypedefs.h>
+#include <math_constants.h>
 
 #include <mutex>
 #include <type_traits>
@@ -103,22 +104,6 @@ __device__ __forceinline__ void load16(const T* p, float* v) {
   load8(p + 8, v + 8);
 }
 
-// packed fp32 pairs (low = first element) for fma.rn.f32x2 / mul.rn.f32x2
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
-}
-__device__ __forceinline__ uint64_t f2_dup(float v) { return f2_pack(v, v); }
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-
 // ---- epilogues: operator() once per (row m, column pair n, n+1), n even;
 // chunk16 once per row and 16 consecutive columns n..n+15 (n a multiple of
 // 16, destination rows aligned for 16-byte vectors; the launcher checks) ----
@@ -141,7 +126,8 @@ struct EpiPlain {
     chunk16(m, n + 16, v + 16);
   }
   __host__ bool vec_ok() const { return N % 16 == 0; }
-  static constexpr int kWarpScratch = 0;  // bytes of shared scratch per epilogue warp
+  static constexpr int kWarpScratch = 0;  // has a warp-cooperative path (warp_block)
+  static constexpr int kRowEpilogue = 0;  // one call per accumulator row (row)
 };
 
 template <typename TY>
@@ -200,6 +186,7 @@ struct EpiQkv {
   }
   __host__ bool vec_ok() const { return hd % 16 == 0 && C % 16 == 0; }
   static constexpr int kWarpScratch = 0;
+  static constexpr int kRowEpilogue = 0;
 };
 
 template <typename TY>
@@ -233,6 +220,7 @@ struct EpiSwiglu {
   }
   __host__ bool vec_ok() const { return hid % 8 == 0; }
   static constexpr int kWarpScratch = 0;
+  static constexpr int kRowEpilogue = 0;
 };
 
 template <typename TX>
@@ -329,6 +317,7 @@ struct EpiPost {
   static constexpr int kHSlot = 8 * 80;                  // 8 rows x (H_post | H_res) floats
   static constexpr int kSlot = kXSlot + kHSlot;
   static constexpr int kWarpScratch = sizeof(TX) == 2 ? 1 : 0;  // has the warp path
+  static constexpr int kRowEpilogue = 0;
   static constexpr int warp_bytes(int depth) { return kYBytes + depth * kSlot; }
   // one pass (chunk step / 4, rows 8 (step % 4) ..) into ring slot `slot`
   __device__ __forceinline__ void prefetch(int64_t m0, int64_t n0, int step, int slot, int lane,
@@ -423,6 +412,106 @@ struct EpiPost {
       cp_async_commit();
     }
     cp_async_wait<0>();
+  }
+};
+
+// Router of the Hadamard MoE (src/model/moe.py:383-447) as the epilogue of
+// h = u W1^T (N = 128 hidden units, one accumulator row per token):
+// silu(h) rounded to the activation type (the operand type of the second
+// layer), logits = silu(h) W2^T with W2 staged in shared memory as float
+// ([hidden][expert], one broadcast 16-byte load per 4 experts), softmax,
+// top-k (ties to the lower expert index) and the routing weights
+// renormalised over the selected experts in ascending order.
+template <typename TU>
+struct EpiRouter {
+  static constexpr int kWarpScratch = 0, kRowEpilogue = 1;
+  static constexpr int E = 16, HID = 128;
+  static constexpr int kRowScratch = E * HID * 4;
+  const TU* w2;  // [E][HID]
+  int top_k;
+  uint8_t* mask;
+  float* probs;
+  float* weights;
+  __host__ bool vec_ok() const { return true; }
+  // all 256 epilogue threads (t = 0..255), before the first tile
+  __device__ __forceinline__ void stage(float* ws, int t) const {
+    for (int i = t; i < E * HID; i += 256) {
+      const int e = i / HID, j = i - e * HID;
+      ws[j * E + e] = to_f(w2[i]);
+    }
+  }
+  __device__ __forceinline__ void row(int64_t m, uint32_t tacc, const float* ws, int64_t M) const {
+    float l[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) l[e] = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < HID; c += 32) {
+      float v[32];
+      tc05::tmem_ld32(tacc + (uint32_t)c, v);
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j) {
+        const float h = to_f(from_f<TU>(siluf_(v[j])));
+        const float4* wr = reinterpret_cast<const float4*>(ws + (c + j) * E);
+#pragma unroll
+        for (int q = 0; q < E / 4; ++q) {
+          const float4 w = wr[q];
+          l[4 * q] = fmaf(h, w.x, l[4 * q]);
+          l[4 * q + 1] = fmaf(h, w.y, l[4 * q + 1]);
+          l[4 * q + 2] = fmaf(h, w.z, l[4 * q + 2]);
+          l[4 * q + 3] = fmaf(h, w.w, l[4 * q + 3]);
+        }
+      }
+    }
+    if (m >= M) return;
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int e = 0; e < E; ++e) mx = fmaxf(mx, l[e]);
+    float p[E], sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      p[e] = expf(l[e] - mx);
+      sum += p[e];
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) p[e] = __fdiv_rn(p[e], sum);
+    uint32_t chosen = 0;
+    for (int k = 0; k < top_k; ++k) {
+      int best = -1;
+      float bv = -1.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (!((chosen >> e) & 1u) && p[e] > bv) {
+          bv = p[e];
+          best = e;
+        }
+      if (best < 0)
+        for (int e = E - 1; e >= 0; --e)
+          if (!((chosen >> e) & 1u)) best = e;
+      chosen |= 1u << best;
+    }
+    float wsum = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      if ((chosen >> e) & 1u) wsum += p[e];
+    wsum = fmaxf(wsum, 1e-8f);
+    float wv[E];
+    uint32_t mk[E / 4];
+#pragma unroll
+    for (int q = 0; q < E / 4; ++q) mk[q] = 0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const bool on = (chosen >> e) & 1u;
+      wv[e] = on ? __fdiv_rn(p[e], wsum) : 0.f;
+      mk[e >> 2] |= (on ? 1u : 0u) << (8 * (e & 3));
+    }
+    float4* wo = reinterpret_cast<float4*>(weights + m * E);
+    float4* po = reinterpret_cast<float4*>(probs + m * E);
+#pragma unroll
+    for (int q = 0; q < E / 4; ++q) {
+      wo[q] = make_float4(wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+      po[q] = make_float4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+    }
+    *reinterpret_cast<uint4*>(mask + m * E) = make_uint4(mk[0], mk[1], mk[2], mk[3]);
   }
 };
 
@@ -576,6 +665,10 @@ struct OctoTcShape {
       stages = K <= 512 ? 2 : 3;
       depth = K <= 512 ? 4 : 2;
       smem = scratch_off(stages) + 8 * Epi::warp_bytes(depth) + 1024;
+    } else if constexpr (Epi::kRowEpilogue > 0) {
+      stages = 3;
+      depth = 0;
+      smem = scratch_off(stages) + Epi::kRowScratch + 1024;
     } else {
       stages = octo_tc::STAGES;
       depth = 0;
@@ -685,6 +778,12 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
     // epilogue warps 2..9: TMEM lane quarter (warp % 4) holds accumulator rows
     // 32 (warp % 4) ..; warps 2-5 take columns 0..127, warps 6-9 128..255
     const int q = warp & 3, half = (warp - 2) >> 2;
+    float* rowscr = nullptr;
+    if constexpr (Epi::kRowEpilogue > 0) {
+      rowscr = reinterpret_cast<float*>(smem + OctoTcShape<Epi>::scratch_off(STAGES));
+      epi.stage(rowscr, threadIdx.x - 64);
+      asm volatile("bar.sync 1, 256;\n" ::: "memory");  // the 8 epilogue warps
+    }
     int i = 0;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int b = i & 1;
@@ -696,6 +795,10 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       const int64_t m = (t / ntl) * BM + q * 32 + lane, n0 = (t % ntl) * BN + half * (BN / 2);
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * ACC_COLS + half * (BN / 2));
       bool done = false;
+      if constexpr (Epi::kRowEpilogue > 0) {
+        if (half == 0) epi.row(m, base, rowscr, M);  // N <= BN / 2: the other half holds no columns
+        done = true;
+      }
       if constexpr (Epi::kWarpScratch > 0) {
         if (vec && n0 + BN / 2 <= N) {  // uniform over the warp
           unsigned char* scr =
@@ -707,21 +810,24 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
           done = true;
         }
       }
+      if constexpr (Epi::kRowEpilogue == 0) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 2 && !done; c += 32) {
-        float v[32];
-        tmem_ld32(base + (uint32_t)c, v);
-        const int64_t n = n0 + c;
-        if (m < M && n < N) {
-          if (vec && n + 32 <= N) {
-            epi.chunk32(m, n, v);
-          } else {
+        for (int c = 0; c < BN / 2 && !done; c += 32) {
+          float v[32];
+          tmem_ld32(base + (uint32_t)c, v);
+          const int64_t n = n0 + c;
+          if (m < M && n < N) {
+            if (vec && n + 32 <= N) {
+              epi.chunk32(m, n, v);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; j += 2)
-              if (n + j < N) epi(m, n + j, v[j], v[j + 1]);
+              for (int j = 0; j < 32; j += 2)
+                if (n + j < N) epi(m, n + j, v[j], v[j + 1]);
+            }
           }
         }
       }
+      (void)done;
       fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -819,6 +925,29 @@ extern "C" walsh_status walsh_octo_linear_fwd(const void* x, int dtype, int64_t 
                              launch_octo<TA>(x, M, K, w_hi, w_lo, N, octo::EpiPlain<TA>{scale, (TA*)y, N}, s));
 }
 
+extern "C" walsh_status walsh_moe_router_tc_fwd(const void* u, int dtype, int64_t ntok, const void* w1,
+                                               const void* w2, int top_k, uint8_t* mask, float* probs,
+                                               float* weights, void* stream) {
+  if (int e = injected("moe_router_tc_fwd")) return e;
+  WALSH_CHECK_ARG(u && w1 && w2 && mask && probs && weights);
+  WALSH_CHECK_SHAPE(ntok >= 0 && ntok <= 2147483647LL && top_k >= 1 && top_k <= 16);
+  if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  if ((((uintptr_t)u) | ((uintptr_t)w1) | ((uintptr_t)mask) | ((uintptr_t)probs) | ((uintptr_t)weights)) & 15u)
+    return WALSH_ERR_ALIGN;
+  if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  int r;
+  if (dtype == WALSH_BF16)
+    r = launch_octo_tc05<__nv_bfloat16>(u, ntok, 512, w1, 128,
+                                        octo::EpiRouter<__nv_bfloat16>{(const __nv_bfloat16*)w2, top_k, mask, probs,
+                                                                       weights},
+                                        s);
+  else
+    r = launch_octo_tc05<__half>(u, ntok, 512, w1, 128,
+                                 octo::EpiRouter<__half>{(const __half*)w2, top_k, mask, probs, weights}, s);
+  return r == 1 ? WALSH_OK : (r == 0 ? WALSH_ERR_SHAPE : r);
+}
+
 extern "C" walsh_status walsh_octo_qkv_fwd(const void* u, int dtype, int B, int T, int C, int n_head,
                                            const void* w_hi, const void* w_lo, int w_dtype, const float* scale,
                                            const float* rope_cos, const float* rope_sin, int n_pos, int start_pos,
@@ -907,10 +1036,12 @@ extern "C" int walsh_octo_set_mainloop(int tcgen05) {
 
 namespace walsh {
 int attn_tc05_error(int reset);  // attention_tc.cu
+int moe_tc05_error(int reset);   // moe.cu
 }
 
 extern "C" int walsh_tc05_error(int reset) {
   const int va = walsh::attn_tc05_error(reset);
+  const int vm = walsh::moe_tc05_error(reset);
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_tc05_error, sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
@@ -920,5 +1051,5 @@ extern "C" int walsh_tc05_error(int reset) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_tc05_error, &zero, sizeof(int));
   }
-  return v ? v : va;
+  return v ? v : (va ? va : vm);
 }

@@ -58,6 +58,18 @@ class FastMoEExperts(nn.Module):
                     ops.unpack(d, self.hidden).to(dtype).contiguous())
         return _prep.cached(self, f"tern_{dtype}", [self.gate_weights, self.up_weights, self.down_weights], build)
 
+    def pair_tc(self, dtype):
+        """Gate/up ternary values of expert pairs side by side, ``dtype`` [E/2, 256, 64]:
+        for pair p rows 0..127 gate, 128..255 up; columns 0..31 expert 2p, 32..63
+        expert 2p + 1 (the operand layout of walsh_moe_experts_tc_fwd)."""
+        def build():
+            g, u, _ = self.ternary_tc(dtype)
+            E, H, D = g.shape
+            gp = g.view(E // 2, 2, H, D).permute(0, 2, 1, 3).reshape(E // 2, H, 2 * D)
+            up = u.view(E // 2, 2, H, D).permute(0, 2, 1, 3).reshape(E // 2, H, 2 * D)
+            return torch.cat([gp, up], dim=1).contiguous()
+        return _prep.cached(self, f"pair_{dtype}", [self.gate_weights, self.up_weights], build)
+
     def forward(self, x: torch.Tensor, expert_weights: torch.Tensor) -> torch.Tensor:
         B, T, E, D = x.shape
         g, u, d, gam = self.packed()
@@ -136,7 +148,7 @@ class HadamardMoE(nn.Module):
         g, u, d, gam = self.experts.packed()
         tc = None
         if dtype != torch.float32:
-            tc = self.router.weights_tc(dtype) + self.experts.ternary_tc(dtype)
+            tc = self.router.weights_tc(dtype) + self.experts.ternary_tc(dtype) + (self.experts.pair_tc(dtype),)
         return w1t, w2, g, u, d, gam, self.router.top_k, tc
 
     @property

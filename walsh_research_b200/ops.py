@@ -157,6 +157,9 @@ def sinkhorn(h, iters=20, eps=1e-8):
 # below this many tokens (about a wave of 64-token tiles) the MoE runs as a
 # router GEMM plus the warp-per-token kernel instead of the 128-token kernels
 MOE_GEMM_ROUTER_BELOW = 148 * 64
+# prefill-sized C = 512 MoE on the tcgen05 router GEMM + expert kernel (False:
+# the single mma.sync kernel of walsh_moe_fwd; kept for comparisons)
+MOE_TC05 = True
 _ONES = {}
 
 
@@ -175,7 +178,7 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
     require_cuda(u)
     tcs = None
     if tc is not None:
-        tcs = _lib.MoeTcWeights(*[ptr(t) for t in tc])
+        tcs = _lib.MoeTcWeights(*[ptr(t) for t in tc[:5]])
     tcp = ctypes.byref(tcs) if tcs is not None else None
     u = _c(u)
     C = u.shape[-1]
@@ -200,6 +203,24 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
              ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0 if fuse is None else 1, ptr(x),
              dcode(x.dtype) if x is not None else dcode(u.dtype), ptr(hmix), ptr(x_out), ptr(mask), ptr(probs),
              ptr(weights), stream())
+        out = y if fuse is None else x_out
+        return (out, mask, probs, weights) if want_stats else out
+    if (MOE_TC05 and tc is not None and len(tc) > 5 and gate_p is not None and weights_in is None
+            and u.dtype != torch.float32 and C == 512 and ntok >= MOE_GEMM_ROUTER_BELOW and tc[0].dtype == u.dtype
+            and (fuse is None or fuse[0].dtype != torch.float32)):
+        # prefill-sized: router GEMM with the routing in its epilogue, then the
+        # experts and the site epilogue, both on the tcgen05 tensor cores
+        if not want_stats:
+            mask = torch.empty(lead + (E,), dtype=torch.uint8, device=u.device)
+            probs = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
+            weights = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
+        call("walsh_moe_router_tc_fwd", ptr(u), dcode(u.dtype), ntok, ptr(tc[0]), ptr(tc[1]), int(top_k), ptr(mask),
+             ptr(probs), ptr(weights), stream())
+        x, hmix, x_out = fuse if fuse is not None else (None, None, None)
+        y = torch.empty_like(u) if fuse is None else None
+        call("walsh_moe_experts_tc_fwd", ptr(u), dcode(u.dtype), ntok, ptr(weights), ptr(tc[5]), ptr(tc[4]),
+             ptr(gammas), ptr(y), 0 if fuse is None else 1, ptr(x),
+             dcode(x.dtype) if x is not None else dcode(u.dtype), ptr(hmix), ptr(x_out), stream())
         out = y if fuse is None else x_out
         return (out, mask, probs, weights) if want_stats else out
     if fuse is None:
