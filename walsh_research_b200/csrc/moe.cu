@@ -839,8 +839,8 @@ constexpr int STAGE = U_BYTES + G_BYTES + 2 * D_EXP;
 constexpr int NSTAGE = 2;
 constexpr int H_ATOM = TOK * 128;
 // site ring of one worker warp: per slot 8 rows x (4 streams x 32 columns of x,
-// H_post | H_res, the 16 routing weights)
-constexpr int XS = 8 * 4 * 64, HS = 8 * 80, WS = 8 * 64, SLOT = XS + HS + WS, DEPTH = 3, RING = DEPTH * SLOT;
+// H_post | H_res, the 4 routing weights around the pass's expert)
+constexpr int XS = 8 * 4 * 64, HS = 8 * 80, WS = 8 * 16, SLOT = XS + HS + WS, DEPTH = 4, RING = DEPTH * SLOT;
 constexpr int OFF_H = NSTAGE * STAGE;
 constexpr int OFF_YS = OFF_H + 2 * H_ATOM;     // 4 site warps x 32 x 32 floats
 constexpr int OFF_RING = OFF_YS + 4 * 4096;
@@ -875,7 +875,7 @@ __device__ __forceinline__ void site_prefetch(int64_t mw, int ex0, int step, int
     cp_async16(sl + XS + rq * 80 + cq * 16, hm + 4 * cq, in ? 16 : 0);
     if (cq == 0) cp_async16(sl + XS + rq * 80 + 64, hm + 16, in ? 16 : 0);
   }
-  cp_async16(sl + XS + HS + rq * 64 + cq * 16, rw + mm * E + 4 * cq, in ? 16 : 0);
+  if (cq == 0) cp_async16(sl + XS + HS + rq * 16, rw + mm * E + ((ex0 + k) & ~3), in ? 16 : 0);
 }
 
 // Site update (or y store) of one worker warp after 8 experts: rows mw ..
@@ -916,7 +916,7 @@ __device__ __forceinline__ void site_block(int64_t mw, int ex0, uint32_t tacc, i
     const int64_t m = mw + rr;
     const unsigned char* sl = ring + (step % DEPTH) * SLOT;
     if (m < ntok) {
-      const float wgt = reinterpret_cast<const float*>(sl + XS + HS + rq * 64)[ex] * gd;
+      const float wgt = reinterpret_cast<const float*>(sl + XS + HS + rq * 16)[ex & 3] * gd;
       const float4 y0 = *reinterpret_cast<const float4*>(ys + rr * 32 + 4 * ((2 * cq) ^ (rr & 7)));
       const float4 y1 = *reinterpret_cast<const float4*>(ys + rr * 32 + 4 * ((2 * cq + 1) ^ (rr & 7)));
       float yf[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};

@@ -156,24 +156,36 @@ struct EpiQkv {
                          : (which == 1 ? kc : vc) + (((size_t)b * n_head + head) * ctx + start_pos + t) * hd + d;
     store2(dst, v0, v1);
   }
-  // 16 columns = 16 dims of one head (hd a multiple of 16)
+  // 16 columns = 16 dims of one head (hd a multiple of 16; the launcher checks
+  // M < 2^31 and 16-byte aligned rows of cos / sin / scale, so the index math is
+  // 32-bit and the table rows are read as float4)
   __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
-    const int which = (int)(n / C);
-    const int c = (int)(n - (int64_t)which * C);
+    const int mi = (int)m, ni = (int)n;
+    const int which = ni / C;
+    const int c = ni - which * C;
     const int head = c / hd, d = c - head * hd;
-    const int b = (int)(m / T), t = (int)(m - (int64_t)b * T);
+    const int b = mi / T, t = mi - b * T;
     float o[16];
+    const float4* s4 = reinterpret_cast<const float4*>(scale + ni);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) o[j] = v[j] * __ldg(scale + n + j);
+    for (int j = 0; j < 4; ++j) {
+      const float4 sv = __ldg(s4 + j);
+      o[4 * j] = v[4 * j] * sv.x;
+      o[4 * j + 1] = v[4 * j + 1] * sv.y;
+      o[4 * j + 2] = v[4 * j + 2] * sv.z;
+      o[4 * j + 3] = v[4 * j + 3] * sv.w;
+    }
     if (which < 2) {
-      const float* cr = cos + (size_t)t * (hd / 2) + (d >> 1);
-      const float* sr = sin + (size_t)t * (hd / 2) + (d >> 1);
+      const float4* cr = reinterpret_cast<const float4*>(cos + (size_t)t * (hd / 2) + (d >> 1));
+      const float4* sr = reinterpret_cast<const float4*>(sin + (size_t)t * (hd / 2) + (d >> 1));
+      const float4 c0 = __ldg(cr), c1 = __ldg(cr + 1), s0 = __ldg(sr), s1 = __ldg(sr + 1);
+      const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float cs = __ldg(cr + j), sn = __ldg(sr + j);
         const float a = o[2 * j], bb = o[2 * j + 1];
-        o[2 * j] = a * cs - bb * sn;
-        o[2 * j + 1] = a * sn + bb * cs;
+        o[2 * j] = a * cs[j] - bb * sn[j];
+        o[2 * j + 1] = a * sn[j] + bb * cs[j];
       }
     }
     TY* dst = which == 0 ? q + (((size_t)b * n_head + head) * T + t) * hd + d
@@ -184,7 +196,9 @@ struct EpiQkv {
     chunk16(m, n, v);
     chunk16(m, n + 16, v + 16);
   }
-  __host__ bool vec_ok() const { return hd % 16 == 0 && C % 16 == 0; }
+  __host__ bool vec_ok() const {
+    return hd % 16 == 0 && C % 16 == 0 && ((((uintptr_t)cos) | ((uintptr_t)sin) | ((uintptr_t)scale)) & 15u) == 0;
+  }
   static constexpr int kWarpScratch = 0;
   static constexpr int kRowEpilogue = 0;
 };
@@ -957,6 +971,7 @@ extern "C" walsh_status walsh_octo_qkv_fwd(const void* u, int dtype, int B, int 
   const int hd = C / n_head;
   WALSH_CHECK_SHAPE(hd % 2 == 0 && start_pos >= 0 && start_pos + T <= ctx && T <= n_pos);
   const int64_t M = (int64_t)B * T;
+  WALSH_CHECK_SHAPE(M <= 2147483647LL);  // the epilogue's index math is 32-bit
   if (walsh_status st = octo_check(u, dtype, M, C, w_hi, w_lo, w_dtype, 3 * (int64_t)C)) return st;
   WALSH_CHECK_ARG(scale && rope_cos && rope_sin && q && k_cache && v_cache);
   if ((((uintptr_t)q) | ((uintptr_t)k_cache) | ((uintptr_t)v_cache)) & 7u) return WALSH_ERR_ALIGN;
