@@ -117,15 +117,22 @@ struct EpiPlain {
   }
   __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
     float o[16];
+    const float4* s4 = reinterpret_cast<const float4*>(scale + n);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) o[j] = v[j] * __ldg(scale + n + j);
+    for (int j = 0; j < 4; ++j) {
+      const float4 sv = __ldg(s4 + j);
+      o[4 * j] = v[4 * j] * sv.x;
+      o[4 * j + 1] = v[4 * j + 1] * sv.y;
+      o[4 * j + 2] = v[4 * j + 2] * sv.z;
+      o[4 * j + 3] = v[4 * j + 3] * sv.w;
+    }
     store16(y + m * N + n, o);
   }
   __device__ __forceinline__ void chunk32(int64_t m, int64_t n, const float* v) const {
     chunk16(m, n, v);
     chunk16(m, n + 16, v + 16);
   }
-  __host__ bool vec_ok() const { return N % 16 == 0; }
+  __host__ bool vec_ok() const { return N % 16 == 0 && (((uintptr_t)scale) & 15u) == 0; }
   static constexpr int kWarpScratch = 0;  // has a warp-cooperative path (warp_block)
   static constexpr int kRowEpilogue = 0;  // one call per accumulator row (row)
 };
@@ -225,14 +232,16 @@ struct EpiSwiglu {
   // 16 outputs h[m, n/2 .. n/2 + 15]; fast exp and division (16-bit output)
   __device__ __forceinline__ void chunk32(int64_t m, int64_t n, const float* v) const {
     float o[16];
+    const float4* s4 = reinterpret_cast<const float4*>(scale + n);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float g = v[2 * j] * __ldg(scale + n + 2 * j), u = v[2 * j + 1] * __ldg(scale + n + 2 * j + 1);
-      o[j] = siluf_(g) * u;
+    for (int j = 0; j < 8; ++j) {
+      const float4 sv = __ldg(s4 + j);
+      o[2 * j] = siluf_(v[4 * j] * sv.x) * (v[4 * j + 1] * sv.y);
+      o[2 * j + 1] = siluf_(v[4 * j + 2] * sv.z) * (v[4 * j + 3] * sv.w);
     }
     store16(h + m * hid + (n >> 1), o);
   }
-  __host__ bool vec_ok() const { return hid % 8 == 0; }
+  __host__ bool vec_ok() const { return hid % 8 == 0 && (((uintptr_t)scale) & 15u) == 0; }
   static constexpr int kWarpScratch = 0;
   static constexpr int kRowEpilogue = 0;
 };
