@@ -155,6 +155,24 @@ class CausalSelfAttention(nn.Module):
         ws = [p for lin in (self.wq, self.wk, self.wv) for p in (lin.weight, lin.inner.alpha, lin.inner.beta)]
         return _prep.cached(self, f"qkv_dense_{dtype}", ws, build)
 
+    def _out_dense(self, dtype):
+        """Head mixer then wo as one dense [C, C] matrix (the mixer applied to the
+        identity rows, composed with wo's full matrix in float64, rounded to the
+        operand dtype) with unit column scales: the operands of the tcgen05 output
+        GEMM with the mHC site epilogue."""
+        def build():
+            C = self.n_embd
+            eye = torch.eye(C, device=self.wo.weight.device, dtype=torch.float32)
+            mix = eye if self.head_mixer is None else self.head_mixer.forward_tokens(
+                eye.view(C, self.n_head, self.head_dim)).reshape(C, C)
+            W = (self.wo.inner.dense().double() @ mix.double().t()).float()
+            return (W.to(ops.octo_operand_dtype(dtype)).contiguous(), None), torch.ones(
+                C, device=W.device, dtype=torch.float32)
+        ws = [self.wo.weight, self.wo.inner.alpha, self.wo.inner.beta]
+        if self.head_mixer is not None:
+            ws += list(self.head_mixer.parameters())
+        return _prep.cached(self, f"out_dense_{dtype}", ws, build)
+
     def _tc(self, x) -> bool:
         return self.algebra == "hadamard" and ops.tc_eligible(x, torch.float16) and self.n_embd == 512
 
@@ -172,6 +190,10 @@ class CausalSelfAttention(nn.Module):
         w, sc = self._qkv_dense(x.dtype)
         ops.octo_qkv(x, H, w, sc, rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
         o = ops.attention(q, k_cache, v_cache, start_pos)
+        if B * T >= ops.MOE_GEMM_ROUTER_BELOW:
+            # prefill-sized: mixer and wo folded into one tcgen05 GEMM with the site epilogue
+            w, sc = self._out_dense(o.dtype)
+            return ops.octo_post(o.view(B, T, C), w, sc, xs, hmix, out=xs)
         wmix = bmix = None
         if self.head_mixer is not None:
             if hd != 16:
