@@ -722,3 +722,23 @@ def test_linear_split_vs_float64(M, K, N, strided, xdt):
     xr = xt.float().cpu().numpy().astype(np.float64)[:, :K]
     ref = xr @ w.astype(np.float64).T + b
     assert rel(y, ref) < 3e-5
+
+
+@pytest.mark.parametrize("D", [2048, 512, 33])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_embed_gather_rows_and_bad_index(D, dtype):
+    """Embedding gather (vector path for 16-byte rows, element path otherwise):
+    rows equal table[idx]; an out-of-range id gives a zero row and
+    WALSH_ERR_INDEX in the status word."""
+    from walsh_research_b200 import ops
+    rng = np.random.default_rng(D)
+    V, n = 1000, 5003
+    table = T(rng.normal(size=(V, D)).astype(np.float32), dtype)
+    idx = torch.from_numpy(rng.integers(0, V, size=n)).to(DEV)
+    idx[17] = V + 3
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.embed_gather(idx, table, err=err)
+    ref = table[idx.clamp(0, V - 1)].clone()
+    ref[17] = 0
+    assert torch.equal(out, ref)
+    assert int(err.item()) == -9

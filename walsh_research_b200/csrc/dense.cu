@@ -25,6 +25,30 @@ __global__ void gather_kernel(const int64_t* __restrict__ idx, int64_t ntok, con
   }
 }
 
+// Row-vectorised gather (rows of D * sizeof(T) bytes, a multiple of 16, table
+// and out 16-byte aligned): one warp per token, the index checked once, the
+// row copied as 16-byte vectors (an out-of-range index writes a zero row and
+// sets *err, as gather_kernel does).
+template <typename T>
+__global__ void __launch_bounds__(256)
+gather_vec_kernel(const int64_t* __restrict__ idx, int64_t ntok, const T* __restrict__ table, int64_t V, int D,
+                  T* __restrict__ out, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarp = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nvec = D * (int)sizeof(T) / 16;
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < ntok; t += nwarp) {
+    const int64_t id = __ldg(idx + t);
+    uint4* dst = reinterpret_cast<uint4*>(out + t * D);
+    if (id < 0 || id >= V) {
+      for (int v = lane; v < nvec; v += 32) dst[v] = make_uint4(0u, 0u, 0u, 0u);
+      if (err && lane == 0) atomicExch(err, (int)WALSH_ERR_INDEX);
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(table + id * D);
+      for (int v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
+    }
+  }
+}
+
 // 64x64 output tile per CTA, 4x4 per thread, K staged 16 at a time.
 template <typename Tx, typename Tw, typename Ty>
 __global__ void __launch_bounds__(256)
@@ -247,9 +271,18 @@ extern "C" walsh_status walsh_embed_gather(const int64_t* idx, int64_t ntok, con
   WALSH_CHECK_ARG(idx && table && out);
   WALSH_CHECK_SHAPE(ntok >= 0 && V > 0 && D > 0);
   if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int esz = dtype == WALSH_F32 ? 4 : 2;
+  if (((int64_t)D * esz) % 16 == 0 && ((((uintptr_t)table) | ((uintptr_t)out)) & 15u) == 0) {
+    int64_t g = (ntok + 7) / 8;  // 8 warps (tokens) per CTA
+    if (g > 148 * 16) g = 148 * 16;
+    return WALSH_DISPATCH_DTYPE(dtype, T,
+                                (gather_vec_kernel<T><<<(unsigned)g, 256, 0, s>>>(idx, ntok, (const T*)table, V, D,
+                                                                                  (T*)out, err),
+                                 launch_status()));
+  }
   int64_t g = (ntok * D + 255) / 256;
   if (g > 148 * 16) g = 148 * 16;
-  cudaStream_t s = (cudaStream_t)stream;
   return WALSH_DISPATCH_DTYPE(dtype, T, (gather_kernel<T><<<(unsigned)g, 256, 0, s>>>(idx, ntok, (const T*)table, V, D,
                                                                                     (T*)out, err),
                                          launch_status()));
