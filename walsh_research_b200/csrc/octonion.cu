@@ -146,6 +146,7 @@ struct EpiQkv {
   const float* cos;  // [T, hd/2]: rows of the tokens' own positions
   const float* sin;
   int T, n_head, hd, C, ctx, start_pos;
+  int c_shift, hd_shift;  // log2 C and log2 hd when they are powers of two, else -1
   __device__ __forceinline__ void operator()(int64_t m, int64_t n, float v0, float v1) const {
     const int which = (int)(n / C);
     const int c = (int)(n - (int64_t)which * C);
@@ -168,9 +169,9 @@ struct EpiQkv {
   // 32-bit and the table rows are read as float4)
   __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
     const int mi = (int)m, ni = (int)n;
-    const int which = ni / C;
+    const int which = c_shift >= 0 ? ni >> c_shift : ni / C;
     const int c = ni - which * C;
-    const int head = c / hd, d = c - head * hd;
+    const int head = hd_shift >= 0 ? c >> hd_shift : c / hd, d = c - head * hd;
     const int b = mi / T, t = mi - b * T;
     float o[16];
     const float4* s4 = reinterpret_cast<const float4*>(scale + ni);
@@ -985,10 +986,17 @@ extern "C" walsh_status walsh_octo_qkv_fwd(const void* u, int dtype, int B, int 
   WALSH_CHECK_ARG(scale && rope_cos && rope_sin && q && k_cache && v_cache);
   if ((((uintptr_t)q) | ((uintptr_t)k_cache) | ((uintptr_t)v_cache)) & 7u) return WALSH_ERR_ALIGN;
   cudaStream_t s = (cudaStream_t)stream;
+  auto log2_or_neg = [](int v) {
+    int k = 0;
+    while ((1 << k) < v) ++k;
+    return (1 << k) == v ? k : -1;
+  };
+  const int c_shift = log2_or_neg(C), hd_shift = log2_or_neg(hd);
   return WALSH_OCTO_DISPATCH(dtype, TA,
                              launch_octo<TA>(u, M, C, w_hi, w_lo, 3 * (int64_t)C,
                                              octo::EpiQkv<TA>{scale, (TA*)q, (TA*)k_cache, (TA*)v_cache, rope_cos,
-                                                              rope_sin, T, n_head, hd, C, ctx, start_pos},
+                                                              rope_sin, T, n_head, hd, C, ctx, start_pos, c_shift,
+                                                              hd_shift},
                                              s));
 }
 
