@@ -334,10 +334,11 @@ int walsh_octo_set_mainloop(int tcgen05);
  * reset != 0 clears it.  No counterpart in the reference. */
 int walsh_tc05_error(int reset);
 
-/* tcgen05 != 0: fp16 prefill attention with head dim 16 and at most 1024
- * keys runs on the 5th-generation tensor cores (S and P V as tcgen05 MMAs
- * into Tensor Memory); 0 (the default, faster at head dim 16): the mma.sync
- * kernels of walsh_attn_fwd.  Returns the previous setting.  Process-wide.
+/* Kernel of fp16 prefill attention with head dim 16 and at most 1024 keys:
+ * 1 = on the 5th-generation tensor cores (S and P V as tcgen05 MMAs into
+ * Tensor Memory); 2 = hybrid (S as a tcgen05 MMA, softmax and P V on
+ * mma.sync); 0 (the default): the mma.sync kernels of walsh_attn_fwd; any
+ * other nonzero value means 1.  Returns the previous setting.  Process-wide.
  * No counterpart in the reference (selects between this library's own
  * kernels, e.g. to compare them in tests). */
 int walsh_attn_set_path(int tcgen05);

@@ -115,10 +115,12 @@ def test_bounded_wait_times_out_and_context_survives():
 
 @pytest.mark.parametrize("B,H,Tq,start", [(2, 3, 1024, 0), (1, 4, 300, 0), (2, 2, 77, 130), (1, 2, 129, 500),
                                           (3, 2, 6, 0), (1, 2, 1000, 24), (2, 1, 640, 0)])
-def test_attention_tcgen05_matches_mma_sync_and_oracle(B, H, Tq, start):
-    """fp16 prefill attention, head dim 16: the tcgen05 kernel (S and P V in
-    Tensor Memory) against the mma.sync whole-head kernel and float64 sdpa on
-    the same fp16 inputs; full and partial 128-row query tiles, cached prefixes."""
+@pytest.mark.parametrize("mode", [1, 2])
+def test_attention_tcgen05_matches_mma_sync_and_oracle(B, H, Tq, start, mode):
+    """fp16 prefill attention, head dim 16: the tcgen05 kernels (mode 1: S and
+    P V in Tensor Memory; mode 2: S in Tensor Memory, softmax and P V on
+    mma.sync) against the mma.sync whole-head kernel and float64 sdpa on the
+    same fp16 inputs; full and partial 128-row query tiles, cached prefixes."""
     from walsh_research_b200 import _lib, ops
     from test_gpu_parity import _attn_ref
     rng = np.random.default_rng(B * 1000 + Tq + start)
@@ -127,7 +129,7 @@ def test_attention_tcgen05_matches_mma_sync_and_oracle(B, H, Tq, start):
     k = T(rng.normal(size=(B, H, ctx, 16)).astype(np.float32), torch.float16)
     v = T(rng.normal(size=(B, H, ctx, 16)).astype(np.float32), torch.float16)
     _lib.call("walsh_tc05_error", 1)
-    prev = _lib.call("walsh_attn_set_path", 1)
+    prev = _lib.call("walsh_attn_set_path", mode)
     try:
         a = ops.attention(q, k, v, start)
         torch.cuda.synchronize()

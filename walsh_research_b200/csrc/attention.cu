@@ -455,29 +455,42 @@ constexpr int kAttnHeadMaxKeys = 2048;
 #define WALSH_ATTN_POLY_PAIRS 0x00
 #endif
 
-__global__ void __launch_bounds__(256)
+// Byte offset of 16-byte half c (0, 1) of key row r in a K or V tile of
+// 32-byte rows: the halves trade places on every other group of four rows,
+// so the eight rows one ldmatrix phase reads (one half each) fall in eight
+// distinct bank quads, with and without .trans.
+__device__ __forceinline__ uint32_t kv_swz(int r, int c) {
+  return (uint32_t)(r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
+}
+
+// 64 KB of K and V at 1024 keys: three CTAs (24 warps) per SM.
+__global__ void __launch_bounds__(256, 3)
 attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc, int H,
                  int Tq, int ctx, int start_pos, float scale_log2, __half* __restrict__ o) {
-  constexpr int HD = 16, LD = HD + 8, KT = 64;
-  extern __shared__ __align__(16) __half smh[];
-  __half* Ks = smh;  // [kpad][LD]
+  constexpr int HD = 16, KT = 64;
+  extern __shared__ __align__(16) unsigned char smb[];
+  unsigned char* Ks = smb;  // [kpad] rows of 32 bytes (kv_swz)
   const int b = blockIdx.y, h = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const size_t bh = (size_t)b * H + h;
   const int kend = start_pos + Tq;
   const int kpad = (kend + KT - 1) / KT * KT;  // the last 64-key step reads up to here
-  __half* Vs = smh + (size_t)kpad * LD;        // [kpad][LD]
+  unsigned char* Vs = smb + (size_t)kpad * 32;  // [kpad] rows of 32 bytes (kv_swz)
   const __half* kb = kc + bh * ctx * HD;
   const __half* vb = vc + bh * ctx * HD;
   for (int i = tid; i < kpad * 2; i += 256) {
-    const int r = i >> 1, c = (i & 1) * 8;
+    const int r = i >> 1, c = i & 1;
     const bool in = r < kend;  // rows kend..kpad-1 are zero-filled
-    cp_async16(Ks + r * LD + c, kb + (size_t)(in ? r : 0) * HD + c, in ? 16 : 0);
-    cp_async16(Vs + r * LD + c, vb + (size_t)(in ? r : 0) * HD + c, in ? 16 : 0);
+    cp_async16(Ks + kv_swz(r, c), kb + (size_t)(in ? r : 0) * HD + c * 8, in ? 16 : 0);
+    cp_async16(Vs + kv_swz(r, c), vb + (size_t)(in ? r : 0) * HD + c * 8, in ? 16 : 0);
   }
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
+  // this lane's ldmatrix row addresses within a 16-key group (the group
+  // start is a multiple of 8 rows, so the swizzle depends on the lane only)
+  const uint32_t k_lane = kv_swz((lane & 7) + ((lane >> 4) << 3), (lane >> 3) & 1);
+  const uint32_t v_lane = kv_swz(lane & 15, lane >> 4);
 
   const __half* qb = q + bh * Tq * HD;
   const int nqt = (Tq + 15) / 16;
@@ -520,7 +533,7 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
 #pragma unroll
       for (int np = 0; np < KT / 16; ++np) {
         uint32_t kf[4];
-        ldsm_x4(kf, Ks + (k0 + np * 16 + (lane & 7) + ((lane >> 4) << 3)) * LD + ((lane >> 3) & 1) * 8);
+        ldsm_x4(kf, Ks + k_lane + (k0 + np * 16) * 32);
         mma_f16_rowc(s[2 * np], qf, kf[0], kf[1], -m_lo, -m_hi);
         mma_f16_rowc(s[2 * np + 1], qf, kf[2], kf[3], -m_lo, -m_hi);
       }
@@ -587,7 +600,7 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk) {
         uint32_t vf[4];
-        ldsm_x4_t(vf, Vs + (k0 + kk * 16 + (lane & 15)) * LD + (lane >> 4) * 8);
+        ldsm_x4_t(vf, Vs + v_lane + (k0 + kk * 16) * 32);
         mma_f16(oacc[0], pf[kk], vf[0], vf[1]);
         mma_f16(oacc[1], pf[kk], vf[2], vf[3]);
         mma_f16(oacc[HD / 8], pf[kk], 0x3C003C00u, 0x3C003C00u);  // row sums of P
@@ -620,7 +633,7 @@ static int launch_attn(const void* q, const void* kc, const void* vc, int B, int
     if (const int r = launch_attn_tc05(q, kc, vc, B, H, Tq, ctx, start_pos, scale_log2, o, s)) return r < 0 ? r : WALSH_OK;
     const int kend = start_pos + Tq;
     if (Tq > 4 && aligned && kend <= kAttnHeadMaxKeys && H <= 65535 && B <= 65535) {
-      const int smem = 2 * ((kend + 63) / 64 * 64) * (HD + 8) * (int)sizeof(__half);
+      const int smem = 2 * ((kend + 63) / 64 * 64) * HD * (int)sizeof(__half);
       if (smem > 48 * 1024 &&
           cudaFuncSetAttribute(attn_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return launch_status();

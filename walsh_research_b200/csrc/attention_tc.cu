@@ -537,11 +537,270 @@ attn_tc05_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
   }
 }
 
-// Off by default: measured on B200 (B64 x H32 x T1024, hd 16) this kernel takes
-// 556-580 us against 418 us for the mma.sync whole-head kernel.  At head dim 16
-// the work is the 1.2 G softmax exponentials per layer: ex2 runs at 16
-// results / clock / SM whether paired (f16x2) or not, a floor of about 260 us,
-// and moving S and P V onto tcgen05 does not shorten it.
+
+// ---------------------------------------------------------------------------
+// Hybrid prefill attention (fp16, head dim 16): S = Q K^T of a 128-row query
+// block and 64 keys per step as one tcgen05 MMA into tensor memory; the
+// softmax and O += P V stay in registers on mma.sync.  The 16x256b form of
+// tcgen05.ld hands a warp its 16 rows of S in exactly the m16n8 accumulator
+// layout (thread t: rows t/4 and t/4 + 8, columns 2 (t % 4) .. of each
+// 8-column group), so the softmax code is that of attn_head_kernel.  Taking
+// S off the mma.sync pipe leaves it 12 of the 20 legacy MMAs per 1024 scores
+// (P V and the row sums).
+// CTA = one (batch, head); its Q (scaled into the exp2 domain) and K are
+// staged packed four 64-row blocks to a 128-byte swizzled row (as in
+// attn_tc05_kernel), V as 32-byte rows with the two 16-byte halves swapped
+// on every other group of four rows (conflict-free ldmatrix.trans).  Warp 8
+// allocates tensor memory and issues the S MMAs into NBUF rotating 64-column
+// S buffers; warp w < 8 owns tensor memory lanes 32 (w % 4) + 16 (w / 4) ..
+// + 15 of each block (its lane quarter, which is also its scheduler
+// partition) and skips the key steps its rows cannot see.  SWAP: odd query
+// blocks are staged with their two 64-row halves exchanged, so the diagonal
+// step only the lower half sees alternates between partitions 0-1 and 2-3.
+// ---------------------------------------------------------------------------
+namespace attn_hy {
+constexpr int NSOFT = 8, MMA_WARP = 8, NTHREADS = 32 * (NSOFT + 1);
+constexpr int MAX_KEYS = 1024, MAX_QB = 8;
+constexpr int QSUPER_BYTES = 128 * 128;  // 4 query blocks of 128 rows
+constexpr int KSUPER_BYTES = 64 * 128;   // 4 key blocks of 64 rows
+__host__ __device__ inline int q_bytes(int nqb) { return (nqb + 3) / 4 * QSUPER_BYTES; }
+__host__ __device__ inline int k_off(int nqb) { return q_bytes(nqb); }
+__host__ __device__ inline int v_off(int nqb, int nkb) { return k_off(nqb) + (nkb + 3) / 4 * KSUPER_BYTES; }
+__host__ __device__ inline int bar_off(int nqb, int nkb) { return v_off(nqb, nkb) + nkb * 64 * 32; }
+__host__ inline int smem_bytes(int nqb, int nkb) { return 1024 + bar_off(nqb, nkb) + 128; }  // barriers, tmem slot, abort flag
+// byte offset of 16-byte chunk c (0, 1) of V row r
+__device__ __forceinline__ uint32_t v_swz(int r, int c) { return (uint32_t)(r * 32 + ((c ^ ((r >> 2) & 1)) << 4)); }
+__device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, float (*s)[4]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s[i][k] = __uint_as_float(r[4 * i + k]);
+}
+__device__ __forceinline__ int block_steps(int qb, int start_pos, int kend) {
+  return (min(kend, start_pos + 128 * qb + 128) + 63) >> 6;
+}
+}  // namespace attn_hy
+
+template <int NBUF, bool SWAP>
+__global__ void __launch_bounds__(attn_hy::NTHREADS, 2)
+attn_hybrid_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc, int H,
+                   int Tq, int ctx, int start_pos, float scale_log2, __half* __restrict__ o) {
+  using namespace attn_hy;
+  using namespace tc05;
+  constexpr int HD = 16, KT = 64;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int kend = start_pos + Tq;
+  const int nqb = (Tq + 127) >> 7, nkb = (kend + 63) >> 6;
+  unsigned char* Qs = smem;
+  unsigned char* Ks = smem + k_off(nqb);
+  unsigned char* Vs = smem + v_off(nqb, nkb);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + bar_off(nqb, nkb));
+  constexpr uint32_t TMEM_COLS = 64 * NBUF;
+  uint64_t* s_full = bars;         // [NBUF] S buffer written (MMA commit)
+  uint64_t* s_free = bars + NBUF;  // [NBUF] S buffer read by the 8 softmax warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NBUF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NBUF; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], NSOFT);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  // ---- stage K (packed), V (swizzled rows, zero past kend) and Q (scaled, packed) ----
+  const size_t bh = (size_t)b * H + h;
+  const __half* kb = kc + bh * ctx * HD;
+  const __half* vb = vc + bh * ctx * HD;
+  const __half* qb = q + bh * Tq * HD;
+  for (int i = threadIdx.x; i < nkb * 64 * 2; i += NTHREADS) {
+    const int key = i >> 1, c = i & 1;
+    const int r = key & 63, slot = (key >> 6) & 3, sb = key >> 8;
+    const bool in = key < kend;
+    cp_async16(Ks + sb * KSUPER_BYTES + attn_tc::sw_off(r, 2 * slot + c), kb + (size_t)(in ? key : 0) * HD + c * 8,
+               in ? 16 : 0);
+    cp_async16(Vs + v_swz(key, c), vb + (size_t)(in ? key : 0) * HD + c * 8, in ? 16 : 0);
+  }
+  cp_async_commit();
+  {
+    const __half2 sc = __float2half2_rn(scale_log2);
+    for (int i = threadIdx.x; i < nqb * 128 * 2; i += NTHREADS) {
+      const int qbk = i >> 8, r = (i >> 1) & 127, c = i & 1;
+      const int row = qbk * 128 + (SWAP ? (r + 64 * (qbk & 1)) & 127 : r);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (row < Tq) {
+        v = __ldg(reinterpret_cast<const uint4*>(qb + (size_t)row * HD + c * 8));
+        __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hv[e] = __hmul2(hv[e], sc);
+      }
+      *reinterpret_cast<uint4*>(Qs + (qbk >> 2) * QSUPER_BYTES + attn_tc::sw_off(r, 2 * (qbk & 3) + c)) = v;
+    }
+  }
+  cp_async_wait<0>();
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == MMA_WARP) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_f16(false, 128, 64);
+      const uint32_t sQ = smem_u32(Qs), sK = smem_u32(Ks);
+      int g2 = 0;
+      bool ok = true;
+      for (int qbk = 0; qbk < nqb && ok; ++qbk) {
+        const int nst = block_steps(qbk, start_pos, kend);
+        for (int j = 0; j < nst; ++j, ++g2) {
+          const int sb = g2 % NBUF;
+          if (g2 >= NBUF && !mbar_wait_sleep(&s_free[sb], (uint32_t)((g2 / NBUF - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint64_t da = sw128_desc(sQ + (qbk >> 2) * QSUPER_BYTES) + 2 * (qbk & 3);
+          const uint64_t db = sw128_desc(sK + (j >> 2) * KSUPER_BYTES) + 2 * (j & 3);
+          umma_f16(tmem + 64 * sb, da, db, IDESC, 0);
+          umma_commit(&s_full[sb]);
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    const int r0 = 32 * (warp & 3) + 16 * (warp >> 2);  // this warp's 16 rows of each block
+    const uint32_t tl = tmem + ((uint32_t)r0 << 16);
+    int g2 = 0;
+    bool ok = true;
+    for (int qbk = 0; qbk < nqb && ok; ++qbk) {
+      const int nst = block_steps(qbk, start_pos, kend);
+      const int q0 = qbk * 128 + (SWAP ? (r0 + 64 * (qbk & 1)) & 127 : r0);
+      const int r_lo = q0 + g, r_hi = r_lo + 8;
+      const int qp_lo = start_pos + r_lo, qp_hi = start_pos + r_hi;
+      const int nkey = min(kend, start_pos + q0 + 16);  // keys visible to some row of the slab
+      float m_lo = 0.f, m_hi = 0.f;
+      float thr_lo = -CUDART_INF_F, thr_hi = -CUDART_INF_F;
+      float oacc[HD / 8 + 1][4];
+#pragma unroll
+      for (int jj = 0; jj < HD / 8 + 1; ++jj) oacc[jj][0] = oacc[jj][1] = oacc[jj][2] = oacc[jj][3] = 0.f;
+      for (int j = 0; j < nst; ++j, ++g2) {
+        const int sb = g2 % NBUF;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)((g2 / NBUF) & 1)))) {
+          ok = false;
+          break;
+        }
+        fence_after_sync();
+        float s[KT / 8][4];
+        tmem_ld_16x256b_x8(tl + 64 * sb, s);
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);
+        const int k0 = j * KT;
+        if (k0 >= nkey) continue;  // no row of this slab sees these keys
+        if (k0 + KT > start_pos + q0 || k0 + KT > kend) {
+#pragma unroll
+          for (int n = 0; n < KT / 8; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = k0 + n * 8 + 2 * t4 + e;
+              if (key > qp_lo || key >= kend) s[n][e] = -CUDART_INF_F;
+              if (key > qp_hi || key >= kend) s[n][2 + e] = -CUDART_INF_F;
+            }
+        }
+        float mt_lo = -CUDART_INF_F, mt_hi = -CUDART_INF_F;
+#pragma unroll
+        for (int n = 0; n < KT / 8; ++n) {
+          mt_lo = fmax3(mt_lo, s[n][0], s[n][1]);
+          mt_hi = fmax3(mt_hi, s[n][2], s[n][3]);
+        }
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+          mt_lo = fmaxf(mt_lo, __shfl_xor_sync(0xffffffffu, mt_lo, off));
+          mt_hi = fmaxf(mt_hi, __shfl_xor_sync(0xffffffffu, mt_hi, off));
+        }
+        // the reference maximum m of a row moves to the row maximum once it passes
+        // m + thr (thr = -inf before the row's first visible key, 8 after)
+        const bool mv_lo = mt_lo > m_lo + thr_lo, mv_hi = mt_hi > m_hi + thr_hi;
+        if (__any_sync(0xffffffffu, mv_lo || mv_hi)) {
+          const float c_lo = !mv_lo ? 1.f : (thr_lo == -CUDART_INF_F ? 0.f : ex2_f32(m_lo - mt_lo));
+          const float c_hi = !mv_hi ? 1.f : (thr_hi == -CUDART_INF_F ? 0.f : ex2_f32(m_hi - mt_hi));
+#pragma unroll
+          for (int jj = 0; jj < HD / 8 + 1; ++jj) {
+            oacc[jj][0] *= c_lo; oacc[jj][1] *= c_lo;
+            oacc[jj][2] *= c_hi; oacc[jj][3] *= c_hi;
+          }
+          if (mv_lo) { m_lo = mt_lo; thr_lo = 8.f; }
+          if (mv_hi) { m_hi = mt_hi; thr_hi = 8.f; }
+        }
+        uint32_t pf[KT / 16][4];
+        const uint64_t one2 = f2_dup(1.f), nm_lo = f2_dup(-m_lo), nm_hi = f2_dup(-m_hi);
+#pragma unroll
+        for (int n = 0; n < KT / 8; ++n) {
+          const uint64_t d_lo = f2_fma(f2_pack(s[n][0], s[n][1]), one2, nm_lo);
+          const uint64_t d_hi = f2_fma(f2_pack(s[n][2], s[n][3]), one2, nm_hi);
+          pf[n >> 1][(n & 1) * 2 + 0] =
+              ex2_f16x2(pack_f16(__uint_as_float((uint32_t)d_lo), __uint_as_float((uint32_t)(d_lo >> 32))));
+          pf[n >> 1][(n & 1) * 2 + 1] =
+              ex2_f16x2(pack_f16(__uint_as_float((uint32_t)d_hi), __uint_as_float((uint32_t)(d_hi >> 32))));
+        }
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk) {
+          uint32_t vf[4];
+          ldsm_x4_t(vf, Vs + v_swz(k0 + kk * 16 + (lane & 15), lane >> 4));
+          mma_f16(oacc[0], pf[kk], vf[0], vf[1]);
+          mma_f16(oacc[1], pf[kk], vf[2], vf[3]);
+          mma_f16(oacc[HD / 8], pf[kk], 0x3C003C00u, 0x3C003C00u);  // row sums of P
+        }
+      }
+      if (!ok) break;
+      const float inv_lo = 1.0f / oacc[HD / 8][0], inv_hi = 1.0f / oacc[HD / 8][2];
+#pragma unroll
+      for (int jj = 0; jj < HD / 8; ++jj) {
+        const int d = jj * 8 + 2 * t4;
+        if (r_lo < Tq)
+          *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + r_lo) * H + h) * HD + d) =
+              pack_f16_sat(oacc[jj][0] * inv_lo, oacc[jj][1] * inv_lo);
+        if (r_hi < Tq)
+          *reinterpret_cast<uint32_t*>(o + (((size_t)b * Tq + r_hi) * H + h) * HD + d) =
+              pack_f16_sat(oacc[jj][2] * inv_hi, oacc[jj][3] * inv_hi);
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  __syncwarp();
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_attn_tc05_error, (int)WALSH_ERR_TIMEOUT);
+  if (warp == MMA_WARP) {
+    fence_after_sync();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// Off by default: measured on B200 (B64 x H32 x T1024, hd 16) the tcgen05
+// kernel takes 556-580 us and the hybrid 455 us against 381 us for the
+// mma.sync whole-head kernel.  At head dim 16 the work is the 1.2 G softmax
+// exponentials per layer: ex2 runs at 16 results / clock / SM whether paired
+// (f16x2) or not, a floor of about 260 us; none of the kernels fills that
+// pipe (about 50 % busy, latency stalls first), and the whole-head kernel
+// issues the fewest instructions per score and holds the most warps per SM.
 static int g_attn_tc05 = 0;
 static int g_attn_poly8 = -1;  // exponent pairs of 8 on the FMA pipe (WALSH_ATTN_TC_POLY8, default 0)
 
@@ -552,6 +811,17 @@ int launch_attn_tc05(const void* q, const void* kc, const void* vc, int B, int H
   const int kend = start_pos + Tq;
   if (!g_attn_tc05 || Tq <= 4 || Tq > MAX_QTILES * 128 || kend > MAX_KEYS || H > 65535 || B > 65535) return 0;
   if (((((uintptr_t)q) | ((uintptr_t)kc) | ((uintptr_t)vc) | ((uintptr_t)o)) & 15u) != 0) return 0;
+  if (g_attn_tc05 == 2) {
+    // two or four S buffers, halves exchanged or not: 454-457 us at B64 x H32 x T1024
+    const int hs = attn_hy::smem_bytes((Tq + 127) / 128, (kend + 63) / 64);
+    auto* kern = attn_hybrid_kernel<2, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, hs) != cudaSuccess)
+      return launch_status();
+    kern<<<dim3(H, B), attn_hy::NTHREADS, hs, s>>>((const __half*)q, (const __half*)kc, (const __half*)vc, H, Tq, ctx,
+                                                   start_pos, scale_log2, (__half*)o);
+    const int e = launch_status();
+    return e == WALSH_OK ? 1 : e;
+  }
   const int smem = smem_bytes((kend + 63) / 64);
   if (g_attn_poly8 < 0) {
     const char* e = getenv("WALSH_ATTN_TC_POLY8");
@@ -593,6 +863,6 @@ int attn_tc05_error(int reset) {
 
 extern "C" int walsh_attn_set_path(int tcgen05) {
   const int prev = walsh::g_attn_tc05;
-  walsh::g_attn_tc05 = tcgen05 ? 1 : 0;
+  walsh::g_attn_tc05 = tcgen05 == 2 ? 2 : (tcgen05 ? 1 : 0);
   return prev;
 }
