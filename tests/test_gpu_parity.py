@@ -406,6 +406,31 @@ def test_model_bf16_prefill_sized_batch():
     _bf16_model_check("model_h512", idx=idx, cfg_override={"block_size": 1024})
 
 
+def test_model_cuda_graph_replay_equals_eager():
+    """enable_cuda_graphs: first call eager, second captured, later calls
+    replayed; every call's logits equal the eager forward on the same ids
+    (same kernels), fresh ids reach the replayed graph, an in-place weight
+    update forces a new capture, and disabling restores the eager path."""
+    cfg, n, idx, sd, model = build_model("model_h512", torch.bfloat16)
+    rng = np.random.default_rng(41)
+    ids = [T(rng.integers(0, cfg["vocab_size"], idx.shape), torch.int64) for _ in range(4)]
+    with torch.no_grad():
+        eager = [model(i)[0].clone() for i in ids]
+        model.enable_cuda_graphs()
+        for rep in range(2):
+            for i, e in zip(ids, eager):
+                lg, loss = model(i)
+                assert loss is None
+                assert rel(lg, e.cpu().numpy()) < 1e-6
+        model.output.weight.mul_(1.5)          # tied embedding: changes the table and the head
+        after = [model(ids[0])[0] for _ in range(3)]   # eager, capture, replay
+        model.enable_cuda_graphs(False)
+        ref = model(ids[0])[0]
+    for lg in after:
+        assert rel(lg, ref.cpu().numpy()) < 1e-6
+    assert rel(ref, eager[0].cpu().numpy()) > 1e-3
+
+
 def test_model_autocast_selects_bf16():
     cfg, n, idx, sd, model = build_model("model_h512")
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):

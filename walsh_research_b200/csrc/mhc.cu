@@ -18,21 +18,30 @@ namespace walsh {
 
 // Sinkhorn-Knopp on a 4x4 matrix held in registers (src/model/mhc.py:214-229):
 // exp, then `iters` x (column, row) normalisation.  Each normalisation takes one
-// correctly rounded reciprocal of (sum + eps) and four multiplies (within one
-// ulp of the reference's four divisions per line).
+// hardware reciprocal of (sum + eps) (rcp.approx, within about one ulp; the
+// sums are at least eps, so never subnormal) and four multiplies: within two
+// ulps of the reference's four divisions per line.  A correctly rounded
+// reciprocal takes several instructions per call, and the normalisations are
+// most of the per-token activation work.
+__device__ __forceinline__ float rcp_fast(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ void sinkhorn4(float* M, int iters, float eps) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) M[i] = expf(M[i]);
   for (int it = 0; it < iters; ++it) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float inv = __frcp_rn((((M[c] + M[4 + c]) + M[8 + c]) + M[12 + c]) + eps);
+      const float inv = rcp_fast((((M[c] + M[4 + c]) + M[8 + c]) + M[12 + c]) + eps);
 #pragma unroll
       for (int r = 0; r < 4; ++r) M[4 * r + c] *= inv;
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const float inv = __frcp_rn((((M[4 * r] + M[4 * r + 1]) + M[4 * r + 2]) + M[4 * r + 3]) + eps);
+      const float inv = rcp_fast((((M[4 * r] + M[4 * r + 1]) + M[4 * r + 2]) + M[4 * r + 3]) + eps);
 #pragma unroll
       for (int c = 0; c < 4; ++c) M[4 * r + c] *= inv;
     }
@@ -478,11 +487,11 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
     for (int it = 0; it < 20; ++it) {
       const float c0 = __shfl_sync(0xffffffffu, M, base + c), c1 = __shfl_sync(0xffffffffu, M, base + 4 + c),
                   c2 = __shfl_sync(0xffffffffu, M, base + 8 + c), c3 = __shfl_sync(0xffffffffu, M, base + 12 + c);
-      M *= __frcp_rn((((c0 + c1) + c2) + c3) + 1e-8f);
+      M *= rcp_fast((((c0 + c1) + c2) + c3) + 1e-8f);
       const float r0 = __shfl_sync(0xffffffffu, M, base + 4 * r), r1 = __shfl_sync(0xffffffffu, M, base + 4 * r + 1),
                   r2 = __shfl_sync(0xffffffffu, M, base + 4 * r + 2),
                   r3 = __shfl_sync(0xffffffffu, M, base + 4 * r + 3);
-      M *= __frcp_rn((((r0 + r1) + r2) + r3) + 1e-8f);
+      M *= rcp_fast((((r0 + r1) + r2) + r3) + 1e-8f);
     }
     if (tok < ntok) hmix[tok * kMapRows + 8 + e] = M;
   }

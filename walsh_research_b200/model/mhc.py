@@ -306,9 +306,57 @@ class mHCWalsh(nn.Module):
             return ops.linear_split(h, *self.head_weights_split())
         return ops.linear(h, self.head_weights(), None, out_dtype=torch.float32)
 
+    # -- CUDA-graph replay of cache-free inference forwards ------------------------------
+    def enable_cuda_graphs(self, enabled: bool = True):
+        """Replay captured CUDA graphs for inference forwards without a KV cache
+        (no targets, no hidden states, gradients off): the first call of a
+        (shape, start_pos, dtype, device) runs eagerly and builds the derived
+        weights, the second captures the whole forward into a graph, later calls
+        copy the ids into the graph's input and replay it, one launch for the
+        host instead of one per kernel.  Logits come back as a new tensor.  A
+        graph is rebuilt after any parameter changes (load_state_dict, in-place
+        update, ``.to()``).  Graphs hold their activations in a private memory
+        pool until disabled."""
+        self._graphs_on = bool(enabled)
+        self.__dict__["_walsh_graphs"] = {}
+
+    def _param_key(self):
+        return tuple((p.data_ptr(), p._version) for p in self.parameters())
+
+    def _graph_forward(self, idx, start_pos):
+        graphs = self.__dict__.setdefault("_walsh_graphs", {})
+        key = (tuple(idx.shape), start_pos, self._act_dtype(), idx.device)
+        pkey = self._param_key()
+        ent = graphs.get(key)
+        if ent is not None and ent["params"] != pkey:
+            del graphs[key]
+            ent = None
+        if ent is None:
+            if graphs.get(("seen",) + key) != pkey:        # first call: eager, builds derived weights
+                graphs[("seen",) + key] = pkey
+                return self._forward(idx, None, None, start_pos, False)
+            static_idx = idx.clone()
+            torch.cuda.synchronize(idx.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                logits, _ = self._forward(static_idx, None, None, start_pos, False)
+            ent = {"graph": g, "idx": static_idx, "logits": logits, "err": self._last_index_error, "params": pkey}
+            graphs[key] = ent
+        else:
+            ent["idx"].copy_(idx, non_blocking=True)
+        ent["graph"].replay()
+        self._last_index_error = ent["err"]
+        return ent["logits"].clone(), None
+
     def forward(self, idx, targets=None, kv_cache=None, start_pos=0, return_hidden=False):
         if not idx.is_cuda:
             raise RuntimeError("walsh_research_b200 runs on CUDA devices only (no CPU fallback)")
+        if (getattr(self, "_graphs_on", False) and kv_cache is None and targets is None and not return_hidden
+                and not torch.is_grad_enabled()):
+            return self._graph_forward(idx, start_pos)
+        return self._forward(idx, targets, kv_cache, start_pos, return_hidden)
+
+    def _forward(self, idx, targets, kv_cache, start_pos, return_hidden):
         B, T = idx.shape
         C, n = self.config.n_embd, self.n_streams
         dt = self._act_dtype()
