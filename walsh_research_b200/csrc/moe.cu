@@ -803,7 +803,8 @@ static int launch_moe_mma(const void* u, int64_t ntok, int top_k, const walsh_mo
 // ---------------------------------------------------------------------------
 // Prefill MoE experts on the 5th-generation tensor cores (C = 512, E = 16
 // experts on 32-wide Hadamard blocks, hidden 128; routing weights come from
-// the router GEMM).  A CTA runs 128-token tiles (persistent).  Per expert
+// the router GEMM).  Persistent CTAs take (128-token tile, quarter of 4
+// experts) units round-robin.  Per expert
 // pair p one TMA stage brings u[:, 64p .. 64p + 63] (both experts' input
 // blocks), the pair's gate/up rows packed side by side ([gate 128 | up 128
 // rows] x [32 inputs of expert 2p | 32 of 2p + 1]) and the two experts' down
@@ -996,7 +997,11 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tiles = (ntok + TOK - 1) / TOK;
+  // work unit = (128-token tile, quarter of 4 experts): the quarters of a tile
+  // are independent (expert e reads u columns 32e .. 32e + 31 and writes only
+  // those columns of the streams), so the persistent CTAs take units
+  // round-robin -- 4x finer than whole tiles, which evens out the last round
+  const int64_t units = (ntok + TOK - 1) / TOK * 4;
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&full[i], 1);
@@ -1026,8 +1031,9 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
   if (warp == 0) {
     if (lane == 0) {
       int64_t g = 0;  // expert pairs loaded by this CTA
-      for (int64_t t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
-        for (int p = 0; p < NPAIR; ++p, ++g) {
+      for (int64_t un = blockIdx.x; un < units && !*abort_flag; un += gridDim.x) {
+        const int64_t t = un >> 2;
+        for (int p = 2 * (int)(un & 3); p < 2 * (int)(un & 3) + 2; ++p, ++g) {
           const int st = (int)(g & 1);
           if (g >= 2 && !mbar_wait_sleep(&empty[st], (uint32_t)(((g >> 1) - 1) & 1))) {
             *abort_flag = 1;
@@ -1052,8 +1058,8 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
       constexpr uint32_t IDESC2 = idesc_f16(std::is_same<TU, __nv_bfloat16>::value, 128, 32);
       // iteration ge: MMA1 of expert ge (as soon as D1 is free), then MMA2 of
       // expert ge - 1 (once its h tile is written); expert ge of this CTA is
-      // expert ge % 16 of its tile ge / 16, pair ge / 2 in stage (ge / 2) % 2
-      const int64_t total = ((tiles - blockIdx.x + gridDim.x - 1) / gridDim.x) * E;
+      // expert ge % 4 of its unit ge / 4, pair ge / 2 in stage (ge / 2) % 2
+      const int64_t total = ((units - blockIdx.x + gridDim.x - 1) / gridDim.x) * 4;
       bool ok = true;
       const uint64_t dH = sw128_desc(smem_u32(smem + OFF_H));
       for (int64_t ge = 0; ge <= total && ok; ++ge) {
@@ -1101,8 +1107,8 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
     const int r = q * 32 + lane;
     int64_t ge = 0;
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-      for (int e = 0; e < E && ok; ++e, ++ge) {
+    for (int64_t un = blockIdx.x; un < units && ok; un += gridDim.x) {
+      for (int e = 4 * (int)(un & 3); e < 4 * (int)(un & 3) + 4 && ok; ++e, ++ge) {
         if (!__all_sync(0xffffffffu, mbar_wait(d1_full, (uint32_t)(ge & 1)))) {
           ok = false;
           break;
@@ -1152,22 +1158,21 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
     unsigned char* ring = smem + OFF_RING + (warp - 6) * RING;
     int64_t gq = 0;
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-      for (int qt = 0; qt < 4 && ok; ++qt, ++gq) {
-        const int yb = (int)(gq & 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&y_full[yb], (uint32_t)((gq >> 1) & 1)))) {
-          ok = false;
-          break;
-        }
-        fence_after_sync();
-        MOE_TC_TRACE(4, 4 * qt);
-        site_block<TU, TX>(t * TOK + q * 32, 4 * qt, tl + COL_Y + 128 * yb, lane, ys, ring, ntok, rw, gd, y,
-                           fuse_post, x, hmix, xo);
-        fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&y_empty[yb]);
-        MOE_TC_TRACE(5, 4 * qt);
+    for (int64_t un = blockIdx.x; un < units && ok; un += gridDim.x, ++gq) {
+      const int64_t t = un >> 2;
+      const int qt = (int)(un & 3), yb = (int)(gq & 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(&y_full[yb], (uint32_t)((gq >> 1) & 1)))) {
+        ok = false;
+        break;
       }
+      fence_after_sync();
+      MOE_TC_TRACE(4, 4 * qt);
+      site_block<TU, TX>(t * TOK + q * 32, 4 * qt, tl + COL_Y + 128 * yb, lane, ys, ring, ntok, rw, gd, y,
+                         fuse_post, x, hmix, xo);
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&y_empty[yb]);
+      MOE_TC_TRACE(5, 4 * qt);
     }
     if (!ok) *abort_flag = 1;
   }
@@ -1202,8 +1207,8 @@ static int launch_moe_experts_tc05(const void* u, int64_t ntok, const float* rw,
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       sms = 148;
   }
-  const int64_t tiles = (ntok + TOK - 1) / TOK;
-  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+  const int64_t units = (ntok + TOK - 1) / TOK * 4;  // (tile, quarter of 4 experts)
+  const unsigned grid = (unsigned)(units < sms ? units : sms);
   kern<<<grid, NTHREADS, SMEM, s>>>(mu, mg, md, ntok, rw, gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
