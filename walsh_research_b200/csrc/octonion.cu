@@ -135,6 +135,7 @@ struct EpiPlain {
   __host__ bool vec_ok() const { return N % 16 == 0 && (((uintptr_t)scale) & 15u) == 0; }
   static constexpr int kWarpScratch = 0;  // has a warp-cooperative path (warp_block)
   static constexpr int kRowEpilogue = 0;  // one call per accumulator row (row)
+  static constexpr int kHalfRow = 0;      // one call per row and 128-column half (half_row)
 };
 
 template <typename TY>
@@ -209,6 +210,67 @@ struct EpiQkv {
   }
   static constexpr int kWarpScratch = 0;
   static constexpr int kRowEpilogue = 0;
+  // Row path of the tcgen05 kernel for hd = 16: the 3C column scales are
+  // staged in shared memory once per CTA, and per tile a thread loads its
+  // token's 8 cos and 8 sin values once (every head of the row uses the same
+  // 8 frequencies) instead of once per 16 columns, then streams its 128
+  // accumulator columns (two 32-column tensor-memory loads in flight).
+  static constexpr int kHalfRow = 1;
+  static constexpr int kRowScratch = 6144 * 4;  // 3C <= 6144
+  __host__ bool half_row_ok() const { return hd == 16 && C % 128 == 0 && 3 * C <= 6144 && vec_ok(); }
+  // all 256 epilogue threads (t = 0..255), before the first tile
+  __device__ __forceinline__ void stage(float* ws, int t) const {
+    for (int i = t; i < 3 * C; i += 256) ws[i] = __ldg(scale + i);
+  }
+  // columns n0 .. n0 + 127 of row m (one of q | k | v: C % 128 == 0); all 32
+  // lanes call it (tensor-memory loads are warp-wide), rows past M store nothing
+  __device__ __forceinline__ void half_row(int64_t m, int64_t n0, uint32_t tacc, const float* ws, int64_t M) const {
+    const bool valid = m < M;
+    const int mi = valid ? (int)m : 0, ni = (int)n0;
+    const int b = mi / T, t = mi - b * T;
+    const int which = c_shift >= 0 ? ni >> c_shift : ni / C;
+    float cs[8], sn[8];
+    if (which < 2) {
+      const float4* cr = reinterpret_cast<const float4*>(cos + (size_t)t * 8);
+      const float4* sr = reinterpret_cast<const float4*>(sin + (size_t)t * 8);
+      const float4 c0 = __ldg(cr), c1 = __ldg(cr + 1), s0 = __ldg(sr), s1 = __ldg(sr + 1);
+      cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+    }
+    const int head0 = (ni - which * C) >> 4;
+    const size_t hstride = (size_t)(which == 0 ? T : ctx) * 16;  // elements between heads
+    TY* row = which == 0 ? q + ((size_t)b * n_head * T + t) * 16
+                         : (which == 1 ? kc : vc) + ((size_t)b * n_head * ctx + start_pos + t) * 16;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 64) {
+      float v[64];
+      tc05::tmem_ld32_nowait(tacc + (uint32_t)c, v);
+      tc05::tmem_ld32_nowait(tacc + (uint32_t)c + 32, v + 32);
+      tc05::tmem_wait_ld();
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) {
+        float o[16];
+        const float4* s4 = reinterpret_cast<const float4*>(ws + ni + c + 16 * hh);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 sv = s4[j];
+          o[4 * j] = v[16 * hh + 4 * j] * sv.x;
+          o[4 * j + 1] = v[16 * hh + 4 * j + 1] * sv.y;
+          o[4 * j + 2] = v[16 * hh + 4 * j + 2] * sv.z;
+          o[4 * j + 3] = v[16 * hh + 4 * j + 3] * sv.w;
+        }
+        if (which < 2) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float a = o[2 * j], bb = o[2 * j + 1];
+            o[2 * j] = a * cs[j] - bb * sn[j];
+            o[2 * j + 1] = a * sn[j] + bb * cs[j];
+          }
+        }
+        if (valid) store16(row + (size_t)(head0 + (c >> 4) + hh) * hstride, o);
+      }
+    }
+  }
 };
 
 template <typename TY>
@@ -244,7 +306,7 @@ struct EpiSwiglu {
   }
   __host__ bool vec_ok() const { return hid % 8 == 0 && (((uintptr_t)scale) & 15u) == 0; }
   static constexpr int kWarpScratch = 0;
-  static constexpr int kRowEpilogue = 0;
+  static constexpr int kRowEpilogue = 0, kHalfRow = 0;
 };
 
 template <typename TX>
@@ -341,7 +403,7 @@ struct EpiPost {
   static constexpr int kHSlot = 8 * 80;                  // 8 rows x (H_post | H_res) floats
   static constexpr int kSlot = kXSlot + kHSlot;
   static constexpr int kWarpScratch = sizeof(TX) == 2 ? 1 : 0;  // has the warp path
-  static constexpr int kRowEpilogue = 0;
+  static constexpr int kRowEpilogue = 0, kHalfRow = 0;
   static constexpr int warp_bytes(int depth) { return kYBytes + depth * kSlot; }
   // one pass (chunk step / 4, rows 8 (step % 4) ..) into ring slot `slot`
   __device__ __forceinline__ void prefetch(int64_t m0, int64_t n0, int step, int slot, int lane,
@@ -448,7 +510,7 @@ struct EpiPost {
 // renormalised over the selected experts in ascending order.
 template <typename TU>
 struct EpiRouter {
-  static constexpr int kWarpScratch = 0, kRowEpilogue = 1;
+  static constexpr int kWarpScratch = 0, kRowEpilogue = 1, kHalfRow = 0;
   static constexpr int E = 16, HID = 128;
   static constexpr int kRowScratch = E * HID * 4;
   const TU* w2;  // [E][HID]
@@ -693,6 +755,10 @@ struct OctoTcShape {
       stages = 3;
       depth = 0;
       smem = scratch_off(stages) + Epi::kRowScratch + 1024;
+    } else if constexpr (Epi::kHalfRow > 0) {
+      stages = octo_tc::STAGES;
+      depth = 0;
+      smem = scratch_off(stages) + Epi::kRowScratch + 1024;
     } else {
       stages = octo_tc::STAGES;
       depth = 0;
@@ -803,9 +869,9 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
     // 32 (warp % 4) ..; warps 2-5 take columns 0..127, warps 6-9 128..255
     const int q = warp & 3, half = (warp - 2) >> 2;
     float* rowscr = nullptr;
-    if constexpr (Epi::kRowEpilogue > 0) {
+    if constexpr (Epi::kRowEpilogue > 0 || Epi::kHalfRow > 0) {
       rowscr = reinterpret_cast<float*>(smem + OctoTcShape<Epi>::scratch_off(STAGES));
-      epi.stage(rowscr, threadIdx.x - 64);
+      if (Epi::kRowEpilogue > 0 || vec == 2) epi.stage(rowscr, threadIdx.x - 64);
       asm volatile("bar.sync 1, 256;\n" ::: "memory");  // the 8 epilogue warps
     }
     int i = 0;
@@ -822,6 +888,12 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       if constexpr (Epi::kRowEpilogue > 0) {
         if (half == 0) epi.row(m, base, rowscr, M);  // N <= BN / 2: the other half holds no columns
         done = true;
+      }
+      if constexpr (Epi::kHalfRow > 0) {
+        if (vec == 2 && n0 + BN / 2 <= N) {  // uniform over the warp
+          epi.half_row(m, n0, base, rowscr, M);
+          done = true;
+        }
       }
       if constexpr (Epi::kWarpScratch > 0) {
         if (vec && n0 + BN / 2 <= N) {  // uniform over the warp
@@ -888,7 +960,11 @@ static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int6
   }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, M, K, N, epi, epi.vec_ok() ? 1 : 0, shp.stages, shp.depth);
+  int vec = epi.vec_ok() ? 1 : 0;  // 2: the epilogue's row path (half_row) applies
+  if constexpr (Epi::kHalfRow > 0) {
+    if (epi.half_row_ok()) vec = 2;
+  }
+  kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, M, K, N, epi, vec, shp.stages, shp.depth);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
 }
