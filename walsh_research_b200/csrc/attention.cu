@@ -464,6 +464,11 @@ __device__ __forceinline__ uint32_t kv_swz(int r, int c) {
 }
 
 // 64 KB of K and V at 1024 keys: three CTAs (24 warps) per SM.
+// F32P: P = 2^(S - m) as f32 exponentials whose row sums are packed f32x2
+// adds on the FMA pipe, P rounded to fp16 only as the P V operand (16 legacy
+// MMAs per 1024 scores); otherwise paired fp16 exponentials with the row sums
+// as an all-ones MMA column (20 MMAs).
+template <bool F32P>
 __global__ void __launch_bounds__(256, 3)
 attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc, int H,
                  int Tq, int ctx, int start_pos, float scale_log2, __half* __restrict__ o) {
@@ -528,6 +533,7 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
     float oacc[HD / 8 + 1][4];
 #pragma unroll
     for (int j = 0; j < HD / 8 + 1; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
+    uint64_t l2_lo = 0, l2_hi = 0;  // F32P: this thread's partial row sums (column pairs)
     for (int k0 = 0; k0 < nkey; k0 += KT) {
       float s[KT / 8][4];
 #pragma unroll
@@ -573,6 +579,10 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
           oacc[j][0] *= c_lo; oacc[j][1] *= c_lo;
           oacc[j][2] *= c_hi; oacc[j][3] *= c_hi;
         }
+        if (F32P) {
+          l2_lo = f2_mul(l2_lo, f2_dup(c_lo));
+          l2_hi = f2_mul(l2_hi, f2_dup(c_hi));
+        }
 #pragma unroll
         for (int n = 0; n < KT / 8; ++n) {
           s[n][0] -= d_lo; s[n][1] -= d_lo;
@@ -587,6 +597,17 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
       // by WALSH_ATTN_POLY_PAIRS on the FMA pipe, the rest as paired fp16 ex2 on
       // the MUFU pipe
       uint32_t pf[KT / 16][4];
+      if (F32P) {
+        const uint64_t one2 = f2_dup(1.f);
+#pragma unroll
+        for (int n = 0; n < KT / 8; ++n) {
+          const float p0 = ex2_f32(s[n][0]), p1 = ex2_f32(s[n][1]), p2 = ex2_f32(s[n][2]), p3 = ex2_f32(s[n][3]);
+          pf[n >> 1][(n & 1) * 2 + 0] = pack_f16(p0, p1);
+          pf[n >> 1][(n & 1) * 2 + 1] = pack_f16(p2, p3);
+          l2_lo = f2_fma(f2_pack(p0, p1), one2, l2_lo);
+          l2_hi = f2_fma(f2_pack(p2, p3), one2, l2_hi);
+        }
+      } else {
 #pragma unroll
       for (int n = 0; n < KT / 8; ++n) {
         if ((WALSH_ATTN_POLY_PAIRS >> n) & 1) {
@@ -597,16 +618,30 @@ attn_head_kernel(const __half* __restrict__ q, const __half* __restrict__ kc, co
           pf[n >> 1][(n & 1) * 2 + 1] = ex2_f16x2(pack_f16(s[n][2], s[n][3]));
         }
       }
+      }
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk) {
         uint32_t vf[4];
         ldsm_x4_t(vf, Vs + v_lane + (k0 + kk * 16) * 32);
         mma_f16(oacc[0], pf[kk], vf[0], vf[1]);
         mma_f16(oacc[1], pf[kk], vf[2], vf[3]);
-        mma_f16(oacc[HD / 8], pf[kk], 0x3C003C00u, 0x3C003C00u);  // row sums of P
+        if (!F32P) mma_f16(oacc[HD / 8], pf[kk], 0x3C003C00u, 0x3C003C00u);  // row sums of P
       }
     }
-    const float inv_lo = 1.0f / oacc[HD / 8][0], inv_hi = 1.0f / oacc[HD / 8][2];
+    float l_lo, l_hi;
+    if (F32P) {  // the quad's four threads hold the row's column pairs
+      l_lo = __uint_as_float((uint32_t)l2_lo) + __uint_as_float((uint32_t)(l2_lo >> 32));
+      l_hi = __uint_as_float((uint32_t)l2_hi) + __uint_as_float((uint32_t)(l2_hi >> 32));
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
+        l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
+      }
+    } else {
+      l_lo = oacc[HD / 8][0];
+      l_hi = oacc[HD / 8][2];
+    }
+    const float inv_lo = 1.0f / l_lo, inv_hi = 1.0f / l_hi;
 #pragma unroll
     for (int j = 0; j < HD / 8; ++j) {
       const int d = j * 8 + 2 * t4;
@@ -634,10 +669,13 @@ static int launch_attn(const void* q, const void* kc, const void* vc, int B, int
     const int kend = start_pos + Tq;
     if (Tq > 4 && aligned && kend <= kAttnHeadMaxKeys && H <= 65535 && B <= 65535) {
       const int smem = 2 * ((kend + 63) / 64 * 64) * HD * (int)sizeof(__half);
+      // f32 exponentials + FMA-pipe row sums: 361 us at B64 x H32 x T1024
+      // against 382 us for the paired fp16 form with the all-ones MMA column
+      auto* kern = attn_head_kernel<true>;
       if (smem > 48 * 1024 &&
-          cudaFuncSetAttribute(attn_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return launch_status();
-      attn_head_kernel<<<dim3(H, B), 256, smem, s>>>((const __half*)q, (const __half*)kc, (const __half*)vc, H, Tq,
+      kern<<<dim3(H, B), 256, smem, s>>>((const __half*)q, (const __half*)kc, (const __half*)vc, H, Tq,
                                                      ctx, start_pos, scale_log2, (__half*)o);
       return launch_status();
     }

@@ -507,12 +507,16 @@ struct EpiPost {
 // layer), logits = silu(h) W2^T with W2 staged in shared memory as float
 // ([hidden][expert], one broadcast 16-byte load per 4 experts), softmax,
 // top-k (ties to the lower expert index) and the routing weights
-// renormalised over the selected experts in ascending order.
+// renormalised over the selected experts in ascending order.  Both epilogue
+// warps of a tensor-memory lane quarter work on a row: the second takes
+// hidden units 64..127 and hands its 16 partial logits to the first through
+// shared memory (double-buffered by tile parity, one named barrier per
+// quarter and tile), which adds them to its own over 0..63 and finishes.
 template <typename TU>
 struct EpiRouter {
   static constexpr int kWarpScratch = 0, kRowEpilogue = 1, kHalfRow = 0;
   static constexpr int E = 16, HID = 128;
-  static constexpr int kRowScratch = E * HID * 4;
+  static constexpr int kRowScratch = E * HID * 4 + 2 * 128 * E * 4;  // W2 + partial-logit exchange
   const TU* w2;  // [E][HID]
   int top_k;
   uint8_t* mask;
@@ -526,12 +530,15 @@ struct EpiRouter {
       ws[j * E + e] = to_f(w2[i]);
     }
   }
-  __device__ __forceinline__ void row(int64_t m, uint32_t tacc, const float* ws, int64_t M) const {
+  // tacc: column 0 of this row's accumulator; half: which 64 hidden units;
+  // r: the row within the tile (lane quarter x 32 + lane); par: tile parity
+  __device__ __forceinline__ void row(int64_t m, uint32_t tacc, int half, int r, int par, float* ws,
+                                      int64_t M) const {
     float l[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) l[e] = 0.f;
 #pragma unroll 1
-    for (int c = 0; c < HID; c += 32) {
+    for (int c = half * (HID / 2); c < (half + 1) * (HID / 2); c += 32) {
       float v[32];
       tc05::tmem_ld32(tacc + (uint32_t)c, v);
 #pragma unroll 4
@@ -547,6 +554,21 @@ struct EpiRouter {
           l[4 * q + 3] = fmaf(h, w.w, l[4 * q + 3]);
         }
       }
+    }
+    float4* xg = reinterpret_cast<float4*>(ws + E * HID + (par * 128 + r) * E);
+    if (half) {
+#pragma unroll
+      for (int q = 0; q < E / 4; ++q) xg[q] = make_float4(l[4 * q], l[4 * q + 1], l[4 * q + 2], l[4 * q + 3]);
+    }
+    asm volatile("bar.sync %0, 64;\n" ::"r"(2 + (r >> 5)) : "memory");  // the quarter's two warps
+    if (half) return;
+#pragma unroll
+    for (int q = 0; q < E / 4; ++q) {
+      const float4 o = xg[q];
+      l[4 * q] += o.x;
+      l[4 * q + 1] += o.y;
+      l[4 * q + 2] += o.z;
+      l[4 * q + 3] += o.w;
     }
     if (m >= M) return;
     float mx = -CUDART_INF_F;
@@ -885,8 +907,8 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       const int64_t m = (t / ntl) * BM + q * 32 + lane, n0 = (t % ntl) * BN + half * (BN / 2);
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * ACC_COLS + half * (BN / 2));
       bool done = false;
-      if constexpr (Epi::kRowEpilogue > 0) {
-        if (half == 0) epi.row(m, base, rowscr, M);  // N <= BN / 2: the other half holds no columns
+      if constexpr (Epi::kRowEpilogue > 0) {  // N <= BN / 2: both halves split the first 128 columns
+        epi.row(m, base - (uint32_t)(half * (BN / 2)), half, q * 32 + lane, i & 1, rowscr, M);
         done = true;
       }
       if constexpr (Epi::kHalfRow > 0) {
