@@ -43,7 +43,7 @@ METRIC = "Walsh-512 prefill tokens/s"
 UNIT = "tokens/s"
 CPU_SAMPLE = (1, 1024)  # oracle sample per step: B1 x T1024
 DECODE_BATCH, DECODE_CTX = 256, 1024
-ATTN_TRAFFIC_B64 = 250.10e6  # ncu DRAM bytes of one prefill attention launch at B64 x T1024
+ATTN_TRAFFIC_B64 = 246.10e6  # ncu DRAM bytes of one prefill attention launch at B64 x T1024
 
 
 def max_over_ranks(value: float, dist, device) -> float:
@@ -698,7 +698,7 @@ def dominant_kernel_roofline(model, idx, B, T, dev):
     hbm, tflops, src = peaks()
     achieved = flops / sec / 1e12
     # DRAM bytes read + written by one launch of this kernel at B64 x T1024, from one ncu
-    # capture (dram__bytes_read.sum 201.34 MB + dram__bytes_write.sum 48.76 MB)
+    # capture (dram__bytes_read.sum 201.34 MB + dram__bytes_write.sum 44.76 MB)
     traffic = ATTN_TRAFFIC_B64 * B / 64 if T == SEQ else None
     return {"kernel": "walsh_attn_fwd (prefill, causal, hd16, fp16)", "bound": "tensor", "achieved": achieved,
             "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops, "traffic": traffic,
