@@ -330,6 +330,27 @@ def test_channel_modulation_long_segments_vs_oracle():
     assert rel(y, O.channel_mod(x.astype(np.float64), w0, w2, np.array([0.25]))) < 1e-5
 
 
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_chmod_16bit_rows_in_place_match_fp32(dt):
+    """16-bit rows at C = 512 (the vectorised stats and apply kernels, several
+    rows per warp) against the fp32 kernels on the same values, in place as the
+    block runs it (out aliases x), with the norm weight and the input added."""
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model.moe import HadamardChannelModulation
+    rng = np.random.default_rng(12)
+    m = HadamardChannelModulation(512).to(DEV)
+    w1, w2c, gam, temp = m.kernel_args()
+    nseg, seg = 64, 1024
+    x = T(rng.normal(size=(nseg * seg, 512)).astype(np.float32), dt)
+    nw = T(rng.uniform(0.5, 1.5, size=512).astype(np.float32))
+    ref, s_ref, h_ref = ops.chmod(x.float(), seg, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True)
+    y = x.clone()
+    _, sc, sh = ops.chmod(y, seg, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True, out=y)
+    assert rel(sc, s_ref.cpu().numpy()) < 1e-4
+    assert rel(sh, h_ref.cpu().numpy()) < 1e-4
+    assert rel(y, ref.cpu().numpy()) < (2e-3 if dt == torch.float16 else 1.6e-2)
+
+
 # ---------------------------------------------------------------------------
 # whole model
 # ---------------------------------------------------------------------------
