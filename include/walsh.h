@@ -410,6 +410,20 @@ walsh_status walsh_chmod_mlp(const float* partial, int nseg, int seg_len, int C,
                              const float* gammas, const float* scale_temp, float* scale,
                              float* shift, void* stream);
 
+/* walsh_chmod_mlp with the first layer on the tensor cores, for large
+ * segment counts (batched decode has one segment per stream row): the fp32
+ * segment means are split into three bf16 rows (hi + mid + lo = the mean to
+ * fp32 precision), one GEMM against W1 as dense bf16 [C/4, C] (the ternary
+ * values, exact in bf16; g1 is applied after the three fp32 results are
+ * added), then layer 2 as in walsh_chmod_mlp.  scratch: a device buffer of
+ * walsh_chmod_mlp_tc_scratch_bytes(nseg, C) bytes, 16-byte aligned.
+ * C % 64 == 0.  Replaces the same lines of src/model/moe.py as
+ * walsh_chmod_mlp. */
+int64_t walsh_chmod_mlp_tc_scratch_bytes(int nseg, int C);
+walsh_status walsh_chmod_mlp_tc(const float* partial, int nseg, int seg_len, int C, const void* w1_bf16,
+                                const uint8_t* w2_2bit, const float* gammas, const float* scale_temp,
+                                void* scratch, float* scale, float* shift, void* stream);
+
 /* out = [x +] xn + r (xn * scale_b + 0.1 shift_b - xn) per 32-wide block b,
  * r = residual_scale (0.5 in mHCLlamaBlock),
  * with xn the RMSNorm'd row (xn = x when norm_w is NULL) and (scale, shift)

@@ -351,6 +351,48 @@ def test_chmod_16bit_rows_in_place_match_fp32(dt):
     assert rel(y, ref.cpu().numpy()) < (2e-3 if dt == torch.float16 else 1.6e-2)
 
 
+@pytest.mark.parametrize("C,nseg,seg_len,dt", [(512, 1024, 1, torch.float16), (2048, 1024, 1, torch.float16),
+                                              (512, 600, 70, torch.bfloat16), (2048, 512, 3, torch.float32)])
+def test_chmod_tensor_core_mlp_matches_cuda_core_mlp(C, nseg, seg_len, dt):
+    """Modulation MLP with its first layer as a tensor-core GEMM over the
+    three-way bf16 split of the segment means (walsh_chmod_mlp_tc) against
+    the CUDA-core kernel (walsh_chmod_mlp) on the same stats: scale and shift
+    to fp32 rounding, and the applied rows; decode-shaped (one row per
+    segment) and multi-row segments with a ragged last stats chunk."""
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model.moe import HadamardChannelModulation
+    rng = np.random.default_rng(C + nseg + seg_len)
+    m = HadamardChannelModulation(C).to(DEV)
+    with torch.no_grad():
+        m.context_mlp[0].weight.copy_(torch.from_numpy(rng.normal(size=(C // 4, C)).astype(np.float32)))
+        m.context_mlp[2].weight.copy_(torch.from_numpy(rng.normal(size=(C // 16, C // 4)).astype(np.float32)))
+        m.scale_temp.fill_(0.3)
+    w1, w2c, gam, temp = m.kernel_args()
+    x = T((rng.normal(size=(nseg * seg_len, C)) * 3).astype(np.float32), dt)
+    nw = T(rng.uniform(0.5, 1.5, size=C).astype(np.float32))
+    y0, s0, h0 = ops.chmod(x, seg_len, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True)
+    y1, s1, h1 = ops.chmod(x, seg_len, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True,
+                           w1_dense=m.w1_dense())
+    # float64 MLP on the same segment means (RMSNorm'd rows x norm weight, averaged)
+    xf = x.double().cpu().numpy().reshape(nseg, seg_len, C)
+    xn = xf / np.sqrt((xf * xf).mean(-1, keepdims=True) + 1e-6) * nw.double().cpu().numpy()
+    bulk = xn.mean(1)
+    t1 = ops.unpack(w1, C).double().cpu().numpy()
+    t2 = ops.unpack(w2c, C // 4).double().cpu().numpy()
+    g = gam.double().cpu().numpy()
+    a1 = bulk @ t1.T * g[0]
+    a2 = (a1 / (1 + np.exp(-a1))) @ t2.T * g[1]
+    E = C // 32
+    s_ref, h_ref = 1 + 0.3 * np.tanh(a2[:, :E]), a2[:, E:]
+    for got, want, cuda_core in ((s1, s_ref, s0), (h1, h_ref, h0)):
+        # fp32 rounding of the two K = C sums (unit-variance test weights): the
+        # tensor-core path is as close to float64 as the CUDA-core path
+        err_tc, err_cc = rel(got, want), rel(cuda_core, want)
+        assert err_tc < max(2 * err_cc, 1e-5), (err_tc, err_cc)
+    tol = {torch.float32: 1e-4, torch.float16: 2e-3, torch.bfloat16: 1.6e-2}[dt]  # a few output ulps
+    assert rel(y1, y0.float().cpu().numpy()) < tol
+
+
 # ---------------------------------------------------------------------------
 # whole model
 # ---------------------------------------------------------------------------

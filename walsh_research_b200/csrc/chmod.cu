@@ -8,6 +8,7 @@
 //          reduction order is fixed;
 //   mlp:   bulk mean -> scaled-ternary MLP -> per-(segment, block) scale/shift;
 //   apply: out = x + xn + 0.5 * (xn * scale + 0.1 * shift - xn).
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -165,6 +166,43 @@ chmod_apply_vec_kernel(const T* x, int64_t nrows, int seg_len, const float* __re
   }
 }
 
+// Second MLP layer for SPB segments whose hidden activations hid [SPB][C/4]
+// are in shared memory: m = g2 W2q h, scale = 1 + clamp(scale_temp) tanh(m[:E]),
+// shift = m[E:] (all 256 threads; sums in byte order of the packed rows).
+template <int SPB>
+__device__ __forceinline__ void chmod_layer2(const float* hid, int ns, int seg0, int C,
+                                             const uint8_t* __restrict__ w2, float g2,
+                                             const float* __restrict__ scale_temp, float* __restrict__ scale,
+                                             float* __restrict__ shift) {
+  const int HIDN = C / 4, E = C / 32;
+  const float st = fminf(fmaxf(__ldg(scale_temp), 0.1f), 0.5f);
+  const int kb2 = HIDN / 4;
+  for (int r = threadIdx.x; r < 2 * E; r += 256) {
+    const uint8_t* row = w2 + (size_t)r * kb2;
+    float acc[SPB];
+#pragma unroll
+    for (int z = 0; z < SPB; ++z) acc[z] = 0.f;
+#pragma unroll 8
+    for (int b = 0; b < kb2; ++b) {
+      const uint32_t byte = __ldg(row + b);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float w = tern_val(byte, q);
+#pragma unroll
+        for (int z = 0; z < SPB; ++z) acc[z] = fmaf(w, hid[z * HIDN + 4 * b + q], acc[z]);
+      }
+    }
+#pragma unroll
+    for (int z = 0; z < SPB; ++z) {
+      if (z >= ns) break;
+      const float a = acc[z] * g2;
+      const size_t seg = (size_t)(seg0 + z);
+      if (r < E) scale[seg * E + r] = 1.0f + st * tanhf(a);
+      else shift[seg * E + (r - E)] = a;
+    }
+  }
+}
+
 // SPB segments per CTA: the packed weights are read once per CTA and every
 // weight is applied to SPB segments' activations (register-blocked); each
 // segment's sums keep the single-segment order, so results do not depend
@@ -235,32 +273,61 @@ chmod_mlp_kernel(const float* __restrict__ partial, int nseg, int nch, int seg_l
     }
   }
   __syncthreads();
-  const float st = fminf(fmaxf(__ldg(scale_temp), 0.1f), 0.5f);
-  const int kb2 = HIDN / 4;
-  for (int r = threadIdx.x; r < 2 * E; r += 256) {
-    const uint8_t* row = w2 + (size_t)r * kb2;
-    float acc[SPB];
-#pragma unroll
-    for (int z = 0; z < SPB; ++z) acc[z] = 0.f;
-#pragma unroll 8
-    for (int b = 0; b < kb2; ++b) {
-      const uint32_t byte = __ldg(row + b);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float w = tern_val(byte, q);
-#pragma unroll
-        for (int z = 0; z < SPB; ++z) acc[z] = fmaf(w, hid[z * HIDN + 4 * b + q], acc[z]);
-      }
-    }
-#pragma unroll
-    for (int z = 0; z < SPB; ++z) {
-      if (z >= ns) break;
-      const float a = acc[z] * g2;
-      const size_t seg = (size_t)(seg0 + z);
-      if (r < E) scale[seg * E + r] = 1.0f + st * tanhf(a);
-      else shift[seg * E + (r - E)] = a;
-    }
+  chmod_layer2<SPB>(hid, ns, seg0, C, w2, g2, scale_temp, scale, shift);
+}
+
+// Tensor-core form of the MLP's first layer for large segment counts
+// (batched decode: one segment per stream row).  The fp32 segment means are
+// split into three bf16 rows (hi, mid, lo: hi + mid + lo = bulk to fp32
+// precision, with bf16's exponent range), all 3 nseg rows go through one
+// GEMM against W1 as dense bf16 (ternary values are exact), and layer 2 sums
+// the three fp32 results before the SiLU.
+int gemm_bf16_f32out(const __nv_bfloat16* a, int64_t M, int K, const __nv_bfloat16* w, int64_t N, float* y,
+                     cudaStream_t s);  // octonion.cu
+
+__global__ void chmod_bulk_split_kernel(const float* __restrict__ partial, int nseg, int nch, int seg_len, int C,
+                                        __nv_bfloat16* __restrict__ a) {
+  const int64_t total = (int64_t)nseg * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t seg = i / C;
+    const int c = (int)(i - seg * C);
+    float sum = 0.f;
+    for (int k = 0; k < nch; ++k) sum += partial[((size_t)seg * nch + k) * C + c];
+    const float b = sum / (float)seg_len;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(b);
+    const float r1 = b - __bfloat162float(hi);
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+    a[i] = hi;
+    a[total + i] = mid;
+    a[2 * total + i] = lo;
   }
+}
+
+template <int SPB>
+__global__ void __launch_bounds__(256)
+chmod_mlp2_kernel(const float* __restrict__ h1, int nseg, int C, const uint8_t* __restrict__ w2,
+                  const float* __restrict__ gammas, const float* __restrict__ scale_temp, float* __restrict__ scale,
+                  float* __restrict__ shift) {
+  extern __shared__ float4 smem4[];
+  float* hid = reinterpret_cast<float*>(smem4);  // [SPB][C/4]
+  const int seg0 = blockIdx.x * SPB;
+  const int ns = min(SPB, nseg - seg0);
+  const int HIDN = C / 4;
+  const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
+  const size_t plane = (size_t)nseg * HIDN;
+  for (int i = threadIdx.x; i < SPB * HIDN; i += 256) {
+    const int z = i / HIDN, j = i - z * HIDN;
+    float v = 0.f;
+    if (z < ns) {
+      const size_t o = (size_t)(seg0 + z) * HIDN + j;
+      v = (h1[o] + h1[plane + o]) + h1[2 * plane + o];
+    }
+    const float a = v * g1;
+    hid[i] = a / (1.0f + expf(-a));
+  }
+  __syncthreads();
+  chmod_layer2<SPB>(hid, ns, seg0, C, w2, g2, scale_temp, scale, shift);
 }
 
 // Warp per row.
@@ -349,6 +416,48 @@ extern "C" walsh_status walsh_chmod_mlp(const float* partial, int nseg, int seg_
     case 4: return go(chmod_mlp_kernel<4>);
     case 2: return go(chmod_mlp_kernel<2>);
     default: return go(chmod_mlp_kernel<1>);
+  }
+}
+
+extern "C" int64_t walsh_chmod_mlp_tc_scratch_bytes(int nseg, int C) {
+  return ((int64_t)3 * nseg * C * 2 + 255) / 256 * 256 + (int64_t)3 * nseg * (C / 4) * 4;
+}
+
+extern "C" walsh_status walsh_chmod_mlp_tc(const float* partial, int nseg, int seg_len, int C, const void* w1_bf16,
+                                           const uint8_t* w2_2bit, const float* gammas, const float* scale_temp,
+                                           void* scratch, float* scale, float* shift, void* stream) {
+  if (int e = injected("chmod_mlp_tc")) return e;
+  WALSH_CHECK_ARG(partial && w1_bf16 && w2_2bit && gammas && scale_temp && scratch && scale && shift);
+  WALSH_CHECK_SHAPE(nseg > 0 && seg_len > 0 && C > 0 && C % 64 == 0 && C <= 8192 &&
+                    (int64_t)3 * nseg <= 2147483647LL);
+  if ((((uintptr_t)w1_bf16) | ((uintptr_t)scratch)) & 15u) return WALSH_ERR_ALIGN;
+  const int nch = (seg_len + kChunkRows - 1) / kChunkRows;
+  cudaStream_t s = (cudaStream_t)stream;
+  __nv_bfloat16* a = reinterpret_cast<__nv_bfloat16*>(scratch);
+  float* h1 = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) +
+                                       ((int64_t)3 * nseg * C * 2 + 255) / 256 * 256);
+  const int64_t total = (int64_t)nseg * C;
+  const unsigned sgrid = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  chmod_bulk_split_kernel<<<sgrid, 256, 0, s>>>(partial, nseg, nch, seg_len, C, a);
+  if (int e = launch_status()) return e;
+  if (int e = gemm_bf16_f32out(a, (int64_t)3 * nseg, C, reinterpret_cast<const __nv_bfloat16*>(w1_bf16), C / 4,
+                               h1, s))
+    return e;
+  const int spb = nseg >= 148 * 8 ? 8 : nseg >= 148 * 4 ? 4 : nseg >= 148 * 2 ? 2 : 1;
+  const size_t smem = (size_t)spb * (C / 4) * sizeof(float);
+  const unsigned grid = (unsigned)((nseg + spb - 1) / spb);
+  auto go = [&](auto kernel) -> int {
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return launch_status();
+    kernel<<<grid, 256, smem, s>>>(h1, nseg, C, w2_2bit, gammas, scale_temp, scale, shift);
+    return launch_status();
+  };
+  switch (spb) {
+    case 8: return go(chmod_mlp2_kernel<8>);
+    case 4: return go(chmod_mlp2_kernel<4>);
+    case 2: return go(chmod_mlp2_kernel<2>);
+    default: return go(chmod_mlp2_kernel<1>);
   }
 }
 

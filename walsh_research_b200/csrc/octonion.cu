@@ -273,6 +273,27 @@ struct EpiQkv {
   }
 };
 
+// fp32 accumulator rows stored unscaled: y [M, N] float (N % 16 == 0, rows
+// 16-byte aligned; the caller checks)
+struct EpiStoreF32 {
+  float* y;
+  int64_t N;
+  __device__ __forceinline__ void operator()(int64_t m, int64_t n, float v0, float v1) const {
+    *reinterpret_cast<float2*>(y + m * N + n) = make_float2(v0, v1);
+  }
+  __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
+    float4* d = reinterpret_cast<float4*>(y + m * N + n);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) d[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  __device__ __forceinline__ void chunk32(int64_t m, int64_t n, const float* v) const {
+    chunk16(m, n, v);
+    chunk16(m, n + 16, v + 16);
+  }
+  __host__ bool vec_ok() const { return N % 16 == 0 && (((uintptr_t)y) & 15u) == 0; }
+  static constexpr int kWarpScratch = 0, kRowEpilogue = 0, kHalfRow = 0;
+};
+
 template <typename TY>
 struct EpiSwiglu {
   const float* scale;  // [2 hidden], interleaved like the weight rows
@@ -1008,6 +1029,14 @@ static int launch_octo(const void* a, int64_t M, int K, const void* whi, const v
   dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
   kern<<<grid, NT, smem, s>>>((const TA*)a, M, K, (const TE<TA>*)whi, (const TE<TA>*)wlo, N, epi);
   return launch_status();
+}
+
+// y [M, N] float = a [M, K] w^T (bf16 a and w), on the tcgen05 kernel when it
+// applies, else the mma.sync kernel.  Internal: the channel-modulation MLP's
+// first layer (its fp32 input split into bf16 hi, mid and lo rows).
+int gemm_bf16_f32out(const __nv_bfloat16* a, int64_t M, int K, const __nv_bfloat16* w, int64_t N, float* y,
+                     cudaStream_t s) {
+  return launch_octo<__nv_bfloat16>(a, M, K, w, nullptr, N, octo::EpiStoreF32{y, N}, s);
 }
 
 // Shared argument checks: x dtype selects the weight dtype (fp16 W for fp16

@@ -174,10 +174,11 @@ class mHCLlamaBlock(nn.Module):
         # channel modulation over the [B*n, T, C] reinterpretation of x
         if self.use_channel_mod:
             w1, w2c, gam, temp = self.channel_mod.kernel_args()
+            w1d = self.channel_mod.w1_dense() if B * n >= ops.CHMOD_MLP_TC_FROM else None
             _, scale, shift = ops.chmod(x.view(B * T * n, C), T, w1, w2c, gam, temp,
                                         norm_w=self._w(self.channel_mod_norm.weight),
                                         norm_eps=self.channel_mod_norm.eps, add_input=True, out=x.view(B * T * n, C),
-                                        residual_scale=self.channel_mod.residual_scale)
+                                        residual_scale=self.channel_mod.residual_scale, w1_dense=w1d)
             self.channel_mod._last_scale, self.channel_mod._last_shift = scale, shift
         return x
 

@@ -245,6 +245,14 @@ class HadamardChannelModulation(nn.Module):
         w1, w2, gam = self.packed()
         return w1, w2, gam, self.scale_temp.detach().float().contiguous()
 
+    def w1_dense(self):
+        """W1's ternary values as dense bfloat16 [C/4, C] (exact), for the
+        tensor-core first layer of the modulation MLP."""
+        def build():
+            w1, _, _ = self.packed()
+            return ops.unpack(w1, self.context_mlp[0].weight.shape[1]).to(torch.bfloat16).contiguous()
+        return _prep.cached(self, "w1_dense", [self.context_mlp[0].weight], build)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, C = x.shape
         w1, w2, gam, temp = self.kernel_args()

@@ -238,9 +238,16 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
     return (out, mask, probs, weights) if want_stats else out
 
 
+# from this many segments (batched decode: one per stream row) the
+# channel-modulation MLP's first layer runs as a tensor-core GEMM
+CHMOD_MLP_TC_FROM = 512
+
+
 def chmod(x, seg_len, w1_p, w2_p, gammas, scale_temp, norm_w=None, norm_eps=1e-6, add_input=True, out=None,
-          residual_scale=0.5):
-    """Channel modulation over rows of x viewed as [nseg, seg_len, C]."""
+          residual_scale=0.5, w1_dense=None):
+    """Channel modulation over rows of x viewed as [nseg, seg_len, C].
+    ``w1_dense``: W1 as dense bfloat16 [C/4, C] (the ternary values), enabling
+    the tensor-core first layer from CHMOD_MLP_TC_FROM segments."""
     require_cuda(x)
     x = _c(x)
     C = x.shape[-1]
@@ -256,8 +263,14 @@ def chmod(x, seg_len, w1_p, w2_p, gammas, scale_temp, norm_w=None, norm_eps=1e-6
     E = C // 32
     scale = torch.empty((nseg, E), dtype=torch.float32, device=x.device)
     shift = torch.empty((nseg, E), dtype=torch.float32, device=x.device)
-    call("walsh_chmod_mlp", ptr(partial), nseg, int(seg_len), C, ptr(w1_p), ptr(w2_p), ptr(gammas),
-         ptr(scale_temp), ptr(scale), ptr(shift), stream())
+    if w1_dense is not None and nseg >= CHMOD_MLP_TC_FROM and C % 64 == 0:
+        nbytes = call("walsh_chmod_mlp_tc_scratch_bytes", nseg, C)
+        scratch = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        call("walsh_chmod_mlp_tc", ptr(partial), nseg, int(seg_len), C, ptr(w1_dense), ptr(w2_p), ptr(gammas),
+             ptr(scale_temp), ptr(scratch), ptr(scale), ptr(shift), stream())
+    else:
+        call("walsh_chmod_mlp", ptr(partial), nseg, int(seg_len), C, ptr(w1_p), ptr(w2_p), ptr(gammas),
+             ptr(scale_temp), ptr(scale), ptr(shift), stream())
     out = out if out is not None else torch.empty_like(x)
     call("walsh_chmod_apply", ptr(x), dcode(x.dtype), nrows, C, int(seg_len), ptr(norm_w), float(norm_eps),
          ptr(scale), ptr(shift), float(residual_scale), 1 if add_input else 0, ptr(out), stream())
