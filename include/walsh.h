@@ -476,6 +476,17 @@ walsh_status walsh_linear_fwd(const void* x, int x_dtype, int64_t M, int K, int6
                               const void* w, int w_dtype, int64_t N, const float* bias, void* y,
                               int y_dtype, void* stream);
 
+/* walsh_linear_split_fwd for float32 x without bias on the 5th-generation
+ * tensor cores: the three split products as one GEMM with K tripled,
+ * [x_hi | x_hi | x_lo] w3^T with w3 [N, 3K] bfloat16 = [w_hi | w_lo | w_hi]
+ * (rows 16-byte aligned: K % 8 == 0), fp32 accumulation, y float32 [M, N]
+ * (any N).  scratch: walsh_linear_split_tc_scratch_bytes(M, K) bytes,
+ * 16-byte aligned.  Same role as walsh_linear_split_fwd for the tied output
+ * projection (src/model/mhc.py:654-676). */
+int64_t walsh_linear_split_tc_scratch_bytes(int64_t M, int K);
+walsh_status walsh_linear_split_tc_fwd(const float* x, int64_t M, int K, const void* w3, int64_t N,
+                                       void* scratch, float* y, void* stream);
+
 /* y[m, n] = sum_k x[m*ldx + k] w[n, k] + bias[n] in float32 on the tensor
  * cores, with w given as two bfloat16 matrices w_hi + w_lo (w_hi = bf16(w),
  * w_lo = bf16(w - w_hi)); a float32 or float16 x is split the same way, a

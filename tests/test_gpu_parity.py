@@ -393,6 +393,21 @@ def test_chmod_tensor_core_mlp_matches_cuda_core_mlp(C, nseg, seg_len, dt):
     assert rel(y1, y0.float().cpu().numpy()) < tol
 
 
+@pytest.mark.parametrize("M,K,N", [(256, 512, 50257), (5, 2048, 1000), (300, 64, 40)])
+def test_linear_split_tc_matches_float64_like_linear_split(M, K, N):
+    """The split-bf16 float32 GEMM on tcgen05 (one GEMM with K tripled; odd N,
+    ragged tiles) against float64, as accurate as the mma.sync split kernel."""
+    from walsh_research_b200 import ops
+    rng = np.random.default_rng(M + K + N)
+    x = rng.normal(size=(M, K)).astype(np.float32)
+    w = (rng.normal(size=(N, K)) * 0.02).astype(np.float32)
+    ref = x.astype(np.float64) @ w.astype(np.float64).T
+    y_tc = ops.linear_split_tc(T(x), ops.split3_weights(T(w)))
+    y_mma = ops.linear_split(T(x), *ops.split_bf16(T(w)))
+    err_tc, err_mma = rel(y_tc, ref), rel(y_mma, ref)
+    assert err_tc < max(2 * err_mma, 1e-5), (err_tc, err_mma)
+
+
 # ---------------------------------------------------------------------------
 # whole model
 # ---------------------------------------------------------------------------

@@ -58,6 +58,8 @@ SIGNATURES = {
     "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],
     "walsh_chmod_apply": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, c_float, c_int, P, P],
     "walsh_chmod_mlp_tc": [P, c_int, c_int, c_int, P, P, P, P, P, P, P, P],
+    "walsh_linear_split_tc_fwd": [P, c_int64, c_int, P, c_int64, P, P, P],
+    "walsh_linear_split_tc_scratch_bytes": [c_int64, c_int],
     "walsh_chmod_mlp_tc_scratch_bytes": [c_int, c_int],
     "walsh_chmod_fwd_noalloc": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, P, P, c_float, c_int, P, P],
     "walsh_embed_gather": [P, c_int64, P, c_int, c_int64, c_int, P, P, P],
@@ -65,10 +67,12 @@ SIGNATURES = {
     "walsh_linear_split_fwd": [P, c_int, c_int64, c_int, c_int64, P, P, c_int64, P, P, P],
     "walsh_rmsnorm": [P, c_int, c_int64, c_int, P, c_float, P, c_int, P],
 }
-_RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64}
+_RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,
+            "walsh_linear_split_tc_scratch_bytes": ctypes.c_int64}
 # kernels each entry point launches (for the launch accounting reported by bench.py)
 KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_octo_set_mainloop": 0,
                     "walsh_chmod_mlp_tc": 3, "walsh_chmod_mlp_tc_scratch_bytes": 0,
+                    "walsh_linear_split_tc_fwd": 2, "walsh_linear_split_tc_scratch_bytes": 0,
                     "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
                     "walsh_abi_version": 0}
 launch_count = 0

@@ -1,6 +1,7 @@
 // Dense helpers around the layer stack: embedding gather, a tiled
 // y = x W^T + b kernel (stream_merge, tied logits, load-time folding of
 // stream_proj into the embedding table) and the chassis RMSNorm.
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -317,6 +318,49 @@ extern "C" walsh_status walsh_rmsnorm(const void* x, int dtype, int64_t rows, in
   cudaStream_t s = (cudaStream_t)stream;
   return WALSH_DISPATCH_DTYPE(dtype, T, WALSH_DISPATCH_DTYPE(y_dtype, TY,
       (rmsnorm_kernel<T, TY><<<(unsigned)g, 256, 0, s>>>((const T*)x, rows, C, w, eps, (TY*)y), launch_status())));
+}
+
+namespace walsh {
+
+// The same three-product split on the tcgen05 kernel as ONE GEMM with K
+// tripled: [x_hi | x_hi | x_lo] [w_hi | w_lo | w_hi]^T = x_hi w_hi^T +
+// x_hi w_lo^T + x_lo w_hi^T, fp32 accumulation, fp32 store.
+int gemm_bf16_f32out(const __nv_bfloat16* a, int64_t M, int K, const __nv_bfloat16* w, int64_t N, float* y,
+                     cudaStream_t s);  // octonion.cu
+
+__global__ void split3_rows_kernel(const float* __restrict__ x, int64_t M, int K, __nv_bfloat16* __restrict__ a3) {
+  const int64_t total = M * K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / K;
+    const int k = (int)(i - m * K);
+    const float v = x[i];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+    __nv_bfloat16* row = a3 + m * 3 * K;
+    row[k] = hi;
+    row[K + k] = hi;
+    row[2 * K + k] = lo;
+  }
+}
+
+}  // namespace walsh
+
+extern "C" int64_t walsh_linear_split_tc_scratch_bytes(int64_t M, int K) { return (M * 3 * K * 2 + 255) / 256 * 256; }
+
+extern "C" walsh_status walsh_linear_split_tc_fwd(const float* x, int64_t M, int K, const void* w3, int64_t N,
+                                                  void* scratch, float* y, void* stream) {
+  using namespace walsh;
+  if (int e = injected("linear_split_tc_fwd")) return e;
+  WALSH_CHECK_ARG(x && w3 && scratch && y);
+  WALSH_CHECK_SHAPE(M >= 0 && K > 0 && N > 0 && K % 8 == 0 && M <= 2147483647LL && N <= 2147483647LL);
+  if ((((uintptr_t)x) | ((uintptr_t)w3) | ((uintptr_t)scratch)) & 15u) return WALSH_ERR_ALIGN;
+  if (M == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  __nv_bfloat16* a3 = reinterpret_cast<__nv_bfloat16*>(scratch);
+  const unsigned g = (unsigned)std::min<int64_t>((M * K + 255) / 256, 148 * 16);
+  split3_rows_kernel<<<g, 256, 0, s>>>(x, M, K, a3);
+  if (int e = launch_status()) return e;
+  return gemm_bf16_f32out(a3, M, 3 * K, reinterpret_cast<const __nv_bfloat16*>(w3), N, y, s);
 }
 
 extern "C" walsh_status walsh_linear_split_fwd(const void* x, int x_dtype, int64_t M, int K, int64_t ldx,

@@ -273,13 +273,14 @@ struct EpiQkv {
   }
 };
 
-// fp32 accumulator rows stored unscaled: y [M, N] float (N % 16 == 0, rows
-// 16-byte aligned; the caller checks)
+// fp32 accumulator rows stored unscaled: y [M, N] float; any N (the vector
+// path needs N % 16 == 0 and a 16-byte aligned y, else scalar stores)
 struct EpiStoreF32 {
   float* y;
   int64_t N;
   __device__ __forceinline__ void operator()(int64_t m, int64_t n, float v0, float v1) const {
-    *reinterpret_cast<float2*>(y + m * N + n) = make_float2(v0, v1);
+    y[m * N + n] = v0;
+    if (n + 1 < N) y[m * N + n + 1] = v1;
   }
   __device__ __forceinline__ void chunk16(int64_t m, int64_t n, const float* v) const {
     float4* d = reinterpret_cast<float4*>(y + m * N + n);

@@ -277,6 +277,11 @@ class mHCWalsh(nn.Module):
         emb = self.tok_embeddings.weight
         return _prep.cached(self, "emb_split", [emb], lambda: ops.split_bf16(emb))
 
+    def head_weights_split3(self):
+        """The tied output projection as [w_hi | w_lo | w_hi] bf16 [V, 3C] (linear_split_tc)."""
+        emb = self.tok_embeddings.weight
+        return _prep.cached(self, "emb_split3", [emb], lambda: ops.split3_weights(emb))
+
     def merge_weights_split(self):
         W = self.stream_merge.weight
         return _prep.cached(self, "merge_split", [W], lambda: ops.split_bf16(W))
@@ -303,6 +308,9 @@ class mHCWalsh(nn.Module):
 
     def _logits(self, h):
         """h [M, C] float32 -> logits [M, V] float32 against the tied embedding."""
+        if h.dtype == torch.float32 and h.shape[-1] % 8 == 0 and self.compute_dtype != torch.float32:
+            # 16-bit mode: the split products on the tcgen05 tensor cores
+            return ops.linear_split_tc(h, self.head_weights_split3())
         if ops.split_eligible(h, h.shape[-1]):
             return ops.linear_split(h, *self.head_weights_split())
         return ops.linear(h, self.head_weights(), None, out_dtype=torch.float32)

@@ -429,6 +429,27 @@ def split_eligible(x, K, ldx=None) -> bool:
             and (ld * esz) % 16 == 0)
 
 
+def split3_weights(w):
+    """[w_hi | w_lo | w_hi] bfloat16 [N, 3K] for linear_split_tc."""
+    hi, lo = split_bf16(w)
+    return torch.cat([hi, lo, hi], dim=1).contiguous()
+
+
+def linear_split_tc(x, w3):
+    """y = x W^T (float32 x [..., K], float32 y) on the tcgen05 tensor cores,
+    W given as split3_weights(W); the same three split products as
+    linear_split in one GEMM with K tripled."""
+    require_cuda(x, w3)
+    x = _c(x.float())
+    N, K3 = w3.shape
+    K = K3 // 3
+    M = x.numel() // K
+    y = torch.empty(x.shape[:-1] + (N,), dtype=torch.float32, device=x.device)
+    scratch = torch.empty(call("walsh_linear_split_tc_scratch_bytes", M, K), dtype=torch.uint8, device=x.device)
+    call("walsh_linear_split_tc_fwd", ptr(x), M, K, ptr(w3), N, ptr(scratch), ptr(y), stream())
+    return y
+
+
 def linear_split(x, w_hi, w_lo, bias=None, ldx=None, M=None, out=None):
     """y = x W^T + b (float32) with W given as its bf16 split (see split_bf16)."""
     require_cuda(x, w_hi, w_lo)
