@@ -466,8 +466,9 @@ def test_model_bf16_matches_reference():
 
 
 def test_model_bf16_walsh2048():
-    """C = 2048 (64 heads of 32, 64 experts) in 16-bit mode: the CUDA-core
-    q/k/v, MoE and mapping kernels and the hd-32 attention."""
+    """C = 2048 (64 heads of 32, 64 experts) in 16-bit mode: the tcgen05 q/k/v
+    GEMM (hd-32 RoPE epilogue) and folded output GEMM with the site epilogue,
+    the CUDA-core MoE and mapping kernels and the hd-32 attention."""
     _bf16_model_check("model_h2048")
 
 

@@ -174,7 +174,10 @@ class CausalSelfAttention(nn.Module):
         return _prep.cached(self, f"out_dense_{dtype}", ws, build)
 
     def _tc(self, x) -> bool:
-        return self.algebra == "hadamard" and ops.tc_eligible(x, torch.float16) and self.n_embd == 512
+        """16-bit Hadamard attention site on the tcgen05 GEMMs (dense q | k | v with
+        RoPE and the cache write, folded mixer + wo with the site epilogue)."""
+        return (self.algebra == "hadamard" and x.dtype == torch.float16 and self.n_embd in (512, 2048)
+                and self.head_dim % 16 == 0)
 
     def forward_site(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, xs, hmix):
         """Attention plus the mHC site epilogue: xs [B, T, n, C] <- H_res xs + H_post attn(x)."""
@@ -190,8 +193,8 @@ class CausalSelfAttention(nn.Module):
         w, sc = self._qkv_dense(x.dtype)
         ops.octo_qkv(x, H, w, sc, rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
         o = ops.attention(q, k_cache, v_cache, start_pos)
-        if B * T >= ops.MOE_GEMM_ROUTER_BELOW:
-            # prefill-sized: mixer and wo folded into one tcgen05 GEMM with the site epilogue
+        if B * T >= ops.ATTN_OUT_DENSE_FROM:
+            # mixer and wo folded into one tcgen05 GEMM with the site epilogue
             w, sc = self._out_dense(o.dtype)
             return ops.octo_post(o.view(B, T, C), w, sc, xs, hmix, out=xs)
         wmix = bmix = None

@@ -157,6 +157,11 @@ def sinkhorn(h, iters=20, eps=1e-8):
 # below this many tokens (about a wave of 64-token tiles) the MoE runs as a
 # router GEMM plus the warp-per-token kernel instead of the 128-token kernels
 MOE_GEMM_ROUTER_BELOW = 148 * 64
+# from this many tokens the attention output (head mixer and wo folded into
+# one dense matrix) is a tcgen05 GEMM with the mHC site epilogue; below it
+# the mma.sync attn_out_tc kernel.  Measured at B256 decode (Walsh-512): the
+# GEMM form 3.57 ms per step against 3.74 ms, so it applies from one token
+ATTN_OUT_DENSE_FROM = 1
 # prefill-sized C = 512 MoE on the tcgen05 router GEMM + expert kernel (False:
 # the single mma.sync kernel of walsh_moe_fwd; kept for comparisons)
 MOE_TC05 = True
