@@ -558,39 +558,17 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
   }
 }
 
-// ---------------------------------------------------------------------------
-// Decode-sized MoE (a few hundred tokens): router layer 1 is a tcgen05 GEMM
-// done by the caller (hpre = u W1^T, one row per token); this kernel runs one
-// warp per token for the rest: silu, router layer 2 (lane e holds expert e),
-// softmax, top-k (ties to the lower index), renormalisation over the selected
-// experts in ascending order, only the k selected ternary experts (gate/up
-// hidden units 4 per lane, down outputs 1 per lane), and the mHC site
-// epilogue.  Weights stay in L2; per-warp scratch (silu(hpre), the expert
-// hidden activations and the output row) is in shared memory.
-// ---------------------------------------------------------------------------
-template <typename TU, typename TX, int C>
-__global__ void __launch_bounds__(256)
-moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, int top_k,
-                 const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
-                 const uint8_t* __restrict__ dp, const float* __restrict__ gammas, TU* __restrict__ y,
-                 int fuse_post, const TX* x, const float* __restrict__ hmix, TX* xo, uint8_t* __restrict__ mask_out,
-                 float* __restrict__ probs_out, float* __restrict__ weights_out) {
-  constexpr int E = C / 32, HID = C / 4, EH = kExpertHidden, PER = HID + C + EH;
+// Router layer 2 of one token on one warp (hs: silu(hpre) in shared memory,
+// lane e holds expert e), softmax, top-k (ties to the lower index) and the
+// renormalisation over the selected experts in ascending order; every lane
+// gets sel[k] and its routing weight selw[k] = p / sum of the selected p.
+template <int C>
+__device__ __forceinline__ void moe_route_warp(const float* hs, const float* __restrict__ w2, int64_t tok,
+                                               int top_k, int lane, int* sel, float* selw,
+                                               uint8_t* __restrict__ mask_out, float* __restrict__ probs_out,
+                                               float* __restrict__ weights_out) {
+  constexpr int E = C / 32, HID = C / 4;
   constexpr int EL = (E + 31) / 32;  // experts per lane (1 for E = 16, 2 for E = 64)
-  extern __shared__ float4 smem4[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* hs = reinterpret_cast<float*>(smem4) + warp * PER;  // [HID]
-  float* ys = hs + HID;                                        // [C]
-  float* as = ys + C;                                          // [EH]
-  const int64_t tok = (int64_t)blockIdx.x * 8 + warp;
-  if (tok >= ntok) return;  // whole warp
-  // silu of router layer 1
-  for (int j = lane; j < HID; j += 32) {
-    const float v = to_f(hpre[tok * HID + j]);
-    hs[j] = v / (1.0f + expf(-v));
-  }
-  for (int c = lane; c < C; c += 32) ys[c] = 0.f;
-  __syncwarp();
   // router layer 2 and softmax
   float l[EL], p[EL];
 #pragma unroll
@@ -625,7 +603,6 @@ moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t 
   for (int q = 0; q < EL; ++q) p[q] = __fdiv_rn(p[q], sum);
   // top-k by warp arg-max; ties go to the lower expert index
   uint32_t chosen = 0;  // bit q: this lane's expert lane + 32 q
-  int sel[8];
   for (int k = 0; k < top_k; ++k) {
     float bv = -2.f;
     int bi = E;
@@ -669,12 +646,24 @@ moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t 
       if (weights_out) weights_out[tok * E + e] = on ? __fdiv_rn(p[q], wsum) : 0.f;
     }
   }
-  // the selected experts
-  const float gg = __ldg(gammas + 0), gu = __ldg(gammas + 1), gd = __ldg(gammas + 2);
   for (int k = 0; k < top_k; ++k) {
     const int e = sel[k];
     const float pe = __shfl_sync(0xffffffffu, p[e >> 5 < EL ? e >> 5 : 0], e & 31);
-    const float wgt = __fdiv_rn(pe, wsum);
+    selw[k] = __fdiv_rn(pe, wsum);
+  }
+}
+
+// One selected expert of a token on one warp (lane k holds input k of the
+// expert's 32-wide block): gate/up hidden units 4 per lane, SiLU(g) v into
+// the warp's scratch as[EH], down outputs 1 per lane; writes its 32 outputs
+// (scaled by gd and the routing weight wgt) to ys[e * 32 + lane].
+template <typename TU, int C>
+__device__ __forceinline__ void moe_expert_warp(const TU* __restrict__ u, int64_t tok, int e, float wgt,
+                                                const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
+                                                const uint8_t* __restrict__ dp, const float* __restrict__ gammas,
+                                                int lane, float* as, float* ys) {
+  constexpr int EH = kExpertHidden;
+  const float gg = __ldg(gammas + 0), gu = __ldg(gammas + 1), gd = __ldg(gammas + 2);
     const float ub = to_f(u[tok * C + e * 32 + lane]);  // lane k holds input k of the block
     float ga[4] = {0.f, 0.f, 0.f, 0.f}, ua[4] = {0.f, 0.f, 0.f, 0.f};
     uint2 gw[4], uw[4];
@@ -721,6 +710,46 @@ moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t 
         }
     }
     ys[e * 32 + lane] = acc * gd * wgt;
+}
+
+// ---------------------------------------------------------------------------
+// Decode-sized MoE (a few hundred tokens): router layer 1 is a tcgen05 GEMM
+// done by the caller (hpre = u W1^T, one row per token); this kernel runs one
+// warp per token for the rest: silu, router layer 2 (lane e holds expert e),
+// softmax, top-k (ties to the lower index), renormalisation over the selected
+// experts in ascending order, only the k selected ternary experts (gate/up
+// hidden units 4 per lane, down outputs 1 per lane), and the mHC site
+// epilogue.  Weights stay in L2; per-warp scratch (silu(hpre), the expert
+// hidden activations and the output row) is in shared memory.
+// ---------------------------------------------------------------------------
+template <typename TU, typename TX, int C>
+__global__ void __launch_bounds__(256)
+moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, int top_k,
+                 const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
+                 const uint8_t* __restrict__ dp, const float* __restrict__ gammas, TU* __restrict__ y,
+                 int fuse_post, const TX* x, const float* __restrict__ hmix, TX* xo, uint8_t* __restrict__ mask_out,
+                 float* __restrict__ probs_out, float* __restrict__ weights_out) {
+  constexpr int HID = C / 4, EH = kExpertHidden, PER = HID + C + EH;
+  extern __shared__ float4 smem4[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* hs = reinterpret_cast<float*>(smem4) + warp * PER;  // [HID]
+  float* ys = hs + HID;                                        // [C]
+  float* as = ys + C;                                          // [EH]
+  const int64_t tok = (int64_t)blockIdx.x * 8 + warp;
+  if (tok >= ntok) return;  // whole warp
+  // silu of router layer 1
+  for (int j = lane; j < HID; j += 32) {
+    const float v = to_f(hpre[tok * HID + j]);
+    hs[j] = v / (1.0f + expf(-v));
+  }
+  for (int c = lane; c < C; c += 32) ys[c] = 0.f;
+  __syncwarp();
+  int sel[8];
+  float selw[8];
+  moe_route_warp<C>(hs, w2, tok, top_k, lane, sel, selw, mask_out, probs_out, weights_out);
+  // the selected experts
+  for (int k = 0; k < top_k; ++k) {
+    moe_expert_warp<TU, C>(u, tok, sel[k], selw[k], gp, upp, dp, gammas, lane, as, ys);
     __syncwarp();
   }
   // output row, or the mHC site epilogue
@@ -751,11 +780,87 @@ moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t 
   }
 }
 
+// Decode MoE with the selected experts spread over warps: CTA = one token,
+// 8 warps.  Warp 0 routes (moe_route_warp); warp k < top_k then runs the
+// token's k-th selected expert (an expert writes only its own 32-column block
+// of the output row, so no two warps write the same column and the row equals
+// moe_token_kernel's); all 256 threads finish with the output row or the mHC
+// site epilogue, one (8-column chunk, output stream) pair per thread.  The
+// token's latency is the router plus one expert instead of the router plus
+// top_k experts in sequence.
+template <typename TU, typename TX, int C>
+__global__ void __launch_bounds__(256)
+moe_token_split_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, int top_k,
+                       const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
+                       const uint8_t* __restrict__ dp, const float* __restrict__ gammas, TU* __restrict__ y,
+                       int fuse_post, const TX* x, const float* __restrict__ hmix, TX* xo,
+                       uint8_t* __restrict__ mask_out, float* __restrict__ probs_out,
+                       float* __restrict__ weights_out) {
+  constexpr int HID = C / 4, EH = kExpertHidden;
+  extern __shared__ float4 smem4[];
+  float* hs = reinterpret_cast<float*>(smem4);  // [HID]
+  float* ys = hs + HID;                         // [C]
+  float* as = ys + C;                           // [8][EH]
+  __shared__ int s_sel[8];
+  __shared__ float s_w[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tok = blockIdx.x;
+  for (int j = threadIdx.x; j < HID; j += 256) {
+    const float v = to_f(hpre[tok * HID + j]);
+    hs[j] = v / (1.0f + expf(-v));
+  }
+  for (int c = threadIdx.x; c < C; c += 256) ys[c] = 0.f;
+  __syncthreads();
+  if (warp == 0) {
+    int sel[8];
+    float selw[8];
+    moe_route_warp<C>(hs, w2, tok, top_k, lane, sel, selw, mask_out, probs_out, weights_out);
+    if (lane == 0)
+      for (int k = 0; k < top_k; ++k) {
+        s_sel[k] = sel[k];
+        s_w[k] = selw[k];
+      }
+  }
+  __syncthreads();
+  if (warp < top_k) moe_expert_warp<TU, C>(u, tok, s_sel[warp], s_w[warp], gp, upp, dp, gammas, lane, as + warp * EH, ys);
+  __syncthreads();
+  if (!fuse_post) {
+    for (int c = threadIdx.x; c < C; c += 256) y[tok * C + c] = from_f<TU>(ys[c]);
+    return;
+  }
+  const float* hm = hmix + tok * kMapRows;
+  for (int i = threadIdx.x; i < (C / 8) * 4; i += 256) {
+    const int r = i & 3, c = (i >> 2) * 8;
+    const size_t base = (size_t)tok * 4 * C + c;
+    const float h0 = __ldg(hm + 8 + 4 * r), h1 = __ldg(hm + 9 + 4 * r), h2 = __ldg(hm + 10 + 4 * r),
+                h3 = __ldg(hm + 11 + 4 * r), hp = __ldg(hm + 4 + r);
+    float xs[4][8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) load8(x + base + (size_t)j * C, xs[j]);
+    float o[8];
+#pragma unroll
+    for (int e8 = 0; e8 < 8; ++e8)
+      o[e8] = (((h0 * xs[0][e8] + h1 * xs[1][e8]) + h2 * xs[2][e8]) + h3 * xs[3][e8]) + hp * ys[c + e8];
+    store8(xo + base + (size_t)r * C, o);
+  }
+}
+
 template <typename TU, typename TX, int C>
 static int launch_moe_token(const void* u, const void* hpre, int64_t ntok, int top_k, const float* w2,
                             const uint8_t* gp, const uint8_t* upp, const uint8_t* dp, const float* gammas, void* y,
                             int fuse_post, const void* x, const float* hmix, void* xo, uint8_t* mask_out,
                             float* probs_out, float* weights_out, cudaStream_t s) {
+  if (top_k <= 8) {
+    const int smem2 = (C / 4 + C + 8 * kExpertHidden) * (int)sizeof(float);
+    auto k2 = moe_token_split_kernel<TU, TX, C>;
+    if (smem2 > 48 * 1024 &&
+        cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) != cudaSuccess)
+      return launch_status();
+    k2<<<(unsigned)ntok, 256, smem2, s>>>((const TU*)u, (const TU*)hpre, ntok, top_k, w2, gp, upp, dp, gammas,
+                                          (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo, mask_out, probs_out,
+                                          weights_out);
+    return launch_status();
+  }
   constexpr int PER = C / 4 + C + kExpertHidden;
   const int smem = 8 * PER * (int)sizeof(float);
   auto kern = moe_token_kernel<TU, TX, C>;
