@@ -342,11 +342,13 @@ mhc_map_mma_kernel(const TX* __restrict__ x, int64_t ntok, const TX* __restrict_
 //      memory, two tokens per warp.
 // x is read from HBM once (the two-pass kernel reads it twice).
 // ---------------------------------------------------------------------------
-// C = 512: 16 tokens per CTA (64 KB of x); C = 2048: 8 tokens (128 KB; the
-// MMA's rows 8..15 then read the next box and are discarded).
-template <int C>
+// TOKN tokens per CTA: 16 (C = 512, 64 KB of x) or 8 (C = 2048: 128 KB; and
+// C = 512 at small token counts, for twice the CTAs).  With 8 the MMA's rows
+// 8..15 read the next box (the last box: the reduction scratch after it) and
+// are discarded.
+template <int C, int TOKN>
 struct MapTma {
-  static constexpr int TOK = C == 512 ? 16 : 8, NW = 8, D = 4 * C, BOXC = 64, NBOX = D / BOXC;
+  static constexpr int TOK = TOKN, NW = 8, D = 4 * C, BOXC = 64, NBOX = D / BOXC;
   static constexpr int BOX_BYTES = TOK * BOXC * 2;
   static constexpr int X_BYTES = NBOX * BOX_BYTES;
   static constexpr int RED_FLOATS = NW * 16 * (kMapRows + 1);
@@ -360,12 +362,12 @@ struct MapTma {
 
 __device__ int g_map_tma_error;
 
-template <int C, typename TX, typename TU>
+template <int C, typename TX, typename TU, int TOKN>
 __global__ void __launch_bounds__(256)
 mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const uint2* __restrict__ phif,
                    const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
                    TU* __restrict__ u, float* __restrict__ hmix) {
-  using G = MapTma<C>;
+  using G = MapTma<C, TOKN>;
   constexpr int TOK = G::TOK, NW = G::NW, D = G::D, BOXC = G::BOXC, NBOX = G::NBOX, BOX_BYTES = G::BOX_BYTES,
                 X_BYTES = G::X_BYTES, RED_FLOATS = G::RED_FLOATS;
   constexpr int KS = D / 16 / NW;  // k-steps per warp
@@ -586,15 +588,31 @@ static inline int grid_for(int64_t total, int threads) {
 
 using namespace walsh;
 
+template <int C, typename TX, typename TU, int TOKN>
+static int launch_map_tma_n(const void* x, int64_t ntok, const void* phi_frag, const float* mp, float map_eps,
+                            const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s);
+
 // Single-pass TMA kernel launch; 1 = ran, 0 = not applicable, < 0 = error.
 template <int C, typename TX, typename TU>
 static int launch_map_tma(const void* x, int64_t ntok, const void* phi_frag, const float* mp, float map_eps,
                           const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s) {
-  using G = MapTma<C>;
+  // 8 tokens per CTA for C = 2048, and for C = 512 while 16-token CTAs
+  // would not fill the SMs
+  if constexpr (C == 512) {
+    if (ntok > 148 * 16)
+      return launch_map_tma_n<C, TX, TU, 16>(x, ntok, phi_frag, mp, map_eps, norm_w, norm_eps, u, hmix, s);
+  }
+  return launch_map_tma_n<C, TX, TU, 8>(x, ntok, phi_frag, mp, map_eps, norm_w, norm_eps, u, hmix, s);
+}
+
+template <int C, typename TX, typename TU, int TOKN>
+static int launch_map_tma_n(const void* x, int64_t ntok, const void* phi_frag, const float* mp, float map_eps,
+                            const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s) {
+  using G = MapTma<C, TOKN>;
   if (ntok > 2147483647LL) return 0;
   CUtensorMap m;
   if (!make_tile_map(&m, x, std::is_same<TX, __nv_bfloat16>::value, ntok, G::D, G::BOXC, G::TOK)) return 0;
-  auto kern = mhc_map_tma_kernel<C, TX, TU>;
+  auto kern = mhc_map_tma_kernel<C, TX, TU, TOKN>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM) != cudaSuccess)
     return launch_status();
   kern<<<(unsigned)((ntok + G::TOK - 1) / G::TOK), 256, G::SMEM, s>>>(m, ntok, (const uint2*)phi_frag, mp, map_eps,
