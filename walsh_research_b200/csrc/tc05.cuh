@@ -7,7 +7,7 @@
 //    1024-byte aligned; the UMMA shared-memory descriptor of such a tile has
 //    SBO = 1024 B and layout SWIZZLE_128B, and the k-th 16-element step
 //    starts 32 B further (the hardware applies the swizzle to the address);
-//  - one CTA (cta_group::1), no clusters and no multicast;
+//  - one CTA (cta_group::1), no clusters; every TMA load fills only its own CTA;
 //  - every wait on an mbarrier is bounded by a clock budget: on expiry the
 //    waiter reports failure and the kernel records WALSH_ERR_TIMEOUT instead
 //    of spinning forever.
