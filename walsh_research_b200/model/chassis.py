@@ -194,9 +194,13 @@ class CausalSelfAttention(nn.Module):
         ops.octo_qkv(x, H, w, sc, rope_cos, rope_sin, start_pos, q, k_cache, v_cache)
         o = ops.attention(q, k_cache, v_cache, start_pos)
         if B * T >= ops.ATTN_OUT_DENSE_FROM:
-            # mixer and wo folded into one tcgen05 GEMM with the site epilogue
+            # mixer and wo folded into one tcgen05 GEMM, the site update in its
+            # epilogue (or, for few tokens, mhc_post after it)
             w, sc = self._out_dense(o.dtype)
-            return ops.octo_post(o.view(B, T, C), w, sc, xs, hmix, out=xs)
+            if B * T >= ops.ATTN_OUT_FUSED_FROM:
+                return ops.octo_post(o.view(B, T, C), w, sc, xs, hmix, out=xs)
+            f = ops.octo_linear(o.view(B, T, C), w, sc)
+            return ops.mhc_post(xs, f, hmix, out=xs)
         wmix = bmix = None
         if self.head_mixer is not None:
             if hd != 16:

@@ -162,6 +162,12 @@ MOE_GEMM_ROUTER_BELOW = 148 * 64
 # the mma.sync attn_out_tc kernel.  Measured at B256 decode (Walsh-512): the
 # GEMM form 3.57 ms per step against 3.74 ms, so it applies from one token
 ATTN_OUT_DENSE_FROM = 1
+# from this many tokens the site update runs in that GEMM's epilogue; below
+# it the GEMM stores the attention output and mhc_post (spread over all SMs)
+# applies the site update, since a few hundred tokens give the fused GEMM
+# only M/128 x C/256 CTAs (B256 decode: 3.13 ms per step against 3.31 ms
+# fused at Walsh-512, 21.19 against 21.48 ms at Walsh-2048)
+ATTN_OUT_FUSED_FROM = 4096
 # prefill-sized C = 512 MoE on the tcgen05 router GEMM + expert kernel (False:
 # the single mma.sync kernel of walsh_moe_fwd; kept for comparisons)
 MOE_TC05 = True
