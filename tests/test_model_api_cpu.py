@@ -51,3 +51,67 @@ def test_forward_refuses_cpu():
     model = mHCWalsh(wm.WalshConfig(**cfg), n_streams=4)
     with pytest.raises(RuntimeError, match="CUDA"):
         model(torch.zeros(1, 4, dtype=torch.long))
+
+
+def test_cuda_graph_cache_host_logic(monkeypatch):
+    """mHCWalsh's graph cache (enable_cuda_graphs), host side, with fakes for the
+    CUDA graph calls: first call of a shape runs eagerly, the second captures
+    and replays, later calls copy the ids in and replay; another shape or
+    start_pos gets its own entry; an in-place parameter update drops the graph
+    (eager again, then a new capture); disabling releases the graphs."""
+    cfg = dict(cases.MODEL_CASES["model_h512"][0], n_layer=1)
+    model = mHCWalsh(wm.WalshConfig(**cfg), n_streams=4)
+    log = []
+
+    class FakeGraph:
+        def __init__(self):
+            self.id = len([e for e in log if e[0] == "capture"])
+
+        def replay(self):
+            log.append(("replay", self.id))
+
+    class FakeCapture:
+        def __init__(self, g):
+            self.g = g
+
+        def __enter__(self):
+            log.append(("capture", self.g.id))
+
+        def __exit__(self, *a):
+            return False
+
+    def fake_forward(idx, targets, kv_cache, start_pos, return_hidden):
+        log.append(("forward", tuple(idx.shape), start_pos))
+        model._last_index_error = None
+        return torch.zeros(idx.shape[0], 1, 4) + idx.sum().float(), None
+
+    monkeypatch.setattr(torch.cuda, "CUDAGraph", FakeGraph)
+    monkeypatch.setattr(torch.cuda, "graph", FakeCapture)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a, **k: None)
+    monkeypatch.setattr(model, "_forward", fake_forward)
+
+    model.enable_cuda_graphs()
+    a, b = torch.ones(2, 3, dtype=torch.long), torch.full((2, 3), 2, dtype=torch.long)
+    with torch.no_grad():
+        model._graph_forward(a, 0)                     # eager
+        assert log[-1][0] == "forward"
+        model._graph_forward(a, 0)                     # capture (one traced forward) + replay
+        assert [e[0] for e in log[-3:]] == ["capture", "forward", "replay"]
+        n = len(log)
+        out, _ = model._graph_forward(b, 0)            # replay with the new ids copied in
+        assert [e[0] for e in log[n:]] == ["replay"]
+        graphs = model.__dict__["_walsh_graphs"]
+        key = ((2, 3), 0, model._act_dtype(), a.device)
+        assert torch.equal(graphs[key]["idx"], b)
+        model._graph_forward(a, 5)                     # other start_pos: its own entry, eager first
+        assert log[-1] == ("forward", (2, 3), 5)
+        with torch.no_grad():
+            model.output.weight.mul_(2.0)              # parameter change: graph dropped
+        n = len(log)
+        model._graph_forward(a, 0)
+        assert [e[0] for e in log[n:]] == ["forward"]
+        assert key not in graphs
+        model._graph_forward(a, 0)                     # recaptured
+        assert "capture" in [e[0] for e in log[n:]]
+    model.enable_cuda_graphs(False)
+    assert model.__dict__["_walsh_graphs"] == {}
