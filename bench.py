@@ -22,6 +22,7 @@ import argparse
 import json
 import os
 import re
+import select
 import statistics
 import subprocess
 import sys
@@ -125,12 +126,22 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        # a sample every 20 ms; the timed region starts once the first sample
+        # has arrived (at most 5 s of waiting), so the samples fall inside it
+        self.first = []
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={CLOCK_FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+        if self.proc is not None:
+            try:
+                ready, _, _ = select.select([self.proc.stdout], [], [], 5.0)
+                if ready:
+                    self.first = [self.proc.stdout.readline()]
+            except (OSError, ValueError):
+                pass
         return self
 
     def __exit__(self, *a):
@@ -142,7 +153,7 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.lines = [l for l in self.first + out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
