@@ -115,3 +115,22 @@ def test_cuda_graph_cache_host_logic(monkeypatch):
         assert "capture" in [e[0] for e in log[n:]]
     model.enable_cuda_graphs(False)
     assert model.__dict__["_walsh_graphs"] == {}
+
+
+def test_split3_weight_layout_cpu():
+    """Operand B of the tensor-core logits GEMM: [W_hi | W_lo | W_hi] in bf16,
+    hi + lo = W to about 2^-16 relative, so that [x_hi | x_hi | x_lo] against
+    it gives x_hi W_hi + x_hi W_lo + x_lo W_hi."""
+    from walsh_research_b200 import ops
+    w = torch.from_numpy(np.random.default_rng(3).normal(size=(37, 64)).astype(np.float32))
+    w3 = ops.split3_weights(w)
+    assert w3.dtype == torch.bfloat16 and tuple(w3.shape) == (37, 192) and w3.is_contiguous()
+    hi, lo, hi2 = w3[:, :64].float(), w3[:, 64:128].float(), w3[:, 128:].float()
+    assert torch.equal(hi, hi2)
+    assert float(((hi + lo) - w).abs().max() / w.abs().max()) < 2.0 ** -15
+    x = torch.from_numpy(np.random.default_rng(4).normal(size=(5, 64)).astype(np.float32))
+    x_hi = x.to(torch.bfloat16).float()
+    x_lo = (x - x_hi).to(torch.bfloat16).float()
+    y = torch.cat([x_hi, x_hi, x_lo], 1).double() @ w3.double().t()
+    ref = x.double() @ w.double().t()
+    assert float((y - ref).abs().max() / ref.abs().max()) < 1e-4
