@@ -127,8 +127,9 @@ class ClockSampler:
 
     def __enter__(self):
         # a sample every 20 ms; the timed region starts once the first sample
-        # has arrived (at most 5 s of waiting), so the samples fall inside it
-        self.first = []
+        # has arrived (at most 5 s of waiting).  That first sample only signals
+        # that the sampler runs: it was taken before the timed region and is
+        # dropped, so the kept samples fall inside it
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={CLOCK_FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "20"],
@@ -139,7 +140,7 @@ class ClockSampler:
             try:
                 ready, _, _ = select.select([self.proc.stdout], [], [], 5.0)
                 if ready:
-                    self.first = [self.proc.stdout.readline()]
+                    self.proc.stdout.readline()
             except (OSError, ValueError):
                 pass
         return self
@@ -153,7 +154,7 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in self.first + out.splitlines() if l.strip()]
+            self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()

@@ -446,10 +446,13 @@ walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrows, int C, i
  * Limit: round64(nseg*nchunk*C) + 2*round64(nseg*C/32) <= 1,048,576 floats
  * (4 MiB; nchunk = ceil(seg_len / walsh_chmod_chunk_rows), round64 = round up
  * to a multiple of 64), else WALSH_ERR_SCRATCH before any launch.
- * The first call on a device, with that device current, looks up the array's
- * address (set-up); make it before any stream capture.  The array is shared:
- * calls that overlap on the device race and must be ordered by the caller.
- * Nothing in it needs to start at zero. */
+ * The first call in a CUDA context (per device, with that device current)
+ * looks up the array's address (set-up); make it before any stream capture.
+ * The address is cached under the context's process-unique id, so a device
+ * reset, or another context made current on the device, is looked up again
+ * on its first call (also outside capture).  The array is shared: calls that
+ * overlap on the device race and must be ordered by the caller.  Nothing in
+ * it needs to start at zero. */
 walsh_status walsh_chmod_fwd_noalloc(const void* x, int dtype, int64_t nrows, int C, int seg_len,
                                      const float* norm_w, float norm_eps, const uint8_t* w1_2bit,
                                      const uint8_t* w2_2bit, const float* gammas,

@@ -1,12 +1,20 @@
 """walsh_chmod_fwd_noalloc: channel modulation with library-owned scratch.
 
-The allocation-free entry point runs the same three kernels as the
-caller-scratch path (walsh_chmod_stats / _mlp / _apply through ops.chmod),
-so its output must equal that path's bit for bit.  The file is named to be
-collected last: the entry point's per-device set-up must work both in a
-fresh process and after every other test has used the device.
+Some hosts cannot allocate device memory when a layer runs: a runtime whose
+device memory is planned once at start-up, or a memory-budgeted serving
+process.  The allocation-free entry point serves them by keeping its scratch
+in a fixed array inside the library.  It runs the same three kernels as the
+caller-scratch path (walsh_chmod_stats / _mlp / _apply through ops.chmod), so
+its output must equal that path's bit for bit, on consecutive calls that
+reuse the shared array.  The file is named to be collected last.  The
+per-context set-up is checked three ways: in this process after every other
+test has used the device, in a fresh process (where the set-up runs on the
+entry point's first call there), and on a second device when one is visible.
 """
 import ctypes
+import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -60,9 +68,8 @@ def test_scratch_limit_rejected_on_host():
     assert "allocation-free" in _lib.status_str(rc)
 
 
-@pytest.mark.gpu
-def test_noalloc_matches_caller_scratch_path_two_calls_in_a_row():
-    dev = torch.device("cuda", 0)
+def _check_two_calls_in_a_row(index):
+    dev = torch.device("cuda", index)
     torch.cuda.set_device(dev)
     g = torch.Generator(device="cpu").manual_seed(11)
 
@@ -98,3 +105,30 @@ def test_noalloc_matches_caller_scratch_path_two_calls_in_a_row():
     torch.cuda.synchronize()
     assert torch.equal(x1c, want1)
     assert np.isfinite(got1.float().cpu().numpy()).all()
+
+
+@pytest.mark.gpu
+def test_noalloc_matches_caller_scratch_path_two_calls_in_a_row():
+    _check_two_calls_in_a_row(0)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(os.environ.get("WALSH_NOALLOC_CHILD") == "1", reason="already the fresh process")
+def test_noalloc_in_a_fresh_process():
+    """The same check as the first call of a new process on the device."""
+    env = dict(os.environ, WALSH_NOALLOC_CHILD="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider",
+                        __file__ + "::test_noalloc_matches_caller_scratch_path_two_calls_in_a_row"],
+                       capture_output=True, text=True, env=env, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "1 passed" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_on_a_second_device():
+    """Each device's context has its own copy of the array: the set-up on
+    device 1 must not reuse device 0's address."""
+    _check_two_calls_in_a_row(1)
+    _check_two_calls_in_a_row(0)
+    torch.cuda.set_device(0)

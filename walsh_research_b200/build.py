@@ -39,7 +39,8 @@ def nvcc() -> str:
 
 
 def _deps() -> list[str]:
-    return glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
+    return (glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))
+            + glob.glob(os.path.join(INCLUDE, "*.h")))
 
 
 def _stale(target: str, sources: list[str]) -> bool:

@@ -12,7 +12,10 @@
 #include <atomic>
 #include <mutex>
 
+#include <cuda.h>
+
 #include "common.cuh"
+#include "ctx_cache.h"
 
 namespace walsh {
 
@@ -512,39 +515,75 @@ namespace walsh {
 
 constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;  // 4 MiB of float32
 constexpr int64_t kNoAllocAlignFloats = 64;                  // 256-byte sub-buffers
-constexpr int kNoAllocMaxDevices = 64;
+constexpr int kNoAllocMaxContexts = 64;
 
 __device__ __align__(256) float g_chmod_scratch[kNoAllocScratchFloats];
 
-std::atomic<float*> g_chmod_scratch_ptr[kNoAllocMaxDevices];
-std::mutex g_chmod_scratch_mu;
+ContextAddressCache<kNoAllocMaxContexts> g_chmod_scratch_cache;
 
 static int64_t round_up_floats(int64_t n) { return (n + kNoAllocAlignFloats - 1) / kNoAllocAlignFloats * kNoAllocAlignFloats; }
 
-// Device address of this device's scratch array, looked up once per device
-// (with that device current) and cached.
-static walsh_status chmod_scratch_for_current_device(float** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+// Driver calls reached through the runtime's entry-point table (no link
+// against libcuda): the current context and its process-unique id.
+using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+static bool ctx_fns(PfnCtxGetCurrent* get_cur, PfnCtxGetId* get_id) {
+  static PfnCtxGetCurrent cur = nullptr;
+  static PfnCtxGetId id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      cur = reinterpret_cast<PfnCtxGetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      id = reinterpret_cast<PfnCtxGetId>(p);
+    cudaGetLastError();
+  });
+  *get_cur = cur;
+  *get_id = id;
+  return cur && id;
+}
+
+// Id of the context current on this thread, 0 when there is none.
+static uint64_t current_ctx_id(PfnCtxGetCurrent get_cur, PfnCtxGetId get_id) {
+  CUcontext ctx = nullptr;
+  if (get_cur(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of the scratch array in the current context.  The set-up
+// (cudaGetSymbolAddress, with the caller's device current) runs on the first
+// call in each context and is cached under the context's id; a device reset or
+// a different current context on the same device is a new context and is
+// looked up again.  Every later call costs two driver queries.
+static walsh_status chmod_scratch_for_current_context(float** out) {
+  PfnCtxGetCurrent get_cur;
+  PfnCtxGetId get_id;
+  if (!ctx_fns(&get_cur, &get_id)) return WALSH_ERR_NOT_INIT;
+  uint64_t id = current_ctx_id(get_cur, get_id);
+  if (void* p = g_chmod_scratch_cache.find(id)) {
+    *out = static_cast<float*>(p);
+    return WALSH_OK;
+  }
+  // set-up: the lookup also makes the device's primary context current when
+  // no context was yet
+  void* addr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&addr, g_chmod_scratch);
+  if (e != cudaSuccess || addr == nullptr) {
     cudaGetLastError();
     return WALSH_ERR_NOT_INIT;
   }
-  float* p = g_chmod_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (!p) {
-    std::lock_guard<std::mutex> lock(g_chmod_scratch_mu);
-    p = g_chmod_scratch_ptr[dev].load(std::memory_order_relaxed);
-    if (!p) {
-      void* addr = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&addr, g_chmod_scratch);
-      if (e != cudaSuccess || addr == nullptr) {
-        cudaGetLastError();
-        return WALSH_ERR_NOT_INIT;
-      }
-      p = static_cast<float*>(addr);
-      g_chmod_scratch_ptr[dev].store(p, std::memory_order_release);
-    }
-  }
-  *out = p;
+  id = current_ctx_id(get_cur, get_id);
+  if (id == 0) return WALSH_ERR_NOT_INIT;
+  g_chmod_scratch_cache.insert(id, addr);
+  *out = static_cast<float*>(addr);
   return WALSH_OK;
 }
 
@@ -571,7 +610,7 @@ extern "C" walsh_status walsh_chmod_fwd_noalloc(const void* x, int dtype, int64_
   WALSH_CHECK_SHAPE(nseg <= 65535);
   if (chmod_noalloc_scratch_floats(nseg, C, seg_len) > kNoAllocScratchFloats) return WALSH_ERR_SCRATCH;
   float* scratch = nullptr;
-  if (walsh_status st = chmod_scratch_for_current_device(&scratch)) return st;
+  if (walsh_status st = chmod_scratch_for_current_context(&scratch)) return st;
   const int64_t nch = (seg_len + kChunkRows - 1) / kChunkRows;
   float* partial = scratch;
   float* scale = partial + round_up_floats(nseg * nch * C);
