@@ -13,8 +13,10 @@ between steps.
 Prints one JSON line (rank 0).  `value` times graph replays of the forward
 with inputs resident in HBM; `e2e` times the public ``mHCWalsh.forward`` call
 with the token ids copied from pinned host memory and the logits copied back
-every step.  `--impl reference` times the CPU oracle (a numpy restatement of
-the reference's PyTorch forward) on the host cores instead.
+every step.  `--impl reference` times the reference's own PyTorch forward
+(its src/model package, installed unmodified under baseline/_ref) on the host
+cores, one B1xT1024 slice of the same workload per step in bf16 autocast; when
+that install is absent it times the numpy oracle port instead and says so.
 """
 from __future__ import annotations
 
@@ -177,8 +179,61 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# reference arm / CPU baseline: the numpy oracle on the host cores
+# reference arm / CPU baseline: the reference's own PyTorch forward on the host
+# cores (its src/model package, installed unmodified under baseline/_ref);
+# the numpy oracle port stands in only when that install is absent
 # ---------------------------------------------------------------------------
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_model_cpu():
+    """The reference's mHCWalsh (src/model/mhc.py:538-681) built from its own
+    package with this bench's seeded weights loaded through its
+    ``load_state_dict`` (the state-dict layouts are identical).  Returns
+    (model, None), or (None, reason) when the reference cannot be imported."""
+    if not os.path.isdir(os.path.join(REF_DIR, "src", "model")):
+        return None, "reference package not installed under baseline/_ref"
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        from src.model import WalshConfig as RefConfig, mHCWalsh as RefWalsh
+    except Exception as e:  # noqa: BLE001 - any import failure means: use the port
+        return None, f"reference import failed: {type(e).__name__}: {e}"
+    ours = build_model_cpu()
+    torch.manual_seed(0)
+    ref = RefWalsh(RefConfig(**CONFIG), n_streams=N_STREAMS).eval()
+    ref.load_state_dict(ours.state_dict(), strict=True)
+    return ref, None
+
+
+def cpu_model_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def time_reference_torch(ref, steps, warmup):
+    """Mean seconds of one B1xT1024 forward of the reference on the host cores
+    (bf16 autocast, the config's dtype; every host thread)."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, T = CPU_SAMPLE
+    idx = token_ids(B, T, seed=2)
+    times = []
+    with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+        for _ in range(warmup):
+            ref(idx)
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            ref(idx)
+            times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    return B * T / sec, sec
+
 
 def oracle_inputs():
     model = build_model_cpu()
@@ -211,21 +266,37 @@ def cpu_threads():
         return os.cpu_count()
 
 
+def cpu_baseline(steps, warmup):
+    """The CPU leg: the reference's PyTorch forward when installed (kind
+    "reference"), else the numpy oracle port (kind "port").  Returns the
+    cpu_baseline object, the seconds per step and the dtype label."""
+    B, T = CPU_SAMPLE
+    ref, why = reference_model_cpu()
+    if ref is not None:
+        value, sec = time_reference_torch(ref, steps, warmup)
+        return ({"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "reference",
+                 "sample": f"one B{B}xT{T} forward per step of the reference's own mHCWalsh (src/model, "
+                           f"PyTorch on the host CPU, bf16 autocast) with the same architecture and weights",
+                 "cpu": cpu_model_name()}, sec, "bf16 (CPU autocast)")
+    value, sec = time_oracle(oracle_inputs(), steps, warmup)
+    return ({"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+             "sample": f"numpy oracle float32, one B{B}xT{T} forward per step (same architecture and weights)",
+             "cpu": cpu_model_name(), "why_port": why}, sec, "f32")
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    sd = oracle_inputs()
-    value, sec = time_oracle(sd, args.steps, args.warmup)
+    cpu, sec, dtype = cpu_baseline(args.steps, args.warmup)
+    value = cpu["value"]
     B, T = CPU_SAMPLE
-    cores = cpu_threads()
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
             "config": {"workload": f"Walsh-512 mHC+MoE+chmod prefill (config 3 architecture), sample B{B}xT{T}",
                        "global_batch": B, "seq_len": T},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"one B{B}xT{T} forward of the numpy oracle per step, float32"},
+            "cpu_baseline": cpu,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -269,12 +340,7 @@ def main():
     from walsh_research_b200.model.mhc import MAP_EPS, site_params
 
     B, T = args.batch, SEQ
-    cpu_model = build_model_cpu()
-    sd_np = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sd_np = {k: v.detach().float().numpy() for k, v in cpu_model.state_dict().items()
-                 if k != "freqs_cis" and not k.endswith(".H")}
-    model = cpu_model.to(dev).eval()
+    model = build_model_cpu().to(dev).eval()
     model.compute_dtype = torch.bfloat16
     idx_host = token_ids(B, T, seed=rank_token_seed(1, rank)).pin_memory()
     idx = idx_host.to(dev)
@@ -356,11 +422,8 @@ def main():
     if rank != 0:
         return
     cpu = None
-    if sd_np is not None:
-        v, sec = time_oracle(sd_np, steps=2, warmup=1)
-        Bc, Tc = CPU_SAMPLE
-        cpu = {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-               "sample": f"numpy oracle float32, one B{Bc}xT{Tc} forward per step (same architecture and weights)"}
+    if world == 1 and not args.no_cpu_baseline:
+        cpu, _, _ = cpu_baseline(steps=3, warmup=1)
     hbm, tflops, src = peaks()
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
