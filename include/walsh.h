@@ -245,6 +245,25 @@ walsh_status walsh_sinkhorn(const float* h, int64_t n, int iters, float eps, flo
  * FastMoEExperts.forward (src/model/moe.py:337-380) and HadamardMoE.forward
  * (src/model/moe.py:512-542) followed by the ffn-site epilogue of
  * mHCResidualStream.forward (src/model/mhc.py:366-381). */
+/* Expert selection of the MoE entry points below (pass NULL for the
+ * reference's rule).
+ * WALSH_ROUTE_TOPK: top_k experts by router probability, ties to the lower
+ *   expert index -- what HadamardRouter.forward runs (src/model/moe.py:432-436).
+ * WALSH_ROUTE_THRESHOLD: every expert whose probability exceeds `threshold`,
+ *   at least `min_experts` and at most top_k of them, taken in descending
+ *   probability -- the rule HadamardRouter's docstring and constructor
+ *   arguments describe (threshold, min_experts, max_experts;
+ *   src/model/moe.py:383-403) but its forward does not apply.  Opt-in.
+ * In both modes the routing weights are renormalised over the selected
+ * experts.  WALSH_ERR_ARG for an unknown mode, min_experts outside
+ * [1, top_k] or a threshold outside [0, 1]. */
+enum { WALSH_ROUTE_TOPK = 0, WALSH_ROUTE_THRESHOLD = 1 };
+typedef struct {
+  int mode;
+  int min_experts;
+  float threshold;
+} walsh_moe_routing;
+
 typedef struct {   /* all in the dtype of u (bf16 or fp16) */
   const void* w1;   /* [C/4, C]   router layer 1 (nn.Linear layout) */
   const void* w2;   /* [E, C/4]   router layer 2 */
@@ -259,7 +278,7 @@ walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, int C, int to
                            void* y, int fuse_post, const void* x, int x_dtype, const float* hmix,
                            void* x_out, const float* weights_in, uint8_t* mask_out,
                            float* probs_out, float* weights_out, const walsh_moe_tc_weights* tc,
-                           void* stream);
+                           const walsh_moe_routing* routing, void* stream);
 
 /* MoE after router layer 1 (for decode-sized token counts): hpre = u W1^T
  * [ntok, C/4] (u's dtype, computed by the caller, e.g. walsh_octo_linear_fwd
@@ -276,7 +295,8 @@ walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, int dtype, in
                                   const uint8_t* up_2bit, const uint8_t* down_2bit,
                                   const float* gammas, void* y, int fuse_post, const void* x,
                                   int x_dtype, const float* hmix, void* x_out, uint8_t* mask_out,
-                                  float* probs_out, float* weights_out, void* stream);
+                                  float* probs_out, float* weights_out, const walsh_moe_routing* routing,
+                                  void* stream);
 
 /* Prefill-sized MoE for C = 512 (E = 16, router hidden 128) on the
  * 5th-generation tensor cores, in two calls.
@@ -290,7 +310,7 @@ walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, int dtype, in
  * HadamardRouter.forward (src/model/moe.py:418-447). */
 walsh_status walsh_moe_router_tc_fwd(const void* u, int dtype, int64_t ntok, const void* w1,
                                      const void* w2, int top_k, uint8_t* mask, float* probs,
-                                     float* weights, void* stream);
+                                     float* weights, const walsh_moe_routing* routing, void* stream);
 
 /* walsh_moe_experts_tc_fwd: the 16 ternary SwiGLU experts (all evaluated,
  * weighted by `weights`, 0 outside the top-k) and either y [ntok, 512]

@@ -259,15 +259,26 @@ def stream_mapping(x_flat, phi, alpha, bias, kind, n=4):
     return s if kind == "pre" else 2.0 * s
 
 
-def router(x, w0, w2, top_k):
+def router(x, w0, w2, top_k, threshold=None, min_experts=1):
     """HadamardRouter.forward (src/model/moe.py:418-447): softmax(W2 SiLU(W1 x)),
-    top-k mask (ties to the lower expert index), renormalised weights."""
+    top-k mask (ties to the lower expert index), renormalised weights.
+
+    With ``threshold`` set: the threshold rule that HadamardRouter's docstring
+    and arguments describe (src/model/moe.py:383-403) but its forward does not
+    run -- every expert with p > threshold, at least ``min_experts`` and at most
+    top_k of them, taken in descending probability (ties to the lower index)."""
     probs = softmax(silu(x @ w0.T) @ w2.T, -1)
     E = probs.shape[-1]
     k = min(top_k, E)
     order = np.argsort(-probs, axis=-1, kind="stable")[..., :k]
+    if threshold is None:
+        take = np.ones(order.shape, dtype=bool)
+    else:
+        above = (probs > threshold).sum(-1, keepdims=True)
+        kt = np.clip(above, min_experts, k)
+        take = np.arange(k) < kt
     mask = np.zeros_like(probs)
-    np.put_along_axis(mask, order, 1.0, axis=-1)
+    np.put_along_axis(mask, order, take.astype(probs.dtype), axis=-1)
     masked = probs * mask
     weights = masked / np.maximum(masked.sum(-1, keepdims=True), 1e-8)
     return weights, mask, probs
@@ -289,12 +300,14 @@ def experts(xb, weights, gate_w, up_w, down_w):
     return out * weights[..., None]
 
 
-def moe(x, p, prefix, top_k, forced_mask=None):
+def moe(x, p, prefix, top_k, forced_mask=None, threshold=None, min_experts=1):
     """HadamardMoE.forward (src/model/moe.py:512-542).  ``forced_mask`` (test
-    hook) replaces the top-k selection with a given 0/1 mask."""
+    hook) replaces the top-k selection with a given 0/1 mask; ``threshold``
+    selects the router's threshold rule (see ``router``)."""
     C = x.shape[-1]
     E = C // 32
-    w, mask, probs = router(x, p[prefix + "router.gate.0.weight"], p[prefix + "router.gate.2.weight"], top_k)
+    w, mask, probs = router(x, p[prefix + "router.gate.0.weight"], p[prefix + "router.gate.2.weight"], top_k,
+                            threshold, min_experts)
     if forced_mask is not None:
         masked = probs * forced_mask
         w = masked / np.maximum(masked.sum(-1, keepdims=True), 1e-8)
@@ -406,7 +419,9 @@ def block(cfg, p, l, x, cos, sin, n=4, cache=None, dtype=np.float64, trace=None,
         un = rmsnorm(u, p[pre + "ffn_norm.weight"])
         if cfg["use_moe"]:
             fm = None if forced_masks is None else forced_masks[l]
-            y, mask, probs = moe(un, p, pre + "feed_forward.", cfg["moe_max_experts"], fm)
+            thr = cfg["moe_threshold"] if cfg.get("moe_routing", "topk") == "threshold" else None
+            y, mask, probs = moe(un, p, pre + "feed_forward.", cfg["moe_max_experts"], fm, thr,
+                                 cfg.get("moe_min_experts", 1))
             if trace is not None:
                 trace.setdefault("router_mask", []).append(mask)
                 trace.setdefault("router_probs", []).append(probs)

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_status_strings_and_version():
-    assert _lib.call("walsh_abi_version") >= 1
+    assert _lib.call("walsh_abi_version") >= 2
     assert _lib.status_str(0) == "ok"
     for code in range(-9, 0):
         assert _lib.status_str(code) != "unknown walsh status"
@@ -57,7 +57,8 @@ def test_fault_injection(monkeypatch):
     L = _lib.lib()
     monkeypatch.setenv("WALSH_INJECT_FAULT", "moe_fwd")
     p = ctypes.c_void_p(16)
-    rc = L.walsh_moe_fwd(p, 0, 4, 512, 6, p, p, p, p, p, p, p, 0, None, 0, None, None, None, None, None, None, None, None)
+    rc = L.walsh_moe_fwd(p, 0, 4, 512, 6, p, p, p, p, p, p, p, 0, None, 0, None, None, None, None, None, None, None,
+                         None, None)
     assert rc == -7
     monkeypatch.setenv("WALSH_INJECT_FAULT", "sinkhorn")
     with pytest.raises(_lib.WalshError, match="injected"):
@@ -71,3 +72,21 @@ def test_cpu_tensors_are_rejected():
     from walsh_research_b200 import ops
     with pytest.raises(RuntimeError, match="CUDA devices only"):
         ops.rmsnorm(torch.ones(2, 8), torch.ones(8))
+
+
+@pytest.mark.parametrize("mode,kmin,thr", [(7, 1, 0.1), (1, 0, 0.1), (1, 7, 0.1), (1, 1, 1.5), (1, 1, float("nan"))])
+def test_bad_routing_rule_rejected_on_host(mode, kmin, thr):
+    """An unknown selection mode, min_experts outside [1, top_k] or a
+    threshold outside [0, 1] is an argument error before any launch (the
+    device pointers below are never dereferenced)."""
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    rt = ctypes.byref(_lib.MoeRouting(mode, kmin, thr))
+    rc = L.walsh_moe_fwd(p, 0, 4, 512, 6, p, p, p, p, p, p, p, 0, None, 0, None, None, None, None, None, None, None,
+                         rt, None)
+    assert rc == -1
+    rc = L.walsh_moe_hidden_fwd(p, p, 1, 4, 512, 6, p, p, p, p, p, p, 0, None, 1, None, None, None, None, None, rt,
+                                None)
+    assert rc == -1
+    rc = L.walsh_moe_router_tc_fwd(p, 1, 4, p, p, 6, p, p, p, rt, None)
+    assert rc == -1

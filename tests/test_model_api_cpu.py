@@ -101,8 +101,15 @@ def test_cuda_graph_cache_host_logic(monkeypatch):
         out, _ = model._graph_forward(b, 0)            # replay with the new ids copied in
         assert [e[0] for e in log[n:]] == ["replay"]
         graphs = model.__dict__["_walsh_graphs"]
-        key = ((2, 3), 0, model._act_dtype(), a.device)
+        key = model._graph_key(a, 0)
+        assert key[:4] == ((2, 3), 0, model._act_dtype(), a.device)
         assert torch.equal(graphs[key]["idx"], b)
+        # another expert-selection rule is another graph: eager first
+        model.layers[0].feed_forward.router.routing_mode = "threshold"
+        model._graph_forward(a, 0)
+        assert log[-1] == ("forward", (2, 3), 0)
+        assert model._graph_key(a, 0) != key and key in graphs
+        model.layers[0].feed_forward.router.routing_mode = "topk"
         model._graph_forward(a, 5)                     # other start_pos: its own entry, eager first
         assert log[-1] == ("forward", (2, 3), 5)
         with torch.no_grad():

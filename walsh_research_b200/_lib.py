@@ -39,11 +39,11 @@ SIGNATURES = {
     "walsh_mhc_post": [P, P, P, c_int, c_int64, c_int, P, P],
     "walsh_sinkhorn": [P, c_int64, c_int, c_float, P, P],
     "walsh_moe_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, P, c_int, P, c_int, P, P, P, P, P, P, P,
-                      P],
+                      P, P],
     "walsh_octo_set_mainloop": [c_int],
     "walsh_tc05_error": [c_int],
     "walsh_attn_set_path": [c_int],
-    "walsh_moe_router_tc_fwd": [P, c_int, c_int64, P, P, c_int, P, P, P, P],
+    "walsh_moe_router_tc_fwd": [P, c_int, c_int64, P, P, c_int, P, P, P, P, P],
     "walsh_moe_experts_tc_fwd": [P, c_int, c_int64, P, P, P, P, P, c_int, P, c_int, P, P, P],
     "walsh_tc05_wait_selftest": [ctypes.c_longlong, P],
     "walsh_octo_linear_fwd": [P, c_int, c_int64, c_int, P, P, c_int, c_int64, P, P, P],
@@ -52,7 +52,7 @@ SIGNATURES = {
     "walsh_octo_swiglu_fwd": [P, c_int, c_int64, c_int, P, P, c_int, P, c_int64, P, P],
     "walsh_octo_post_fwd": [P, c_int, c_int64, c_int, P, P, c_int, P, c_int, P, c_int, P, P, P],
     "walsh_moe_hidden_fwd": [P, P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, c_int, P, c_int, P, P, P, P, P,
-                             P],
+                             P, P],
     "walsh_chmod_chunk_rows": [c_int],
     "walsh_chmod_stats": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P],
     "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],
@@ -84,6 +84,14 @@ _PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows", "walsh_octo_set_mai
 class MoeTcWeights(ctypes.Structure):
     """walsh_moe_tc_weights: bfloat16 copies of the router / expert weights."""
     _fields_ = [("w1", P), ("w2", P), ("gate", P), ("up", P), ("down", P)]
+
+
+ROUTE_TOPK, ROUTE_THRESHOLD = 0, 1
+
+
+class MoeRouting(ctypes.Structure):
+    """walsh_moe_routing: the expert-selection rule (NULL = the reference's top-k)."""
+    _fields_ = [("mode", c_int), ("min_experts", c_int), ("threshold", c_float)]
 
 
 class WalshError(RuntimeError):

@@ -40,4 +40,4 @@ extern "C" const char* walsh_status_str(walsh_status s) {
   }
 }
 
-extern "C" int walsh_abi_version(void) { return 1; }
+extern "C" int walsh_abi_version(void) { return 2; }

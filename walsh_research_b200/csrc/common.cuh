@@ -30,6 +30,31 @@ template <> __device__ __forceinline__ __half from_f<__half>(float v) {
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
+// Expert-selection rule of the MoE router.  Experts are taken in descending
+// probability (ties to the lower index), at most kmax of them; the k-th pick
+// (k >= kmin, counted from 0) is not taken when its probability is not above
+// thr.  The reference's top-k is kmin = kmax (never stops early); the
+// threshold rule keeps every expert with p > thr, at least kmin, at most kmax.
+struct RouteRule {
+  int kmax, kmin;
+  float thr;
+  __host__ __device__ __forceinline__ bool stop(int k, float p) const { return k >= kmin && !(p > thr); }
+};
+
+// Host: the rule for a top_k argument and an optional walsh_moe_routing.
+static inline int make_route_rule(int top_k, const walsh_moe_routing* r, RouteRule* rr) {
+  rr->kmax = top_k;
+  rr->kmin = top_k;
+  rr->thr = -1.f;
+  if (r == nullptr || r->mode == WALSH_ROUTE_TOPK) return WALSH_OK;
+  if (r->mode != WALSH_ROUTE_THRESHOLD) return WALSH_ERR_ARG;
+  if (r->min_experts < 1 || r->min_experts > top_k || !(r->threshold >= 0.f && r->threshold <= 1.f))
+    return WALSH_ERR_ARG;
+  rr->kmin = r->min_experts;
+  rr->thr = r->threshold;
+  return WALSH_OK;
+}
+
 // 8 consecutive elements <-> float[8] (16-byte accesses for 16-bit types, 2 x 16 for float).
 __device__ __forceinline__ void load8(const float* p, float* v) {
   const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);

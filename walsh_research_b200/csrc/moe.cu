@@ -29,7 +29,7 @@ struct MoeCfg {
 
 template <typename T, typename TX, int C>
 __global__ void __launch_bounds__(256)
-moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __restrict__ w1t,
+moe_kernel(const T* __restrict__ u, int64_t ntok, RouteRule rr, const float* __restrict__ w1t,
            const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
            const uint8_t* __restrict__ dp, const float* __restrict__ gammas, T* __restrict__ y, int fuse_post,
            const TX* x, const float* __restrict__ hmix, TX* xo, const float* __restrict__ weights_in,
@@ -124,7 +124,8 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
     for (int e = 0; e < E; ++e) l[e] = __fdiv_rn(l[e], sum);
     uint64_t chosen = 0;
     float wsum = 0.f;
-    for (int k = 0; k < top_k; ++k) {
+    int nk = 0;
+    for (int k = 0; k < rr.kmax; ++k) {
       int best = -1;
       float bv = -1.f;
       for (int e = 0; e < E; ++e)
@@ -134,16 +135,18 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
           if (!((chosen >> e) & 1ull)) best = e;
         bv = 0.f;
       }
+      if (rr.stop(k, bv)) break;
       chosen |= 1ull << best;
       sel[tid * E + k] = best;
       selw[tid * E + k] = bv;
+      ++nk;
     }
-    nsel[tid] = top_k;
+    nsel[tid] = nk;
     // renormalise in ascending expert order, as (probs * mask).sum(-1) does
     for (int e = 0; e < E; ++e)
       if ((chosen >> e) & 1ull) wsum += l[e];
     wsum = fmaxf(wsum, 1e-8f);
-    for (int k = 0; k < top_k; ++k) selw[tid * E + k] = __fdiv_rn(selw[tid * E + k], wsum);
+    for (int k = 0; k < nk; ++k) selw[tid * E + k] = __fdiv_rn(selw[tid * E + k], wsum);
     const int64_t tok = t0 + tid;
     for (int e = 0; e < E; ++e) {
       const bool on = (chosen >> e) & 1ull;
@@ -159,7 +162,7 @@ moe_kernel(const T* __restrict__ u, int64_t ntok, int top_k, const float* __rest
   // experts: one warp per selected (token, expert) pair
   const float gg = __ldg(gammas + 0), gu = __ldg(gammas + 1), gd = __ldg(gammas + 2);
   float* aw = as + warp * kExpertHidden;
-  const int slots = weights_in ? E : top_k;
+  const int slots = weights_in ? E : rr.kmax;
   for (int item = warp; item < ntile * slots; item += 8) {
     const int t = item / slots, k = item - t * slots;
     if (k >= nsel[t]) continue;
@@ -263,7 +266,7 @@ constexpr size_t smem_bytes() {
 
 template <typename TU, typename TX>
 __global__ void __launch_bounds__(256, 1)
-moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* __restrict__ w1b,
+moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, RouteRule rr, const TU* __restrict__ w1b,
                   const TU* __restrict__ w2b, const TU* __restrict__ gb, const TU* __restrict__ ub,
                   const TU* __restrict__ db, const float* __restrict__ gammas, TU* __restrict__ y, int fuse_post,
                   const TX* x, const float* __restrict__ hmix, TX* xo,
@@ -379,7 +382,7 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
 #pragma unroll
     for (int e = 0; e < E; ++e) p[e] = __fdiv_rn(p[e], sum);
     uint32_t chosen = 0;
-    for (int k = 0; k < top_k; ++k) {
+    for (int k = 0; k < rr.kmax; ++k) {
       int best = -1;
       float bv = -1.f;
 #pragma unroll
@@ -388,6 +391,7 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
       if (best < 0)
         for (int e = E - 1; e >= 0; --e)
           if (!((chosen >> e) & 1u)) best = e;
+      if (rr.stop(k, bv)) break;
       chosen |= 1u << best;
     }
     float wsum = 0.f;
@@ -563,8 +567,8 @@ moe_mma512_kernel(const TU* __restrict__ u, int64_t ntok, int top_k, const TU* _
 // renormalisation over the selected experts in ascending order; every lane
 // gets sel[k] and its routing weight selw[k] = p / sum of the selected p.
 template <int C>
-__device__ __forceinline__ void moe_route_warp(const float* hs, const float* __restrict__ w2, int64_t tok,
-                                               int top_k, int lane, int* sel, float* selw,
+__device__ __forceinline__ int moe_route_warp(const float* hs, const float* __restrict__ w2, int64_t tok,
+                                              RouteRule rr, int lane, int* sel, float* selw,
                                                uint8_t* __restrict__ mask_out, float* __restrict__ probs_out,
                                                float* __restrict__ weights_out) {
   constexpr int E = C / 32, HID = C / 4;
@@ -603,7 +607,8 @@ __device__ __forceinline__ void moe_route_warp(const float* hs, const float* __r
   for (int q = 0; q < EL; ++q) p[q] = __fdiv_rn(p[q], sum);
   // top-k by warp arg-max; ties go to the lower expert index
   uint32_t chosen = 0;  // bit q: this lane's expert lane + 32 q
-  for (int k = 0; k < top_k; ++k) {
+  int nk = 0;           // the same on every lane: the arg-max below is a butterfly
+  for (int k = 0; k < rr.kmax; ++k) {
     float bv = -2.f;
     int bi = E;
 #pragma unroll
@@ -624,9 +629,12 @@ __device__ __forceinline__ void moe_route_warp(const float* hs, const float* __r
         const uint32_t cb = __shfl_sync(0xffffffffu, chosen, e & 31);
         if (!((cb >> (e >> 5)) & 1u)) bi = e;
       }
+      bv = -1.f;
     }
+    if (rr.stop(k, bv)) break;
     sel[k] = bi;
     if ((bi & 31) == lane) chosen |= 1u << (bi >> 5);
+    ++nk;
   }
   // renormalise over the selected probabilities, summed in ascending expert order
   float wsum = 0.f;
@@ -646,11 +654,12 @@ __device__ __forceinline__ void moe_route_warp(const float* hs, const float* __r
       if (weights_out) weights_out[tok * E + e] = on ? __fdiv_rn(p[q], wsum) : 0.f;
     }
   }
-  for (int k = 0; k < top_k; ++k) {
+  for (int k = 0; k < nk; ++k) {
     const int e = sel[k];
     const float pe = __shfl_sync(0xffffffffu, p[e >> 5 < EL ? e >> 5 : 0], e & 31);
     selw[k] = __fdiv_rn(pe, wsum);
   }
+  return nk;
 }
 
 // One selected expert of a token on one warp (lane k holds input k of the
@@ -724,7 +733,7 @@ __device__ __forceinline__ void moe_expert_warp(const TU* __restrict__ u, int64_
 // ---------------------------------------------------------------------------
 template <typename TU, typename TX, int C>
 __global__ void __launch_bounds__(256)
-moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, int top_k,
+moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, RouteRule rr,
                  const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
                  const uint8_t* __restrict__ dp, const float* __restrict__ gammas, TU* __restrict__ y,
                  int fuse_post, const TX* x, const float* __restrict__ hmix, TX* xo, uint8_t* __restrict__ mask_out,
@@ -746,9 +755,9 @@ moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t 
   __syncwarp();
   int sel[8];
   float selw[8];
-  moe_route_warp<C>(hs, w2, tok, top_k, lane, sel, selw, mask_out, probs_out, weights_out);
+  const int nk = moe_route_warp<C>(hs, w2, tok, rr, lane, sel, selw, mask_out, probs_out, weights_out);
   // the selected experts
-  for (int k = 0; k < top_k; ++k) {
+  for (int k = 0; k < nk; ++k) {
     moe_expert_warp<TU, C>(u, tok, sel[k], selw[k], gp, upp, dp, gammas, lane, as, ys);
     __syncwarp();
   }
@@ -790,7 +799,7 @@ moe_token_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t 
 // top_k experts in sequence.
 template <typename TU, typename TX, int C>
 __global__ void __launch_bounds__(256)
-moe_token_split_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, int top_k,
+moe_token_split_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, int64_t ntok, RouteRule rr,
                        const float* __restrict__ w2, const uint8_t* __restrict__ gp, const uint8_t* __restrict__ upp,
                        const uint8_t* __restrict__ dp, const float* __restrict__ gammas, TU* __restrict__ y,
                        int fuse_post, const TX* x, const float* __restrict__ hmix, TX* xo,
@@ -803,6 +812,7 @@ moe_token_split_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, in
   float* as = ys + C;                           // [8][EH]
   __shared__ int s_sel[8];
   __shared__ float s_w[8];
+  __shared__ int s_nk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tok = blockIdx.x;
   for (int j = threadIdx.x; j < HID; j += 256) {
@@ -814,15 +824,17 @@ moe_token_split_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, in
   if (warp == 0) {
     int sel[8];
     float selw[8];
-    moe_route_warp<C>(hs, w2, tok, top_k, lane, sel, selw, mask_out, probs_out, weights_out);
-    if (lane == 0)
-      for (int k = 0; k < top_k; ++k) {
+    const int nk = moe_route_warp<C>(hs, w2, tok, rr, lane, sel, selw, mask_out, probs_out, weights_out);
+    if (lane == 0) {
+      for (int k = 0; k < nk; ++k) {
         s_sel[k] = sel[k];
         s_w[k] = selw[k];
       }
+      s_nk = nk;
+    }
   }
   __syncthreads();
-  if (warp < top_k) moe_expert_warp<TU, C>(u, tok, s_sel[warp], s_w[warp], gp, upp, dp, gammas, lane, as + warp * EH, ys);
+  if (warp < s_nk) moe_expert_warp<TU, C>(u, tok, s_sel[warp], s_w[warp], gp, upp, dp, gammas, lane, as + warp * EH, ys);
   __syncthreads();
   if (!fuse_post) {
     for (int c = threadIdx.x; c < C; c += 256) y[tok * C + c] = from_f<TU>(ys[c]);
@@ -846,17 +858,17 @@ moe_token_split_kernel(const TU* __restrict__ u, const TU* __restrict__ hpre, in
 }
 
 template <typename TU, typename TX, int C>
-static int launch_moe_token(const void* u, const void* hpre, int64_t ntok, int top_k, const float* w2,
+static int launch_moe_token(const void* u, const void* hpre, int64_t ntok, RouteRule rr, const float* w2,
                             const uint8_t* gp, const uint8_t* upp, const uint8_t* dp, const float* gammas, void* y,
                             int fuse_post, const void* x, const float* hmix, void* xo, uint8_t* mask_out,
                             float* probs_out, float* weights_out, cudaStream_t s) {
-  if (top_k <= 8) {
+  if (rr.kmax <= 8) {
     const int smem2 = (C / 4 + C + 8 * kExpertHidden) * (int)sizeof(float);
     auto k2 = moe_token_split_kernel<TU, TX, C>;
     if (smem2 > 48 * 1024 &&
         cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) != cudaSuccess)
       return launch_status();
-    k2<<<(unsigned)ntok, 256, smem2, s>>>((const TU*)u, (const TU*)hpre, ntok, top_k, w2, gp, upp, dp, gammas,
+    k2<<<(unsigned)ntok, 256, smem2, s>>>((const TU*)u, (const TU*)hpre, ntok, rr, w2, gp, upp, dp, gammas,
                                           (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo, mask_out, probs_out,
                                           weights_out);
     return launch_status();
@@ -867,14 +879,14 @@ static int launch_moe_token(const void* u, const void* hpre, int64_t ntok, int t
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status();
-  kern<<<(unsigned)((ntok + 7) / 8), 256, smem, s>>>((const TU*)u, (const TU*)hpre, ntok, top_k, w2, gp, upp, dp,
+  kern<<<(unsigned)((ntok + 7) / 8), 256, smem, s>>>((const TU*)u, (const TU*)hpre, ntok, rr, w2, gp, upp, dp,
                                                      gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo,
                                                      mask_out, probs_out, weights_out);
   return launch_status();
 }
 
 template <typename T, typename TX, int C>
-static int launch_moe(const void* u, int64_t ntok, int top_k, const float* w1t, const float* w2, const uint8_t* gp,
+static int launch_moe(const void* u, int64_t ntok, RouteRule rr, const float* w1t, const float* w2, const uint8_t* gp,
                       const uint8_t* upp, const uint8_t* dp, const float* gammas, void* y, int fuse_post,
                       const void* x, const float* hmix, void* xo, const float* weights_in, uint8_t* mask_out,
                       float* probs_out, float* weights_out, cudaStream_t s) {
@@ -884,13 +896,13 @@ static int launch_moe(const void* u, int64_t ntok, int top_k, const float* w1t, 
   auto kern = moe_kernel<T, TX, C>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t grid = (ntok + M::TM - 1) / M::TM;
-  kern<<<(unsigned)grid, 256, smem, s>>>((const T*)u, ntok, top_k, w1t, w2, gp, upp, dp, gammas, (T*)y, fuse_post,
+  kern<<<(unsigned)grid, 256, smem, s>>>((const T*)u, ntok, rr, w1t, w2, gp, upp, dp, gammas, (T*)y, fuse_post,
                                          (const TX*)x, hmix, (TX*)xo, weights_in, mask_out, probs_out, weights_out);
   return launch_status();
 }
 
 template <typename TU, typename TX>
-static int launch_moe_mma(const void* u, int64_t ntok, int top_k, const walsh_moe_tc_weights* tc, bool experts,
+static int launch_moe_mma(const void* u, int64_t ntok, RouteRule rr, const walsh_moe_tc_weights* tc, bool experts,
                           const float* gammas, void* y, int fuse_post, const void* x, const float* hmix, void* xo,
                           uint8_t* mask_out, float* probs_out, float* weights_out, cudaStream_t s) {
   const unsigned grid = (unsigned)((ntok + moe_tc::TOK - 1) / moe_tc::TOK);
@@ -899,7 +911,7 @@ static int launch_moe_mma(const void* u, int64_t ntok, int top_k, const walsh_mo
       cudaSuccess)
     return WALSH_ERR_LAUNCH;
   moe_mma512_kernel<TU, TX><<<grid, 256, smem, s>>>(
-      (const TU*)u, ntok, top_k, (const TU*)tc->w1, (const TU*)tc->w2, experts ? (const TU*)tc->gate : nullptr,
+      (const TU*)u, ntok, rr, (const TU*)tc->w1, (const TU*)tc->w2, experts ? (const TU*)tc->gate : nullptr,
       (const TU*)tc->up, (const TU*)tc->down, gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo, mask_out,
       probs_out, weights_out);
   return launch_status();
@@ -1375,7 +1387,8 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
                                       const uint8_t* down_2bit, const float* gammas, void* y, int fuse_post,
                                       const void* x, int x_dtype, const float* hmix, void* x_out,
                                       const float* weights_in, uint8_t* mask_out, float* probs_out,
-                                      float* weights_out, const walsh_moe_tc_weights* tc, void* stream) {
+                                      float* weights_out, const walsh_moe_tc_weights* tc,
+                                      const walsh_moe_routing* routing, void* stream) {
   if (int e = injected("moe_fwd")) return e;
   WALSH_CHECK_DTYPE(dtype);
   WALSH_CHECK_DTYPE(x_dtype);
@@ -1387,6 +1400,8 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
   WALSH_CHECK_ARG(!experts || (fuse_post ? (x && hmix && x_out) : (y != nullptr)));
   WALSH_CHECK_SHAPE(ntok >= 0);
   WALSH_CHECK_SHAPE(top_k >= 1 && top_k <= MoeCfg<512>::MAXK && top_k <= C / 32);
+  RouteRule rr;
+  if (int e = make_route_rule(top_k, routing, &rr)) return e;
   WALSH_CHECK_ARG(!experts ||
                   ((((uintptr_t)gate_2bit | (uintptr_t)up_2bit) & 7u) == 0 && ((uintptr_t)down_2bit & 15u) == 0));
   if (ntok == 0) return WALSH_OK;
@@ -1399,20 +1414,20 @@ extern "C" walsh_status walsh_moe_fwd(const void* u, int dtype, int64_t ntok, in
         ((uintptr_t)hmix)) & 15u) == 0) {
     const bool xh = fuse_post && x_dtype == WALSH_F16;  // stream type of the fused epilogue
     if (dtype == WALSH_F16)
-      return xh ? launch_moe_mma<__half, __half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix, x_out,
+      return xh ? launch_moe_mma<__half, __half>(u, ntok, rr, tc, experts, gammas, y, fuse_post, x, hmix, x_out,
                                                  mask_out, probs_out, weights_out, s)
-                : launch_moe_mma<__half, __nv_bfloat16>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix,
+                : launch_moe_mma<__half, __nv_bfloat16>(u, ntok, rr, tc, experts, gammas, y, fuse_post, x, hmix,
                                                         x_out, mask_out, probs_out, weights_out, s);
-    return xh ? launch_moe_mma<__nv_bfloat16, __half>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x, hmix,
+    return xh ? launch_moe_mma<__nv_bfloat16, __half>(u, ntok, rr, tc, experts, gammas, y, fuse_post, x, hmix,
                                                       x_out, mask_out, probs_out, weights_out, s)
-              : launch_moe_mma<__nv_bfloat16, __nv_bfloat16>(u, ntok, top_k, tc, experts, gammas, y, fuse_post, x,
+              : launch_moe_mma<__nv_bfloat16, __nv_bfloat16>(u, ntok, rr, tc, experts, gammas, y, fuse_post, x,
                                                              hmix, x_out, mask_out, probs_out, weights_out, s);
   }
   if (C != 512 && C != 2048) return WALSH_ERR_SHAPE;
   return WALSH_DISPATCH_DTYPE(dtype, TU, WALSH_DISPATCH_DTYPE(x_dtype, TX,
-      C == 512 ? launch_moe<TU, TX, 512>(u, ntok, top_k, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y, fuse_post,
+      C == 512 ? launch_moe<TU, TX, 512>(u, ntok, rr, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y, fuse_post,
                                          x, hmix, x_out, weights_in, mask_out, probs_out, weights_out, s)
-               : launch_moe<TU, TX, 2048>(u, ntok, top_k, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y,
+               : launch_moe<TU, TX, 2048>(u, ntok, rr, w1, w2, gate_2bit, up_2bit, down_2bit, gammas, y,
                                           fuse_post, x, hmix, x_out, weights_in, mask_out, probs_out, weights_out,
                                           s)));
 }
@@ -1422,7 +1437,7 @@ extern "C" walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, in
                                              const uint8_t* up_2bit, const uint8_t* down_2bit, const float* gammas,
                                              void* y, int fuse_post, const void* x, int x_dtype, const float* hmix,
                                              void* x_out, uint8_t* mask_out, float* probs_out, float* weights_out,
-                                             void* stream) {
+                                             const walsh_moe_routing* routing, void* stream) {
   if (int e = injected("moe_hidden_fwd")) return e;
   WALSH_CHECK_DTYPE(dtype);
   WALSH_CHECK_DTYPE(x_dtype);
@@ -1430,13 +1445,15 @@ extern "C" walsh_status walsh_moe_hidden_fwd(const void* u, const void* hpre, in
   WALSH_CHECK_ARG(fuse_post ? (x && hmix && x_out) : (y != nullptr));
   WALSH_CHECK_SHAPE(ntok >= 0 && (C == 512 || C == 2048));
   WALSH_CHECK_SHAPE(top_k >= 1 && top_k <= 8 && top_k <= C / 32);
+  RouteRule rr;
+  if (int e = make_route_rule(top_k, routing, &rr)) return e;
   WALSH_CHECK_ARG(((((uintptr_t)gate_2bit | (uintptr_t)up_2bit) & 7u) == 0) && (((uintptr_t)down_2bit & 15u) == 0) &&
                   (((uintptr_t)w2 & 15u) == 0) && (!fuse_post || ((((uintptr_t)x) | ((uintptr_t)x_out)) & 15u) == 0));
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
   return WALSH_DISPATCH_DTYPE(dtype, TU, WALSH_DISPATCH_DTYPE(x_dtype, TX,
-      C == 512 ? launch_moe_token<TU, TX, 512>(u, hpre, ntok, top_k, w2, gate_2bit, up_2bit, down_2bit, gammas, y,
+      C == 512 ? launch_moe_token<TU, TX, 512>(u, hpre, ntok, rr, w2, gate_2bit, up_2bit, down_2bit, gammas, y,
                                                fuse_post, x, hmix, x_out, mask_out, probs_out, weights_out, s)
-               : launch_moe_token<TU, TX, 2048>(u, hpre, ntok, top_k, w2, gate_2bit, up_2bit, down_2bit, gammas,
+               : launch_moe_token<TU, TX, 2048>(u, hpre, ntok, rr, w2, gate_2bit, up_2bit, down_2bit, gammas,
                                                 y, fuse_post, x, hmix, x_out, mask_out, probs_out, weights_out, s)));
 }

@@ -540,7 +540,7 @@ struct EpiRouter {
   static constexpr int E = 16, HID = 128;
   static constexpr int kRowScratch = E * HID * 4 + 2 * 128 * E * 4;  // W2 + partial-logit exchange
   const TU* w2;  // [E][HID]
-  int top_k;
+  RouteRule rr;  // expert-selection rule
   uint8_t* mask;
   float* probs;
   float* weights;
@@ -605,7 +605,7 @@ struct EpiRouter {
 #pragma unroll
     for (int e = 0; e < E; ++e) p[e] = __fdiv_rn(p[e], sum);
     uint32_t chosen = 0;
-    for (int k = 0; k < top_k; ++k) {
+    for (int k = 0; k < rr.kmax; ++k) {
       int best = -1;
       float bv = -1.f;
 #pragma unroll
@@ -617,6 +617,7 @@ struct EpiRouter {
       if (best < 0)
         for (int e = E - 1; e >= 0; --e)
           if (!((chosen >> e) & 1u)) best = e;
+      if (rr.stop(k, bv)) break;
       chosen |= 1u << best;
     }
     float wsum = 0.f;
@@ -1079,10 +1080,12 @@ extern "C" walsh_status walsh_octo_linear_fwd(const void* x, int dtype, int64_t 
 
 extern "C" walsh_status walsh_moe_router_tc_fwd(const void* u, int dtype, int64_t ntok, const void* w1,
                                                const void* w2, int top_k, uint8_t* mask, float* probs,
-                                               float* weights, void* stream) {
+                                               float* weights, const walsh_moe_routing* routing, void* stream) {
   if (int e = injected("moe_router_tc_fwd")) return e;
   WALSH_CHECK_ARG(u && w1 && w2 && mask && probs && weights);
   WALSH_CHECK_SHAPE(ntok >= 0 && ntok <= 2147483647LL && top_k >= 1 && top_k <= 16);
+  RouteRule rr;
+  if (int e = make_route_rule(top_k, routing, &rr)) return e;
   if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
   if ((((uintptr_t)u) | ((uintptr_t)w1) | ((uintptr_t)mask) | ((uintptr_t)probs) | ((uintptr_t)weights)) & 15u)
     return WALSH_ERR_ALIGN;
@@ -1091,12 +1094,12 @@ extern "C" walsh_status walsh_moe_router_tc_fwd(const void* u, int dtype, int64_
   int r;
   if (dtype == WALSH_BF16)
     r = launch_octo_tc05<__nv_bfloat16>(u, ntok, 512, w1, 128,
-                                        octo::EpiRouter<__nv_bfloat16>{(const __nv_bfloat16*)w2, top_k, mask, probs,
+                                        octo::EpiRouter<__nv_bfloat16>{(const __nv_bfloat16*)w2, rr, mask, probs,
                                                                        weights},
                                         s);
   else
     r = launch_octo_tc05<__half>(u, ntok, 512, w1, 128,
-                                 octo::EpiRouter<__half>{(const __half*)w2, top_k, mask, probs, weights}, s);
+                                 octo::EpiRouter<__half>{(const __half*)w2, rr, mask, probs, weights}, s);
   return r == 1 ? WALSH_OK : (r == 0 ? WALSH_ERR_SHAPE : r);
 }
 

@@ -162,11 +162,13 @@ class mHCLlamaBlock(nn.Module):
         ff = self.feed_forward
         if hasattr(ff, "kernel_args"):
             w1t, w2, g, up, d, gam, k, tc = ff.kernel_args(idt)
+            rt = ff.router.routing()
             if record_stats:
-                _, mask, probs, _ = ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True, tc=tc)
+                _, mask, probs, _ = ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True, tc=tc,
+                                            routing=rt)
                 ff._record(mask, probs, B * T)
             else:
-                ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), tc=tc)
+                ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), tc=tc, routing=rt)
         elif hasattr(ff, "forward_site"):
             ff.forward_site(u, x, hmix)
         else:
@@ -329,12 +331,32 @@ class mHCWalsh(nn.Module):
         self._graphs_on = bool(enabled)
         self.__dict__["_walsh_graphs"] = {}
 
+    def set_moe_routing(self, mode: str = "topk"):
+        """Expert selection of every MoE layer: "topk" (the reference's forward,
+        src/model/moe.py:432-436) or "threshold" (every expert with router
+        probability above config.moe_threshold, at least moe_min_experts and
+        at most moe_max_experts; the rule src/model/moe.py:383-403 documents).
+        Captured CUDA graphs are dropped, since they hold the rule."""
+        if mode not in ("topk", "threshold"):
+            raise ValueError(f"routing mode must be 'topk' or 'threshold', got {mode!r}")
+        for layer in self.layers:
+            ff = layer.feed_forward
+            if hasattr(ff, "router"):
+                ff.router.routing_mode = mode
+        self.__dict__["_walsh_graphs"] = {}
+
     def _param_key(self):
         return tuple((p.data_ptr(), p._version) for p in self.parameters())
 
+    def _graph_key(self, idx, start_pos):
+        """Cache key of a captured forward: ids shape, start_pos, activation
+        dtype, device and the experts' selection rule of every layer."""
+        rule = tuple(getattr(getattr(l.feed_forward, "router", None), "routing_mode", None) for l in self.layers)
+        return (tuple(idx.shape), start_pos, self._act_dtype(), idx.device, rule)
+
     def _graph_forward(self, idx, start_pos):
         graphs = self.__dict__.setdefault("_walsh_graphs", {})
-        key = (tuple(idx.shape), start_pos, self._act_dtype(), idx.device)
+        key = self._graph_key(idx, start_pos)
         pkey = self._param_key()
         ent = graphs.get(key)
         if ent is not None and ent["params"] != pkey:

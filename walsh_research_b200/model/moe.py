@@ -79,8 +79,11 @@ class FastMoEExperts(nn.Module):
 
 class HadamardRouter(nn.Module):
     """softmax(W2 SiLU(W1 x)) with top-k selection (src/model/moe.py:383-447).
-    ``threshold`` and ``min_experts`` are stored but, as in the reference, the
-    selection is top-k with k = min(max_experts, n_experts)."""
+    ``threshold`` and ``min_experts`` are stored and, by default, unused: as in
+    the reference, the selection is top-k with k = min(max_experts,
+    n_experts).  ``routing_mode = "threshold"`` switches to the rule the
+    reference's docstring describes: every expert with p > threshold, at least
+    min_experts and at most k of them (opt-in; not the reference's forward)."""
 
     def __init__(self, n_embd: int, n_experts: int = 8, threshold: float = 0.1, min_experts: int = 1,
                  max_experts: int = 4):
@@ -95,10 +98,20 @@ class HadamardRouter(nn.Module):
         for m in self.gate:
             if isinstance(m, nn.Linear):
                 nn.init.normal_(m.weight, std=0.01)
+        self.routing_mode = "topk"
 
     @property
     def top_k(self) -> int:
         return min(self.max_experts, self.n_experts)
+
+    def routing(self):
+        """The kernels' selection rule: None for the reference's top-k, or
+        (min_experts, threshold) in threshold mode."""
+        if self.routing_mode == "topk":
+            return None
+        if self.routing_mode == "threshold":
+            return (max(1, min(int(self.min_experts), self.top_k)), float(self.threshold))
+        raise ValueError(f"routing_mode must be 'topk' or 'threshold', got {self.routing_mode!r}")
 
     def weights_dev(self):
         """(W1 transposed [C, C/4], W2 [E, C/4]) float32 on the device."""
@@ -115,7 +128,8 @@ class HadamardRouter(nn.Module):
     def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         w1t, w2 = self.weights_dev()
         tc = self.weights_tc(x.dtype) + (None, None, None) if x.dtype != torch.float32 else None
-        _, mask, probs, weights = ops.moe(x, w1t, w2, None, None, None, None, self.top_k, want_stats=True, tc=tc)
+        _, mask, probs, weights = ops.moe(x, w1t, w2, None, None, None, None, self.top_k, want_stats=True, tc=tc,
+                                          routing=self.routing())
         return weights, mask.float(), probs
 
 
@@ -173,7 +187,8 @@ class HadamardMoE(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, C = x.shape
         w1t, w2, g, u, d, gam, k, tc = self.kernel_args(x.dtype)
-        y, mask, probs, _ = ops.moe(x, w1t, w2, g, u, d, gam, k, want_stats=True, tc=tc)
+        y, mask, probs, _ = ops.moe(x, w1t, w2, g, u, d, gam, k, want_stats=True, tc=tc,
+                                    routing=self.router.routing())
         self._record(mask, probs, B * T)
         return y
 

@@ -181,12 +181,26 @@ def _ones(n, device):
     return _ONES[key]
 
 
-def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=None, want_stats=False, tc=None):
+def routing_struct(routing):
+    """ctypes pointer for an expert-selection rule: None (the reference's
+    top-k) or (min_experts, threshold) for the threshold rule."""
+    if routing is None:
+        return None
+    kmin, thr = routing
+    return ctypes.byref(_lib.MoeRouting(_lib.ROUTE_THRESHOLD, int(kmin), float(thr)))
+
+
+def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=None, want_stats=False, tc=None,
+        routing=None):
     """Router + experts.  With ``fuse=(x, hmix, x_out)`` the mHC epilogue is
     applied and ``x_out`` returned; otherwise the expert output y.
     With ``want_stats`` also returns (mask uint8, probs, weights).
-    ``tc``: (w1, w2, gate, up, down) bfloat16 copies enabling the tensor-core kernel."""
+    ``tc``: (w1, w2, gate, up, down) bfloat16 copies enabling the tensor-core kernel.
+    ``routing``: None for the reference's top-k selection, or (min_experts,
+    threshold) for the threshold rule (every expert with p > threshold, at
+    least min_experts, at most top_k)."""
     require_cuda(u)
+    rt = routing_struct(routing)
     tcs = None
     if tc is not None:
         tcs = _lib.MoeTcWeights(*[ptr(t) for t in tc[:5]])
@@ -213,7 +227,7 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
         call("walsh_moe_hidden_fwd", ptr(u), ptr(hpre), dcode(u.dtype), ntok, C, int(top_k), ptr(w2), ptr(gate_p),
              ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0 if fuse is None else 1, ptr(x),
              dcode(x.dtype) if x is not None else dcode(u.dtype), ptr(hmix), ptr(x_out), ptr(mask), ptr(probs),
-             ptr(weights), stream())
+             ptr(weights), rt, stream())
         out = y if fuse is None else x_out
         return (out, mask, probs, weights) if want_stats else out
     if (MOE_TC05 and tc is not None and len(tc) > 5 and gate_p is not None and weights_in is None
@@ -226,7 +240,7 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
             probs = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
             weights = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
         call("walsh_moe_router_tc_fwd", ptr(u), dcode(u.dtype), ntok, ptr(tc[0]), ptr(tc[1]), int(top_k), ptr(mask),
-             ptr(probs), ptr(weights), stream())
+             ptr(probs), ptr(weights), rt, stream())
         x, hmix, x_out = fuse if fuse is not None else (None, None, None)
         y = torch.empty_like(u) if fuse is None else None
         call("walsh_moe_experts_tc_fwd", ptr(u), dcode(u.dtype), ntok, ptr(weights), ptr(tc[5]), ptr(tc[4]),
@@ -238,13 +252,13 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
         y = torch.empty_like(u)
         call("walsh_moe_fwd", ptr(u), dcode(u.dtype), ntok, C, int(top_k), ptr(w1t), ptr(w2), ptr(gate_p),
              ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0, None, dcode(u.dtype), None, None, ptr(weights_in),
-             ptr(mask), ptr(probs), ptr(weights), tcp, stream())
+             ptr(mask), ptr(probs), ptr(weights), tcp, rt, stream())
         out = y
     else:
         x, hmix, x_out = fuse
         call("walsh_moe_fwd", ptr(u), dcode(u.dtype), ntok, C, int(top_k), ptr(w1t), ptr(w2), ptr(gate_p),
              ptr(up_p), ptr(down_p), ptr(gammas), None, 1, ptr(x), dcode(x.dtype), ptr(hmix), ptr(x_out),
-             ptr(weights_in), ptr(mask), ptr(probs), ptr(weights), tcp, stream())
+             ptr(weights_in), ptr(mask), ptr(probs), ptr(weights), tcp, rt, stream())
         out = x_out
     return (out, mask, probs, weights) if want_stats else out
 
