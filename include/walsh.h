@@ -198,10 +198,18 @@ walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const 
                            float map_eps, const float* norm_w, float norm_eps, void* u, int u_dtype,
                            float* hmix, void* stream);
 
-/* Status word of the single-pass map kernel's bounded TMA wait (0 or
+/* Status word of the single-pass map kernels' bounded TMA waits (0 or
  * WALSH_ERR_TIMEOUT); synchronous read, reset != 0 clears it.  No counterpart
  * in the reference. */
 int walsh_map_error(int reset);
+
+/* Kernel choice of walsh_mhc_map for C = 512, 16-bit x and at least 9472
+ * tokens when phi_frag is given: on != 0 the persistent pipelined
+ * single-pass kernel (x read from HBM once; the default), 0 the two-pass
+ * tensor-core kernel (x read twice).  on < 0 only queries.  Returns the
+ * previous setting.  Process-wide; for comparisons.  No counterpart in the
+ * reference. */
+int walsh_map_set_pipe(int on);
 
 /* Site epilogue: x_out[i] = sum_j H_res[i][j] x[j] + H_post[i] f for each
  * token (x, x_out: [ntok, 4, C]; f: [ntok, C]; x_out may alias x).

@@ -165,15 +165,19 @@ def test_stream_mapping():
 
 @pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("kernel,ntok,C", [("two_pass", 10000, 512), ("single_pass", 9000, 512),
-                                           ("single_pass", 37, 512), ("single_pass", 37, 2048)])
+                                           ("single_pass", 37, 512), ("single_pass", 37, 2048),
+                                           ("pipelined", 10000, 512), ("pipelined", 150 * 16 * 5 + 7, 512)])
 def test_tensor_core_mapping_vs_oracle(xdt, kernel, ntok, C):
     """The tensor-core site prologues for either 16-bit stream type: the
-    two-pass kernel (chosen from 9472 tokens up) and the single-pass TMA
-    kernel (phi in fragment order; below 9472 tokens, ragged last tile):
-    H_pre/H_post/H_res vs the oracle on the same rounded stream values, and
-    the pre-mixed, normed u."""
+    two-pass kernel (from 9472 tokens without phi fragments, or with the
+    pipelined kernel switched off), the single-pass TMA kernel (phi in
+    fragment order; below 9472 tokens, ragged last tile) and the persistent
+    pipelined single-pass kernel (from 9472 tokens; several tiles per CTA and
+    passes round the buffer ring, ragged last tile): H_pre/H_post/H_res vs the
+    oracle on the same rounded stream values, and the pre-mixed, normed u."""
     from walsh_research_b200 import _lib
     from walsh_research_b200 import ops
+    assert _lib.call("walsh_map_set_pipe", -1) == 1
     from walsh_research_b200.model.mhc import MAP_EPS, ResidualStreamMapping, mHCResidualStream, site_params
     rng = np.random.default_rng(41)
     st = mHCResidualStream(C, 4)
@@ -188,8 +192,18 @@ def test_tensor_core_mapping_vs_oracle(xdt, kernel, ntok, C):
     phi, mp, phil, phif = site_params(st, xdt)
     _lib.call("walsh_map_error", 1)
     u, hmix = ops.mhc_map(x, phi, mp, MAP_EPS, nw, 1e-6, phi_lp=phil, u_dtype=torch.float16,
-                          phi_frag=phif if kernel == "single_pass" else None)
+                          phi_frag=None if kernel == "two_pass" else phif)
     torch.cuda.synchronize()
+    if kernel == "pipelined":
+        # against the two-pass kernel on the same input: both are within the
+        # oracle tolerances below, and they agree to fp16 rounding of u
+        _lib.call("walsh_map_set_pipe", 0)
+        try:
+            u2, hmix2 = ops.mhc_map(x, phi, mp, MAP_EPS, nw, 1e-6, phi_lp=phil, u_dtype=torch.float16, phi_frag=phif)
+        finally:
+            _lib.call("walsh_map_set_pipe", 1)
+        assert float((hmix - hmix2).abs().max()) < 1e-4
+        assert rel(u, u2.float().cpu().numpy()) < 2e-3
     assert _lib.call("walsh_map_error", 1) == 0
     xf = x.float().cpu().numpy().astype(np.float64).reshape(1, ntok, 4 * C)
     p = {k: v.detach().cpu().numpy() for k, v in st.state_dict().items()}

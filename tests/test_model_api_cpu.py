@@ -141,3 +141,22 @@ def test_split3_weight_layout_cpu():
     y = torch.cat([x_hi, x_hi, x_lo], 1).double() @ w3.double().t()
     ref = x.double() @ w.double().t()
     assert float((y - ref).abs().max() / ref.abs().max()) < 1e-4
+
+
+def test_sampling_step_matches_the_reference_rule():
+    """mHCWalsh._sample on CPU logits against the reference's own steps
+    (temperature, top-k mask, softmax, multinomial) with the same generator."""
+    import torch.nn.functional as F
+    from walsh_research_b200.model.mhc import mHCWalsh
+    logits = torch.randn(5, 300, generator=torch.Generator().manual_seed(0)) * 3
+    for temp, k in ((1.0, None), (0.7, 20), (1.3, 1), (0.5, 0)):
+        got = mHCWalsh._sample(logits, temp, k, torch.Generator().manual_seed(7))
+        z = logits / temp
+        if k is not None and k > 0:
+            v, _ = torch.topk(z, min(k, z.size(-1)))
+            z = z.clone()
+            z[z < v[:, [-1]]] = -float("Inf")
+        want = torch.multinomial(F.softmax(z, dim=-1), num_samples=1, generator=torch.Generator().manual_seed(7))
+        assert torch.equal(got, want)
+        if k == 1:
+            assert torch.equal(got[:, 0], logits.argmax(-1))

@@ -36,6 +36,7 @@ SIGNATURES = {
     "walsh_attn_out_tc_fwd": [P, c_int64, P, P, P, P, P, P, c_int, P, P, P],
     "walsh_mhc_map": [P, c_int, c_int64, c_int, P, P, P, P, c_float, P, c_float, P, c_int, P, P],
     "walsh_map_error": [c_int],
+    "walsh_map_set_pipe": [c_int],
     "walsh_mhc_post": [P, P, P, c_int, c_int64, c_int, P, P],
     "walsh_sinkhorn": [P, c_int64, c_int, c_float, P, P],
     "walsh_moe_fwd": [P, c_int, c_int64, c_int, c_int, P, P, P, P, P, P, P, c_int, P, c_int, P, P, P, P, P, P, P,
@@ -73,12 +74,12 @@ _RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_chmod_mlp_tc_scratch_byt
 KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_octo_set_mainloop": 0,
                     "walsh_chmod_mlp_tc": 3, "walsh_chmod_mlp_tc_scratch_bytes": 0,
                     "walsh_linear_split_tc_fwd": 2, "walsh_linear_split_tc_scratch_bytes": 0,
-                    "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
+                    "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_map_set_pipe": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
                     "walsh_abi_version": 0}
 launch_count = 0
 # entry points that return a plain int rather than a status
 _PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows", "walsh_octo_set_mainloop", "walsh_tc05_error",
-              "walsh_map_error", "walsh_attn_set_path"}
+              "walsh_map_error", "walsh_attn_set_path", "walsh_map_set_pipe"}
 
 
 class MoeTcWeights(ctypes.Structure):

@@ -537,6 +537,260 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill-sized mapping (C = 512, 16-bit x), x read from HBM once.  One CTA
+// per SM walks 16-token tiles (a tile's stream rows are one contiguous 64 KB
+// block).  The rows come through a ring of STAGES shared-memory buffers, one
+// bulk copy (cp.async.bulk, completing on the stage's mbarrier) per 4 KB
+// token row into rows padded by 16 bytes so that ldmatrix's eight rows fall
+// in distinct banks; thread 0 refills a stage with the tile STAGES ahead as
+// soon as the stage is released, so the next tiles' loads run while the
+// current one is computed.  Sixteen main warps do, per tile:
+//   1. projections and sum of squares on the tensor cores from shared memory,
+//      each warp a 128-column slice of the 16 tokens (the slice's phi
+//      fragments stay in registers for all tiles), partials to shared memory;
+//   2. warp w then adds token w's 16 partials (lane v: index v, warp order),
+//      takes the RMS factor, H_pre / H_post, the pre-exponential H_res logits
+//      (posted to shared memory for the Sinkhorn warp) and the pre-mix
+//      u = sum_j H_pre[j] x_j with the block RMSNorm, reading the stream rows
+//      from the ring buffer, which is then refilled with the tile STAGES ahead.
+// A 17th warp runs the 16 tokens' Sinkhorn of each tile (one token per lane,
+// in registers) while the main warps go on with the next tile; two named
+// barriers hand the logits over (full: main warps arrive, Sinkhorn warp
+// waits; empty: the reverse).  Every mbarrier wait is bounded: if one runs
+// out, the main warps record WALSH_ERR_TIMEOUT (walsh_map_error), release
+// the Sinkhorn warp through the same barriers with an abort flag, wait
+// (bounded) for the copies they have in flight and return.
+// Measured at 65 536 tokens: with the Sinkhorn on warp 0, 182 us (45 of them
+// Sinkhorn); the Sinkhorn warp with 16-byte cp.async loads, 140 us; a TMA form
+// of the ring (32 boxes of 64 columns x 16 rows per tile), 190 us; the
+// two-pass kernel 142 us.
+// ---------------------------------------------------------------------------
+namespace map_pipe {
+constexpr int STAGES = 3, TOK = 16, NW = 16, THREADS = (NW + 1) * 32, C = 512, D = 4 * C;
+constexpr int ROWB = D * 2 + 16;             // bytes per token row in shared memory (padded)
+constexpr int STAGE_BYTES = TOK * ROWB;
+constexpr int RS = kMapRows + 1;             // partial row: 24 projections + sum of squares
+constexpr int RED_FLOATS = NW * TOK * RS;    // [warp][token][RS]
+constexpr int SMEM = STAGES * STAGE_BYTES + RED_FLOATS * 4 + TOK * 16 * 4 + STAGES * 8 + 16 + 128;
+// named barriers (0 is __syncthreads): main warps only; logits full; logits empty
+constexpr int BAR_MAIN = 1, BAR_FULL = 2, BAR_EMPTY = 3;
+}  // namespace map_pipe
+
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory");
+}
+// named barrier that also returns whether any participating thread passed p
+__device__ __forceinline__ bool named_sync_or(int id, int n, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n"
+      ".reg .pred pi, po;\n"
+      "setp.ne.u32 pi, %1, 0;\n"
+      "bar.red.or.pred po, %2, %3, pi;\n"
+      "selp.u32 %0, 1, 0, po;\n"
+      "}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+template <typename TX, typename TU>
+__global__ void __launch_bounds__(map_pipe::THREADS, 1)
+mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restrict__ phif,
+                    const float* __restrict__ mp, float map_eps, const float* __restrict__ norm_w, float norm_eps,
+                    TU* __restrict__ u, float* __restrict__ hmix) {
+  using namespace map_pipe;
+  constexpr int KS = D / 16 / NW;  // k-steps per warp (8)
+  constexpr int VPL = C / 256;     // 16-byte chunks per lane and stream row
+  constexpr int MT = NW * 32;      // main threads
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* ring = smem_raw;
+  float* red = reinterpret_cast<float*>(ring + STAGES * STAGE_BYTES);  // [NW][TOK][RS]
+  float* hres = red + RED_FLOATS;                                      // [TOK][16] H_res logits
+  uint64_t* bar = reinterpret_cast<uint64_t*>(hres + TOK * 16);        // [STAGES] stage full
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + STAGES);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+  const int64_t ntiles = (ntok + TOK - 1) / TOK;
+  if (tid == 0) {
+    for (int st = 0; st < STAGES; ++st) tc05::mbar_init(bar + st, 1);
+    tc05::fence_barrier_init();
+    *abort_flag = 0;
+  }
+  __syncthreads();
+
+  if (warp == NW) {
+    // ---- the Sinkhorn warp
+    named_arrive(BAR_EMPTY, THREADS);  // the logits buffer starts empty
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      named_sync(BAR_FULL, THREADS);
+      if (*abort_flag) return;
+      float M[16];
+      if (lane < TOK) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) M[q] = hres[lane * 16 + q];
+      }
+      // the main warps wait for this before writing the next tile's logits
+      // (no arrival after the last tile: every barrier phase completes)
+      if (tile + gridDim.x < ntiles) named_arrive(BAR_EMPTY, THREADS);
+      const int64_t tk = tile * TOK + lane;
+      if (lane < TOK && tk < ntok) {
+        sinkhorn4(M, 20, 1e-8f);
+        float4* hd = reinterpret_cast<float4*>(hmix + tk * kMapRows + 8);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) hd[q] = make_float4(M[4 * q], M[4 * q + 1], M[4 * q + 2], M[4 * q + 3]);
+      }
+    }
+    return;
+  }
+
+  // ---- the main warps
+  // thread 0 fills stage st with the tile's valid token rows (rows past ntok
+  // keep stale values; their results are never stored)
+  auto load = [&](int st, int64_t tile) {
+    if (tid == 0 && tile < ntiles) {
+      const int rows = (int)min64(TOK, ntok - tile * TOK);
+      tc05::mbar_arrive_expect_tx(bar + st, (uint32_t)rows * (D * 2));
+      for (int r = 0; r < rows; ++r)
+        tc05::bulk_load(ring + st * STAGE_BYTES + r * ROWB, x + (tile * TOK + r) * D, D * 2, bar + st);
+    }
+  };
+#pragma unroll
+  for (int st = 0; st < STAGES; ++st) load(st, blockIdx.x + (int64_t)st * gridDim.x);
+  // this warp's phi fragments: its column slice is the same for every tile,
+  // so they are loaded once and stay in registers
+  uint2 fr[KS][3];
+#pragma unroll
+  for (int j = 0; j < KS; ++j) {
+    const uint2* fp = phif + ((size_t)(warp * KS + j) * 32 + lane) * 3;
+    fr[j][0] = __ldg(fp);
+    fr[j][1] = __ldg(fp + 1);
+    fr[j][2] = __ldg(fp + 2);
+  }
+  // lane constants of step 2 (lane v serves partial index v of the warp's token)
+  const float a_pre = __ldg(mp + 0), a_post = __ldg(mp + 1), a_res = __ldg(mp + 2);
+  const float b_lane = lane < 4 ? __ldg(mp + 4 + lane)
+                                : (lane < 8 ? __ldg(mp + 8 + (lane - 4)) : (lane < 24 ? __ldg(mp + 12 + (lane - 8)) : 0.f));
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+    const int st = it % STAGES;
+    const int64_t tok0 = tile * TOK;
+    const unsigned char* xs = ring + st * STAGE_BYTES;
+    const bool ok = tc05::mbar_wait(bar + st, (uint32_t)(it / STAGES) & 1u);
+    if (named_sync_or(BAR_MAIN, MT, !ok)) {
+      // release the Sinkhorn warp (its logits-buffer arrival for this tile is
+      // in), then wait (bounded) for this CTA's copies in flight
+      named_sync(BAR_EMPTY, THREADS);
+      if (tid == 0) {
+        *abort_flag = 1;
+        atomicExch(&g_map_tma_error, (int)WALSH_ERR_TIMEOUT);
+      }
+      named_arrive(BAR_FULL, THREADS);
+      if (tid == 0)
+        for (int k = 0; k < STAGES; ++k) {
+          const int64_t t2 = tile + (int64_t)k * gridDim.x;
+          if (t2 < ntiles) tc05::mbar_wait(bar + (it + k) % STAGES, (uint32_t)((it + k) / STAGES) & 1u, 200000000LL);
+        }
+      return;
+    }
+    // 1. partial projections over this warp's columns
+    float acc[3][4];
+#pragma unroll
+    for (int n = 0; n < 3; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    float ss_lo = 0.f, ss_hi = 0.f;
+    const uint32_t xbase = tc05::smem_u32(xs);
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+      const int ks = warp * KS + j;
+      const int rr = lane & 15, col = ks * 16 + (lane >> 4) * 8;
+      uint32_t a[4];
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                   : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                   : "r"(xbase + (uint32_t)(rr * ROWB + col * 2)));
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 v = unpack2<TX>(a[q]);
+        if (q & 1) ss_hi = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_hi));
+        else ss_lo = fmaf(v.x, v.x, fmaf(v.y, v.y, ss_lo));
+      }
+      mma16<TX>(acc[0], a, fr[j][0].x, fr[j][0].y);
+      mma16<TX>(acc[1], a, fr[j][1].x, fr[j][1].y);
+      mma16<TX>(acc[2], a, fr[j][2].x, fr[j][2].y);
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      ss_lo += __shfl_xor_sync(0xffffffffu, ss_lo, off);
+      ss_hi += __shfl_xor_sync(0xffffffffu, ss_hi, off);
+    }
+    float* rw = red + warp * TOK * RS;
+#pragma unroll
+    for (int n = 0; n < 3; ++n) {
+      rw[g * RS + 8 * n + 2 * t4] = acc[n][0];
+      rw[g * RS + 8 * n + 2 * t4 + 1] = acc[n][1];
+      rw[(g + 8) * RS + 8 * n + 2 * t4] = acc[n][2];
+      rw[(g + 8) * RS + 8 * n + 2 * t4 + 1] = acc[n][3];
+    }
+    if (t4 == 0) {
+      rw[g * RS + kMapRows] = ss_lo;
+      rw[(g + 8) * RS + kMapRows] = ss_hi;
+    }
+    named_sync(BAR_MAIN, MT);  // partials complete
+    // 2. this warp's token: lane v < 25 adds partial v over the 16 warps in order
+    const int t = warp;
+    const int64_t tok = tok0 + t;
+    float d = 0.f;
+    if (lane < RS) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) d += red[(w * TOK + t) * RS + lane];
+    }
+    const float rms = rsqrtf(__shfl_sync(0xffffffffu, d, kMapRows) / (float)D + map_eps);
+    const float dn = d * rms;
+    float hph = 0.f;
+    if (lane < 4) hph = 1.0f / (1.0f + expf(-(a_pre * dn + b_lane)));
+    else if (lane < 8) hph = 2.0f * (1.0f / (1.0f + expf(-(a_post * dn + b_lane))));
+    if (lane < 8 && tok < ntok) hmix[tok * kMapRows + lane] = hph;
+    named_sync(BAR_EMPTY, THREADS);  // the Sinkhorn warp has taken the previous tile's logits
+    if (lane >= 8 && lane < 24) hres[t * 16 + (lane - 8)] = a_res * dn + b_lane;
+    named_arrive(BAR_FULL, THREADS);
+    // pre-mix and RMSNorm of the token, its stream rows read from the ring buffer
+    {
+      const float h0 = __shfl_sync(0xffffffffu, hph, 0), h1 = __shfl_sync(0xffffffffu, hph, 1),
+                  h2 = __shfl_sync(0xffffffffu, hph, 2), h3 = __shfl_sync(0xffffffffu, hph, 3);
+      float uv[VPL][8];
+      float s2 = 0.f;
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) {
+        float f[4][8];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          unpack8(*reinterpret_cast<const uint4*>(xs + t * ROWB + (jj * C + (lane + 32 * v) * 8) * 2), f[jj],
+                  (const TX*)nullptr);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uv[v][q] = ((h0 * f[0][q] + h1 * f[1][q]) + h2 * f[2][q]) + h3 * f[3][q];
+          s2 = fmaf(uv[v][q], uv[v][q], s2);
+        }
+      }
+      s2 = warp_sum(s2);
+      const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
+      if (tok < ntok) {
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+          const int cc = (lane + 32 * v) * 8;
+          float o[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) o[q] = uv[v][q] * rn * (norm_w ? __ldg(norm_w + cc + q) : 1.f);
+          store8(u + tok * C + cc, o);
+        }
+      }
+    }
+    named_sync(BAR_MAIN, MT);  // the ring buffer and the partials are free
+    load(st, tile + (int64_t)STAGES * gridDim.x);
+  }
+}
+
 template <typename T>
 __global__ void mhc_post_kernel(const T* x, const T* __restrict__ f, const float* __restrict__ hmix, int64_t ntok,
                                 int C, T* xo) {
@@ -621,6 +875,44 @@ static int launch_map_tma_n(const void* x, int64_t ntok, const void* phi_frag, c
   return st == WALSH_OK ? 1 : st;
 }
 
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+      n = v;
+    else {
+      cudaGetLastError();
+      return 148;
+    }
+  }
+  return n;
+}
+
+// Persistent pipelined kernel for prefill-sized C = 512 calls.
+template <typename TX, typename TU>
+static int launch_map_pipe(const void* x, int64_t ntok, const void* phi_frag, const float* mp, float map_eps,
+                           const float* norm_w, float norm_eps, void* u, float* hmix, cudaStream_t s) {
+  using namespace map_pipe;
+  auto kern = mhc_map_pipe_kernel<TX, TU>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    return launch_status();
+  const int64_t ntiles = (ntok + TOK - 1) / TOK;
+  const int grid = (int)min64(ntiles, num_sms());
+  kern<<<grid, THREADS, SMEM, s>>>((const TX*)x, ntok, (const uint2*)phi_frag, mp, map_eps, norm_w, norm_eps,
+                                   (TU*)u, hmix);
+  return launch_status();
+}
+
+// mapping kernel choice for prefill-sized C = 512 calls: 1 = the pipelined
+// single-pass kernel (default), 0 = the two-pass tensor-core kernel
+static int g_map_pipe = 1;
+extern "C" int walsh_map_set_pipe(int on) {
+  const int old = g_map_pipe;
+  if (on >= 0) g_map_pipe = on ? 1 : 0;
+  return old;
+}
+
 extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, int C, const float* phi,
                                       const void* phi_lp, const void* phi_frag, const float* mparams,
                                       float map_eps, const float* norm_w, float norm_eps, void* u, int u_dtype,
@@ -659,6 +951,19 @@ extern "C" walsh_status walsh_mhc_map(const void* x, int dtype, int64_t ntok, in
     }
 #undef WALSH_MAP_TMA
     if (r != 0) return r > 0 ? WALSH_OK : r;
+  }
+  if (many && g_map_pipe && phi_frag && C == 512 && (dtype == WALSH_BF16 || dtype == WALSH_F16) &&
+      u_dtype != WALSH_F32 && ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_frag)) & 15u) == 0) {
+    if (dtype == WALSH_BF16)
+      return u_dtype == WALSH_F16
+                 ? launch_map_pipe<__nv_bfloat16, __half>(x, ntok, phi_frag, mparams, map_eps, norm_w, norm_eps, u,
+                                                          hmix, s)
+                 : launch_map_pipe<__nv_bfloat16, __nv_bfloat16>(x, ntok, phi_frag, mparams, map_eps, norm_w,
+                                                                 norm_eps, u, hmix, s);
+    return u_dtype == WALSH_F16
+               ? launch_map_pipe<__half, __half>(x, ntok, phi_frag, mparams, map_eps, norm_w, norm_eps, u, hmix, s)
+               : launch_map_pipe<__half, __nv_bfloat16>(x, ntok, phi_frag, mparams, map_eps, norm_w, norm_eps, u,
+                                                        hmix, s);
   }
   const bool vec_ok = ((((uintptr_t)x) | ((uintptr_t)u) | ((uintptr_t)phi_lp)) & 15u) == 0;
   // the two-pass tensor-core kernel takes 128 tokens per CTA: below about a

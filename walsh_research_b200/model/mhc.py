@@ -464,17 +464,55 @@ class mHCWalsh(nn.Module):
             return {}
         return {k: sum(s[k] for s in stats) / len(stats) for k in ("scale_mean", "scale_std", "shift_mean")}
 
+    @staticmethod
+    def _sample(logits, temperature, top_k, generator=None):
+        """One token per row of logits [B, V]: scale by 1/temperature, keep the
+        top_k largest (others to -inf) when top_k is set, softmax, one
+        multinomial draw -- the reference's sampling step
+        (src/model/mhc.py:767-782).  Returns [B, 1] int64 on the logits' device."""
+        z = logits.float() / temperature
+        if top_k is not None and top_k > 0:
+            kth = torch.topk(z, min(int(top_k), z.shape[-1]), dim=-1).values[:, -1:]
+            z = z.masked_fill(z < kth, float("-inf"))
+        return torch.multinomial(F.softmax(z, dim=-1), num_samples=1, generator=generator)
+
     @torch.no_grad()
-    def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None):
-        """Sampling loop with the reference's semantics (src/model/mhc.py:753-789):
-        full re-forward of the (block-size-cropped) context per new token."""
-        for _ in range(max_new_tokens):
-            idx_cond = idx if idx.size(1) <= self.config.block_size else idx[:, -self.config.block_size:]
-            logits, _ = self(idx_cond)
-            logits = logits[:, -1, :] / temperature
-            if top_k is not None and top_k > 0:
-                v, _ = torch.topk(logits, min(top_k, logits.size(-1)))
-                logits[logits < v[:, [-1]]] = -float("Inf")
-            probs = F.softmax(logits, dim=-1)
-            idx = torch.cat((idx, torch.multinomial(probs, num_samples=1)), dim=1)
-        return idx
+    def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None, use_cache=True, generator=None):
+        """Autoregressive sampling, [B, T] -> [B, T + new] token ids, with the
+        reference's per-step rule (temperature, optional top-k, multinomial;
+        src/model/mhc.py:753-789).
+
+        use_cache=True (default): the prompt (its last block_size tokens) is
+        prefilled once into a batched KV cache of block_size positions and each
+        later step forwards only the B new tokens, as the reference's cached
+        Walsh.generate does for one sequence (src/model/chassis.py:600-655);
+        generation stops early once the cache is full.  use_cache=False
+        re-forwards the cropped context for every token, as mHCWalsh.generate
+        does in the reference.  ``generator`` seeds the draws (a
+        torch.Generator on the model's device)."""
+        if max_new_tokens <= 0:
+            return idx
+        bs = self.config.block_size
+        if not use_cache:
+            seq = idx
+            for _ in range(max_new_tokens):
+                logits, _ = self(seq[:, -bs:])
+                seq = torch.cat((seq, self._sample(logits[:, -1, :], temperature, top_k, generator)), dim=1)
+            return seq
+        ctx = idx[:, -bs:]
+        B, T = ctx.shape
+        C, H = self.config.n_embd, self.config.n_head
+        cache = KVCache(self.config.n_layer, bs, H, C // H, idx.device, dtype=_lib.inner_dtype(self._act_dtype()),
+                        batch_size=B)
+        logits, _ = self(ctx, kv_cache=cache, start_pos=0)
+        cache.increment(T)
+        nxt = self._sample(logits[:, -1, :], temperature, top_k, generator)
+        out = [idx, nxt]
+        for _ in range(max_new_tokens - 1):
+            if cache.cached_len >= bs:
+                break
+            logits, _ = self(nxt, kv_cache=cache, start_pos=cache.cached_len)
+            cache.increment(1)
+            nxt = self._sample(logits[:, -1, :], temperature, top_k, generator)
+            out.append(nxt)
+        return torch.cat(out, dim=1)
