@@ -581,6 +581,47 @@ __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sy
 __device__ __forceinline__ void named_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory");
 }
+// packed pairs of floats (lo in the low word) for the f32x2 pipe
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2unpack(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(lo), "=f"(hi) : "l"(v));
+  return make_float2(lo, hi);
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// a 16-bit pair (lo in the low half) as a packed float pair
+template <typename T16>
+__device__ __forceinline__ uint64_t f2from16(uint32_t w) {
+  const float2 f = unpack2<T16>(w);
+  return f2pack(f.x, f.y);
+}
+template <>
+__device__ __forceinline__ uint64_t f2from16<__nv_bfloat16>(uint32_t w) {
+  // a bfloat16 is the upper half of the float with the same value
+  return (uint64_t)(w << 16) | ((uint64_t)(w & 0xffff0000u) << 32);
+}
+// a packed float pair rounded to a 16-bit pair (fp16: saturating, as from_f)
+template <typename TU>
+__device__ __forceinline__ uint32_t f2to16(uint64_t v) {
+  const float2 f = f2unpack(v);
+  return pack2<TU>(f.x, f.y);
+}
+template <>
+__device__ __forceinline__ uint32_t f2to16<float>(uint64_t) { return 0; }  // not used (u is 16-bit here)
+
 // named barrier that also returns whether any participating thread passed p
 __device__ __forceinline__ bool named_sync_or(int id, int n, bool p) {
   uint32_t r;
@@ -754,35 +795,52 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
     named_sync(BAR_EMPTY, THREADS);  // the Sinkhorn warp has taken the previous tile's logits
     if (lane >= 8 && lane < 24) hres[t * 16 + (lane - 8)] = a_res * dn + b_lane;
     named_arrive(BAR_FULL, THREADS);
-    // pre-mix and RMSNorm of the token, its stream rows read from the ring buffer
+    // pre-mix and RMSNorm of the token, its stream rows read from the ring buffer;
+    // element pairs on the f32x2 pipe, products and sums in the order of the
+    // scalar form ((h0 x0 + h1 x1) + h2 x2) + h3 x3
     {
       const float h0 = __shfl_sync(0xffffffffu, hph, 0), h1 = __shfl_sync(0xffffffffu, hph, 1),
                   h2 = __shfl_sync(0xffffffffu, hph, 2), h3 = __shfl_sync(0xffffffffu, hph, 3);
-      float uv[VPL][8];
-      float s2 = 0.f;
+      const uint64_t h02 = f2pack(h0, h0), h12 = f2pack(h1, h1), h22 = f2pack(h2, h2), h32 = f2pack(h3, h3);
+      uint64_t uv[VPL][4];
+      uint64_t s2a = f2pack(0.f, 0.f), s2b = s2a;
 #pragma unroll
       for (int v = 0; v < VPL; ++v) {
-        float f[4][8];
+        uint4 xq[4];
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj)
-          unpack8(*reinterpret_cast<const uint4*>(xs + t * ROWB + (jj * C + (lane + 32 * v) * 8) * 2), f[jj],
-                  (const TX*)nullptr);
+          xq[jj] = *reinterpret_cast<const uint4*>(xs + t * ROWB + (jj * C + (lane + 32 * v) * 8) * 2);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uv[v][q] = ((h0 * f[0][q] + h1 * f[1][q]) + h2 * f[2][q]) + h3 * f[3][q];
-          s2 = fmaf(uv[v][q], uv[v][q], s2);
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t w0 = (&xq[0].x)[q], w1 = (&xq[1].x)[q], w2 = (&xq[2].x)[q], w3 = (&xq[3].x)[q];
+          uint64_t a = f2mul(h02, f2from16<TX>(w0));
+          a = f2fma(h12, f2from16<TX>(w1), a);
+          a = f2fma(h22, f2from16<TX>(w2), a);
+          a = f2fma(h32, f2from16<TX>(w3), a);
+          uv[v][q] = a;
+          if (q & 1) s2b = f2fma(a, a, s2b);
+          else s2a = f2fma(a, a, s2a);
         }
       }
-      s2 = warp_sum(s2);
+      const float2 sa = f2unpack(s2a), sb = f2unpack(s2b);
+      const float s2 = warp_sum((sa.x + sa.y) + (sb.x + sb.y));
       const float rn = norm_w ? rsqrtf(s2 / (float)C + norm_eps) : 1.0f;
+      const uint64_t rn2 = f2pack(rn, rn);
       if (tok < ntok) {
 #pragma unroll
         for (int v = 0; v < VPL; ++v) {
           const int cc = (lane + 32 * v) * 8;
-          float o[8];
+          float4 nwa = make_float4(1.f, 1.f, 1.f, 1.f), nwb = nwa;
+          if (norm_w) {
+            nwa = __ldg(reinterpret_cast<const float4*>(norm_w + cc));
+            nwb = __ldg(reinterpret_cast<const float4*>(norm_w + cc + 4));
+          }
+          const uint64_t nw2[4] = {f2pack(nwa.x, nwa.y), f2pack(nwa.z, nwa.w), f2pack(nwb.x, nwb.y),
+                                   f2pack(nwb.z, nwb.w)};
+          uint32_t w[4];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) o[q] = uv[v][q] * rn * (norm_w ? __ldg(norm_w + cc + q) : 1.f);
-          store8(u + tok * C + cc, o);
+          for (int q = 0; q < 4; ++q) w[q] = f2to16<TU>(f2mul(f2mul(uv[v][q], rn2), nw2[q]));
+          *reinterpret_cast<uint4*>(u + tok * C + cc) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
     }
