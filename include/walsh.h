@@ -487,6 +487,66 @@ walsh_status walsh_chmod_fwd_noalloc(const void* x, int dtype, int64_t nrows, in
                                      const float* scale_temp, float residual_scale, int add_input,
                                      void* out, void* stream);
 
+/* Part of the tensor-core expert kernel of walsh_moe_experts_tc_fwd: only
+ * experts first_expert .. first_expert + n_experts - 1 (whole quarters of 4
+ * containing them are evaluated), output y [ntok, 512] in u's dtype with
+ * only those quarters' columns written.  For expert parallelism, where a
+ * rank evaluates the experts it owns over the rows it received.
+ * Replaces FastMoEExperts.forward (src/model/moe.py:337-380) for a subset
+ * of the experts. */
+walsh_status walsh_moe_experts_tc_part_fwd(const void* u, int dtype, int64_t ntok, const float* weights,
+                                           const void* w_gu, const void* w_down, const float* gammas,
+                                           int first_expert, int n_experts, void* y, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Expert parallelism over NVLink (HadamardMoE, src/model/moe.py:512-542: expert
+ * e consumes and produces only feature block e, lines 536-541).
+ *
+ * world ranks (one per GPU, world <= 8) each hold ntok tokens (the same ntok
+ * on every rank); rank j owns experts [j E/world, (j + 1) E/world), E = C/32.
+ * Each rank allocates, in memory its peers can write (walsh_ipc_*), recv_u
+ * [world * ntok, C] (u's dtype), recv_w float [world * ntok, E], y_full
+ * [ntok, C] (u's dtype) and flags uint32 [2 * world] (zeroed once); and, in
+ * its own memory, counters uint32 [2 * world] (zeroed once).  The peer_*
+ * arguments are host arrays of world device pointers (this rank's own
+ * buffer at index `rank`).  `epoch` (non-zero, the same on every rank, new
+ * for every exchange) is the value written to the flags.
+ *
+ * walsh_ep_dispatch: rows of u and of the routing weights (float [ntok, E])
+ * to every rank: the columns of rank j's experts into rank j's recv_u rows
+ * rank * ntok .. + ntok - 1, the weights (zero outside rank j's experts)
+ * into its recv_w; then flags[rank] = epoch on rank j.
+ * walsh_ep_combine: y [world * ntok, C], this rank's experts' outputs over
+ * its received rows, back to the owners of the tokens: the columns of this
+ * rank's experts of rows j * ntok .. into rank j's y_full; then flags[world
+ * + rank] = epoch on rank j.
+ * walsh_ep_wait: one small kernel waiting until flags[first .. first + n - 1]
+ * all equal epoch, for at most timeout_cycles SM clock cycles; on expiry it
+ * writes WALSH_ERR_TIMEOUT to *status (device int) and returns, so that the
+ * host reads the failure at its next synchronisation.
+ * The exchange kernels use plain 16-byte stores to peer memory and a system-
+ * scope release of the flag; no TMA and no multicast.  No counterpart in the
+ * reference (its MoE runs on one device). */
+walsh_status walsh_ep_dispatch(const void* u, int dtype, int64_t ntok, int C, const float* weights, int rank,
+                               int world, void* const* peer_recv_u, float* const* peer_recv_w,
+                               uint32_t* const* peer_flags, uint32_t* counters, uint32_t epoch, void* stream);
+walsh_status walsh_ep_combine(const void* y, int dtype, int64_t ntok, int C, int rank, int world,
+                              void* const* peer_y, uint32_t* const* peer_flags, uint32_t* counters,
+                              uint32_t epoch, void* stream);
+walsh_status walsh_ep_wait(const uint32_t* flags, int first, int n, uint32_t epoch, long long timeout_cycles,
+                           int* status, void* stream);
+
+/* CUDA IPC plumbing for the exchange buffers.  walsh_ipc_handle: the handle
+ * (walsh_ipc_handle_bytes() bytes) of the allocation dev_ptr lies in, and
+ * dev_ptr's byte offset in it (pooling allocators hand out sub-ranges).
+ * walsh_ipc_open: the mapping of such a handle in another process (peer
+ * access enabled on first use): *dev_ptr_out = base + offset, *base_out =
+ * the mapping to pass to walsh_ipc_close.  No counterpart in the reference. */
+walsh_status walsh_ipc_handle(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+walsh_status walsh_ipc_open(const void* handle, int64_t offset, void** dev_ptr_out, void** base_out);
+walsh_status walsh_ipc_close(void* base);
+int walsh_ipc_handle_bytes(void);
+
 /* ---------------------------------------------------------------------------
  * Dense helpers around the layer stack
  * ------------------------------------------------------------------------- */

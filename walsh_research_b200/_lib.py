@@ -67,15 +67,24 @@ SIGNATURES = {
     "walsh_linear_fwd": [P, c_int, c_int64, c_int, c_int64, P, c_int, c_int64, P, P, c_int, P],
     "walsh_linear_split_fwd": [P, c_int, c_int64, c_int, c_int64, P, P, c_int64, P, P, P],
     "walsh_rmsnorm": [P, c_int, c_int64, c_int, P, c_float, P, c_int, P],
+    "walsh_moe_experts_tc_part_fwd": [P, c_int, c_int64, P, P, P, P, c_int, c_int, P, P],
+    "walsh_ep_dispatch": [P, c_int, c_int64, c_int, P, c_int, c_int, P, P, P, P, ctypes.c_uint32, P],
+    "walsh_ep_combine": [P, c_int, c_int64, c_int, c_int, c_int, P, P, P, ctypes.c_uint32, P],
+    "walsh_ep_wait": [P, c_int, c_int, ctypes.c_uint32, ctypes.c_longlong, P, P],
+    "walsh_ipc_handle": [P, P, P],
+    "walsh_ipc_open": [P, c_int64, P, P],
+    "walsh_ipc_close": [P],
+    "walsh_ipc_handle_bytes": [],
 }
-_RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,
+_RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_ipc_handle_bytes": c_int, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,
             "walsh_linear_split_tc_scratch_bytes": ctypes.c_int64}
 # kernels each entry point launches (for the launch accounting reported by bench.py)
 KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_octo_set_mainloop": 0,
                     "walsh_chmod_mlp_tc": 3, "walsh_chmod_mlp_tc_scratch_bytes": 0,
                     "walsh_linear_split_tc_fwd": 2, "walsh_linear_split_tc_scratch_bytes": 0,
                     "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_map_set_pipe": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
-                    "walsh_abi_version": 0}
+                    "walsh_abi_version": 0, "walsh_ipc_handle": 0, "walsh_ipc_open": 0, "walsh_ipc_close": 0,
+                    "walsh_ipc_handle_bytes": 0}
 launch_count = 0
 # entry points that return a plain int rather than a status
 _PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows", "walsh_octo_set_mainloop", "walsh_tc05_error",

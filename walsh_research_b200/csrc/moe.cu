@@ -1097,7 +1097,7 @@ __global__ void __launch_bounds__(moe_tc5::NTHREADS, 1)
 moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_g,
                         const __grid_constant__ CUtensorMap tm_d, int64_t ntok, const float* __restrict__ rw,
                         const float* __restrict__ gammas, TU* __restrict__ y, int fuse_post, const TX* x,
-                        const float* __restrict__ hmix, TX* xo) {
+                        const float* __restrict__ hmix, TX* xo, int q0, int nq) {
   using namespace moe_tc5;
   using namespace tc05;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -1117,8 +1117,11 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
   // work unit = (128-token tile, quarter of 4 experts): the quarters of a tile
   // are independent (expert e reads u columns 32e .. 32e + 31 and writes only
   // those columns of the streams), so the persistent CTAs take units
-  // round-robin -- 4x finer than whole tiles, which evens out the last round
-  const int64_t units = (ntok + TOK - 1) / TOK * 4;
+  // round-robin -- 4x finer than whole tiles, which evens out the last round.
+  // Only quarters q0 .. q0 + nq - 1 are evaluated (all four by default; an
+  // expert-parallel rank takes the quarters of the experts it owns): unit un
+  // is tile un / nq, quarter q0 + un % nq.
+  const int64_t units = (ntok + TOK - 1) / TOK * nq;
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&full[i], 1);
@@ -1149,8 +1152,9 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
     if (lane == 0) {
       int64_t g = 0;  // expert pairs loaded by this CTA
       for (int64_t un = blockIdx.x; un < units && !*abort_flag; un += gridDim.x) {
-        const int64_t t = un >> 2;
-        for (int p = 2 * (int)(un & 3); p < 2 * (int)(un & 3) + 2; ++p, ++g) {
+        const int64_t t = un / nq;
+        const int qu = q0 + (int)(un % nq);
+        for (int p = 2 * qu; p < 2 * qu + 2; ++p, ++g) {
           const int st = (int)(g & 1);
           if (g >= 2 && !mbar_wait_sleep(&empty[st], (uint32_t)(((g >> 1) - 1) & 1))) {
             *abort_flag = 1;
@@ -1225,7 +1229,8 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
     int64_t ge = 0;
     bool ok = true;
     for (int64_t un = blockIdx.x; un < units && ok; un += gridDim.x) {
-      for (int e = 4 * (int)(un & 3); e < 4 * (int)(un & 3) + 4 && ok; ++e, ++ge) {
+      const int qu = q0 + (int)(un % nq);
+      for (int e = 4 * qu; e < 4 * qu + 4 && ok; ++e, ++ge) {
         if (!__all_sync(0xffffffffu, mbar_wait(d1_full, (uint32_t)(ge & 1)))) {
           ok = false;
           break;
@@ -1276,8 +1281,8 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
     int64_t gq = 0;
     bool ok = true;
     for (int64_t un = blockIdx.x; un < units && ok; un += gridDim.x, ++gq) {
-      const int64_t t = un >> 2;
-      const int qt = (int)(un & 3), yb = (int)(gq & 1);
+      const int64_t t = un / nq;
+      const int qt = q0 + (int)(un % nq), yb = (int)(gq & 1);
       if (!__all_sync(0xffffffffu, mbar_wait(&y_full[yb], (uint32_t)((gq >> 1) & 1)))) {
         ok = false;
         break;
@@ -1307,7 +1312,7 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
 template <typename TU, typename TX>
 static int launch_moe_experts_tc05(const void* u, int64_t ntok, const float* rw, const void* wgu, const void* wdown,
                                    const float* gammas, void* y, int fuse_post, const void* x, const float* hmix,
-                                   void* xo, cudaStream_t s) {
+                                   void* xo, cudaStream_t s, int q0 = 0, int nq = 4) {
   using namespace moe_tc5;
   constexpr bool BF = std::is_same<TU, __nv_bfloat16>::value;
   CUtensorMap mu, mg, md;
@@ -1324,9 +1329,10 @@ static int launch_moe_experts_tc05(const void* u, int64_t ntok, const float* rw,
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       sms = 148;
   }
-  const int64_t units = (ntok + TOK - 1) / TOK * 4;  // (tile, quarter of 4 experts)
+  const int64_t units = (ntok + TOK - 1) / TOK * nq;  // (tile, quarter of 4 experts)
   const unsigned grid = (unsigned)(units < sms ? units : sms);
-  kern<<<grid, NTHREADS, SMEM, s>>>(mu, mg, md, ntok, rw, gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo);
+  kern<<<grid, NTHREADS, SMEM, s>>>(mu, mg, md, ntok, rw, gammas, (TU*)y, fuse_post, (const TX*)x, hmix, (TX*)xo, q0,
+                                    nq);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
 }
@@ -1379,6 +1385,26 @@ extern "C" walsh_status walsh_moe_experts_tc_fwd(const void* u, int dtype, int64
                                                              x, hmix, x_out, s)
             : launch_moe_experts_tc05<__half, __half>(u, ntok, weights, w_gu, w_down, gammas, y, fuse_post, x, hmix,
                                                       x_out, s);
+  return r == 1 ? WALSH_OK : (r == 0 ? WALSH_ERR_SHAPE : r);
+}
+
+extern "C" walsh_status walsh_moe_experts_tc_part_fwd(const void* u, int dtype, int64_t ntok, const float* weights,
+                                                      const void* w_gu, const void* w_down, const float* gammas,
+                                                      int first_expert, int n_experts, void* y, void* stream) {
+  if (int e = injected("moe_experts_tc_part_fwd")) return e;
+  WALSH_CHECK_ARG(u && weights && w_gu && w_down && gammas && y);
+  WALSH_CHECK_SHAPE(ntok >= 0 && ntok <= 2147483647LL && first_expert >= 0 && n_experts >= 1 &&
+                    first_expert + n_experts <= 16);
+  if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  if ((((uintptr_t)u) | ((uintptr_t)w_gu) | ((uintptr_t)w_down) | ((uintptr_t)y)) & 15u) return WALSH_ERR_ALIGN;
+  if (ntok == 0) return WALSH_OK;
+  const int q0 = first_expert / 4, nq = (first_expert + n_experts + 3) / 4 - q0;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int r = dtype == WALSH_BF16
+                    ? launch_moe_experts_tc05<__nv_bfloat16, __nv_bfloat16>(u, ntok, weights, w_gu, w_down, gammas,
+                                                                            y, 0, nullptr, nullptr, nullptr, s, q0, nq)
+                    : launch_moe_experts_tc05<__half, __half>(u, ntok, weights, w_gu, w_down, gammas, y, 0, nullptr,
+                                                              nullptr, nullptr, s, q0, nq);
   return r == 1 ? WALSH_OK : (r == 0 ? WALSH_ERR_SHAPE : r);
 }
 

@@ -160,7 +160,13 @@ class mHCLlamaBlock(nn.Module):
                               phi_frag=phif,
                               u_dtype=idt)
         ff = self.feed_forward
-        if hasattr(ff, "kernel_args"):
+        ep = self.__dict__.get("_ep")
+        if ep is not None and hasattr(ff, "kernel_args") and idt != torch.float32 and C == 512:
+            from .. import ep as ep_mod
+            mask, probs = ep_mod.moe_site(u, x, hmix, ff, ep)
+            if record_stats:
+                ff._record(mask.view(B, T, -1), probs.view(B, T, -1), B * T)
+        elif hasattr(ff, "kernel_args"):
             w1t, w2, g, up, d, gam, k, tc = ff.kernel_args(idt)
             rt = ff.router.routing()
             if record_stats:
@@ -329,6 +335,16 @@ class mHCWalsh(nn.Module):
         update, ``.to()``).  Graphs hold their activations in a private memory
         pool until disabled."""
         self._graphs_on = bool(enabled)
+        self.__dict__["_walsh_graphs"] = {}
+
+    def enable_expert_parallel(self, ep=None):
+        """Evaluate the MoE layers expert-parallel through ``ep`` (an
+        walsh_research_b200.ep.ExpertParallel of the process group; every rank
+        runs the same forward on its own tokens), or replicated again with
+        None.  Applies to 16-bit forwards with n_embd = 512; others stay
+        replicated.  Captured CUDA graphs are dropped."""
+        for layer in self.layers:
+            layer.__dict__["_ep"] = ep
         self.__dict__["_walsh_graphs"] = {}
 
     def set_moe_routing(self, mode: str = "topk"):
