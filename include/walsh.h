@@ -525,7 +525,7 @@ walsh_status walsh_moe_experts_tc_part_fwd(const void* u, int dtype, int64_t nto
  * writes WALSH_ERR_TIMEOUT to *status (device int) and returns, so that the
  * host reads the failure at its next synchronisation.
  * The exchange kernels use plain 16-byte stores to peer memory and a system-
- * scope release of the flag; no TMA and no multicast.  No counterpart in the
+ * scope release of the flag (no TMA).  No counterpart in the
  * reference (its MoE runs on one device). */
 walsh_status walsh_ep_dispatch(const void* u, int dtype, int64_t ntok, int C, const float* weights, int rank,
                                int world, void* const* peer_recv_u, float* const* peer_recv_w,

@@ -20,8 +20,8 @@
 // counter) fences at system scope and releases that destination's flag.  No
 // kernel waits on another kernel of the same GPU.  The waits on peers are a
 // separate one-CTA kernel with a clock budget: on expiry it records
-// WALSH_ERR_TIMEOUT in the caller's status word and returns.  No TMA, no
-// multicast.
+// WALSH_ERR_TIMEOUT in the caller's status word and returns.  The data moves
+// by plain stores only (no TMA).
 #include <cuda.h>
 #include <string.h>
 
