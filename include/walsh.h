@@ -547,6 +547,19 @@ walsh_status walsh_ipc_open(const void* handle, int64_t offset, void** dev_ptr_o
 walsh_status walsh_ipc_close(void* base);
 int walsh_ipc_handle_bytes(void);
 
+/* Ternary tensor of a .walsh v4 file ('B' chunk: bitmask + sign bits, as
+ * compress.py:36-93 writes it and generate_compressed.py:70-105 reads it) to
+ * dense float values (row-major, `total` = rows x k elements) and,
+ * optionally (packed != NULL), this library's 2-bit layout [rows, ceil(k/4)]
+ * for the last dimension k.  All pointers are device memory; mask_bytes and
+ * sign_bytes are the chunk's array lengths.  A population count of the
+ * bitmask different from num_nonzero sets *err = WALSH_ERR_ARG (device
+ * int, read by the caller after synchronising).
+ * Replaces unpack_bitmask_ternary (generate_compressed.py:70-105). */
+walsh_status walsh_bitmask_ternary_unpack(const uint8_t* bitmask, int64_t mask_bytes, const uint8_t* sign_bits,
+                                          int64_t sign_bytes, int64_t total, int64_t num_nonzero, int k,
+                                          float* dense, uint8_t* packed, int* err, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Dense helpers around the layer stack
  * ------------------------------------------------------------------------- */

@@ -76,6 +76,20 @@ def unpack_ternary(packed: np.ndarray, k: int) -> np.ndarray:
     return v.reshape(p.shape[:-1] + (p.shape[-1] * 4,))[..., :k].astype(np.float32)
 
 
+def bitmask_ternary_decode(bitmask: bytes, sign_bits: bytes, shape, num_nonzero: int) -> np.ndarray:
+    """Ternary weights from the .walsh v4 bitmask + sign form
+    (generate_compressed.py:70-105; written by compress.py:36-93): bit b of
+    bitmask byte i marks position 8 i + b non-zero; the j-th non-zero (in
+    position order) is +1 when bit j % 8 of sign byte j // 8 is set, else -1."""
+    total = int(np.prod(shape))
+    nz = np.unpackbits(np.frombuffer(bitmask, dtype=np.uint8), bitorder="little")[:total].astype(bool)
+    signs = np.unpackbits(np.frombuffer(sign_bits, dtype=np.uint8), bitorder="little")[:num_nonzero]
+    out = np.zeros(total, dtype=np.float32)
+    pos = np.flatnonzero(nz)[:num_nonzero]
+    out[pos] = np.where(signs[: len(pos)] == 1, 1.0, -1.0)
+    return out.reshape(shape)
+
+
 def absmean_gamma(w: np.ndarray) -> np.float32:
     """gamma = mean(|W|) + 1e-8 in float32 (src/model/physics.py:23-25, src/model/moe.py:277-279)."""
     return np.float32(np.abs(np.asarray(w, dtype=np.float64)).mean()) + np.float32(1e-8)
