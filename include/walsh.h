@@ -560,6 +560,18 @@ walsh_status walsh_bitmask_ternary_unpack(const uint8_t* bitmask, int64_t mask_b
                                           int64_t sign_bytes, int64_t total, int64_t num_nonzero, int k,
                                           float* dense, uint8_t* packed, int* err, void* stream);
 
+/* Rows row0 .. row0 + nrows - 1 of the hash-embedding matrix:
+ * out[r, :] = scale * sum_t importance[v, t] * tables[t, indices[v, t], :],
+ * v = row0 + r (tables float [num_tables, buckets, C], importance float
+ * [V, num_tables], indices int64 [V, num_tables], out float [nrows, C]; C a
+ * multiple of 4, tables and out 16-byte aligned).  An index outside
+ * [0, buckets) is skipped and sets *err = WALSH_ERR_INDEX (device int).
+ * Replaces HashEmbedding._get_chunk_embeddings (src/model/chassis.py:175-191),
+ * which the forward, output_projection and chunked_cross_entropy use. */
+walsh_status walsh_hash_embed_rows(const float* tables, int64_t buckets, const float* importance,
+                                   const int64_t* indices, int num_tables, int C, float scale, int64_t row0,
+                                   int64_t nrows, float* out, int* err, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Dense helpers around the layer stack
  * ------------------------------------------------------------------------- */

@@ -371,6 +371,33 @@ class KVCache:
         self.cached_len += n
 
 
+def hash_embedding_matrix(tables, importance, indices, n_embd):
+    """HashEmbedding._get_chunk_embeddings over the whole vocabulary
+    (src/model/chassis.py:175-191): row v = sqrt(n_embd) * sum_i
+    importance[v, i] * tables[i][indices[v, i]], summed table by table."""
+    out = np.zeros((importance.shape[0], n_embd), dtype=np.result_type(tables, importance))
+    for i in range(tables.shape[0]):
+        out = out + tables[i][indices[:, i]] * importance[:, i:i + 1]
+    return out * out.dtype.type(math.sqrt(n_embd))
+
+
+def hash_indices(hash_a, hash_b, prime, vocab_size, bucket_size):
+    """((a v + b) mod p) mod buckets for every token v, [V, num_tables]
+    (src/model/chassis.py:141-148)."""
+    v = np.arange(vocab_size, dtype=np.int64)
+    return (((v[None, :] * np.asarray(hash_a).reshape(-1, 1) + np.asarray(hash_b).reshape(-1, 1)) % int(prime))
+            % bucket_size).T
+
+
+def _embedding(cfg, p):
+    if cfg.get("hash_embeddings"):
+        nt = sum(1 for k in p if k.startswith("tok_embeddings.emb_tables."))
+        tables = np.stack([p[f"tok_embeddings.emb_tables.{i}.weight"] for i in range(nt)])
+        return hash_embedding_matrix(tables, p["tok_embeddings.importance.weight"],
+                                     np.asarray(p["tok_embeddings.all_indices"]).astype(np.int64), cfg["n_embd"])
+    return p["tok_embeddings.weight"]
+
+
 def _algebra_linear(cfg, p, name, x, dtype):
     if cfg["algebra"] == "hadamard":
         return hadamard_linear(x, p[name + ".inner.weight"], p[name + ".inner.alpha"],
@@ -463,7 +490,7 @@ def mhc_walsh_forward(cfg, p, idx, n_streams=4, cache=None, start_pos=0, dtype=n
          for k, v in p.items()}
     B, T = idx.shape
     C = cfg["n_embd"]
-    emb = p["tok_embeddings.weight"]
+    emb = _embedding(cfg, p)
     h = emb[idx] @ p["stream_proj.weight"].T + p["stream_proj.bias"]
     x = h.reshape(B, T, n_streams, C)
     cos, sin = precompute_rope(C // cfg["n_head"], 2 * cfg["block_size"])

@@ -267,9 +267,16 @@ def op_case(name: str) -> dict:
         return dict(x=r("x").normal(0, 1, (2, 8, 8, 16)).astype(np.float32),
                     W=r("W").normal(0, 0.25, (8, 16, 16)).astype(np.float32),
                     beta=(math.sqrt(3 / 32) * r("b").uniform(0.8, 1.2, (16,))).astype(np.float32))
+    if name == "hash_emb":
+        V, C, nb, nt = 1000, 64, 1021, 3
+        return dict(tables=r("t").normal(0, 0.02, (nt, nb, C)).astype(np.float32),
+                    importance=r("i").normal(1.0, 0.1, (V, nt)).astype(np.float32),
+                    x=r("x").integers(0, V, (2, 7)).astype(np.int64),
+                    h=r("h").normal(0, 1, (2, 5, C)).astype(np.float32),
+                    targets=r("y").integers(0, V, (2, 5)).astype(np.int64))
     raise KeyError(name)
 
 
 OP_CASES = ["pack", "quant", "hlin_512", "hlin_512_latent", "hlin_2048", "hlin_512x2048",
             "hlin_2048x512", "headmix", "headmix32", "sinkhorn", "mapping", "moe", "chmod",
-            "octo_lin", "octo_headmix"]
+            "octo_lin", "octo_headmix", "hash_emb"]

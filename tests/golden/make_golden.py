@@ -155,6 +155,18 @@ def run_op_case(ref, name):
             layer = chassis.OctonionHeadMixer(16).eval()
             layer.W.copy_(_t(d["W"])); layer.beta.copy_(_t(d["beta"]))
             return dict(y=layer(_t(d["x"])).numpy())
+        if name == "hash_emb":
+            nt, nb, C = d["tables"].shape
+            V = d["importance"].shape[0]
+            m = chassis.HashEmbedding(V, C, bucket_size=nb, num_tables=nt).eval()
+            for i in range(nt):
+                m.emb_tables[i].weight.copy_(_t(d["tables"][i]))
+            m.importance.weight.copy_(_t(d["importance"]))
+            return dict(y=m(_t(d["x"])).numpy(), all_indices=m.all_indices.numpy(),
+                        hash_a=m.hash_a.numpy(), hash_b=m.hash_b.numpy(),
+                        all_embeddings=m._get_all_embeddings().numpy(),
+                        logits=m.output_projection(_t(d["h"])).numpy(),
+                        loss=np.array(m.chunked_cross_entropy(_t(d["h"]), _t(d["targets"]), chunk_size=256).item()))
     raise KeyError(name)
 
 

@@ -138,3 +138,27 @@ def test_fht_properties():
     assert np.abs(H @ (H @ x) - x).max() < 1e-5
     y = (np.arange(32) + 1) / 32.0
     assert abs(np.linalg.norm(H @ y) - np.linalg.norm(y)) < 1e-5
+
+
+def test_hash_embedding_oracle_and_buffers_match_reference():
+    """Hash embeddings (src/model/chassis.py:109-260): the oracle's matrix,
+    lookup, output projection and cross entropy, and this package's hashing
+    buffers, against the reference's own module (tests/golden/hash_emb.npz)."""
+    import torch
+    from walsh_research_b200.model.hash_embeddings import HashEmbedding
+    d, g = cases.op_case("hash_emb"), np.load(os.path.join(GOLDEN, "hash_emb.npz"))
+    nt, nb, C = d["tables"].shape
+    V = d["importance"].shape[0]
+    m = HashEmbedding(V, C, bucket_size=nb, num_tables=nt)
+    np.testing.assert_array_equal(m.hash_a.numpy(), g["hash_a"])
+    np.testing.assert_array_equal(m.hash_b.numpy(), g["hash_b"])
+    np.testing.assert_array_equal(m.all_indices.numpy(), g["all_indices"])
+    np.testing.assert_array_equal(O.hash_indices(g["hash_a"], g["hash_b"], 1000000007, V, nb), g["all_indices"])
+    E = O.hash_embedding_matrix(d["tables"], d["importance"], g["all_indices"], C)
+    np.testing.assert_allclose(E, g["all_embeddings"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(E[d["x"]], g["y"], rtol=1e-6, atol=1e-7)
+    logits = d["h"].astype(np.float64) @ E.astype(np.float64).T
+    np.testing.assert_allclose(logits, g["logits"], rtol=1e-5, atol=1e-6)
+    lse = np.log(np.exp(logits - logits.max(-1, keepdims=True)).sum(-1)) + logits.max(-1)
+    loss = float(np.mean(lse - np.take_along_axis(logits, d["targets"][..., None], -1)[..., 0]))
+    assert abs(loss - float(g["loss"])) < 1e-5

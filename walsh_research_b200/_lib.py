@@ -76,6 +76,7 @@ SIGNATURES = {
     "walsh_ipc_close": [P],
     "walsh_ipc_handle_bytes": [],
     "walsh_bitmask_ternary_unpack": [P, c_int64, P, c_int64, c_int64, c_int64, c_int, P, P, P, P],
+    "walsh_hash_embed_rows": [P, c_int64, P, P, c_int, c_int, c_float, c_int64, c_int64, P, P, P],
 }
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_ipc_handle_bytes": c_int, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,
             "walsh_linear_split_tc_scratch_bytes": ctypes.c_int64}

@@ -228,10 +228,13 @@ class mHCWalsh(nn.Module):
         self.compute_dtype = torch.float32
         self.stream_dtype = None  # 16-bit mode stream storage: None -> float16
         if getattr(config, "hash_embeddings", False):
-            raise NotImplementedError("hash embeddings are outside the B200 hot path")
-        self.tok_embeddings = nn.Embedding(config.vocab_size, config.n_embd)
-        self.output = nn.Linear(config.n_embd, config.vocab_size, bias=False)
-        self.tok_embeddings.weight = self.output.weight
+            from .hash_embeddings import HashEmbedding
+            self.tok_embeddings = HashEmbedding(config.vocab_size, config.n_embd)
+            self.output = None
+        else:
+            self.tok_embeddings = nn.Embedding(config.vocab_size, config.n_embd)
+            self.output = nn.Linear(config.n_embd, config.vocab_size, bias=False)
+            self.tok_embeddings.weight = self.output.weight
         self.stream_proj = nn.Linear(config.n_embd, n_streams * config.n_embd)
         self.layers = nn.ModuleList([mHCLlamaBlock(config, n_streams) for _ in range(config.n_layer)])
         self.stream_merge = nn.Linear(n_streams * config.n_embd, config.n_embd)
@@ -263,9 +266,16 @@ class mHCWalsh(nn.Module):
             return dt
         return self.stream_dtype or torch.float16
 
+    def embedding_matrix(self):
+        """The [V, C] token embedding, tied to the output projection: the
+        embedding weight, or the matrix a hash embedding represents."""
+        if self.output is None:
+            return self.tok_embeddings.weight_matrix()
+        return self.tok_embeddings.weight
+
     def stream_table(self, dtype):
         """tok_embeddings folded with stream_proj: row v = stream_proj(emb[v]), [V, n*C]."""
-        emb, W, b = self.tok_embeddings.weight, self.stream_proj.weight, self.stream_proj.bias
+        emb, W, b = self.embedding_matrix(), self.stream_proj.weight, self.stream_proj.bias
 
         def build():
             e = emb.detach().float().contiguous()
@@ -277,17 +287,17 @@ class mHCWalsh(nn.Module):
 
     def head_weights(self):
         """The tied output projection, float32 (logits are always computed against fp32 weights)."""
-        emb = self.tok_embeddings.weight
+        emb = self.embedding_matrix()
         return _prep.cached(self, "emb_f32", [emb], lambda: emb.detach().float().contiguous())
 
     def head_weights_split(self):
         """The tied output projection as its bf16 split (w_hi, w_lo)."""
-        emb = self.tok_embeddings.weight
+        emb = self.embedding_matrix()
         return _prep.cached(self, "emb_split", [emb], lambda: ops.split_bf16(emb))
 
     def head_weights_split3(self):
         """The tied output projection as [w_hi | w_lo | w_hi] bf16 [V, 3C] (linear_split_tc)."""
-        emb = self.tok_embeddings.weight
+        emb = self.embedding_matrix()
         return _prep.cached(self, "emb_split3", [emb], lambda: ops.split3_weights(emb))
 
     def merge_weights_split(self):
@@ -431,7 +441,11 @@ class mHCWalsh(nn.Module):
         self._last_index_error = err
         need_all = return_hidden or targets is not None
         h_out = self._merge_norm(x, rows_last_only=not need_all)
-        if targets is not None:
+        if targets is not None and self.output is None:
+            # hash embeddings: the reference returns the chunked cross entropy and no logits
+            loss = F.cross_entropy(self._logits(h_out.reshape(B * T, C)), targets.reshape(-1), ignore_index=-1)
+            logits = None
+        elif targets is not None:
             logits = self._logits(h_out.reshape(B * T, C)).view(B, T, -1)
             loss = F.cross_entropy(logits.view(-1, logits.size(-1)), targets.view(-1), ignore_index=-1)
         else:
