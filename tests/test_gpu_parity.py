@@ -112,6 +112,37 @@ def test_hadamard_linear_bf16(name):
     assert rel(y, g["y"]) < 2e-2
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("ntok", [1, 31, 32, 33, 4097, 150 * 32 * 2 + 5])
+def test_hadamard_linear_packed_weights_vs_oracle(dt, ntok):
+    """The 16-bit HadamardLinear(512, 512) that reads the 2-bit packed weights
+    (ragged last tile, several tiles per persistent CTA and both buffers of
+    its ring) against the float64 oracle on the same rounded inputs, and
+    against the mma.sync kernel with fp16 weight copies.  16-bit
+    intermediates: 1e-2 of the largest output."""
+    from walsh_research_b200 import _lib, ops
+    rng = np.random.default_rng(ntok)
+    d = dict(x=rng.normal(size=(1, ntok, 512)).astype(np.float32), weight=rng.normal(size=(32, 16, 16)).astype(np.float32),
+             alpha=rng.uniform(0.5, 1.5, (32, 16)).astype(np.float32),
+             beta=rng.uniform(0.1, 0.4, (32, 16)).astype(np.float32))
+    layer = _hlin(d)
+    x = T(d["x"], dt)
+    _lib.call("walsh_hlin_pk_error", 1)
+    y = layer(x)
+    assert y.dtype == dt
+    ref = O.hadamard_linear(x.double().cpu().numpy(), d["weight"], d["alpha"], d["beta"])
+    assert rel(y, ref) < 1e-2
+    if dt == torch.bfloat16:
+        ops.HLIN_PACKED = False
+        try:
+            y_old = layer(x)
+        finally:
+            ops.HLIN_PACKED = True
+        assert rel(y, y_old.float().cpu().numpy()) < 1e-2
+    torch.cuda.synchronize()
+    assert _lib.call("walsh_hlin_pk_error", 1) == 0
+
+
 @pytest.mark.parametrize("fin,fout,ntok", [(512, 512, 4096 + 3), (2048, 2048, 517), (512, 2048, 33),
                                             (2048, 512, 1), (512, 512, 1)])
 def test_hadamard_linear_vs_oracle_sizes(fin, fout, ntok):

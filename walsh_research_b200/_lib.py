@@ -77,6 +77,8 @@ SIGNATURES = {
     "walsh_ipc_handle_bytes": [],
     "walsh_bitmask_ternary_unpack": [P, c_int64, P, c_int64, c_int64, c_int64, c_int, P, P, P, P],
     "walsh_hash_embed_rows": [P, c_int64, P, P, c_int, c_int, c_float, c_int64, c_int64, P, P, P],
+    "walsh_hadamard_linear_pk_fwd": [P, c_int, c_int64, P, P, P, P, P],
+    "walsh_hlin_pk_error": [c_int],
 }
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_ipc_handle_bytes": c_int, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,
             "walsh_linear_split_tc_scratch_bytes": ctypes.c_int64}
@@ -84,13 +86,13 @@ _RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_ipc_handle_bytes": c_int
 KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_octo_set_mainloop": 0,
                     "walsh_chmod_mlp_tc": 3, "walsh_chmod_mlp_tc_scratch_bytes": 0,
                     "walsh_linear_split_tc_fwd": 2, "walsh_linear_split_tc_scratch_bytes": 0,
-                    "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_map_set_pipe": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
+                    "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_map_set_pipe": 0, "walsh_hlin_pk_error": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
                     "walsh_abi_version": 0, "walsh_ipc_handle": 0, "walsh_ipc_open": 0, "walsh_ipc_close": 0,
                     "walsh_ipc_handle_bytes": 0}
 launch_count = 0
 # entry points that return a plain int rather than a status
 _PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows", "walsh_octo_set_mainloop", "walsh_tc05_error",
-              "walsh_map_error", "walsh_attn_set_path", "walsh_map_set_pipe"}
+              "walsh_map_error", "walsh_attn_set_path", "walsh_map_set_pipe", "walsh_hlin_pk_error"}
 
 
 class MoeTcWeights(ctypes.Structure):

@@ -1,0 +1,261 @@
+// HadamardLinear for 16-bit activations with the ternary weights read in
+// their 2-bit packed form (C_in = C_out = 512: 32 groups x 16).
+//
+// Per token (src/model/fht_cuda.py:489-519), with H the +-1 Sylvester matrix
+// of order 32 (the reference's H is H / sqrt(32)):
+//   Z[g][i] = sum_g' H[g][g'] alpha[g'][i] x[g'][i]          (transform A)
+//   V[g][o] = sum_i  w[g][o][i] Z[g][i]                       (ternary mat-vecs)
+//   y[h][o] = beta[h][o] / 32 * sum_g H[h][g] V[g][o]         (transform C)
+//
+// One persistent CTA of 16 warps per SM walks 64-token tiles.  Per tile:
+//   A  thread (t, p) takes columns 2p, 2p + 1 of token t, read straight from
+//      global memory (32 four-byte loads per thread; four tokens x 32 bytes
+//      per warp access), scaled by alpha, transformed by in-register
+//      butterflies on float pairs, rounded to the 16-bit type into shared
+//      memory; the next tile's loads are then issued into the same registers,
+//      so they arrive while this tile finishes;
+//   B  warp w takes groups 2w, 2w + 1: m16n8k16 MMAs with A = the 64 tokens'
+//      16-wide slice of group g (ldmatrix) and B = w_g^T, whose fragments
+//      were built once from the 2-bit codes (the packed weights, 2 KB, are
+//      staged with 128-bit loads); float32 results to shared memory;
+//   C  thread (t, p): output columns 2p, 2p + 1 over the 32 groups, the
+//      butterfly transform, beta / 32, rounded and written straight to
+//      global memory.
+// Rows are padded in shared memory (16-bit rows by 32 bytes, float32 rows by
+// 32 bytes) so that a warp's accesses fall in distinct banks.  The kernel
+// has no waits besides block barriers (walsh_hlin_pk_error stays 0; it is
+// kept for the status interface of the entry point).
+#include <type_traits>
+
+#include "common.cuh"
+#include "mma.cuh"
+#include "tc05.cuh"
+
+namespace walsh {
+
+__device__ int g_hlin_pk_error;
+
+template <typename T16>
+__device__ __forceinline__ uint32_t ternary_pair16(int a, int b) {
+  // (a, b) in {-1, 0, 1} as a 16-bit pair (a in the low half)
+  const uint16_t one = std::is_same<T16, __half>::value ? 0x3C00u : 0x3F80u;
+  const uint16_t va = a == 0 ? 0 : (uint16_t)(one | (a < 0 ? 0x8000u : 0u));
+  const uint16_t vb = b == 0 ? 0 : (uint16_t)(one | (b < 0 ? 0x8000u : 0u));
+  return (uint32_t)va | ((uint32_t)vb << 16);
+}
+
+namespace hpk2 {
+constexpr int C = 512, G = 32, IO = 16, TM = 64, NW = 16, NT = NW * 32;
+constexpr int ZROW = C * 2 + 32;       // bytes per token of the transformed input (16-bit)
+constexpr int VROW = G * IO * 4 + 32;  // bytes per token of the mat-vec results (float32)
+constexpr int WBYTES = G * IO * IO / 4;  // packed weights
+constexpr int OFF_V = TM * ZROW, OFF_AB = OFF_V + TM * VROW, OFF_W = OFF_AB + 2 * G * IO * 4;
+constexpr int SMEM = OFF_W + WBYTES + 128;
+}  // namespace hpk2
+
+__device__ __forceinline__ uint64_t hpk_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 hpk_unpack(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(lo), "=f"(hi) : "l"(v));
+  return make_float2(lo, hi);
+}
+__device__ __forceinline__ uint64_t hpk_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t hpk_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t hpk_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// unnormalised 32-point Walsh-Hadamard transform of 32 float pairs (Sylvester order)
+__device__ __forceinline__ void fht32x2(uint64_t* v) {
+#pragma unroll
+  for (int s = 1; s < 32; s <<= 1)
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if ((i & s) == 0) {
+        const uint64_t a = v[i], b = v[i + s];
+        v[i] = hpk_add(a, b);
+        v[i + s] = hpk_sub(a, b);
+      }
+}
+
+template <typename T16>
+__global__ void __launch_bounds__(hpk2::NT, 1)
+hlin_packed_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* __restrict__ w2,
+                   const float* __restrict__ alpha, const float* __restrict__ beta, T16* __restrict__ y) {
+  using namespace hpk2;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char* sm = smem_raw;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, t4 = lane & 3;
+  const int64_t ntiles = (ntok + TM - 1) / TM;
+  // packed weights (16 bytes per thread), alpha and beta / 32 into shared memory
+  if (tid < WBYTES / 16)
+    reinterpret_cast<uint4*>(sm + OFF_W)[tid] = __ldg(reinterpret_cast<const uint4*>(w2) + tid);
+  float* ab = reinterpret_cast<float*>(sm + OFF_AB);  // [G][IO] alpha, then [G][IO] beta / 32
+  for (int q = tid; q < G * IO; q += NT) {
+    ab[q] = __ldg(alpha + q);
+    ab[G * IO + q] = __ldg(beta + q) * (1.0f / 32.0f);
+  }
+  __syncthreads();
+  // B fragments of w_g^T for this warp's groups 2w, 2w + 1 (n-tiles: o 0-7, 8-15)
+  uint32_t bf[2][2][2];
+  {
+    const uint8_t* ws = sm + OFF_W;
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int g = 2 * warp + q, o = 8 * nt + gid, i0 = 8 * h + 2 * t4;
+          const uint32_t byte = ws[(g * IO + o) * 4 + (i0 >> 2)];
+          const int s0 = 6 - 2 * (i0 & 3);
+          const int a = (int)((byte >> s0) & 3u) - 1, b = (int)((byte >> (s0 - 2)) & 3u) - 1;
+          bf[q][nt][h] = ternary_pair16<T16>(a, b);
+        }
+  }
+  const int trow = tid >> 3, pc = (tid & 7) * 2;  // token row and first column of this thread in A and C
+  const uint64_t* ab2 = reinterpret_cast<const uint64_t*>(ab);
+  uint32_t xr[G];  // this thread's two input columns of its token, 16-bit pairs
+  auto load_x = [&](int64_t tile) {
+    const int64_t tok = tile * TM + trow;
+    if (tile < ntiles && tok < ntok) {
+      const uint32_t* xp = reinterpret_cast<const uint32_t*>(x + tok * C + pc);
+#pragma unroll
+      for (int g = 0; g < G; ++g) xr[g] = __ldg(xp + g * (IO / 2));
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) xr[g] = 0u;
+    }
+  };
+  load_x(blockIdx.x);
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int64_t tok = tile * TM + trow;
+    // ---- A
+    {
+      uint64_t v[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float2 f = unpack2<T16>(xr[g]);
+        v[g] = hpk_mul(hpk_pack(f.x, f.y), ab2[(g * IO + pc) / 2]);
+      }
+      load_x(tile + gridDim.x);  // next tile's columns, in flight during B and C
+      fht32x2(v);
+      unsigned char* zp = sm + trow * ZROW + pc * 2;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float2 f = hpk_unpack(v[g]);
+        *reinterpret_cast<uint32_t*>(zp + g * IO * 2) = pack2<T16>(f.x, f.y);
+      }
+    }
+    __syncthreads();
+    // ---- B: the ternary mat-vecs of groups 2w, 2w + 1 on the tensor cores
+    {
+      const uint32_t zs = tc05::smem_u32(sm);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int g = 2 * warp + q;
+#pragma unroll
+        for (int mt = 0; mt < TM / 16; ++mt) {
+          uint32_t a[4];
+          const uint32_t addr = zs + (uint32_t)((16 * mt + (lane & 15)) * ZROW + g * IO * 2 + (lane >> 4) * 16);
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                       : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                       : "r"(addr));
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16<T16>(c, a, bf[q][nt][0], bf[q][nt][1]);
+            const int t0 = 16 * mt + gid, o = 8 * nt + 2 * t4;
+            *reinterpret_cast<float2*>(sm + OFF_V + t0 * VROW + (g * IO + o) * 4) = make_float2(c[0], c[1]);
+            *reinterpret_cast<float2*>(sm + OFF_V + (t0 + 8) * VROW + (g * IO + o) * 4) = make_float2(c[2], c[3]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    // ---- C: output columns pc, pc + 1 of token trow over the 32 groups, to global memory
+    {
+      const unsigned char* vp = sm + OFF_V + trow * VROW + pc * 4;
+      uint64_t v[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) v[g] = *reinterpret_cast<const uint64_t*>(vp + g * IO * 4);
+      fht32x2(v);
+      if (tok < ntok) {
+        uint32_t* yp = reinterpret_cast<uint32_t*>(y + tok * C + pc);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float2 f = hpk_unpack(hpk_mul(v[h], ab2[(G * IO + h * IO + pc) / 2]));
+          yp[h * (IO / 2)] = pack2<T16>(f.x, f.y);
+        }
+      }
+    }
+    __syncthreads();  // Z and V are free for the next tile
+  }
+}
+
+static int hlin_pk_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      n = 148;
+    }
+  }
+  return n;
+}
+
+}  // namespace walsh
+
+using namespace walsh;
+
+extern "C" walsh_status walsh_hadamard_linear_pk_fwd(const void* x, int dtype, int64_t ntok, const uint8_t* w_2bit,
+                                                     const float* alpha, const float* beta, void* y, void* stream) {
+  if (int e = injected("hadamard_linear_pk_fwd")) return e;
+  WALSH_CHECK_ARG(x && w_2bit && alpha && beta && y);
+  WALSH_CHECK_SHAPE(ntok >= 0);
+  if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  if ((((uintptr_t)x) | ((uintptr_t)y) | ((uintptr_t)w_2bit)) & 15u) return WALSH_ERR_ALIGN;
+  if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t ntiles = (ntok + hpk2::TM - 1) / hpk2::TM;
+  const int grid = (int)min64(ntiles, hlin_pk_sms());
+  if (dtype == WALSH_BF16) {
+    auto k = hlin_packed_kernel<__nv_bfloat16>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, hpk2::SMEM) != cudaSuccess)
+      return launch_status();
+    k<<<grid, hpk2::NT, hpk2::SMEM, s>>>((const __nv_bfloat16*)x, ntok, w_2bit, alpha, beta, (__nv_bfloat16*)y);
+  } else {
+    auto k = hlin_packed_kernel<__half>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, hpk2::SMEM) != cudaSuccess)
+      return launch_status();
+    k<<<grid, hpk2::NT, hpk2::SMEM, s>>>((const __half*)x, ntok, w_2bit, alpha, beta, (__half*)y);
+  }
+  return launch_status();
+}
+
+extern "C" int walsh_hlin_pk_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_hlin_pk_error, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return WALSH_ERR_LAUNCH;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_hlin_pk_error, &zero, sizeof(int));
+  }
+  return v;
+}

@@ -78,6 +78,23 @@ def hadamard_linear_tc(x, w_f16, alpha, beta, w_scale: float = 1.0):
     return y
 
 
+# HadamardLinear(512, 512) on 16-bit activations: True reads the 2-bit packed
+# weights (walsh_hadamard_linear_pk_fwd), False the fp16 weight copies of the
+# mma.sync chain (walsh_hadamard_linear_tc_fwd; kept for comparisons)
+HLIN_PACKED = True
+
+
+def hadamard_linear_pk(x, packed, alpha, beta):
+    """y = HadamardLinear(x) for x [..., 512] in bfloat16 or float16, weights
+    2-bit packed [32, 16, 4]; y in x's dtype."""
+    require_cuda(x)
+    x = _c(x)
+    y = torch.empty_like(x)
+    call("walsh_hadamard_linear_pk_fwd", ptr(x), dcode(x.dtype), x.numel() // 512, ptr(packed), ptr(alpha),
+         ptr(beta), ptr(y), stream())
+    return y
+
+
 def attn_out_tc(o, wmix, beta_mix, wo, alpha_o, beta_o, x, hmix, out=None):
     """Head mixer (wmix may be None) + wo + mHC site epilogue; returns x_out."""
     require_cuda(o, x)
