@@ -317,6 +317,8 @@ def main():
     ap.add_argument("--no-octonion", action="store_true", help="skip the config-2 octonion measurement")
     ap.add_argument("--no-micro", action="store_true", help="skip the config-1 HadamardLinear microbenchmark")
     ap.add_argument("--no-2048", action="store_true", help="skip the config-4 Walsh-2048 decode measurement")
+    ap.add_argument("--ep", action="store_true",
+                    help="with N > 1: also time the prefill with expert-parallel MoE layers (NVLink exchange)")
     ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode", "octonion", "decode2048"],
                     help="run one warm-up and one eager forward only (for ncu launch lists)")
     args = ap.parse_args()
@@ -411,6 +413,8 @@ def main():
         roof = dominant_kernel_roofline(model, idx, B, T, dev)
     del graph, logits_g
     torch.cuda.empty_cache()
+    ep_line = measure_prefill_ep(model, idx, B, T, dev, args.steps, max(3, args.warmup), world, dist) \
+        if (args.ep and world > 1) else None
     decode = None if args.no_decode else measure_decode(model, dev, args.steps, max(3, args.warmup), rank, world, dist)
     octo = None if args.no_octonion else measure_octonion(dev, args.steps, max(3, args.warmup), rank, world, dist)
     micro = None if args.no_micro else measure_hlin_microbench(dev)
@@ -432,10 +436,41 @@ def main():
                        "batch_per_gpu": B, "seq_len": T, "parallelism": f"replicas x{world} (batch-sharded)",
                        "l2": "working set > L2 (stream state 268 MB per layer), no flush"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(), "decode": decode,
-            "octonion": octo, "hlin_microbench": micro, "decode_2048": d2048,
+            "octonion": octo, "hlin_microbench": micro, "decode_2048": d2048, "prefill_ep": ep_line,
             "gpu_launches": launches_per_forward * args.steps,
             "peaks": src}
     print(json.dumps(line), flush=True)
+
+
+def measure_prefill_ep(model, idx, B, T, dev, steps, warmup, world, dist):
+    """Config-3 prefill with every MoE layer expert-parallel (each rank owns
+    16 / N experts and evaluates them for every rank's tokens, through the
+    NVLink exchange kernels), against the same eager forward with replicated
+    experts; CUDA events, max over ranks.  Eager (no graph): the exchange
+    epochs are host arguments."""
+    from walsh_research_b200.ep import ExpertParallel
+    ep = ExpertParallel(max_tokens=B * T, C=CONFIG["n_embd"], dtype=torch.float16, transport="nvlink")
+    out = {}
+    with torch.no_grad():
+        for mode in ("replicated", "expert_parallel"):
+            model.enable_expert_parallel(ep if mode == "expert_parallel" else None)
+            for _ in range(warmup):
+                model(idx)
+            torch.cuda.synchronize()
+            dist.barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(steps):
+                model(idx)
+            e.record()
+            torch.cuda.synchronize()
+            ms = max_over_ranks(s.elapsed_time(e) / steps, dist, dev)
+            out[mode] = {"value": world * B * T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms}
+        ep.check()
+        model.enable_expert_parallel(None)
+    ep.close()
+    out["config"] = {"experts_per_rank": 16 // world, "transport": "NVLink exchange kernels", "mode": "eager"}
+    return out
 
 
 def run_profile(args):
