@@ -90,6 +90,10 @@ def main():
         t = torch.tensor([s.elapsed_time(e) / 20], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out["replicated_us"] = float(t.item()) * 1e3
+    out_dir = os.environ.get("EP_OUT_DIR")
+    if out_dir:
+        with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
+            json.dump(out, f)
     print(json.dumps(out), flush=True)
     dist.barrier()
     dist.destroy_process_group()

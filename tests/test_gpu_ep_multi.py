@@ -26,17 +26,16 @@ def _free_port():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
-def test_expert_parallel_across_gpus_equals_replicated(parity_report):
+def test_expert_parallel_across_gpus_equals_replicated(parity_report, tmp_path):
     n = min(torch.cuda.device_count(), 8)
     n = 8 if n >= 8 else (4 if n >= 4 else 2)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_TOKENS="10000")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_TOKENS="10000", EP_OUT_DIR=str(tmp_path))
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "tests", "ep_multi_worker.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    lines = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
-    assert len(lines) == n
+    lines = [json.load(open(tmp_path / f"rank{k}.json")) for k in range(n)]
     for d in lines:
         assert d["nvlink_equal"], d
         assert d["nccl_equal"], d
