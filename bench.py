@@ -319,7 +319,7 @@ def main():
     ap.add_argument("--no-2048", action="store_true", help="skip the config-4 Walsh-2048 decode measurement")
     ap.add_argument("--ep", action="store_true",
                     help="with N > 1: also time the prefill with expert-parallel MoE layers (NVLink exchange)")
-    ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode", "octonion", "decode2048"],
+    ap.add_argument("--profile", nargs="?", const="prefill", choices=["prefill", "decode", "octonion", "decode2048", "hlin"],
                     help="run one warm-up and one eager forward only (for ncu launch lists)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -477,6 +477,26 @@ def run_profile(args):
     """One warm-up forward then one profiled forward, eager (no graph)."""
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
+    if args.profile == "hlin":
+        # config 1: HadamardLinear(n, n), n = 512 then 2048, over 65536 bf16
+        # tokens (16384 for n = 2048 with --batch below 64), three calls each
+        from walsh_research_b200.model.fht_cuda import HadamardLinear
+        g = torch.Generator().manual_seed(0)
+        for n in (512, 2048):
+            lin = HadamardLinear(n, n)
+            with torch.no_grad():
+                lin.weight.copy_(torch.randint(-1, 2, lin.weight.shape, generator=g).float())
+                lin.alpha.copy_(torch.rand(lin.alpha.shape, generator=g) + 0.5)
+            lin = lin.to(dev)
+            ntok = 65536 if (n == 512 or args.batch >= BATCH) else 16384
+            x = torch.randn((ntok, n), generator=g).to(dev, torch.bfloat16)
+            with torch.no_grad():
+                for _ in range(3):
+                    y = lin(x)
+            torch.cuda.synchronize()
+            print(f"profile hlin {n} x {ntok} done", float(y.float().abs().mean()), flush=True)
+            del x, y
+        return
     model = build_model_cpu().to(dev).eval()
     model.compute_dtype = torch.bfloat16
     if args.profile == "decode2048":

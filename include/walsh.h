@@ -572,15 +572,18 @@ walsh_status walsh_hash_embed_rows(const float* tables, int64_t buckets, const f
                                    const int64_t* indices, int num_tables, int C, float scale, int64_t row0,
                                    int64_t nrows, float* out, int* err, void* stream);
 
-/* HadamardLinear(512, 512) for 16-bit activations reading the ternary
- * weights in their 2-bit packed form: x, y [ntok, 512] (dtype WALSH_BF16 or
- * WALSH_F16, 16-byte aligned), w_2bit [32, 16, 4] (the reference encoding,
- * 16-byte aligned), alpha, beta float [32, 16]; weight scale 1 (the
- * HadamardLinear semantics).  Transforms in float32 on the CUDA cores, the
- * ternary mat-vecs on the tensor cores with 16-bit operands and float32
- * accumulation.  Replaces HadamardLinear.forward (src/model/fht_cuda.py:489-519). */
-walsh_status walsh_hadamard_linear_pk_fwd(const void* x, int dtype, int64_t ntok, const uint8_t* w_2bit,
-                                          const float* alpha, const float* beta, void* y, void* stream);
+/* HadamardLinear(F, F), F = features = 512 or 2048, for 16-bit activations
+ * reading the ternary weights in their 2-bit packed form: x, y [ntok, F]
+ * (dtype WALSH_BF16 or WALSH_F16, 16-byte aligned), w_2bit [32, F/32, F/128]
+ * (the reference encoding, 16-byte aligned), alpha, beta float [32, F/32];
+ * weight scale 1 (the HadamardLinear semantics).  Transforms in float32 on
+ * the CUDA cores, the ternary mat-vecs on the tensor cores with 16-bit
+ * operands and float32 accumulation (F = 2048: mat-vec results rounded to
+ * the 16-bit type before the output transform).  Other F: WALSH_ERR_SHAPE.
+ * Replaces HadamardLinear.forward (src/model/fht_cuda.py:489-519). */
+walsh_status walsh_hadamard_linear_pk_fwd(const void* x, int dtype, int64_t ntok, int features,
+                                          const uint8_t* w_2bit, const float* alpha, const float* beta, void* y,
+                                          void* stream);
 /* Status word of walsh_hadamard_linear_pk_fwd's bounded waits (0 or
  * WALSH_ERR_TIMEOUT); synchronous read, reset != 0 clears it. */
 int walsh_hlin_pk_error(int reset);

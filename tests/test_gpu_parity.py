@@ -113,18 +113,20 @@ def test_hadamard_linear_bf16(name):
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("ntok", [1, 31, 32, 33, 4097, 150 * 32 * 2 + 5])
-def test_hadamard_linear_packed_weights_vs_oracle(dt, ntok):
-    """The 16-bit HadamardLinear(512, 512) that reads the 2-bit packed weights
-    (ragged last tile, several tiles per persistent CTA and both buffers of
-    its ring) against the float64 oracle on the same rounded inputs, and
-    against the mma.sync kernel with fp16 weight copies.  16-bit
-    intermediates: 1e-2 of the largest output."""
+@pytest.mark.parametrize("F,ntok", [(512, 1), (512, 31), (512, 32), (512, 33), (512, 4097), (512, 150 * 32 * 2 + 5),
+                                    (2048, 1), (2048, 15), (2048, 17), (2048, 148 * 16 * 3 + 7)])
+def test_hadamard_linear_packed_weights_vs_oracle(dt, F, ntok):
+    """The 16-bit HadamardLinear(F, F) that reads the 2-bit packed weights
+    (ragged last tile, several tiles per persistent CTA) against the float64
+    oracle on the same rounded inputs, and against the kernel it replaces
+    (512: the mma.sync kernel with fp16 weight copies; 2048: the general
+    kernel).  16-bit intermediates: 1e-2 of the largest output."""
     from walsh_research_b200 import _lib, ops
-    rng = np.random.default_rng(ntok)
-    d = dict(x=rng.normal(size=(1, ntok, 512)).astype(np.float32), weight=rng.normal(size=(32, 16, 16)).astype(np.float32),
-             alpha=rng.uniform(0.5, 1.5, (32, 16)).astype(np.float32),
-             beta=rng.uniform(0.1, 0.4, (32, 16)).astype(np.float32))
+    rng = np.random.default_rng(ntok + F)
+    io = F // 32
+    d = dict(x=rng.normal(size=(1, ntok, F)).astype(np.float32), weight=rng.normal(size=(32, io, io)).astype(np.float32),
+             alpha=rng.uniform(0.5, 1.5, (32, io)).astype(np.float32),
+             beta=rng.uniform(0.1, 0.4, (32, io)).astype(np.float32))
     layer = _hlin(d)
     x = T(d["x"], dt)
     _lib.call("walsh_hlin_pk_error", 1)
@@ -132,7 +134,7 @@ def test_hadamard_linear_packed_weights_vs_oracle(dt, ntok):
     assert y.dtype == dt
     ref = O.hadamard_linear(x.double().cpu().numpy(), d["weight"], d["alpha"], d["beta"])
     assert rel(y, ref) < 1e-2
-    if dt == torch.bfloat16:
+    if dt == torch.bfloat16 or F == 2048:
         ops.HLIN_PACKED = False
         try:
             y_old = layer(x)

@@ -77,7 +77,7 @@ SIGNATURES = {
     "walsh_ipc_handle_bytes": [],
     "walsh_bitmask_ternary_unpack": [P, c_int64, P, c_int64, c_int64, c_int64, c_int, P, P, P, P],
     "walsh_hash_embed_rows": [P, c_int64, P, P, c_int, c_int, c_float, c_int64, c_int64, P, P, P],
-    "walsh_hadamard_linear_pk_fwd": [P, c_int, c_int64, P, P, P, P, P],
+    "walsh_hadamard_linear_pk_fwd": [P, c_int, c_int64, c_int, P, P, P, P, P],
     "walsh_hlin_pk_error": [c_int],
 }
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_ipc_handle_bytes": c_int, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,

@@ -1,5 +1,6 @@
 // HadamardLinear for 16-bit activations with the ternary weights read in
-// their 2-bit packed form (C_in = C_out = 512: 32 groups x 16).
+// their 2-bit packed form: C_in = C_out = 512 (32 groups x 16) and
+// C_in = C_out = 2048 (32 groups x 64).
 //
 // Per token (src/model/fht_cuda.py:489-519), with H the +-1 Sylvester matrix
 // of order 32 (the reference's H is H / sqrt(32)):
@@ -21,8 +22,9 @@
 //   C  thread (t, p): output columns 2p, 2p + 1 over the 32 groups, the
 //      butterfly transform, beta / 32, rounded and written straight to
 //      global memory.
-// Rows are padded in shared memory (16-bit rows by 32 bytes, float32 rows by
-// 32 bytes) so that a warp's accesses fall in distinct banks.  The kernel
+// Rows are padded in shared memory (16-bit rows by 16 bytes, float32 rows by
+// 32 bytes) and a warp takes every other token of eight in A and C, so that
+// a warp's accesses (ldmatrix rows included) fall in distinct banks.  The kernel
 // has no waits besides block barriers (walsh_hlin_pk_error stays 0; it is
 // kept for the status interface of the entry point).
 #include <type_traits>
@@ -46,7 +48,7 @@ __device__ __forceinline__ uint32_t ternary_pair16(int a, int b) {
 
 namespace hpk2 {
 constexpr int C = 512, G = 32, IO = 16, TM = 64, NW = 16, NT = NW * 32;
-constexpr int ZROW = C * 2 + 32;       // bytes per token of the transformed input (16-bit)
+constexpr int ZROW = C * 2 + 16;       // bytes per token of the transformed input (16-bit)
 constexpr int VROW = G * IO * 4 + 32;  // bytes per token of the mat-vec results (float32)
 constexpr int WBYTES = G * IO * IO / 4;  // packed weights
 constexpr int OFF_V = TM * ZROW, OFF_AB = OFF_V + TM * VROW, OFF_W = OFF_AB + 2 * G * IO * 4;
@@ -126,7 +128,11 @@ hlin_packed_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* __res
           bf[q][nt][h] = ternary_pair16<T16>(a, b);
         }
   }
-  const int trow = tid >> 3, pc = (tid & 7) * 2;  // token row and first column of this thread in A and C
+  // token row and first column of this thread in A and C: a warp's four
+  // tokens are b, b + 2, b + 4, b + 6 (b = 8 (w / 2) + w % 2), so that its
+  // 16-bit row pieces (rows 4 banks apart) and the float32 pairs each half
+  // warp reads in C (rows 8 banks apart) fall in distinct banks
+  const int trow = ((warp >> 1) << 3) | (warp & 1) | ((lane >> 3) << 1), pc = (lane & 7) * 2;
   const uint64_t* ab2 = reinterpret_cast<const uint64_t*>(ab);
   uint32_t xr[G];  // this thread's two input columns of its token, 16-bit pairs
   auto load_x = [&](int64_t tile) {
@@ -206,6 +212,180 @@ hlin_packed_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* __res
   }
 }
 
+// ---------------------------------------------------------------------------
+// C = 2048 (32 groups x 64).  One persistent CTA of 16 warps per SM walks
+// 16-token tiles through one buffer of 16 rows (the 16-bit transformed
+// input, then in place the 16-bit mat-vec results):
+//   A  warp t takes token t of the tile, lane p its columns 2p, 2p + 1 in
+//      each group (one 128-byte line per warp load), scaled by alpha,
+//      butterfly-transformed on float pairs, rounded into the row; the next
+//      tile's columns are then loaded into the same registers;
+//   B  warp w takes groups 2w, 2w + 1: A = the 16 x 64 block of group g
+//      (ldmatrix, all four k-steps held before the block is overwritten),
+//      B = w_g^T, 64 fragments per group decoded from this lane's 2-bit
+//      codes (8 words per group, re-laid in shared memory once per CTA:
+//      code pairs at bits 2r and 2r + 16, decoded as the 16-bit integers
+//      1024 + c (fp16) or 128 + c (bf16) less 1025 or 129, exact); each
+//      16 x 8 result is rounded to the 16-bit type and written over its own
+//      columns of the block;
+//   C  warp t, lane p: output columns 2p, 2p + 1 over the 32 groups, the
+//      butterfly transform, beta / 32, written straight to global memory.
+// Row pitch 4112 bytes: ldmatrix rows and fragment stores fall in distinct
+// banks; the A and C accesses of a warp are one contiguous 128-byte row
+// piece.  A thread's C reads and its next A writes touch the same elements,
+// so a tile needs two block barriers.
+// ---------------------------------------------------------------------------
+namespace hpk4 {
+constexpr int C = 2048, G = 32, IO = 64, TM = 16, NW = 16, NT = NW * 32;
+constexpr int ZROW = C * 2 + 16;
+constexpr int OFF_AB = TM * ZROW;
+constexpr int OFF_W = OFF_AB + 2 * G * IO * 4;  // [2 groups][8 n-tiles][NT threads] code words
+constexpr int SMEM = OFF_W + 16 * NT * 4;
+}  // namespace hpk4
+
+template <typename T16>
+__device__ __forceinline__ uint32_t ternary_code_pair(uint32_t word, int r) {
+  // code pair r of a register word (codes at bits 2r and 2r + 16) as the
+  // 16-bit pair (c_lo - 1, c_hi - 1)
+  if constexpr (std::is_same<T16, __half>::value) {
+    const uint32_t v = ((word >> (2 * r)) & 0x00030003u) | 0x64006400u;  // 1024 + c
+    __half2 h;
+    memcpy(&h, &v, 4);
+    h = __hsub2(h, __float2half2_rn(1025.0f));
+    uint32_t o;
+    memcpy(&o, &h, 4);
+    return o;
+  } else {
+    const uint32_t v = ((word >> (2 * r)) & 0x00030003u) | 0x43004300u;  // 128 + c
+    __nv_bfloat162 h;
+    memcpy(&h, &v, 4);
+    h = __hsub2(h, __float2bfloat162_rn(129.0f));
+    uint32_t o;
+    memcpy(&o, &h, 4);
+    return o;
+  }
+}
+
+template <typename T16>
+__global__ void __launch_bounds__(hpk4::NT, 1)
+hlin_packed2048_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* __restrict__ w2,
+                       const float* __restrict__ alpha, const float* __restrict__ beta, T16* __restrict__ y) {
+  using namespace hpk4;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char* sm = smem_raw;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, t4 = lane & 3;
+  const int64_t ntiles = (ntok + TM - 1) / TM;
+  float* ab = reinterpret_cast<float*>(sm + OFF_AB);  // [G][IO] alpha, then [G][IO] beta / 32
+  for (int q = tid; q < G * IO; q += NT) {
+    ab[q] = __ldg(alpha + q);
+    ab[G * IO + q] = __ldg(beta + q) * (1.0f / 32.0f);
+  }
+  // this lane's codes of w_g^T for groups 2w, 2w + 1: word [q][nt] holds the
+  // pairs r = 2 ks + h (k rows 16 ks + 8 h + 2 t4, + 1; column 8 nt + gid)
+  uint32_t* wpk = reinterpret_cast<uint32_t*>(sm + OFF_W);
+#pragma unroll 1
+  for (int q = 0; q < 2; ++q)
+#pragma unroll 1
+    for (int nt = 0; nt < 8; ++nt) {
+      const int g = 2 * warp + q, o = 8 * nt + gid;
+      const uint8_t* row = w2 + (g * IO + o) * (IO / 4);
+      uint32_t wd = 0;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int i0 = 8 * r + 2 * t4;  // = 16 ks + 8 h + 2 t4
+        const uint32_t byte = __ldg(row + (i0 >> 2));
+        const int s0 = 6 - 2 * (i0 & 3);
+        wd |= ((byte >> s0) & 3u) << (2 * r);
+        wd |= ((byte >> (s0 - 2)) & 3u) << (2 * r + 16);
+      }
+      wpk[(q * 8 + nt) * NT + tid] = wd;
+    }
+  __syncthreads();
+  const int pc = 2 * lane;  // columns of this lane in A and C (token = warp)
+  const uint64_t* ab2 = reinterpret_cast<const uint64_t*>(ab);
+  uint32_t xr[G];
+  auto load_x = [&](int64_t tile) {
+    const int64_t tok = tile * TM + warp;
+    if (tile < ntiles && tok < ntok) {
+      const uint32_t* xp = reinterpret_cast<const uint32_t*>(x + tok * C + pc);
+#pragma unroll
+      for (int g = 0; g < G; ++g) xr[g] = __ldg(xp + g * (IO / 2));
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) xr[g] = 0u;
+    }
+  };
+  load_x(blockIdx.x);
+  const uint32_t zs = tc05::smem_u32(sm);
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int64_t tok = tile * TM + warp;
+    unsigned char* zrow = sm + warp * ZROW + pc * 2;
+    // ---- A
+    {
+      uint64_t v[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float2 f = unpack2<T16>(xr[g]);
+        v[g] = hpk_mul(hpk_pack(f.x, f.y), ab2[(g * IO + pc) / 2]);
+      }
+      load_x(tile + gridDim.x);
+      fht32x2(v);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float2 f = hpk_unpack(v[g]);
+        *reinterpret_cast<uint32_t*>(zrow + g * IO * 2) = pack2<T16>(f.x, f.y);
+      }
+    }
+    __syncthreads();
+    // ---- B: groups 2w, 2w + 1, results over their own block
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int g = 2 * warp + q;
+      uint32_t a[4][4];
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t addr = zs + (uint32_t)((lane & 15) * ZROW + (g * IO + ks * 16 + (lane >> 4) * 8) * 2);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                     : "=r"(a[ks][0]), "=r"(a[ks][1]), "=r"(a[ks][2]), "=r"(a[ks][3])
+                     : "r"(addr)
+                     : "memory");
+      }
+      __syncwarp();
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const uint32_t wd = wpk[(q * 8 + nt) * NT + tid];
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma16<T16>(c, a[ks], ternary_code_pair<T16>(wd, 2 * ks), ternary_code_pair<T16>(wd, 2 * ks + 1));
+        unsigned char* vp = sm + gid * ZROW + (g * IO + 8 * nt + 2 * t4) * 2;
+        *reinterpret_cast<uint32_t*>(vp) = pack2<T16>(c[0], c[1]);
+        *reinterpret_cast<uint32_t*>(vp + 8 * ZROW) = pack2<T16>(c[2], c[3]);
+      }
+    }
+    __syncthreads();
+    // ---- C: output columns pc, pc + 1 of this warp's token over the 32 groups
+    {
+      uint64_t v[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float2 f = unpack2<T16>(*reinterpret_cast<const uint32_t*>(zrow + g * IO * 2));
+        v[g] = hpk_pack(f.x, f.y);
+      }
+      fht32x2(v);
+      if (tok < ntok) {
+        uint32_t* yp = reinterpret_cast<uint32_t*>(y + tok * C + pc);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float2 f = hpk_unpack(hpk_mul(v[h], ab2[(G * IO + h * IO + pc) / 2]));
+          yp[h * (IO / 2)] = pack2<T16>(f.x, f.y);
+        }
+      }
+    }
+    // the next tile's A writes only the elements this thread just read
+  }
+}
+
 static int hlin_pk_sms() {
   static int n = 0;
   if (!n) {
@@ -222,15 +402,31 @@ static int hlin_pk_sms() {
 
 using namespace walsh;
 
-extern "C" walsh_status walsh_hadamard_linear_pk_fwd(const void* x, int dtype, int64_t ntok, const uint8_t* w_2bit,
-                                                     const float* alpha, const float* beta, void* y, void* stream) {
+template <typename T16>
+static int launch_hlin_pk2048(const void* x, int64_t ntok, const uint8_t* w2, const float* alpha, const float* beta,
+                              void* y, cudaStream_t s) {
+  const int64_t ntiles = (ntok + hpk4::TM - 1) / hpk4::TM;
+  const int grid = (int)min64(ntiles, hlin_pk_sms());
+  auto k = hlin_packed2048_kernel<T16>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, hpk4::SMEM) != cudaSuccess)
+    return launch_status();
+  k<<<grid, hpk4::NT, hpk4::SMEM, s>>>((const T16*)x, ntok, w2, alpha, beta, (T16*)y);
+  return launch_status();
+}
+
+extern "C" walsh_status walsh_hadamard_linear_pk_fwd(const void* x, int dtype, int64_t ntok, int features,
+                                                     const uint8_t* w_2bit, const float* alpha, const float* beta,
+                                                     void* y, void* stream) {
   if (int e = injected("hadamard_linear_pk_fwd")) return e;
   WALSH_CHECK_ARG(x && w_2bit && alpha && beta && y);
-  WALSH_CHECK_SHAPE(ntok >= 0);
+  WALSH_CHECK_SHAPE(ntok >= 0 && (features == 512 || features == 2048));
   if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
   if ((((uintptr_t)x) | ((uintptr_t)y) | ((uintptr_t)w_2bit)) & 15u) return WALSH_ERR_ALIGN;
   if (ntok == 0) return WALSH_OK;
   cudaStream_t s = (cudaStream_t)stream;
+  if (features == 2048)
+    return dtype == WALSH_BF16 ? launch_hlin_pk2048<__nv_bfloat16>(x, ntok, w_2bit, alpha, beta, y, s)
+                               : launch_hlin_pk2048<__half>(x, ntok, w_2bit, alpha, beta, y, s);
   const int64_t ntiles = (ntok + hpk2::TM - 1) / hpk2::TM;
   const int grid = (int)min64(ntiles, hlin_pk_sms());
   if (dtype == WALSH_BF16) {

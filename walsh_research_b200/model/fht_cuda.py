@@ -93,8 +93,8 @@ class HadamardLinear(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         alpha, beta = self.scales()
-        if (ops.HLIN_PACKED and x.dtype in (torch.bfloat16, torch.float16) and self.in_features == 512
-                and self.out_features == 512):
+        if (ops.HLIN_PACKED and x.dtype in (torch.bfloat16, torch.float16)
+                and self.in_features == self.out_features and self.in_features in ops.HLIN_PACKED_FEATURES):
             return ops.hadamard_linear_pk(x, self.packed(), alpha, beta)
         if ops.tc_eligible(x) and self.in_features == 512 and self.out_features == 512:
             return ops.hadamard_linear_tc(x, self.ternary_f16(), alpha, beta)

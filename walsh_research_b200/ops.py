@@ -78,19 +78,22 @@ def hadamard_linear_tc(x, w_f16, alpha, beta, w_scale: float = 1.0):
     return y
 
 
-# HadamardLinear(512, 512) on 16-bit activations: True reads the 2-bit packed
-# weights (walsh_hadamard_linear_pk_fwd), False the fp16 weight copies of the
-# mma.sync chain (walsh_hadamard_linear_tc_fwd; kept for comparisons)
+# HadamardLinear(512, 512) and (2048, 2048) on 16-bit activations: True reads
+# the 2-bit packed weights (walsh_hadamard_linear_pk_fwd), False the fp16
+# weight copies of the mma.sync chain (512) or the general kernel (2048);
+# kept for comparisons
 HLIN_PACKED = True
+HLIN_PACKED_FEATURES = (512, 2048)
 
 
 def hadamard_linear_pk(x, packed, alpha, beta):
-    """y = HadamardLinear(x) for x [..., 512] in bfloat16 or float16, weights
-    2-bit packed [32, 16, 4]; y in x's dtype."""
+    """y = HadamardLinear(x) for x [..., F] (F = 512 or 2048) in bfloat16 or
+    float16, weights 2-bit packed [32, F/32, F/128]; y in x's dtype."""
     require_cuda(x)
     x = _c(x)
+    F = x.shape[-1]
     y = torch.empty_like(x)
-    call("walsh_hadamard_linear_pk_fwd", ptr(x), dcode(x.dtype), x.numel() // 512, ptr(packed), ptr(alpha),
+    call("walsh_hadamard_linear_pk_fwd", ptr(x), dcode(x.dtype), x.numel() // F, F, ptr(packed), ptr(alpha),
          ptr(beta), ptr(y), stream())
     return y
 
