@@ -465,6 +465,20 @@ walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrows, int C, i
                                const float* shift, float residual_scale, int add_input, void* out,
                                void* stream);
 
+/* Channel modulation of single-row segments (seg_len 1: batched decode, one
+ * segment per stream row) in one launch: walsh_chmod_stats + walsh_chmod_mlp
+ * + walsh_chmod_apply with the same arguments' meaning, C = 512 only, x and
+ * out 16-bit (WALSH_BF16 / WALSH_F16, 16-byte aligned, out may alias x),
+ * packed weights 4-byte aligned.  scale, shift [nrows, C/32] are written as
+ * by walsh_chmod_mlp.  Layer sums in float32 with a different order than the
+ * three-step form (results agree to float32 rounding).
+ * Replaces HadamardChannelModulation.forward on [B*n, 1, C]
+ * (src/model/moe.py:681-762) inside mHCLlamaBlock.forward (src/model/mhc.py:528-532). */
+walsh_status walsh_chmod_rows_fwd(const void* x, int dtype, int64_t nrows, int C, const float* norm_w,
+                                  float norm_eps, const uint8_t* w1_2bit, const uint8_t* w2_2bit,
+                                  const float* gammas, const float* scale_temp, float residual_scale, int add_input,
+                                  float* scale, float* shift, void* out, void* stream);
+
 /* Allocation-free channel modulation: stats, mlp and apply above in one call,
  * with the scratch (partial sums, scale, shift) in a fixed device array inside
  * the library instead of caller buffers.  No counterpart in the reference (its

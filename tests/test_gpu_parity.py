@@ -417,9 +417,13 @@ def test_chmod_tensor_core_mlp_matches_cuda_core_mlp(C, nseg, seg_len, dt):
     w1, w2c, gam, temp = m.kernel_args()
     x = T((rng.normal(size=(nseg * seg_len, C)) * 3).astype(np.float32), dt)
     nw = T(rng.uniform(0.5, 1.5, size=C).astype(np.float32))
-    y0, s0, h0 = ops.chmod(x, seg_len, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True)
-    y1, s1, h1 = ops.chmod(x, seg_len, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True,
-                           w1_dense=m.w1_dense())
+    ops.CHMOD_ROWS_FUSED = False  # the three-step form on both sides
+    try:
+        y0, s0, h0 = ops.chmod(x, seg_len, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True)
+        y1, s1, h1 = ops.chmod(x, seg_len, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True,
+                               w1_dense=m.w1_dense())
+    finally:
+        ops.CHMOD_ROWS_FUSED = True
     # float64 MLP on the same segment means (RMSNorm'd rows x norm weight, averaged)
     xf = x.double().cpu().numpy().reshape(nseg, seg_len, C)
     xn = xf / np.sqrt((xf * xf).mean(-1, keepdims=True) + 1e-6) * nw.double().cpu().numpy()
@@ -438,6 +442,49 @@ def test_chmod_tensor_core_mlp_matches_cuda_core_mlp(C, nseg, seg_len, dt):
         assert err_tc < max(2 * err_cc, 1e-5), (err_tc, err_cc)
     tol = {torch.float32: 1e-4, torch.float16: 2e-3, torch.bfloat16: 1.6e-2}[dt]  # a few output ulps
     assert rel(y1, y0.float().cpu().numpy()) < tol
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("nrows", [1, 3, 4, 1023, 1024])
+def test_chmod_single_row_segments_fused(nrows, dt):
+    """Single-row segments (batched decode) in one launch (walsh_chmod_rows_fwd,
+    ragged last CTA of 4 rows, in place): scale and shift against a float64 MLP
+    on the same rounded rows, and the applied rows against the three-step
+    kernels (stats, tensor-core or CUDA-core MLP, apply) on the same inputs."""
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model.moe import HadamardChannelModulation
+    C = 512
+    rng = np.random.default_rng(nrows + 7)
+    m = HadamardChannelModulation(C).to(DEV)
+    with torch.no_grad():
+        m.context_mlp[0].weight.copy_(torch.from_numpy(rng.normal(size=(C // 4, C)).astype(np.float32)))
+        m.context_mlp[2].weight.copy_(torch.from_numpy(rng.normal(size=(C // 16, C // 4)).astype(np.float32)))
+        m.scale_temp.fill_(0.3)
+    w1, w2c, gam, temp = m.kernel_args()
+    x = T((rng.normal(size=(nrows, C)) * 3).astype(np.float32), dt)
+    nw = T(rng.uniform(0.5, 1.5, size=C).astype(np.float32))
+    y = x.clone()
+    _, s1, h1 = ops.chmod(y, 1, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True, out=y)
+    ops.CHMOD_ROWS_FUSED = False
+    try:
+        y0, s0, h0 = ops.chmod(x, 1, w1, w2c, gam, temp, norm_w=nw, norm_eps=1e-6, add_input=True,
+                               w1_dense=m.w1_dense())
+    finally:
+        ops.CHMOD_ROWS_FUSED = True
+    xf = x.double().cpu().numpy()
+    bulk = xf / np.sqrt((xf * xf).mean(-1, keepdims=True) + 1e-6) * nw.double().cpu().numpy()
+    t1 = ops.unpack(w1, C).double().cpu().numpy()
+    t2 = ops.unpack(w2c, C // 4).double().cpu().numpy()
+    g = gam.double().cpu().numpy()
+    a1 = bulk @ t1.T * g[0]
+    a2 = (a1 / (1 + np.exp(-a1))) @ t2.T * g[1]
+    E = C // 32
+    s_ref, h_ref = 1 + 0.3 * np.tanh(a2[:, :E]), a2[:, E:]
+    for got, want, three_step in ((s1, s_ref, s0), (h1, h_ref, h0)):
+        err_f, err_3 = rel(got, want), rel(three_step, want)
+        assert err_f < max(2 * err_3, 1e-5), (err_f, err_3)
+    tol = {torch.float16: 2e-3, torch.bfloat16: 1.6e-2}[dt]  # a few output ulps
+    assert rel(y, y0.float().cpu().numpy()) < tol
 
 
 @pytest.mark.parametrize("M,K,N", [(256, 512, 50257), (5, 2048, 1000), (300, 64, 40)])

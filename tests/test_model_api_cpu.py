@@ -160,3 +160,27 @@ def test_sampling_step_matches_the_reference_rule():
         assert torch.equal(got, want)
         if k == 1:
             assert torch.equal(got[:, 0], logits.argmax(-1))
+
+
+def test_decode_parts_rule():
+    """Which steps run in parts on separate streams (host logic): only cached
+    steps of at most 4 tokens from DECODE_PARTS_FROM sequences, without
+    gradients or expert parallelism, and never more parts than sequences."""
+    cfg = dict(cases.WALSH512, vocab_size=128, n_layer=1)
+    model = mHCWalsh(wm.WalshConfig(**cfg), n_streams=4)
+    kv = object()
+    big = model.DECODE_PARTS_FROM
+    with torch.no_grad():
+        assert model._decode_parts(big, 1, kv) == 2
+        assert model._decode_parts(big, 4, kv) == 2
+        assert model._decode_parts(big, 5, kv) == 1          # prefill-sized
+        assert model._decode_parts(big - 1, 1, kv) == 1      # small batch
+        assert model._decode_parts(big, 1, None) == 1        # no KV cache
+        model.decode_streams = 1
+        assert model._decode_parts(big, 1, kv) == 1
+        model.decode_streams = 3
+        assert model._decode_parts(big, 1, kv) == 3
+        model.layers[0].__dict__["_ep"] = object()
+        assert model._decode_parts(big, 1, kv) == 1          # expert parallel
+        del model.layers[0].__dict__["_ep"]
+    assert model._decode_parts(big, 1, kv) == 1              # gradients on

@@ -58,6 +58,7 @@ SIGNATURES = {
     "walsh_chmod_stats": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P],
     "walsh_chmod_mlp": [P, c_int, c_int, c_int, P, P, P, P, P, P, P],
     "walsh_chmod_apply": [P, c_int, c_int64, c_int, c_int, P, c_float, P, P, c_float, c_int, P, P],
+    "walsh_chmod_rows_fwd": [P, c_int, c_int64, c_int, P, c_float, P, P, P, P, c_float, c_int, P, P, P, P],
     "walsh_chmod_mlp_tc": [P, c_int, c_int, c_int, P, P, P, P, P, P, P, P],
     "walsh_linear_split_tc_fwd": [P, c_int64, c_int, P, c_int64, P, P, P],
     "walsh_linear_split_tc_scratch_bytes": [c_int64, c_int],

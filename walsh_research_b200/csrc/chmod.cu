@@ -365,6 +365,154 @@ chmod_apply_kernel(const T* x, int64_t nrows, int C, int seg_len, const float* _
   }
 }
 
+// ---------------------------------------------------------------------------
+// Single-row segments (batched decode: each row of the [B*n, 1, C] view is
+// its own segment), C = 512, in one kernel instead of stats / bulk split /
+// layer-1 GEMM / layer 2 / apply.  A CTA of 256 threads takes 4 rows:
+//   rows     warps 0-3, one row each, held in registers for the last step:
+//            RMS factor, xn = x r w_norm, which is also the segment mean;
+//   layer 1  thread (j, half) sums half of hidden unit j's 512 ternary
+//            weights against the 4 rows (packed W1 staged in shared memory
+//            with 132-byte rows: a warp's 32 rows fall in distinct banks;
+//            the means laid out [channel][row], 16 bytes per channel, one
+//            broadcast load per channel), halves added, h = SiLU(g1 a);
+//   layer 2  thread (r, slice) takes 16 hidden units of output r, summed
+//            over the 8 slices by shuffles: m = g2 W2q h,
+//            scale = 1 + clamp(temp, 0.1, 0.5) tanh(m[:E]), shift = m[E:];
+//   apply    out = x + xn + rs (xn scale + 0.1 shift - xn) from the kept rows.
+// Sums in float32 (layer 1 in channel order within each half).
+// ---------------------------------------------------------------------------
+namespace chrow {
+constexpr int C = 512, R = 4, HID = C / 4, E = C / 32, NT = 256;
+constexpr int WWORDS = C / 16;          // packed W1 row: 32 words
+constexpr int WPITCH = WWORDS + 1;      // shared-memory row pitch in words
+__device__ __forceinline__ int bulk_idx(int c) { return (c + (c >> 3)) * R; }  // 16-byte pad per 8 channels
+}  // namespace chrow
+
+template <typename T>
+__global__ void __launch_bounds__(chrow::NT)
+chmod_rows_kernel(const T* x, int64_t nrows, const float* __restrict__ norm_w, float eps,
+                  const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2, const float* __restrict__ gammas,
+                  const float* __restrict__ scale_temp, float rscale, int add_input, float* __restrict__ scale,
+                  float* __restrict__ shift, T* out) {
+  using namespace chrow;
+  __shared__ uint32_t w1s[HID * WPITCH];
+  __shared__ __align__(16) float bulk[(C + C / 8) * R];
+  __shared__ float red[2 * R * HID];
+  __shared__ float hid[R * HID];
+  __shared__ float mod[R * 2 * E];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row0 = (int64_t)blockIdx.x * R;
+  for (int i = tid; i < HID * WWORDS; i += NT)
+    w1s[(i / WWORDS) * WPITCH + (i % WWORDS)] = __ldg(reinterpret_cast<const uint32_t*>(w1) + i);
+  // ---- rows
+  const int64_t row = row0 + warp;
+  const bool has = warp < R && row < nrows;
+  float v[2][8];
+  float rf = 1.f;
+  if (warp < R) {
+    float s = 0.f;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      if (has) unpack_vec8(ld_vec8(x + row * C + p * 256 + lane * 8), v[p]);
+      else
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[p][e] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(v[p][e], v[p][e], s);
+    }
+    s = warp_sum(s);
+    rf = norm_w ? rsqrtf(s / (float)C + eps) : 1.0f;
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = p * 256 + lane * 8 + e;
+        bulk[bulk_idx(c) + warp] = norm_w ? v[p][e] * rf * __ldg(norm_w + c) : v[p][e];
+      }
+  }
+  __syncthreads();
+  // ---- layer 1
+  {
+    const int j = tid & (HID - 1), half = tid >> 7;
+    float acc[R];
+#pragma unroll
+    for (int z = 0; z < R; ++z) acc[z] = 0.f;
+    const uint32_t* wr = w1s + j * WPITCH + half * (WWORDS / 2);
+#pragma unroll 2
+    for (int wd = 0; wd < WWORDS / 2; ++wd) {
+      const uint32_t word = wr[wd];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int c = half * (C / 2) + wd * 16 + q;
+        const float w = (float)((int)((word >> (8 * (q >> 2) + 6 - 2 * (q & 3))) & 3u) - 1);
+        const float4 b = *reinterpret_cast<const float4*>(bulk + bulk_idx(c));
+        acc[0] = fmaf(w, b.x, acc[0]);
+        acc[1] = fmaf(w, b.y, acc[1]);
+        acc[2] = fmaf(w, b.z, acc[2]);
+        acc[3] = fmaf(w, b.w, acc[3]);
+      }
+    }
+#pragma unroll
+    for (int z = 0; z < R; ++z) red[(half * R + z) * HID + j] = acc[z];
+  }
+  __syncthreads();
+  const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
+  for (int i = tid; i < R * HID; i += NT) {
+    const float a = (red[i] + red[R * HID + i]) * g1;
+    hid[i] = a / (1.0f + expf(-a));
+  }
+  __syncthreads();
+  // ---- layer 2
+  {
+    const int r = tid >> 3, sl = tid & 7;
+    const uint32_t word = __ldg(reinterpret_cast<const uint32_t*>(w2 + (size_t)r * (HID / 4)) + sl);
+    float acc[R];
+#pragma unroll
+    for (int z = 0; z < R; ++z) acc[z] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const float w = (float)((int)((word >> (8 * (q >> 2) + 6 - 2 * (q & 3))) & 3u) - 1);
+#pragma unroll
+      for (int z = 0; z < R; ++z) acc[z] = fmaf(w, hid[z * HID + 16 * sl + q], acc[z]);
+    }
+#pragma unroll
+    for (int z = 0; z < R; ++z) {
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) acc[z] += __shfl_xor_sync(0xffffffffu, acc[z], o);
+      if (sl == 0) mod[z * 2 * E + r] = acc[z] * g2;
+    }
+  }
+  __syncthreads();
+  const float st = fminf(fmaxf(__ldg(scale_temp), 0.1f), 0.5f);
+  if (tid < R * 2 * E) {
+    const int z = tid / (2 * E), k = tid % (2 * E);
+    if (row0 + z < nrows) {
+      const float a = mod[tid];
+      if (k < E) scale[(row0 + z) * E + k] = 1.0f + st * tanhf(a);
+      else shift[(row0 + z) * E + (k - E)] = a;
+    }
+  }
+  // ---- apply (each thread recomputes its block's scale from the same m)
+  if (has) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int b = (p * 256 + lane * 8) >> 5;
+      const float sc = 1.0f + st * tanhf(mod[warp * 2 * E + b]), sh = mod[warp * 2 * E + E + b] * 0.1f;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = p * 256 + lane * 8 + e;
+        const float xn = norm_w ? v[p][e] * rf * __ldg(norm_w + c) : v[p][e];
+        const float xm = xn * sc + sh;
+        const float xo = xn + rscale * (xm - xn);
+        o[e] = add_input ? v[p][e] + xo : xo;
+      }
+      store8(out + row * C + p * 256 + lane * 8, o);
+    }
+  }
+}
+
 }  // namespace walsh
 
 using namespace walsh;
@@ -490,6 +638,30 @@ extern "C" walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrow
                                              (const T*)x, nrows, C, seg_len, norm_w, norm_eps, scale, shift,
                                              residual_scale, add_input, (T*)out),
                                          launch_status()));
+}
+
+extern "C" walsh_status walsh_chmod_rows_fwd(const void* x, int dtype, int64_t nrows, int C, const float* norm_w,
+                                             float norm_eps, const uint8_t* w1_2bit, const uint8_t* w2_2bit,
+                                             const float* gammas, const float* scale_temp, float residual_scale,
+                                             int add_input, float* scale, float* shift, void* out, void* stream) {
+  if (int e = injected("chmod_rows_fwd")) return e;
+  WALSH_CHECK_ARG(x && w1_2bit && w2_2bit && gammas && scale_temp && scale && shift && out);
+  WALSH_CHECK_SHAPE(nrows > 0 && C == chrow::C);
+  if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  if ((((uintptr_t)x) | ((uintptr_t)out)) & 15u || (((uintptr_t)w1_2bit) | ((uintptr_t)w2_2bit)) & 3u)
+    return WALSH_ERR_ALIGN;
+  const int64_t grid = (nrows + chrow::R - 1) / chrow::R;
+  if (grid > 2147483647LL) return WALSH_ERR_SHAPE;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == WALSH_BF16)
+    chmod_rows_kernel<__nv_bfloat16><<<(unsigned)grid, chrow::NT, 0, s>>>(
+        (const __nv_bfloat16*)x, nrows, norm_w, norm_eps, w1_2bit, w2_2bit, gammas, scale_temp, residual_scale,
+        add_input, scale, shift, (__nv_bfloat16*)out);
+  else
+    chmod_rows_kernel<__half><<<(unsigned)grid, chrow::NT, 0, s>>>(
+        (const __half*)x, nrows, norm_w, norm_eps, w1_2bit, w2_2bit, gammas, scale_temp, residual_scale, add_input,
+        scale, shift, (__half*)out);
+  return launch_status();
 }
 
 // ---------------------------------------------------------------------------

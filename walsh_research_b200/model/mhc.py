@@ -145,8 +145,12 @@ class mHCLlamaBlock(nn.Module):
     def _w(self, p):
         return p.detach().float().contiguous()
 
-    def forward_fused(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, record_stats=True):
-        """x [B, T, n, C] (updated in place and returned)."""
+    def forward_fused(self, x, rope_cos, rope_sin, k_cache, v_cache, start_pos: int, record_stats=True,
+                      stats_out=None):
+        """x [B, T, n, C] (updated in place and returned).  ``stats_out``: dict
+        of buffers ("mask", "probs", "weights" [B, T, E]; "scale", "shift"
+        [B*n, E]) that receive this call's router and modulation statistics;
+        the caller records them (used when a batch runs in parts)."""
         B, T, n, C = x.shape
         idt = k_cache.dtype  # storage type of u, q/k/v and the attention output
         # attention site
@@ -169,7 +173,10 @@ class mHCLlamaBlock(nn.Module):
         elif hasattr(ff, "kernel_args"):
             w1t, w2, g, up, d, gam, k, tc = ff.kernel_args(idt)
             rt = ff.router.routing()
-            if record_stats:
+            if stats_out is not None:
+                ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True, tc=tc, routing=rt,
+                        stats_out=(stats_out["mask"], stats_out["probs"], stats_out["weights"]))
+            elif record_stats:
                 _, mask, probs, _ = ops.moe(u, w1t, w2, g, up, d, gam, k, fuse=(x, hmix, x), want_stats=True, tc=tc,
                                             routing=rt)
                 ff._record(mask, probs, B * T)
@@ -183,11 +190,14 @@ class mHCLlamaBlock(nn.Module):
         if self.use_channel_mod:
             w1, w2c, gam, temp = self.channel_mod.kernel_args()
             w1d = self.channel_mod.w1_dense() if B * n >= ops.CHMOD_MLP_TC_FROM else None
+            so = stats_out or {}
             _, scale, shift = ops.chmod(x.view(B * T * n, C), T, w1, w2c, gam, temp,
                                         norm_w=self._w(self.channel_mod_norm.weight),
                                         norm_eps=self.channel_mod_norm.eps, add_input=True, out=x.view(B * T * n, C),
-                                        residual_scale=self.channel_mod.residual_scale, w1_dense=w1d)
-            self.channel_mod._last_scale, self.channel_mod._last_shift = scale, shift
+                                        residual_scale=self.channel_mod.residual_scale, w1_dense=w1d,
+                                        scale_out=so.get("scale"), shift_out=so.get("shift"))
+            if stats_out is None:
+                self.channel_mod._last_scale, self.channel_mod._last_shift = scale, shift
         return x
 
     def forward(self, x, freqs_cis, kv_cache=None, layer_idx=0):
@@ -431,13 +441,17 @@ class mHCWalsh(nn.Module):
                              f"{B} x {idt} (a {dt} residual stream keeps attention in {idt})")
         elif kv_cache.cached_len + T > kv_cache.max_seq_len:
             raise ValueError("KV cache is full")
-        for l, layer in enumerate(self.layers):
-            if kv_cache is not None:
-                kc, vc = kv_cache.k_cache[l], kv_cache.v_cache[l]
-                cpos = kv_cache.cached_len
-            else:
-                cpos = 0
-            layer.forward_fused(x, cos, sin, kc, vc, cpos)
+        parts = self._decode_parts(B, T, kv_cache)
+        if parts > 1:
+            self._layers_in_parts(x, cos, sin, kv_cache, parts)
+        else:
+            for l, layer in enumerate(self.layers):
+                if kv_cache is not None:
+                    kc, vc = kv_cache.k_cache[l], kv_cache.v_cache[l]
+                    cpos = kv_cache.cached_len
+                else:
+                    cpos = 0
+                layer.forward_fused(x, cos, sin, kc, vc, cpos)
         self._last_index_error = err
         need_all = return_hidden or targets is not None
         h_out = self._merge_norm(x, rows_last_only=not need_all)
@@ -455,6 +469,65 @@ class mHCWalsh(nn.Module):
         if return_hidden:
             return logits, loss, h_out
         return logits, loss
+
+    # Batched decode runs the batch in `decode_streams` parts, each on its own
+    # CUDA stream: sequences share nothing inside the layer stack, so one
+    # part's latency-bound small kernels (mapping, projections, router, MoE,
+    # modulation) run beside another part's attention, which streams the KV
+    # cache.  Every kernel sees the rows it would see on the whole batch; the
+    # parts join before the final norm and logits.
+    decode_streams = 2
+    DECODE_PARTS_FROM = 128  # batch size from which a T <= 4 step is split
+
+    def _decode_parts(self, B, T, kv_cache):
+        if kv_cache is None or T > 4 or B < self.DECODE_PARTS_FROM or self.decode_streams < 2:
+            return 1
+        if torch.is_grad_enabled() or any(l.__dict__.get("_ep") is not None for l in self.layers):
+            return 1
+        return min(int(self.decode_streams), B)
+
+    def _side_streams(self, dev, k):
+        cache = self.__dict__.setdefault("_part_streams", {})
+        key = (dev.index, k)
+        if key not in cache:
+            cache[key] = [torch.cuda.Stream(device=dev) for _ in range(k)]
+        return cache[key]
+
+    def _layers_in_parts(self, x, cos, sin, kv_cache, parts):
+        B, T, n, C = x.shape
+        E, dev = C // 32, x.device
+        cpos = kv_cache.cached_len
+        bounds = [B * i // parts for i in range(parts + 1)]
+        # full-batch statistics buffers; each part writes its rows
+        stats = []
+        for layer in self.layers:
+            st = {}
+            if hasattr(layer.feed_forward, "kernel_args"):
+                st["mask"] = torch.empty((B, T, E), dtype=torch.uint8, device=dev)
+                st["probs"] = torch.empty((B, T, E), dtype=torch.float32, device=dev)
+                st["weights"] = torch.empty((B, T, E), dtype=torch.float32, device=dev)
+            if layer.use_channel_mod:
+                st["scale"] = torch.empty((B * n, E), dtype=torch.float32, device=dev)
+                st["shift"] = torch.empty((B * n, E), dtype=torch.float32, device=dev)
+            stats.append(st)
+        main = torch.cuda.current_stream(dev)
+        side = self._side_streams(dev, parts - 1)
+        for s in side:
+            s.wait_stream(main)
+        for l, layer in enumerate(self.layers):
+            kc, vc = kv_cache.k_cache[l], kv_cache.v_cache[l]
+            for p in range(parts):
+                b0, b1 = bounds[p], bounds[p + 1]
+                so = {k: (v[b0 * n:b1 * n] if k in ("scale", "shift") else v[b0:b1]) for k, v in stats[l].items()}
+                with torch.cuda.stream(main if p == 0 else side[p - 1]):
+                    layer.forward_fused(x[b0:b1], cos, sin, kc[b0:b1], vc[b0:b1], cpos, stats_out=so)
+        for s in side:
+            main.wait_stream(s)
+        for layer, st in zip(self.layers, stats):
+            if "mask" in st:
+                layer.feed_forward._record(st["mask"], st["probs"], B * T)
+            if "scale" in st:
+                layer.channel_mod._last_scale, layer.channel_mod._last_shift = st["scale"], st["shift"]
 
     def check_token_ids(self):
         """Raise if the last forward saw a token id outside the vocabulary."""

@@ -211,14 +211,15 @@ def routing_struct(routing):
 
 
 def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=None, want_stats=False, tc=None,
-        routing=None):
+        routing=None, stats_out=None):
     """Router + experts.  With ``fuse=(x, hmix, x_out)`` the mHC epilogue is
     applied and ``x_out`` returned; otherwise the expert output y.
     With ``want_stats`` also returns (mask uint8, probs, weights).
     ``tc``: (w1, w2, gate, up, down) bfloat16 copies enabling the tensor-core kernel.
     ``routing``: None for the reference's top-k selection, or (min_experts,
     threshold) for the threshold rule (every expert with p > threshold, at
-    least min_experts, at most top_k)."""
+    least min_experts, at most top_k).  ``stats_out``: (mask, probs, weights)
+    buffers to write the statistics into instead of new tensors."""
     require_cuda(u)
     rt = routing_struct(routing)
     tcs = None
@@ -231,7 +232,9 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
     ntok = u.numel() // C
     lead = u.shape[:-1]
     mask = probs = weights = None
-    if want_stats:
+    if want_stats and stats_out is not None:
+        mask, probs, weights = stats_out
+    elif want_stats:
         mask = torch.empty(lead + (E,), dtype=torch.uint8, device=u.device)
         probs = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
         weights = torch.empty(lead + (E,), dtype=torch.float32, device=u.device)
@@ -286,13 +289,18 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
 # from this many segments (batched decode: one per stream row) the
 # channel-modulation MLP's first layer runs as a tensor-core GEMM
 CHMOD_MLP_TC_FROM = 512
+# single-row segments (seg_len 1, C 512, 16-bit rows) in one launch
+# (walsh_chmod_rows_fwd); False keeps the stats / mlp / apply steps
+CHMOD_ROWS_FUSED = True
 
 
 def chmod(x, seg_len, w1_p, w2_p, gammas, scale_temp, norm_w=None, norm_eps=1e-6, add_input=True, out=None,
-          residual_scale=0.5, w1_dense=None):
+          residual_scale=0.5, w1_dense=None, scale_out=None, shift_out=None):
     """Channel modulation over rows of x viewed as [nseg, seg_len, C].
     ``w1_dense``: W1 as dense bfloat16 [C/4, C] (the ternary values), enabling
-    the tensor-core first layer from CHMOD_MLP_TC_FROM segments."""
+    the tensor-core first layer from CHMOD_MLP_TC_FROM segments.
+    ``scale_out``/``shift_out``: float32 [nseg, C/32] buffers for the
+    per-segment scale and shift (new tensors when None)."""
     require_cuda(x)
     x = _c(x)
     C = x.shape[-1]
@@ -300,14 +308,24 @@ def chmod(x, seg_len, w1_p, w2_p, gammas, scale_temp, norm_w=None, norm_eps=1e-6
     if nrows % seg_len:
         raise ValueError("rows must be a multiple of the segment length")
     nseg = nrows // seg_len
+    E = C // 32
+    if (seg_len == 1 and C == 512 and CHMOD_ROWS_FUSED and x.dtype in (torch.bfloat16, torch.float16)
+            and (out is None or out.dtype == x.dtype)):
+        # one launch for single-row segments (batched decode)
+        scale = scale_out if scale_out is not None else torch.empty((nseg, E), dtype=torch.float32, device=x.device)
+        shift = shift_out if shift_out is not None else torch.empty((nseg, E), dtype=torch.float32, device=x.device)
+        out = out if out is not None else torch.empty_like(x)
+        call("walsh_chmod_rows_fwd", ptr(x), dcode(x.dtype), nrows, C, ptr(norm_w), float(norm_eps), ptr(w1_p),
+             ptr(w2_p), ptr(gammas), ptr(scale_temp), float(residual_scale), 1 if add_input else 0, ptr(scale),
+             ptr(shift), ptr(out), stream())
+        return out, scale, shift
     chunk = call("walsh_chmod_chunk_rows", int(seg_len))
     nch = (seg_len + chunk - 1) // chunk
     partial = torch.empty((nseg, nch, C), dtype=torch.float32, device=x.device)
     call("walsh_chmod_stats", ptr(x), dcode(x.dtype), nrows, C, int(seg_len), ptr(norm_w), float(norm_eps),
          ptr(partial), stream())
-    E = C // 32
-    scale = torch.empty((nseg, E), dtype=torch.float32, device=x.device)
-    shift = torch.empty((nseg, E), dtype=torch.float32, device=x.device)
+    scale = scale_out if scale_out is not None else torch.empty((nseg, E), dtype=torch.float32, device=x.device)
+    shift = shift_out if shift_out is not None else torch.empty((nseg, E), dtype=torch.float32, device=x.device)
     if w1_dense is not None and nseg >= CHMOD_MLP_TC_FROM and C % 64 == 0:
         nbytes = call("walsh_chmod_mlp_tc_scratch_bytes", nseg, C)
         scratch = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
