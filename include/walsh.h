@@ -355,6 +355,11 @@ walsh_status walsh_moe_experts_tc_fwd(const void* u, int dtype, int64_t ntok, co
  * No counterpart in the reference (selects between this library's own two
  * mainloops, e.g. to compare them in tests). */
 int walsh_octo_set_mainloop(int tcgen05);
+/* Few-row GEMMs (a 256-wide tiling that would occupy at most a quarter of the
+ * SMs) run with 64-wide CTA tiles when on (the default); on = 0 keeps the
+ * 256-wide tiles, on < 0 only queries.  Returns the previous setting.  A
+ * switch for comparisons: both tilings give the same sums. */
+int walsh_octo_set_narrow(int on);
 
 /* Status word of the tcgen05 kernels (GEMMs and prefill attention) on the
  * current device: 0, or WALSH_ERR_TIMEOUT once a bounded wait inside one of
@@ -469,7 +474,7 @@ walsh_status walsh_chmod_apply(const void* x, int dtype, int64_t nrows, int C, i
  * segment per stream row) in one launch: walsh_chmod_stats + walsh_chmod_mlp
  * + walsh_chmod_apply with the same arguments' meaning, C = 512 only, x and
  * out 16-bit (WALSH_BF16 / WALSH_F16, 16-byte aligned, out may alias x),
- * packed weights 4-byte aligned.  scale, shift [nrows, C/32] are written as
+ * packed W1 16-byte and W2 4-byte aligned.  scale, shift [nrows, C/32] are written as
  * by walsh_chmod_mlp.  Layer sums in float32 with a different order than the
  * three-step form (results agree to float32 rounding).
  * Replaces HadamardChannelModulation.forward on [B*n, 1, C]

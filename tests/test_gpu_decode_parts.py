@@ -30,7 +30,7 @@ def _step(m, cfg, ids, prompt, parts, graph):
     C, H = cfg["n_embd"], cfg["n_head"]
     idt = _lib.inner_dtype(m._act_dtype())
     kv = KVCache(cfg["n_layer"], cfg["block_size"], H, C // H, DEV, dtype=idt, batch_size=B)
-    m.decode_streams = parts
+    prev, m.decode_streams = m.decode_streams, parts
     with torch.no_grad():
         m(prompt, kv_cache=kv, start_pos=0)
         kv.increment(prompt.shape[1])
@@ -50,7 +50,7 @@ def _step(m, cfg, ids, prompt, parts, graph):
            "probs": ff._last_router_probs.float().cpu().reshape(B, -1)}
     if cm is not None:
         out["scale"] = cm._last_scale.cpu()
-    m.decode_streams = 2
+    m.decode_streams = prev
     return out
 
 
@@ -67,4 +67,11 @@ def test_decode_in_parts_equals_whole_batch(dtype, graph):
     for parts in (2, 3):
         split = _step(m, cfg, ids, prompt, parts, graph)
         for key in whole:
-            assert torch.equal(whole[key], split[key]), (parts, key)
+            if dtype == torch.float32:
+                # float32 modulation MLP: the tensor-core form (split bf16
+                # GEMM) from CHMOD_MLP_TC_FROM segments, the CUDA-core form
+                # below, so a part may take the other one: float32 rounding
+                d = (whole[key] - split[key]).abs().max().item()
+                assert d <= 1e-4 * max(whole[key].abs().max().item(), 1e-30), (parts, key, d)
+            else:
+                assert torch.equal(whole[key], split[key]), (parts, key)

@@ -481,8 +481,10 @@ def test_chmod_single_row_segments_fused(nrows, dt):
     E = C // 32
     s_ref, h_ref = 1 + 0.3 * np.tanh(a2[:, :E]), a2[:, E:]
     for got, want, three_step in ((s1, s_ref, s0), (h1, h_ref, h0)):
+        # float32 sums in channel order (two halves of 256) against the split
+        # bf16 tensor-core GEMM: both at float32 rounding of K = 512 sums
         err_f, err_3 = rel(got, want), rel(three_step, want)
-        assert err_f < max(2 * err_3, 1e-5), (err_f, err_3)
+        assert err_f < max(4 * err_3, 3e-5), (err_f, err_3)
     tol = {torch.float16: 2e-3, torch.bfloat16: 1.6e-2}[dt]  # a few output ulps
     assert rel(y, y0.float().cpu().numpy()) < tol
 

@@ -189,3 +189,58 @@ def test_moe_tcgen05_matches_mma_sync_kernel(n, udt, xdt):
     assert np.abs(y1 - y0)[ok].max() / scale < 1e-2
     fs = np.abs(f0).max()
     assert np.abs(f1 - f0)[ok].max() / fs < 1e-2
+
+
+@pytest.mark.parametrize("M,fin,fout", [(256, 512, 512), (256, 512, 1536), (37, 512, 1368), (129, 64, 200)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_narrow_tiles_equal_wide_tiles(mainloop, M, fin, fout, dtype):
+    """Few-row GEMMs run with 64-wide CTA tiles (more CTAs on the same
+    columns): the same K order per output, so the results equal the 256-wide
+    tiling bit for bit (plain epilogue, ragged N; the q/k/v epilogue with RoPE
+    and the KV-cache rows)."""
+    from walsh_research_b200 import _lib
+    rng = np.random.default_rng(M + fin + fout)
+    m = _layer(fin, fout, rng)
+    x = T(rng.normal(size=(M, fin)).astype(np.float32), dtype)
+    prev = _lib.call("walsh_octo_set_narrow", -1)
+    try:
+        _lib.call("walsh_octo_set_narrow", 1)
+        a = mainloop(lambda: m.forward_flat(x), True)
+        _lib.call("walsh_octo_set_narrow", 0)
+        b = mainloop(lambda: m.forward_flat(x), True)
+    finally:
+        _lib.call("walsh_octo_set_narrow", prev)
+    assert torch.equal(a, b)
+
+
+def test_narrow_tiles_qkv_epilogue_equal_wide(mainloop):
+    from walsh_research_b200 import _lib
+    from walsh_research_b200.model import WalshConfig
+    from walsh_research_b200.model.chassis import CausalSelfAttention, precompute_freqs_cis
+    rng = np.random.default_rng(99)
+    cfg = WalshConfig(n_embd=512, n_head=32, algebra="octonion", head_mixing=True)
+    attn = CausalSelfAttention(cfg)
+    with torch.no_grad():
+        for lin in (attn.wq, attn.wk, attn.wv):
+            lin.weight.copy_(torch.from_numpy(rng.uniform(-1, 1, tuple(lin.weight.shape)).astype(np.float32)))
+    attn = attn.to(DEV)
+    B, Tn, ctx, start = 256, 1, 40, 33
+    u = T(rng.normal(size=(B, Tn, 512)).astype(np.float32), torch.float16)
+    f = precompute_freqs_cis(16, ctx + 16)
+    cos, sin = f.real[start:start + Tn].float().contiguous().to(DEV), f.imag[start:start + Tn].float().contiguous().to(DEV)
+
+    def qkv():
+        q = torch.zeros((B, 32, Tn, 16), dtype=torch.float16, device=DEV)
+        kc = torch.zeros((B, 32, ctx, 16), dtype=torch.float16, device=DEV)
+        vc = torch.zeros_like(kc)
+        attn._octonion_qkv(u, cos, sin, start, q, kc, vc)
+        return torch.cat([q.flatten(), kc.flatten(), vc.flatten()])
+    prev = _lib.call("walsh_octo_set_narrow", -1)
+    try:
+        _lib.call("walsh_octo_set_narrow", 1)
+        a = mainloop(qkv, True)
+        _lib.call("walsh_octo_set_narrow", 0)
+        b = mainloop(qkv, True)
+    finally:
+        _lib.call("walsh_octo_set_narrow", prev)
+    assert torch.equal(a, b)

@@ -170,6 +170,8 @@ def test_decode_parts_rule():
     model = mHCWalsh(wm.WalshConfig(**cfg), n_streams=4)
     kv = object()
     big = model.DECODE_PARTS_FROM
+    assert model.decode_streams == 1 and model._decode_parts(big, 1, kv) == 1  # off by default
+    model.decode_streams = 2
     with torch.no_grad():
         assert model._decode_parts(big, 1, kv) == 2
         assert model._decode_parts(big, 4, kv) == 2

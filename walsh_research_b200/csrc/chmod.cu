@@ -15,6 +15,7 @@
 #include <cuda.h>
 
 #include "common.cuh"
+#include "mma.cuh"
 #include "ctx_cache.h"
 
 namespace walsh {
@@ -370,24 +371,39 @@ chmod_apply_kernel(const T* x, int64_t nrows, int C, int seg_len, const float* _
 // its own segment), C = 512, in one kernel instead of stats / bulk split /
 // layer-1 GEMM / layer 2 / apply.  A CTA of 256 threads takes 4 rows:
 //   rows     warps 0-3, one row each, held in registers for the last step:
-//            RMS factor, xn = x r w_norm, which is also the segment mean;
-//   layer 1  thread (j, half) sums half of hidden unit j's 512 ternary
-//            weights against the 4 rows (packed W1 staged in shared memory
-//            with 132-byte rows: a warp's 32 rows fall in distinct banks;
-//            the means laid out [channel][row], 16 bytes per channel, one
-//            broadcast load per channel), halves added, h = SiLU(g1 a);
+//            RMS factor, xn = x r w_norm, which is also the segment mean,
+//            split into bf16 hi + mid + lo (their sum is xn to float32
+//            precision) as rows z, 4 + z, 8 + z of a 16-row MMA operand
+//            (rows 12-15 zero);
+//   layer 1  warp w: hidden units 16 w .. 16 w + 15 as two m16n8k16 bf16
+//            MMAs per 16 channels, A the split rows (ldmatrix), B the
+//            ternary W1 values decoded from the packed rows staged in shared
+//            memory (132-byte rows: the eight rows a warp reads fall in
+//            distinct banks); h = SiLU(g1 ((hi + mid) + lo)), the sums of the
+//            tensor-core form;
 //   layer 2  thread (r, slice) takes 16 hidden units of output r, summed
 //            over the 8 slices by shuffles: m = g2 W2q h,
 //            scale = 1 + clamp(temp, 0.1, 0.5) tanh(m[:E]), shift = m[E:];
 //   apply    out = x + xn + rs (xn scale + 0.1 shift - xn) from the kept rows.
-// Sums in float32 (layer 1 in channel order within each half).
 // ---------------------------------------------------------------------------
 namespace chrow {
 constexpr int C = 512, R = 4, HID = C / 4, E = C / 32, NT = 256;
-constexpr int WWORDS = C / 16;          // packed W1 row: 32 words
+constexpr int WWORDS = C / 16;          // packed W1 row: 32 words of 16 codes
 constexpr int WPITCH = WWORDS + 1;      // shared-memory row pitch in words
-__device__ __forceinline__ int bulk_idx(int c) { return (c + (c >> 3)) * R; }  // 16-byte pad per 8 channels
+constexpr int APITCH = C + 8;           // MMA operand row pitch in bf16 (1040 bytes)
 }  // namespace chrow
+
+// bf16 pair (c_lo - 1, c_hi - 1) of two 2-bit codes: the integers 128 + c in
+// bf16 less 129 (exact)
+__device__ __forceinline__ uint32_t chrow_code_pair(uint32_t c_lo, uint32_t c_hi) {
+  const uint32_t v = c_lo | (c_hi << 16) | 0x43004300u;
+  __nv_bfloat162 h;
+  memcpy(&h, &v, 4);
+  h = __hsub2(h, __float2bfloat162_rn(129.0f));
+  uint32_t o;
+  memcpy(&o, &h, 4);
+  return o;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(chrow::NT)
@@ -397,14 +413,27 @@ chmod_rows_kernel(const T* x, int64_t nrows, const float* __restrict__ norm_w, f
                   float* __restrict__ shift, T* out) {
   using namespace chrow;
   __shared__ uint32_t w1s[HID * WPITCH];
-  __shared__ __align__(16) float bulk[(C + C / 8) * R];
-  __shared__ float red[2 * R * HID];
+  __shared__ __align__(16) __nv_bfloat16 as[16 * APITCH];
   __shared__ float hid[R * HID];
   __shared__ float mod[R * 2 * E];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, t4 = lane & 3;
   const int64_t row0 = (int64_t)blockIdx.x * R;
-  for (int i = tid; i < HID * WWORDS; i += NT)
-    w1s[(i / WWORDS) * WPITCH + (i % WWORDS)] = __ldg(reinterpret_cast<const uint32_t*>(w1) + i);
+  // packed W1 (16 KB): all four 16-byte loads of a thread in flight at once
+  {
+    constexpr int NV = HID * WWORDS / 4 / NT;  // 4
+    uint4 wv[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) wv[k] = __ldg(reinterpret_cast<const uint4*>(w1) + tid + k * NT);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i4 = tid + k * NT, r = i4 / (WWORDS / 4), w0 = (i4 % (WWORDS / 4)) * 4;
+      uint32_t* d = w1s + r * WPITCH + w0;
+      d[0] = wv[k].x;
+      d[1] = wv[k].y;
+      d[2] = wv[k].z;
+      d[3] = wv[k].w;
+    }
+  }
   // ---- rows
   const int64_t row = row0 + warp;
   const bool has = warp < R && row < nrows;
@@ -424,43 +453,72 @@ chmod_rows_kernel(const T* x, int64_t nrows, const float* __restrict__ norm_w, f
     s = warp_sum(s);
     rf = norm_w ? rsqrtf(s / (float)C + eps) : 1.0f;
 #pragma unroll
-    for (int p = 0; p < 2; ++p)
+    for (int p = 0; p < 2; ++p) {
+      uint32_t hw[4], mw[4], lw[4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int c = p * 256 + lane * 8 + e;
-        bulk[bulk_idx(c) + warp] = norm_w ? v[p][e] * rf * __ldg(norm_w + c) : v[p][e];
+      for (int e = 0; e < 8; e += 2) {
+        float hi2[2], md2[2], lo2[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int c = p * 256 + lane * 8 + e + k;
+          const float b = norm_w ? v[p][e + k] * rf * __ldg(norm_w + c) : v[p][e + k];
+          const float h = __bfloat162float(__float2bfloat16_rn(b));
+          const float r1 = b - h;
+          const float m = __bfloat162float(__float2bfloat16_rn(r1));
+          hi2[k] = h;
+          md2[k] = m;
+          lo2[k] = r1 - m;
+        }
+        hw[e / 2] = pack_bf16(hi2[0], hi2[1]);
+        mw[e / 2] = pack_bf16(md2[0], md2[1]);
+        lw[e / 2] = pack_bf16(lo2[0], lo2[1]);
       }
+      const int c0 = p * 256 + lane * 8;
+      *reinterpret_cast<uint4*>(as + warp * APITCH + c0) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(as + (4 + warp) * APITCH + c0) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+      *reinterpret_cast<uint4*>(as + (8 + warp) * APITCH + c0) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+  } else {
+    // warps 4-7 clear rows 12-15
+    for (int c = lane * 8; c < C; c += 256)
+      *reinterpret_cast<uint4*>(as + (12 + (warp - 4)) * APITCH + c) = make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
-  // ---- layer 1
+  // ---- layer 1 on the tensor cores: warp w, hidden units 16 w + 8 nt + (0..7)
+  const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
   {
-    const int j = tid & (HID - 1), half = tid >> 7;
-    float acc[R];
+    float acc[2][4];
 #pragma unroll
-    for (int z = 0; z < R; ++z) acc[z] = 0.f;
-    const uint32_t* wr = w1s + j * WPITCH + half * (WWORDS / 2);
-#pragma unroll 2
-    for (int wd = 0; wd < WWORDS / 2; ++wd) {
-      const uint32_t word = wr[wd];
+    for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    const uint32_t abase = (uint32_t)__cvta_generic_to_shared(as);
+    const int sh_a = 8 * (t4 >> 1) + 6 - 4 * (t4 & 1);  // code of channel 16 ks + 2 t4 in its word
+#pragma unroll 4
+    for (int ks = 0; ks < WWORDS; ++ks) {
+      uint32_t a[4];
+      const uint32_t addr = abase + (uint32_t)(((lane & 15) * APITCH + ks * 16 + (lane >> 4) * 8) * 2);
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                   : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                   : "r"(addr));
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const int c = half * (C / 2) + wd * 16 + q;
-        const float w = (float)((int)((word >> (8 * (q >> 2) + 6 - 2 * (q & 3))) & 3u) - 1);
-        const float4 b = *reinterpret_cast<const float4*>(bulk + bulk_idx(c));
-        acc[0] = fmaf(w, b.x, acc[0]);
-        acc[1] = fmaf(w, b.y, acc[1]);
-        acc[2] = fmaf(w, b.z, acc[2]);
-        acc[3] = fmaf(w, b.w, acc[3]);
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint32_t wd = w1s[(16 * warp + 8 * nt + gid) * WPITCH + ks];
+        // channels 16 ks + 2 t4, +1 (b0) and + 8, + 9 (b1): bytes t4/2 and t4/2 + 2
+        const uint32_t b0 = chrow_code_pair((wd >> sh_a) & 3u, (wd >> (sh_a - 2)) & 3u);
+        const uint32_t b1 = chrow_code_pair((wd >> (sh_a + 16)) & 3u, (wd >> (sh_a + 14)) & 3u);
+        mma16<__nv_bfloat16>(acc[nt], a, b0, b1);
       }
     }
+    // rows gid (hi for gid < 4, mid for gid >= 4) and gid + 8 (lo for gid < 4)
 #pragma unroll
-    for (int z = 0; z < R; ++z) red[(half * R + z) * HID + j] = acc[z];
-  }
-  __syncthreads();
-  const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
-  for (int i = tid; i < R * HID; i += NT) {
-    const float a = (red[i] + red[R * HID + i]) * g1;
-    hid[i] = a / (1.0f + expf(-a));
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float mid = __shfl_xor_sync(0xffffffffu, acc[nt][e], 16);
+        if (gid < 4) {
+          const float a1 = ((acc[nt][e] + mid) + acc[nt][2 + e]) * g1;
+          hid[gid * HID + 16 * warp + 8 * nt + 2 * t4 + e] = a1 / (1.0f + expf(-a1));
+        }
+      }
   }
   __syncthreads();
   // ---- layer 2
@@ -648,7 +706,7 @@ extern "C" walsh_status walsh_chmod_rows_fwd(const void* x, int dtype, int64_t n
   WALSH_CHECK_ARG(x && w1_2bit && w2_2bit && gammas && scale_temp && scale && shift && out);
   WALSH_CHECK_SHAPE(nrows > 0 && C == chrow::C);
   if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
-  if ((((uintptr_t)x) | ((uintptr_t)out)) & 15u || (((uintptr_t)w1_2bit) | ((uintptr_t)w2_2bit)) & 3u)
+  if ((((uintptr_t)x) | ((uintptr_t)out) | ((uintptr_t)w1_2bit)) & 15u || ((uintptr_t)w2_2bit) & 3u)
     return WALSH_ERR_ALIGN;
   const int64_t grid = (nrows + chrow::R - 1) / chrow::R;
   if (grid > 2147483647LL) return WALSH_ERR_SHAPE;

@@ -388,28 +388,34 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
     tc05::mbar_arrive_expect_tx(bar, X_BYTES);
     for (int b = 0; b < NBOX; ++b) tc05::tma_load_2d(xs + b * BOX_BYTES, &tmx, bar, b * BOXC, (int)tok0);
   }
+  // 1. partial projections over this warp's columns; the first 16 k-steps'
+  // phi fragments are loaded while the TMA copies are in flight
+  constexpr int KB = KS < 16 ? KS : 16;  // k-steps per fragment batch
+  uint2 fr[KB][3];
+  auto load_frags = [&](int kb) {
+#pragma unroll
+    for (int j = 0; j < KB; ++j) {
+      const uint2* fp = phif + ((size_t)(kb + j) * 32 + lane) * 3;
+      fr[j][0] = __ldg(fp);
+      fr[j][1] = __ldg(fp + 1);
+      fr[j][2] = __ldg(fp + 2);
+    }
+  };
+  load_frags(warp * KS);
   if (!tc05::mbar_wait(bar, 0)) {
     if (tid == 0) atomicExch(&g_map_tma_error, (int)WALSH_ERR_TIMEOUT);
     return;
   }
-  // 1. partial projections over this warp's columns (phi fragments loaded 8 k-steps at a time)
   float acc[3][4];
 #pragma unroll
   for (int n = 0; n < 3; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
   float ss_lo = 0.f, ss_hi = 0.f;
   const uint32_t xbase = tc05::smem_u32(xs);
 #pragma unroll 1
-  for (int kb8 = warp * KS; kb8 < warp * KS + KS; kb8 += 8) {
-    uint2 fr[8][3];
+  for (int kb8 = warp * KS; kb8 < warp * KS + KS; kb8 += KB) {
+    if (kb8 != warp * KS) load_frags(kb8);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint2* fp = phif + ((size_t)(kb8 + j) * 32 + lane) * 3;
-      fr[j][0] = __ldg(fp);
-      fr[j][1] = __ldg(fp + 1);
-      fr[j][2] = __ldg(fp + 2);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < KB; ++j) {
       const int ks = kb8 + j;
       const int r = lane & 15, col = ks * 16 + (lane >> 4) * 8;
       uint32_t a[4];

@@ -816,12 +816,16 @@ struct OctoTcShape {
 // Set when a bounded wait of a tcgen05 kernel in this file gave up.
 __device__ int g_tc05_error;
 
-template <typename TA, class Epi>
+template <typename TA, class Epi, int BNT>
 __global__ void __launch_bounds__(octo_tc::NTHREADS, 1)
 octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                       int64_t M, int K, int64_t N, Epi epi, int vec, int nstage, int depth) {
   using namespace octo_tc;
   using namespace tc05;
+  // BNT: the CTA tile's width (256; 64 for few-row GEMMs, so that more CTAs
+  // share the columns); the stage keeps the 256-wide layout's offsets
+  constexpr int BN = BNT, B_BYTES = BN * BK * 2;
+  static_assert(BN == 256 || (BN == 64 && Epi::kRowEpilogue == 0 && Epi::kWarpScratch == 0), "tile width");
   const int STAGES = nstage;  // mainloop stages of this launch (2..4)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -870,7 +874,7 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[st], STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[st], A_BYTES + B_BYTES);
           tma_load_2d(smem + st * STAGE_BYTES, &tma_a, &full[st], kt * BK, m0);
           tma_load_2d(smem + st * STAGE_BYTES + A_BYTES, &tma_b, &full[st], kt * BK, n0);
         }
@@ -934,7 +938,7 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
         epi.row(m, base - (uint32_t)(half * (BN / 2)), half, q * 32 + lane, i & 1, rowscr, M);
         done = true;
       }
-      if constexpr (Epi::kHalfRow > 0) {
+      if constexpr (Epi::kHalfRow > 0 && BN == 256) {
         if (vec == 2 && n0 + BN / 2 <= N) {  // uniform over the warp
           epi.half_row(m, n0, base, rowscr, M);
           done = true;
@@ -983,15 +987,15 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
 
 // 1 when the tcgen05 path ran, 0 when it does not apply (caller falls back),
 // negative on a launch error.
-template <typename TA, class Epi>
-static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int64_t N, const Epi& epi,
-                            cudaStream_t s) {
+template <typename TA, class Epi, int BNT>
+static int launch_octo_tc05_bn(const void* a, int64_t M, int K, const void* w, int64_t N, const Epi& epi,
+                               cudaStream_t s) {
   using namespace octo_tc;
   if (M < 1 || M > 2147483647LL || N > 2147483647LL) return 0;
   constexpr bool BF = std::is_same<TA, __nv_bfloat16>::value;
   CUtensorMap ma, mb;
-  if (!make_tile_map(&ma, a, BF, M, K, octo_tc::BK, BM) || !make_tile_map(&mb, w, BF, N, K, octo_tc::BK, BN)) return 0;
-  auto kern = octo_gemm_tc05_kernel<TA, Epi>;
+  if (!make_tile_map(&ma, a, BF, M, K, octo_tc::BK, BM) || !make_tile_map(&mb, w, BF, N, K, octo_tc::BK, BNT)) return 0;
+  auto kern = octo_gemm_tc05_kernel<TA, Epi, BNT>;
   const OctoTcShape<Epi> shp(K);
   const int SMEM_B = shp.smem;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_B) != cudaSuccess)
@@ -1003,15 +1007,31 @@ static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int6
                                                    cudaSuccess)
       sms = 148;
   }
-  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BNT - 1) / BNT);
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
   int vec = epi.vec_ok() ? 1 : 0;  // 2: the epilogue's row path (half_row) applies
-  if constexpr (Epi::kHalfRow > 0) {
+  if constexpr (Epi::kHalfRow > 0 && BNT == 256) {
     if (epi.half_row_ok()) vec = 2;
   }
   kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, M, K, N, epi, vec, shp.stages, shp.depth);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
+}
+
+// Few-row GEMMs (batched decode: M of a few hundred) whose 256-wide tiles
+// would occupy a small fraction of the SMs run with 64-wide tiles; epilogues
+// with a row or warp-cooperative path keep the 256-wide tile.
+int g_octo_narrow = 1;
+template <typename TA, class Epi>
+static int launch_octo_tc05(const void* a, int64_t M, int K, const void* w, int64_t N, const Epi& epi,
+                            cudaStream_t s) {
+  using namespace octo_tc;
+  if constexpr (Epi::kRowEpilogue == 0 && Epi::kWarpScratch == 0) {
+    const int64_t wide = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    if (g_octo_narrow && wide * 4 <= 148 && N >= 128)
+      return launch_octo_tc05_bn<TA, Epi, 64>(a, M, K, w, N, epi, s);
+  }
+  return launch_octo_tc05_bn<TA, Epi, 256>(a, M, K, w, N, epi, s);
 }
 
 template <typename TA, class Epi>
@@ -1194,6 +1214,12 @@ extern "C" walsh_status walsh_tc05_wait_selftest(long long budget_cycles, void* 
 extern "C" int walsh_octo_set_mainloop(int tcgen05) {
   const int prev = g_octo_tc05;
   g_octo_tc05 = tcgen05 ? 1 : 0;
+  return prev;
+}
+
+extern "C" int walsh_octo_set_narrow(int on) {
+  const int prev = walsh::g_octo_narrow;
+  if (on >= 0) walsh::g_octo_narrow = on ? 1 : 0;
   return prev;
 }
 

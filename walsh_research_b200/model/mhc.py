@@ -470,13 +470,16 @@ class mHCWalsh(nn.Module):
             return logits, loss, h_out
         return logits, loss
 
-    # Batched decode runs the batch in `decode_streams` parts, each on its own
-    # CUDA stream: sequences share nothing inside the layer stack, so one
+    # Batched decode can run the batch in `decode_streams` parts, each on its
+    # own CUDA stream: sequences share nothing inside the layer stack, so one
     # part's latency-bound small kernels (mapping, projections, router, MoE,
-    # modulation) run beside another part's attention, which streams the KV
-    # cache.  Every kernel sees the rows it would see on the whole batch; the
-    # parts join before the final norm and logits.
-    decode_streams = 2
+    # modulation) may run beside another part's attention, which streams the
+    # KV cache.  Every kernel sees the rows it would see on the whole batch;
+    # the parts join before the final norm and logits.  Off by default: at
+    # B256 x ctx 1024 (Walsh-512) two parts measured 2.957 ms per step against
+    # 2.972 ms whole (the attention grid fills every SM, so the small kernels
+    # wait for its CTAs), for twice the launches.
+    decode_streams = 1
     DECODE_PARTS_FROM = 128  # batch size from which a T <= 4 step is split
 
     def _decode_parts(self, B, T, kv_cache):
