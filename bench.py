@@ -312,6 +312,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="walsh", choices=["walsh", "reference"])
     ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--ctx", type=int, default=DECODE_CTX,
+                    help="KV-cache length of --profile decode (a short cache keeps ncu captures small)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode measurement")
     ap.add_argument("--no-octonion", action="store_true", help="skip the config-2 octonion measurement")
@@ -522,7 +524,7 @@ def run_profile(args):
         return
     if args.profile == "decode":
         from walsh_research_b200.model import KVCache
-        B, ctx = DECODE_BATCH, DECODE_CTX
+        B, ctx = DECODE_BATCH, args.ctx
         H, C = CONFIG["n_head"], CONFIG["n_embd"]
         kv = KVCache(CONFIG["n_layer"], ctx, H, C // H, dev, dtype=torch.float16, batch_size=B)
         P = ctx - 2

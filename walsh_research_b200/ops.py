@@ -242,11 +242,11 @@ def moe(u, w1t, w2, gate_p, up_p, down_p, gammas, top_k, weights_in=None, fuse=N
         weights_in = _c(weights_in.float())
     if (tc is not None and gate_p is not None and weights_in is None and u.dtype != torch.float32
             and C in (512, 2048) and ntok < MOE_GEMM_ROUTER_BELOW and tc[0].dtype == u.dtype):
+        x, hmix, x_out = fuse if fuse is not None else (None, None, None)
+        y = torch.empty_like(u) if fuse is None else None
         # decode-sized: router layer 1 as a tcgen05 GEMM, the rest one warp per token
         hid = C // 4
         hpre = octo_linear(u.view(ntok, C), (tc[0], None), _ones(hid, u.device))
-        x, hmix, x_out = fuse if fuse is not None else (None, None, None)
-        y = torch.empty_like(u) if fuse is None else None
         call("walsh_moe_hidden_fwd", ptr(u), ptr(hpre), dcode(u.dtype), ntok, C, int(top_k), ptr(w2), ptr(gate_p),
              ptr(up_p), ptr(down_p), ptr(gammas), ptr(y), 0 if fuse is None else 1, ptr(x),
              dcode(x.dtype) if x is not None else dcode(u.dtype), ptr(hmix), ptr(x_out), ptr(mask), ptr(probs),
