@@ -573,12 +573,12 @@ mhc_map_tma_kernel(const __grid_constant__ CUtensorMap tmx, int64_t ntok, const 
 // two-pass kernel 142 us.
 // ---------------------------------------------------------------------------
 namespace map_pipe {
-constexpr int STAGES = 3, TOK = 16, NW = 16, THREADS = (NW + 1) * 32, C = 512, D = 4 * C;
+constexpr int STAGES = 2, TOK = 16, NW = 16, THREADS = (NW + 1) * 32, C = 512, D = 4 * C;
 constexpr int ROWB = D * 2 + 16;             // bytes per token row in shared memory (padded)
 constexpr int STAGE_BYTES = TOK * ROWB;
 constexpr int RS = kMapRows + 1;             // partial row: 24 projections + sum of squares
-constexpr int RED_FLOATS = NW * TOK * RS;    // [warp][token][RS]
-constexpr int SMEM = STAGES * STAGE_BYTES + RED_FLOATS * 4 + TOK * 16 * 4 + STAGES * 8 + 16 + 128;
+constexpr int RED_FLOATS = NW * TOK * RS;    // [warp][token][RS], two buffers (tiles alternate)
+constexpr int SMEM = STAGES * STAGE_BYTES + 2 * RED_FLOATS * 4 + TOK * 16 * 4 + 2 * STAGES * 8 + 16 + 128;
 // named barriers (0 is __syncthreads): main warps only; logits full; logits empty
 constexpr int BAR_MAIN = 1, BAR_FULL = 2, BAR_EMPTY = 3;
 }  // namespace map_pipe
@@ -656,22 +656,38 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* ring = smem_raw;
   float* red = reinterpret_cast<float*>(ring + STAGES * STAGE_BYTES);  // [NW][TOK][RS]
-  float* hres = red + RED_FLOATS;                                      // [TOK][16] H_res logits
+  float* hres = red + 2 * RED_FLOATS;                                  // [TOK][16] H_res logits
   uint64_t* bar = reinterpret_cast<uint64_t*>(hres + TOK * 16);        // [STAGES] stage full
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + STAGES);
+  uint64_t* ebar = bar + STAGES;                                       // [STAGES] stage read by all main warps
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ebar + STAGES);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const int64_t ntiles = (ntok + TOK - 1) / TOK;
   if (tid == 0) {
-    for (int st = 0; st < STAGES; ++st) tc05::mbar_init(bar + st, 1);
+    for (int st = 0; st < STAGES; ++st) {
+      tc05::mbar_init(bar + st, 1);
+      tc05::mbar_init(ebar + st, NW);
+    }
     tc05::fence_barrier_init();
     *abort_flag = 0;
   }
   __syncthreads();
+  // fills stage st with the tile's valid token rows (rows past ntok keep stale
+  // values; their results are never stored); one thread calls it
+  auto load = [&](int st, int64_t tile) {
+    if (tile < ntiles) {
+      const int rows = (int)min64(TOK, ntok - tile * TOK);
+      tc05::mbar_arrive_expect_tx(bar + st, (uint32_t)rows * (D * 2));
+      for (int r = 0; r < rows; ++r)
+        tc05::bulk_load(ring + st * STAGE_BYTES + r * ROWB, x + (tile * TOK + r) * D, D * 2, bar + st);
+    }
+  };
 
   if (warp == NW) {
-    // ---- the Sinkhorn warp
+    // ---- the Sinkhorn warp, which also refills the ring: stage st takes the
+    // tile STAGES ahead once every main warp has read it
     named_arrive(BAR_EMPTY, THREADS);  // the logits buffer starts empty
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    int it = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       named_sync(BAR_FULL, THREADS);
       if (*abort_flag) return;
       float M[16];
@@ -689,23 +705,21 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
 #pragma unroll
         for (int q = 0; q < 4; ++q) hd[q] = make_float4(M[4 * q], M[4 * q + 1], M[4 * q + 2], M[4 * q + 3]);
       }
+      const int64_t next = tile + (int64_t)STAGES * gridDim.x;
+      if (lane == 0 && next < ntiles) {
+        const int st = it % STAGES;
+        // bounded: gives up only when the main warps stopped (abort)
+        if (tc05::mbar_wait(ebar + st, (uint32_t)(it / STAGES) & 1u) && !*abort_flag) load(st, next);
+      }
+      __syncwarp();
     }
     return;
   }
 
   // ---- the main warps
-  // thread 0 fills stage st with the tile's valid token rows (rows past ntok
-  // keep stale values; their results are never stored)
-  auto load = [&](int st, int64_t tile) {
-    if (tid == 0 && tile < ntiles) {
-      const int rows = (int)min64(TOK, ntok - tile * TOK);
-      tc05::mbar_arrive_expect_tx(bar + st, (uint32_t)rows * (D * 2));
-      for (int r = 0; r < rows; ++r)
-        tc05::bulk_load(ring + st * STAGE_BYTES + r * ROWB, x + (tile * TOK + r) * D, D * 2, bar + st);
-    }
-  };
 #pragma unroll
-  for (int st = 0; st < STAGES; ++st) load(st, blockIdx.x + (int64_t)st * gridDim.x);
+  for (int st = 0; st < STAGES; ++st)
+    if (tid == 0) load(st, blockIdx.x + (int64_t)st * gridDim.x);
   // this warp's phi fragments: its column slice is the same for every tile,
   // so they are loaded once and stay in registers
   uint2 fr[KS][3];
@@ -726,22 +740,7 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
     const int64_t tok0 = tile * TOK;
     const unsigned char* xs = ring + st * STAGE_BYTES;
     const bool ok = tc05::mbar_wait(bar + st, (uint32_t)(it / STAGES) & 1u);
-    if (named_sync_or(BAR_MAIN, MT, !ok)) {
-      // release the Sinkhorn warp (its logits-buffer arrival for this tile is
-      // in), then wait (bounded) for this CTA's copies in flight
-      named_sync(BAR_EMPTY, THREADS);
-      if (tid == 0) {
-        *abort_flag = 1;
-        atomicExch(&g_map_tma_error, (int)WALSH_ERR_TIMEOUT);
-      }
-      named_arrive(BAR_FULL, THREADS);
-      if (tid == 0)
-        for (int k = 0; k < STAGES; ++k) {
-          const int64_t t2 = tile + (int64_t)k * gridDim.x;
-          if (t2 < ntiles) tc05::mbar_wait(bar + (it + k) % STAGES, (uint32_t)((it + k) / STAGES) & 1u, 200000000LL);
-        }
-      return;
-    }
+    float* redb = red + (it & 1) * RED_FLOATS;  // this tile's partials buffer
     // 1. partial projections over this warp's columns
     float acc[3][4];
 #pragma unroll
@@ -771,7 +770,7 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
       ss_lo += __shfl_xor_sync(0xffffffffu, ss_lo, off);
       ss_hi += __shfl_xor_sync(0xffffffffu, ss_hi, off);
     }
-    float* rw = red + warp * TOK * RS;
+    float* rw = redb + warp * TOK * RS;
 #pragma unroll
     for (int n = 0; n < 3; ++n) {
       rw[g * RS + 8 * n + 2 * t4] = acc[n][0];
@@ -783,14 +782,31 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
       rw[g * RS + kMapRows] = ss_lo;
       rw[(g + 8) * RS + kMapRows] = ss_hi;
     }
-    named_sync(BAR_MAIN, MT);  // partials complete
+    // partials complete; a stage wait that ran out on any warp aborts all
+    if (named_sync_or(BAR_MAIN, MT, !ok)) {
+      // release the Sinkhorn warp (its logits-buffer arrival for this tile is
+      // in), then wait (bounded) for this CTA's copies in flight
+      named_sync(BAR_EMPTY, THREADS);
+      if (tid == 0) {
+        *abort_flag = 1;
+        atomicExch(&g_map_tma_error, (int)WALSH_ERR_TIMEOUT);
+      }
+      named_arrive(BAR_FULL, THREADS);
+      if (tid == 0)
+        for (int k = 0; k < STAGES; ++k) {
+          const int64_t t2 = tile + (int64_t)k * gridDim.x;
+          if (t2 < ntiles) tc05::mbar_wait(bar + (it + k) % STAGES, (uint32_t)((it + k) / STAGES) & 1u, 200000000LL);
+        }
+      return;
+    }
+
     // 2. this warp's token: lane v < 25 adds partial v over the 16 warps in order
     const int t = warp;
     const int64_t tok = tok0 + t;
     float d = 0.f;
     if (lane < RS) {
 #pragma unroll
-      for (int w = 0; w < NW; ++w) d += red[(w * TOK + t) * RS + lane];
+      for (int w = 0; w < NW; ++w) d += redb[(w * TOK + t) * RS + lane];
     }
     const float rms = rsqrtf(__shfl_sync(0xffffffffu, d, kMapRows) / (float)D + map_eps);
     const float dn = d * rms;
@@ -850,8 +866,10 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
         }
       }
     }
-    named_sync(BAR_MAIN, MT);  // the ring buffer and the partials are free
-    load(st, tile + (int64_t)STAGES * gridDim.x);
+    // this warp is done with the stage; the next tile's partials go to the
+    // other buffer, so no barrier here
+    __syncwarp();
+    if (lane == 0) tc05::mbar_arrive(ebar + st);
   }
 }
 
