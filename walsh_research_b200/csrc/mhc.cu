@@ -578,7 +578,7 @@ constexpr int ROWB = D * 2 + 16;             // bytes per token row in shared me
 constexpr int STAGE_BYTES = TOK * ROWB;
 constexpr int RS = kMapRows + 1;             // partial row: 24 projections + sum of squares
 constexpr int RED_FLOATS = NW * TOK * RS;    // [warp][token][RS], two buffers (tiles alternate)
-constexpr int SMEM = STAGES * STAGE_BYTES + 2 * RED_FLOATS * 4 + TOK * 16 * 4 + 2 * STAGES * 8 + 16 + 128;
+constexpr int SMEM = STAGES * STAGE_BYTES + 2 * RED_FLOATS * 4 + TOK * 16 * 4 + STAGES * 8 + 16 + 128;
 // named barriers (0 is __syncthreads): main warps only; logits full; logits empty
 constexpr int BAR_MAIN = 1, BAR_FULL = 2, BAR_EMPTY = 3;
 }  // namespace map_pipe
@@ -658,36 +658,32 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
   float* red = reinterpret_cast<float*>(ring + STAGES * STAGE_BYTES);  // [NW][TOK][RS]
   float* hres = red + 2 * RED_FLOATS;                                  // [TOK][16] H_res logits
   uint64_t* bar = reinterpret_cast<uint64_t*>(hres + TOK * 16);        // [STAGES] stage full
-  uint64_t* ebar = bar + STAGES;                                       // [STAGES] stage read by all main warps
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(ebar + STAGES);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + STAGES);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const int64_t ntiles = (ntok + TOK - 1) / TOK;
   if (tid == 0) {
-    for (int st = 0; st < STAGES; ++st) {
-      tc05::mbar_init(bar + st, 1);
-      tc05::mbar_init(ebar + st, NW);
-    }
+    for (int st = 0; st < STAGES; ++st) tc05::mbar_init(bar + st, NW);  // one arrival per main warp
     tc05::fence_barrier_init();
     *abort_flag = 0;
   }
   __syncthreads();
-  // fills stage st with the tile's valid token rows (rows past ntok keep stale
-  // values; their results are never stored); one thread calls it
-  auto load = [&](int st, int64_t tile) {
-    if (tile < ntiles) {
-      const int rows = (int)min64(TOK, ntok - tile * TOK);
-      tc05::mbar_arrive_expect_tx(bar + st, (uint32_t)rows * (D * 2));
-      for (int r = 0; r < rows; ++r)
-        tc05::bulk_load(ring + st * STAGE_BYTES + r * ROWB, x + (tile * TOK + r) * D, D * 2, bar + st);
+  // main warp w fills row w of stage st with its token of the tile (one
+  // arrival per warp; rows past ntok arrive without a copy and keep stale
+  // values, whose results are never stored); lane 0 calls it
+  auto load_row = [&](int st, int64_t tile, int w) {
+    const int64_t tk = tile * TOK + w;
+    if (tk < ntok) {
+      tc05::mbar_arrive_expect_tx(bar + st, (uint32_t)(D * 2));
+      tc05::bulk_load(ring + st * STAGE_BYTES + w * ROWB, x + tk * D, D * 2, bar + st);
+    } else {
+      tc05::mbar_arrive(bar + st);
     }
   };
 
   if (warp == NW) {
-    // ---- the Sinkhorn warp, which also refills the ring: stage st takes the
-    // tile STAGES ahead once every main warp has read it
+    // ---- the Sinkhorn warp
     named_arrive(BAR_EMPTY, THREADS);  // the logits buffer starts empty
-    int it = 0;
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       named_sync(BAR_FULL, THREADS);
       if (*abort_flag) return;
       float M[16];
@@ -705,21 +701,16 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
 #pragma unroll
         for (int q = 0; q < 4; ++q) hd[q] = make_float4(M[4 * q], M[4 * q + 1], M[4 * q + 2], M[4 * q + 3]);
       }
-      const int64_t next = tile + (int64_t)STAGES * gridDim.x;
-      if (lane == 0 && next < ntiles) {
-        const int st = it % STAGES;
-        // bounded: gives up only when the main warps stopped (abort)
-        if (tc05::mbar_wait(ebar + st, (uint32_t)(it / STAGES) & 1u) && !*abort_flag) load(st, next);
-      }
-      __syncwarp();
     }
     return;
   }
 
   // ---- the main warps
 #pragma unroll
-  for (int st = 0; st < STAGES; ++st)
-    if (tid == 0) load(st, blockIdx.x + (int64_t)st * gridDim.x);
+  for (int st = 0; st < STAGES; ++st) {
+    const int64_t t0 = blockIdx.x + (int64_t)st * gridDim.x;
+    if (lane == 0 && t0 < ntiles) load_row(st, t0, warp);
+  }
   // this warp's phi fragments: its column slice is the same for every tile,
   // so they are loaded once and stay in registers
   uint2 fr[KS][3];
@@ -866,10 +857,16 @@ mhc_map_pipe_kernel(const TX* __restrict__ x, int64_t ntok, const uint2* __restr
         }
       }
     }
-    // this warp is done with the stage; the next tile's partials go to the
+    // every warp has read the whole stage (phase 1, before the partials
+    // barrier) and this warp is done with its row: refill the row with its
+    // token of the tile STAGES ahead; the next tile's partials go to the
     // other buffer, so no barrier here
     __syncwarp();
-    if (lane == 0) tc05::mbar_arrive(ebar + st);
+    const int64_t next = tile + (int64_t)STAGES * gridDim.x;
+    if (lane == 0 && next < ntiles) {
+      tc05::fence_proxy_async();
+      load_row(st, next, warp);
+    }
   }
 }
 
