@@ -369,14 +369,14 @@ chmod_apply_kernel(const T* x, int64_t nrows, int C, int seg_len, const float* _
 // ---------------------------------------------------------------------------
 // Single-row segments (batched decode: each row of the [B*n, 1, C] view is
 // its own segment), C = 512, in one kernel instead of stats / bulk split /
-// layer-1 GEMM / layer 2 / apply.  A CTA of 256 threads takes 4 rows:
-//   rows     warps 0-3, one row each, held in registers for the last step:
+// layer-1 GEMM / layer 2 / apply.  A CTA of 256 threads takes 8 rows:
+//   rows     warps 0-7, one row each, held in registers for the last step:
 //            RMS factor, xn = x r w_norm, which is also the segment mean,
 //            split into bf16 hi + mid + lo (their sum is xn to float32
-//            precision) as rows z, 4 + z, 8 + z of a 16-row MMA operand
-//            (rows 12-15 zero);
-//   layer 1  warp w: hidden units 16 w .. 16 w + 15 as two m16n8k16 bf16
-//            MMAs per 16 channels, A the split rows (ldmatrix), B the
+//            precision) as rows z, 8 + z, 16 + z of a 32-row MMA operand
+//            (rows 24-31 read one zero row);
+//   layer 1  warp w: hidden units 16 w .. 16 w + 15 as m16n8k16 bf16 MMAs
+//            over the two 16-row tiles, A the split rows (ldmatrix), B the
 //            ternary W1 values decoded from the packed rows staged in shared
 //            memory (132-byte rows: the eight rows a warp reads fall in
 //            distinct banks); h = SiLU(g1 ((hi + mid) + lo)), the sums of the
@@ -387,7 +387,7 @@ chmod_apply_kernel(const T* x, int64_t nrows, int C, int seg_len, const float* _
 //   apply    out = x + xn + rs (xn scale + 0.1 shift - xn) from the kept rows.
 // ---------------------------------------------------------------------------
 namespace chrow {
-constexpr int C = 512, R = 4, HID = C / 4, E = C / 32, NT = 256;
+constexpr int C = 512, R = 8, HID = C / 4, E = C / 32, NT = 256;
 constexpr int WWORDS = C / 16;          // packed W1 row: 32 words of 16 codes
 constexpr int WPITCH = WWORDS + 1;      // shared-memory row pitch in words
 constexpr int APITCH = C + 8;           // MMA operand row pitch in bf16 (1040 bytes)
@@ -413,7 +413,7 @@ chmod_rows_kernel(const T* x, int64_t nrows, const float* __restrict__ norm_w, f
                   float* __restrict__ shift, T* out) {
   using namespace chrow;
   __shared__ uint32_t w1s[HID * WPITCH];
-  __shared__ __align__(16) __nv_bfloat16 as[16 * APITCH];
+  __shared__ __align__(16) __nv_bfloat16 as[25 * APITCH];  // rows z, 8 + z, 16 + z: hi, mid, lo; row 24 zero
   __shared__ float hid[R * HID];
   __shared__ float mod[R * 2 * E];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, t4 = lane & 3;
@@ -475,49 +475,52 @@ chmod_rows_kernel(const T* x, int64_t nrows, const float* __restrict__ norm_w, f
       }
       const int c0 = p * 256 + lane * 8;
       *reinterpret_cast<uint4*>(as + warp * APITCH + c0) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(as + (4 + warp) * APITCH + c0) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
-      *reinterpret_cast<uint4*>(as + (8 + warp) * APITCH + c0) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      *reinterpret_cast<uint4*>(as + (8 + warp) * APITCH + c0) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+      *reinterpret_cast<uint4*>(as + (16 + warp) * APITCH + c0) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
-  } else {
-    // warps 4-7 clear rows 12-15
-    for (int c = lane * 8; c < C; c += 256)
-      *reinterpret_cast<uint4*>(as + (12 + (warp - 4)) * APITCH + c) = make_uint4(0u, 0u, 0u, 0u);
   }
+  if (tid < APITCH / 8) *reinterpret_cast<uint4*>(as + 24 * APITCH + tid * 8) = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
   // ---- layer 1 on the tensor cores: warp w, hidden units 16 w + 8 nt + (0..7)
   const float g1 = __ldg(gammas + 0), g2 = __ldg(gammas + 1);
   {
-    float acc[2][4];
+    // acc[m][nt]: row tile m (rows 16 m ..), hidden n-tile nt; each decoded B
+    // fragment serves both row tiles
+    float acc[2][2][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) acc[m][nt][0] = acc[m][nt][1] = acc[m][nt][2] = acc[m][nt][3] = 0.f;
     const uint32_t abase = (uint32_t)__cvta_generic_to_shared(as);
     const int sh_a = 8 * (t4 >> 1) + 6 - 4 * (t4 & 1);  // code of channel 16 ks + 2 t4 in its word
 #pragma unroll 4
     for (int ks = 0; ks < WWORDS; ++ks) {
-      uint32_t a[4];
-      const uint32_t addr = abase + (uint32_t)(((lane & 15) * APITCH + ks * 16 + (lane >> 4) * 8) * 2);
-      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                   : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
-                   : "r"(addr));
+      uint32_t a[2][4];
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const int arow = min(16 * m + (lane & 15), 24);  // tile 1 rows 8-15 read the zero row
+        const uint32_t addr = abase + (uint32_t)((arow * APITCH + ks * 16 + (lane >> 4) * 8) * 2);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                     : "=r"(a[m][0]), "=r"(a[m][1]), "=r"(a[m][2]), "=r"(a[m][3])
+                     : "r"(addr));
+      }
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         const uint32_t wd = w1s[(16 * warp + 8 * nt + gid) * WPITCH + ks];
         // channels 16 ks + 2 t4, +1 (b0) and + 8, + 9 (b1): bytes t4/2 and t4/2 + 2
         const uint32_t b0 = chrow_code_pair((wd >> sh_a) & 3u, (wd >> (sh_a - 2)) & 3u);
         const uint32_t b1 = chrow_code_pair((wd >> (sh_a + 16)) & 3u, (wd >> (sh_a + 14)) & 3u);
-        mma16<__nv_bfloat16>(acc[nt], a, b0, b1);
+        mma16<__nv_bfloat16>(acc[0][nt], a[0], b0, b1);
+        mma16<__nv_bfloat16>(acc[1][nt], a[1], b0, b1);
       }
     }
-    // rows gid (hi for gid < 4, mid for gid >= 4) and gid + 8 (lo for gid < 4)
+    // row z = gid: hi in tile 0 row gid, mid in tile 0 row gid + 8, lo in tile 1 row gid
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const float mid = __shfl_xor_sync(0xffffffffu, acc[nt][e], 16);
-        if (gid < 4) {
-          const float a1 = ((acc[nt][e] + mid) + acc[nt][2 + e]) * g1;
-          hid[gid * HID + 16 * warp + 8 * nt + 2 * t4 + e] = a1 / (1.0f + expf(-a1));
-        }
+        const float a1 = ((acc[0][nt][e] + acc[0][nt][2 + e]) + acc[1][nt][e]) * g1;
+        hid[gid * HID + 16 * warp + 8 * nt + 2 * t4 + e] = a1 / (1.0f + expf(-a1));
       }
   }
   __syncthreads();
