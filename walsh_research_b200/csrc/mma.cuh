@@ -45,6 +45,9 @@ __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
 }
 __device__ __forceinline__ uint64_t f2_dup(float v) { return f2_pack(v, v); }
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_swap(uint64_t v) { return (v >> 32) | (v << 32); }
 __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));

@@ -155,9 +155,9 @@ struct EpiQkv {
     const int b = (int)(m / T), t = (int)(m - (int64_t)b * T);
     v0 *= __ldg(scale + n);
     v1 *= __ldg(scale + n + 1);
-    if (which < 2) {
+    if (which < 2) {  // the roundings of the pair form in half_row
       const float cs = __ldg(cos + (size_t)t * (hd / 2) + (d >> 1)), sn = __ldg(sin + (size_t)t * (hd / 2) + (d >> 1));
-      const float r0 = v0 * cs - v1 * sn, r1 = v0 * sn + v1 * cs;
+      const float r0 = fmaf(v1, -sn, __fmul_rn(v0, cs)), r1 = fmaf(v0, sn, __fmul_rn(v1, cs));
       v0 = r0;
       v1 = r1;
     }
@@ -191,10 +191,10 @@ struct EpiQkv {
       const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
       const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 8; ++j) {  // the roundings of the pair form in half_row
         const float a = o[2 * j], bb = o[2 * j + 1];
-        o[2 * j] = a * cs[j] - bb * sn[j];
-        o[2 * j + 1] = a * sn[j] + bb * cs[j];
+        o[2 * j] = fmaf(bb, -sn[j], __fmul_rn(a, cs[j]));
+        o[2 * j + 1] = fmaf(a, sn[j], __fmul_rn(bb, cs[j]));
       }
     }
     TY* dst = which == 0 ? q + (((size_t)b * n_head + head) * T + t) * hd + d
@@ -241,6 +241,14 @@ struct EpiQkv {
     const size_t hstride = (size_t)(which == 0 ? T : ctx) * 16;  // elements between heads
     TY* row = which == 0 ? q + ((size_t)b * n_head * T + t) * 16
                          : (which == 1 ? kc : vc) + ((size_t)b * n_head * ctx + start_pos + t) * 16;
+    // RoPE on pairs (a, b) -> (a c - b s, a s + b c) as two f32x2 operations:
+    // (b, a) (-s, s) + (a, b) (c, c)
+    uint64_t rc[8], rs[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      rc[j] = which < 2 ? f2_dup(cs[j]) : 0;
+      rs[j] = which < 2 ? f2_pack(-sn[j], sn[j]) : 0;
+    }
 #pragma unroll 1
     for (int c = 0; c < 128; c += 64) {
       float v[64];
@@ -249,25 +257,26 @@ struct EpiQkv {
       tc05::tmem_wait_ld();
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh) {
-        float o[16];
+        uint32_t w[8];
         const float4* s4 = reinterpret_cast<const float4*>(ws + ni + c + 16 * hh);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float4 sv = s4[j];
-          o[4 * j] = v[16 * hh + 4 * j] * sv.x;
-          o[4 * j + 1] = v[16 * hh + 4 * j + 1] * sv.y;
-          o[4 * j + 2] = v[16 * hh + 4 * j + 2] * sv.z;
-          o[4 * j + 3] = v[16 * hh + 4 * j + 3] * sv.w;
-        }
-        if (which < 2) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float a = o[2 * j], bb = o[2 * j + 1];
-            o[2 * j] = a * cs[j] - bb * sn[j];
-            o[2 * j + 1] = a * sn[j] + bb * cs[j];
+          const float* vv = v + 16 * hh + 4 * j;
+          uint64_t p0 = f2_mul(f2_pack(vv[0], vv[1]), f2_pack(sv.x, sv.y));
+          uint64_t p1 = f2_mul(f2_pack(vv[2], vv[3]), f2_pack(sv.z, sv.w));
+          if (which < 2) {
+            p0 = f2_fma(f2_swap(p0), rs[2 * j], f2_mul(p0, rc[2 * j]));
+            p1 = f2_fma(f2_swap(p1), rs[2 * j + 1], f2_mul(p1, rc[2 * j + 1]));
           }
+          w[2 * j] = pack2<TY>(f2_lo(p0), f2_hi(p0));
+          w[2 * j + 1] = pack2<TY>(f2_lo(p1), f2_hi(p1));
         }
-        if (valid) store16(row + (size_t)(head0 + (c >> 4) + hh) * hstride, o);
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(row + (size_t)(head0 + (c >> 4) + hh) * hstride);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       }
     }
   }
