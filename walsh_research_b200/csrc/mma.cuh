@@ -112,6 +112,13 @@ __device__ __forceinline__ float ex2_f32(float x) {
   return r;
 }
 
+// 1 / x (PTX rcp.approx.ftz.f32); +inf -> +0.
+__device__ __forceinline__ float rcp_f32(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // max of three floats in one instruction (sm_100)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;

@@ -1224,6 +1224,9 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
     const int q = warp & 3;
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
     const float gg = __ldg(gammas), gu = __ldg(gammas + 1);
+    // h = SiLU(gg g) (gu v) = g v gg gu / (1 + 2^(-gg log2(e) g)): two MUFU
+    // operations per value, the rest on float pairs
+    const uint64_t cexp = f2_dup(-gg * 1.4426950408889634f), cgu = f2_dup(gg * gu), one2 = f2_dup(1.0f);
     const uint32_t sH = smem_u32(smem + OFF_H);
     const int r = q * 32 + lane;
     int64_t ge = 0;
@@ -1250,8 +1253,14 @@ moe_experts_tc05_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_c
           }
           uint32_t a[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            a[i] = pack2<TU>(siluf_(gg * gv[2 * i]) * (gu * uv[2 * i]), siluf_(gg * gv[2 * i + 1]) * (gu * uv[2 * i + 1]));
+          for (int i = 0; i < 16; ++i) {
+            const uint64_t g2 = f2_pack(gv[2 * i], gv[2 * i + 1]);
+            const uint64_t t = f2_mul(g2, cexp);
+            const uint64_t d = f2_fma(f2_pack(ex2_f32(f2_lo(t)), ex2_f32(f2_hi(t))), one2, one2);
+            const uint64_t hs = f2_mul(f2_mul(g2, f2_pack(rcp_f32(f2_lo(d)), rcp_f32(f2_hi(d)))),
+                                       f2_mul(f2_pack(uv[2 * i], uv[2 * i + 1]), cgu));
+            a[i] = pack2<TU>(f2_lo(hs), f2_hi(hs));
+          }
           if (c == 0 && ge > 0 && !__all_sync(0xffffffffu, mbar_wait(h_empty, (uint32_t)((ge - 1) & 1)))) {
             ok = false;
             break;
