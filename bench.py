@@ -767,7 +767,10 @@ def measure_hlin_microbench(dev, iters=20):
     weights i.i.d. uniform {-1, 0, 1}, alpha ~ U(0.5, 1.5), beta at the reference
     init.  Each entry times `iters` calls through the module's forward with CUDA
     events, cycling over enough input/output buffers that one pass over them
-    exceeds L2 (no flush needed).  Algorithmic bytes per call:
+    exceeds L2 (no flush needed): `us` called from Python one by one,
+    `us_graph` the same calls replayed from a CUDA graph (device time).  n =
+    512 from HLIN_DENSE_FROM tokens on runs the dense tcgen05 GEMM form, below
+    it and for n = 2048 the packed kernel.  Algorithmic bytes per call:
     T (32 in_o + 32 out_o) 2 + 32 out_o ceil(in_o / 4) + 4 * 32 (in_o + out_o)."""
     from walsh_research_b200.model.fht_cuda import HadamardLinear
     hbm, _, _ = peaks()
@@ -794,10 +797,26 @@ def measure_hlin_microbench(dev, iters=20):
                 s1.record()
                 torch.cuda.synchronize()
             sec = s0.elapsed_time(s1) / iters / 1e3
+            # the same calls replayed from a CUDA graph: device time without
+            # the Python and launch overhead of each call
+            with torch.no_grad():
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    for i in range(iters):
+                        lin(xs[i % nbuf])
+                gr.replay()
+                torch.cuda.synchronize()
+                s0.record()
+                gr.replay()
+                s1.record()
+                torch.cuda.synchronize()
+            gsec = s0.elapsed_time(s1) / iters / 1e3
+            del gr
             nbytes = T * (32 * in_o + 32 * out_o) * 2 + 32 * out_o * ((in_o + 3) // 4) + 4 * 32 * (in_o + out_o)
-            e = {"n": n, "T": T, "us": sec * 1e6, "GB/s": nbytes / sec / 1e9}
+            e = {"n": n, "T": T, "us": sec * 1e6, "GB/s": nbytes / sec / 1e9, "us_graph": gsec * 1e6}
             if T >= 4096:
                 e["roofline_frac"] = nbytes / sec / 1e9 / hbm
+                e["roofline_frac_graph"] = nbytes / gsec / 1e9 / hbm
             out.append(e)
             del xs
     torch.cuda.empty_cache()

@@ -603,6 +603,28 @@ walsh_status walsh_hash_embed_rows(const float* tables, int64_t buckets, const f
 walsh_status walsh_hadamard_linear_pk_fwd(const void* x, int dtype, int64_t ntok, int features,
                                           const uint8_t* w_2bit, const float* alpha, const float* beta, void* y,
                                           void* stream);
+/* HadamardLinear(F, F) as one dense matrix for the tensor-core GEMM form of
+ * walsh_hadamard_linear_dense_fwd: from the 2-bit packed weights w_2bit
+ * [32, F/32, F/128] and alpha, beta float [32, F/32] (F = features = 512 or
+ * 2048) writes w_dense [F, F] in dtype (WALSH_BF16 or WALSH_F16) and scale
+ * float [F] with scale[r] w_dense[r, c] = beta . H W H . alpha at (r, c), the
+ * two normalised 32-point transforms included.  Each entry is an integer in
+ * [-32, 32] times alpha[c] and a power of two, rounded once to the 16-bit
+ * type.  Derived from HadamardLinear.forward (src/model/fht_cuda.py:489-519):
+ * the reference has no such matrix; this is weight preparation, run once
+ * per weight update. */
+walsh_status walsh_hadamard_linear_dense_weights(const uint8_t* w_2bit, const float* alpha, const float* beta,
+                                                 int features, int dtype, void* w_dense, float* scale,
+                                                 void* stream);
+/* HadamardLinear(F, F) for 16-bit activations as one tcgen05 GEMM over the
+ * matrix of walsh_hadamard_linear_dense_weights: y[t, r] = scale[r] sum_c
+ * x[t, c] w_dense[r, c], float32 accumulation, y rounded once to dtype.  x, y
+ * [ntok, F] (16-byte aligned), w_dense [F, F] in x's dtype (16-byte aligned),
+ * scale float [F] (16-byte aligned).  Replaces HadamardLinear.forward
+ * (src/model/fht_cuda.py:489-519) where it is faster than the packed kernel
+ * (F = 512 at thousands of tokens). */
+walsh_status walsh_hadamard_linear_dense_fwd(const void* x, int dtype, int64_t ntok, int features,
+                                             const void* w_dense, const float* scale, void* y, void* stream);
 /* Status word of walsh_hadamard_linear_pk_fwd's bounded waits (0 or
  * WALSH_ERR_TIMEOUT); synchronous read, reset != 0 clears it. */
 int walsh_hlin_pk_error(int reset);

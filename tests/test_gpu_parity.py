@@ -130,7 +130,11 @@ def test_hadamard_linear_packed_weights_vs_oracle(dt, F, ntok):
     layer = _hlin(d)
     x = T(d["x"], dt)
     _lib.call("walsh_hlin_pk_error", 1)
-    y = layer(x)
+    ops.HLIN_DENSE = False
+    try:
+        y = layer(x)
+    finally:
+        ops.HLIN_DENSE = True
     assert y.dtype == dt
     ref = O.hadamard_linear(x.double().cpu().numpy(), d["weight"], d["alpha"], d["beta"])
     assert rel(y, ref) < 1e-2
@@ -143,6 +147,66 @@ def test_hadamard_linear_packed_weights_vs_oracle(dt, F, ntok):
         assert rel(y, y_old.float().cpu().numpy()) < 1e-2
     torch.cuda.synchronize()
     assert _lib.call("walsh_hlin_pk_error", 1) == 0
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("alpha_hi", [1.5, 300.0])
+def test_hadamard_linear_dense_weights_match_float_matrix(dt, alpha_hi):
+    """The dense matrix of the GEMM form (integer H W H sums times alpha and
+    a power of two, rounded once to the 16-bit type) times its row scale
+    against the layer's float64-built float32 matrix, entry by entry: within
+    the 16-bit type's rounding.  alpha up to 300 exercises the power-of-two
+    normalisation that keeps float16 entries in range."""
+    from walsh_research_b200 import ops
+    rng = np.random.default_rng(5)
+    F, io = 512, 16
+    d = dict(x=np.zeros((1, 1, F), np.float32), weight=rng.normal(size=(32, io, io)).astype(np.float32),
+             alpha=rng.uniform(alpha_hi / 6, alpha_hi, (32, io)).astype(np.float32),
+             beta=rng.uniform(0.1, 0.4, (32, io)).astype(np.float32))
+    layer = _hlin(d)
+    w, scale = layer.dense16(dt)
+    assert w.dtype == dt and w.shape == (F, F) and w.abs().max().item() <= 1.0
+    got = (w.float() * scale[:, None]).cpu().numpy()
+    ref = layer.dense().cpu().numpy()
+    ulp = 2.0 ** (-8 if dt == torch.bfloat16 else -11)
+    err = np.abs(got - ref) / np.maximum(np.abs(ref), 1e-30)
+    assert err[ref != 0].max() <= ulp * 1.01
+    assert np.all(got[ref == 0] == 0)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("ntok", [1, 33, 4097, 150 * 128 + 77, 32768 + 5])
+def test_hadamard_linear_dense_vs_oracle_and_packed(dt, ntok):
+    """HadamardLinear(512, 512) as one tcgen05 GEMM over the dense matrix
+    (the default from HLIN_DENSE_FROM tokens on; forced here for every size:
+    narrow tiles for few tokens, ragged last row tile): against the float64
+    oracle on the same rounded inputs and against the packed kernel, within
+    1e-2 of the largest output (16-bit operands)."""
+    from walsh_research_b200 import _lib, ops
+    rng = np.random.default_rng(ntok)
+    F, io = 512, 16
+    d = dict(x=rng.normal(size=(1, ntok, F)).astype(np.float32), weight=rng.normal(size=(32, io, io)).astype(np.float32),
+             alpha=rng.uniform(0.5, 1.5, (32, io)).astype(np.float32),
+             beta=rng.uniform(0.1, 0.4, (32, io)).astype(np.float32))
+    layer = _hlin(d)
+    x = T(d["x"], dt)
+    _lib.call("walsh_tc05_error", 1)
+    prev, ops.HLIN_DENSE_FROM = ops.HLIN_DENSE_FROM, 1
+    try:
+        y = layer(x)
+    finally:
+        ops.HLIN_DENSE_FROM = prev
+    torch.cuda.synchronize()
+    assert _lib.call("walsh_tc05_error", 1) == 0
+    assert y.dtype == dt
+    ref = O.hadamard_linear(x.double().cpu().numpy(), d["weight"], d["alpha"], d["beta"])
+    assert rel(y, ref) < 1e-2
+    ops.HLIN_DENSE = False
+    try:
+        y_pk = layer(x)
+    finally:
+        ops.HLIN_DENSE = True
+    assert rel(y, y_pk.float().cpu().numpy()) < 1e-2
 
 
 @pytest.mark.parametrize("fin,fout,ntok", [(512, 512, 4096 + 3), (2048, 2048, 517), (512, 2048, 33),

@@ -80,6 +80,8 @@ SIGNATURES = {
     "walsh_bitmask_ternary_unpack": [P, c_int64, P, c_int64, c_int64, c_int64, c_int, P, P, P, P],
     "walsh_hash_embed_rows": [P, c_int64, P, P, c_int, c_int, c_float, c_int64, c_int64, P, P, P],
     "walsh_hadamard_linear_pk_fwd": [P, c_int, c_int64, c_int, P, P, P, P, P],
+    "walsh_hadamard_linear_dense_weights": [P, P, P, c_int, c_int, P, P, P],
+    "walsh_hadamard_linear_dense_fwd": [P, c_int, c_int64, c_int, P, P, P, P],
     "walsh_hlin_pk_error": [c_int],
 }
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_ipc_handle_bytes": c_int, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,
@@ -179,7 +181,14 @@ def inner_dtype(stream_dtype: torch.dtype) -> torch.dtype:
     return torch.float16 if stream_dtype in (torch.bfloat16, torch.float16) else stream_dtype
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream() -> int:
+    """Handle of the current CUDA stream of the current device (read without
+    building a torch.cuda.Stream object: a few microseconds less per op)."""
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(torch._C._cuda_getDevice())
     return torch.cuda.current_stream().cuda_stream
 
 

@@ -414,6 +414,65 @@ static int launch_hlin_pk2048(const void* x, int64_t ntok, const uint8_t* w2, co
   return launch_status();
 }
 
+// HadamardLinear(F, F) as one matrix for the dense tensor-core form:
+// out row r = (h, o), column c = (p, i), with the unnormalised Sylvester
+// matrix H[a, b] = (-1)^popcount(a & b):
+//   w_dense[r, c] = alpha[p, i] sum_g H[g, h] H[p, g] w[g, o, i] / (32 q),
+//   scale[r]      = beta[h, o] q,
+// so that y = scale . (x w_dense^T) equals beta . H W H (alpha . x) with the
+// reference's normalised transforms (HadamardLinear.forward,
+// src/model/fht_cuda.py:489-519).  The 32-term sum is an integer in
+// [-32, 32]; q is the power of two at or above max |alpha|, which keeps
+// every entry at most 1 in magnitude (float16 range).  One block per row.
+template <typename T16>
+__global__ void __launch_bounds__(256) hlin_dense_prep_kernel(const uint8_t* __restrict__ w2,
+                                                              const float* __restrict__ alpha,
+                                                              const float* __restrict__ beta, int io,
+                                                              T16* __restrict__ wd, float* __restrict__ scale) {
+  __shared__ float red[8];
+  const int F = 32 * io, row = blockIdx.x, h = row / io, o = row % io, kb = (io + 3) / 4;
+  float a = 0.f;
+  for (int c = threadIdx.x; c < F; c += blockDim.x) a = fmaxf(a, fabsf(__ldg(alpha + c)));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+  __syncthreads();
+  a = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) a = fmaxf(a, red[w]);
+  int e = 0;
+  if (a > 0.f && a <= 3.0e38f) frexpf(a, &e);  // a = m 2^e, m in [0.5, 1)
+  const float q = ldexpf(1.f, e), inv = ldexpf(1.f, -e - 5);
+  if (threadIdx.x == 0) scale[row] = __ldg(beta + row) * q;
+  for (int c = threadIdx.x; c < F; c += blockDim.x) {
+    const int p = c / io, i = c % io;
+    int sum = 0;
+#pragma unroll 8
+    for (int g = 0; g < 32; ++g) {
+      const int v = (int)((__ldg(w2 + ((size_t)g * io + o) * kb + (i >> 2)) >> (6 - 2 * (i & 3))) & 3u) - 1;
+      sum += ((__popc(g & h) + __popc(p & g)) & 1) ? -v : v;
+    }
+    wd[(size_t)row * F + c] = from_f<T16>((float)sum * __ldg(alpha + c) * inv);
+  }
+}
+
+extern "C" walsh_status walsh_hadamard_linear_dense_weights(const uint8_t* w_2bit, const float* alpha,
+                                                            const float* beta, int features, int dtype,
+                                                            void* w_dense, float* scale, void* stream) {
+  if (int e = injected("hadamard_linear_dense_weights")) return e;
+  WALSH_CHECK_ARG(w_2bit && alpha && beta && w_dense && scale);
+  WALSH_CHECK_SHAPE(features == 512 || features == 2048);
+  if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int io = features / 32;
+  if (dtype == WALSH_BF16)
+    hlin_dense_prep_kernel<__nv_bfloat16><<<features, 256, 0, s>>>(w_2bit, alpha, beta, io,
+                                                                   (__nv_bfloat16*)w_dense, scale);
+  else
+    hlin_dense_prep_kernel<__half><<<features, 256, 0, s>>>(w_2bit, alpha, beta, io, (__half*)w_dense, scale);
+  return launch_status();
+}
+
 extern "C" walsh_status walsh_hadamard_linear_pk_fwd(const void* x, int dtype, int64_t ntok, int features,
                                                      const uint8_t* w_2bit, const float* alpha, const float* beta,
                                                      void* y, void* stream) {

@@ -1107,6 +1107,24 @@ extern "C" walsh_status walsh_octo_linear_fwd(const void* x, int dtype, int64_t 
                              launch_octo<TA>(x, M, K, w_hi, w_lo, N, octo::EpiPlain<TA>{scale, (TA*)y, N}, s));
 }
 
+extern "C" walsh_status walsh_hadamard_linear_dense_fwd(const void* x, int dtype, int64_t ntok, int features,
+                                                        const void* w_dense, const float* scale, void* y,
+                                                        void* stream) {
+  if (int e = injected("hadamard_linear_dense_fwd")) return e;
+  WALSH_CHECK_SHAPE(features == 512 || features == 2048);
+  if (dtype != WALSH_BF16 && dtype != WALSH_F16) return WALSH_ERR_DTYPE;
+  if (walsh_status st = octo_check(x, dtype, ntok, features, w_dense, nullptr, dtype, features)) return st;
+  WALSH_CHECK_ARG(scale && y);
+  if ((((uintptr_t)y) | ((uintptr_t)scale)) & 15u) return WALSH_ERR_ALIGN;
+  if (ntok == 0) return WALSH_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == WALSH_BF16)
+    return launch_octo<__nv_bfloat16>(x, ntok, features, w_dense, nullptr, features,
+                                      octo::EpiPlain<__nv_bfloat16>{scale, (__nv_bfloat16*)y, features}, s);
+  return launch_octo<__half>(x, ntok, features, w_dense, nullptr, features,
+                             octo::EpiPlain<__half>{scale, (__half*)y, features}, s);
+}
+
 extern "C" walsh_status walsh_moe_router_tc_fwd(const void* u, int dtype, int64_t ntok, const void* w1,
                                                const void* w2, int top_k, uint8_t* mask, float* probs,
                                                float* weights, const walsh_moe_routing* routing, void* stream) {

@@ -91,10 +91,20 @@ class HadamardLinear(nn.Module):
             return W.reshape(self.out_features, self.in_features).float().contiguous()
         return _prep.cached(self, "dense", [self.weight, self.alpha, self.beta], build)
 
+    def dense16(self, dtype):
+        """(w_dense [out, in] in dtype, scale float [out]) of the dense GEMM form."""
+        alpha, beta = self.scales()
+        return _prep.cached(self, f"dense16_{dtype}", [self.weight, self.alpha, self.beta],
+                            lambda: ops.hadamard_linear_dense_weights(self.packed(), alpha, beta, self.in_features,
+                                                                      dtype))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         alpha, beta = self.scales()
-        if (ops.HLIN_PACKED and x.dtype in (torch.bfloat16, torch.float16)
-                and self.in_features == self.out_features and self.in_features in ops.HLIN_PACKED_FEATURES):
+        sixteen = x.dtype in (torch.bfloat16, torch.float16) and self.in_features == self.out_features
+        if (sixteen and ops.HLIN_DENSE and self.in_features in ops.HLIN_DENSE_FEATURES
+                and x.numel() >= ops.HLIN_DENSE_FROM * self.in_features):
+            return ops.hadamard_linear_dense(x, *self.dense16(x.dtype))
+        if ops.HLIN_PACKED and sixteen and self.in_features in ops.HLIN_PACKED_FEATURES:
             return ops.hadamard_linear_pk(x, self.packed(), alpha, beta)
         if ops.tc_eligible(x) and self.in_features == 512 and self.out_features == 512:
             return ops.hadamard_linear_tc(x, self.ternary_f16(), alpha, beta)

@@ -84,6 +84,39 @@ def hadamard_linear_tc(x, w_f16, alpha, beta, w_scale: float = 1.0):
 # kept for comparisons
 HLIN_PACKED = True
 HLIN_PACKED_FEATURES = (512, 2048)
+# 16-bit HadamardLinear(512, 512) from this many tokens on runs as one
+# tcgen05 GEMM over the layer's dense matrix (hadamard_linear_dense; 65536
+# tokens: 49.6 us against the packed kernel's 57.7 us); below it (16384
+# tokens: 16.4 against 14.6 us of GPU time), and for 2048 (where the dense
+# GEMM has 4 times the multiply-adds per token of 512 and measured 464 us
+# against 207 us), the packed kernel
+HLIN_DENSE = True
+HLIN_DENSE_FEATURES = (512,)
+HLIN_DENSE_FROM = 32768
+
+
+def hadamard_linear_dense_weights(packed, alpha, beta, features, dtype):
+    """(w_dense [F, F] in dtype, scale float [F]) of HadamardLinear(F, F):
+    y = scale . (x w_dense^T)."""
+    require_cuda(packed)
+    w = torch.empty((features, features), dtype=dtype, device=packed.device)
+    scale = torch.empty((features,), dtype=torch.float32, device=packed.device)
+    call("walsh_hadamard_linear_dense_weights", ptr(_c(packed)), ptr(_c(alpha)), ptr(_c(beta)), features,
+         dcode(dtype), ptr(w), ptr(scale), stream())
+    return w, scale
+
+
+def hadamard_linear_dense(x, w_dense, scale):
+    """y = HadamardLinear(x) for 16-bit x [..., F] on the tcgen05 GEMM; y in x's dtype."""
+    require_cuda(x)
+    x = _c(x)
+    F = x.shape[-1]
+    if w_dense.dtype != x.dtype:
+        raise ValueError(f"dense HadamardLinear weights are {w_dense.dtype}; activations are {x.dtype}")
+    y = torch.empty_like(x)
+    call("walsh_hadamard_linear_dense_fwd", ptr(x), dcode(x.dtype), x.numel() // F, F, ptr(w_dense), ptr(scale),
+         ptr(y), stream())
+    return y
 
 
 def hadamard_linear_pk(x, packed, alpha, beta):
