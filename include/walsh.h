@@ -360,6 +360,13 @@ int walsh_octo_set_mainloop(int tcgen05);
  * 256-wide tiles, on < 0 only queries.  Returns the previous setting.  A
  * switch for comparisons: both tilings give the same sums. */
 int walsh_octo_set_narrow(int on);
+/* GEMMs with the plain epilogue (walsh_octo_linear_fwd,
+ * walsh_hadamard_linear_dense_fwd) on the tcgen05 kernel stage each scaled
+ * 32 x 32 output block in shared memory and write it with a TMA store when
+ * on (the default; 16-bit outputs, N a multiple of 32); on = 0 keeps each
+ * lane's row stores, on < 0 only queries.  Returns the previous setting.  A
+ * switch for comparisons: both give the same bits. */
+int walsh_octo_set_tma_store(int on);
 
 /* Status word of the tcgen05 kernels (GEMMs and prefill attention) on the
  * current device: 0, or WALSH_ERR_TIMEOUT once a bounded wait inside one of

@@ -244,3 +244,31 @@ def test_narrow_tiles_qkv_epilogue_equal_wide(mainloop):
     finally:
         _lib.call("walsh_octo_set_narrow", prev)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("M,fin,fout", [(1, 512, 512), (100, 512, 256), (4099, 512, 1536), (20003, 512, 512),
+                                        (777, 1368, 512), (333, 512, 1368)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_tma_store_epilogue_equals_row_stores(mainloop, M, fin, fout, dtype):
+    """The plain epilogue's TMA-store form (each warp's scaled 32 x 32 block
+    staged in shared memory with the 64-byte swizzle, clipped by the output
+    map at ragged M; narrow tiles for few rows) against each lane storing its
+    own row: the same rounding of the same sums, so equal bit for bit.  N not
+    a multiple of 32 keeps the row stores."""
+    from walsh_research_b200 import _lib
+    rng = np.random.default_rng(M + 7 * fin + fout)
+    m = _layer(fin, fout, rng)
+    x = T(rng.normal(size=(M, fin)).astype(np.float32), dtype)
+    prev = _lib.call("walsh_octo_set_tma_store", -1)
+    try:
+        _lib.call("walsh_octo_set_tma_store", 1)
+        a = mainloop(lambda: m.forward_flat(x), True)
+        _lib.call("walsh_octo_set_tma_store", 0)
+        b = mainloop(lambda: m.forward_flat(x), True)
+    finally:
+        _lib.call("walsh_octo_set_tma_store", prev)
+    assert torch.equal(a, b)
+    w, be = m.weight.detach().cpu().numpy(), m.beta.detach().cpu().numpy()
+    rows = np.r_[0:min(M, 200), max(0, M - 200):M]
+    ref = O.octonion_linear(x[rows].float().cpu().numpy(), w, be)
+    assert rel(a[rows], ref) < (3e-3 if dtype == torch.float16 else 1e-2)

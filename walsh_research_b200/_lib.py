@@ -43,6 +43,7 @@ SIGNATURES = {
                       P, P],
     "walsh_octo_set_mainloop": [c_int],
     "walsh_octo_set_narrow": [c_int],
+    "walsh_octo_set_tma_store": [c_int],
     "walsh_tc05_error": [c_int],
     "walsh_attn_set_path": [c_int],
     "walsh_moe_router_tc_fwd": [P, c_int, c_int64, P, P, c_int, P, P, P, P, P],
@@ -87,7 +88,7 @@ SIGNATURES = {
 _RESTYPE = {"walsh_status_str": ctypes.c_char_p, "walsh_ipc_handle_bytes": c_int, "walsh_chmod_mlp_tc_scratch_bytes": ctypes.c_int64,
             "walsh_linear_split_tc_scratch_bytes": ctypes.c_int64}
 # kernels each entry point launches (for the launch accounting reported by bench.py)
-KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_octo_set_mainloop": 0, "walsh_octo_set_narrow": 0,
+KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc": 3, "walsh_octo_set_mainloop": 0, "walsh_octo_set_narrow": 0, "walsh_octo_set_tma_store": 0,
                     "walsh_chmod_mlp_tc": 3, "walsh_chmod_mlp_tc_scratch_bytes": 0,
                     "walsh_linear_split_tc_fwd": 2, "walsh_linear_split_tc_scratch_bytes": 0,
                     "walsh_tc05_error": 0, "walsh_attn_set_path": 0, "walsh_map_error": 0, "walsh_map_set_pipe": 0, "walsh_hlin_pk_error": 0, "walsh_chmod_chunk_rows": 0, "walsh_status_str": 0,
@@ -95,7 +96,7 @@ KERNELS_PER_CALL = {"walsh_ternary_quantize_pack": 2, "walsh_chmod_fwd_noalloc":
                     "walsh_ipc_handle_bytes": 0}
 launch_count = 0
 # entry points that return a plain int rather than a status
-_PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows", "walsh_octo_set_mainloop", "walsh_octo_set_narrow", "walsh_tc05_error",
+_PLAIN_INT = {"walsh_abi_version", "walsh_chmod_chunk_rows", "walsh_octo_set_mainloop", "walsh_octo_set_narrow", "walsh_octo_set_tma_store", "walsh_tc05_error",
               "walsh_map_error", "walsh_attn_set_path", "walsh_map_set_pipe", "walsh_hlin_pk_error"}
 
 

@@ -26,6 +26,7 @@
 #include <cudaTypedefs.h>
 #include <math_constants.h>
 
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -132,10 +133,26 @@ struct EpiPlain {
     chunk16(m, n, v);
     chunk16(m, n + 16, v + 16);
   }
+  // v[j] *= scale[n + j], j < 32 (n a multiple of 32, scale 16-byte aligned)
+  __device__ __forceinline__ void scale32(int64_t n, float* v) const {
+    const float4* s4 = reinterpret_cast<const float4*>(scale + n);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 sv = __ldg(s4 + j);
+      v[4 * j] *= sv.x;
+      v[4 * j + 1] *= sv.y;
+      v[4 * j + 2] *= sv.z;
+      v[4 * j + 3] *= sv.w;
+    }
+  }
   __host__ bool vec_ok() const { return N % 16 == 0 && (((uintptr_t)scale) & 15u) == 0; }
+  // TMA-store form: whole 32-column blocks (scale32), y 16-byte aligned
+  __host__ bool tma_ok() const { return vec_ok() && N % 32 == 0 && (((uintptr_t)y) & 15u) == 0; }
+  using out_t = TY;
   static constexpr int kWarpScratch = 0;  // has a warp-cooperative path (warp_block)
   static constexpr int kRowEpilogue = 0;  // one call per accumulator row (row)
   static constexpr int kHalfRow = 0;      // one call per row and 128-column half (half_row)
+  static constexpr int kTmaStore = 1;     // scale32 + the kernel's TMA-store path
 };
 
 template <typename TY>
@@ -794,6 +811,16 @@ constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
 }  // namespace octo_tc
 
+// Epilogues with a TMA-store path declare kTmaStore = 1 (scale32, out_t).
+template <class E, class = void>
+struct TmaStoreOf {
+  static constexpr int value = 0;
+};
+template <class E>
+struct TmaStoreOf<E, std::void_t<decltype(E::kTmaStore)>> {
+  static constexpr int value = E::kTmaStore;
+};
+
 // Launch shape: mainloop stages, epilogue ring depth and shared memory.  An
 // epilogue with a warp path trades mainloop stages for in-flight stream
 // rows: 2 stages and a 4-slot ring for K <= 512 (short mainloops), else 3 and 2.
@@ -813,12 +840,19 @@ struct OctoTcShape {
       stages = octo_tc::STAGES;
       depth = 0;
       smem = scratch_off(stages) + Epi::kRowScratch + 1024;
+    } else if constexpr (TmaStoreOf<Epi>::value > 0) {
+      // per epilogue warp two 32 x 32 16-bit staging blocks (64-byte
+      // swizzle), 1024-byte aligned after the barriers
+      stages = octo_tc::STAGES;
+      depth = 0;
+      smem = tma_stage_off(stages) + 8 * 2 * 2048 + 1024;
     } else {
       stages = octo_tc::STAGES;
       depth = 0;
       smem = scratch_off(stages) + 1024;
     }
   }
+  __host__ __device__ static int tma_stage_off(int stages) { return (scratch_off(stages) + 1023) & ~1023; }
   __host__ __device__ static int scratch_off(int stages) { return stages * octo_tc::STAGE_BYTES + 256; }
 };
 
@@ -828,7 +862,8 @@ __device__ int g_tc05_error;
 template <typename TA, class Epi, int BNT>
 __global__ void __launch_bounds__(octo_tc::NTHREADS, 1)
 octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                      int64_t M, int K, int64_t N, Epi epi, int vec, int nstage, int depth) {
+                      const __grid_constant__ CUtensorMap tma_y, int64_t M, int K, int64_t N, Epi epi, int vec,
+                      int nstage, int depth) {
   using namespace octo_tc;
   using namespace tc05;
   // BNT: the CTA tile's width (256; 64 for few-row GEMMs, so that more CTAs
@@ -932,6 +967,9 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       if (Epi::kRowEpilogue > 0 || vec == 2) epi.stage(rowscr, threadIdx.x - 64);
       asm volatile("bar.sync 1, 256;\n" ::: "memory");  // the 8 epilogue warps
     }
+    // TMA-store form (vec == 3): each warp's two 32 x 32 staging blocks
+    unsigned char* stg = smem + OctoTcShape<Epi>::tma_stage_off(STAGES) + (warp - 2) * 4096;
+    int nst = 0;  // blocks this warp has stored
     int i = 0;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int b = i & 1;
@@ -943,6 +981,42 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       const int64_t m = (t / ntl) * BM + q * 32 + lane, n0 = (t % ntl) * BN + half * (BN / 2);
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * ACC_COLS + half * (BN / 2));
       bool done = false;
+      if constexpr (TmaStoreOf<Epi>::value > 0) {
+        if (vec == 3) {
+          // lane = row: scaled, rounded 32-column block into a staging block
+          // (16-byte chunk j of row r at chunk j ^ ((r >> 1) & 3), the 64-byte
+          // swizzle of the output map), then one lane stores the block; a
+          // block is rewritten only after the store issued two blocks
+          // earlier has read it.  The map clips rows >= M and columns >= N.
+          using TO = typename Epi::out_t;
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 32, ++nst) {
+            float v[32];
+            tmem_ld32(base + (uint32_t)c, v);
+            const int64_t n = n0 + c;
+            if (n < N) epi.scale32(n, v);
+            unsigned char* blk = stg + (nst & 1) * 2048;
+            if (lane == 0) bulk_wait_read1();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 w;
+              w.x = pack2<TO>(v[8 * j], v[8 * j + 1]);
+              w.y = pack2<TO>(v[8 * j + 2], v[8 * j + 3]);
+              w.z = pack2<TO>(v[8 * j + 4], v[8 * j + 5]);
+              w.w = pack2<TO>(v[8 * j + 6], v[8 * j + 7]);
+              *reinterpret_cast<uint4*>(blk + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0 && n < N && m < M) {  // m: the warp's first row (lane 0)
+              tma_store_2d(&tma_y, blk, (int)n, (int)m);
+              bulk_commit();
+            }
+          }
+          done = true;
+        }
+      }
       if constexpr (Epi::kRowEpilogue > 0) {  // N <= BN / 2: both halves split the first 128 columns
         epi.row(m, base - (uint32_t)(half * (BN / 2)), half, q * 32 + lane, i & 1, rowscr, M);
         done = true;
@@ -986,6 +1060,7 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
+    if (lane == 0 && nst > 0) bulk_wait_all();  // the stores are done before the CTA exits
   }
   __syncwarp();
   fence_before_sync();
@@ -996,14 +1071,19 @@ octo_gemm_tc05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
 
 // 1 when the tcgen05 path ran, 0 when it does not apply (caller falls back),
 // negative on a launch error.
+// Plain-epilogue GEMMs store their output through shared memory by TMA
+// when on (walsh_octo_set_tma_store).
+int g_octo_tma_store = 1;
+
 template <typename TA, class Epi, int BNT>
 static int launch_octo_tc05_bn(const void* a, int64_t M, int K, const void* w, int64_t N, const Epi& epi,
                                cudaStream_t s) {
   using namespace octo_tc;
   if (M < 1 || M > 2147483647LL || N > 2147483647LL) return 0;
   constexpr bool BF = std::is_same<TA, __nv_bfloat16>::value;
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, my;
   if (!make_tile_map(&ma, a, BF, M, K, octo_tc::BK, BM) || !make_tile_map(&mb, w, BF, N, K, octo_tc::BK, BNT)) return 0;
+  memset(&my, 0, sizeof(my));
   auto kern = octo_gemm_tc05_kernel<TA, Epi, BNT>;
   const OctoTcShape<Epi> shp(K);
   const int SMEM_B = shp.smem;
@@ -1022,7 +1102,13 @@ static int launch_octo_tc05_bn(const void* a, int64_t M, int K, const void* w, i
   if constexpr (Epi::kHalfRow > 0 && BNT == 256) {
     if (epi.half_row_ok()) vec = 2;
   }
-  kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, M, K, N, epi, vec, shp.stages, shp.depth);
+  if constexpr (TmaStoreOf<Epi>::value > 0) {
+    // 3: scaled blocks leave through shared memory by TMA stores
+    if (g_octo_tma_store && epi.tma_ok() && std::is_same<typename Epi::out_t, TA>::value &&
+        make_store_map(&my, epi.y, BF, M, N))
+      vec = 3;
+  }
+  kern<<<grid, NTHREADS, SMEM_B, s>>>(ma, mb, my, M, K, N, epi, vec, shp.stages, shp.depth);
   const int st = launch_status();
   return st == WALSH_OK ? 1 : st;
 }
@@ -1247,6 +1333,12 @@ extern "C" int walsh_octo_set_mainloop(int tcgen05) {
 extern "C" int walsh_octo_set_narrow(int on) {
   const int prev = walsh::g_octo_narrow;
   if (on >= 0) walsh::g_octo_narrow = on ? 1 : 0;
+  return prev;
+}
+
+extern "C" int walsh_octo_set_tma_store(int on) {
+  const int prev = walsh::g_octo_tma_store;
+  if (on >= 0) walsh::g_octo_tma_store = on ? 1 : 0;
   return prev;
 }
 

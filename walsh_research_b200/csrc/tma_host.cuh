@@ -43,4 +43,21 @@ static bool make_tile_map(CUtensorMap* map, const void* base, bool bf16, int64_t
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Output map of a row-major [rows, cols] 16-bit matrix for TMA stores of
+// 32 x 32 blocks staged with the 64-byte swizzle (16-byte chunk j of block
+// row r at chunk j ^ ((r >> 1) & 3)); cols a multiple of 8, base 16-byte
+// aligned.
+static bool make_store_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows, int64_t cols) {
+  auto enc = tensor_map_encoder();
+  if (!enc || cols % 8 != 0 || (((uintptr_t)base) & 15u)) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace walsh
