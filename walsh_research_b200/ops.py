@@ -85,14 +85,14 @@ def hadamard_linear_tc(x, w_f16, alpha, beta, w_scale: float = 1.0):
 HLIN_PACKED = True
 HLIN_PACKED_FEATURES = (512, 2048)
 # 16-bit HadamardLinear(512, 512) from this many tokens on runs as one
-# tcgen05 GEMM over the layer's dense matrix (hadamard_linear_dense; 65536
-# tokens: 49.6 us against the packed kernel's 57.7 us); below it (16384
-# tokens: 16.4 against 14.6 us of GPU time), and for 2048 (where the dense
-# GEMM has 4 times the multiply-adds per token of 512 and measured 464 us
-# against 207 us), the packed kernel
+# tcgen05 GEMM over the layer's dense matrix (hadamard_linear_dense; device
+# time at 16384 / 65536 tokens: 13.9 / 37.1 us against the packed kernel's
+# 16.2 / 54.6 us); below it (4096 - 8192 tokens: 9.0 - 9.3 against 8.4 -
+# 8.5 us), and for 2048 (where the dense GEMM has 4 times the multiply-adds
+# per token of 512 and measured 464 us against 207 us), the packed kernel
 HLIN_DENSE = True
 HLIN_DENSE_FEATURES = (512,)
-HLIN_DENSE_FROM = 32768
+HLIN_DENSE_FROM = 16384
 
 
 def hadamard_linear_dense_weights(packed, alpha, beta, features, dtype):
