@@ -214,21 +214,22 @@ hlin_packed_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* __res
 
 // ---------------------------------------------------------------------------
 // C = 2048 (32 groups x 64).  One persistent CTA of 16 warps per SM walks
-// 16-token tiles through one buffer of 16 rows (the 16-bit transformed
-// input, then in place the 16-bit mat-vec results):
-//   A  warp t takes token t of the tile, lane p its columns 2p, 2p + 1 in
+// 32-token tiles (16-token tiles while there are at most as many as SMs) through
+// one buffer of 32 (16) rows (the 16-bit transformed input, then in place
+// the 16-bit mat-vec results):
+//   A  warp t takes tokens t and 16 + t of the tile, lane p its columns 2p, 2p + 1 in
 //      each group (one 128-byte line per warp load), scaled by alpha,
 //      butterfly-transformed on float pairs, rounded into the row; the next
 //      tile's columns are then loaded into the same registers;
-//   B  warp w takes groups 2w, 2w + 1: A = the 16 x 64 block of group g
-//      (ldmatrix, all four k-steps held before the block is overwritten),
-//      B = w_g^T, 64 fragments per group decoded from this lane's 2-bit
+//   B  warp w takes groups 2w, 2w + 1: A = the two 16 x 64 blocks of group g
+//      (ldmatrix, all k-steps held before the blocks are overwritten),
+//      B = w_g^T, 32 fragments per group (each used by both blocks' MMAs) decoded from this lane's 2-bit
 //      codes (8 words per group, re-laid in shared memory once per CTA:
 //      code pairs at bits 2r and 2r + 16, decoded as the 16-bit integers
 //      1024 + c (fp16) or 128 + c (bf16) less 1025 or 129, exact); each
 //      16 x 8 result is rounded to the 16-bit type and written over its own
 //      columns of the block;
-//   C  warp t, lane p: output columns 2p, 2p + 1 over the 32 groups, the
+//   C  warp t, lane p: its two tokens' output columns 2p, 2p + 1 over the 32 groups, the
 //      butterfly transform, beta / 32, written straight to global memory.
 // Row pitch 4112 bytes: ldmatrix rows and fragment stores fall in distinct
 // banks; the A and C accesses of a warp are one contiguous 128-byte row
@@ -236,11 +237,16 @@ hlin_packed_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* __res
 // so a tile needs two block barriers.
 // ---------------------------------------------------------------------------
 namespace hpk4 {
-constexpr int C = 2048, G = 32, IO = 64, TM = 16, NW = 16, NT = NW * 32;
+constexpr int C = 2048, G = 32, IO = 64, TS = 16, NW = 16, NT = NW * 32;
 constexpr int ZROW = C * 2 + 16;
-constexpr int OFF_AB = TM * ZROW;
-constexpr int OFF_W = OFF_AB + 2 * G * IO * 4;  // [2 groups][8 n-tiles][NT threads] code words
-constexpr int SMEM = OFF_W + 16 * NT * 4;
+// tiles of NH 16-token halves (NH = 2 from a wave of 32-token tiles on; 1 below)
+template <int NH>
+struct Lay {
+  static constexpr int TM = NH * TS;
+  static constexpr int OFF_AB = TM * ZROW;
+  static constexpr int OFF_W = OFF_AB + 2 * G * IO * 4;  // [2 groups][8 n-tiles][NT threads] code words
+  static constexpr int SMEM = OFF_W + 16 * NT * 4;
+};
 }  // namespace hpk4
 
 template <typename T16>
@@ -266,15 +272,16 @@ __device__ __forceinline__ uint32_t ternary_code_pair(uint32_t word, int r) {
   }
 }
 
-template <typename T16>
+template <typename T16, int NH>
 __global__ void __launch_bounds__(hpk4::NT, 1)
 hlin_packed2048_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* __restrict__ w2,
                        const float* __restrict__ alpha, const float* __restrict__ beta, T16* __restrict__ y) {
   using namespace hpk4;
+  constexpr int TM = Lay<NH>::TM, OFF_AB = Lay<NH>::OFF_AB, OFF_W = Lay<NH>::OFF_W;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* sm = smem_raw;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, t4 = lane & 3;
-  const int64_t ntiles = (ntok + TM - 1) / TM;
+  const int64_t ntiles = (ntok + TM - 1) / TM;  // tiles of NH 16-token halves
   float* ab = reinterpret_cast<float*>(sm + OFF_AB);  // [G][IO] alpha, then [G][IO] beta / 32
   for (int q = tid; q < G * IO; q += NT) {
     ab[q] = __ldg(alpha + q);
@@ -304,8 +311,9 @@ hlin_packed2048_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* _
   const int pc = 2 * lane;  // columns of this lane in A and C (token = warp)
   const uint64_t* ab2 = reinterpret_cast<const uint64_t*>(ab);
   uint32_t xr[G];
-  auto load_x = [&](int64_t tile) {
-    const int64_t tok = tile * TM + warp;
+  // token row `half` (0 .. NH - 1) of tile `tile` for this warp
+  auto load_x = [&](int64_t tile, int half) {
+    const int64_t tok = tile * TM + half * TS + warp;
     if (tile < ntiles && tok < ntok) {
       const uint32_t* xp = reinterpret_cast<const uint32_t*>(x + tok * C + pc);
 #pragma unroll
@@ -315,20 +323,23 @@ hlin_packed2048_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* _
       for (int g = 0; g < G; ++g) xr[g] = 0u;
     }
   };
-  load_x(blockIdx.x);
+  load_x(blockIdx.x, 0);
   const uint32_t zs = tc05::smem_u32(sm);
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int64_t tok = tile * TM + warp;
-    unsigned char* zrow = sm + warp * ZROW + pc * 2;
-    // ---- A
-    {
+    // ---- A, for tokens warp (and 16 + warp) of the tile
+#pragma unroll 1
+    for (int half = 0; half < NH; ++half) {
+      unsigned char* zrow = sm + (half * TS + warp) * ZROW + pc * 2;
       uint64_t v[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float2 f = unpack2<T16>(xr[g]);
         v[g] = hpk_mul(hpk_pack(f.x, f.y), ab2[(g * IO + pc) / 2]);
       }
-      load_x(tile + gridDim.x);
+      if (half + 1 < NH)
+        load_x(tile, half + 1);
+      else
+        load_x(tile + gridDim.x, 0);
       fht32x2(v);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -337,35 +348,50 @@ hlin_packed2048_kernel(const T16* __restrict__ x, int64_t ntok, const uint8_t* _
       }
     }
     __syncthreads();
-    // ---- B: groups 2w, 2w + 1, results over their own block
-#pragma unroll
+    // ---- B: groups 2w, 2w + 1 over the NH 16-row halves (each decoded B
+    // fragment serves NH MMAs), results over their own block
+#pragma unroll 1
     for (int q = 0; q < 2; ++q) {
       const int g = 2 * warp + q;
-      uint32_t a[4][4];
+      uint32_t a[NH][4][4];
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint32_t addr = zs + (uint32_t)((lane & 15) * ZROW + (g * IO + ks * 16 + (lane >> 4) * 8) * 2);
-        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                     : "=r"(a[ks][0]), "=r"(a[ks][1]), "=r"(a[ks][2]), "=r"(a[ks][3])
-                     : "r"(addr)
-                     : "memory");
-      }
+      for (int mt = 0; mt < NH; ++mt)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t addr =
+              zs + (uint32_t)((mt * TS + (lane & 15)) * ZROW + (g * IO + ks * 16 + (lane >> 4) * 8) * 2);
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                       : "=r"(a[mt][ks][0]), "=r"(a[mt][ks][1]), "=r"(a[mt][ks][2]), "=r"(a[mt][ks][3])
+                       : "r"(addr)
+                       : "memory");
+        }
       __syncwarp();
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const uint32_t wd = wpk[(q * 8 + nt) * NT + tid];
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        float cc[NH][4];
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          mma16<T16>(c, a[ks], ternary_code_pair<T16>(wd, 2 * ks), ternary_code_pair<T16>(wd, 2 * ks + 1));
+        for (int mt = 0; mt < NH; ++mt) cc[mt][0] = cc[mt][1] = cc[mt][2] = cc[mt][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t b0 = ternary_code_pair<T16>(wd, 2 * ks), b1 = ternary_code_pair<T16>(wd, 2 * ks + 1);
+#pragma unroll
+          for (int mt = 0; mt < NH; ++mt) mma16<T16>(cc[mt], a[mt][ks], b0, b1);
+        }
         unsigned char* vp = sm + gid * ZROW + (g * IO + 8 * nt + 2 * t4) * 2;
-        *reinterpret_cast<uint32_t*>(vp) = pack2<T16>(c[0], c[1]);
-        *reinterpret_cast<uint32_t*>(vp + 8 * ZROW) = pack2<T16>(c[2], c[3]);
+#pragma unroll
+        for (int mt = 0; mt < NH; ++mt) {
+          *reinterpret_cast<uint32_t*>(vp + mt * TS * ZROW) = pack2<T16>(cc[mt][0], cc[mt][1]);
+          *reinterpret_cast<uint32_t*>(vp + (mt * TS + 8) * ZROW) = pack2<T16>(cc[mt][2], cc[mt][3]);
+        }
       }
     }
     __syncthreads();
-    // ---- C: output columns pc, pc + 1 of this warp's token over the 32 groups
-    {
+    // ---- C: output columns pc, pc + 1 of this warp's tokens over the 32 groups
+#pragma unroll 1
+    for (int half = 0; half < NH; ++half) {
+      const int64_t tok = tile * TM + half * TS + warp;
+      const unsigned char* zrow = sm + (half * TS + warp) * ZROW + pc * 2;
       uint64_t v[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -405,12 +431,28 @@ using namespace walsh;
 template <typename T16>
 static int launch_hlin_pk2048(const void* x, int64_t ntok, const uint8_t* w2, const float* alpha, const float* beta,
                               void* y, cudaStream_t s) {
-  const int64_t ntiles = (ntok + hpk4::TM - 1) / hpk4::TM;
-  const int grid = (int)min64(ntiles, hlin_pk_sms());
-  auto k = hlin_packed2048_kernel<T16>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, hpk4::SMEM) != cudaSuccess)
+  // 32-token tiles (each decoded weight fragment serves two 16-token MMAs)
+  // once 16-token tiles would give a CTA more than one (4096 tokens: 20.1
+  // against 22.1 us); 16-token tiles below, for more CTAs (64 tokens: 13.7
+  // against 18.4 us)
+  const int sms = hlin_pk_sms();
+  if ((ntok + 15) / 16 > sms) {
+    using L = hpk4::Lay<2>;
+    const int64_t ntiles = (ntok + L::TM - 1) / L::TM;
+    const int grid = (int)min64(ntiles, sms);
+    auto k = hlin_packed2048_kernel<T16, 2>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM) != cudaSuccess)
+      return launch_status();
+    k<<<grid, hpk4::NT, L::SMEM, s>>>((const T16*)x, ntok, w2, alpha, beta, (T16*)y);
     return launch_status();
-  k<<<grid, hpk4::NT, hpk4::SMEM, s>>>((const T16*)x, ntok, w2, alpha, beta, (T16*)y);
+  }
+  using L = hpk4::Lay<1>;
+  const int64_t ntiles = (ntok + L::TM - 1) / L::TM;
+  const int grid = (int)min64(ntiles, sms);
+  auto k = hlin_packed2048_kernel<T16, 1>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM) != cudaSuccess)
+    return launch_status();
+  k<<<grid, hpk4::NT, L::SMEM, s>>>((const T16*)x, ntok, w2, alpha, beta, (T16*)y);
   return launch_status();
 }
 
