@@ -186,3 +186,39 @@ def test_decode_parts_rule():
         assert model._decode_parts(big, 1, kv) == 1          # expert parallel
         del model.layers[0].__dict__["_ep"]
     assert model._decode_parts(big, 1, kv) == 1              # gradients on
+
+
+def test_hadamard_linear_form_selection_host_logic(monkeypatch):
+    """HadamardLinear.forward's choice of device form, with the device calls
+    replaced by recorders: 16-bit HadamardLinear(512, 512) from
+    HLIN_DENSE_FROM tokens on takes the dense tensor-core GEMM (its matrix
+    built once and cached), below that and for 2048 the packed 2-bit kernel,
+    float32 the general kernel; HLIN_DENSE = False keeps the packed kernel."""
+    from walsh_research_b200 import ops
+    from walsh_research_b200.model.fht_cuda import HadamardLinear
+    calls, built = [], []
+    monkeypatch.setattr(ops, "quantize_pack", lambda w: (torch.zeros(1, dtype=torch.uint8), None))
+    monkeypatch.setattr(ops, "hadamard_linear_dense_weights",
+                        lambda p, a, b, F, dt: built.append(dt) or (torch.zeros(F, F, dtype=dt), torch.ones(F)))
+    monkeypatch.setattr(ops, "hadamard_linear_dense", lambda x, w, s: calls.append("dense") or x)
+    monkeypatch.setattr(ops, "hadamard_linear_pk", lambda x, p, a, b: calls.append("packed") or x)
+    monkeypatch.setattr(ops, "tc_eligible", lambda x: False)
+    monkeypatch.setattr(ops, "hadamard_linear", lambda x, *a, **k: calls.append("general") or x)
+    for F in (512, 2048):
+        lin = HadamardLinear(F, F)
+        for T in (1, ops.HLIN_DENSE_FROM - 1, ops.HLIN_DENSE_FROM):
+            for dt in (torch.bfloat16, torch.float16, torch.float32):
+                calls.clear()
+                lin(torch.empty((T, F), dtype=dt))
+                if dt == torch.float32:
+                    want = "general"
+                elif F == 512 and T >= ops.HLIN_DENSE_FROM:
+                    want = "dense"
+                else:
+                    want = "packed"
+                assert calls == [want], (F, T, dt, calls)
+    assert built == [torch.bfloat16, torch.float16]  # one dense matrix per 16-bit type, cached
+    monkeypatch.setattr(ops, "HLIN_DENSE", False)
+    calls.clear()
+    HadamardLinear(512, 512)(torch.empty((ops.HLIN_DENSE_FROM, 512), dtype=torch.bfloat16))
+    assert calls == ["packed"]
